@@ -1,0 +1,130 @@
+// extern "C" entry points of libkda_b200.so: argument validation (fail
+// closed, before any launch) and dispatch to the kernels.
+#include <cuda_runtime.h>
+
+#include "kda_common.cuh"
+
+namespace kda {
+int decode_launch(float* S, const void* q, const void* k, const void* v, const void* g,
+                  const void* beta, void* o, int N, int dk, int dv, int in_dt, int o_dt,
+                  cudaStream_t st);
+size_t simt_bwd_workspace_bytes(int B, int H, int dk, int dv, int C);
+int simt_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                    const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
+                    int dk, int dv, int C, int in_dt, int o_dt, int ck_dt, cudaStream_t st);
+int simt_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                    const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
+                    void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T,
+                    int H, int dk, int dv, int C, int in_dt, int do_dt, int ck_dt,
+                    cudaStream_t st);
+}  // namespace kda
+
+namespace {
+
+bool valid_dtype(int d) { return d == KDA_F32 || d == KDA_BF16; }
+
+int check_dims(int B, int T, int H, int dk, int dv, int chunk) {
+  if (B < 0 || T < 0 || H < 0) return KDA_ERR_SHAPE;
+  if (dk < 8 || dk > 128 || dk % 8 || dv < 8 || dv > 128 || dv % 8) return KDA_ERR_SHAPE;
+  if (chunk != 16 && chunk != 32 && chunk != 64) return KDA_ERR_SHAPE;
+  if (static_cast<long long>(B) * H > 65535LL * 65535LL) return KDA_ERR_SHAPE;
+  if (B > 65535 || H > 65535) return KDA_ERR_SHAPE;
+  return KDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kda_version(void) { return 100; }
+
+const char* kda_strerror(int status) {
+  switch (status) {
+    case KDA_OK: return "ok";
+    case KDA_ERR_SHAPE: return "unsupported or inconsistent dimensions";
+    case KDA_ERR_DTYPE: return "unsupported element type";
+    case KDA_ERR_ALIGN: return "pointer not 16-byte aligned";
+    case KDA_ERR_NULL: return "required pointer is NULL";
+    case KDA_ERR_LAUNCH: return "CUDA launch failed";
+    case KDA_ERR_WORKSPACE: return "workspace missing or too small";
+    case KDA_ERR_DEVICE: return "no usable CUDA device";
+    default: return "unknown status";
+  }
+}
+
+size_t kda_ckpt_elems(int B, int T, int H, int dk, int dv, int chunk) {
+  if (chunk <= 0 || B < 0 || T < 0 || H < 0 || dk < 0 || dv < 0) return 0;
+  const size_t n = (static_cast<size_t>(T) + chunk - 1) / chunk;
+  return static_cast<size_t>(B) * H * n * dk * dv;
+}
+
+int kda_fwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
+            const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H, int dk,
+            int dv, int chunk, int in_dtype, int o_dtype, int ckpt_dtype, kda_stream_t stream) {
+  int rc = check_dims(B, T, H, dk, dv, chunk);
+  if (rc != KDA_OK) return rc;
+  if (!valid_dtype(in_dtype) || !valid_dtype(o_dtype) || !valid_dtype(ckpt_dtype))
+    return KDA_ERR_DTYPE;
+  if (B == 0 || H == 0) return KDA_OK;
+  if (T == 0) {
+    if (s_out) {
+      const size_t bytes = static_cast<size_t>(B) * H * dk * dv * sizeof(float);
+      cudaError_t e = s0 ? cudaMemcpyAsync(s_out, s0, bytes, cudaMemcpyDeviceToDevice, stream)
+                         : cudaMemsetAsync(s_out, 0, bytes, stream);
+      return e == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+    }
+    return KDA_OK;
+  }
+  if (!q || !k || !v || !g || !beta || !o) return KDA_ERR_NULL;
+  return kda::simt_fwd_launch(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, dk, dv, chunk,
+                              in_dtype, o_dtype, ckpt_dtype, stream);
+}
+
+size_t kda_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dtype) {
+  (void)T;
+  (void)in_dtype;
+  if (check_dims(B, T, H, dk, dv, chunk) != KDA_OK) return 0;
+  return kda::simt_bwd_workspace_bytes(B, H, dk, dv, chunk);
+}
+
+int kda_bwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
+            const void* s_ckpt, const void* do_, const float* dsT, void* dq, void* dk_, void* dv_,
+            void* dg, void* dbeta, float* ds0, void* workspace, size_t workspace_bytes, int B,
+            int T, int H, int dk, int dv, int chunk, int in_dtype, int do_dtype, int ckpt_dtype,
+            kda_stream_t stream) {
+  int rc = check_dims(B, T, H, dk, dv, chunk);
+  if (rc != KDA_OK) return rc;
+  if (!valid_dtype(in_dtype) || !valid_dtype(do_dtype) || !valid_dtype(ckpt_dtype))
+    return KDA_ERR_DTYPE;
+  if (B == 0 || H == 0) return KDA_OK;
+  if (T == 0) {
+    if (ds0) {
+      const size_t bytes = static_cast<size_t>(B) * H * dk * dv * sizeof(float);
+      cudaError_t e = dsT ? cudaMemcpyAsync(ds0, dsT, bytes, cudaMemcpyDeviceToDevice, stream)
+                          : cudaMemsetAsync(ds0, 0, bytes, stream);
+      return e == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+    }
+    return KDA_OK;
+  }
+  if (!q || !k || !v || !g || !beta || !s_ckpt || !do_ || !dq || !dk_ || !dv_ || !dg || !dbeta)
+    return KDA_ERR_NULL;
+  const size_t need = kda_bwd_workspace_bytes(B, T, H, dk, dv, chunk, in_dtype);
+  if (need && (!workspace || workspace_bytes < need)) return KDA_ERR_WORKSPACE;
+  return kda::simt_bwd_launch(q, k, v, g, beta, s_ckpt, do_, dsT, dq, dk_, dv_, dg, dbeta, ds0,
+                              workspace, B, T, H, dk, dv, chunk, in_dtype, do_dtype, ckpt_dtype,
+                              stream);
+}
+
+int kda_decode(float* S, const void* q, const void* k, const void* v, const void* g,
+               const void* beta, void* o, int N, int dk, int dv, int in_dtype, int o_dtype,
+               kda_stream_t stream) {
+  if (N < 0) return KDA_ERR_SHAPE;
+  if (!valid_dtype(in_dtype) || !valid_dtype(o_dtype)) return KDA_ERR_DTYPE;
+  if (!((dk == 64 || dk == 128) && (dv == 64 || dv == 128))) return KDA_ERR_SHAPE;
+  if (N == 0) return KDA_OK;
+  if (!S || !q || !k || !v || !g || !beta || !o) return KDA_ERR_NULL;
+  if (!kda::aligned16(S)) return KDA_ERR_ALIGN;
+  return kda::decode_launch(S, q, k, v, g, beta, o, N, dk, dv, in_dtype, o_dtype, stream);
+}
+
+}  // extern "C"

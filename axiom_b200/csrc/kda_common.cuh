@@ -1,0 +1,41 @@
+// Shared device helpers of the KDA library: element loads/stores for the two
+// supported element types and small launch utilities.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kda_b200.h"
+
+namespace kda {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ float ldf(const float* p) { return *p; }
+__device__ __forceinline__ float ldf(const bf16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void stf(float* p, float x) { *p = x; }
+__device__ __forceinline__ void stf(bf16* p, float x) { *p = __float2bfloat16_rn(x); }
+
+// Convert a status of the CUDA runtime after a launch into a KDA status.
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Opt a kernel into more than 48 KB of dynamic shared memory, once per device.
+template <typename Kern>
+inline int ensure_smem(Kern kern, int bytes, bool* done_per_device, int max_devices = 64) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= max_devices) return KDA_ERR_DEVICE;
+  if (!done_per_device[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+      return KDA_ERR_LAUNCH;
+    done_per_device[dev] = true;
+  }
+  return KDA_OK;
+}
+
+}  // namespace kda

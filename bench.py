@@ -1,0 +1,439 @@
+"""Benchmark of the B200 KDA core (the BASELINE headline: chunked fwd+bwd).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One process per GPU (torchrun for N > 1, NCCL).  The workload is BASELINE
+config 3 per rank (weak scaling over the batch: each rank owns B = 4
+sequences of T = 8192 tokens, H = 32 heads, dk = dv = 128, chunk 64, bf16
+inputs, fp32 state).  A step is one forward (with the chunk-boundary
+checkpoint) plus one fused backward from a bf16 upstream cotangent.  Inputs
+(268 MB per q/k/v/g tensor) are larger than the 126 MB L2, so no flush is
+needed between steps.  Rank 0 prints ONE JSON line.
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+NumPy restatement in ``oracle/``; the reference itself is JAX, which is not
+installed) on the host cores over a bounded sample and prints the same line
+with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "KDA fwd+bwd tokens/s/GPU (H=32,d=128,T=8K bf16); %tensor peak; decode HBM GB/s"
+CFG3 = dict(B=4, T=8192, H=32, dk=128, dv=128, chunk=64)
+CFG2 = dict(B=8, T=4096, H=16, dk=128, dv=128, chunk=64)
+CFG4 = dict(N=256 * 32, dk=128, dv=128)
+
+# Algorithmic work (per chunk-head at C=64, dk=dv=128): forward 11.62 MFLOP,
+# backward adjoint 23.07 MFLOP (recompute excluded).
+FWD_FLOP_PER_CHUNK_HEAD = 11.62e6
+BWD_FLOP_PER_CHUNK_HEAD = 23.07e6
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm=float(p["hbm_gbs"]), bf16=float(p["bf16_tflops"]),
+                    bf16_sustained=float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                    source="measured")
+    except (OSError, KeyError, ValueError):
+        return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 8:
+                        rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            if self.path:
+                try:
+                    os.unlink(self.path)
+                except OSError:
+                    pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        sm = []
+        smax = None
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, r[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs (BASELINE distributions), generated on the device
+# ---------------------------------------------------------------------------
+
+
+def make_train_inputs(torch, cfg, seed, device):
+    B, T, H, dk, dv = cfg["B"], cfg["T"], cfg["H"], cfg["dk"], cfg["dv"]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    bf = torch.bfloat16
+
+    def normal(*shape):
+        return torch.randn(*shape, generator=gen, device=device, dtype=torch.float32)
+
+    q = torch.nn.functional.normalize(normal(B, T, H, dk), dim=-1).to(bf)
+    k = torch.nn.functional.normalize(normal(B, T, H, dk), dim=-1).to(bf)
+    v = normal(B, T, H, dv).to(bf)
+    g = torch.nn.functional.logsigmoid(normal(B, T, H, dk) + 3.0).to(bf)
+    beta = torch.sigmoid(normal(B, T, H)).to(bf)
+    do = normal(B, T, H, dv).to(bf)
+    return q, k, v, g, beta, do
+
+
+# ---------------------------------------------------------------------------
+# the B200 arm
+# ---------------------------------------------------------------------------
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    from axiom_b200 import kda as KD
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    peaks = _peaks()
+    cfg = dict(CFG3)
+    B, T, H, dk, dv, C = (cfg[k] for k in ("B", "T", "H", "dk", "dv", "chunk"))
+    n_chunks = (T + C - 1) // C
+    q, k, v, g, beta, do = make_train_inputs(torch, cfg, seed=1234 + rank, device=dev)
+
+    events = []
+
+    def step(record):
+        if record:
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+        o, s_t, ckpt = KD.kda_fwd(q, k, v, g, beta, None, chunk=C, need_ckpt=True)
+        if record:
+            e1.record()
+        grads = KD.kda_bwd(q, k, v, g, beta, ckpt, do, None, chunk=C, need_ds0=False)
+        if record:
+            e2.record()
+            events.append((e0, e1, e2))
+        return grads
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step(True)
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    fwd_ms = sum(a.elapsed_time(b) for a, b, _ in events) / len(events)
+    bwd_ms = sum(b.elapsed_time(c) for _, b, c in events) / len(events)
+    stats = torch.tensor([ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ms, fwd_ms, bwd_ms = (float(x) for x in stats.tolist())
+    clocks = clk.summary()
+
+    tokens_per_step = world * B * T
+    value = tokens_per_step * args.steps / (ms / 1e3)
+    units = B * H * n_chunks
+    fwd_flop = FWD_FLOP_PER_CHUNK_HEAD * units
+    bwd_flop = BWD_FLOP_PER_CHUNK_HEAD * units
+    dom_ms, dom_flop, dom = (bwd_ms, bwd_flop, "kda_bwd") if bwd_ms >= fwd_ms else (fwd_ms, fwd_flop, "kda_fwd")
+    achieved = dom_flop / (dom_ms / 1e3) / 1e12
+    peak = peaks["bf16_sustained"] if ms * args.steps > 1000.0 else peaks["bf16"]
+
+    # e2e through the public API with host buffers (rank-local), after the device timing
+    e2e = run_e2e(torch, KD, q, k, v, g, beta, do, C, args, dev)
+    if world > 1:
+        t = torch.tensor([e2e["ms"]], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e["ms"] = float(t.item())
+    e2e_value = tokens_per_step / (e2e["ms"] / 1e3)
+
+    extra = {}
+    if rank == 0 and not args.no_extra:
+        extra["decode"] = run_decode(torch, KD, dev, peaks)
+        extra["prefill"] = run_prefill(torch, KD, dev, peaks)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(sample_heads=args.cpu_heads, cfg=cfg)
+
+    launches_per_step = 2  # kda_fwd + kda_bwd, one kernel each on the current path
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (BASELINE distributions, seeded per rank)",
+            "config": {"workload": "cfg3 KDA chunked fwd+bwd", "B_per_rank": B, "T": T, "H": H,
+                       "dk": dk, "dv": dv, "chunk": C, "global_batch": B * world,
+                       "parallelism": f"batch-sharded x{world}, no collective",
+                       "l2": "inputs larger than L2 (no flush)",
+                       "value_is": "whole-job tokens/s over all GPUs"},
+            "kernels_ms": {"kda_fwd": fwd_ms, "kda_bwd": bwd_ms},
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_source": peaks["source"] + (" sustained" if peak == peaks["bf16_sustained"] else " burst"),
+                         "traffic": None},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
+                    "d2h_bytes_per_step": e2e["d2h"]},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(torch, KD, q, k, v, g, beta, do, C, args, dev):
+    """Host (pinned) inputs -> device -> fwd+bwd -> gradients back to host, per step."""
+    host_in = [x.cpu().pin_memory() for x in (q, k, v, g, beta, do)]
+    dev_in = [torch.empty_like(x) for x in (q, k, v, g, beta, do)]
+    host_out = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in (q, k, v, g, beta)]
+    h2d = sum(x.numel() * x.element_size() for x in host_in)
+    d2h = sum(x.numel() * x.element_size() for x in host_out)
+
+    def step():
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        qd, kd, vd, gd, bd, dod = dev_in
+        _, _, ckpt = KD.kda_fwd(qd, kd, vd, gd, bd, None, chunk=C, need_ckpt=True)
+        grads = KD.kda_bwd(qd, kd, vd, gd, bd, ckpt, dod, None, chunk=C, need_ds0=False)
+        for h_, d_ in zip(host_out, grads[:5]):
+            h_.copy_(d_, non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        step()
+    torch.cuda.synchronize()
+    n = max(1, min(args.steps, 3))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(n):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    return {"ms": s.elapsed_time(e) / n, "h2d": h2d, "d2h": d2h}
+
+
+def run_decode(torch, KD, dev, peaks, steps=64, warmup=8):
+    """256 sequences x 32 heads, fp32 128x128 states, one token per step."""
+    N, dk, dv = CFG4["N"], CFG4["dk"], CFG4["dv"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    S = torch.randn(N, dk, dv, generator=gen, device=dev) * 0.02
+    nb = 16  # distinct token batches cycled through (inputs for every step are new data)
+    bf = torch.bfloat16
+    qs = torch.nn.functional.normalize(torch.randn(nb, N, dk, generator=gen, device=dev), dim=-1).to(bf)
+    ks = torch.nn.functional.normalize(torch.randn(nb, N, dk, generator=gen, device=dev), dim=-1).to(bf)
+    vs = torch.randn(nb, N, dv, generator=gen, device=dev).to(bf)
+    gs = torch.nn.functional.logsigmoid(torch.randn(nb, N, dk, generator=gen, device=dev) + 3.0).to(bf)
+    bs = torch.sigmoid(torch.randn(nb, N, generator=gen, device=dev)).to(bf)
+    for i in range(warmup):
+        KD.decode_step(S, qs[i % nb], ks[i % nb], vs[i % nb], gs[i % nb], bs[i % nb])
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        KD.decode_step(S, qs[i % nb], ks[i % nb], vs[i % nb], gs[i % nb], bs[i % nb])
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    state_bytes = 2 * N * dk * dv * 4
+    in_bytes = N * (3 * dk * 2 + dv * 2 + 2) + N * dv * 2
+    gbs = (state_bytes + in_bytes) / (ms / 1e3) / 1e9
+    return {"workload": "cfg4 decode step, 256 seqs x 32 heads, fp32 128x128 state",
+            "us_per_step": ms * 1e3, "GB/s": gbs, "peak_GB/s": peaks["hbm"],
+            "frac": gbs / peaks["hbm"], "bytes_per_step": state_bytes + in_bytes, "steps": steps}
+
+
+def run_prefill(torch, KD, dev, peaks, steps=5, warmup=3):
+    """forward only, B=8, T=4096, H=16, S0 ~ N(0, 0.02)."""
+    cfg = dict(CFG2)
+    q, k, v, g, beta, _ = make_train_inputs(torch, cfg, seed=99, device=dev)
+    S0 = torch.randn(cfg["B"], cfg["H"], cfg["dk"], cfg["dv"], device=dev) * 0.02
+    for _ in range(warmup):
+        KD.kda_fwd(q, k, v, g, beta, S0, chunk=cfg["chunk"])
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        KD.kda_fwd(q, k, v, g, beta, S0, chunk=cfg["chunk"])
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    units = cfg["B"] * cfg["H"] * (cfg["T"] // cfg["chunk"])
+    tf = FWD_FLOP_PER_CHUNK_HEAD * units / (ms / 1e3) / 1e12
+    return {"workload": "cfg2 prefill fwd, B=8 T=4096 H=16", "ms": ms,
+            "tokens/s": cfg["B"] * cfg["T"] / (ms / 1e3), "TFLOP/s": tf,
+            "frac_bf16_peak": tf / peaks["bf16"]}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm
+# ---------------------------------------------------------------------------
+
+
+def cpu_baseline(sample_heads, cfg, T=None):
+    """Time the reference algorithm (NumPy restatement, fp32) on a bounded sample:
+    ``sample_heads`` (b, h) units at full T, fwd+bwd; scaled to the whole
+    workload by B*H/sample_heads (units are independent)."""
+    import numpy as np
+
+    from oracle import kda_oracle as K
+
+    T = cfg["T"] if T is None else T
+    x = K.make_inputs(1, T, sample_heads, cfg["dk"], cfg["dv"], seed=0)
+    do = np.random.default_rng(1).standard_normal((1, T, sample_heads, cfg["dv"])).astype(np.float32)
+    t0 = time.perf_counter()
+    K.chunk_fwd(x["q"], x["k"], x["v"], x["g"], x["beta"], None, chunk=cfg["chunk"], dtype=np.float32)
+    K.chunk_bwd(x["q"], x["k"], x["v"], x["g"], x["beta"], None, do, None, chunk=cfg["chunk"],
+                dtype=np.float32)
+    dt = time.perf_counter() - t0
+    full_step_s = dt * (cfg["B"] * cfg["H"] / sample_heads) * (cfg["T"] / T)
+    tokens = cfg["B"] * cfg["T"]
+    return {"value": tokens / full_step_s, "unit": "tokens/s", "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"{sample_heads} (b,h) units x T={T} fwd+bwd in {dt:.2f} s, NumPy fp32 "
+                      f"restatement of the reference JAX path (JAX absent), scaled by B*H",
+            "threads": "OpenBLAS default (all host cores)"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = dict(CFG3)
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(sample_heads=1, cfg=cfg, T=1024)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(sample_heads=args.cpu_heads, cfg=cfg)["value"])
+    wall = time.perf_counter() - t0
+    value = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": cfg["B"] * cfg["T"] / value * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg3 KDA chunked fwd+bwd", "B_per_rank": cfg["B"], "T": cfg["T"],
+                   "H": cfg["H"], "dk": cfg["dk"], "dv": cfg["dv"], "chunk": cfg["chunk"]},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"per step {args.cpu_heads} (b,h) units x T={cfg['T']} fwd+bwd, "
+                                   "NumPy fp32 restatement (reference JAX not installed), "
+                                   f"scaled by B*H; {wall:.1f} s wall"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-heads", type=int, default=8)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-extra", action="store_true", help="skip the decode/prefill extras")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)  # the timing contract needs >= 3 untimed warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,123 @@
+/*
+ * kda_b200.h -- C ABI of the B200 (sm_100a) Kimi Delta Attention core.
+ *
+ * The library replaces the reference's KDA core interval (AXIOM, pure
+ * JAX/Pallas): the operand-form whole-sequence scan and its custom_vjp,
+ *
+ *   cc_scan(q, k, v, alpha, beta32, S, tile, chunk) -> (o, S_T)
+ *       net/kernels/kda_cc_fused_persist.py:920-932   (custom_vjp entry)
+ *   kernel(...)      forward launch   net/kernels/kda_cc_fused_persist.py:718-759
+ *   kernel_bwd(...)  backward launch  net/kernels/kda_cc_fused_persist.py:1707-1763
+ *   _delta_step + o = S^T q           net/kda.py:298-310, :293  (decode)
+ *
+ * Conventions
+ *   - Tensors are dense row-major device buffers:
+ *       q, k, g : [B, T, H, dk]     v, o : [B, T, H, dv]     beta : [B, T, H]
+ *       S0, S_T : [B, H, dk, dv] fp32
+ *     (the reference's per-batch (T, H*D) interval layout with B in front).
+ *   - g is the per-channel log-decay (alpha = exp(g), g <= 0); the reference
+ *     passes alpha and takes log(alpha) itself, so dg here is its dalpha*alpha.
+ *   - beta is the write gate per (token, head); the reference's beta32 is
+ *     this value replicated over 32 columns.
+ *   - T need not be a multiple of the chunk: the ragged tail is computed as
+ *     zero-padded rows (q = k = v = 0, beta = 0, g = 0), which leaves the state
+ *     and every real row exactly as the padded reference computes them.
+ *   - Every entry point is stateless, allocates nothing, never synchronises
+ *     the host, and only enqueues work on `stream` (NULL = legacy default
+ *     stream).  Scratch memory comes from the caller (`workspace`).
+ *   - Return value: KDA_OK (0) or a negative KDA_ERR_* code; invalid shapes,
+ *     dtypes, alignment or null pointers are rejected before any launch
+ *     (fail-closed, the reference's typed-error contract net/kda.py:759-763).
+ */
+#ifndef KDA_B200_H
+#define KDA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kda_stream_t;
+
+/* element types */
+enum {
+  KDA_F32 = 0,
+  KDA_BF16 = 1
+};
+
+/* status codes */
+enum {
+  KDA_OK = 0,
+  KDA_ERR_SHAPE = -1,   /* unsupported or inconsistent dimensions */
+  KDA_ERR_DTYPE = -2,   /* unsupported element type combination */
+  KDA_ERR_ALIGN = -3,   /* a pointer is not 16-byte aligned */
+  KDA_ERR_NULL = -4,    /* a required pointer is NULL */
+  KDA_ERR_LAUNCH = -5,  /* the CUDA launch itself failed */
+  KDA_ERR_WORKSPACE = -6, /* workspace missing or too small */
+  KDA_ERR_DEVICE = -7   /* no sm_100 device / device query failed */
+};
+
+/* Library version (major*10000 + minor*100 + patch). */
+int kda_version(void);
+
+/* Human-readable text of a status code. */
+const char* kda_strerror(int status);
+
+/* Number of chunk-boundary states the forward stores for the backward:
+ * B * H * ceil(T / chunk) * dk * dv elements.  Entry c of [B, H, n, dk, dv]
+ * is the state entering chunk c (the reference's pass-A state chain,
+ * net/kernels/kda_cc_fused_persist.py:1282-1370). */
+size_t kda_ckpt_elems(int B, int T, int H, int dk, int dv, int chunk);
+
+/* Chunked forward (replaces kernel / cc_scan's forward rule,
+ * net/kernels/kda_cc_fused_persist.py:718-759).
+ *   in_dtype   : dtype of q, k, v, g, beta (KDA_F32 or KDA_BF16)
+ *   o_dtype    : dtype of o
+ *   s0         : [B,H,dk,dv] fp32 initial state, or NULL for zeros
+ *   s_out      : [B,H,dk,dv] fp32 final state, or NULL
+ *   s_ckpt     : chunk-boundary states for the backward (kda_ckpt_elems
+ *                elements of ckpt_dtype), or NULL when not training.
+ * Supported: 1 <= dk, dv <= 128 (multiples of 8), chunk in {16, 32, 64}.
+ * bf16 inputs with dk = dv = 128, chunk = 64 take the tensor-core path. */
+int kda_fwd(const void* q, const void* k, const void* v, const void* g,
+            const void* beta, const float* s0, void* o, float* s_out,
+            void* s_ckpt, int B, int T, int H, int dk, int dv, int chunk,
+            int in_dtype, int o_dtype, int ckpt_dtype, kda_stream_t stream);
+
+/* Bytes of caller-provided scratch kda_bwd needs for these dimensions. */
+size_t kda_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
+                               int in_dtype);
+
+/* Fused backward (replaces kernel_bwd / cc_scan's backward rule,
+ * net/kernels/kda_cc_fused_persist.py:1707-1763 and reference_bwd_scan
+ * :794-849).  Walks the chunks in reverse, recomputing each chunk from its
+ * checkpointed boundary state (s_ckpt written by kda_fwd with the same
+ * dimensions and ckpt_dtype), and produces
+ *   dq, dk : [B,T,H,dk]   dv : [B,T,H,dv]   dg : [B,T,H,dk]   dbeta : [B,T,H]
+ * in in_dtype, and ds0 : [B,H,dk,dv] fp32 (may be NULL).
+ *   do_    : [B,T,H,dv] upstream cotangent of o, in do_dtype
+ *   dsT    : [B,H,dk,dv] fp32 cotangent of the final state, or NULL (zero). */
+int kda_bwd(const void* q, const void* k, const void* v, const void* g,
+            const void* beta, const void* s_ckpt, const void* do_,
+            const float* dsT, void* dq, void* dk_, void* dv_, void* dg,
+            void* dbeta, float* ds0, void* workspace, size_t workspace_bytes,
+            int B, int T, int H, int dk, int dv, int chunk, int in_dtype,
+            int do_dtype, int ckpt_dtype, kda_stream_t stream);
+
+/* One recurrent decode step for N independent (sequence, head) states
+ * (replaces _delta_step + o = S^T q, net/kda.py:298-310, :293):
+ *   S <- diag(alpha) S - beta k ((alpha*k)^T S) + beta k v^T ;  o = S^T q
+ * with alpha = exp(g).  S : [N, dk, dv] fp32, updated in place;
+ * q, k, g : [N, dk]; v : [N, dv]; beta : [N] (in_dtype); o : [N, dv].
+ * Supported: dk, dv in {64, 128}. */
+int kda_decode(float* S, const void* q, const void* k, const void* v,
+               const void* g, const void* beta, void* o, int N, int dk, int dv,
+               int in_dtype, int o_dtype, kda_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KDA_B200_H */

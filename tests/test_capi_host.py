@@ -1,0 +1,115 @@
+"""Host-side checks of the C ABI and the Python mirror (no GPU needed).
+
+* the library loads and exports every function ``include/kda_b200.h`` declares;
+* argument validation fails closed before any launch (typed error codes);
+* the implementation switch fails closed on unknown values
+  (``net/kda.py:708-729``) and the operators refuse a GPU-less host with a
+  typed error instead of falling back (``net/kda.py:759-763``).
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from axiom_b200 import _lib
+from axiom_b200 import kda as K
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "kda_b200.h")
+
+
+def _declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(kda_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = _declared_functions()
+    assert names, "no declarations parsed from the header"
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared in kda_b200.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version_and_strerror():
+    lib = _lib.lib()
+    assert lib.kda_version() >= 100
+    assert lib.kda_strerror(0) == b"ok"
+    assert b"dimensions" in lib.kda_strerror(-1)
+
+
+def test_ckpt_elems():
+    lib = _lib.lib()
+    assert lib.kda_ckpt_elems(4, 8192, 32, 128, 128, 64) == 4 * 32 * 128 * 128 * 128
+    assert lib.kda_ckpt_elems(1, 100, 2, 16, 8, 64) == 1 * 2 * 2 * 16 * 8
+
+
+@pytest.mark.parametrize("dims", [
+    (1, 64, 1, 7, 64, 64),     # dk not a multiple of 8
+    (1, 64, 1, 64, 136, 64),   # dv too large
+    (1, 64, 1, 64, 64, 48),    # unsupported chunk
+    (-1, 64, 1, 64, 64, 64),   # negative batch
+])
+def test_fwd_rejects_bad_shapes_before_launch(dims):
+    lib = _lib.lib()
+    B, T, H, dk, dv, C = dims
+    rc = lib.kda_fwd(None, None, None, None, None, None, None, None, None,
+                     B, T, H, dk, dv, C, 1, 1, 1, None)
+    assert rc == -1
+
+
+def test_fwd_rejects_bad_dtype_and_null_pointers():
+    lib = _lib.lib()
+    assert lib.kda_fwd(*([None] * 9), 1, 64, 1, 64, 64, 64, 7, 1, 1, None) == -2
+    assert lib.kda_fwd(*([None] * 9), 1, 64, 1, 64, 64, 64, 1, 1, 1, None) == -4
+
+
+def test_bwd_validation():
+    lib = _lib.lib()
+    args = [None] * 14 + [None, 0]
+    assert lib.kda_bwd(*args, 1, 64, 1, 64, 64, 63, 1, 1, 1, None) == -1
+    assert lib.kda_bwd(*args, 1, 64, 1, 64, 64, 64, 1, 1, 1, None) == -4
+    fake = ctypes.c_void_p(16)
+    full = [fake] * 14 + [None, 0]
+    assert lib.kda_bwd(*full, 1, 64, 1, 64, 64, 64, 1, 1, 1, None) == -6  # workspace missing
+    assert lib.kda_bwd_workspace_bytes(1, 64, 1, 64, 64, 64, 1) > 0
+
+
+def test_decode_validation():
+    lib = _lib.lib()
+    assert lib.kda_decode(*([None] * 7), 4, 96, 128, 1, 1, None) == -1
+    assert lib.kda_decode(*([None] * 7), 4, 128, 128, 1, 1, None) == -4
+    assert lib.kda_decode(*([None] * 7), 0, 128, 128, 1, 1, None) == 0
+    odd = ctypes.c_void_p(8)
+    assert lib.kda_decode(odd, *([ctypes.c_void_p(16)] * 6), 4, 128, 128, 1, 1, None) == -3
+
+
+def test_impl_switch_fails_closed(monkeypatch):
+    monkeypatch.setenv("AXIOM_KDA_CC_IMPL", "b200")
+    assert K.kda_cc_impl() == "b200"
+    monkeypatch.setenv("AXIOM_KDA_CC_IMPL", "jax")
+    assert K.kda_cc_impl() == "jax"
+    monkeypatch.setenv("AXIOM_KDA_CC_IMPL", "triton")
+    with pytest.raises(ValueError):
+        K.kda_cc_impl()
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the GPU-less refusal")
+def test_operators_refuse_a_gpu_less_host():
+    x = torch.zeros(1, 64, 1, 64)
+    with pytest.raises(RuntimeError, match="no CPU"):
+        K.kda_fwd(x, x, x, x, torch.zeros(1, 64, 1))
+    with pytest.raises(RuntimeError, match="no CPU"):
+        K.decode_step(torch.zeros(2, 64, 64), *([torch.zeros(2, 64)] * 4), torch.zeros(2))
+
+
+def test_missing_library_raises(monkeypatch):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", os.path.join(ROOT, "does_not_exist.so"))
+    with pytest.raises(RuntimeError, match="not built"):
+        _lib.lib()

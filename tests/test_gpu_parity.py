@@ -1,0 +1,187 @@
+"""GPU parity of the KDA kernels against the CPU oracle and the reference goldens.
+
+Tolerances (scale-relative ``max|x - ref| / max|ref|``, the reference's
+convention ``net/tests/test_kda_cc_fused_bwd.py:88-106``):
+* fp32 inputs: <= 1e-4 on O and the final state, and on every gradient;
+* bf16 inputs with an fp32 state: <= 1e-2 on O, the final state and every
+  gradient, against the oracle evaluated on the same bf16-rounded inputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import kda_oracle as K
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32 = 1e-4
+TOL_BF16 = 1e-2
+GRADS = ["dq", "dk", "dv", "dg", "dbeta", "dS0"]
+
+
+def _dev(x, dtype=torch.float32):
+    return torch.as_tensor(np.ascontiguousarray(x), dtype=torch.float32).to("cuda").to(dtype).contiguous()
+
+
+def _np(x):
+    return x.detach().float().cpu().numpy()
+
+
+def _rounded(x, dtype):
+    return {k: (K.bf16_round(v) if dtype == torch.bfloat16 and k != "S0" else v) for k, v in x.items()}
+
+
+def _run_fwd_bwd(x, do, dST, chunk, dtype):
+    from axiom_b200 import kda_bwd, kda_fwd
+
+    q, k, v, g, beta = (_dev(x[n], dtype) for n in ("q", "k", "v", "g", "beta"))
+    S0 = _dev(x["S0"])
+    o, s_t, ckpt = kda_fwd(q, k, v, g, beta, S0, chunk=chunk, o_dtype=torch.float32, need_ckpt=True)
+    res = None
+    if do is not None:
+        res = kda_bwd(q, k, v, g, beta, ckpt, _dev(do, dtype), _dev(dST), chunk=chunk)
+    torch.cuda.synchronize()
+    return _np(o), _np(s_t), (None if res is None else [_np(r) for r in res])
+
+
+# ---------------------------------------------------------------------------
+# decode
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dk,dv", [(128, 128), (64, 128), (128, 64), (64, 64)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_step_matches_recurrence(dk, dv, dtype):
+    from axiom_b200 import decode_step
+
+    x = K.make_inputs(8, 3, 4, dk, dv, seed=dk + dv, s0_std=0.02)
+    xr = _rounded(x, dtype)
+    S = _dev(x["S0"])
+    s_ref = x["S0"].astype(np.float64)
+    for t in range(3):
+        args = [_dev(x[n][:, t], dtype) for n in ("q", "k", "v", "g", "beta")]
+        o = decode_step(S, *args, o_dtype=torch.float32)
+        o_ref, s_ref = K.decode_step(s_ref, *(xr[n][:, t] for n in ("q", "k", "v", "g", "beta")))
+        assert K.scale_rel_err(_np(o), o_ref) <= 1e-5
+    assert K.scale_rel_err(_np(S), s_ref) <= 1e-5
+
+
+def test_decode_many_states_in_place():
+    """cfg4-shaped step at reduced batch: 64 sequences x 32 heads, fp32 state."""
+    from axiom_b200 import decode_step
+
+    x = K.make_inputs(64, 1, 32, 128, 128, seed=11, s0_std=0.02)
+    xr = _rounded(x, torch.bfloat16)
+    S = _dev(x["S0"])
+    o = decode_step(S, *(_dev(x[n][:, 0], torch.bfloat16) for n in ("q", "k", "v", "g", "beta")))
+    o_ref, s_ref = K.decode_step(x["S0"], *(xr[n][:, 0] for n in ("q", "k", "v", "g", "beta")))
+    assert K.scale_rel_err(_np(S), s_ref) <= 1e-5
+    assert K.scale_rel_err(_np(o), o_ref) <= TOL_BF16
+
+
+# ---------------------------------------------------------------------------
+# forward / backward against the reference goldens (fp32)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("case", ["chunk_a", "chunk_b", "chunk_c", "scan_a", "scan_b", "scan_c", "scan_d"])
+def test_forward_matches_reference_golden(golden, case):
+    d = golden[case]
+    o, s, _ = _run_fwd_bwd(d, None, None, int(d["chunk"]), torch.float32)
+    assert K.scale_rel_err(o, d["o"]) <= TOL_F32
+    assert K.scale_rel_err(s, d["S_T"]) <= TOL_F32
+
+
+@pytest.mark.parametrize("case", ["bwd_chunk", "bwd_scan", "bwd_scan_strong", "bwd_scan_medium"])
+def test_backward_matches_reference_golden(golden, case):
+    d = golden[case]
+    _, _, grads = _run_fwd_bwd(d, d["do"], d["dST"], int(d["chunk"]), torch.float32)
+    for name, gr in zip(GRADS, grads):
+        assert K.scale_rel_err(gr, d[name]) <= TOL_F32, name
+
+
+# ---------------------------------------------------------------------------
+# BASELINE config 1 (fp32) and small bf16 configs against the oracle
+# ---------------------------------------------------------------------------
+
+
+def test_config1_fp32_forward_matches_oracle_and_recurrence():
+    """B=1, T=512, H=4, dk=dv=64, C=64, fp32, zero S0."""
+    x = K.make_inputs(1, 512, 4, 64, 64, seed=0)
+    o, s, _ = _run_fwd_bwd(x, None, None, 64, torch.float32)
+    o_c, s_c = K.chunk_fwd(x["q"], x["k"], x["v"], x["g"], x["beta"], x["S0"], chunk=64)
+    o_r, s_r = K.recurrent(x["q"], x["k"], x["v"], x["g"], x["beta"], x["S0"])
+    assert K.scale_rel_err(o, o_c) <= TOL_F32 and K.scale_rel_err(s, s_c) <= TOL_F32
+    assert K.scale_rel_err(o, o_r) <= TOL_F32 and K.scale_rel_err(s, s_r) <= TOL_F32
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, TOL_F32), (torch.bfloat16, TOL_BF16)])
+@pytest.mark.parametrize("shape", [(2, 192, 2, 64, 64, 64), (1, 130, 2, 32, 16, 32),
+                                   (1, 100, 1, 128, 128, 64), (2, 40, 3, 16, 24, 16)])
+def test_forward_backward_match_oracle(dtype, tol, shape):
+    B, T, H, dk, dv, C = shape
+    x = K.make_inputs(B, T, H, dk, dv, seed=T + dk, s0_std=0.1)
+    rng = np.random.default_rng(T)
+    do = rng.standard_normal((B, T, H, dv)).astype(np.float32)
+    dST = rng.standard_normal((B, H, dk, dv)).astype(np.float32)
+    o, s, grads = _run_fwd_bwd(x, do, dST, C, dtype)
+    xr = _rounded(x, dtype)
+    dor = K.bf16_round(do) if dtype == torch.bfloat16 else do
+    o_ref, s_ref = K.chunk_fwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], chunk=C)
+    assert K.scale_rel_err(o, o_ref) <= tol
+    assert K.scale_rel_err(s, s_ref) <= tol
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], dor, dST, chunk=C)
+    for name, gr, rf in zip(GRADS, grads, ref):
+        assert K.scale_rel_err(gr, rf) <= tol, name
+
+
+@pytest.mark.parametrize("T", [1, 5, 63, 65])
+def test_short_and_ragged_sequences(T):
+    x = K.make_inputs(1, T, 2, 64, 64, seed=T, s0_std=0.1, decay="strong")
+    o, s, _ = _run_fwd_bwd(x, None, None, 64, torch.float32)
+    o_r, s_r = K.recurrent(x["q"], x["k"], x["v"], x["g"], x["beta"], x["S0"])
+    assert o.shape == o_r.shape
+    assert K.scale_rel_err(o, o_r) <= TOL_F32 and K.scale_rel_err(s, s_r) <= TOL_F32
+
+
+def test_empty_sequence_passes_state_through():
+    from axiom_b200 import kda_fwd
+
+    z = torch.zeros(1, 0, 2, 64, device="cuda")
+    S0 = torch.randn(1, 2, 64, 64, device="cuda")
+    o, s, _ = kda_fwd(z, z, z, z, torch.zeros(1, 0, 2, device="cuda"), S0)
+    assert o.shape == (1, 0, 2, 64)
+    assert torch.equal(s, S0)
+
+
+def test_operand_form_kernel_and_cc_scan(golden):
+    """The reference's (q, k, v, alpha, beta32, S) form through ``kernel``/``cc_scan``."""
+    from axiom_b200 import cc_scan, kernel
+
+    d = golden["bwd_scan"]
+    T, H, dk = d["q"].shape[1:]
+    dv = d["v"].shape[-1]
+    C = int(d["chunk"])
+    q = _dev(d["q"].reshape(T, H * dk)).requires_grad_()
+    k = _dev(d["k"].reshape(T, H * dk)).requires_grad_()
+    v = _dev(d["v"].reshape(T, H * dv)).requires_grad_()
+    alpha = _dev(np.exp(d["g"]).reshape(T, H * dk)).requires_grad_()
+    b32 = np.broadcast_to(d["beta"].reshape(T, H, 1), (T, H, 32)).reshape(T, H * 32)
+    beta32 = _dev(b32).requires_grad_()
+    S = _dev(d["S0"][0]).requires_grad_()
+    o, s_t = kernel(q, k, v, alpha, beta32, S, chunk=C)
+    o_ref, s_ref = K.chunk_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], chunk=C)
+    assert K.scale_rel_err(_np(o), o_ref.reshape(T, -1)) <= TOL_F32
+    o2, s2 = cc_scan(q, k, v, alpha, beta32, S, 16, C)
+    (o2 * _dev(d["do"].reshape(T, -1))).sum().backward(retain_graph=True)
+    (s2 * _dev(d["dST"][0])).sum().backward()
+    assert K.scale_rel_err(_np(q.grad), d["dq"].reshape(T, -1)) <= TOL_F32
+    assert K.scale_rel_err(_np(v.grad), d["dv"].reshape(T, -1)) <= TOL_F32
+    dalpha_ref = d["dg"].reshape(T, -1) / np.exp(d["g"]).reshape(T, -1)
+    assert K.scale_rel_err(_np(alpha.grad), dalpha_ref) <= TOL_F32
+    dbeta_ref = np.repeat(d["dbeta"].reshape(T, H, 1) / 32.0, 32, axis=2).reshape(T, -1)
+    assert K.scale_rel_err(_np(beta32.grad), dbeta_ref) <= TOL_F32
+    assert K.scale_rel_err(_np(S.grad), d["dS0"][0]) <= TOL_F32
+    with pytest.raises(ValueError, match="multiple of the chunk"):
+        kernel(q[:T - 1], k[:T - 1], v[:T - 1], alpha[:T - 1], beta32[:T - 1], S, chunk=C)
