@@ -12,6 +12,10 @@ size_t simt_bwd_workspace_bytes(int B, int H, int dk, int dv, int C);
 int simt_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                     const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
                     int dk, int dv, int C, int in_dt, int o_dt, int ck_dt, cudaStream_t st);
+bool tc_fwd_supported(int dk, int dv, int C_, int in_dt);
+int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                  const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
+                  int o_dt, int ck_dt, cudaStream_t st);
 int simt_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                     const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                     void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T,
@@ -76,6 +80,14 @@ int kda_fwd(const void* q, const void* k, const void* v, const void* g, const vo
     return KDA_OK;
   }
   if (!q || !k || !v || !g || !beta || !o) return KDA_ERR_NULL;
+  if (kda::tc_fwd_supported(dk, dv, chunk, in_dtype)) {
+    if (!kda::aligned16(q) || !kda::aligned16(k) || !kda::aligned16(v) || !kda::aligned16(g) ||
+        !kda::aligned16(o) || (s_ckpt && !kda::aligned16(s_ckpt)) || (s_out && !kda::aligned16(s_out)) ||
+        (s0 && !kda::aligned16(s0)))
+      return KDA_ERR_ALIGN;
+    return kda::tc_fwd_launch(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, o_dtype, ckpt_dtype,
+                              stream);
+  }
   return kda::simt_fwd_launch(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, dk, dv, chunk,
                               in_dtype, o_dtype, ckpt_dtype, stream);
 }

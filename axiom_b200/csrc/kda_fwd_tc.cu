@@ -1,0 +1,587 @@
+// Tensor-core (tcgen05) chunked KDA forward for bf16 inputs, dk = dv = 128,
+// chunk C = 64.  One CTA per (batch, head) walks the sequence chunk by chunk;
+// the fp32 state S (128 x 128) lives in TMEM for the whole sequence.
+//
+// Per chunk (the reference's chunked_cc body, net/kda.py:669-702, with the
+// products regrouped so that every tensor-core product is an M = 128 MMA):
+//   G = cumsum(g), Gam = exp(G), Gi = exp(-G), lam = exp(G_C - G)
+//   MMA_sc : [Q*Gam ; K*Gam] (K*Gi)^T          -> Aqk (rows 0-63), Akk (64-127)
+//            (single anchor at the chunk start; valid while max|G_C| <= 80,
+//             else the scores are evaluated exactly on the CUDA cores)
+//   solve  : T = (I + L)^-1, L = strict(beta_r Akk) (fp32, blocked substitution)
+//            P = Aqk T
+//   MMA_wu : [T diag(beta) ; P diag(beta)] [K*Gam | V]
+//            -> W = T(beta Gam K), U = T(beta V), Aqk W, Aqk U
+//   Q~ = Gam*Q - Aqk W                       (so that O = Q~ S + Aqk U)
+//   MMA_1  : [W ; Q~] S_bf16                 -> W S (rows 0-63), Q~ S (64-127)
+//   v~ = U - W S ;  O = Q~ S + Aqk U
+//   MMA_3  : S <- Gam_C * S + (lam K)^T v~   (accumulated in TMEM)
+// The chunk-boundary state (bf16 or fp32) is written for the backward.
+#include "kda_common.cuh"
+#include "kda_tc.cuh"
+
+namespace kda {
+namespace {
+
+using namespace tc;
+
+constexpr int C = 64, DK = 128, DV = 128, NT = 256;
+constexpr float kExpBudget = 80.f;  // the reference's COL_EXP_BUDGET
+
+// shared-memory map (bytes)
+constexpr int OFF_SQ = 0;                       // staging q   CM[64][128]
+constexpr int OFF_SK = OFF_SQ + 16384;          // staging k
+constexpr int OFF_SG = OFF_SK + 16384;          // staging g
+constexpr int OFF_V = OFF_SG + 16384;           // v (operand) CM[64][128]
+constexpr int OFF_A3 = OFF_V + 16384;           // [W ; Q~ ; K*Gam] CM[192][128]
+constexpr int OFF_KI = OFF_A3 + 49152;          // K*Gi CM[64][128]   | T fp32 | G fp32 (slow)
+constexpr int OFF_TP = OFF_KI + 16384;          // [T b ; P b] CM[128][64]    | G fp32 (slow)
+constexpr int OFF_KL = OFF_TP + 16384;          // lam*K CM[64][128]
+constexpr int OFF_SB = OFF_KL + 16384;          // S bf16 CM[128][128] | Aqk fp32 + L fp32
+constexpr int OFF_VT = OFF_SB + 32768;          // v~ CM[64][128]      | cumsum partials
+constexpr int OFF_BETA = OFF_VT + 16384;        // beta fp32[64]
+constexpr int OFF_GC = OFF_BETA + 256;          // Gam_C fp32[128]
+constexpr int OFF_BAR = OFF_GC + 512;           // mbarrier + tmem slot
+constexpr int SMEM_BYTES = OFF_BAR + 64;
+
+// fp32 64x64 matrices with a 16-byte-chunk XOR swizzle (conflict-free row writes)
+__device__ __forceinline__ int sw64(int r, int c) {
+  return (r << 6) + ((((c >> 2) ^ (r & 15)) << 2) | (c & 3));
+}
+
+__device__ __forceinline__ uint4 ld16(const unsigned char* base, uint32_t off) {
+  return *reinterpret_cast<const uint4*>(base + off);
+}
+__device__ __forceinline__ void st16(unsigned char* base, uint32_t off, uint4 v) {
+  *reinterpret_cast<uint4*>(base + off) = v;
+}
+
+template <typename To>
+__device__ __forceinline__ void store_row32(To* dst, const float* v);
+template <>
+__device__ __forceinline__ void store_row32<float>(float* dst, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+}
+template <>
+__device__ __forceinline__ void store_row32<bf16>(bf16* dst, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = pack_bf16x8(v + j);
+}
+
+// Issue the cp.async copies of one chunk's q, k, g (qkg = true) or v into CM tiles.
+__device__ __forceinline__ void stage_chunk(unsigned char* sm, const bf16* q, const bf16* k,
+                                            const bf16* g, const bf16* v, size_t row0, int rows_valid,
+                                            int H, bool qkg) {
+  const int tid = threadIdx.x;
+  const size_t rstride = static_cast<size_t>(H) * DK;  // elements between tokens
+  if (qkg) {
+    for (int i = tid; i < 3 * C * 16; i += NT) {
+      const int which = i / (C * 16), rem = i % (C * 16), r = rem >> 4, cg = rem & 15;
+      const bf16* src = which == 0 ? q : (which == 1 ? k : g);
+      const bool ok = r < rows_valid;
+      const bf16* p = ok ? src + (row0 + r) * rstride + cg * 8 : src;
+      cp_async16(sm + (which == 0 ? OFF_SQ : which == 1 ? OFF_SK : OFF_SG) + cm_off(r, cg * 8, DK), p, ok);
+    }
+  } else {
+    for (int i = tid; i < C * 16; i += NT) {
+      const int r = i >> 4, cg = i & 15;
+      const bool ok = r < rows_valid;
+      const bf16* p = ok ? v + (row0 + r) * rstride + cg * 8 : v;
+      cp_async16(sm + OFF_V + cm_off(r, cg * 8, DV), p, ok);
+    }
+  }
+  cp_async_commit();
+}
+
+template <typename To, typename Tc>
+__global__ void __launch_bounds__(NT, 1)
+fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+              const bf16* __restrict__ g, const bf16* __restrict__ beta,
+              const float* __restrict__ s0, To* __restrict__ o, float* __restrict__ s_out,
+              Tc* __restrict__ s_ckpt, int T, int H, int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  float* beta_s = reinterpret_cast<float*>(sm + OFF_BETA);
+  float* gamC = reinterpret_cast<float*>(sm + OFF_GC);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qw = warp & 3, hh = warp >> 2;  // TMEM lane quarter, column half
+  const int h = blockIdx.x % H, b = blockIdx.x / H;
+  const int n_chunks = (T + C - 1) / C;
+  const size_t tok0 = static_cast<size_t>(b) * T;   // first token row of this sequence
+  const size_t head_off = static_cast<size_t>(h) * DK;
+  const bf16* qh = q + head_off;
+  const bf16* kh = k + head_off;
+  const bf16* gh = g + head_off;
+  const bf16* vh = v + static_cast<size_t>(h) * DV;
+
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  // stage chunk 0
+  stage_chunk(sm, qh, kh, gh, vh, tok0, min(C, T), H, true);
+  stage_chunk(sm, qh, kh, gh, vh, tok0, min(C, T), H, false);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t t_lane = static_cast<uint32_t>(32 * qw) << 16;
+  const uint32_t T_D = tbase;          // cols [0, 256): MMA results
+  const uint32_t T_S = tbase + 256;    // cols [256, 384): the state
+  uint32_t phase = 0;
+  bool failed = false;
+
+  // S0 -> TMEM (row d = lane, 64 columns per warp)
+  {
+    const int d = 32 * qw + lane;
+    const size_t sb = ((static_cast<size_t>(b) * H + h) * DK + d) * DV;
+    for (int half = 0; half < 2; ++half) {
+      float vals[32];
+      const int c0 = hh * 64 + half * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) vals[j] = s0 ? s0[sb + c0 + j] : 0.f;
+      tmem_st32(T_S + t_lane + c0, vals);
+    }
+    tmem_wait_st();
+  }
+
+  auto mma_wait = [&]() -> bool {
+    const bool ok = mbar_wait(mbar, phase);
+    phase ^= 1u;
+    tc_fence_after();
+    return ok;
+  };
+
+  unsigned char* A3 = sm + OFF_A3;
+  const uint32_t a3_addr = smem_u32(A3);
+
+  for (int c = 0; c < n_chunks; ++c) {
+    const int t0 = c * C;
+    const int rows_valid = min(C, T - t0);
+    cp_async_wait<0>();
+    if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
+    __syncthreads();
+
+    // ---------------- prep: G, exponentials, operand tiles ----------------
+    const int cg = tid & 15, rg4 = tid >> 4;   // channels 8cg..8cg+7, rows 4rg4..4rg4+3
+    float G[4][8];
+    {
+      float* part = reinterpret_cast<float*>(sm + OFF_VT);  // [16][16][8]
+      float run[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) run[e] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float gv[8];
+        unpack_bf16x8(ld16(sm + OFF_SG, cm_off(4 * rg4 + i, 8 * cg, DK)), gv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { run[e] += gv[e]; G[i][e] = run[e]; }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part[(rg4 * 16 + cg) * 8 + e] = run[e];
+      __syncthreads();
+      float pre[8], tot[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) { pre[e] = 0.f; tot[e] = 0.f; }
+      for (int p = 0; p < 16; ++p) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x = part[(p * 16 + cg) * 8 + e];
+          tot[e] += x;
+          if (p < rg4) pre[e] += x;
+        }
+      }
+      bool strong = false;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        strong |= fabsf(tot[e]) > kExpBudget;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) G[i][e] += pre[e];
+      }
+      if (rg4 == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) gamC[8 * cg + e] = __expf(tot[e]);
+      }
+      // one barrier: publishes gamC and decides the path for the whole CTA
+      const bool slow = __syncthreads_or(strong) != 0;
+      float gc_e[8], gce[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) { gc_e[e] = tot[e]; gce[e] = __expf(tot[e]); }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 4 * rg4 + i;
+        float qv[8], kv[8], qg[8], kg[8], ki[8], kl[8];
+        unpack_bf16x8(ld16(sm + OFF_SQ, cm_off(r, 8 * cg, DK)), qv);
+        unpack_bf16x8(ld16(sm + OFF_SK, cm_off(r, 8 * cg, DK)), kv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float gam = __expf(G[i][e]);
+          qg[e] = qv[e] * gam;
+          kg[e] = kv[e] * gam;
+          if (!slow) {
+            const float gi = __expf(-G[i][e]);
+            ki[e] = kv[e] * gi;
+            kl[e] = kv[e] * (gi * gce[e]);
+          } else {
+            ki[e] = 0.f;
+            kl[e] = kv[e] * __expf(fminf(gc_e[e] - G[i][e], 0.f));
+          }
+        }
+        st16(A3, cm_off(64 + r, 8 * cg, DK), pack_bf16x8(qg));
+        st16(A3, cm_off(128 + r, 8 * cg, DK), pack_bf16x8(kg));
+        if (!slow) st16(sm + OFF_KI, cm_off(r, 8 * cg, DK), pack_bf16x8(ki));
+        st16(sm + OFF_KL, cm_off(r, 8 * cg, DK), pack_bf16x8(kl));
+      }
+      float* Aq = reinterpret_cast<float*>(sm + OFF_SB);
+      float* Lm = Aq + 4096;
+      if (!slow) {
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+          tc_fence_after();
+          const uint32_t idesc = idesc_bf16(128, 64, false, false);
+#pragma unroll
+          for (int ks = 0; ks < DK / 16; ++ks)
+            mma_bf16(T_D, desc_kmajor(a3_addr + 64 * 256 + ks * 256, DK),
+                     desc_kmajor(smem_u32(sm + OFF_KI) + ks * 256, DK), idesc, ks > 0);
+          mma_commit(mbar);
+        }
+        // prefetch the next chunk's q, k, g (staging is free)
+        if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, true);
+        failed |= !mma_wait();
+        if (__syncthreads_or(failed)) break;
+        // E1: scores -> Aqk (masked, fp32) and L = strict(beta_r Akk)
+        {
+          float vals[32];
+          tmem_ld32(T_D + t_lane + hh * 32, vals);
+          tmem_wait_ld();
+          const int R = 32 * qw + lane;
+          if (R < 64) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const int i0 = hh * 32 + j;
+              float4 w4;
+              w4.x = (i0 + 0 <= R) ? vals[j + 0] : 0.f;
+              w4.y = (i0 + 1 <= R) ? vals[j + 1] : 0.f;
+              w4.z = (i0 + 2 <= R) ? vals[j + 2] : 0.f;
+              w4.w = (i0 + 3 <= R) ? vals[j + 3] : 0.f;
+              *reinterpret_cast<float4*>(Aq + sw64(R, i0)) = w4;
+            }
+          } else {
+            const int r = R - 64;
+            const float br = beta_s[r];
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const int i0 = hh * 32 + j;
+              float4 w4;
+              w4.x = (i0 + 0 < r) ? br * vals[j + 0] : 0.f;
+              w4.y = (i0 + 1 < r) ? br * vals[j + 1] : 0.f;
+              w4.z = (i0 + 2 < r) ? br * vals[j + 2] : 0.f;
+              w4.w = (i0 + 3 < r) ? br * vals[j + 3] : 0.f;
+              *reinterpret_cast<float4*>(Lm + sw64(r, i0)) = w4;
+            }
+          }
+        }
+      } else {
+        // exact scores on the CUDA cores (strong decay: the single anchor would overflow)
+        float* Gf = reinterpret_cast<float*>(sm + OFF_KI);  // [64][128] fp32 across KI|TP
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) Gf[(4 * rg4 + i) * DK + 8 * cg + e] = G[i][e];
+        __syncthreads();
+        for (int idx = tid; idx < C * C; idx += NT) {
+          const int r = idx >> 6, i = idx & 63;
+          float a = 0.f, l = 0.f;
+          if (i <= r) {
+            for (int d8 = 0; d8 < DK; d8 += 8) {
+              float qr[8], kr[8], ki8[8];
+              unpack_bf16x8(ld16(sm + OFF_SQ, cm_off(r, d8, DK)), qr);
+              unpack_bf16x8(ld16(sm + OFF_SK, cm_off(r, d8, DK)), kr);
+              unpack_bf16x8(ld16(sm + OFF_SK, cm_off(i, d8, DK)), ki8);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float ex = __expf(fminf(Gf[r * DK + d8 + e] - Gf[i * DK + d8 + e], 0.f));
+                a += qr[e] * ki8[e] * ex;
+                l += kr[e] * ki8[e] * ex;
+              }
+            }
+          }
+          Aq[sw64(r, i)] = a;
+          Lm[sw64(r, i)] = (i < r) ? beta_s[r] * l : 0.f;
+        }
+        __syncthreads();
+        if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, true);
+      }
+    }
+    // ---------------- solve: T = (I + L)^-1 (blocked), P = Aqk T ----------------
+    {
+      float* Aq = reinterpret_cast<float*>(sm + OFF_SB);
+      float* Lm = Aq + 4096;
+      float* Tm = reinterpret_cast<float*>(sm + OFF_KI);
+      for (int idx = tid; idx < C * C; idx += NT) Tm[idx] = 0.f;  // swizzle is a permutation
+      __syncthreads();
+      if (tid < 64) {  // diagonal 16x16 blocks, one column per thread
+        const int bb = tid >> 4, j = tid & 15, o = 16 * bb;
+        float x[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float acc = (i == j) ? 1.f : 0.f;
+#pragma unroll
+          for (int m = 0; m < i; ++m) acc -= Lm[sw64(o + i, o + m)] * x[m];
+          x[i] = acc;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) Tm[sw64(o + i, o + j)] = x[i];
+      }
+      __syncthreads();
+      for (int dl = 1; dl < 4; ++dl) {  // off-diagonal blocks, by distance from the diagonal
+        const int nblk = 4 - dl;
+        float xs[3];
+        for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
+          const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+          const int bi = bj + dl;
+          float acc = 0.f;
+          for (int m = 16 * bj; m < 16 * bi; ++m) acc += Lm[sw64(16 * bi + r, m)] * Tm[sw64(m, 16 * bj + cc)];
+          xs[n] = acc;
+        }
+        __syncthreads();
+        for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
+          const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+          Tm[sw64(16 * (bj + dl) + r, 16 * bj + cc)] = xs[n];
+        }
+        __syncthreads();
+        for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
+          const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+          const int bi = bj + dl;
+          float acc = 0.f;
+#pragma unroll
+          for (int m = 0; m < 16; ++m)
+            acc -= Tm[sw64(16 * bi + r, 16 * bi + m)] * Tm[sw64(16 * bi + m, 16 * bj + cc)];
+          xs[n] = acc;
+        }
+        __syncthreads();
+        for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
+          const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+          Tm[sw64(16 * (bj + dl) + r, 16 * bj + cc)] = xs[n];
+        }
+        __syncthreads();
+      }
+      // P = Aqk T (row r, 16 columns per thread) and the [T b ; P b] bf16 operand
+      {
+        const int r = tid >> 2, c0 = (tid & 3) * 16;
+        float p[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) p[j] = 0.f;
+        for (int m = 0; m <= r; ++m) {
+          const float a = Aq[sw64(r, m)];
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            const float4 t4 = *reinterpret_cast<const float4*>(Tm + sw64(m, c0 + j));
+            p[j] += a * t4.x; p[j + 1] += a * t4.y; p[j + 2] += a * t4.z; p[j + 3] += a * t4.w;
+          }
+        }
+        unsigned char* TP = sm + OFF_TP;
+        float tv[16];
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          const float4 t4 = *reinterpret_cast<const float4*>(Tm + sw64(r, c0 + j));
+          tv[j] = t4.x; tv[j + 1] = t4.y; tv[j + 2] = t4.z; tv[j + 3] = t4.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float bc = beta_s[c0 + j];
+          p[j] *= bc;
+          tv[j] *= bc;
+        }
+        __syncthreads();  // TP aliases the slow path's G; all reads of it are done
+        st16(TP, cm_off(r, c0, C), pack_bf16x8(tv));
+        st16(TP, cm_off(r, c0 + 8, C), pack_bf16x8(tv + 8));
+        st16(TP, cm_off(64 + r, c0, C), pack_bf16x8(p));
+        st16(TP, cm_off(64 + r, c0 + 8, C), pack_bf16x8(p + 8));
+      }
+    }
+    fence_async_smem();
+    __syncthreads();
+    // ---------------- MMA_wu: [Tb ; Pb] [K*Gam | V] ----------------
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16(128, 128, false, true);
+      const uint32_t tp = smem_u32(sm + OFF_TP);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks) {
+        const uint64_t ad = desc_kmajor(tp + ks * 256, C);
+        mma_bf16(T_D, ad, desc_mnmajor(a3_addr + 128 * 256 + ks * 4096, DK), idesc, ks > 0);
+        mma_bf16(T_D + 128, ad, desc_mnmajor(smem_u32(sm + OFF_V) + ks * 4096, DV), idesc, ks > 0);
+      }
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, false);
+    // ---------------- E2: W -> A3[0:64), Q~ = Gam Q - Aqk W -> A3[64:128) ----------------
+    {
+      const int R = 32 * qw + lane;
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float vals[32];
+        tmem_ld32(T_D + t_lane + c0, vals);
+        tmem_wait_ld();
+        if (R < 64) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) st16(A3, cm_off(R, c0 + j, DK), pack_bf16x8(vals + j));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float qg[8];
+            const uint32_t off = cm_off(R, c0 + j, DK);  // rows 64..127 of A3 hold Gam*Q
+            unpack_bf16x8(ld16(A3, off), qg);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qg[e] -= vals[j + e];
+            st16(A3, off, pack_bf16x8(qg));
+          }
+        }
+      }
+    }
+    // ---------------- S pass: S_c -> bf16 operand (+ checkpoint), S *= Gam_C ----------------
+    {
+      const int d = 32 * qw + lane;
+      const float gcd = gamC[d];
+      Tc* ck = s_ckpt ? s_ckpt + ((static_cast<size_t>(b) * H + h) * n_chunks + c) * (DK * DV) + d * DV : nullptr;
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float vals[32];
+        tmem_ld32(T_S + t_lane + c0, vals);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) st16(sm + OFF_SB, cm_off(d, c0 + j, DV), pack_bf16x8(vals + j));
+        if (ck) store_row32<Tc>(ck + c0, vals);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) vals[j] *= gcd;
+        tmem_st32(T_S + t_lane + c0, vals);
+      }
+      tmem_wait_st();
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---------------- MMA_1: [W ; Q~] S ----------------
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16(128, 128, false, true);
+      const uint32_t sb = smem_u32(sm + OFF_SB);
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks)
+        mma_bf16(T_D, desc_kmajor(a3_addr + ks * 256, DK), desc_mnmajor(sb + ks * 4096, DV), idesc, ks > 0);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    // ---------------- E3: v~ = U - W S -> bf16 ; O = Q~ S + Aqk U -> global ----------------
+    {
+      const int R = 32 * qw + lane;
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float ws[32], u[32];
+        tmem_ld32(T_D + t_lane + c0, ws);
+        tmem_ld32(T_D + t_lane + 128 + c0, u);
+        tmem_wait_ld();
+        if (R < 64) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) u[j] -= ws[j];
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) st16(sm + OFF_VT, cm_off(R, c0 + j, DV), pack_bf16x8(u + j));
+        } else {
+          const int r = R - 64;
+          if (r < rows_valid) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) u[j] += ws[j];
+            store_row32<To>(o + ((tok0 + t0 + r) * H + h) * DV + c0, u);
+          }
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---------------- MMA_3: S += (lam K)^T v~ ----------------
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16(128, 128, true, true);
+      const uint32_t kl = smem_u32(sm + OFF_KL), vt = smem_u32(sm + OFF_VT);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_S, desc_mnmajor(kl + ks * 4096, DK), desc_mnmajor(vt + ks * 4096, DV), idesc, 1u);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+  }
+
+  if (!failed && s_out) {
+    const int d = 32 * qw + lane;
+    float* so = s_out + ((static_cast<size_t>(b) * H + h) * DK + d) * DV;
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = hh * 64 + half * 32;
+      float vals[32];
+      tmem_ld32(T_S + t_lane + c0, vals);
+      tmem_wait_ld();
+      store_row32<float>(so + c0, vals);
+    }
+  }
+  if (failed && tid == 0 && err) atomicExch(err, 1);
+  cp_async_wait<0>();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, 512);
+}
+
+__device__ int g_fwd_tc_error = 0;
+
+template <typename To, typename Tc>
+int launch_t(const void* q, const void* k, const void* v, const void* g, const void* beta,
+             const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
+             cudaStream_t st) {
+  static bool done[64] = {false};
+  auto kern = fwd_tc_kernel<To, Tc>;
+  int rc = ensure_smem(kern, SMEM_BYTES, done);
+  if (rc != KDA_OK) return rc;
+  int* err = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_fwd_tc_error) != cudaSuccess) return KDA_ERR_LAUNCH;
+  kern<<<B * H, NT, SMEM_BYTES, st>>>(
+      static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v),
+      static_cast<const bf16*>(g), static_cast<const bf16*>(beta), s0, static_cast<To*>(o), s_out,
+      static_cast<Tc*>(s_ckpt), T, H, err);
+  return launch_status();
+}
+
+}  // namespace
+
+bool tc_fwd_supported(int dk, int dv, int C_, int in_dt) {
+  return dk == DK && dv == DV && C_ == C && in_dt == KDA_BF16;
+}
+
+int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                  const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
+                  int o_dt, int ck_dt, cudaStream_t st) {
+  if (static_cast<long long>(B) * H > 0x7fffffffLL) return KDA_ERR_SHAPE;
+  if (o_dt == KDA_BF16 && ck_dt == KDA_BF16) return launch_t<bf16, bf16>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, st);
+  if (o_dt == KDA_BF16 && ck_dt == KDA_F32) return launch_t<bf16, float>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, st);
+  if (o_dt == KDA_F32 && ck_dt == KDA_BF16) return launch_t<float, bf16>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, st);
+  if (o_dt == KDA_F32 && ck_dt == KDA_F32) return launch_t<float, float>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, st);
+  return KDA_ERR_DTYPE;
+}
+
+int tc_fwd_poll_error(int* value) {
+  return cudaMemcpyFromSymbol(value, g_fwd_tc_error, sizeof(int)) == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+}
+
+}  // namespace kda

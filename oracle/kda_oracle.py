@@ -65,7 +65,8 @@ def make_inputs(B, T, H, dk, dv, seed=0, s0_std=None, decay="baseline"):
     q, k ~ N(0,1) then L2-normalised per (token, head); v ~ N(0,1);
     beta = sigmoid(N(0,1)); g = logsigmoid(N(3,1)) per key channel
     (``decay="strong"``: g = -5 sigmoid(3 N(0,1)), the reference's
-    strong-decay test range ``net/tests/test_kda_chunked_cc.py:231``).
+    strong-decay test range ``net/tests/test_kda_chunked_cc.py:231``;
+    ``decay="medium"``: g = -sigmoid(2 N(0,1))).
     S0 ~ N(0, s0_std) or zeros.  Returns float32 arrays.
     """
     rng = np.random.default_rng(seed)
@@ -80,6 +81,8 @@ def make_inputs(B, T, H, dk, dv, seed=0, s0_std=None, decay="baseline"):
     elif decay == "strong":
         z = rng.standard_normal((B, T, H, dk))
         g = -5.0 / (1.0 + np.exp(-3.0 * z))
+    elif decay == "medium":
+        g = -1.0 / (1.0 + np.exp(-2.0 * rng.standard_normal((B, T, H, dk))))
     else:
         raise ValueError(f"unknown decay {decay!r}")
     if s0_std is None:

@@ -1,0 +1,86 @@
+"""GPU parity of the tensor-core path (bf16 inputs, dk = dv = 128, chunk 64).
+
+The oracle runs on the same bf16-rounded inputs in float64; the tolerance is
+the BASELINE bf16 bar, scale-relative 1e-2 on O, the final state, the
+chunk-boundary checkpoint and every gradient.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import kda_oracle as K
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+GRADS = ["dq", "dk", "dv", "dg", "dbeta", "dS0"]
+
+
+def _dev(x, dtype):
+    return torch.as_tensor(np.ascontiguousarray(x), dtype=torch.float32).cuda().to(dtype).contiguous()
+
+
+def _np(x):
+    return x.detach().float().cpu().numpy()
+
+
+def _bf16_inputs(B, T, H, seed, s0_std=None, decay="baseline"):
+    x = K.make_inputs(B, T, H, 128, 128, seed=seed, s0_std=s0_std, decay=decay)
+    xr = {k: (K.bf16_round(v) if k != "S0" else v) for k, v in x.items()}
+    dev = {k: _dev(v, torch.bfloat16 if k != "S0" else torch.float32) for k, v in x.items()}
+    return xr, dev
+
+
+@pytest.mark.parametrize("B,T,H,s0,decay", [
+    (2, 512, 4, 0.02, "baseline"),    # config-2 distributions at reduced size
+    (1, 200, 2, 0.1, "baseline"),     # ragged tail
+    (1, 5, 3, 0.1, "baseline"),       # shorter than one chunk
+    (1, 256, 2, 0.1, "strong"),       # strong decay: exact CUDA-core score path
+    (1, 320, 2, 0.0, "medium"),
+])
+def test_tc_forward_matches_oracle(B, T, H, s0, decay):
+    from axiom_b200 import kda_fwd
+
+    xr, d = _bf16_inputs(B, T, H, seed=T + H, s0_std=s0 if s0 else None, decay=decay)
+    S0 = d["S0"] if s0 else None
+    o, s_t, ckpt = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], S0, chunk=64,
+                           o_dtype=torch.float32, need_ckpt=True)
+    torch.cuda.synchronize()
+    o_ref, s_ref, states = K.chunk_fwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"],
+                                       xr["S0"] if s0 else None, chunk=64, return_states=True)
+    assert K.scale_rel_err(_np(o), o_ref) <= TOL
+    assert K.scale_rel_err(_np(s_t), s_ref) <= TOL
+    n = states.shape[2]
+    assert K.scale_rel_err(_np(ckpt).reshape(B, H, n, 128, 128), states) <= TOL
+
+
+def test_tc_forward_bf16_output_and_repeatability():
+    from axiom_b200 import kda_fwd
+
+    xr, d = _bf16_inputs(2, 384, 2, seed=3, s0_std=0.02)
+    o1, s1, _ = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"])
+    o2, s2, _ = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"])
+    torch.cuda.synchronize()
+    assert o1.dtype == torch.bfloat16
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)  # deterministic
+    o_ref, s_ref = K.chunk_fwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], chunk=64)
+    assert K.scale_rel_err(_np(o1), o_ref) <= TOL
+
+
+@pytest.mark.parametrize("T,decay", [(256, "baseline"), (130, "strong")])
+def test_tc_training_step_matches_oracle(T, decay):
+    from axiom_b200 import chunk_kda
+
+    B, H = 1, 2
+    xr, d = _bf16_inputs(B, T, H, seed=T, s0_std=0.05, decay=decay)
+    rng = np.random.default_rng(T)
+    do = K.bf16_round(rng.standard_normal((B, T, H, 128)))
+    dST = rng.standard_normal((B, H, 128, 128)).astype(np.float32)
+    leaves = {n: d[n].clone().requires_grad_() for n in ("q", "k", "v", "g", "beta", "S0")}
+    o, s_t = chunk_kda(*(leaves[n] for n in ("q", "k", "v", "g", "beta", "S0")))
+    (o.float() * _dev(do, torch.float32)).sum().backward(retain_graph=True)
+    (s_t * _dev(dST, torch.float32)).sum().backward()
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64)
+    for name, leaf, rf in zip(GRADS, ("q", "k", "v", "g", "beta", "S0"), ref):
+        assert K.scale_rel_err(_np(leaves[leaf].grad), rf) <= TOL, name
