@@ -1,0 +1,879 @@
+// Tensor-core (tcgen05) backward of the chunked KDA core for bf16 inputs,
+// dk = dv = 128, chunk C = 64.  The analytic adjoint is the reference's
+// (net/kernels/kda_cc_fused_bwd.py:117-239), run as two kernels:
+//
+// bwd_seq  -- one CTA per (batch, head), chunks in reverse.  Recomputes the
+//   chunk-local W, Gam*Q, lam*K and Aqk from the inputs and runs the state
+//   cotangent recurrence with dS' (fp32) resident in TMEM:
+//     dU^T = dS'^T (lam K)^T + dO^T Aqk                (the cotangent of U = v~)
+//     dS   = Gam_C dS' + (Gam Q)^T dO - W^T dU
+//   Before each chunk it stores that chunk's incoming dS' (bf16) for bwd_par.
+//
+// bwd_par  -- persistent over all (batch, head, chunk) units, no sequential
+//   dependency.  Recomputes the chunk (scores, T, W, U, v~ = U - W S_c from
+//   the forward's checkpoint S_c), then forms every gradient.  All large
+//   products are M = 128 MMAs whose results come out transposed (TMEM lane =
+//   key/value channel, column = chunk row), so the final reverse cumulative
+//   sum that gives dg runs inside one thread per channel:
+//     dU^T   = dS'^T (lam K)^T + dO^T Aqk
+//     dKL^T  = dS' v~^T                      (cotangent of lam*K)
+//     S [dO^T | dU^T]  -> (dO S^T)^T, (dU S^T)^T = -dW^T
+//     Yw^T = dW^T T,  Yu^T = dU^T T          (transposed UT-solve adjoints)
+//     dAqk = tril(dO v~^T),  dL = -strict(Yu U^T + Yw W^T)       (M = 64)
+//     [dQG^T | dKG^T] += KI^T [dAqk ; beta dL]^T,  dKI^T = QG^T dAqk + KG^T beta dL
+//   with QG = Gam Q, KG = Gam K, KI = K exp(-G), KL = lam K, then
+//     dq = dQG Gam,  dk = dKG Gam + dKI Gi + dKL lam,  dv = beta Yu,
+//     dG = dQG QG + dKG KG - dKI KI - dKL KL,  dg = revcumsum(dG) + dG_C,
+//     dbeta = rowsum(Yu v) + rowsum(Yw KG) + rowsum(dL Akk).
+// Chunks whose decay exceeds the single-anchor budget take the exact
+// CUDA-core path for the score products and their adjoints.
+#include "kda_chunk.cuh"
+
+namespace kda {
+namespace {
+
+using namespace tc;
+using namespace chunk;
+
+__device__ __forceinline__ uint32_t lane_off(int qw) { return static_cast<uint32_t>(32 * qw) << 16; }
+
+// ===========================================================================
+// bwd_seq
+// ===========================================================================
+constexpr int Q_SQ = 0, Q_SK = 16384, Q_SG = 32768, Q_DO = 49152;
+constexpr int Q_A3 = 65536;              // [-W ; Gam Q ; Gam K] CM[192][128]
+constexpr int Q_KI = Q_A3 + 49152;       // K Gi            | T fp32 | G fp32 (slow, with TP)
+constexpr int Q_TP = Q_KI + 16384;       // T beta [64][64] | dU^T [128][64] | prep partials
+constexpr int Q_KL = Q_TP + 16384;       // lam K
+constexpr int Q_SB = Q_KL + 16384;       // dS' bf16 [128][128] | Aqk + Akk fp32
+constexpr int Q_AQB = Q_SB + 32768;      // Aqk bf16 [64][64]
+constexpr int Q_BETA = Q_AQB + 8192;
+constexpr int Q_GC = Q_BETA + 256;
+constexpr int Q_BAR = Q_GC + 512;
+constexpr int SEQ_SMEM = Q_BAR + 64;
+
+__global__ void __launch_bounds__(NT, 1)
+bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ g,
+               const bf16* __restrict__ beta, const bf16* __restrict__ dout,
+               const float* __restrict__ dsT, float* __restrict__ ds0, bf16* __restrict__ dsw,
+               int T, int H, int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  float* beta_s = reinterpret_cast<float*>(sm + Q_BETA);
+  float* gamC = reinterpret_cast<float*>(sm + Q_GC);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + Q_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + Q_BAR + 8);
+  unsigned char* A3 = sm + Q_A3;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qw = warp & 3, hh = warp >> 2;
+  const int h = blockIdx.x % H, b = blockIdx.x / H;
+  const int n_chunks = (T + C - 1) / C;
+  const size_t tok0 = static_cast<size_t>(b) * T;
+  const size_t rstride = static_cast<size_t>(H) * DK;
+  const bf16* qh = q + static_cast<size_t>(h) * DK;
+  const bf16* kh = k + static_cast<size_t>(h) * DK;
+  const bf16* gh = g + static_cast<size_t>(h) * DK;
+  const bf16* doh = dout + static_cast<size_t>(h) * DV;
+  const size_t unit = static_cast<size_t>(b) * H + h;
+
+  if (tid == 0) { mbar_init(mbar, 1); mbar_fence_init(); }
+  if (warp == 0) { tmem_alloc(tslot, 512); tmem_relinquish(); }
+  {
+    const int c = n_chunks - 1, t0 = c * C, rv = min(C, T - t0);
+    stage_tile(sm + Q_SQ, qh + (tok0 + t0) * rstride, rv, rstride);
+    stage_tile(sm + Q_SK, kh + (tok0 + t0) * rstride, rv, rstride);
+    stage_tile(sm + Q_SG, gh + (tok0 + t0) * rstride, rv, rstride);
+    stage_tile(sm + Q_DO, doh + (tok0 + t0) * rstride, rv, rstride);
+    cp_async_commit();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t T_DS = tbase, T_SC = tbase + 128, T_W = tbase + 256, T_U = tbase + 384;
+  const uint32_t tl = lane_off(qw);
+  uint32_t phase = 0;
+  bool failed = false;
+  auto mma_wait = [&]() -> bool {
+    const bool ok = mbar_wait(mbar, phase);
+    phase ^= 1u;
+    tc_fence_after();
+    return ok;
+  };
+  {  // dS_T -> TMEM
+    const int d = 32 * qw + lane;
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = hh * 64 + half * 32;
+      float vals[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) vals[j] = dsT ? dsT[(unit * DK + d) * DV + c0 + j] : 0.f;
+      tmem_st32(T_DS + tl + c0, vals);
+    }
+    tmem_wait_st();
+  }
+  const uint32_t a3 = smem_u32(A3);
+  float* Aq = reinterpret_cast<float*>(sm + Q_SB);
+  float* Akk = Aq + 4096;
+
+  for (int c = n_chunks - 1; c >= 0; --c) {
+    const int t0 = c * C, rows_valid = min(C, T - t0);
+    cp_async_wait<0>();
+    if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
+    __syncthreads();
+    float G[4][8];
+    const bool slow = prep(sm + Q_SQ, sm + Q_SK, sm + Q_SG, A3 + cm_off(64, 0, DK),
+                           A3 + cm_off(128, 0, DK), sm + Q_KI, sm + Q_KL,
+                           reinterpret_cast<float*>(sm + Q_TP), gamC, G);
+    const bool more = c > 0;
+    const int tp0 = (c - 1) * C;
+    if (!slow) {
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t id = idesc_bf16(128, 64, false, false);
+#pragma unroll
+        for (int ks = 0; ks < DK / 16; ++ks)
+          mma_bf16(T_SC, desc_kmajor(a3 + 64 * 256 + ks * 256, DK),
+                   desc_kmajor(smem_u32(sm + Q_KI) + ks * 256, DK), id, ks > 0);
+        mma_commit(mbar);
+      }
+      if (more) {
+        stage_tile(sm + Q_SQ, qh + (tok0 + tp0) * rstride, C, rstride);
+        stage_tile(sm + Q_SK, kh + (tok0 + tp0) * rstride, C, rstride);
+        stage_tile(sm + Q_SG, gh + (tok0 + tp0) * rstride, C, rstride);
+        cp_async_commit();
+      }
+      failed |= !mma_wait();
+      if (__syncthreads_or(failed)) break;
+      scores_epilogue(T_SC, Aq, Akk);
+    } else {
+      float* Gf = reinterpret_cast<float*>(sm + Q_KI);
+      store_G(Gf, G);
+      __syncthreads();
+      scores_exact(sm + Q_SQ, sm + Q_SK, Gf, Aq, Akk);
+      __syncthreads();
+      if (more) {
+        stage_tile(sm + Q_SQ, qh + (tok0 + tp0) * rstride, C, rstride);
+        stage_tile(sm + Q_SK, kh + (tok0 + tp0) * rstride, C, rstride);
+        stage_tile(sm + Q_SG, gh + (tok0 + tp0) * rstride, C, rstride);
+        cp_async_commit();
+      }
+    }
+    __syncthreads();
+    float* Tm = reinterpret_cast<float*>(sm + Q_KI);
+    solve_T(Akk, beta_s, Tm);
+    {
+      const int r = tid >> 2, c0 = (tid & 3) * 16;
+      row16_to_cm(sm + Q_TP, r, Tm, r, c0, beta_s);
+      row16_to_cm(sm + Q_AQB, r, Aq, r, c0, nullptr);
+    }
+    fence_async_smem();
+    __syncthreads();
+    // W = (T beta) (Gam K)   (M = 64: rows r at lanes 32(r/16) + r%16)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t id = idesc_bf16(64, 128, false, true);
+      const uint32_t tp = smem_u32(sm + Q_TP);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_W, desc_kmajor(tp + ks * 256, C), desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), id, ks > 0);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // -W -> A3 rows 0..63
+      const int r = 16 * qw + lane;
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float vals[32];
+        tmem_ld32(T_W + tl + c0, vals);
+        tmem_wait_ld();
+        if (lane < 16) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) vals[j] = -vals[j];
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) st16(A3, cm_off(r, c0 + j, DK), pack_bf16x8(vals + j));
+        }
+      }
+    }
+    {  // dS' pass: bf16 operand + workspace copy, then dS *= Gam_C
+      const int d = 32 * qw + lane;
+      bf16* wrow = dsw + ((unit * n_chunks + c) * DK + d) * DV;
+      const float gcd = gamC[d];
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float vals[32];
+        tmem_ld32(T_DS + tl + c0, vals);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          const uint4 pk = pack_bf16x8(vals + j);
+          st16(sm + Q_SB, cm_off(d, c0 + j, DV), pk);
+          *reinterpret_cast<uint4*>(wrow + c0 + j) = pk;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) vals[j] *= gcd;
+        tmem_st32(T_DS + tl + c0, vals);
+      }
+      tmem_wait_st();
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // dU^T = dS'^T (lam K)^T + dO^T Aqk
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t sb = smem_u32(sm + Q_SB), kl = smem_u32(sm + Q_KL);
+      const uint32_t dob = smem_u32(sm + Q_DO), aqb = smem_u32(sm + Q_AQB);
+      const uint32_t id1 = idesc_bf16(128, 64, true, false), id2 = idesc_bf16(128, 64, true, true);
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks)
+        mma_bf16(T_U, desc_mnmajor(sb + ks * 4096, DV), desc_kmajor(kl + ks * 256, DK), id1, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_U, desc_mnmajor(dob + ks * 4096, DV), desc_mnmajor(aqb + ks * 2048, C), id2, 1u);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // dU^T -> bf16 [j][c] (TP region)
+      const int j = 32 * qw + lane;
+      float vals[32];
+      tmem_ld32(T_U + tl + hh * 32, vals);
+      tmem_wait_ld();
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 8) st16(sm + Q_TP, cm_off(j, hh * 32 + jj, C), pack_bf16x8(vals + jj));
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // dS += (Gam Q)^T dO + (-W)^T dU
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t dob = smem_u32(sm + Q_DO), dut = smem_u32(sm + Q_TP);
+      const uint32_t id1 = idesc_bf16(128, 128, true, true), id2 = idesc_bf16(128, 128, true, false);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_DS, desc_mnmajor(a3 + 64 * 256 + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id1, 1u);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_DS, desc_mnmajor(a3 + ks * 4096, DK), desc_kmajor(dut + ks * 256, C), id2, 1u);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    if (more) {
+      stage_tile(sm + Q_DO, doh + (tok0 + tp0) * rstride, C, rstride);
+      cp_async_commit();
+    }
+  }
+  if (!failed && ds0) {
+    const int d = 32 * qw + lane;
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = hh * 64 + half * 32;
+      float vals[32];
+      tmem_ld32(T_DS + tl + c0, vals);
+      tmem_wait_ld();
+      store_row32<float>(ds0 + (unit * DK + d) * DV + c0, vals);
+    }
+  }
+  if (failed && tid == 0 && err) atomicExch(err, 1);
+  cp_async_wait<0>();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, 512);
+}
+
+// ===========================================================================
+// bwd_par
+// ===========================================================================
+constexpr int P_SQ = 0;                  // q staging | T fp32 | dO
+constexpr int P_SK = 16384;              // k staging | dS' (lo) | dW^T [128][64]
+constexpr int P_SG = 32768;              // g staging | dS' (hi)
+constexpr int P_V = 49152;               // v staging | U bf16 [64][128]
+constexpr int P_A3 = 65536;              // [W ; Gam Q ; Gam K]
+constexpr int P_KI = P_A3 + 49152;       // K Gi
+constexpr int P_KL = P_KI + 16384;       // lam K | dU^T [128][64] | [dAqk ; beta dL] [128][64]
+constexpr int P_SB = P_KL + 16384;       // Aqk+Akk fp32 | S_c bf16 [128][128] | Yw^T, Yu^T | G fp32 (slow)
+constexpr int P_TP = P_SB + 32768;       // [Tb ; Pb] | partials | v~ bf16 [64][128] | G (slow, with TB/AQB)
+constexpr int P_TB = P_TP + 16384;       // T bf16 [64][64]
+constexpr int P_AQB = P_TB + 8192;       // Aqk bf16
+constexpr int P_AKB = P_AQB + 8192;      // Akk bf16
+constexpr int P_BETA = P_AKB + 8192;     // beta fp32[64]
+constexpr int P_GC = P_BETA + 256;       // Gam_C fp32[128]
+constexpr int P_DGC = P_GC + 512;        // dGam_C partial fp32[128]
+constexpr int P_DB = P_DGC + 512;        // dbeta accum fp32[64]
+constexpr int P_XCH = P_DB + 256;        // half-exchange fp32[2][2][128]
+constexpr int P_BAR = P_XCH + 2048;
+constexpr int PAR_SMEM = P_BAR + 64;
+
+template <typename Tc>
+__device__ __forceinline__ void stage_ckpt(unsigned char* dst, const Tc* src);
+template <>
+__device__ __forceinline__ void stage_ckpt<bf16>(unsigned char* dst, const bf16* src) {
+  stage_square(dst, src);
+}
+template <>
+__device__ __forceinline__ void stage_ckpt<float>(unsigned char* dst, const float* src) {
+  for (int i = threadIdx.x; i < 128 * 16; i += NT) {
+    const int r = i >> 4, cg = i & 15;
+    const float4 a = *reinterpret_cast<const float4*>(src + r * 128 + cg * 8);
+    const float4 bb = *reinterpret_cast<const float4*>(src + r * 128 + cg * 8 + 4);
+    const float f[8] = {a.x, a.y, a.z, a.w, bb.x, bb.y, bb.z, bb.w};
+    st16(dst, cm_off(r, cg * 8, 128), pack_bf16x8(f));
+  }
+}
+
+template <typename Tc>
+__global__ void __launch_bounds__(NT, 1)
+bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+               const bf16* __restrict__ g, const bf16* __restrict__ beta,
+               const Tc* __restrict__ s_ckpt, const bf16* __restrict__ dsw,
+               const bf16* __restrict__ dout, bf16* __restrict__ dq, bf16* __restrict__ dk,
+               bf16* __restrict__ dv, bf16* __restrict__ dg, bf16* __restrict__ dbeta, int B,
+               int T, int H, int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  float* beta_s = reinterpret_cast<float*>(sm + P_BETA);
+  float* gamC = reinterpret_cast<float*>(sm + P_GC);
+  float* dgc = reinterpret_cast<float*>(sm + P_DGC);
+  float* dbs = reinterpret_cast<float*>(sm + P_DB);
+  float* xch = reinterpret_cast<float*>(sm + P_XCH);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P_BAR + 8);
+  unsigned char* A3 = sm + P_A3;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qw = warp & 3, hh = warp >> 2;
+  const int n_chunks = (T + C - 1) / C;
+  const long long n_units = static_cast<long long>(B) * H * n_chunks;
+  const size_t rstride = static_cast<size_t>(H) * DK;
+
+  if (tid == 0) { mbar_init(mbar, 1); mbar_fence_init(); }
+  if (warp == 0) { tmem_alloc(tslot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  // TMEM columns
+  const uint32_t T_IV = tbase;            // [0,128): W | (dO S^T)^T, dKG^T
+  const uint32_t T_UF = tbase + 128;      // [128,256): U (fp32) | Yw^T, Yu^T
+  const uint32_t T_SC = tbase + 256;      // [256,320): scores | W S (64..) | dAqk | dKI^T
+  const uint32_t T_WS = tbase + 256;      // [256,384): W S (M = 64)
+  const uint32_t T_L = tbase + 320;       // [320,384): dL (negated)
+  const uint32_t T_DU = tbase + 384;      // [384,448): dU^T
+  const uint32_t T_KL = tbase + 448;      // [448,512): dKL^T
+  const uint32_t tl = lane_off(qw);
+  uint32_t phase = 0;
+  bool failed = false;
+  auto mma_wait = [&]() -> bool {
+    const bool ok = mbar_wait(mbar, phase);
+    phase ^= 1u;
+    tc_fence_after();
+    return ok;
+  };
+  const uint32_t a3 = smem_u32(A3);
+  float* Aq = reinterpret_cast<float*>(sm + P_SB);
+  float* Akk = Aq + 4096;
+
+  for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const int c = static_cast<int>(u % n_chunks);
+    const long long bh = u / n_chunks;
+    const int h = static_cast<int>(bh % H), b = static_cast<int>(bh / H);
+    const int t0 = c * C, rows_valid = min(C, T - t0);
+    const size_t tok0 = static_cast<size_t>(b) * T + t0;
+    const size_t hoff = static_cast<size_t>(h) * DK;
+    const size_t unit_sq = (static_cast<size_t>(b) * H + h) * n_chunks + c;  // chunk index
+
+    stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
+    stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
+    stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
+    stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
+    cp_async_commit();
+    if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + tid) * H + h]) : 0.f;
+    if (tid < 128) dgc[tid] = 0.f;
+    if (tid < 64) dbs[tid] = 0.f;
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- recompute: prep, scores, T, W, U ----
+    float G[4][8];
+    const bool slow = prep(sm + P_SQ, sm + P_SK, sm + P_SG, A3 + cm_off(64, 0, DK),
+                           A3 + cm_off(128, 0, DK), sm + P_KI, sm + P_KL,
+                           reinterpret_cast<float*>(sm + P_TP), gamC, G);
+    if (!slow) {
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t id = idesc_bf16(128, 64, false, false);
+#pragma unroll
+        for (int ks = 0; ks < DK / 16; ++ks)
+          mma_bf16(T_SC, desc_kmajor(a3 + 64 * 256 + ks * 256, DK),
+                   desc_kmajor(smem_u32(sm + P_KI) + ks * 256, DK), id, ks > 0);
+        mma_commit(mbar);
+      }
+      failed |= !mma_wait();
+      if (__syncthreads_or(failed)) break;
+      scores_epilogue(T_SC, Aq, Akk);
+    } else {
+      float* Gf = reinterpret_cast<float*>(sm + P_TP);  // TP|TB|AQB = 32 KB
+      store_G(Gf, G);
+      __syncthreads();
+      scores_exact(sm + P_SQ, sm + P_SK, Gf, Aq, Akk);
+    }
+    __syncthreads();
+    // dS' into the free k/g staging
+    stage_square(sm + P_SK, dsw + unit_sq * (DK * DV));
+    cp_async_commit();
+    float* Tm = reinterpret_cast<float*>(sm + P_SQ);
+    solve_T(Akk, beta_s, Tm);
+    {
+      const int r = tid >> 2, c0 = (tid & 3) * 16;
+      row16_to_cm(sm + P_TP, r, Tm, r, c0, beta_s);
+      row16_to_cm(sm + P_TB, r, Tm, r, c0, nullptr);
+      row16_to_cm(sm + P_AQB, r, Aq, r, c0, nullptr);
+      row16_to_cm(sm + P_AKB, r, Akk, r, c0, nullptr);
+    }
+    fence_async_smem();
+    __syncthreads();
+    // W = (T b)(Gam K), U = (T b) V   (M = 64)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t id = idesc_bf16(64, 128, false, true);
+      const uint32_t tp = smem_u32(sm + P_TP), vb = smem_u32(sm + P_V);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks) {
+        const uint64_t ad = desc_kmajor(tp + ks * 256, C);
+        mma_bf16(T_IV, ad, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), id, ks > 0);
+        mma_bf16(T_UF, ad, desc_mnmajor(vb + ks * 4096, DV), id, ks > 0);
+      }
+      mma_commit(mbar);
+    }
+    // dO over the free T buffer, S_c over the free score buffer
+    __syncthreads();
+    stage_tile(sm + P_SQ, dout + hoff + tok0 * rstride, rows_valid, rstride);
+    if constexpr (sizeof(Tc) == 2) {
+      stage_ckpt<Tc>(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
+    }
+    cp_async_commit();
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    if constexpr (sizeof(Tc) == 4) stage_ckpt<Tc>(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
+    {  // W -> A3 rows 0..63, U -> bf16 (V region); U fp32 stays in TMEM
+      const int r = 16 * qw + lane;
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float w[32], uu[32];
+        tmem_ld32(T_IV + tl + c0, w);
+        tmem_ld32(T_UF + tl + c0, uu);
+        tmem_wait_ld();
+        if (lane < 16) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            st16(A3, cm_off(r, c0 + j, DK), pack_bf16x8(w + j));
+            st16(sm + P_V, cm_off(r, c0 + j, DV), pack_bf16x8(uu + j));
+          }
+        }
+      }
+    }
+    cp_async_wait<0>();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // W S_c  (M = 64)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t id = idesc_bf16(64, 128, false, true);
+      const uint32_t sb = smem_u32(sm + P_SB);
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks)
+        mma_bf16(T_WS, desc_kmajor(a3 + ks * 256, DK), desc_mnmajor(sb + ks * 4096, DV), id, ks > 0);
+      mma_commit(mbar);
+    }
+    {  // dGam_C partial sums: sum_j S_c[d][j] dS'[d][j]
+      const int d = tid >> 1, j0 = (tid & 1) * 64;
+      float acc = 0.f;
+      for (int j = j0; j < j0 + 64; j += 8) {
+        float a[8], bb[8];
+        unpack_bf16x8(ld16(sm + P_SB, cm_off(d, j, DV)), a);
+        unpack_bf16x8(ld16(sm + P_SK, cm_off(d, j, DV)), bb);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc += a[e] * bb[e];
+      }
+      atomicAdd(&dgc[d], acc);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // v~ = U - W S -> bf16 (TP region)
+      const int r = 16 * qw + lane;
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float ws[32], uu[32];
+        tmem_ld32(T_WS + tl + c0, ws);
+        tmem_ld32(T_UF + tl + c0, uu);
+        tmem_wait_ld();
+        if (lane < 16) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) uu[j] -= ws[j];
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) st16(sm + P_TP, cm_off(r, c0 + j, DV), pack_bf16x8(uu + j));
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // dU^T = dS'^T (lam K)^T + dO^T Aqk ;  dKL^T = dS' v~^T
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t dsp = smem_u32(sm + P_SK), kl = smem_u32(sm + P_KL);
+      const uint32_t dob = smem_u32(sm + P_SQ), aqb = smem_u32(sm + P_AQB), vt = smem_u32(sm + P_TP);
+      const uint32_t id1 = idesc_bf16(128, 64, true, false), id2 = idesc_bf16(128, 64, true, true);
+      const uint32_t id3 = idesc_bf16(128, 64, false, false);
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks)
+        mma_bf16(T_DU, desc_mnmajor(dsp + ks * 4096, DV), desc_kmajor(kl + ks * 256, DK), id1, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_DU, desc_mnmajor(dob + ks * 4096, DV), desc_mnmajor(aqb + ks * 2048, C), id2, 1u);
+#pragma unroll
+      for (int ks = 0; ks < DV / 16; ++ks)
+        mma_bf16(T_KL, desc_kmajor(dsp + ks * 256, DV), desc_kmajor(vt + ks * 256, DV), id3, ks > 0);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // dU^T -> bf16 [j][c] (KL region)
+      const int j = 32 * qw + lane;
+      float vals[32];
+      tmem_ld32(T_DU + tl + hh * 32, vals);
+      tmem_wait_ld();
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 8) st16(sm + P_KL, cm_off(j, hh * 32 + jj, C), pack_bf16x8(vals + jj));
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // S_c [dO^T | dU^T] -> (dO S^T)^T | (dU S^T)^T
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t sb = smem_u32(sm + P_SB), dob = smem_u32(sm + P_SQ), dut = smem_u32(sm + P_KL);
+      const uint32_t id1 = idesc_bf16(128, 64, false, false), id2 = idesc_bf16(128, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < DV / 16; ++ks) {
+        const uint64_t ad = desc_kmajor(sb + ks * 256, DV);
+        mma_bf16(T_IV, ad, desc_kmajor(dob + ks * 256, DV), id1, ks > 0);
+        mma_bf16(T_IV + 64, ad, desc_mnmajor(dut + ks * 2048, C), id2, ks > 0);
+      }
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // dW^T = -(dU S^T)^T -> bf16 [d][c] (SK region)
+      const int d = 32 * qw + lane;
+      float vals[32];
+      tmem_ld32(T_IV + 64 + tl + hh * 32, vals);
+      tmem_wait_ld();
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) vals[jj] = -vals[jj];
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 8) st16(sm + P_SK, cm_off(d, hh * 32 + jj, C), pack_bf16x8(vals + jj));
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // Yw^T = dW^T T,  Yu^T = dU^T T
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t dwt = smem_u32(sm + P_SK), dut = smem_u32(sm + P_KL), tb = smem_u32(sm + P_TB);
+      const uint32_t id = idesc_bf16(128, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks) {
+        const uint64_t bd = desc_mnmajor(tb + ks * 2048, C);
+        mma_bf16(T_UF, desc_kmajor(dwt + ks * 256, C), bd, id, ks > 0);
+        mma_bf16(T_UF + 64, desc_kmajor(dut + ks * 256, C), bd, id, ks > 0);
+      }
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // Yw^T, Yu^T -> bf16 (SB region); beta_c Yw^T -> TMEM [64,128)
+      const int d = 32 * qw + lane;
+      float yw[32], yu[32];
+      tmem_ld32(T_UF + tl + hh * 32, yw);
+      tmem_ld32(T_UF + 64 + tl + hh * 32, yu);
+      tmem_wait_ld();
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 8) {
+        st16(sm + P_SB, cm_off(d, hh * 32 + jj, C), pack_bf16x8(yw + jj));
+        st16(sm + P_SB + 16384, cm_off(d, hh * 32 + jj, C), pack_bf16x8(yu + jj));
+      }
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) yw[jj] *= beta_s[hh * 32 + jj];
+      tmem_st32(T_IV + 64 + tl + hh * 32, yw);
+      tmem_wait_st();
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // dAqk = dO v~^T, dL~ = Yu U^T + Yw W^T   (M = 64)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t dob = smem_u32(sm + P_SQ), vt = smem_u32(sm + P_TP);
+      const uint32_t ywt = smem_u32(sm + P_SB), yut = smem_u32(sm + P_SB + 16384), ub = smem_u32(sm + P_V);
+      const uint32_t id1 = idesc_bf16(64, 64, false, false), id2 = idesc_bf16(64, 64, true, false);
+#pragma unroll
+      for (int ks = 0; ks < DV / 16; ++ks)
+        mma_bf16(T_SC, desc_kmajor(dob + ks * 256, DV), desc_kmajor(vt + ks * 256, DV), id1, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < DV / 16; ++ks)
+        mma_bf16(T_L, desc_mnmajor(yut + ks * 2048, C), desc_kmajor(ub + ks * 256, DV), id2, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks)
+        mma_bf16(T_L, desc_mnmajor(ywt + ks * 2048, C), desc_kmajor(a3 + ks * 256, DK), id2, 1u);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // [dAqk ; beta dL] -> bf16 [128][64] (KL region); dbeta += rowsum(dL * Akk)
+      const int r = 16 * qw + lane;
+      float da[32], dl[32];
+      tmem_ld32(T_SC + tl + hh * 32, da);
+      tmem_ld32(T_L + tl + hh * 32, dl);
+      tmem_wait_ld();
+      if (lane < 16) {
+        const float br = beta_s[r];
+        float part = 0.f;
+        float akk[32];
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 8) unpack_bf16x8(ld16(sm + P_AKB, cm_off(r, hh * 32 + jj, C)), akk + jj);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int i = hh * 32 + jj;
+          da[jj] = (i <= r) ? da[jj] : 0.f;
+          const float l = (i < r) ? -dl[jj] : 0.f;
+          part += l * akk[jj];
+          dl[jj] = br * l;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 8) {
+          st16(sm + P_KL, cm_off(r, hh * 32 + jj, C), pack_bf16x8(da + jj));
+          st16(sm + P_KL, cm_off(64 + r, hh * 32 + jj, C), pack_bf16x8(dl + jj));
+        }
+        atomicAdd(&dbs[r], part);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (!slow) {
+      // [dQG^T | dKG^T] += KI^T [dAqk ; beta dL]^T ;  dKI^T = QG^T dAqk + KG^T (beta dL)
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t ki = smem_u32(sm + P_KI), da = smem_u32(sm + P_KL);
+        const uint32_t id1 = idesc_bf16(128, 128, true, false), id2 = idesc_bf16(128, 64, true, true);
+#pragma unroll
+        for (int ks = 0; ks < C / 16; ++ks)
+          mma_bf16(T_IV, desc_mnmajor(ki + ks * 4096, DK), desc_kmajor(da + ks * 256, C), id1, 1u);
+#pragma unroll
+        for (int ks = 0; ks < C / 16; ++ks)
+          mma_bf16(T_SC, desc_mnmajor(a3 + 64 * 256 + ks * 4096, DK), desc_mnmajor(da + ks * 2048, C), id2, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < C / 16; ++ks)
+          mma_bf16(T_SC, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), desc_mnmajor(da + 8192 + ks * 2048, C), id2, 1u);
+        mma_commit(mbar);
+      }
+      failed |= !mma_wait();
+      if (__syncthreads_or(failed)) break;
+    } else {
+      // exact path needs raw q, k and G fp32 (restaged over dead buffers)
+      stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
+      stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
+      cp_async_commit();
+      store_G(reinterpret_cast<float*>(sm + P_SB), G);
+      cp_async_wait<0>();
+      __syncthreads();
+    }
+    // ---- final epilogue: thread = channel d (lane), columns c in [32 hh, 32 hh + 32) ----
+    {
+      const int d = 32 * qw + lane;
+      const int cb = hh * 32;
+      float dqg[32], dkg[32], dki[32], dkl[32];
+      tmem_ld32(T_IV + tl + cb, dqg);
+      tmem_ld32(T_IV + 64 + tl + cb, dkg);
+      tmem_ld32(T_SC + tl + cb, dki);
+      tmem_ld32(T_KL + tl + cb, dkl);
+      tmem_wait_ld();
+      if (slow) {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dki[jj] = 0.f;
+      }
+      // G column: prefix over the chunk, my 32 rows
+      const bf16* gcol = g + hoff + tok0 * rstride + d;
+      float pre = 0.f, gtot = 0.f;
+      for (int cc = 0; cc < C; ++cc) {
+        const float x = cc < rows_valid ? __bfloat162float(gcol[cc * rstride]) : 0.f;
+        if (cc < cb) pre += x;
+        gtot += x;
+      }
+      float dG[32], dqv[32], dkv[32];
+      float run = pre, klsum = 0.f, kgam[32];
+      const bf16* qcol = q + hoff + tok0 * rstride + d;
+      const bf16* kcol = k + hoff + tok0 * rstride + d;
+      for (int jj = 0; jj < 32; ++jj) {
+        const int cc = cb + jj;
+        const bool ok = cc < rows_valid;
+        run += ok ? __bfloat162float(gcol[cc * rstride]) : 0.f;
+        const float qv = ok ? __bfloat162float(qcol[cc * rstride]) : 0.f;
+        const float kv = ok ? __bfloat162float(kcol[cc * rstride]) : 0.f;
+        const float gam = __expf(run);
+        const float gi = slow ? 0.f : __expf(-run);
+        const float lam = __expf(fminf(gtot - run, 0.f));
+        dqv[jj] = dqg[jj] * gam;
+        dkv[jj] = dkg[jj] * gam + dki[jj] * gi + dkl[jj] * lam;
+        const float klt = dkl[jj] * kv * lam;
+        dG[jj] = dqg[jj] * qv * gam + dkg[jj] * kv * gam - dki[jj] * kv * gi - klt;
+        klsum += klt;
+        kgam[jj] = kv * gam;
+      }
+      if (slow) {
+        const float* Gs = reinterpret_cast<const float*>(sm + P_SB);
+        for (int jj = 0; jj < 32; ++jj) {
+          const int cc = cb + jj;
+          const float Gc = Gs[cc * DK + d];
+          const float qc = ldbf(sm + P_SQ, cm_off(cc, d, DK)), kc = ldbf(sm + P_SK, cm_off(cc, d, DK));
+          float dra = 0.f, drk = 0.f, dca = 0.f, dck = 0.f;
+          for (int i = 0; i <= cc; ++i) {
+            const float ke = ldbf(sm + P_SK, cm_off(i, d, DK)) * __expf(fminf(Gc - Gs[i * DK + d], 0.f));
+            dra += ldbf(sm + P_KL, cm_off(cc, i, C)) * ke;
+            drk += ldbf(sm + P_KL, cm_off(64 + cc, i, C)) * ke;
+          }
+          for (int r2 = cc; r2 < C; ++r2) {
+            const float e = __expf(fminf(Gs[r2 * DK + d] - Gc, 0.f));
+            dca += ldbf(sm + P_KL, cm_off(r2, cc, C)) * ldbf(sm + P_SQ, cm_off(r2, d, DK)) * e;
+            dck += ldbf(sm + P_KL, cm_off(64 + r2, cc, C)) * ldbf(sm + P_SK, cm_off(r2, d, DK)) * e;
+          }
+          dqv[jj] += dra;
+          dkv[jj] += drk + dca + dck;
+          dG[jj] += dra * qc + drk * kc - (dca + dck) * kc;
+        }
+      }
+      float gsum = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) gsum += dG[jj];
+      xch[(0 * 2 + hh) * 128 + d] = gsum;
+      xch[(1 * 2 + hh) * 128 + d] = klsum;
+      // dbeta += rowsum(Yw (Gam K)) over d, and rowsum(Yu v) over j (same lane index)
+      {
+        float yw[32], yu[32];
+        tmem_ld32(T_UF + tl + cb, yw);
+        tmem_ld32(T_UF + 64 + tl + cb, yu);
+        tmem_wait_ld();
+        const bf16* vcol = v + hoff + tok0 * rstride + d;
+        bf16* dvcol = dv + hoff + tok0 * rstride + d;
+        for (int s = 0; s < 32; ++s) {
+          const int jj = (s + lane) & 31;  // stagger the shared-memory atomics
+          const int cc = cb + jj;
+          const bool ok = cc < rows_valid;
+          const float vv = ok ? __bfloat162float(vcol[cc * rstride]) : 0.f;
+          atomicAdd(&dbs[cc], yw[jj] * kgam[jj] + yu[jj] * vv);
+        }
+        for (int jj = 0; jj < 32; ++jj) {
+          const int cc = cb + jj;
+          if (cc < rows_valid) dvcol[cc * rstride] = __float2bfloat16_rn(beta_s[cc] * yu[jj]);
+        }
+      }
+      __syncthreads();
+      const float dGC = xch[(1 * 2 + 0) * 128 + d] + xch[(1 * 2 + 1) * 128 + d] + gamC[d] * dgc[d];
+      float acc = dGC + (hh == 0 ? xch[(0 * 2 + 1) * 128 + d] : 0.f);
+      bf16* dqcol = dq + hoff + tok0 * rstride + d;
+      bf16* dkcol = dk + hoff + tok0 * rstride + d;
+      bf16* dgcol = dg + hoff + tok0 * rstride + d;
+      for (int jj = 31; jj >= 0; --jj) {
+        acc += dG[jj];
+        const int cc = cb + jj;
+        if (cc < rows_valid) {
+          dqcol[cc * rstride] = __float2bfloat16_rn(dqv[jj]);
+          dkcol[cc * rstride] = __float2bfloat16_rn(dkv[jj]);
+          dgcol[cc * rstride] = __float2bfloat16_rn(acc);
+        }
+      }
+      if (tid < C && tid < rows_valid) dbeta[(tok0 + tid) * H + h] = __float2bfloat16_rn(dbs[tid]);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  if (failed && tid == 0 && err) atomicExch(err, 1);
+  cp_async_wait<0>();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, 512);
+}
+
+__device__ int g_bwd_tc_error = 0;
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <typename Tc>
+int launch_bwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
+               const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
+               void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
+               cudaStream_t st) {
+  static bool done_seq[64] = {false}, done_par[64] = {false};
+  int rc = ensure_smem(bwd_seq_kernel, SEQ_SMEM, done_seq);
+  if (rc != KDA_OK) return rc;
+  rc = ensure_smem(bwd_par_kernel<Tc>, PAR_SMEM, done_par);
+  if (rc != KDA_OK) return rc;
+  int* err = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_bwd_tc_error) != cudaSuccess) return KDA_ERR_LAUNCH;
+  bf16* dsw = static_cast<bf16*>(work);
+  bwd_seq_kernel<<<B * H, NT, SEQ_SMEM, st>>>(
+      static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(g),
+      static_cast<const bf16*>(beta), static_cast<const bf16*>(dout), dsT, ds0, dsw, T, H, err);
+  rc = launch_status();
+  if (rc != KDA_OK) return rc;
+  const long long units = static_cast<long long>(B) * H * ((T + C - 1) / C);
+  const int grid = static_cast<int>(units < sm_count() ? units : sm_count());
+  bwd_par_kernel<Tc><<<grid, NT, PAR_SMEM, st>>>(
+      static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v),
+      static_cast<const bf16*>(g), static_cast<const bf16*>(beta), static_cast<const Tc*>(s_ckpt),
+      dsw, static_cast<const bf16*>(dout), static_cast<bf16*>(dq), static_cast<bf16*>(dk_),
+      static_cast<bf16*>(dv_), static_cast<bf16*>(dg), static_cast<bf16*>(dbeta), B, T, H, err);
+  return launch_status();
+}
+
+}  // namespace
+
+bool tc_bwd_supported(int dk, int dv, int C_, int in_dt, int do_dt) {
+  return dk == DK && dv == DV && C_ == C && in_dt == KDA_BF16 && do_dt == KDA_BF16;
+}
+
+size_t tc_bwd_workspace_bytes(int B, int T, int H) {
+  const size_t n = (static_cast<size_t>(T) + C - 1) / C;
+  return static_cast<size_t>(B) * H * n * DK * DV * sizeof(bf16);
+}
+
+int tc_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                  const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
+                  void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
+                  int ck_dt, cudaStream_t st) {
+  if (ck_dt == KDA_BF16)
+    return launch_bwd<bf16>(q, k, v, g, beta, s_ckpt, dout, dsT, dq, dk_, dv_, dg, dbeta, ds0, work, B, T, H, st);
+  if (ck_dt == KDA_F32)
+    return launch_bwd<float>(q, k, v, g, beta, s_ckpt, dout, dsT, dq, dk_, dv_, dg, dbeta, ds0, work, B, T, H, st);
+  return KDA_ERR_DTYPE;
+}
+
+}  // namespace kda

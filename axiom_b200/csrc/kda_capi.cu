@@ -16,6 +16,12 @@ bool tc_fwd_supported(int dk, int dv, int C_, int in_dt);
 int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                   const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
                   int o_dt, int ck_dt, cudaStream_t st);
+bool tc_bwd_supported(int dk, int dv, int C_, int in_dt, int do_dt);
+size_t tc_bwd_workspace_bytes(int B, int T, int H);
+int tc_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                  const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
+                  void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
+                  int ck_dt, cudaStream_t st);
 int simt_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                     const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                     void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T,
@@ -93,10 +99,13 @@ int kda_fwd(const void* q, const void* k, const void* v, const void* g, const vo
 }
 
 size_t kda_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dtype) {
-  (void)T;
-  (void)in_dtype;
   if (check_dims(B, T, H, dk, dv, chunk) != KDA_OK) return 0;
-  return kda::simt_bwd_workspace_bytes(B, H, dk, dv, chunk);
+  size_t n = kda::simt_bwd_workspace_bytes(B, H, dk, dv, chunk);
+  if (kda::tc_bwd_supported(dk, dv, chunk, in_dtype, KDA_BF16)) {
+    const size_t t = kda::tc_bwd_workspace_bytes(B, T, H);
+    if (t > n) n = t;
+  }
+  return n;
 }
 
 int kda_bwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
@@ -120,7 +129,16 @@ int kda_bwd(const void* q, const void* k, const void* v, const void* g, const vo
   }
   if (!q || !k || !v || !g || !beta || !s_ckpt || !do_ || !dq || !dk_ || !dv_ || !dg || !dbeta)
     return KDA_ERR_NULL;
-  const size_t need = kda_bwd_workspace_bytes(B, T, H, dk, dv, chunk, in_dtype);
+  if (kda::tc_bwd_supported(dk, dv, chunk, in_dtype, do_dtype)) {
+    const size_t need = kda::tc_bwd_workspace_bytes(B, T, H);
+    if (!workspace || workspace_bytes < need) return KDA_ERR_WORKSPACE;
+    const void* ptrs[] = {q, k, v, g, do_, dq, dk_, dv_, dg, s_ckpt, workspace};
+    for (const void* p : ptrs)
+      if (!kda::aligned16(p)) return KDA_ERR_ALIGN;
+    return kda::tc_bwd_launch(q, k, v, g, beta, s_ckpt, do_, dsT, dq, dk_, dv_, dg, dbeta, ds0,
+                              workspace, B, T, H, ckpt_dtype, stream);
+  }
+  const size_t need = kda::simt_bwd_workspace_bytes(B, H, dk, dv, chunk);
   if (need && (!workspace || workspace_bytes < need)) return KDA_ERR_WORKSPACE;
   return kda::simt_bwd_launch(q, k, v, g, beta, s_ckpt, do_, dsT, dq, dk_, dv_, dg, dbeta, ds0,
                               workspace, B, T, H, dk, dv, chunk, in_dtype, do_dtype, ckpt_dtype,

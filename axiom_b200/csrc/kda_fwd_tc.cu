@@ -17,16 +17,13 @@
 //   v~ = U - W S ;  O = Q~ S + Aqk U
 //   MMA_3  : S <- Gam_C * S + (lam K)^T v~   (accumulated in TMEM)
 // The chunk-boundary state (bf16 or fp32) is written for the backward.
-#include "kda_common.cuh"
-#include "kda_tc.cuh"
+#include "kda_chunk.cuh"
 
 namespace kda {
 namespace {
 
 using namespace tc;
-
-constexpr int C = 64, DK = 128, DV = 128, NT = 256;
-constexpr float kExpBudget = 80.f;  // the reference's COL_EXP_BUDGET
+using namespace chunk;
 
 // shared-memory map (bytes)
 constexpr int OFF_SQ = 0;                       // staging q   CM[64][128]
@@ -37,59 +34,24 @@ constexpr int OFF_A3 = OFF_V + 16384;           // [W ; Q~ ; K*Gam] CM[192][128]
 constexpr int OFF_KI = OFF_A3 + 49152;          // K*Gi CM[64][128]   | T fp32 | G fp32 (slow)
 constexpr int OFF_TP = OFF_KI + 16384;          // [T b ; P b] CM[128][64]    | G fp32 (slow)
 constexpr int OFF_KL = OFF_TP + 16384;          // lam*K CM[64][128]
-constexpr int OFF_SB = OFF_KL + 16384;          // S bf16 CM[128][128] | Aqk fp32 + L fp32
+constexpr int OFF_SB = OFF_KL + 16384;          // S bf16 CM[128][128] | Aqk fp32 + Akk fp32
 constexpr int OFF_VT = OFF_SB + 32768;          // v~ CM[64][128]      | cumsum partials
 constexpr int OFF_BETA = OFF_VT + 16384;        // beta fp32[64]
 constexpr int OFF_GC = OFF_BETA + 256;          // Gam_C fp32[128]
 constexpr int OFF_BAR = OFF_GC + 512;           // mbarrier + tmem slot
 constexpr int SMEM_BYTES = OFF_BAR + 64;
 
-// fp32 64x64 matrices with a 16-byte-chunk XOR swizzle (conflict-free row writes)
-__device__ __forceinline__ int sw64(int r, int c) {
-  return (r << 6) + ((((c >> 2) ^ (r & 15)) << 2) | (c & 3));
-}
-
-__device__ __forceinline__ uint4 ld16(const unsigned char* base, uint32_t off) {
-  return *reinterpret_cast<const uint4*>(base + off);
-}
-__device__ __forceinline__ void st16(unsigned char* base, uint32_t off, uint4 v) {
-  *reinterpret_cast<uint4*>(base + off) = v;
-}
-
-template <typename To>
-__device__ __forceinline__ void store_row32(To* dst, const float* v);
-template <>
-__device__ __forceinline__ void store_row32<float>(float* dst, const float* v) {
-#pragma unroll
-  for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-}
-template <>
-__device__ __forceinline__ void store_row32<bf16>(bf16* dst, const float* v) {
-#pragma unroll
-  for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = pack_bf16x8(v + j);
-}
-
 // Issue the cp.async copies of one chunk's q, k, g (qkg = true) or v into CM tiles.
 __device__ __forceinline__ void stage_chunk(unsigned char* sm, const bf16* q, const bf16* k,
                                             const bf16* g, const bf16* v, size_t row0, int rows_valid,
                                             int H, bool qkg) {
-  const int tid = threadIdx.x;
   const size_t rstride = static_cast<size_t>(H) * DK;  // elements between tokens
   if (qkg) {
-    for (int i = tid; i < 3 * C * 16; i += NT) {
-      const int which = i / (C * 16), rem = i % (C * 16), r = rem >> 4, cg = rem & 15;
-      const bf16* src = which == 0 ? q : (which == 1 ? k : g);
-      const bool ok = r < rows_valid;
-      const bf16* p = ok ? src + (row0 + r) * rstride + cg * 8 : src;
-      cp_async16(sm + (which == 0 ? OFF_SQ : which == 1 ? OFF_SK : OFF_SG) + cm_off(r, cg * 8, DK), p, ok);
-    }
+    stage_tile(sm + OFF_SQ, q + row0 * rstride, rows_valid, rstride);
+    stage_tile(sm + OFF_SK, k + row0 * rstride, rows_valid, rstride);
+    stage_tile(sm + OFF_SG, g + row0 * rstride, rows_valid, rstride);
   } else {
-    for (int i = tid; i < C * 16; i += NT) {
-      const int r = i >> 4, cg = i & 15;
-      const bool ok = r < rows_valid;
-      const bf16* p = ok ? v + (row0 + r) * rstride + cg * 8 : v;
-      cp_async16(sm + OFF_V + cm_off(r, cg * 8, DV), p, ok);
-    }
+    stage_tile(sm + OFF_V, v + row0 * rstride, rows_valid, rstride);
   }
   cp_async_commit();
 }
@@ -170,77 +132,13 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     __syncthreads();
 
     // ---------------- prep: G, exponentials, operand tiles ----------------
-    const int cg = tid & 15, rg4 = tid >> 4;   // channels 8cg..8cg+7, rows 4rg4..4rg4+3
-    float G[4][8];
+    float* Aq = reinterpret_cast<float*>(sm + OFF_SB);
+    float* Akk = Aq + 4096;
     {
-      float* part = reinterpret_cast<float*>(sm + OFF_VT);  // [16][16][8]
-      float run[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) run[e] = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float gv[8];
-        unpack_bf16x8(ld16(sm + OFF_SG, cm_off(4 * rg4 + i, 8 * cg, DK)), gv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) { run[e] += gv[e]; G[i][e] = run[e]; }
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) part[(rg4 * 16 + cg) * 8 + e] = run[e];
-      __syncthreads();
-      float pre[8], tot[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) { pre[e] = 0.f; tot[e] = 0.f; }
-      for (int p = 0; p < 16; ++p) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float x = part[(p * 16 + cg) * 8 + e];
-          tot[e] += x;
-          if (p < rg4) pre[e] += x;
-        }
-      }
-      bool strong = false;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        strong |= fabsf(tot[e]) > kExpBudget;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) G[i][e] += pre[e];
-      }
-      if (rg4 == 0) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) gamC[8 * cg + e] = __expf(tot[e]);
-      }
-      // one barrier: publishes gamC and decides the path for the whole CTA
-      const bool slow = __syncthreads_or(strong) != 0;
-      float gc_e[8], gce[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) { gc_e[e] = tot[e]; gce[e] = __expf(tot[e]); }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = 4 * rg4 + i;
-        float qv[8], kv[8], qg[8], kg[8], ki[8], kl[8];
-        unpack_bf16x8(ld16(sm + OFF_SQ, cm_off(r, 8 * cg, DK)), qv);
-        unpack_bf16x8(ld16(sm + OFF_SK, cm_off(r, 8 * cg, DK)), kv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float gam = __expf(G[i][e]);
-          qg[e] = qv[e] * gam;
-          kg[e] = kv[e] * gam;
-          if (!slow) {
-            const float gi = __expf(-G[i][e]);
-            ki[e] = kv[e] * gi;
-            kl[e] = kv[e] * (gi * gce[e]);
-          } else {
-            ki[e] = 0.f;
-            kl[e] = kv[e] * __expf(fminf(gc_e[e] - G[i][e], 0.f));
-          }
-        }
-        st16(A3, cm_off(64 + r, 8 * cg, DK), pack_bf16x8(qg));
-        st16(A3, cm_off(128 + r, 8 * cg, DK), pack_bf16x8(kg));
-        if (!slow) st16(sm + OFF_KI, cm_off(r, 8 * cg, DK), pack_bf16x8(ki));
-        st16(sm + OFF_KL, cm_off(r, 8 * cg, DK), pack_bf16x8(kl));
-      }
-      float* Aq = reinterpret_cast<float*>(sm + OFF_SB);
-      float* Lm = Aq + 4096;
+      float G[4][8];
+      const bool slow = prep(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, A3 + cm_off(64, 0, DK),
+                             A3 + cm_off(128, 0, DK), sm + OFF_KI, sm + OFF_KL,
+                             reinterpret_cast<float*>(sm + OFF_VT), gamC, G);
       if (!slow) {
         fence_async_smem();
         __syncthreads();
@@ -257,156 +155,41 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, true);
         failed |= !mma_wait();
         if (__syncthreads_or(failed)) break;
-        // E1: scores -> Aqk (masked, fp32) and L = strict(beta_r Akk)
-        {
-          float vals[32];
-          tmem_ld32(T_D + t_lane + hh * 32, vals);
-          tmem_wait_ld();
-          const int R = 32 * qw + lane;
-          if (R < 64) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const int i0 = hh * 32 + j;
-              float4 w4;
-              w4.x = (i0 + 0 <= R) ? vals[j + 0] : 0.f;
-              w4.y = (i0 + 1 <= R) ? vals[j + 1] : 0.f;
-              w4.z = (i0 + 2 <= R) ? vals[j + 2] : 0.f;
-              w4.w = (i0 + 3 <= R) ? vals[j + 3] : 0.f;
-              *reinterpret_cast<float4*>(Aq + sw64(R, i0)) = w4;
-            }
-          } else {
-            const int r = R - 64;
-            const float br = beta_s[r];
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const int i0 = hh * 32 + j;
-              float4 w4;
-              w4.x = (i0 + 0 < r) ? br * vals[j + 0] : 0.f;
-              w4.y = (i0 + 1 < r) ? br * vals[j + 1] : 0.f;
-              w4.z = (i0 + 2 < r) ? br * vals[j + 2] : 0.f;
-              w4.w = (i0 + 3 < r) ? br * vals[j + 3] : 0.f;
-              *reinterpret_cast<float4*>(Lm + sw64(r, i0)) = w4;
-            }
-          }
-        }
+        scores_epilogue(T_D, Aq, Akk);
       } else {
         // exact scores on the CUDA cores (strong decay: the single anchor would overflow)
         float* Gf = reinterpret_cast<float*>(sm + OFF_KI);  // [64][128] fp32 across KI|TP
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) Gf[(4 * rg4 + i) * DK + 8 * cg + e] = G[i][e];
+        store_G(Gf, G);
         __syncthreads();
-        for (int idx = tid; idx < C * C; idx += NT) {
-          const int r = idx >> 6, i = idx & 63;
-          float a = 0.f, l = 0.f;
-          if (i <= r) {
-            for (int d8 = 0; d8 < DK; d8 += 8) {
-              float qr[8], kr[8], ki8[8];
-              unpack_bf16x8(ld16(sm + OFF_SQ, cm_off(r, d8, DK)), qr);
-              unpack_bf16x8(ld16(sm + OFF_SK, cm_off(r, d8, DK)), kr);
-              unpack_bf16x8(ld16(sm + OFF_SK, cm_off(i, d8, DK)), ki8);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const float ex = __expf(fminf(Gf[r * DK + d8 + e] - Gf[i * DK + d8 + e], 0.f));
-                a += qr[e] * ki8[e] * ex;
-                l += kr[e] * ki8[e] * ex;
-              }
-            }
-          }
-          Aq[sw64(r, i)] = a;
-          Lm[sw64(r, i)] = (i < r) ? beta_s[r] * l : 0.f;
-        }
+        scores_exact(sm + OFF_SQ, sm + OFF_SK, Gf, Aq, Akk);
         __syncthreads();
         if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, true);
       }
     }
     // ---------------- solve: T = (I + L)^-1 (blocked), P = Aqk T ----------------
     {
-      float* Aq = reinterpret_cast<float*>(sm + OFF_SB);
-      float* Lm = Aq + 4096;
       float* Tm = reinterpret_cast<float*>(sm + OFF_KI);
-      for (int idx = tid; idx < C * C; idx += NT) Tm[idx] = 0.f;  // swizzle is a permutation
       __syncthreads();
-      if (tid < 64) {  // diagonal 16x16 blocks, one column per thread
-        const int bb = tid >> 4, j = tid & 15, o = 16 * bb;
-        float x[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float acc = (i == j) ? 1.f : 0.f;
-#pragma unroll
-          for (int m = 0; m < i; ++m) acc -= Lm[sw64(o + i, o + m)] * x[m];
-          x[i] = acc;
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) Tm[sw64(o + i, o + j)] = x[i];
-      }
-      __syncthreads();
-      for (int dl = 1; dl < 4; ++dl) {  // off-diagonal blocks, by distance from the diagonal
-        const int nblk = 4 - dl;
-        float xs[3];
-        for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
-          const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-          const int bi = bj + dl;
-          float acc = 0.f;
-          for (int m = 16 * bj; m < 16 * bi; ++m) acc += Lm[sw64(16 * bi + r, m)] * Tm[sw64(m, 16 * bj + cc)];
-          xs[n] = acc;
-        }
-        __syncthreads();
-        for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
-          const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-          Tm[sw64(16 * (bj + dl) + r, 16 * bj + cc)] = xs[n];
-        }
-        __syncthreads();
-        for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
-          const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-          const int bi = bj + dl;
-          float acc = 0.f;
-#pragma unroll
-          for (int m = 0; m < 16; ++m)
-            acc -= Tm[sw64(16 * bi + r, 16 * bi + m)] * Tm[sw64(16 * bi + m, 16 * bj + cc)];
-          xs[n] = acc;
-        }
-        __syncthreads();
-        for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
-          const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-          Tm[sw64(16 * (bj + dl) + r, 16 * bj + cc)] = xs[n];
-        }
-        __syncthreads();
-      }
+      solve_T(Akk, beta_s, Tm);
       // P = Aqk T (row r, 16 columns per thread) and the [T b ; P b] bf16 operand
-      {
-        const int r = tid >> 2, c0 = (tid & 3) * 16;
-        float p[16];
+      const int r = tid >> 2, c0 = (tid & 3) * 16;
+      float p[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) p[j] = 0.f;
-        for (int m = 0; m <= r; ++m) {
-          const float a = Aq[sw64(r, m)];
-#pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const float4 t4 = *reinterpret_cast<const float4*>(Tm + sw64(m, c0 + j));
-            p[j] += a * t4.x; p[j + 1] += a * t4.y; p[j + 2] += a * t4.z; p[j + 3] += a * t4.w;
-          }
-        }
-        unsigned char* TP = sm + OFF_TP;
-        float tv[16];
+      for (int j = 0; j < 16; ++j) p[j] = 0.f;
+      for (int m = 0; m <= r; ++m) {
+        const float a = Aq[sw64(r, m)];
 #pragma unroll
         for (int j = 0; j < 16; j += 4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(Tm + sw64(r, c0 + j));
-          tv[j] = t4.x; tv[j + 1] = t4.y; tv[j + 2] = t4.z; tv[j + 3] = t4.w;
+          const float4 t4 = *reinterpret_cast<const float4*>(Tm + sw64(m, c0 + j));
+          p[j] += a * t4.x; p[j + 1] += a * t4.y; p[j + 2] += a * t4.z; p[j + 3] += a * t4.w;
         }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float bc = beta_s[c0 + j];
-          p[j] *= bc;
-          tv[j] *= bc;
-        }
-        __syncthreads();  // TP aliases the slow path's G; all reads of it are done
-        st16(TP, cm_off(r, c0, C), pack_bf16x8(tv));
-        st16(TP, cm_off(r, c0 + 8, C), pack_bf16x8(tv + 8));
-        st16(TP, cm_off(64 + r, c0, C), pack_bf16x8(p));
-        st16(TP, cm_off(64 + r, c0 + 8, C), pack_bf16x8(p + 8));
       }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) p[j] *= beta_s[c0 + j];
+      unsigned char* TP = sm + OFF_TP;
+      row16_to_cm(TP, r, Tm, r, c0, beta_s);
+      st16(TP, cm_off(64 + r, c0, C), pack_bf16x8(p));
+      st16(TP, cm_off(64 + r, c0 + 8, C), pack_bf16x8(p + 8));
     }
     fence_async_smem();
     __syncthreads();

@@ -84,3 +84,21 @@ def test_tc_training_step_matches_oracle(T, decay):
     ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64)
     for name, leaf, rf in zip(GRADS, ("q", "k", "v", "g", "beta", "S0"), ref):
         assert K.scale_rel_err(_np(leaves[leaf].grad), rf) <= TOL, name
+
+
+def test_tc_backward_many_units_matches_oracle():
+    """More (batch, head, chunk) units than SMs: bwd_par's persistent loop."""
+    from axiom_b200 import kda_bwd, kda_fwd
+
+    B, T, H = 2, 2048, 4
+    xr, d = _bf16_inputs(B, T, H, seed=21, s0_std=0.02)
+    rng = np.random.default_rng(22)
+    do = K.bf16_round(rng.standard_normal((B, T, H, 128)))
+    dST = rng.standard_normal((B, H, 128, 128)).astype(np.float32)
+    o, s_t, ckpt = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], need_ckpt=True)
+    grads = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, _dev(do, torch.bfloat16),
+                    _dev(dST, torch.float32))
+    torch.cuda.synchronize()
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64)
+    for name, gr, rf in zip(GRADS, grads, ref):
+        assert K.scale_rel_err(_np(gr), rf) <= TOL, name
