@@ -114,15 +114,16 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   float* Aq = reinterpret_cast<float*>(sm + Q_SB);
   float* Akk = Aq + 4096;
 
+  KDA_PT_INIT();
   for (int c = n_chunks - 1; c >= 0; --c) {
     const int t0 = c * C, rows_valid = min(C, T - t0);
     cp_async_wait<0>();
     if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
     __syncthreads();
+    KDA_PT(1, 0);
     float G[4][8];
     const bool slow = prep(sm + Q_SQ, sm + Q_SK, sm + Q_SG, A3 + cm_off(64, 0, DK),
-                           A3 + cm_off(128, 0, DK), sm + Q_KI, sm + Q_KL,
-                           reinterpret_cast<float*>(sm + Q_TP), gamC, G);
+                           A3 + cm_off(128, 0, DK), sm + Q_KI, sm + Q_KL, gamC, G);
     const bool more = c > 0;
     const int tp0 = (c - 1) * C;
     if (!slow) {
@@ -159,6 +160,7 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         cp_async_commit();
       }
     }
+    KDA_PT(1, 1);
     __syncthreads();
     float* Tm = reinterpret_cast<float*>(sm + Q_KI);
     solve_T(Akk, beta_s, Tm);
@@ -167,6 +169,7 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       row16_to_cm(sm + Q_TP, r, Tm, r, c0, beta_s);
       row16_to_cm(sm + Q_AQB, r, Aq, r, c0, nullptr);
     }
+    KDA_PT(1, 2);
     fence_async_smem();
     __syncthreads();
     // W = (T beta) (Gam K)   (M = 64: rows r at lanes 32(r/16) + r%16)
@@ -181,6 +184,7 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(1, 3);
     {  // -W -> A3 rows 0..63
       const int r = 16 * qw + lane;
       for (int half = 0; half < 2; ++half) {
@@ -217,6 +221,7 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       }
       tmem_wait_st();
     }
+    KDA_PT(1, 4);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -236,6 +241,7 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(1, 5);
     {  // dU^T -> bf16 [j][c] (TP region)
       const int j = 32 * qw + lane;
       float vals[32];
@@ -262,6 +268,7 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(1, 6);
     if (more) {
       stage_tile(sm + Q_DO, doh + (tok0 + tp0) * rstride, C, rstride);
       cp_async_commit();
@@ -375,6 +382,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   float* Aq = reinterpret_cast<float*>(sm + P_SB);
   float* Akk = Aq + 4096;
 
+  KDA_PT_INIT();
   for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
     const int c = static_cast<int>(u % n_chunks);
     const long long bh = u / n_chunks;
@@ -395,11 +403,11 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     cp_async_wait<0>();
     __syncthreads();
 
+    KDA_PT(2, 0);
     // ---- recompute: prep, scores, T, W, U ----
     float G[4][8];
     const bool slow = prep(sm + P_SQ, sm + P_SK, sm + P_SG, A3 + cm_off(64, 0, DK),
-                           A3 + cm_off(128, 0, DK), sm + P_KI, sm + P_KL,
-                           reinterpret_cast<float*>(sm + P_TP), gamC, G);
+                           A3 + cm_off(128, 0, DK), sm + P_KI, sm + P_KL, gamC, G);
     if (!slow) {
       fence_async_smem();
       __syncthreads();
@@ -422,6 +430,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       scores_exact(sm + P_SQ, sm + P_SK, Gf, Aq, Akk);
     }
     __syncthreads();
+    KDA_PT(2, 1);
     // dS' into the free k/g staging
     stage_square(sm + P_SK, dsw + unit_sq * (DK * DV));
     cp_async_commit();
@@ -436,6 +445,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     fence_async_smem();
     __syncthreads();
+    KDA_PT(2, 2);
     // W = (T b)(Gam K), U = (T b) V   (M = 64)
     if (tid == 0) {
       tc_fence_after();
@@ -459,6 +469,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
     if constexpr (sizeof(Tc) == 4) stage_ckpt<Tc>(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
+    KDA_PT(2, 3);
     {  // W -> A3 rows 0..63, U -> bf16 (V region); U fp32 stays in TMEM
       const int r = 16 * qw + lane;
       for (int half = 0; half < 2; ++half) {
@@ -480,6 +491,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    KDA_PT(2, 4);
     // W S_c  (M = 64)
     if (tid == 0) {
       tc_fence_after();
@@ -504,6 +516,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(2, 5);
     {  // v~ = U - W S -> bf16 (TP region)
       const int r = 16 * qw + lane;
       for (int half = 0; half < 2; ++half) {
@@ -523,6 +536,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    KDA_PT(2, 6);
     // dU^T = dS'^T (lam K)^T + dO^T Aqk ;  dKL^T = dS' v~^T
     if (tid == 0) {
       tc_fence_after();
@@ -543,6 +557,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(2, 7);
     {  // dU^T -> bf16 [j][c] (KL region)
       const int j = 32 * qw + lane;
       float vals[32];
@@ -554,6 +569,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    KDA_PT(2, 8);
     // S_c [dO^T | dU^T] -> (dO S^T)^T | (dU S^T)^T
     if (tid == 0) {
       tc_fence_after();
@@ -569,6 +585,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(2, 9);
     {  // dW^T = -(dU S^T)^T -> bf16 [d][c] (SK region)
       const int d = 32 * qw + lane;
       float vals[32];
@@ -582,6 +599,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    KDA_PT(2, 10);
     // Yw^T = dW^T T,  Yu^T = dU^T T
     if (tid == 0) {
       tc_fence_after();
@@ -597,6 +615,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(2, 11);
     {  // Yw^T, Yu^T -> bf16 (SB region); beta_c Yw^T -> TMEM [64,128)
       const int d = 32 * qw + lane;
       float yw[32], yu[32];
@@ -616,6 +635,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    KDA_PT(2, 12);
     // dAqk = dO v~^T, dL~ = Yu U^T + Yw W^T   (M = 64)
     if (tid == 0) {
       tc_fence_after();
@@ -635,6 +655,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(2, 13);
     {  // [dAqk ; beta dL] -> bf16 [128][64] (KL region); dbeta += rowsum(dL * Akk)
       const int r = 16 * qw + lane;
       float da[32], dl[32];
@@ -666,6 +687,16 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    KDA_PT(2, 14);
+    // dO, U, Yw^T/Yu^T, v~, T and Aqk are dead: restage g (and v) for the epilogue,
+    // and raw q, k for the exact path.
+    stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
+    stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
+    if (slow) {
+      stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
+      stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
+    }
+    cp_async_commit();
     if (!slow) {
       // [dQG^T | dKG^T] += KI^T [dAqk ; beta dL]^T ;  dKI^T = QG^T dAqk + KG^T (beta dL)
       if (tid == 0) {
@@ -684,78 +715,97 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         mma_commit(mbar);
       }
       failed |= !mma_wait();
-      if (__syncthreads_or(failed)) break;
-    } else {
-      // exact path needs raw q, k and G fp32 (restaged over dead buffers)
-      stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
-      stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
-      cp_async_commit();
-      store_G(reinterpret_cast<float*>(sm + P_SB), G);
-      cp_async_wait<0>();
-      __syncthreads();
     }
+    cp_async_wait<0>();
+    if (__syncthreads_or(failed)) break;
+    KDA_PT(2, 15);
     // ---- final epilogue: thread = channel d (lane), columns c in [32 hh, 32 hh + 32) ----
     {
       const int d = 32 * qw + lane;
       const int cb = hh * 32;
-      float dqg[32], dkg[32], dki[32], dkl[32];
-      tmem_ld32(T_IV + tl + cb, dqg);
-      tmem_ld32(T_IV + 64 + tl + cb, dkg);
-      tmem_ld32(T_SC + tl + cb, dki);
-      tmem_ld32(T_KL + tl + cb, dkl);
-      tmem_wait_ld();
-      if (slow) {
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dki[jj] = 0.f;
-      }
-      // G column: prefix over the chunk, my 32 rows
-      const bf16* gcol = g + hoff + tok0 * rstride + d;
+      const unsigned char* sgt = sm + P_SG;
       float pre = 0.f, gtot = 0.f;
       for (int cc = 0; cc < C; ++cc) {
-        const float x = cc < rows_valid ? __bfloat162float(gcol[cc * rstride]) : 0.f;
-        if (cc < cb) pre += x;
+        const float x = ldbf(sgt, cm_off(cc, d, DK));
+        pre += (cc < cb) ? x : 0.f;
         gtot += x;
       }
-      float dG[32], dqv[32], dkv[32];
-      float run = pre, klsum = 0.f, kgam[32];
-      const bf16* qcol = q + hoff + tok0 * rstride + d;
-      const bf16* kcol = k + hoff + tok0 * rstride + d;
-      for (int jj = 0; jj < 32; ++jj) {
-        const int cc = cb + jj;
-        const bool ok = cc < rows_valid;
-        run += ok ? __bfloat162float(gcol[cc * rstride]) : 0.f;
-        const float qv = ok ? __bfloat162float(qcol[cc * rstride]) : 0.f;
-        const float kv = ok ? __bfloat162float(kcol[cc * rstride]) : 0.f;
-        const float gam = __expf(run);
-        const float gi = slow ? 0.f : __expf(-run);
-        const float lam = __expf(fminf(gtot - run, 0.f));
-        dqv[jj] = dqg[jj] * gam;
-        dkv[jj] = dkg[jj] * gam + dki[jj] * gi + dkl[jj] * lam;
-        const float klt = dkl[jj] * kv * lam;
-        dG[jj] = dqg[jj] * qv * gam + dkg[jj] * kv * gam - dki[jj] * kv * gi - klt;
-        klsum += klt;
-        kgam[jj] = kv * gam;
-      }
+      const float gC = gamC[d];
+      float* Gs = reinterpret_cast<float*>(sm + P_TP);  // exact path: G fp32 [64][128]
       if (slow) {
-        const float* Gs = reinterpret_cast<const float*>(sm + P_SB);
+        float run2 = pre;
         for (int jj = 0; jj < 32; ++jj) {
-          const int cc = cb + jj;
-          const float Gc = Gs[cc * DK + d];
-          const float qc = ldbf(sm + P_SQ, cm_off(cc, d, DK)), kc = ldbf(sm + P_SK, cm_off(cc, d, DK));
-          float dra = 0.f, drk = 0.f, dca = 0.f, dck = 0.f;
-          for (int i = 0; i <= cc; ++i) {
-            const float ke = ldbf(sm + P_SK, cm_off(i, d, DK)) * __expf(fminf(Gc - Gs[i * DK + d], 0.f));
-            dra += ldbf(sm + P_KL, cm_off(cc, i, C)) * ke;
-            drk += ldbf(sm + P_KL, cm_off(64 + cc, i, C)) * ke;
+          run2 += ldbf(sgt, cm_off(cb + jj, d, DK));
+          Gs[(cb + jj) * DK + d] = run2;
+        }
+        __syncthreads();
+      }
+      float dG[32];
+      float run = pre, klsum = 0.f;
+      float* TR = reinterpret_cast<float*>(sm + P_SB);  // dbeta partials [128][64], xor-swizzled
+      const size_t gbase = hoff + tok0 * rstride + d;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        const int c16 = cb + 16 * part;
+        float dqg[16], dkg[16], dki[16], dkl[16], yw[16], yu[16];
+        tmem_ld16(T_IV + tl + c16, dqg);
+        tmem_ld16(T_IV + 64 + tl + c16, dkg);
+        tmem_ld16(T_SC + tl + c16, dki);
+        tmem_ld16(T_KL + tl + c16, dkl);
+        tmem_ld16(T_UF + tl + c16, yw);
+        tmem_ld16(T_UF + 64 + tl + c16, yu);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int cc = c16 + i;
+          const bool ok = cc < rows_valid;
+          run += ldbf(sgt, cm_off(cc, d, DK));
+          const float gam = __expf(run);
+          float dqv, dkv, dGv, kgam;
+          if (!slow) {
+            const float gi = __expf(-run);
+            const float qg = ldbf(A3, cm_off(64 + cc, d, DK));
+            const float kg = ldbf(A3, cm_off(128 + cc, d, DK));
+            const float ki = ldbf(sm + P_KI, cm_off(cc, d, DK));
+            const float s2 = dki[i] + gC * dkl[i];
+            dqv = dqg[i] * gam;
+            dkv = dkg[i] * gam + s2 * gi;
+            dGv = dqg[i] * qg + dkg[i] * kg - s2 * ki;
+            klsum += gC * dkl[i] * ki;
+            kgam = kg;
+          } else {
+            const float qv = ldbf(sm + P_SQ, cm_off(cc, d, DK));
+            const float kv = ldbf(sm + P_SK, cm_off(cc, d, DK));
+            const float lam = __expf(fminf(gtot - run, 0.f));
+            dqv = dqg[i] * gam;
+            dkv = dkg[i] * gam + dkl[i] * lam;
+            dGv = dqg[i] * qv * gam + dkg[i] * kv * gam - dkl[i] * kv * lam;
+            klsum += dkl[i] * kv * lam;
+            kgam = kv * gam;
+            // exact score adjoints (direct decay ratio)
+            float dra = 0.f, drk = 0.f, dca = 0.f, dck = 0.f;
+            for (int i2 = 0; i2 <= cc; ++i2) {
+              const float ke = ldbf(sm + P_SK, cm_off(i2, d, DK)) * __expf(fminf(run - Gs[i2 * DK + d], 0.f));
+              dra += ldbf(sm + P_KL, cm_off(cc, i2, C)) * ke;
+              drk += ldbf(sm + P_KL, cm_off(64 + cc, i2, C)) * ke;
+            }
+            for (int r2 = cc; r2 < C; ++r2) {
+              const float e = __expf(fminf(Gs[r2 * DK + d] - run, 0.f));
+              dca += ldbf(sm + P_KL, cm_off(r2, cc, C)) * ldbf(sm + P_SQ, cm_off(r2, d, DK)) * e;
+              dck += ldbf(sm + P_KL, cm_off(64 + r2, cc, C)) * ldbf(sm + P_SK, cm_off(r2, d, DK)) * e;
+            }
+            dqv += dra;
+            dkv += drk + dca + dck;
+            dGv += dra * qv + drk * kv - (dca + dck) * kv;
           }
-          for (int r2 = cc; r2 < C; ++r2) {
-            const float e = __expf(fminf(Gs[r2 * DK + d] - Gc, 0.f));
-            dca += ldbf(sm + P_KL, cm_off(r2, cc, C)) * ldbf(sm + P_SQ, cm_off(r2, d, DK)) * e;
-            dck += ldbf(sm + P_KL, cm_off(64 + r2, cc, C)) * ldbf(sm + P_SK, cm_off(r2, d, DK)) * e;
+          dG[16 * part + i] = dGv;
+          const float vv = ldbf(sm + P_V, cm_off(cc, d, DV));
+          TR[d * 64 + (cc ^ (d & 63))] = yw[i] * kgam + yu[i] * vv;
+          if (ok) {
+            dq[gbase + cc * rstride] = __float2bfloat16_rn(dqv);
+            dk[gbase + cc * rstride] = __float2bfloat16_rn(dkv);
+            dv[gbase + cc * rstride] = __float2bfloat16_rn(beta_s[cc] * yu[i]);
           }
-          dqv[jj] += dra;
-          dkv[jj] += drk + dca + dck;
-          dG[jj] += dra * qc + drk * kc - (dca + dck) * kc;
         }
       }
       float gsum = 0.f;
@@ -763,43 +813,24 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       for (int jj = 0; jj < 32; ++jj) gsum += dG[jj];
       xch[(0 * 2 + hh) * 128 + d] = gsum;
       xch[(1 * 2 + hh) * 128 + d] = klsum;
-      // dbeta += rowsum(Yw (Gam K)) over d, and rowsum(Yu v) over j (same lane index)
-      {
-        float yw[32], yu[32];
-        tmem_ld32(T_UF + tl + cb, yw);
-        tmem_ld32(T_UF + 64 + tl + cb, yu);
-        tmem_wait_ld();
-        const bf16* vcol = v + hoff + tok0 * rstride + d;
-        bf16* dvcol = dv + hoff + tok0 * rstride + d;
-        for (int s = 0; s < 32; ++s) {
-          const int jj = (s + lane) & 31;  // stagger the shared-memory atomics
-          const int cc = cb + jj;
-          const bool ok = cc < rows_valid;
-          const float vv = ok ? __bfloat162float(vcol[cc * rstride]) : 0.f;
-          atomicAdd(&dbs[cc], yw[jj] * kgam[jj] + yu[jj] * vv);
-        }
-        for (int jj = 0; jj < 32; ++jj) {
-          const int cc = cb + jj;
-          if (cc < rows_valid) dvcol[cc * rstride] = __float2bfloat16_rn(beta_s[cc] * yu[jj]);
-        }
-      }
+      KDA_PT(2, 16);
       __syncthreads();
-      const float dGC = xch[(1 * 2 + 0) * 128 + d] + xch[(1 * 2 + 1) * 128 + d] + gamC[d] * dgc[d];
+      if (tid < C) {  // dbeta: rowsum over the 128 channels of the partials
+        float acc = dbs[tid];
+        for (int dd = 0; dd < 128; ++dd) acc += TR[dd * 64 + (tid ^ (dd & 63))];
+        if (tid < rows_valid) dbeta[(tok0 + tid) * H + h] = __float2bfloat16_rn(acc);
+      }
+      KDA_PT(2, 17);
+      const float dGC = xch[(1 * 2 + 0) * 128 + d] + xch[(1 * 2 + 1) * 128 + d] + gC * dgc[d];
       float acc = dGC + (hh == 0 ? xch[(0 * 2 + 1) * 128 + d] : 0.f);
-      bf16* dqcol = dq + hoff + tok0 * rstride + d;
-      bf16* dkcol = dk + hoff + tok0 * rstride + d;
-      bf16* dgcol = dg + hoff + tok0 * rstride + d;
+#pragma unroll
       for (int jj = 31; jj >= 0; --jj) {
         acc += dG[jj];
         const int cc = cb + jj;
-        if (cc < rows_valid) {
-          dqcol[cc * rstride] = __float2bfloat16_rn(dqv[jj]);
-          dkcol[cc * rstride] = __float2bfloat16_rn(dkv[jj]);
-          dgcol[cc * rstride] = __float2bfloat16_rn(acc);
-        }
+        if (cc < rows_valid) dg[gbase + cc * rstride] = __float2bfloat16_rn(acc);
       }
-      if (tid < C && tid < rows_valid) dbeta[(tok0 + tid) * H + h] = __float2bfloat16_rn(dbs[tid]);
     }
+    KDA_PT(2, 18);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();

@@ -48,12 +48,22 @@ __device__ __forceinline__ void store_row32<bf16>(bf16* dst, const float* v) {
   for (int j = 0; j < 32; j += 8) *reinterpret_cast<uint4*>(dst + j) = pack_bf16x8(v + j);
 }
 
+// Thread -> 16-byte chunk mapping for CM tiles: 8 consecutive lanes cover the
+// 8 rows of one core matrix (conflict-free in shared memory) and lanes l, l+8,
+// l+16, l+24 cover 64 contiguous bytes of one row in global memory.
+__device__ __forceinline__ void chunk_of(int i, int n_rg, int& r, int& cg) {
+  const int cq = i & 7, cgl = (i >> 3) & 3, rest = i >> 5;
+  r = 8 * (rest % n_rg) + cq;
+  cg = 4 * (rest / n_rg) + cgl;
+}
+
 // cp.async a [64][128] bf16 tile whose row r starts at src + r*rstride into a
 // CM tile (rows >= rows_valid are zero-filled).  Does not commit.
 __device__ __forceinline__ void stage_tile(unsigned char* dst, const bf16* src, int rows_valid,
                                            size_t rstride) {
   for (int i = threadIdx.x; i < C * 16; i += NT) {
-    const int r = i >> 4, cg = i & 15;
+    int r, cg;
+    chunk_of(i, 8, r, cg);
     const bool ok = r < rows_valid;
     const bf16* p = ok ? src + static_cast<size_t>(r) * rstride + cg * 8 : src;
     cp_async16(dst + cm_off(r, cg * 8, 128), p, ok);
@@ -63,85 +73,95 @@ __device__ __forceinline__ void stage_tile(unsigned char* dst, const bf16* src, 
 // cp.async a contiguous [128][128] bf16 matrix (row stride 128) into a CM tile.
 __device__ __forceinline__ void stage_square(unsigned char* dst, const bf16* src) {
   for (int i = threadIdx.x; i < 128 * 16; i += NT) {
-    const int r = i >> 4, cg = i & 15;
+    int r, cg;
+    chunk_of(i, 16, r, cg);
     cp_async16(dst + cm_off(r, cg * 8, 128), src + r * 128 + cg * 8, true);
   }
 }
 
-// Decay prep for one chunk.  Thread t owns channels 8(t&15).. and rows
-// 4(t>>4)..+3.  Reads the staged q, k, g tiles and writes the bf16 operand
+// Decay prep for one chunk.  Thread t owns channels 8(t>>4)..+7 and the rows
+// 8k + (t&7) for k in [4h, 4h+4), h = (t>>3)&1, so each group of 8 lanes reads
+// and writes whole core matrices (conflict-free).  G = cumsum(g) over the chunk
+// is formed with warp shuffles (no shared memory).  Writes the bf16 operand
 // tiles (CM, 128 columns):
 //   qg = q*Gam, kg = k*Gam, ki = k*exp(-G) (fast path only), kl = k*exp(G_C - G)
-// with G = cumsum(g) over the chunk, Gam = exp(G).  gamC[d] = exp(G_C[d]).
-// Any of the destinations may be null.  Returns true ("slow") when some
-// channel decays by more than kExpBudget over the chunk; the caller must then
-// use the exact score path.  `part` is 8 KB of scratch.  G (fp32) is returned
-// in registers for the caller.
+// with Gam = exp(G); gamC[d] = exp(G_C[d]).  Any destination may be null.
+// Returns true ("slow") when some channel decays by more than kExpBudget over
+// the chunk; the caller must then use the exact score path.  G (fp32) for the
+// thread's 4 rows x 8 channels is returned in registers.
+__device__ __forceinline__ int prep_row(int k) {
+  const int t = threadIdx.x;
+  return 8 * (4 * ((t >> 3) & 1) + k) + (t & 7);
+}
+
 __device__ __forceinline__ bool prep(const unsigned char* sq, const unsigned char* sk,
                                      const unsigned char* sg, unsigned char* qg_dst,
                                      unsigned char* kg_dst, unsigned char* ki_dst,
-                                     unsigned char* kl_dst, float* part, float* gamC,
-                                     float (&G)[4][8]) {
-  const int tid = threadIdx.x, cg = tid & 15, rg4 = tid >> 4;
+                                     unsigned char* kl_dst, float* gamC, float (&G)[4][8]) {
+  const int tid = threadIdx.x, cg = tid >> 4, half = (tid >> 3) & 1, rr = tid & 7;
+  const unsigned full = 0xffffffffu;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) unpack_bf16x8(ld16(sg, cm_off(prep_row(k), 8 * cg, 128)), G[k]);
   float run[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) run[e] = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float gv[8];
-    unpack_bf16x8(ld16(sg, cm_off(4 * rg4 + i, 8 * cg, 128)), gv);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) { run[e] += gv[e]; G[i][e] = run[e]; }
-  }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) part[(rg4 * 16 + cg) * 8 + e] = run[e];
-  __syncthreads();
-  float pre[8], tot[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) { pre[e] = 0.f; tot[e] = 0.f; }
-  for (int p = 0; p < 16; ++p) {
+  for (int k = 0; k < 4; ++k) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float x = part[(p * 16 + cg) * 8 + e];
-      tot[e] += x;
-      if (p < rg4) pre[e] += x;
+      float x = G[k][e];
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) {
+        const float y = __shfl_up_sync(full, x, off, 8);
+        if (rr >= off) x += y;
+      }
+      const float grp = __shfl_sync(full, x, 7, 8);  // total of this 8-row group
+      G[k][e] = x + run[e];
+      run[e] += grp;
     }
   }
   bool strong = false;
+  float tot[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    strong |= fabsf(tot[e]) > kExpBudget;
+    const float lo = __shfl_up_sync(full, run[e], 8);    // half 0's total, seen by half 1
+    const float hi = __shfl_down_sync(full, run[e], 8);  // half 1's total, seen by half 0
+    if (half) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) G[i][e] += pre[e];
+      for (int k = 0; k < 4; ++k) G[k][e] += lo;
+      tot[e] = lo + run[e];
+    } else {
+      tot[e] = run[e] + hi;
+    }
+    strong |= fabsf(tot[e]) > kExpBudget;
   }
   float gce[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) gce[e] = __expf(tot[e]);
-  if (rg4 == 0) {
+  if (half == 0 && rr == 0) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) gamC[8 * cg + e] = gce[e];
   }
-  // one barrier publishes gamC, frees `part`, and decides the path CTA-wide
+  // one barrier publishes gamC and decides the path for the whole CTA
   const bool slow = __syncthreads_or(strong) != 0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = 4 * rg4 + i;
-    const uint32_t off = cm_off(r, 8 * cg, 128);
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t off = cm_off(prep_row(k), 8 * cg, 128);
     float qv[8], kv[8], qg[8], kg[8], ki[8], kl[8];
     unpack_bf16x8(ld16(sq, off), qv);
     unpack_bf16x8(ld16(sk, off), kv);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float gam = __expf(G[i][e]);
+      const float gam = __expf(G[k][e]);
       qg[e] = qv[e] * gam;
       kg[e] = kv[e] * gam;
       if (!slow) {
-        const float gi = __expf(-G[i][e]);
+        const float gi = __expf(-G[k][e]);
         ki[e] = kv[e] * gi;
         kl[e] = kv[e] * (gi * gce[e]);
       } else {
         ki[e] = 0.f;
-        kl[e] = kv[e] * __expf(fminf(tot[e] - G[i][e], 0.f));
+        kl[e] = kv[e] * __expf(fminf(tot[e] - G[k][e], 0.f));
       }
     }
     if (qg_dst) st16(qg_dst, off, pack_bf16x8(qg));
@@ -205,64 +225,86 @@ __device__ __forceinline__ void scores_exact(const unsigned char* sq, const unsi
 
 // Store G (registers of prep) as fp32 [64][128] for scores_exact.
 __device__ __forceinline__ void store_G(float* Gf, const float (&G)[4][8]) {
-  const int cg = threadIdx.x & 15, rg4 = threadIdx.x >> 4;
+  const int cg = threadIdx.x >> 4;
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int k = 0; k < 4; ++k)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) Gf[(4 * rg4 + i) * DK + 8 * cg + e] = G[i][e];
+    for (int e = 0; e < 8; ++e) Gf[prep_row(k) * DK + 8 * cg + e] = G[k][e];
 }
 
-// T = (I + L)^-1 with L = diag(beta) Akk (strictly lower, 64 x 64), by blocked
-// forward substitution on 16 x 16 blocks.  All threads take part; ends synced.
+// One merge step of the recursive-doubling inverse: for every pair of BS x BS
+// diagonal blocks already inverted (A^-1 above, B^-1 below), fill the block
+// between them with -B^-1 diag(beta) C A^-1.  All loops have compile-time
+// bounds (fully unrolled, so the shared-memory loads issue back to back).
+template <int BS>
+__device__ __forceinline__ void solve_merge(const float* Akk, const float* beta_s, float* Tm) {
+  constexpr int PER = (C / (2 * BS)) * BS * BS / NT;  // outputs per thread: 1, 2, 4
+  const int tid = threadIdx.x;
+  float x[PER];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int idx = tid + e * NT;
+    const int blk = idx / (BS * BS), r = (idx / BS) % BS, c = idx % BS, o = 2 * BS * blk;
+    float acc = 0.f;
+#pragma unroll
+    for (int p = 0; p < BS; ++p)
+      if (p >= c) acc += Akk[sw64(o + BS + r, o + p)] * Tm[sw64(o + p, o + c)];
+    x[e] = beta_s[o + BS + r] * acc;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int idx = tid + e * NT;
+    const int blk = idx / (BS * BS), r = (idx / BS) % BS, c = idx % BS, o = 2 * BS * blk;
+    Tm[sw64(o + BS + r, o + c)] = x[e];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int idx = tid + e * NT;
+    const int blk = idx / (BS * BS), r = (idx / BS) % BS, c = idx % BS, o = 2 * BS * blk;
+    float acc = 0.f;
+#pragma unroll
+    for (int m = 0; m < BS; ++m)
+      if (m <= r) acc += Tm[sw64(o + BS + r, o + BS + m)] * Tm[sw64(o + BS + m, o + c)];
+    x[e] = -acc;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int idx = tid + e * NT;
+    const int blk = idx / (BS * BS), r = (idx / BS) % BS, c = idx % BS, o = 2 * BS * blk;
+    Tm[sw64(o + BS + r, o + c)] = x[e];
+  }
+  __syncthreads();
+}
+
+// T = (I + L)^-1 with L = diag(beta) Akk (strictly lower, 64 x 64) by
+// recursive doubling: the eight 8 x 8 diagonal blocks are inverted by forward
+// substitution, then blocks of 8, 16 and 32 are merged pairwise with
+//   [A 0; C B]^-1 = [A^-1 0; -B^-1 C A^-1 B^-1]   (fp32 throughout).
+// All threads take part; ends synced.
 __device__ __forceinline__ void solve_T(const float* Akk, const float* beta_s, float* Tm) {
   const int tid = threadIdx.x;
   for (int idx = tid; idx < C * C; idx += NT) Tm[idx] = 0.f;  // the swizzle is a permutation
   __syncthreads();
-  if (tid < 64) {  // diagonal blocks, one column per thread
-    const int bb = tid >> 4, j = tid & 15, o = 16 * bb;
-    float x[16];
+  if (tid < 64) {  // diagonal 8x8 blocks, one column per thread
+    const int o = 8 * (tid >> 3), j = tid & 7;
+    float x[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       float acc = 0.f;
 #pragma unroll
       for (int m = 0; m < i; ++m) acc += Akk[sw64(o + i, o + m)] * x[m];
       x[i] = ((i == j) ? 1.f : 0.f) - beta_s[o + i] * acc;
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) Tm[sw64(o + i, o + j)] = x[i];
+    for (int i = 0; i < 8; ++i) Tm[sw64(o + i, o + j)] = x[i];
   }
   __syncthreads();
-  for (int dl = 1; dl < 4; ++dl) {  // off-diagonal blocks by distance from the diagonal
-    const int nblk = 4 - dl;
-    float xs[3];
-    for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
-      const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      const int bi = bj + dl;
-      float acc = 0.f;
-      for (int m = 16 * bj; m < 16 * bi; ++m) acc += Akk[sw64(16 * bi + r, m)] * Tm[sw64(m, 16 * bj + cc)];
-      xs[n] = beta_s[16 * bi + r] * acc;
-    }
-    __syncthreads();
-    for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
-      const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      Tm[sw64(16 * (bj + dl) + r, 16 * bj + cc)] = xs[n];
-    }
-    __syncthreads();
-    for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
-      const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      const int bi = bj + dl;
-      float acc = 0.f;
-#pragma unroll
-      for (int m = 0; m < 16; ++m) acc -= Tm[sw64(16 * bi + r, 16 * bi + m)] * Tm[sw64(16 * bi + m, 16 * bj + cc)];
-      xs[n] = acc;
-    }
-    __syncthreads();
-    for (int e = tid, n = 0; e < nblk * 256; e += NT, ++n) {
-      const int bj = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      Tm[sw64(16 * (bj + dl) + r, 16 * bj + cc)] = xs[n];
-    }
-    __syncthreads();
-  }
+  solve_merge<8>(Akk, beta_s, Tm);
+  solve_merge<16>(Akk, beta_s, Tm);
+  solve_merge<32>(Akk, beta_s, Tm);
 }
 
 // Write row r, columns c0..c0+15 of a fp32 swizzled 64x64 matrix M (times

@@ -35,7 +35,7 @@ constexpr int OFF_KI = OFF_A3 + 49152;          // K*Gi CM[64][128]   | T fp32 |
 constexpr int OFF_TP = OFF_KI + 16384;          // [T b ; P b] CM[128][64]    | G fp32 (slow)
 constexpr int OFF_KL = OFF_TP + 16384;          // lam*K CM[64][128]
 constexpr int OFF_SB = OFF_KL + 16384;          // S bf16 CM[128][128] | Aqk fp32 + Akk fp32
-constexpr int OFF_VT = OFF_SB + 32768;          // v~ CM[64][128]      | cumsum partials
+constexpr int OFF_VT = OFF_SB + 32768;          // v~ CM[64][128]      | T, Aqk bf16 [64][64]
 constexpr int OFF_BETA = OFF_VT + 16384;        // beta fp32[64]
 constexpr int OFF_GC = OFF_BETA + 256;          // Gam_C fp32[128]
 constexpr int OFF_BAR = OFF_GC + 512;           // mbarrier + tmem slot
@@ -97,6 +97,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   const uint32_t t_lane = static_cast<uint32_t>(32 * qw) << 16;
   const uint32_t T_D = tbase;          // cols [0, 256): MMA results
   const uint32_t T_S = tbase + 256;    // cols [256, 384): the state
+  const uint32_t T_P = tbase + 384;    // cols [384, 448): P = Aqk T
   uint32_t phase = 0;
   bool failed = false;
 
@@ -124,6 +125,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   unsigned char* A3 = sm + OFF_A3;
   const uint32_t a3_addr = smem_u32(A3);
 
+  KDA_PT_INIT();
   for (int c = 0; c < n_chunks; ++c) {
     const int t0 = c * C;
     const int rows_valid = min(C, T - t0);
@@ -131,14 +133,15 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
     __syncthreads();
 
+    KDA_PT(0, 0);
     // ---------------- prep: G, exponentials, operand tiles ----------------
     float* Aq = reinterpret_cast<float*>(sm + OFF_SB);
     float* Akk = Aq + 4096;
     {
       float G[4][8];
       const bool slow = prep(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, A3 + cm_off(64, 0, DK),
-                             A3 + cm_off(128, 0, DK), sm + OFF_KI, sm + OFF_KL,
-                             reinterpret_cast<float*>(sm + OFF_VT), gamC, G);
+                             A3 + cm_off(128, 0, DK), sm + OFF_KI, sm + OFF_KL, gamC, G);
+      KDA_PT(0, 1);
       if (!slow) {
         fence_async_smem();
         __syncthreads();
@@ -155,7 +158,9 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, true);
         failed |= !mma_wait();
         if (__syncthreads_or(failed)) break;
+        KDA_PT(0, 2);
         scores_epilogue(T_D, Aq, Akk);
+        KDA_PT(0, 3);
       } else {
         // exact scores on the CUDA cores (strong decay: the single anchor would overflow)
         float* Gf = reinterpret_cast<float*>(sm + OFF_KI);  // [64][128] fp32 across KI|TP
@@ -166,31 +171,44 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, true);
       }
     }
-    // ---------------- solve: T = (I + L)^-1 (blocked), P = Aqk T ----------------
+    // ---------------- solve: T = (I + L)^-1, then P = Aqk T on the tensor cores ----------------
     {
       float* Tm = reinterpret_cast<float*>(sm + OFF_KI);
       __syncthreads();
+      KDA_PT(0, 12);
       solve_T(Akk, beta_s, Tm);
-      // P = Aqk T (row r, 16 columns per thread) and the [T b ; P b] bf16 operand
+      KDA_PT(0, 4);
       const int r = tid >> 2, c0 = (tid & 3) * 16;
-      float p[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) p[j] = 0.f;
-      for (int m = 0; m <= r; ++m) {
-        const float a = Aq[sw64(r, m)];
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(Tm + sw64(m, c0 + j));
-          p[j] += a * t4.x; p[j + 1] += a * t4.y; p[j + 2] += a * t4.z; p[j + 3] += a * t4.w;
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) p[j] *= beta_s[c0 + j];
-      unsigned char* TP = sm + OFF_TP;
-      row16_to_cm(TP, r, Tm, r, c0, beta_s);
-      st16(TP, cm_off(64 + r, c0, C), pack_bf16x8(p));
-      st16(TP, cm_off(64 + r, c0 + 8, C), pack_bf16x8(p + 8));
+      row16_to_cm(sm + OFF_TP, r, Tm, r, c0, beta_s);          // T diag(beta)
+      row16_to_cm(sm + OFF_VT, r, Tm, r, c0, nullptr);         // T      (bf16, K x N)
+      row16_to_cm(sm + OFF_VT + 8192, r, Aq, r, c0, nullptr);  // Aqk    (bf16, M x K)
     }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {  // P = Aqk T   (M = 64: row r at lane 32(r/16) + r%16)
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16(64, 64, false, true);
+      const uint32_t tb = smem_u32(sm + OFF_VT), aqb = smem_u32(sm + OFF_VT + 8192);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_P, desc_kmajor(aqb + ks * 256, C), desc_mnmajor(tb + ks * 2048, C), idesc, ks > 0);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // P diag(beta) -> rows 64..127 of the [T b ; P b] operand
+      float vals[32];
+      tmem_ld32(T_P + t_lane + hh * 32, vals);
+      tmem_wait_ld();
+      if (lane < 16) {
+        const int r = 16 * qw + lane;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) vals[j] *= beta_s[hh * 32 + j];
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) st16(sm + OFF_TP, cm_off(64 + r, hh * 32 + j, C), pack_bf16x8(vals + j));
+      }
+    }
+    KDA_PT(0, 5);
     fence_async_smem();
     __syncthreads();
     // ---------------- MMA_wu: [Tb ; Pb] [K*Gam | V] ----------------
@@ -209,6 +227,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
     if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, false);
+    KDA_PT(0, 6);
     // ---------------- E2: W -> A3[0:64), Q~ = Gam Q - Aqk W -> A3[64:128) ----------------
     {
       const int R = 32 * qw + lane;
@@ -233,6 +252,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         }
       }
     }
+    KDA_PT(0, 7);
     // ---------------- S pass: S_c -> bf16 operand (+ checkpoint), S *= Gam_C ----------------
     {
       const int d = 32 * qw + lane;
@@ -255,6 +275,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    KDA_PT(0, 8);
     // ---------------- MMA_1: [W ; Q~] S ----------------
     if (tid == 0) {
       tc_fence_after();
@@ -267,6 +288,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(0, 9);
     // ---------------- E3: v~ = U - W S -> bf16 ; O = Q~ S + Aqk U -> global ----------------
     {
       const int R = 32 * qw + lane;
@@ -294,6 +316,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    KDA_PT(0, 10);
     // ---------------- MMA_3: S += (lam K)^T v~ ----------------
     if (tid == 0) {
       tc_fence_after();
@@ -306,6 +329,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
+    KDA_PT(0, 11);
   }
 
   if (!failed && s_out) {

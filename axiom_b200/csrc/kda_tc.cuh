@@ -109,6 +109,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 16 columns: thread i gets lane (base+i), cols [c, c+16).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
   const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
   asm volatile(
@@ -186,3 +197,22 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
 
 }  // namespace tc
 }  // namespace kda
+
+// Optional per-phase cycle counters for performance work: compiled only with
+// -DKDA_PHASE_TIMERS (never in the shipped library), in a single-translation-
+// unit build that defines `__device__ unsigned long long g_kda_phase[3][32]`
+// before including this header.  Thread 0 of CTA 0 adds the cycles since the
+// previous mark to slot i.
+#ifdef KDA_PHASE_TIMERS
+#define KDA_PT_INIT() long long kda_pt_prev_ = clock64()
+#define KDA_PT(k, i)                                                        \
+  do {                                                                      \
+    const long long kda_pt_now_ = clock64();                                \
+    if (blockIdx.x == 0 && threadIdx.x == 0)                                \
+      g_kda_phase[k][i] += static_cast<unsigned long long>(kda_pt_now_ - kda_pt_prev_); \
+    kda_pt_prev_ = kda_pt_now_;                                             \
+  } while (0)
+#else
+#define KDA_PT_INIT() do {} while (0)
+#define KDA_PT(k, i) do {} while (0)
+#endif

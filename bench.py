@@ -165,6 +165,9 @@ def run_b200(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     peaks = _peaks()
     cfg = dict(CFG3)
+    for key, val in (("B", args.batch), ("T", args.seqlen), ("H", args.heads)):
+        if val:
+            cfg[key] = val
     B, T, H, dk, dv, C = (cfg[k] for k in ("B", "T", "H", "dk", "dv", "chunk"))
     n_chunks = (T + C - 1) // C
     q, k, v, g, beta, do = make_train_inputs(torch, cfg, seed=1234 + rank, device=dev)
@@ -219,7 +222,7 @@ def run_b200(args):
     peak = peaks["bf16_sustained"] if ms * args.steps > 1000.0 else peaks["bf16"]
 
     # e2e through the public API with host buffers (rank-local), after the device timing
-    e2e = run_e2e(torch, KD, q, k, v, g, beta, do, C, args, dev)
+    e2e = run_e2e(torch, KD, q, k, v, g, beta, do, C, args, dev) if not args.no_e2e else {"ms": float("nan"), "h2d": 0, "d2h": 0}
     if world > 1:
         t = torch.tensor([e2e["ms"]], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -234,7 +237,7 @@ def run_b200(args):
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(sample_heads=args.cpu_heads, cfg=cfg)
 
-    launches_per_step = 2  # kda_fwd + kda_bwd, one kernel each on the current path
+    launches_per_step = 3  # kda_fwd (1 kernel) + kda_bwd (bwd_seq + bwd_par)
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -249,7 +252,7 @@ def run_b200(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (BASELINE distributions, seeded per rank)",
-            "config": {"workload": "cfg3 KDA chunked fwd+bwd", "B_per_rank": B, "T": T, "H": H,
+            "config": {"workload": "cfg3 KDA chunked fwd+bwd" if cfg == CFG3 else "reduced profiling case", "B_per_rank": B, "T": T, "H": H,
                        "dk": dk, "dv": dv, "chunk": C, "global_batch": B * world,
                        "parallelism": f"batch-sharded x{world}, no collective",
                        "l2": "inputs larger than L2 (no flush)",
@@ -427,6 +430,10 @@ def main():
     ap.add_argument("--cpu-heads", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the decode/prefill extras")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--batch", type=int, default=0, help="override B per rank (profiling cases)")
+    ap.add_argument("--seqlen", type=int, default=0, help="override T (profiling cases)")
+    ap.add_argument("--heads", type=int, default=0, help="override H (profiling cases)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # the timing contract needs >= 3 untimed warm-up steps
     if args.impl == "reference":
