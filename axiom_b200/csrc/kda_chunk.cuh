@@ -234,48 +234,83 @@ __device__ __forceinline__ void store_G(float* Gf, const float (&G)[4][8]) {
 
 // One merge step of the recursive-doubling inverse: for every pair of BS x BS
 // diagonal blocks already inverted (A^-1 above, B^-1 below), fill the block
-// between them with -B^-1 diag(beta) C A^-1.  All loops have compile-time
-// bounds (fully unrolled, so the shared-memory loads issue back to back).
-template <int BS>
+// between them with -B^-1 diag(beta) C A^-1.  Each thread owns an RB x CB
+// block of outputs (register blocking: RB + 1 shared-memory loads per RB*CB
+// FMAs); 256 threads cover the (64 / 2BS) blocks of BS x BS outputs.
+template <int BS, int RB, int CB>
 __device__ __forceinline__ void solve_merge(const float* Akk, const float* beta_s, float* Tm) {
-  constexpr int PER = (C / (2 * BS)) * BS * BS / NT;  // outputs per thread: 1, 2, 4
+  static_assert((C / (2 * BS)) * (BS / RB) * (BS / CB) == NT, "one output block per thread");
   const int tid = threadIdx.x;
-  float x[PER];
+  constexpr int NR = BS / RB, NC = BS / CB;
+  const int blk = tid / (NR * NC), rem = tid % (NR * NC);
+  const int r0 = (rem / NC) * RB, c0 = (rem % NC) * CB, o = 2 * BS * blk;
+  float x[RB][CB];
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NT;
-    const int blk = idx / (BS * BS), r = (idx / BS) % BS, c = idx % BS, o = 2 * BS * blk;
-    float acc = 0.f;
+  for (int i = 0; i < RB; ++i)
 #pragma unroll
-    for (int p = 0; p < BS; ++p)
-      if (p >= c) acc += Akk[sw64(o + BS + r, o + p)] * Tm[sw64(o + p, o + c)];
-    x[e] = beta_s[o + BS + r] * acc;
+    for (int j = 0; j < CB; ++j) x[i][j] = 0.f;
+  // X = C A^-1 (A^-1 lower triangular: rows p >= c0 only)
+#pragma unroll
+  for (int p = 0; p < BS; ++p) {
+    if (p >= c0) {
+      float a[CB];
+      if (CB == 2) {
+        const float2 t2 = *reinterpret_cast<const float2*>(Tm + sw64(o + p, o + c0));
+        a[0] = t2.x;
+        a[CB - 1] = t2.y;
+      } else {
+        a[0] = Tm[sw64(o + p, o + c0)];
+      }
+#pragma unroll
+      for (int i = 0; i < RB; ++i) {
+        const float cv = Akk[sw64(o + BS + r0 + i, o + p)];
+#pragma unroll
+        for (int j = 0; j < CB; ++j) x[i][j] += cv * a[j];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RB; ++i) {
+    const float b = beta_s[o + BS + r0 + i];
+#pragma unroll
+    for (int j = 0; j < CB; ++j) x[i][j] *= b;
   }
   __syncthreads();
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NT;
-    const int blk = idx / (BS * BS), r = (idx / BS) % BS, c = idx % BS, o = 2 * BS * blk;
-    Tm[sw64(o + BS + r, o + c)] = x[e];
+  for (int i = 0; i < RB; ++i)
+#pragma unroll
+    for (int j = 0; j < CB; ++j) Tm[sw64(o + BS + r0 + i, o + c0 + j)] = x[i][j];
+  __syncthreads();
+  // Y = -B^-1 X (B^-1 lower triangular: columns m <= r only)
+  float y[RB][CB];
+#pragma unroll
+  for (int i = 0; i < RB; ++i)
+#pragma unroll
+    for (int j = 0; j < CB; ++j) y[i][j] = 0.f;
+#pragma unroll
+  for (int m = 0; m < BS; ++m) {
+    if (m <= r0 + RB - 1) {
+      float xv[CB];
+      if (CB == 2) {
+        const float2 t2 = *reinterpret_cast<const float2*>(Tm + sw64(o + BS + m, o + c0));
+        xv[0] = t2.x;
+        xv[CB - 1] = t2.y;
+      } else {
+        xv[0] = Tm[sw64(o + BS + m, o + c0)];
+      }
+#pragma unroll
+      for (int i = 0; i < RB; ++i) {
+        const float bv = Tm[sw64(o + BS + r0 + i, o + BS + m)];
+#pragma unroll
+        for (int j = 0; j < CB; ++j) y[i][j] -= bv * xv[j];
+      }
+    }
   }
   __syncthreads();
 #pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NT;
-    const int blk = idx / (BS * BS), r = (idx / BS) % BS, c = idx % BS, o = 2 * BS * blk;
-    float acc = 0.f;
+  for (int i = 0; i < RB; ++i)
 #pragma unroll
-    for (int m = 0; m < BS; ++m)
-      if (m <= r) acc += Tm[sw64(o + BS + r, o + BS + m)] * Tm[sw64(o + BS + m, o + c)];
-    x[e] = -acc;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int e = 0; e < PER; ++e) {
-    const int idx = tid + e * NT;
-    const int blk = idx / (BS * BS), r = (idx / BS) % BS, c = idx % BS, o = 2 * BS * blk;
-    Tm[sw64(o + BS + r, o + c)] = x[e];
-  }
+    for (int j = 0; j < CB; ++j) Tm[sw64(o + BS + r0 + i, o + c0 + j)] = y[i][j];
   __syncthreads();
 }
 
@@ -302,9 +337,9 @@ __device__ __forceinline__ void solve_T(const float* Akk, const float* beta_s, f
     for (int i = 0; i < 8; ++i) Tm[sw64(o + i, o + j)] = x[i];
   }
   __syncthreads();
-  solve_merge<8>(Akk, beta_s, Tm);
-  solve_merge<16>(Akk, beta_s, Tm);
-  solve_merge<32>(Akk, beta_s, Tm);
+  solve_merge<8, 1, 1>(Akk, beta_s, Tm);
+  solve_merge<16, 2, 1>(Akk, beta_s, Tm);
+  solve_merge<32, 2, 2>(Akk, beta_s, Tm);
 }
 
 // Write row r, columns c0..c0+15 of a fp32 swizzled 64x64 matrix M (times
