@@ -27,6 +27,7 @@ SIGNATURES = {
     "kda_bwd_workspace_bytes": ([_I] * 7, _Z),
     "kda_bwd": ([_P] * 14 + [_P, _Z] + [_I] * 9 + [_P], _I),
     "kda_decode": ([_P] * 7 + [_I] * 5 + [_P], _I),
+    "kda_bwd_noalloc": ([_P] * 14 + [_I] * 9 + [_P], _I),
 }
 
 _lib = None

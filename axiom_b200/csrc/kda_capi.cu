@@ -58,6 +58,8 @@ const char* kda_strerror(int status) {
     case KDA_ERR_LAUNCH: return "CUDA launch failed";
     case KDA_ERR_WORKSPACE: return "workspace missing or too small";
     case KDA_ERR_DEVICE: return "no usable CUDA device";
+    case KDA_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than kda_bwd_noalloc's fixed array (KDA_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown status";
   }
 }

@@ -22,9 +22,11 @@
  *   - T need not be a multiple of the chunk: the ragged tail is computed as
  *     zero-padded rows (q = k = v = 0, beta = 0, g = 0), which leaves the state
  *     and every real row exactly as the padded reference computes them.
- *   - Every entry point is stateless, allocates nothing, never synchronises
- *     the host, and only enqueues work on `stream` (NULL = legacy default
- *     stream).  Scratch memory comes from the caller (`workspace`).
+ *   - Every entry point allocates nothing, never synchronises the host, and
+ *     only enqueues work on `stream` (NULL = legacy default stream).  Scratch
+ *     memory comes from the caller (`workspace`), except for kda_bwd_noalloc,
+ *     which uses a fixed array built into the library (see its comment); all
+ *     other entry points are stateless.
  *   - Return value: KDA_OK (0) or a negative KDA_ERR_* code; invalid shapes,
  *     dtypes, alignment or null pointers are rejected before any launch
  *     (fail-closed, the reference's typed-error contract net/kda.py:759-763).
@@ -56,7 +58,8 @@ enum {
   KDA_ERR_NULL = -4,    /* a required pointer is NULL */
   KDA_ERR_LAUNCH = -5,  /* the CUDA launch itself failed */
   KDA_ERR_WORKSPACE = -6, /* workspace missing or too small */
-  KDA_ERR_DEVICE = -7   /* no sm_100 device / device query failed */
+  KDA_ERR_DEVICE = -7,  /* no sm_100 device / device query failed */
+  KDA_ERR_SCRATCH_LIMIT = -8 /* problem needs more than kda_bwd_noalloc's fixed scratch */
 };
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -105,6 +108,29 @@ int kda_bwd(const void* q, const void* k, const void* v, const void* g,
             void* dbeta, float* ds0, void* workspace, size_t workspace_bytes,
             int B, int T, int H, int dk, int dv, int chunk, int in_dtype,
             int do_dtype, int ckpt_dtype, kda_stream_t stream);
+
+/* Size of the fixed device scratch array used by kda_bwd_noalloc (32 MiB). */
+#define KDA_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* kda_bwd for callers that cannot allocate device memory.  No counterpart in
+ * the reference (XLA hands its kernels scratch through its own allocator).
+ * A framework's custom-call handler, a serving loop with a fixed memory
+ * budget, or any code that must not call cudaMalloc (it would take memory the
+ * framework has reserved, and it synchronises the device) cannot supply
+ * kda_bwd's workspace; this entry point takes the same arguments minus the
+ * workspace and uses a file-scope device array of KDA_NOALLOC_SCRATCH_BYTES
+ * instead, which every GPU that loads the library holds until exit.  It
+ * allocates nothing.  Problems whose kda_bwd_workspace_bytes exceeds the
+ * array are rejected with KDA_ERR_SCRATCH_LIMIT.  The first call on a device
+ * looks up the array's device address (make it before any stream capture).
+ * All calls share the array: calls whose kernels overlap on the GPU race and
+ * must be serialised; no scratch content needs clearing between calls. */
+int kda_bwd_noalloc(const void* q, const void* k, const void* v, const void* g,
+                    const void* beta, const void* s_ckpt, const void* do_,
+                    const float* dsT, void* dq, void* dk_, void* dv_, void* dg,
+                    void* dbeta, float* ds0, int B, int T, int H, int dk, int dv,
+                    int chunk, int in_dtype, int do_dtype, int ckpt_dtype,
+                    kda_stream_t stream);
 
 /* One recurrent decode step for N independent (sequence, head) states
  * (replaces _delta_step + o = S^T q, net/kda.py:298-310, :293):
