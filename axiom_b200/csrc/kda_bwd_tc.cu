@@ -37,6 +37,19 @@ using namespace chunk;
 
 __device__ __forceinline__ uint32_t lane_off(int qw) { return static_cast<uint32_t>(32 * qw) << 16; }
 
+// Backward workspace, one block per (batch, head, chunk) unit, written by
+// bwd_seq and read by bwd_par:
+//   [0, 32K)    dS' bf16 [128][128] row-major (the state cotangent entering the chunk)
+//   [32K, 40K)  T = (I + diag(beta) Akk)^-1   bf16 [64][64], CM byte layout
+//   [40K, 48K)  Aqk                           bf16 [64][64], CM byte layout
+//   [48K, 56K)  Akk                           bf16 [64][64], CM byte layout
+constexpr size_t WS_UNIT = 57344, WS_T = 32768, WS_AQ = 40960, WS_AK = 49152;
+
+// cp.async `bytes` (multiple of 16 * NT) contiguous bytes.
+__device__ __forceinline__ void stage_bytes(unsigned char* dst, const unsigned char* src, int bytes) {
+  for (int i = threadIdx.x; i < bytes / 16; i += NT) cp_async16(dst + 16 * i, src + 16 * i, true);
+}
+
 // ===========================================================================
 // bwd_seq
 // ===========================================================================
@@ -163,11 +176,15 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     KDA_PT(1, 1);
     __syncthreads();
     float* Tm = reinterpret_cast<float*>(sm + Q_KI);
-    solve_T(Akk, beta_s, Tm);
+    solve_T(Akk, beta_s, Tm, reinterpret_cast<float*>(sm + Q_TP));
     {
       const int r = tid >> 2, c0 = (tid & 3) * 16;
       row16_to_cm(sm + Q_TP, r, Tm, r, c0, beta_s);
       row16_to_cm(sm + Q_AQB, r, Aq, r, c0, nullptr);
+      unsigned char* wu = reinterpret_cast<unsigned char*>(dsw) + (unit * n_chunks + c) * WS_UNIT;
+      row16_to_cm(wu + WS_T, r, Tm, r, c0, nullptr);
+      row16_to_cm(wu + WS_AQ, r, Aq, r, c0, nullptr);
+      row16_to_cm(wu + WS_AK, r, Akk, r, c0, nullptr);
     }
     KDA_PT(1, 2);
     fence_async_smem();
@@ -202,7 +219,8 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     {  // dS' pass: bf16 operand + workspace copy, then dS *= Gam_C
       const int d = 32 * qw + lane;
-      bf16* wrow = dsw + ((unit * n_chunks + c) * DK + d) * DV;
+      bf16* wrow = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(dsw) +
+                                           (unit * n_chunks + c) * WS_UNIT) + d * DV;
       const float gcd = gamC[d];
       for (int half = 0; half < 2; ++half) {
         const int c0 = hh * 64 + half * 32;
@@ -295,15 +313,15 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 // ===========================================================================
 // bwd_par
 // ===========================================================================
-constexpr int P_SQ = 0;                  // q staging | T fp32 | dO
+constexpr int P_SQ = 0;                  // q staging | dO | raw q (exact path)
 constexpr int P_SK = 16384;              // k staging | dS' (lo) | dW^T [128][64]
 constexpr int P_SG = 32768;              // g staging | dS' (hi)
 constexpr int P_V = 49152;               // v staging | U bf16 [64][128]
 constexpr int P_A3 = 65536;              // [W ; Gam Q ; Gam K]
 constexpr int P_KI = P_A3 + 49152;       // K Gi
 constexpr int P_KL = P_KI + 16384;       // lam K | dU^T [128][64] | [dAqk ; beta dL] [128][64]
-constexpr int P_SB = P_KL + 16384;       // Aqk+Akk fp32 | S_c bf16 [128][128] | Yw^T, Yu^T | G fp32 (slow)
-constexpr int P_TP = P_SB + 32768;       // [Tb ; Pb] | partials | v~ bf16 [64][128] | G (slow, with TB/AQB)
+constexpr int P_SB = P_KL + 16384;       // S_c bf16 [128][128] | Yw^T, Yu^T | dbeta partials
+constexpr int P_TP = P_SB + 32768;       // T beta [64][64] | v~ bf16 [64][128] | G fp32 (exact path, with TB/AQB)
 constexpr int P_TB = P_TP + 16384;       // T bf16 [64][64]
 constexpr int P_AQB = P_TB + 8192;       // Aqk bf16
 constexpr int P_AKB = P_AQB + 8192;      // Akk bf16
@@ -379,8 +397,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     return ok;
   };
   const uint32_t a3 = smem_u32(A3);
-  float* Aq = reinterpret_cast<float*>(sm + P_SB);
-  float* Akk = Aq + 4096;
 
   KDA_PT_INIT();
   for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -392,10 +408,14 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     const size_t hoff = static_cast<size_t>(h) * DK;
     const size_t unit_sq = (static_cast<size_t>(b) * H + h) * n_chunks + c;  // chunk index
 
+    const unsigned char* wunit = reinterpret_cast<const unsigned char*>(dsw) + unit_sq * WS_UNIT;
     stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
     stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
     stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
     stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
+    stage_bytes(sm + P_TB, wunit + WS_T, 8192);   // T, Aqk, Akk from bwd_seq
+    stage_bytes(sm + P_AQB, wunit + WS_AQ, 8192);
+    stage_bytes(sm + P_AKB, wunit + WS_AK, 8192);
     cp_async_commit();
     if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + tid) * H + h]) : 0.f;
     if (tid < 128) dgc[tid] = 0.f;
@@ -404,44 +424,24 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     __syncthreads();
 
     KDA_PT(2, 0);
-    // ---- recompute: prep, scores, T, W, U ----
+    // ---- recompute: prep (the scores and T come from bwd_seq), then W, U ----
     float G[4][8];
     const bool slow = prep(sm + P_SQ, sm + P_SK, sm + P_SG, A3 + cm_off(64, 0, DK),
                            A3 + cm_off(128, 0, DK), sm + P_KI, sm + P_KL, gamC, G);
-    if (!slow) {
-      fence_async_smem();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        const uint32_t id = idesc_bf16(128, 64, false, false);
-#pragma unroll
-        for (int ks = 0; ks < DK / 16; ++ks)
-          mma_bf16(T_SC, desc_kmajor(a3 + 64 * 256 + ks * 256, DK),
-                   desc_kmajor(smem_u32(sm + P_KI) + ks * 256, DK), id, ks > 0);
-        mma_commit(mbar);
-      }
-      failed |= !mma_wait();
-      if (__syncthreads_or(failed)) break;
-      scores_epilogue(T_SC, Aq, Akk);
-    } else {
-      float* Gf = reinterpret_cast<float*>(sm + P_TP);  // TP|TB|AQB = 32 KB
-      store_G(Gf, G);
-      __syncthreads();
-      scores_exact(sm + P_SQ, sm + P_SK, Gf, Aq, Akk);
-    }
-    __syncthreads();
     KDA_PT(2, 1);
+    __syncthreads();
     // dS' into the free k/g staging
-    stage_square(sm + P_SK, dsw + unit_sq * (DK * DV));
+    stage_square(sm + P_SK, reinterpret_cast<const bf16*>(wunit));
     cp_async_commit();
-    float* Tm = reinterpret_cast<float*>(sm + P_SQ);
-    solve_T(Akk, beta_s, Tm);
-    {
+    {  // T diag(beta) from the bf16 T tile
       const int r = tid >> 2, c0 = (tid & 3) * 16;
-      row16_to_cm(sm + P_TP, r, Tm, r, c0, beta_s);
-      row16_to_cm(sm + P_TB, r, Tm, r, c0, nullptr);
-      row16_to_cm(sm + P_AQB, r, Aq, r, c0, nullptr);
-      row16_to_cm(sm + P_AKB, r, Akk, r, c0, nullptr);
+      float tv[16];
+      unpack_bf16x8(ld16(sm + P_TB, cm_off(r, c0, C)), tv);
+      unpack_bf16x8(ld16(sm + P_TB, cm_off(r, c0 + 8, C)), tv + 8);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) tv[j] *= beta_s[c0 + j];
+      st16(sm + P_TP, cm_off(r, c0, C), pack_bf16x8(tv));
+      st16(sm + P_TP, cm_off(r, c0 + 8, C), pack_bf16x8(tv + 8));
     }
     fence_async_smem();
     __syncthreads();
@@ -893,7 +893,7 @@ bool tc_bwd_supported(int dk, int dv, int C_, int in_dt, int do_dt) {
 
 size_t tc_bwd_workspace_bytes(int B, int T, int H) {
   const size_t n = (static_cast<size_t>(T) + C - 1) / C;
-  return static_cast<size_t>(B) * H * n * DK * DV * sizeof(bf16);
+  return static_cast<size_t>(B) * H * n * WS_UNIT;
 }
 
 int tc_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,

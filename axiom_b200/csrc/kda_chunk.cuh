@@ -235,10 +235,14 @@ __device__ __forceinline__ void store_G(float* Gf, const float (&G)[4][8]) {
 // One merge step of the recursive-doubling inverse: for every pair of BS x BS
 // diagonal blocks already inverted (A^-1 above, B^-1 below), fill the block
 // between them with -B^-1 diag(beta) C A^-1.  Each thread owns an RB x CB
-// block of outputs (register blocking: RB + 1 shared-memory loads per RB*CB
-// FMAs); 256 threads cover the (64 / 2BS) blocks of BS x BS outputs.
+// block of outputs; 256 threads cover the (64 / 2BS) blocks of BS x BS
+// outputs.  The loops run over whole blocks (the strictly upper parts of A^-1
+// and B^-1 are zero), four k-steps per iteration with float4 loads of the C /
+// B^-1 rows, so the shared-memory loads issue ahead of the FMAs.  X = C A^-1
+// goes through `xs` (32 * BS floats) so the step needs two barriers.
 template <int BS, int RB, int CB>
-__device__ __forceinline__ void solve_merge(const float* Akk, const float* beta_s, float* Tm) {
+__device__ __forceinline__ void solve_merge(const float* Akk, const float* beta_s, float* Tm,
+                                            float* xs) {
   static_assert((C / (2 * BS)) * (BS / RB) * (BS / CB) == NT, "one output block per thread");
   const int tid = threadIdx.x;
   constexpr int NR = BS / RB, NC = BS / CB;
@@ -249,64 +253,55 @@ __device__ __forceinline__ void solve_merge(const float* Akk, const float* beta_
   for (int i = 0; i < RB; ++i)
 #pragma unroll
     for (int j = 0; j < CB; ++j) x[i][j] = 0.f;
-  // X = C A^-1 (A^-1 lower triangular: rows p >= c0 only)
 #pragma unroll
-  for (int p = 0; p < BS; ++p) {
-    if (p >= c0) {
-      float a[CB];
+  for (int p = 0; p < BS; p += 4) {
+    float a[4][CB];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
       if (CB == 2) {
-        const float2 t2 = *reinterpret_cast<const float2*>(Tm + sw64(o + p, o + c0));
-        a[0] = t2.x;
-        a[CB - 1] = t2.y;
+        const float2 t2 = *reinterpret_cast<const float2*>(Tm + sw64(o + p + u, o + c0));
+        a[u][0] = t2.x;
+        a[u][CB - 1] = t2.y;
       } else {
-        a[0] = Tm[sw64(o + p, o + c0)];
-      }
-#pragma unroll
-      for (int i = 0; i < RB; ++i) {
-        const float cv = Akk[sw64(o + BS + r0 + i, o + p)];
-#pragma unroll
-        for (int j = 0; j < CB; ++j) x[i][j] += cv * a[j];
+        a[u][0] = Tm[sw64(o + p + u, o + c0)];
       }
     }
+#pragma unroll
+    for (int i = 0; i < RB; ++i) {
+      const float4 cv = *reinterpret_cast<const float4*>(Akk + sw64(o + BS + r0 + i, o + p));
+#pragma unroll
+      for (int j = 0; j < CB; ++j)
+        x[i][j] += cv.x * a[0][j] + cv.y * a[1][j] + cv.z * a[2][j] + cv.w * a[3][j];
+    }
   }
+  // X (scaled by beta) -> xs[blk][r][c], row-major BS x BS per block
 #pragma unroll
   for (int i = 0; i < RB; ++i) {
-    const float b = beta_s[o + BS + r0 + i];
+    const float bb = beta_s[o + BS + r0 + i];
 #pragma unroll
-    for (int j = 0; j < CB; ++j) x[i][j] *= b;
+    for (int j = 0; j < CB; ++j) xs[(blk * BS + r0 + i) * BS + c0 + j] = bb * x[i][j];
   }
   __syncthreads();
-#pragma unroll
-  for (int i = 0; i < RB; ++i)
-#pragma unroll
-    for (int j = 0; j < CB; ++j) Tm[sw64(o + BS + r0 + i, o + c0 + j)] = x[i][j];
-  __syncthreads();
-  // Y = -B^-1 X (B^-1 lower triangular: columns m <= r only)
   float y[RB][CB];
 #pragma unroll
   for (int i = 0; i < RB; ++i)
 #pragma unroll
     for (int j = 0; j < CB; ++j) y[i][j] = 0.f;
 #pragma unroll
-  for (int m = 0; m < BS; ++m) {
-    if (m <= r0 + RB - 1) {
-      float xv[CB];
-      if (CB == 2) {
-        const float2 t2 = *reinterpret_cast<const float2*>(Tm + sw64(o + BS + m, o + c0));
-        xv[0] = t2.x;
-        xv[CB - 1] = t2.y;
-      } else {
-        xv[0] = Tm[sw64(o + BS + m, o + c0)];
-      }
+  for (int m = 0; m < BS; m += 4) {
+    float xv[4][CB];
 #pragma unroll
-      for (int i = 0; i < RB; ++i) {
-        const float bv = Tm[sw64(o + BS + r0 + i, o + BS + m)];
+    for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int j = 0; j < CB; ++j) y[i][j] -= bv * xv[j];
-      }
+      for (int j = 0; j < CB; ++j) xv[u][j] = xs[(blk * BS + m + u) * BS + c0 + j];
+#pragma unroll
+    for (int i = 0; i < RB; ++i) {
+      const float4 bv = *reinterpret_cast<const float4*>(Tm + sw64(o + BS + r0 + i, o + BS + m));
+#pragma unroll
+      for (int j = 0; j < CB; ++j)
+        y[i][j] -= bv.x * xv[0][j] + bv.y * xv[1][j] + bv.z * xv[2][j] + bv.w * xv[3][j];
     }
   }
-  __syncthreads();
 #pragma unroll
   for (int i = 0; i < RB; ++i)
 #pragma unroll
@@ -318,8 +313,9 @@ __device__ __forceinline__ void solve_merge(const float* Akk, const float* beta_
 // recursive doubling: the eight 8 x 8 diagonal blocks are inverted by forward
 // substitution, then blocks of 8, 16 and 32 are merged pairwise with
 //   [A 0; C B]^-1 = [A^-1 0; -B^-1 C A^-1 B^-1]   (fp32 throughout).
-// All threads take part; ends synced.
-__device__ __forceinline__ void solve_T(const float* Akk, const float* beta_s, float* Tm) {
+// `xs` is 4 KB of scratch.  All threads take part; ends synced.
+__device__ __forceinline__ void solve_T(const float* Akk, const float* beta_s, float* Tm,
+                                        float* xs) {
   const int tid = threadIdx.x;
   for (int idx = tid; idx < C * C; idx += NT) Tm[idx] = 0.f;  // the swizzle is a permutation
   __syncthreads();
@@ -337,9 +333,9 @@ __device__ __forceinline__ void solve_T(const float* Akk, const float* beta_s, f
     for (int i = 0; i < 8; ++i) Tm[sw64(o + i, o + j)] = x[i];
   }
   __syncthreads();
-  solve_merge<8, 1, 1>(Akk, beta_s, Tm);
-  solve_merge<16, 2, 1>(Akk, beta_s, Tm);
-  solve_merge<32, 2, 2>(Akk, beta_s, Tm);
+  solve_merge<8, 1, 1>(Akk, beta_s, Tm, xs);
+  solve_merge<16, 2, 1>(Akk, beta_s, Tm, xs);
+  solve_merge<32, 2, 2>(Akk, beta_s, Tm, xs);
 }
 
 // Write row r, columns c0..c0+15 of a fp32 swizzled 64x64 matrix M (times

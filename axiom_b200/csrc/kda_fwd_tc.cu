@@ -176,7 +176,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       float* Tm = reinterpret_cast<float*>(sm + OFF_KI);
       __syncthreads();
       KDA_PT(0, 12);
-      solve_T(Akk, beta_s, Tm);
+      solve_T(Akk, beta_s, Tm, reinterpret_cast<float*>(sm + OFF_VT));
       KDA_PT(0, 4);
       const int r = tid >> 2, c0 = (tid & 3) * 16;
       row16_to_cm(sm + OFF_TP, r, Tm, r, c0, beta_s);          // T diag(beta)
