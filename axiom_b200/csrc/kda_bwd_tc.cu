@@ -714,74 +714,117 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           mma_bf16(T_SC, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), desc_mnmajor(da + 8192 + ks * 2048, C), id2, 1u);
         mma_commit(mbar);
       }
+      // channel-major copies for the epilogue: QG -> TP, KG -> TB|AQB (the MMAs only read them)
+      transpose_cm<64, 128>(smem_u32(sm + P_TP), a3 + 64 * 256, warp, lane, NT / 32);
+      transpose_cm<64, 128>(smem_u32(sm + P_TB), a3 + 128 * 256, warp, lane, NT / 32);
+      cp_async_wait<0>();
+      __syncthreads();
+      transpose_cm<64, 128>(smem_u32(sm + P_SQ), smem_u32(sm + P_SG), warp, lane, NT / 32);  // g
+      transpose_cm<64, 128>(smem_u32(sm + P_SK), smem_u32(sm + P_V), warp, lane, NT / 32);   // v
       failed |= !mma_wait();
+      if (__syncthreads_or(failed)) break;
+      transpose_cm<64, 128>(smem_u32(sm + P_KL), smem_u32(sm + P_KI), warp, lane, NT / 32);  // KI
+      __syncthreads();
+    } else {
+      cp_async_wait<0>();
+      if (__syncthreads_or(failed)) break;
     }
-    cp_async_wait<0>();
-    if (__syncthreads_or(failed)) break;
     KDA_PT(2, 15);
     // ---- final epilogue: thread = channel d (lane), columns c in [32 hh, 32 hh + 32) ----
     {
       const int d = 32 * qw + lane;
       const int cb = hh * 32;
-      const unsigned char* sgt = sm + P_SG;
-      float pre = 0.f, gtot = 0.f;
-      for (int cc = 0; cc < C; ++cc) {
-        const float x = ldbf(sgt, cm_off(cc, d, DK));
-        pre += (cc < cb) ? x : 0.f;
-        gtot += x;
-      }
       const float gC = gamC[d];
-      float* Gs = reinterpret_cast<float*>(sm + P_TP);  // exact path: G fp32 [64][128]
-      if (slow) {
-        float run2 = pre;
-        for (int jj = 0; jj < 32; ++jj) {
-          run2 += ldbf(sgt, cm_off(cb + jj, d, DK));
-          Gs[(cb + jj) * DK + d] = run2;
-        }
-        __syncthreads();
-      }
       float dG[32];
-      float run = pre, klsum = 0.f;
+      float klsum = 0.f;
       float* TR = reinterpret_cast<float*>(sm + P_SB);  // dbeta partials [128][64], xor-swizzled
       const size_t gbase = hoff + tok0 * rstride + d;
+      if (!slow) {
+        // channel-major tiles: g (SQ), v (SK), QG (TP), KG (TB), KI (KL), each [128][64]
+        float gm[32];
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        const int c16 = cb + 16 * part;
-        float dqg[16], dkg[16], dki[16], dkl[16], yw[16], yu[16];
-        tmem_ld16(T_IV + tl + c16, dqg);
-        tmem_ld16(T_IV + 64 + tl + c16, dkg);
-        tmem_ld16(T_SC + tl + c16, dki);
-        tmem_ld16(T_KL + tl + c16, dkl);
-        tmem_ld16(T_UF + tl + c16, yw);
-        tmem_ld16(T_UF + 64 + tl + c16, yu);
-        tmem_wait_ld();
+        for (int j = 0; j < 4; ++j) unpack_bf16x8(ld16(sm + P_SQ, cm_off(d, cb + 8 * j, C)), gm + 8 * j);
+        float run = 0.f;
+        if (hh) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int cc = c16 + i;
-          const bool ok = cc < rows_valid;
-          run += ldbf(sgt, cm_off(cc, d, DK));
-          const float gam = __expf(run);
-          float dqv, dkv, dGv, kgam;
-          if (!slow) {
-            const float gi = __expf(-run);
-            const float qg = ldbf(A3, cm_off(64 + cc, d, DK));
-            const float kg = ldbf(A3, cm_off(128 + cc, d, DK));
-            const float ki = ldbf(sm + P_KI, cm_off(cc, d, DK));
+          for (int j = 0; j < 4; ++j) {
+            float t8[8];
+            unpack_bf16x8(ld16(sm + P_SQ, cm_off(d, 8 * j, C)), t8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) run += t8[e];
+          }
+        }
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          const int c8 = cb + 8 * qq;
+          float dqg[8], dkg[8], dki[8], dkl[8], yw[8], yu[8], qg[8], kg[8], ki[8], vv[8];
+          tmem_ld8(T_IV + tl + c8, dqg);
+          tmem_ld8(T_IV + 64 + tl + c8, dkg);
+          tmem_ld8(T_SC + tl + c8, dki);
+          tmem_ld8(T_KL + tl + c8, dkl);
+          tmem_ld8(T_UF + tl + c8, yw);
+          tmem_ld8(T_UF + 64 + tl + c8, yu);
+          unpack_bf16x8(ld16(sm + P_TP, cm_off(d, c8, C)), qg);
+          unpack_bf16x8(ld16(sm + P_TB, cm_off(d, c8, C)), kg);
+          unpack_bf16x8(ld16(sm + P_KL, cm_off(d, c8, C)), ki);
+          unpack_bf16x8(ld16(sm + P_SK, cm_off(d, c8, C)), vv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int cc = c8 + i;
+            run += gm[8 * qq + i];
+            const float gam = __expf(run), gi = __expf(-run);
             const float s2 = dki[i] + gC * dkl[i];
-            dqv = dqg[i] * gam;
-            dkv = dkg[i] * gam + s2 * gi;
-            dGv = dqg[i] * qg + dkg[i] * kg - s2 * ki;
-            klsum += gC * dkl[i] * ki;
-            kgam = kg;
-          } else {
+            dG[8 * qq + i] = dqg[i] * qg[i] + dkg[i] * kg[i] - s2 * ki[i];
+            klsum += gC * dkl[i] * ki[i];
+            TR[d * 64 + (cc ^ (d & 63))] = yw[i] * kg[i] + yu[i] * vv[i];
+            if (cc < rows_valid) {
+              dq[gbase + cc * rstride] = __float2bfloat16_rn(dqg[i] * gam);
+              dk[gbase + cc * rstride] = __float2bfloat16_rn(dkg[i] * gam + s2 * gi);
+              dv[gbase + cc * rstride] = __float2bfloat16_rn(beta_s[cc] * yu[i]);
+            }
+          }
+        }
+      } else {
+        const unsigned char* sgt = sm + P_SG;
+        float pre = 0.f, gtot = 0.f;
+        for (int cc = 0; cc < C; ++cc) {
+          const float x = ldbf(sgt, cm_off(cc, d, DK));
+          pre += (cc < cb) ? x : 0.f;
+          gtot += x;
+        }
+        float* Gs = reinterpret_cast<float*>(sm + P_TP);  // exact path: G fp32 [64][128]
+        {
+          float run2 = pre;
+          for (int jj = 0; jj < 32; ++jj) {
+            run2 += ldbf(sgt, cm_off(cb + jj, d, DK));
+            Gs[(cb + jj) * DK + d] = run2;
+          }
+        }
+        __syncthreads();
+        float run = pre;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const int c16 = cb + 16 * part;
+          float dqg[16], dkg[16], dkl[16], yw[16], yu[16];
+          tmem_ld16(T_IV + tl + c16, dqg);
+          tmem_ld16(T_IV + 64 + tl + c16, dkg);
+          tmem_ld16(T_KL + tl + c16, dkl);
+          tmem_ld16(T_UF + tl + c16, yw);
+          tmem_ld16(T_UF + 64 + tl + c16, yu);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int cc = c16 + i;
+            run += ldbf(sgt, cm_off(cc, d, DK));
+            const float gam = __expf(run);
             const float qv = ldbf(sm + P_SQ, cm_off(cc, d, DK));
             const float kv = ldbf(sm + P_SK, cm_off(cc, d, DK));
             const float lam = __expf(fminf(gtot - run, 0.f));
-            dqv = dqg[i] * gam;
-            dkv = dkg[i] * gam + dkl[i] * lam;
-            dGv = dqg[i] * qv * gam + dkg[i] * kv * gam - dkl[i] * kv * lam;
+            float dqv = dqg[i] * gam;
+            float dkv = dkg[i] * gam + dkl[i] * lam;
+            float dGv = dqg[i] * qv * gam + dkg[i] * kv * gam - dkl[i] * kv * lam;
             klsum += dkl[i] * kv * lam;
-            kgam = kv * gam;
             // exact score adjoints (direct decay ratio)
             float dra = 0.f, drk = 0.f, dca = 0.f, dck = 0.f;
             for (int i2 = 0; i2 <= cc; ++i2) {
@@ -797,14 +840,14 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
             dqv += dra;
             dkv += drk + dca + dck;
             dGv += dra * qv + drk * kv - (dca + dck) * kv;
-          }
-          dG[16 * part + i] = dGv;
-          const float vv = ldbf(sm + P_V, cm_off(cc, d, DV));
-          TR[d * 64 + (cc ^ (d & 63))] = yw[i] * kgam + yu[i] * vv;
-          if (ok) {
-            dq[gbase + cc * rstride] = __float2bfloat16_rn(dqv);
-            dk[gbase + cc * rstride] = __float2bfloat16_rn(dkv);
-            dv[gbase + cc * rstride] = __float2bfloat16_rn(beta_s[cc] * yu[i]);
+            dG[16 * part + i] = dGv;
+            const float vv = ldbf(sm + P_V, cm_off(cc, d, DV));
+            TR[d * 64 + (cc ^ (d & 63))] = yw[i] * kv * gam + yu[i] * vv;
+            if (cc < rows_valid) {
+              dq[gbase + cc * rstride] = __float2bfloat16_rn(dqv);
+              dk[gbase + cc * rstride] = __float2bfloat16_rn(dkv);
+              dv[gbase + cc * rstride] = __float2bfloat16_rn(beta_s[cc] * yu[i]);
+            }
           }
         }
       }

@@ -109,6 +109,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 8 columns: thread i gets lane (base+i), cols [c, c+8).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr));
+}
 // 32 lanes x 16 columns: thread i gets lane (base+i), cols [c, c+16).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
@@ -138,6 +147,31 @@ __device__ __forceinline__ void tmem_wait_ld() {
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---- 8x8 b16 matrix moves (warp-collective) ---------------------------------
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(saddr));
+}
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t saddr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};"
+               :: "r"(saddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]) : "memory");
+}
+
+// Transpose a CM tile of R x Cc bf16 into a CM tile of Cc x R (core matrix
+// (rg, cg) -> (cg, rg), each 8x8 block transposed), four core matrices per
+// warp instruction; all warps of the CTA (nwarps) take part.
+template <int R, int Cc>
+__device__ __forceinline__ void transpose_cm(uint32_t dst, uint32_t src, int warp, int lane, int nwarps) {
+  constexpr int NCM = (R / 8) * (Cc / 8);
+  for (int j0 = 4 * warp; j0 < NCM; j0 += 4 * nwarps) {
+    const int j = j0 + (lane >> 3), row = lane & 7;
+    const int rg = j / (Cc / 8), cg = j % (Cc / 8);
+    uint32_t f[4];
+    ldmatrix_x4(f, src + ((rg * (Cc / 8) + cg) << 7) + (row << 4));
+    stmatrix_x4_trans(dst + ((cg * (R / 8) + rg) << 7) + (row << 4), f);
+  }
 }
 
 // ---- mbarrier ----------------------------------------------------------------
