@@ -22,7 +22,7 @@ _Z = ctypes.c_size_t
 SIGNATURES = {
     "kda_version": ([], _I),
     "kda_strerror": ([_I], ctypes.c_char_p),
-    "kda_ckpt_elems": ([_I] * 6, _Z),
+    "kda_ckpt_bytes": ([_I] * 8, _Z),
     "kda_fwd": ([_P] * 9 + [_I] * 9 + [_P], _I),
     "kda_bwd_workspace_bytes": ([_I] * 7, _Z),
     "kda_bwd": ([_P] * 14 + [_P, _Z] + [_I] * 9 + [_P], _I),

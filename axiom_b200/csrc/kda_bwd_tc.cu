@@ -37,13 +37,13 @@ using namespace chunk;
 
 __device__ __forceinline__ uint32_t lane_off(int qw) { return static_cast<uint32_t>(32 * qw) << 16; }
 
-// Backward workspace, one block per (batch, head, chunk) unit, written by
-// bwd_seq and read by bwd_par:
-//   [0, 32K)    dS' bf16 [128][128] row-major (the state cotangent entering the chunk)
-//   [32K, 40K)  T = (I + diag(beta) Akk)^-1   bf16 [64][64], CM byte layout
-//   [40K, 48K)  Aqk                           bf16 [64][64], CM byte layout
-//   [48K, 56K)  Akk                           bf16 [64][64], CM byte layout
-constexpr size_t WS_UNIT = 57344, WS_T = 32768, WS_AQ = 40960, WS_AK = 49152;
+// Backward workspace: one dS' (bf16 [128][128] row-major, the state cotangent
+// entering the chunk) per (batch, head, chunk) unit, written by bwd_seq and
+// read by bwd_par.
+constexpr size_t WS_UNIT = 32768;
+// Per-chunk factors the forward stores after the boundary states of its
+// checkpoint: T = (I + diag(beta) Akk)^-1, Aqk, Akk, bf16 [64][64] CM tiles.
+constexpr size_t FAC_UNIT = 24576, FAC_T = 0, FAC_AQ = 8192, FAC_AK = 16384;
 
 // cp.async `bytes` (multiple of 16 * NT) contiguous bytes.
 __device__ __forceinline__ void stage_bytes(unsigned char* dst, const unsigned char* src, int bytes) {
@@ -68,8 +68,9 @@ constexpr int SEQ_SMEM = Q_BAR + 64;
 __global__ void __launch_bounds__(NT, 1)
 bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ g,
                const bf16* __restrict__ beta, const bf16* __restrict__ dout,
-               const float* __restrict__ dsT, float* __restrict__ ds0, bf16* __restrict__ dsw,
-               int T, int H, int* __restrict__ err) {
+               const unsigned char* __restrict__ factors, const float* __restrict__ dsT,
+               float* __restrict__ ds0, bf16* __restrict__ dsw, int T, int H,
+               int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char sm[];
   float* beta_s = reinterpret_cast<float*>(sm + Q_BETA);
   float* gamC = reinterpret_cast<float*>(sm + Q_GC);
@@ -96,13 +97,16 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     stage_tile(sm + Q_SK, kh + (tok0 + t0) * rstride, rv, rstride);
     stage_tile(sm + Q_SG, gh + (tok0 + t0) * rstride, rv, rstride);
     stage_tile(sm + Q_DO, doh + (tok0 + t0) * rstride, rv, rstride);
+    const unsigned char* fu = factors + ((unit * n_chunks) + c) * FAC_UNIT;
+    stage_bytes(sm + Q_TP + 8192, fu + FAC_T, 8192);
+    stage_bytes(sm + Q_AQB, fu + FAC_AQ, 8192);
     cp_async_commit();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
-  const uint32_t T_DS = tbase, T_SC = tbase + 128, T_W = tbase + 256, T_U = tbase + 384;
+  const uint32_t T_DS = tbase, T_W = tbase + 256, T_U = tbase + 384;
   const uint32_t tl = lane_off(qw);
   uint32_t phase = 0;
   bool failed = false;
@@ -124,8 +128,6 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     tmem_wait_st();
   }
   const uint32_t a3 = smem_u32(A3);
-  float* Aq = reinterpret_cast<float*>(sm + Q_SB);
-  float* Akk = Aq + 4096;
 
   KDA_PT_INIT();
   for (int c = n_chunks - 1; c >= 0; --c) {
@@ -135,56 +137,27 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     __syncthreads();
     KDA_PT(1, 0);
     float G[4][8];
-    const bool slow = prep(sm + Q_SQ, sm + Q_SK, sm + Q_SG, A3 + cm_off(64, 0, DK),
-                           A3 + cm_off(128, 0, DK), sm + Q_KI, sm + Q_KL, gamC, G);
+    prep(sm + Q_SQ, sm + Q_SK, sm + Q_SG, A3 + cm_off(64, 0, DK), A3 + cm_off(128, 0, DK),
+         nullptr, sm + Q_KL, gamC, G);
     const bool more = c > 0;
     const int tp0 = (c - 1) * C;
-    if (!slow) {
-      fence_async_smem();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        const uint32_t id = idesc_bf16(128, 64, false, false);
-#pragma unroll
-        for (int ks = 0; ks < DK / 16; ++ks)
-          mma_bf16(T_SC, desc_kmajor(a3 + 64 * 256 + ks * 256, DK),
-                   desc_kmajor(smem_u32(sm + Q_KI) + ks * 256, DK), id, ks > 0);
-        mma_commit(mbar);
-      }
-      if (more) {
-        stage_tile(sm + Q_SQ, qh + (tok0 + tp0) * rstride, C, rstride);
-        stage_tile(sm + Q_SK, kh + (tok0 + tp0) * rstride, C, rstride);
-        stage_tile(sm + Q_SG, gh + (tok0 + tp0) * rstride, C, rstride);
-        cp_async_commit();
-      }
-      failed |= !mma_wait();
-      if (__syncthreads_or(failed)) break;
-      scores_epilogue(T_SC, Aq, Akk);
-    } else {
-      float* Gf = reinterpret_cast<float*>(sm + Q_KI);
-      store_G(Gf, G);
-      __syncthreads();
-      scores_exact(sm + Q_SQ, sm + Q_SK, Gf, Aq, Akk);
-      __syncthreads();
-      if (more) {
-        stage_tile(sm + Q_SQ, qh + (tok0 + tp0) * rstride, C, rstride);
-        stage_tile(sm + Q_SK, kh + (tok0 + tp0) * rstride, C, rstride);
-        stage_tile(sm + Q_SG, gh + (tok0 + tp0) * rstride, C, rstride);
-        cp_async_commit();
-      }
-    }
     KDA_PT(1, 1);
     __syncthreads();
-    float* Tm = reinterpret_cast<float*>(sm + Q_KI);
-    solve_T(Akk, beta_s, Tm, reinterpret_cast<float*>(sm + Q_TP));
-    {
+    if (more) {  // next chunk's q, k, g into the free staging
+      stage_tile(sm + Q_SQ, qh + (tok0 + tp0) * rstride, C, rstride);
+      stage_tile(sm + Q_SK, kh + (tok0 + tp0) * rstride, C, rstride);
+      stage_tile(sm + Q_SG, gh + (tok0 + tp0) * rstride, C, rstride);
+      cp_async_commit();
+    }
+    {  // T diag(beta) from the forward's bf16 T tile
       const int r = tid >> 2, c0 = (tid & 3) * 16;
-      row16_to_cm(sm + Q_TP, r, Tm, r, c0, beta_s);
-      row16_to_cm(sm + Q_AQB, r, Aq, r, c0, nullptr);
-      unsigned char* wu = reinterpret_cast<unsigned char*>(dsw) + (unit * n_chunks + c) * WS_UNIT;
-      row16_to_cm(wu + WS_T, r, Tm, r, c0, nullptr);
-      row16_to_cm(wu + WS_AQ, r, Aq, r, c0, nullptr);
-      row16_to_cm(wu + WS_AK, r, Akk, r, c0, nullptr);
+      float tv[16];
+      unpack_bf16x8(ld16(sm + Q_TP + 8192, cm_off(r, c0, C)), tv);
+      unpack_bf16x8(ld16(sm + Q_TP + 8192, cm_off(r, c0 + 8, C)), tv + 8);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) tv[j] *= beta_s[c0 + j];
+      st16(sm + Q_TP, cm_off(r, c0, C), pack_bf16x8(tv));
+      st16(sm + Q_TP, cm_off(r, c0 + 8, C), pack_bf16x8(tv + 8));
     }
     KDA_PT(1, 2);
     fence_async_smem();
@@ -289,6 +262,9 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     KDA_PT(1, 6);
     if (more) {
       stage_tile(sm + Q_DO, doh + (tok0 + tp0) * rstride, C, rstride);
+      const unsigned char* fu = factors + ((unit * n_chunks) + c - 1) * FAC_UNIT;
+      stage_bytes(sm + Q_TP + 8192, fu + FAC_T, 8192);
+      stage_bytes(sm + Q_AQB, fu + FAC_AQ, 8192);
       cp_async_commit();
     }
   }
@@ -354,7 +330,8 @@ template <typename Tc>
 __global__ void __launch_bounds__(NT, 1)
 bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
                const bf16* __restrict__ g, const bf16* __restrict__ beta,
-               const Tc* __restrict__ s_ckpt, const bf16* __restrict__ dsw,
+               const Tc* __restrict__ s_ckpt, const unsigned char* __restrict__ factors,
+               const bf16* __restrict__ dsw,
                const bf16* __restrict__ dout, bf16* __restrict__ dq, bf16* __restrict__ dk,
                bf16* __restrict__ dv, bf16* __restrict__ dg, bf16* __restrict__ dbeta, int B,
                int T, int H, int* __restrict__ err) {
@@ -413,9 +390,10 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
     stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
     stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
-    stage_bytes(sm + P_TB, wunit + WS_T, 8192);   // T, Aqk, Akk from bwd_seq
-    stage_bytes(sm + P_AQB, wunit + WS_AQ, 8192);
-    stage_bytes(sm + P_AKB, wunit + WS_AK, 8192);
+    const unsigned char* fu = factors + unit_sq * FAC_UNIT;  // T, Aqk, Akk from the forward
+    stage_bytes(sm + P_TB, fu + FAC_T, 8192);
+    stage_bytes(sm + P_AQB, fu + FAC_AQ, 8192);
+    stage_bytes(sm + P_AKB, fu + FAC_AK, 8192);
     cp_async_commit();
     if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + tid) * H + h]) : 0.f;
     if (tid < 128) dgc[tid] = 0.f;
@@ -913,9 +891,13 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
   int* err = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_bwd_tc_error) != cudaSuccess) return KDA_ERR_LAUNCH;
   bf16* dsw = static_cast<bf16*>(work);
+  const size_t n = (static_cast<size_t>(T) + C - 1) / C;
+  const unsigned char* factors =
+      static_cast<const unsigned char*>(s_ckpt) + static_cast<size_t>(B) * H * n * DK * DV * sizeof(Tc);
   bwd_seq_kernel<<<B * H, NT, SEQ_SMEM, st>>>(
       static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(g),
-      static_cast<const bf16*>(beta), static_cast<const bf16*>(dout), dsT, ds0, dsw, T, H, err);
+      static_cast<const bf16*>(beta), static_cast<const bf16*>(dout), factors, dsT, ds0, dsw, T, H,
+      err);
   rc = launch_status();
   if (rc != KDA_OK) return rc;
   const long long units = static_cast<long long>(B) * H * ((T + C - 1) / C);
@@ -923,7 +905,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
   bwd_par_kernel<Tc><<<grid, NT, PAR_SMEM, st>>>(
       static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v),
       static_cast<const bf16*>(g), static_cast<const bf16*>(beta), static_cast<const Tc*>(s_ckpt),
-      dsw, static_cast<const bf16*>(dout), static_cast<bf16*>(dq), static_cast<bf16*>(dk_),
+      factors, dsw, static_cast<const bf16*>(dout), static_cast<bf16*>(dq), static_cast<bf16*>(dk_),
       static_cast<bf16*>(dv_), static_cast<bf16*>(dg), static_cast<bf16*>(dbeta), B, T, H, err);
   return launch_status();
 }

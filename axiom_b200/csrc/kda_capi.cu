@@ -13,6 +13,7 @@ int simt_fwd_launch(const void* q, const void* k, const void* v, const void* g, 
                     const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
                     int dk, int dv, int C, int in_dt, int o_dt, int ck_dt, cudaStream_t st);
 bool tc_fwd_supported(int dk, int dv, int C_, int in_dt);
+constexpr size_t kTcFactorBytes = 3 * 64 * 64 * 2;  // T, Aqk, Akk (bf16) per chunk-head
 int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                   const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
                   int o_dt, int ck_dt, cudaStream_t st);
@@ -64,10 +65,16 @@ const char* kda_strerror(int status) {
   }
 }
 
-size_t kda_ckpt_elems(int B, int T, int H, int dk, int dv, int chunk) {
-  if (chunk <= 0 || B < 0 || T < 0 || H < 0 || dk < 0 || dv < 0) return 0;
+size_t kda_ckpt_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dtype,
+                      int ckpt_dtype) {
+  if (check_dims(B, T, H, dk, dv, chunk) != KDA_OK || !valid_dtype(in_dtype) ||
+      !valid_dtype(ckpt_dtype))
+    return 0;
   const size_t n = (static_cast<size_t>(T) + chunk - 1) / chunk;
-  return static_cast<size_t>(B) * H * n * dk * dv;
+  const size_t units = static_cast<size_t>(B) * H * n;
+  size_t bytes = units * dk * dv * (ckpt_dtype == KDA_F32 ? 4 : 2);
+  if (kda::tc_fwd_supported(dk, dv, chunk, in_dtype)) bytes += units * kda::kTcFactorBytes;
+  return bytes;
 }
 
 int kda_fwd(const void* q, const void* k, const void* v, const void* g, const void* beta,

@@ -61,7 +61,8 @@ __global__ void __launch_bounds__(NT, 1)
 fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
               const bf16* __restrict__ g, const bf16* __restrict__ beta,
               const float* __restrict__ s0, To* __restrict__ o, float* __restrict__ s_out,
-              Tc* __restrict__ s_ckpt, int T, int H, int* __restrict__ err) {
+              Tc* __restrict__ s_ckpt, unsigned char* __restrict__ factors, int T, int H,
+              int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char sm[];
   float* beta_s = reinterpret_cast<float*>(sm + OFF_BETA);
   float* gamC = reinterpret_cast<float*>(sm + OFF_GC);
@@ -193,6 +194,12 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       for (int ks = 0; ks < C / 16; ++ks)
         mma_bf16(T_P, desc_kmajor(aqb + ks * 256, C), desc_mnmajor(tb + ks * 2048, C), idesc, ks > 0);
       mma_commit(mbar);
+    }
+    if (factors) {  // T, Aqk, Akk (bf16 CM tiles) into the checkpoint for the backward
+      unsigned char* fu = factors + ((static_cast<size_t>(b) * H + h) * n_chunks + c) * 24576;
+      for (int i = tid; i < 1024; i += NT)
+        *reinterpret_cast<uint4*>(fu + 16 * i) = *reinterpret_cast<const uint4*>(sm + OFF_VT + 16 * i);
+      row16_to_cm(fu + 16384, tid >> 2, Akk, tid >> 2, (tid & 3) * 16, nullptr);
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
@@ -363,10 +370,15 @@ int launch_t(const void* q, const void* k, const void* v, const void* g, const v
   if (rc != KDA_OK) return rc;
   int* err = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_fwd_tc_error) != cudaSuccess) return KDA_ERR_LAUNCH;
+  unsigned char* factors = nullptr;
+  if (s_ckpt) {  // the per-chunk factors follow the boundary states
+    const size_t n = (static_cast<size_t>(T) + C - 1) / C;
+    factors = static_cast<unsigned char*>(s_ckpt) + static_cast<size_t>(B) * H * n * DK * DV * sizeof(Tc);
+  }
   kern<<<B * H, NT, SMEM_BYTES, st>>>(
       static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v),
       static_cast<const bf16*>(g), static_cast<const bf16*>(beta), s0, static_cast<To*>(o), s_out,
-      static_cast<Tc*>(s_ckpt), T, H, err);
+      static_cast<Tc*>(s_ckpt), factors, T, H, err);
   return launch_status();
 }
 

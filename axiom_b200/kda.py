@@ -97,6 +97,10 @@ def kda_fwd(q, k, v, g, beta, S0=None, *, chunk=CHUNK, o_dtype=None, need_ckpt=F
             ckpt_dtype=None):
     """Chunked forward; returns ``(o, S_T, ckpt)`` (``ckpt`` is None unless requested).
 
+    ``ckpt`` (1-D, ``kda_ckpt_bytes`` bytes) starts with the chunk-boundary
+    states ``[B, H, ceil(T/chunk), dk, dv]`` in ``ckpt_dtype``; on the
+    tensor-core path per-chunk factors for the backward follow them.
+
     ``q, k, g``: ``[B, T, H, dk]``; ``v``: ``[B, T, H, dv]``; ``beta``: ``[B, T, H]``,
     all of one dtype (bf16 or fp32); ``S0``: ``[B, H, dk, dv]`` fp32 or None.
     """
@@ -115,8 +119,9 @@ def kda_fwd(q, k, v, g, beta, S0=None, *, chunk=CHUNK, o_dtype=None, need_ckpt=F
     s_out = torch.empty((B, H, dk, dv), dtype=torch.float32, device=q.device)
     ckpt = None
     if need_ckpt:
-        n = lib().kda_ckpt_elems(B, T, H, dk, dv, chunk)
-        ckpt = torch.empty(n, dtype=ckpt_dtype, device=q.device)
+        nbytes = lib().kda_ckpt_bytes(B, T, H, dk, dv, chunk, _dt(q, "q"), _DT[ckpt_dtype])
+        esz = 4 if ckpt_dtype == torch.float32 else 2
+        ckpt = torch.empty(-(-nbytes // esz), dtype=ckpt_dtype, device=q.device)
     rc = lib().kda_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(S0), _ptr(o),
                        _ptr(s_out), _ptr(ckpt), B, T, H, dk, dv, int(chunk), _dt(q, "q"),
                        _DT[o_dtype], _DT[ckpt_dtype], _stream())
@@ -136,9 +141,11 @@ def kda_bwd(q, k, v, g, beta, ckpt, do, dST=None, *, chunk=CHUNK, need_ds0=True)
     _check_tensor(do, "do", (B, T, H, dv))
     if dST is not None:
         _check_tensor(dST, "dST", (B, H, dk, dv), torch.float32)
-    n = lib().kda_ckpt_elems(B, T, H, dk, dv, chunk)
-    if ckpt is None or ckpt.numel() != n or not ckpt.is_contiguous():
-        raise ValueError("kda_bwd: ckpt must be the forward's chunk-boundary checkpoint")
+    if ckpt is None or ckpt.dtype not in _DT or not ckpt.is_contiguous():
+        raise ValueError("kda_bwd: ckpt must be the forward's checkpoint")
+    nbytes = lib().kda_ckpt_bytes(B, T, H, dk, dv, chunk, _dt(q, "q"), _DT[ckpt.dtype])
+    if ckpt.numel() * ckpt.element_size() < nbytes:
+        raise ValueError("kda_bwd: ckpt is smaller than the forward's checkpoint for these shapes")
     dq = torch.empty_like(q)
     dk_ = torch.empty_like(k)
     dv_ = torch.empty_like(v)

@@ -68,11 +68,16 @@ int kda_version(void);
 /* Human-readable text of a status code. */
 const char* kda_strerror(int status);
 
-/* Number of chunk-boundary states the forward stores for the backward:
- * B * H * ceil(T / chunk) * dk * dv elements.  Entry c of [B, H, n, dk, dv]
- * is the state entering chunk c (the reference's pass-A state chain,
- * net/kernels/kda_cc_fused_persist.py:1282-1370). */
-size_t kda_ckpt_elems(int B, int T, int H, int dk, int dv, int chunk);
+/* Bytes of the checkpoint the forward stores for the backward (its
+ * residuals).  It starts with the chunk-boundary states, [B, H, n, dk, dv]
+ * elements of ckpt_dtype with n = ceil(T / chunk), entry c being the state
+ * entering chunk c (the reference's pass-A state chain,
+ * net/kernels/kda_cc_fused_persist.py:1282-1370).  On the tensor-core path
+ * (bf16 inputs, dk = dv = 128, chunk = 64) it continues with per-chunk
+ * factors the backward would otherwise recompute: T = (I + diag(beta) Akk)^-1,
+ * Aqk and Akk, bf16 64 x 64 each (24 KB per chunk-head). */
+size_t kda_ckpt_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dtype,
+                      int ckpt_dtype);
 
 /* Chunked forward (replaces kernel / cc_scan's forward rule,
  * net/kernels/kda_cc_fused_persist.py:718-759).
@@ -80,8 +85,8 @@ size_t kda_ckpt_elems(int B, int T, int H, int dk, int dv, int chunk);
  *   o_dtype    : dtype of o
  *   s0         : [B,H,dk,dv] fp32 initial state, or NULL for zeros
  *   s_out      : [B,H,dk,dv] fp32 final state, or NULL
- *   s_ckpt     : chunk-boundary states for the backward (kda_ckpt_elems
- *                elements of ckpt_dtype), or NULL when not training.
+ *   s_ckpt     : the checkpoint for the backward (kda_ckpt_bytes bytes),
+ *                or NULL when not training.
  * Supported: 1 <= dk, dv <= 128 (multiples of 8), chunk in {16, 32, 64}.
  * bf16 inputs with dk = dv = 128, chunk = 64 take the tensor-core path. */
 int kda_fwd(const void* q, const void* k, const void* v, const void* g,
@@ -97,7 +102,7 @@ size_t kda_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
  * net/kernels/kda_cc_fused_persist.py:1707-1763 and reference_bwd_scan
  * :794-849).  Walks the chunks in reverse, recomputing each chunk from its
  * checkpointed boundary state (s_ckpt written by kda_fwd with the same
- * dimensions and ckpt_dtype), and produces
+ * dimensions, dtypes and ckpt_dtype), and produces
  *   dq, dk : [B,T,H,dk]   dv : [B,T,H,dv]   dg : [B,T,H,dk]   dbeta : [B,T,H]
  * in in_dtype, and ds0 : [B,H,dk,dv] fp32 (may be NULL).
  *   do_    : [B,T,H,dv] upstream cotangent of o, in do_dtype

@@ -43,10 +43,15 @@ def test_version_and_strerror():
     assert b"dimensions" in lib.kda_strerror(-1)
 
 
-def test_ckpt_elems():
+def test_ckpt_bytes():
     lib = _lib.lib()
-    assert lib.kda_ckpt_elems(4, 8192, 32, 128, 128, 64) == 4 * 32 * 128 * 128 * 128
-    assert lib.kda_ckpt_elems(1, 100, 2, 16, 8, 64) == 1 * 2 * 2 * 16 * 8
+    units = 4 * 32 * 128
+    # tensor-core path: bf16 states + T, Aqk, Akk (3 x 64 x 64 bf16) per chunk-head
+    assert lib.kda_ckpt_bytes(4, 8192, 32, 128, 128, 64, 1, 1) == units * (128 * 128 * 2 + 3 * 64 * 64 * 2)
+    assert lib.kda_ckpt_bytes(4, 8192, 32, 128, 128, 64, 1, 0) == units * (128 * 128 * 4 + 3 * 64 * 64 * 2)
+    # exact path: states only
+    assert lib.kda_ckpt_bytes(1, 100, 2, 16, 8, 64, 0, 0) == 1 * 2 * 2 * 16 * 8 * 4
+    assert lib.kda_ckpt_bytes(1, 64, 1, 64, 64, 48, 1, 1) == 0  # unsupported chunk
 
 
 @pytest.mark.parametrize("dims", [

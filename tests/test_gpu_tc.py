@@ -52,7 +52,8 @@ def test_tc_forward_matches_oracle(B, T, H, s0, decay):
     assert K.scale_rel_err(_np(o), o_ref) <= TOL
     assert K.scale_rel_err(_np(s_t), s_ref) <= TOL
     n = states.shape[2]
-    assert K.scale_rel_err(_np(ckpt).reshape(B, H, n, 128, 128), states) <= TOL
+    ck_states = _np(ckpt)[: B * H * n * 128 * 128].reshape(B, H, n, 128, 128)
+    assert K.scale_rel_err(ck_states, states) <= TOL
 
 
 def test_tc_forward_bf16_output_and_repeatability():
