@@ -37,9 +37,9 @@ using namespace chunk;
 
 __device__ __forceinline__ uint32_t lane_off(int qw) { return static_cast<uint32_t>(32 * qw) << 16; }
 
-// Backward workspace: one dS' (bf16 [128][128] row-major, the state cotangent
-// entering the chunk) per (batch, head, chunk) unit, written by bwd_seq and
-// read by bwd_par.
+// Backward workspace: one dS' (the state cotangent entering the chunk, bf16
+// [128][128] as the CM operand image) per (batch, head, chunk) unit, written by
+// bwd_seq and read by bwd_par, each with one bulk copy.
 constexpr size_t WS_UNIT = 32768;
 // Per-chunk factors the forward stores after the boundary states of its
 // checkpoint: T = (I + diag(beta) Akk)^-1, Aqk, Akk, bf16 [64][64] CM tiles.
@@ -58,7 +58,7 @@ constexpr int Q_A3 = 65536;              // [-W ; Gam Q ; Gam K] CM[192][128]
 constexpr int Q_KI = Q_A3 + 49152;       // K Gi            | T fp32 | G fp32 (slow, with TP)
 constexpr int Q_TP = Q_KI + 16384;       // T beta [64][64] | dU^T [128][64] | prep partials
 constexpr int Q_KL = Q_TP + 16384;       // lam K
-constexpr int Q_SB = Q_KL + 16384;       // dS' bf16 [128][128] | Aqk + Akk fp32
+constexpr int Q_SB = Q_KL + 16384;       // dS' bf16 [128][128] (also stored to the workspace)
 constexpr int Q_AQB = Q_SB + 32768;      // Aqk bf16 [64][64]
 constexpr int Q_BETA = Q_AQB + 8192;
 constexpr int Q_GC = Q_BETA + 256;
@@ -133,6 +133,7 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   for (int c = n_chunks - 1; c >= 0; --c) {
     const int t0 = c * C, rows_valid = min(C, T - t0);
     cp_async_wait<0>();
+    if (tid == 0) bulk_wait_read();  // SB may be rewritten: the previous dS' image is stored
     if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
     __syncthreads();
     KDA_PT(1, 0);
@@ -190,10 +191,8 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         }
       }
     }
-    {  // dS' pass: bf16 operand + workspace copy, then dS *= Gam_C
+    {  // dS' pass: bf16 operand (stored to the workspace below), then dS *= Gam_C
       const int d = 32 * qw + lane;
-      bf16* wrow = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(dsw) +
-                                           (unit * n_chunks + c) * WS_UNIT) + d * DV;
       const float gcd = gamC[d];
       for (int half = 0; half < 2; ++half) {
         const int c0 = hh * 64 + half * 32;
@@ -202,9 +201,7 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 32; j += 8) {
-          const uint4 pk = pack_bf16x8(vals + j);
-          st16(sm + Q_SB, cm_off(d, c0 + j, DV), pk);
-          *reinterpret_cast<uint4*>(wrow + c0 + j) = pk;
+          st16(sm + Q_SB, cm_off(d, c0 + j, DV), pack_bf16x8(vals + j));
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) vals[j] *= gcd;
@@ -218,6 +215,10 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     __syncthreads();
     // dU^T = dS'^T (lam K)^T + dO^T Aqk
     if (tid == 0) {
+      // the workspace entry of chunk c is the dS' operand image (one bulk copy)
+      bulk_store(reinterpret_cast<unsigned char*>(dsw) + (unit * n_chunks + c) * WS_UNIT, sm + Q_SB,
+                 WS_UNIT);
+      bulk_commit();
       tc_fence_after();
       const uint32_t sb = smem_u32(sm + Q_SB), kl = smem_u32(sm + Q_KL);
       const uint32_t dob = smem_u32(sm + Q_DO), aqb = smem_u32(sm + Q_AQB);
@@ -280,24 +281,26 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   }
   if (failed && tid == 0 && err) atomicExch(err, 1);
   cp_async_wait<0>();
+  if (tid == 0) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);
+  KDA_PT_FLUSH(1);
 }
 
 // ===========================================================================
 // bwd_par
 // ===========================================================================
-constexpr int P_SQ = 0;                  // q staging | dO | raw q (exact path)
-constexpr int P_SK = 16384;              // k staging | dS' (lo) | dW^T [128][64]
-constexpr int P_SG = 32768;              // g staging | dS' (hi)
-constexpr int P_V = 49152;               // v staging | U bf16 [64][128]
-constexpr int P_A3 = 65536;              // [W ; Gam Q ; Gam K]
-constexpr int P_KI = P_A3 + 49152;       // K Gi
-constexpr int P_KL = P_KI + 16384;       // lam K | dU^T [128][64] | [dAqk ; beta dL] [128][64]
+constexpr int P_SQ = 0;                  // dO | raw q (exact path) | g^T [128][64]
+constexpr int P_SK = 16384;              // dS' (lo) | dW^T [128][64] | raw k (exact path) | v^T
+constexpr int P_SG = 32768;              // dS' (hi) | raw g
+constexpr int P_V = 49152;               // v staging | U bf16 [64][128] | raw v
+constexpr int P_A3 = 65536;              // [W ; Gam Q ; Gam K] (q, k staged in place) | KG^T
+constexpr int P_KI = P_A3 + 49152;       // g staging | K Gi
+constexpr int P_KL = P_KI + 16384;       // lam K | dU^T [128][64] | [dAqk ; beta dL] [128][64] | KI^T
 constexpr int P_SB = P_KL + 16384;       // S_c bf16 [128][128] | Yw^T, Yu^T | dbeta partials
-constexpr int P_TP = P_SB + 32768;       // T beta [64][64] | v~ bf16 [64][128] | G fp32 (exact path, with TB/AQB)
+constexpr int P_TP = P_SB + 32768;       // T beta [64][64] | v~ bf16 [64][128] | QG^T | G fp32 (exact path, with TB/AQB)
 constexpr int P_TB = P_TP + 16384;       // T bf16 [64][64]
 constexpr int P_AQB = P_TB + 8192;       // Aqk bf16
 constexpr int P_AKB = P_AQB + 8192;      // Akk bf16
@@ -308,15 +311,13 @@ constexpr int P_DB = P_DGC + 512;        // dbeta accum fp32[64]
 constexpr int P_XCH = P_DB + 256;        // half-exchange fp32[2][2][128]
 constexpr int P_BAR = P_XCH + 2048;
 constexpr int PAR_SMEM = P_BAR + 64;
+// the factor block is copied in one piece: TB, AQB, AKB mirror FAC_T, FAC_AQ, FAC_AK
+static_assert(P_AQB - P_TB == static_cast<int>(FAC_AQ) && P_AKB - P_TB == static_cast<int>(FAC_AK) &&
+                  P_BETA - P_TB == static_cast<int>(FAC_UNIT),
+              "factor staging layout");
 
-template <typename Tc>
-__device__ __forceinline__ void stage_ckpt(unsigned char* dst, const Tc* src);
-template <>
-__device__ __forceinline__ void stage_ckpt<bf16>(unsigned char* dst, const bf16* src) {
-  stage_square(dst, src);
-}
-template <>
-__device__ __forceinline__ void stage_ckpt<float>(unsigned char* dst, const float* src) {
+// fp32 checkpoint state (row-major) -> bf16 CM operand tile.
+__device__ __forceinline__ void stage_ckpt_f32(unsigned char* dst, const float* src) {
   for (int i = threadIdx.x; i < 128 * 16; i += NT) {
     const int r = i >> 4, cg = i & 15;
     const float4 a = *reinterpret_cast<const float4*>(src + r * 128 + cg * 8);
@@ -343,6 +344,8 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   float* xch = reinterpret_cast<float*>(sm + P_XCH);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P_BAR + 8);
+  uint64_t* mbar_fac = reinterpret_cast<uint64_t*>(sm + P_BAR + 16);   // T, Aqk, Akk bulk load
+  uint64_t* mbar_late = reinterpret_cast<uint64_t*>(sm + P_BAR + 24);  // dS', S_c bulk loads
   unsigned char* A3 = sm + P_A3;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;
@@ -350,7 +353,12 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   const long long n_units = static_cast<long long>(B) * H * n_chunks;
   const size_t rstride = static_cast<size_t>(H) * DK;
 
-  if (tid == 0) { mbar_init(mbar, 1); mbar_fence_init(); }
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_init(mbar_fac, 1);
+    mbar_init(mbar_late, 1);
+    mbar_fence_init();
+  }
   if (warp == 0) { tmem_alloc(tslot, 512); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
@@ -375,6 +383,40 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   };
   const uint32_t a3 = smem_u32(A3);
 
+  // Unit inputs q, k, g, v and the forward's T, Aqk, Akk are staged where prep
+  // and the MMAs consume them: q, k into A3 rows 64..191 (prep scales them in
+  // place), g into KI (overwritten by K Gi).  They are issued one unit ahead,
+  // during the previous unit's epilogue: the tiles as one cp.async group, the
+  // contiguous 24 KB factor block (TB, AQB, AKB are adjacent) as one bulk load
+  // completing on mbar_fac.  Every bulk phase is waited before the CTA exits.
+  int it = 0;                                      // units processed by this CTA
+  bool fac_pending = false, late_pending = false;  // bulk loads issued, not yet waited
+  uint32_t fac_par = 0, late_par = 0;
+  auto issue_inputs = [&](long long uu, float& beta_nx) {
+    const int cc = static_cast<int>(uu % n_chunks);
+    const long long bhn = uu / n_chunks;
+    const int hn = static_cast<int>(bhn % H), bn = static_cast<int>(bhn / H);
+    const int rv = min(C, T - cc * C);
+    const size_t tk = static_cast<size_t>(bn) * T + static_cast<size_t>(cc) * C;
+    const size_t src = static_cast<size_t>(hn) * DK + tk * rstride;
+    stage_tile(A3 + cm_off(64, 0, DK), q + src, rv, rstride);
+    stage_tile(A3 + cm_off(128, 0, DK), k + src, rv, rstride);
+    stage_tile(sm + P_KI, g + src, rv, rstride);
+    stage_tile(sm + P_V, v + src, rv, rstride);
+    cp_async_commit();
+    if (tid == 0) {
+      const unsigned char* fu = factors + ((static_cast<size_t>(bn) * H + hn) * n_chunks + cc) * FAC_UNIT;
+      fence_async_smem();
+      mbar_expect_tx(mbar_fac, FAC_UNIT);
+      bulk_load(sm + P_TB, fu, FAC_UNIT, mbar_fac);
+    }
+    fac_pending = true;
+    fac_par = static_cast<uint32_t>(uu == blockIdx.x ? it : it + 1) & 1u;
+    beta_nx = tid < rv ? __bfloat162float(beta[(tk + tid) * H + hn]) : 0.f;
+  };
+  float beta_nx = 0.f;
+  if (blockIdx.x < n_units) issue_inputs(blockIdx.x, beta_nx);
+
   KDA_PT_INIT();
   for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
     const int c = static_cast<int>(u % n_chunks);
@@ -384,33 +426,40 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     const size_t tok0 = static_cast<size_t>(b) * T + t0;
     const size_t hoff = static_cast<size_t>(h) * DK;
     const size_t unit_sq = (static_cast<size_t>(b) * H + h) * n_chunks + c;  // chunk index
+    const long long u_next = u + gridDim.x;
+    bool prefetched = false;
 
-    const unsigned char* wunit = reinterpret_cast<const unsigned char*>(dsw) + unit_sq * WS_UNIT;
-    stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
-    stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
-    stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
-    stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
-    const unsigned char* fu = factors + unit_sq * FAC_UNIT;  // T, Aqk, Akk from the forward
-    stage_bytes(sm + P_TB, fu + FAC_T, 8192);
-    stage_bytes(sm + P_AQB, fu + FAC_AQ, 8192);
-    stage_bytes(sm + P_AKB, fu + FAC_AK, 8192);
+    // dO, dS' and S_c (bf16 checkpoint: the operand image) land while prep and
+    // the W, U MMAs run
+    stage_tile(sm + P_SQ, dout + hoff + tok0 * rstride, rows_valid, rstride);
     cp_async_commit();
-    if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + tid) * H + h]) : 0.f;
+    if (tid == 0) {
+      constexpr uint32_t late_bytes = WS_UNIT + (sizeof(Tc) == 2 ? DK * DV * 2 : 0);
+      fence_async_smem();
+      mbar_expect_tx(mbar_late, late_bytes);
+      bulk_load(sm + P_SK, reinterpret_cast<const unsigned char*>(dsw) + unit_sq * WS_UNIT, WS_UNIT, mbar_late);
+      if constexpr (sizeof(Tc) == 2) bulk_load(sm + P_SB, s_ckpt + unit_sq * (DK * DV), DK * DV * 2, mbar_late);
+    }
+    late_pending = true;
+    late_par = static_cast<uint32_t>(it) & 1u;
+    if (tid < C) beta_s[tid] = beta_nx;
     if (tid < 128) dgc[tid] = 0.f;
     if (tid < 64) dbs[tid] = 0.f;
-    cp_async_wait<0>();
-    __syncthreads();
+    KDA_PT(2, 26);
+    cp_async_wait<1>();
+    failed |= !mbar_wait(mbar_fac, fac_par);
+    fac_pending = false;
+    KDA_PT(2, 27);
+    if (__syncthreads_or(failed)) break;
 
     KDA_PT(2, 0);
-    // ---- recompute: prep (the scores and T come from bwd_seq), then W, U ----
+    // ---- recompute: prep (T and the scores come from the forward), then W, U ----
     float G[4][8];
-    const bool slow = prep(sm + P_SQ, sm + P_SK, sm + P_SG, A3 + cm_off(64, 0, DK),
-                           A3 + cm_off(128, 0, DK), sm + P_KI, sm + P_KL, gamC, G);
+    unsigned char* qk = A3 + cm_off(64, 0, DK);
+    unsigned char* kk = A3 + cm_off(128, 0, DK);
+    const bool slow = prep(qk, kk, sm + P_KI, qk, kk, sm + P_KI, sm + P_KL, gamC, G);
     KDA_PT(2, 1);
     __syncthreads();
-    // dS' into the free k/g staging
-    stage_square(sm + P_SK, reinterpret_cast<const bf16*>(wunit));
-    cp_async_commit();
     {  // T diag(beta) from the bf16 T tile
       const int r = tid >> 2, c0 = (tid & 3) * 16;
       float tv[16];
@@ -429,7 +478,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       tc_fence_after();
       const uint32_t id = idesc_bf16(64, 128, false, true);
       const uint32_t tp = smem_u32(sm + P_TP), vb = smem_u32(sm + P_V);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks) {
         const uint64_t ad = desc_kmajor(tp + ks * 256, C);
         mma_bf16(T_IV, ad, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), id, ks > 0);
@@ -437,16 +486,9 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       }
       mma_commit(mbar);
     }
-    // dO over the free T buffer, S_c over the free score buffer
-    __syncthreads();
-    stage_tile(sm + P_SQ, dout + hoff + tok0 * rstride, rows_valid, rstride);
-    if constexpr (sizeof(Tc) == 2) {
-      stage_ckpt<Tc>(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
-    }
-    cp_async_commit();
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
-    if constexpr (sizeof(Tc) == 4) stage_ckpt<Tc>(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
+    if constexpr (sizeof(Tc) == 4) stage_ckpt_f32(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
     KDA_PT(2, 3);
     {  // W -> A3 rows 0..63, U -> bf16 (V region); U fp32 stays in TMEM
       const int r = 16 * qw + lane;
@@ -466,16 +508,18 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       }
     }
     cp_async_wait<0>();
+    failed |= !mbar_wait(mbar_late, late_par);
+    late_pending = false;
     fence_async_smem();
     tc_fence_before();
-    __syncthreads();
+    if (__syncthreads_or(failed)) break;
     KDA_PT(2, 4);
     // W S_c  (M = 64)
     if (tid == 0) {
       tc_fence_after();
       const uint32_t id = idesc_bf16(64, 128, false, true);
       const uint32_t sb = smem_u32(sm + P_SB);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < DK / 16; ++ks)
         mma_bf16(T_WS, desc_kmajor(a3 + ks * 256, DK), desc_mnmajor(sb + ks * 4096, DV), id, ks > 0);
       mma_commit(mbar);
@@ -522,20 +566,25 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       const uint32_t dob = smem_u32(sm + P_SQ), aqb = smem_u32(sm + P_AQB), vt = smem_u32(sm + P_TP);
       const uint32_t id1 = idesc_bf16(128, 64, true, false), id2 = idesc_bf16(128, 64, true, true);
       const uint32_t id3 = idesc_bf16(128, 64, false, false);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < DK / 16; ++ks)
         mma_bf16(T_DU, desc_mnmajor(dsp + ks * 4096, DV), desc_kmajor(kl + ks * 256, DK), id1, ks > 0);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks)
         mma_bf16(T_DU, desc_mnmajor(dob + ks * 4096, DV), desc_mnmajor(aqb + ks * 2048, C), id2, 1u);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < DV / 16; ++ks)
         mma_bf16(T_KL, desc_kmajor(dsp + ks * 256, DV), desc_kmajor(vt + ks * 256, DV), id3, ks > 0);
       mma_commit(mbar);
+      KDA_PT(2, 20);
     }
     failed |= !mma_wait();
+    KDA_PT(2, 21);
     if (__syncthreads_or(failed)) break;
     KDA_PT(2, 7);
+    // dS' is dead: restage g (for the epilogue) over its upper half
+    stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
+    cp_async_commit();
     {  // dU^T -> bf16 [j][c] (KL region)
       const int j = 32 * qw + lane;
       float vals[32];
@@ -553,15 +602,17 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       tc_fence_after();
       const uint32_t sb = smem_u32(sm + P_SB), dob = smem_u32(sm + P_SQ), dut = smem_u32(sm + P_KL);
       const uint32_t id1 = idesc_bf16(128, 64, false, false), id2 = idesc_bf16(128, 64, false, true);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < DV / 16; ++ks) {
         const uint64_t ad = desc_kmajor(sb + ks * 256, DV);
         mma_bf16(T_IV, ad, desc_kmajor(dob + ks * 256, DV), id1, ks > 0);
         mma_bf16(T_IV + 64, ad, desc_mnmajor(dut + ks * 2048, C), id2, ks > 0);
       }
       mma_commit(mbar);
+      KDA_PT(2, 22);
     }
     failed |= !mma_wait();
+    KDA_PT(2, 23);
     if (__syncthreads_or(failed)) break;
     KDA_PT(2, 9);
     {  // dW^T = -(dU S^T)^T -> bf16 [d][c] (SK region)
@@ -583,7 +634,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       tc_fence_after();
       const uint32_t dwt = smem_u32(sm + P_SK), dut = smem_u32(sm + P_KL), tb = smem_u32(sm + P_TB);
       const uint32_t id = idesc_bf16(128, 64, false, true);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks) {
         const uint64_t bd = desc_mnmajor(tb + ks * 2048, C);
         mma_bf16(T_UF, desc_kmajor(dwt + ks * 256, C), bd, id, ks > 0);
@@ -620,20 +671,29 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       const uint32_t dob = smem_u32(sm + P_SQ), vt = smem_u32(sm + P_TP);
       const uint32_t ywt = smem_u32(sm + P_SB), yut = smem_u32(sm + P_SB + 16384), ub = smem_u32(sm + P_V);
       const uint32_t id1 = idesc_bf16(64, 64, false, false), id2 = idesc_bf16(64, 64, true, false);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < DV / 16; ++ks)
         mma_bf16(T_SC, desc_kmajor(dob + ks * 256, DV), desc_kmajor(vt + ks * 256, DV), id1, ks > 0);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < DV / 16; ++ks)
         mma_bf16(T_L, desc_mnmajor(yut + ks * 2048, C), desc_kmajor(ub + ks * 256, DV), id2, ks > 0);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < DK / 16; ++ks)
         mma_bf16(T_L, desc_mnmajor(ywt + ks * 2048, C), desc_kmajor(a3 + ks * 256, DK), id2, 1u);
       mma_commit(mbar);
+      KDA_PT(2, 24);
     }
     failed |= !mma_wait();
+    KDA_PT(2, 25);
     if (__syncthreads_or(failed)) break;
     KDA_PT(2, 13);
+    // U, dO and dW^T are dead: restage v (and raw q, k for the exact path)
+    stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
+    if (slow) {
+      stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
+      stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
+    }
+    cp_async_commit();
     {  // [dAqk ; beta dL] -> bf16 [128][64] (KL region); dbeta += rowsum(dL * Akk)
       const int r = 16 * qw + lane;
       float da[32], dl[32];
@@ -666,35 +726,27 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     tc_fence_before();
     __syncthreads();
     KDA_PT(2, 14);
-    // dO, U, Yw^T/Yu^T, v~, T and Aqk are dead: restage g (and v) for the epilogue,
-    // and raw q, k for the exact path.
-    stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
-    stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
-    if (slow) {
-      stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
-      stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
-    }
-    cp_async_commit();
     if (!slow) {
       // [dQG^T | dKG^T] += KI^T [dAqk ; beta dL]^T ;  dKI^T = QG^T dAqk + KG^T (beta dL)
       if (tid == 0) {
         tc_fence_after();
         const uint32_t ki = smem_u32(sm + P_KI), da = smem_u32(sm + P_KL);
         const uint32_t id1 = idesc_bf16(128, 128, true, false), id2 = idesc_bf16(128, 64, true, true);
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < C / 16; ++ks)
           mma_bf16(T_IV, desc_mnmajor(ki + ks * 4096, DK), desc_kmajor(da + ks * 256, C), id1, 1u);
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < C / 16; ++ks)
           mma_bf16(T_SC, desc_mnmajor(a3 + 64 * 256 + ks * 4096, DK), desc_mnmajor(da + ks * 2048, C), id2, ks > 0);
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < C / 16; ++ks)
           mma_bf16(T_SC, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), desc_mnmajor(da + 8192 + ks * 2048, C), id2, 1u);
         mma_commit(mbar);
       }
-      // channel-major copies for the epilogue: QG -> TP, KG -> TB|AQB (the MMAs only read them)
+      // channel-major copies for the epilogue: QG -> TP, KG -> A3 rows 0..63 (W is dead;
+      // the MMAs only read QG, KG)
       transpose_cm<64, 128>(smem_u32(sm + P_TP), a3 + 64 * 256, warp, lane, NT / 32);
-      transpose_cm<64, 128>(smem_u32(sm + P_TB), a3 + 128 * 256, warp, lane, NT / 32);
+      transpose_cm<64, 128>(a3, a3 + 128 * 256, warp, lane, NT / 32);
       cp_async_wait<0>();
       __syncthreads();
       transpose_cm<64, 128>(smem_u32(sm + P_SQ), smem_u32(sm + P_SG), warp, lane, NT / 32);  // g
@@ -703,6 +755,9 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       if (__syncthreads_or(failed)) break;
       transpose_cm<64, 128>(smem_u32(sm + P_KL), smem_u32(sm + P_KI), warp, lane, NT / 32);  // KI
       __syncthreads();
+      // A3 rows 64..191, KI, V, TB, AQB and AKB are free: stage the next unit
+      if (u_next < n_units) issue_inputs(u_next, beta_nx);
+      prefetched = true;
     } else {
       cp_async_wait<0>();
       if (__syncthreads_or(failed)) break;
@@ -718,7 +773,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       float* TR = reinterpret_cast<float*>(sm + P_SB);  // dbeta partials [128][64], xor-swizzled
       const size_t gbase = hoff + tok0 * rstride + d;
       if (!slow) {
-        // channel-major tiles: g (SQ), v (SK), QG (TP), KG (TB), KI (KL), each [128][64]
+        // channel-major tiles: g (SQ), v (SK), QG (TP), KG (A3), KI (KL), each [128][64]
         float gm[32];
 #pragma unroll
         for (int j = 0; j < 4; ++j) unpack_bf16x8(ld16(sm + P_SQ, cm_off(d, cb + 8 * j, C)), gm + 8 * j);
@@ -743,7 +798,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           tmem_ld8(T_UF + tl + c8, yw);
           tmem_ld8(T_UF + 64 + tl + c8, yu);
           unpack_bf16x8(ld16(sm + P_TP, cm_off(d, c8, C)), qg);
-          unpack_bf16x8(ld16(sm + P_TB, cm_off(d, c8, C)), kg);
+          unpack_bf16x8(ld16(A3, cm_off(d, c8, C)), kg);
           unpack_bf16x8(ld16(sm + P_KL, cm_off(d, c8, C)), ki);
           unpack_bf16x8(ld16(sm + P_SK, cm_off(d, c8, C)), vv);
           tmem_wait_ld();
@@ -836,10 +891,12 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       xch[(1 * 2 + hh) * 128 + d] = klsum;
       KDA_PT(2, 16);
       __syncthreads();
-      if (tid < C) {  // dbeta: rowsum over the 128 channels of the partials
-        float acc = dbs[tid];
-        for (int dd = 0; dd < 128; ++dd) acc += TR[dd * 64 + (tid ^ (dd & 63))];
-        if (tid < rows_valid) dbeta[(tok0 + tid) * H + h] = __float2bfloat16_rn(acc);
+      {  // dbeta: rowsum over the 128 channels of the partials, a quarter per thread
+        const int r = tid & 63, d0 = (tid >> 6) * 32;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int dd = d0; dd < d0 + 32; ++dd) acc += TR[dd * 64 + (r ^ (dd & 63))];
+        atomicAdd(&dbs[r], acc);
       }
       KDA_PT(2, 17);
       const float dGC = xch[(1 * 2 + 0) * 128 + d] + xch[(1 * 2 + 1) * 128 + d] + gC * dgc[d];
@@ -855,13 +912,22 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    KDA_PT(2, 28);
+    if (tid < rows_valid) dbeta[(tok0 + tid) * H + h] = __float2bfloat16_rn(dbs[tid]);
+    if (!prefetched && u_next < n_units) issue_inputs(u_next, beta_nx);
+    ++it;
   }
   if (failed && tid == 0 && err) atomicExch(err, 1);
   cp_async_wait<0>();
+  // a unit abandoned on a timeout may leave bulk loads in flight: wait (bounded)
+  // for them before the shared memory is released
+  if (fac_pending) mbar_wait(mbar_fac, fac_par);
+  if (late_pending) mbar_wait(mbar_late, late_par);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);
+  KDA_PT_FLUSH(2);
 }
 
 __device__ int g_bwd_tc_error = 0;

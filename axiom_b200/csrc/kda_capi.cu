@@ -27,7 +27,7 @@ int simt_bwd_launch(const void* q, const void* k, const void* v, const void* g, 
                     const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                     void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T,
                     int H, int dk, int dv, int C, int in_dt, int do_dt, int ck_dt,
-                    cudaStream_t st);
+                    int states_cm, cudaStream_t st);
 }  // namespace kda
 
 namespace {
@@ -149,9 +149,11 @@ int kda_bwd(const void* q, const void* k, const void* v, const void* g, const vo
   }
   const size_t need = kda::simt_bwd_workspace_bytes(B, H, dk, dv, chunk);
   if (need && (!workspace || workspace_bytes < need)) return KDA_ERR_WORKSPACE;
+  // a bf16 checkpoint written by the tensor-core forward holds operand images
+  const int states_cm = kda::tc_fwd_supported(dk, dv, chunk, in_dtype) && ckpt_dtype == KDA_BF16;
   return kda::simt_bwd_launch(q, k, v, g, beta, s_ckpt, do_, dsT, dq, dk_, dv_, dg, dbeta, ds0,
                               workspace, B, T, H, dk, dv, chunk, in_dtype, do_dtype, ckpt_dtype,
-                              stream);
+                              states_cm, stream);
 }
 
 int kda_decode(float* S, const void* q, const void* k, const void* v, const void* g,

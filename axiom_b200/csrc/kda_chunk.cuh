@@ -70,15 +70,6 @@ __device__ __forceinline__ void stage_tile(unsigned char* dst, const bf16* src, 
   }
 }
 
-// cp.async a contiguous [128][128] bf16 matrix (row stride 128) into a CM tile.
-__device__ __forceinline__ void stage_square(unsigned char* dst, const bf16* src) {
-  for (int i = threadIdx.x; i < 128 * 16; i += NT) {
-    int r, cg;
-    chunk_of(i, 16, r, cg);
-    cp_async16(dst + cm_off(r, cg * 8, 128), src + r * 128 + cg * 8, true);
-  }
-}
-
 // Decay prep for one chunk.  Thread t owns channels 8(t>>4)..+7 and the rows
 // 8k + (t&7) for k in [4h, 4h+4), h = (t>>3)&1, so each group of 8 lanes reads
 // and writes whole core matrices (conflict-free).  G = cumsum(g) over the chunk

@@ -131,6 +131,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     const int t0 = c * C;
     const int rows_valid = min(C, T - t0);
     cp_async_wait<0>();
+    if (tid == 0) bulk_wait_read();  // the previous state image in SB has been stored
     if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
     __syncthreads();
 
@@ -261,10 +262,13 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     }
     KDA_PT(0, 7);
     // ---------------- S pass: S_c -> bf16 operand (+ checkpoint), S *= Gam_C ----------------
+    // A bf16 checkpoint entry is the operand image itself, stored below with one
+    // bulk copy; an fp32 checkpoint is written row-major here.
+    Tc* ck_unit = s_ckpt ? s_ckpt + ((static_cast<size_t>(b) * H + h) * n_chunks + c) * (DK * DV) : nullptr;
     {
       const int d = 32 * qw + lane;
       const float gcd = gamC[d];
-      Tc* ck = s_ckpt ? s_ckpt + ((static_cast<size_t>(b) * H + h) * n_chunks + c) * (DK * DV) + d * DV : nullptr;
+      Tc* ck = (sizeof(Tc) == 4 && ck_unit) ? ck_unit + d * DV : nullptr;
       for (int half = 0; half < 2; ++half) {
         const int c0 = hh * 64 + half * 32;
         float vals[32];
@@ -285,6 +289,10 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     KDA_PT(0, 8);
     // ---------------- MMA_1: [W ; Q~] S ----------------
     if (tid == 0) {
+      if (sizeof(Tc) == 2 && ck_unit) {
+        bulk_store(ck_unit, sm + OFF_SB, DK * DV * 2);
+        bulk_commit();
+      }
       tc_fence_after();
       const uint32_t idesc = idesc_bf16(128, 128, false, true);
       const uint32_t sb = smem_u32(sm + OFF_SB);
@@ -352,10 +360,12 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   }
   if (failed && tid == 0 && err) atomicExch(err, 1);
   cp_async_wait<0>();
+  if (tid == 0) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);
+  KDA_PT_FLUSH(0);
 }
 
 __device__ int g_fwd_tc_error = 0;

@@ -196,7 +196,7 @@ bwd_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin*
                 const float* __restrict__ dsT, Tin* __restrict__ dq, Tin* __restrict__ dkout,
                 Tin* __restrict__ dvout, Tin* __restrict__ dg, Tin* __restrict__ dbeta,
                 float* __restrict__ ds0, float* __restrict__ work, int T, int H, int dk, int dv,
-                int C) {
+                int C, int states_cm) {
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, nt = blockDim.x;
   const size_t unit = static_cast<size_t>(b) * H + h;
@@ -232,7 +232,12 @@ bwd_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin*
     }
     {
       const Tc* ck = s_ckpt + (unit * n_chunks + c) * dk * dv;
-      for (int idx = tid; idx < dk * dv; idx += nt) s.Sc[idx] = ldf(ck + idx);
+      // states_cm: the entry is an 8 x 8 core-matrix operand image (tensor-core forward)
+      for (int idx = tid; idx < dk * dv; idx += nt) {
+        const int r = idx / dv, j = idx % dv;
+        const int e = states_cm ? (((r >> 3) * (dv >> 3) + (j >> 3)) << 6) + ((r & 7) << 3) + (j & 7) : idx;
+        s.Sc[idx] = ldf(ck + e);
+      }
     }
     __syncthreads();
     // (2) G = cumsum(g)
@@ -465,14 +470,14 @@ template <typename Tin, typename Td, typename Tc>
 int bwd_launch_t(const void* q, const void* k, const void* v, const void* g, const void* beta,
                  const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                  void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
-                 int dk, int dv, int C, cudaStream_t st) {
+                 int dk, int dv, int C, int states_cm, cudaStream_t st) {
   dim3 grid(H, B);
   bwd_simt_kernel<Tin, Td, Tc><<<grid, kBwdThreads, 0, st>>>(
       static_cast<const Tin*>(q), static_cast<const Tin*>(k), static_cast<const Tin*>(v),
       static_cast<const Tin*>(g), static_cast<const Tin*>(beta), static_cast<const Tc*>(s_ckpt),
       static_cast<const Td*>(dout), dsT, static_cast<Tin*>(dq), static_cast<Tin*>(dk_),
       static_cast<Tin*>(dv_), static_cast<Tin*>(dg), static_cast<Tin*>(dbeta), ds0,
-      static_cast<float*>(work), T, H, dk, dv, C);
+      static_cast<float*>(work), T, H, dk, dv, C, states_cm);
   return launch_status();
 }
 
@@ -504,11 +509,11 @@ int simt_bwd_launch(const void* q, const void* k, const void* v, const void* g, 
                     const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                     void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T,
                     int H, int dk, int dv, int C, int in_dt, int do_dt, int ck_dt,
-                    cudaStream_t st) {
+                    int states_cm, cudaStream_t st) {
 #define KDA_BWD_CASE(I, D, K, TI, TD, TK)                                                     \
   if (in_dt == I && do_dt == D && ck_dt == K)                                                \
     return bwd_launch_t<TI, TD, TK>(q, k, v, g, beta, s_ckpt, dout, dsT, dq, dk_, dv_, dg,   \
-                                    dbeta, ds0, work, B, T, H, dk, dv, C, st);
+                                    dbeta, ds0, work, B, T, H, dk, dv, C, states_cm, st);
   KDA_BWD_CASE(KDA_F32, KDA_F32, KDA_F32, float, float, float)
   KDA_BWD_CASE(KDA_F32, KDA_F32, KDA_BF16, float, float, bf16)
   KDA_BWD_CASE(KDA_F32, KDA_BF16, KDA_F32, float, bf16, float)

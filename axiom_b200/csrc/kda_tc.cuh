@@ -210,6 +210,30 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
+// ---- bulk copies (cp.async.bulk, contiguous, no tensor map) --------------------
+// Issued by one thread.  Both addresses 16-byte aligned, size a multiple of 16.
+// Arms `mbar` for one arrival plus `bytes` transaction bytes.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               :: "r"(smem_u32(mbar)), "r"(bytes) : "memory");
+}
+// global -> shared; completes `bytes` transaction bytes on `mbar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
+}
+// shared -> global, tracked by this thread's bulk async-groups.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               :: "l"(dst), "r"(smem_u32(src)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The shared source of every committed bulk store may be overwritten.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed bulk store has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ---- bf16 packing ---------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -234,19 +258,33 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
 
 // Optional per-phase cycle counters for performance work: compiled only with
 // -DKDA_PHASE_TIMERS (never in the shipped library), in a single-translation-
-// unit build that defines `__device__ unsigned long long g_kda_phase[3][32]`
-// before including this header.  Thread 0 of CTA 0 adds the cycles since the
-// previous mark to slot i.
+// unit build that defines `__device__ unsigned long long g_kda_phase[3][8][32]`
+// before including this header.  Lane 0 of each warp adds the cycles since its
+// previous mark to slot i of a shared-memory table (one shared load per mark,
+// so the counters barely perturb what they measure); KDA_PT_FLUSH copies CTA
+// 0's table to g_kda_phase[k] at the kernel's converged exit.
 #ifdef KDA_PHASE_TIMERS
-#define KDA_PT_INIT() long long kda_pt_prev_ = clock64()
+#define KDA_PT_INIT()                                                       \
+  __shared__ unsigned long long kda_pt_sm_[8][32];                          \
+  for (int i_ = threadIdx.x; i_ < 256; i_ += blockDim.x) kda_pt_sm_[i_ >> 5][i_ & 31] = 0; \
+  __syncthreads();                                                          \
+  long long kda_pt_prev_ = clock64()
 #define KDA_PT(k, i)                                                        \
   do {                                                                      \
     const long long kda_pt_now_ = clock64();                                \
-    if (blockIdx.x == 0 && threadIdx.x == 0)                                \
-      g_kda_phase[k][i] += static_cast<unsigned long long>(kda_pt_now_ - kda_pt_prev_); \
+    if ((threadIdx.x & 31) == 0)                                            \
+      kda_pt_sm_[threadIdx.x >> 5][i] += static_cast<unsigned long long>(kda_pt_now_ - kda_pt_prev_); \
     kda_pt_prev_ = kda_pt_now_;                                             \
+  } while (0)
+#define KDA_PT_FLUSH(k)                                                     \
+  do {                                                                      \
+    __syncthreads();                                                        \
+    if (blockIdx.x == 0)                                                    \
+      for (int i_ = threadIdx.x; i_ < 256; i_ += blockDim.x)                \
+        g_kda_phase[k][i_ >> 5][i_ & 31] += kda_pt_sm_[i_ >> 5][i_ & 31];   \
   } while (0)
 #else
 #define KDA_PT_INIT() do {} while (0)
 #define KDA_PT(k, i) do {} while (0)
+#define KDA_PT_FLUSH(k) do {} while (0)
 #endif

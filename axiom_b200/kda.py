@@ -97,9 +97,9 @@ def kda_fwd(q, k, v, g, beta, S0=None, *, chunk=CHUNK, o_dtype=None, need_ckpt=F
             ckpt_dtype=None):
     """Chunked forward; returns ``(o, S_T, ckpt)`` (``ckpt`` is None unless requested).
 
-    ``ckpt`` (1-D, ``kda_ckpt_bytes`` bytes) starts with the chunk-boundary
-    states ``[B, H, ceil(T/chunk), dk, dv]`` in ``ckpt_dtype``; on the
-    tensor-core path per-chunk factors for the backward follow them.
+    ``ckpt`` (1-D, ``kda_ckpt_bytes`` bytes) is opaque: it starts with the
+    chunk-boundary states (``ckpt_states`` gives them as ``[B, H, n, dk, dv]``)
+    and, on the tensor-core path, per-chunk factors for the backward follow.
 
     ``q, k, g``: ``[B, T, H, dk]``; ``v``: ``[B, T, H, dv]``; ``beta``: ``[B, T, H]``,
     all of one dtype (bf16 or fp32); ``S0``: ``[B, H, dk, dv]`` fp32 or None.
@@ -127,6 +127,24 @@ def kda_fwd(q, k, v, g, beta, S0=None, *, chunk=CHUNK, o_dtype=None, need_ckpt=F
                        _DT[o_dtype], _DT[ckpt_dtype], _stream())
     check("kda_fwd", rc)
     return o, s_out, ckpt
+
+
+def ckpt_states(ckpt, B, T, H, dk, dv, *, chunk=CHUNK, in_dtype=torch.bfloat16):
+    """The chunk-boundary states held in a forward checkpoint, ``[B, H, n, dk, dv]``
+    (entry ``c`` is the state entering chunk ``c``), in the checkpoint's dtype.
+
+    A bf16 checkpoint written by the tensor-core forward stores each state as
+    its 8 x 8 core-matrix operand image (core ``(i, j)`` holds rows ``8i..8i+7``
+    and columns ``8j..8j+7`` row-major); this undoes that arrangement.
+    """
+    n = -(-T // chunk)
+    flat = ckpt[: B * H * n * dk * dv]
+    tc = (in_dtype == torch.bfloat16 and dk == 128 and dv == 128 and chunk == 64
+          and ckpt.dtype == torch.bfloat16)
+    if not tc:
+        return flat.reshape(B, H, n, dk, dv)
+    cores = flat.reshape(B, H, n, dk // 8, dv // 8, 8, 8)
+    return cores.permute(0, 1, 2, 3, 5, 4, 6).reshape(B, H, n, dk, dv)
 
 
 def kda_bwd(q, k, v, g, beta, ckpt, do, dST=None, *, chunk=CHUNK, need_ds0=True):

@@ -75,7 +75,12 @@ const char* kda_strerror(int status);
  * net/kernels/kda_cc_fused_persist.py:1282-1370).  On the tensor-core path
  * (bf16 inputs, dk = dv = 128, chunk = 64) it continues with per-chunk
  * factors the backward would otherwise recompute: T = (I + diag(beta) Akk)^-1,
- * Aqk and Akk, bf16 64 x 64 each (24 KB per chunk-head). */
+ * Aqk and Akk, bf16 64 x 64 each (24 KB per chunk-head).  The checkpoint is
+ * an opaque blob passed from kda_fwd to kda_bwd: on the tensor-core path with
+ * a bf16 checkpoint each state is stored as the shared-memory operand image
+ * the kernels copy in one bulk transfer (8 x 8 core matrices of 128 bytes,
+ * core (i, j) at byte ((i * dv / 8) + j) * 128, row-major inside), otherwise
+ * row-major. */
 size_t kda_ckpt_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dtype,
                       int ckpt_dtype);
 

@@ -54,6 +54,29 @@ def test_ckpt_bytes():
     assert lib.kda_ckpt_bytes(1, 64, 1, 64, 64, 48, 1, 1) == 0  # unsupported chunk
 
 
+def test_ckpt_states_undoes_the_operand_image():
+    # byte offset of element (r, c) in a CM tile with `cols` columns, as in the kernels:
+    # 8 x 8 core matrices of 128 bytes, core (r/8, c/8) at ((r/8)*(cols/8) + c/8)*128
+    def cm_off(r, c, cols):
+        return ((r // 8) * (cols // 8) + c // 8) * 128 + (r % 8) * 16 + (c % 8) * 2
+
+    B, T, H, n = 1, 130, 2, 3
+    states = torch.randn(B, H, n, 128, 128).to(torch.bfloat16)
+    image = torch.empty(B * H * n * 128 * 128, dtype=torch.bfloat16)
+    r = torch.arange(128).view(128, 1).expand(128, 128)
+    c = torch.arange(128).view(1, 128).expand(128, 128)
+    elem = torch.tensor([[cm_off(i, j, 128) // 2 for j in range(128)] for i in range(128)])
+    assert torch.equal(elem, ((r // 8) * 16 + c // 8) * 64 + (r % 8) * 8 + c % 8)
+    for u in range(B * H * n):
+        image[u * 16384 + elem.reshape(-1)] = states.reshape(-1, 128, 128)[u].reshape(-1)
+    ckpt = torch.cat([image, torch.zeros(B * H * n * 3 * 64 * 64, dtype=torch.bfloat16)])
+    assert torch.equal(K.ckpt_states(ckpt, B, T, H, 128, 128), states)
+    # other layouts are row-major
+    flat = torch.randn(B * H * n * 64 * 64)
+    assert torch.equal(K.ckpt_states(flat, B, T, H, 64, 64, in_dtype=torch.float32),
+                       flat.reshape(B, H, n, 64, 64))
+
+
 @pytest.mark.parametrize("dims", [
     (1, 64, 1, 7, 64, 64),     # dk not a multiple of 8
     (1, 64, 1, 64, 136, 64),   # dv too large

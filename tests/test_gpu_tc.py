@@ -41,6 +41,7 @@ def _bf16_inputs(B, T, H, seed, s0_std=None, decay="baseline"):
 ])
 def test_tc_forward_matches_oracle(B, T, H, s0, decay):
     from axiom_b200 import kda_fwd
+    from axiom_b200.kda import ckpt_states
 
     xr, d = _bf16_inputs(B, T, H, seed=T + H, s0_std=s0 if s0 else None, decay=decay)
     S0 = d["S0"] if s0 else None
@@ -51,8 +52,8 @@ def test_tc_forward_matches_oracle(B, T, H, s0, decay):
                                        xr["S0"] if s0 else None, chunk=64, return_states=True)
     assert K.scale_rel_err(_np(o), o_ref) <= TOL
     assert K.scale_rel_err(_np(s_t), s_ref) <= TOL
-    n = states.shape[2]
-    ck_states = _np(ckpt)[: B * H * n * 128 * 128].reshape(B, H, n, 128, 128)
+    ck_states = _np(ckpt_states(ckpt, B, T, H, 128, 128, chunk=64))
+    assert ck_states.shape == states.shape
     assert K.scale_rel_err(ck_states, states) <= TOL
 
 
@@ -103,3 +104,25 @@ def test_tc_backward_many_units_matches_oracle():
     ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64)
     for name, gr, rf in zip(GRADS, grads, ref):
         assert K.scale_rel_err(_np(gr), rf) <= TOL, name
+
+
+def test_tc_forward_checkpoint_feeds_the_exact_backward():
+    """A bf16 checkpoint from the tensor-core forward (operand-image states) read by
+    the exact backward, which takes over when dO is fp32."""
+    from axiom_b200 import kda_bwd, kda_fwd
+
+    B, T, H = 1, 200, 2
+    xr, d = _bf16_inputs(B, T, H, seed=31, s0_std=0.05)
+    rng = np.random.default_rng(32)
+    do = K.bf16_round(rng.standard_normal((B, T, H, 128)))
+    dST = rng.standard_normal((B, H, 128, 128)).astype(np.float32)
+    _, _, ckpt = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], need_ckpt=True)
+    exact = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, _dev(do, torch.float32),
+                    _dev(dST, torch.float32))
+    tc = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, _dev(do, torch.bfloat16),
+                 _dev(dST, torch.float32))
+    torch.cuda.synchronize()
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64)
+    for name, ge, gt, rf in zip(GRADS, exact, tc, ref):
+        assert K.scale_rel_err(_np(ge), rf) <= TOL, name
+        assert K.scale_rel_err(_np(gt), rf) <= TOL, name
