@@ -54,70 +54,132 @@ def _peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed region
+    runs: read-only NVML queries every 2 ms from a thread (the region can be a few
+    tens of ms), or ``nvidia-smi -lms 200`` when NVML is not importable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
+    def __init__(self, index, pci_bus=None):
         self.index = index
-        self.proc = None
-        self.path = None
+        self.pci_bus = pci_bus  # "DDDDDDDD:BB:DD.0" of the CUDA device, to find it in NVML
+        self.samples = []       # (sm_mhz, [reason names])
+        self.sm_max = None
+        self.proc = self.path = self.thread = None
+        self.source = None
 
-    def __enter__(self):
+    # -- NVML ------------------------------------------------------------------------
+    def _nvml_start(self):
+        import threading
+
+        import pynvml as nv
+        nv.nvmlInit()
+        try:
+            h = nv.nvmlDeviceGetHandleByPciBusId(self.pci_bus) if self.pci_bus else None
+        except nv.NVMLError:
+            h = None
+        if h is None:
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+        self.sm_max = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        masks = [(n, getattr(nv, c)) for n, c in self.REASONS if hasattr(nv, c)]
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        self._stop = threading.Event()
+
+        def poll():
+            while True:
+                try:
+                    sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    bits = get_reasons(h)
+                except nv.NVMLError:
+                    break
+                self.samples.append((sm, [n for n, m in masks if bits & m]))
+                if self._stop.wait(0.002):
+                    break
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+        self.source = "nvml"
+
+    # -- nvidia-smi fallback ---------------------------------------------------------
+    def _smi_start(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
+        self.proc = subprocess.Popen(
+            ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.SMI_FIELDS}",
+             "--format=csv,noheader,nounits", "-lms", "200"],
+            stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        self.source = "nvidia-smi"
+
+    def _smi_collect(self):
+        names = [n for n, _ in self.REASONS[:4]]
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 8:
+                        continue
+                    try:
+                        sm, smax = float(parts[1]), float(parts[2])
+                    except ValueError:
+                        continue
+                    self.sm_max = smax
+                    self.samples.append((sm, [n for n, v in zip(names, parts[4:8])
+                                              if v.lower().startswith("active")]))
         except OSError:
-            self.proc = None
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+
+    def __enter__(self):
+        try:
+            self._nvml_start()
+        except Exception:  # noqa: BLE001 - NVML missing or refused: fall back
+            self.thread = None
+            try:
+                self._smi_start()
+            except OSError:
+                self.proc = None
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self._smi_collect()
 
     def summary(self):
-        rows = []
-        try:
-            with open(self.path) as f:
-                for line in f:
-                    parts = [p.strip() for p in line.split(",")]
-                    if len(parts) >= 8:
-                        rows.append(parts)
-        except OSError:
-            pass
-        finally:
-            if self.path:
-                try:
-                    os.unlink(self.path)
-                except OSError:
-                    pass
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        sm = []
-        smax = None
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                smax = float(r[2])
-            except ValueError:
-                continue
-            for n, val in zip(names, r[4:8]):
-                if val.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.sm_max, "reasons": ["no clock samples"],
+                    "samples": 0, "source": self.source}
+        reasons = sorted({r for _, rs in self.samples for r in rs})
+        return {"sm_mhz": statistics.median(sm for sm, _ in self.samples), "sm_max_mhz": self.sm_max,
+                "reasons": reasons, "samples": len(self.samples), "source": self.source}
+
+
+def pci_bus_id(torch, index):
+    """NVML-style PCI bus id of CUDA device `index` (None if torch does not expose it)."""
+    try:
+        p = torch.cuda.get_device_properties(index)
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except (AttributeError, RuntimeError):
+        return None
 
 
 # ---------------------------------------------------------------------------
@@ -196,7 +258,7 @@ def run_b200(args):
     torch.cuda.synchronize()
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, pci_bus_id(torch, local)) as clk:
         start.record()
         for _ in range(args.steps):
             step(True)
@@ -227,7 +289,7 @@ def run_b200(args):
         t = torch.tensor([e2e["ms"]], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e["ms"] = float(t.item())
-    e2e_value = tokens_per_step / (e2e["ms"] / 1e3)
+    e2e_value = None if args.no_e2e else tokens_per_step / (e2e["ms"] / 1e3)
 
     extra = {}
     if rank == 0 and not args.no_extra:
@@ -263,7 +325,8 @@ def run_b200(args):
                          "peak_source": peaks["source"] + (" sustained" if peak == peaks["bf16_sustained"] else " burst"),
                          "traffic": None},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
-                    "d2h_bytes_per_step": e2e["d2h"]},
+                    "d2h_bytes_per_step": e2e["d2h"], "steps": e2e.get("steps"),
+                    "overlap": e2e.get("overlap")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
@@ -277,33 +340,60 @@ def run_b200(args):
 
 
 def run_e2e(torch, KD, q, k, v, g, beta, do, C, args, dev):
-    """Host (pinned) inputs -> device -> fwd+bwd -> gradients back to host, per step."""
-    host_in = [x.cpu().pin_memory() for x in (q, k, v, g, beta, do)]
-    dev_in = [torch.empty_like(x) for x in (q, k, v, g, beta, do)]
-    host_out = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in (q, k, v, g, beta)]
+    """Host (pinned) inputs -> device -> fwd+bwd -> gradients back to host, every step.
+
+    Steps are pipelined the way a training loop with a prefetching loader runs:
+    step i+1's inputs travel host->device on one copy stream while step i
+    computes, and step i's gradients travel device->host on a second copy
+    stream (PCIe is full duplex, each direction has its own copy engine).
+    Device inputs and host outputs are double-buffered.  The timed region runs
+    from the first input copy to the last gradient copy; ms is its length / n.
+    """
+    ins = (q, k, v, g, beta, do)
+    host_in = [x.cpu().pin_memory() for x in ins]
+    dev_in = [[torch.empty_like(x) for x in ins] for _ in range(2)]
+    host_out = [[torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in ins[:5]] for _ in range(2)]
     h2d = sum(x.numel() * x.element_size() for x in host_in)
-    d2h = sum(x.numel() * x.element_size() for x in host_out)
+    d2h = sum(x.numel() * x.element_size() for x in host_out[0])
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_comp = torch.cuda.current_stream(dev)
 
-    def step():
-        for d_, h_ in zip(dev_in, host_in):
-            d_.copy_(h_, non_blocking=True)
-        qd, kd, vd, gd, bd, dod = dev_in
-        _, _, ckpt = KD.kda_fwd(qd, kd, vd, gd, bd, None, chunk=C, need_ckpt=True)
-        grads = KD.kda_bwd(qd, kd, vd, gd, bd, ckpt, dod, None, chunk=C, need_ds0=False)
-        for h_, d_ in zip(host_out, grads[:5]):
-            h_.copy_(d_, non_blocking=True)
+    def run(n, timed):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        computed = [None, None]  # per buffer: event after the step that read it
+        copied = [None, None]    # per host-out buffer: event after its last D2H
+        if timed:
+            s_in.record_event(start)
+        for i in range(n):
+            j = i & 1
+            with torch.cuda.stream(s_in):
+                if computed[j] is not None:
+                    s_in.wait_event(computed[j])  # step i-2 no longer reads buffer j
+                for d_, h_ in zip(dev_in[j], host_in):
+                    d_.copy_(h_, non_blocking=True)
+                loaded = s_in.record_event()
+            s_comp.wait_event(loaded)
+            qd, kd, vd, gd, bd, dod = dev_in[j]
+            _, _, ckpt = KD.kda_fwd(qd, kd, vd, gd, bd, None, chunk=C, need_ckpt=True)
+            grads = KD.kda_bwd(qd, kd, vd, gd, bd, ckpt, dod, None, chunk=C, need_ds0=False)[:5]
+            computed[j] = s_comp.record_event()
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(computed[j])
+                if copied[j] is not None:
+                    s_out.wait_event(copied[j])
+                for h_, d_ in zip(host_out[j], grads):
+                    h_.copy_(d_, non_blocking=True)
+                    d_.record_stream(s_out)
+                copied[j] = s_out.record_event()
+        if timed:
+            s_out.record_event(end)
+        torch.cuda.synchronize(dev)
+        return start.elapsed_time(end) / n if timed else None
 
-    for _ in range(max(1, args.warmup // 2)):
-        step()
-    torch.cuda.synchronize()
-    n = max(1, min(args.steps, 3))
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(n):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    return {"ms": s.elapsed_time(e) / n, "h2d": h2d, "d2h": d2h}
+    run(max(2, args.warmup // 2), False)
+    n = max(4, min(args.steps, 8))
+    return {"ms": run(n, True), "h2d": h2d, "d2h": d2h, "steps": n,
+            "overlap": "H2D of step i+1 and D2H of step i-1 overlap step i's compute"}
 
 
 def run_decode(torch, KD, dev, peaks, steps=64, warmup=8):
