@@ -28,6 +28,8 @@
 // Chunks whose decay exceeds the single-anchor budget take the exact
 // CUDA-core path for the score products and their adjoints.
 #include "kda_chunk.cuh"
+#include "kda_tma.cuh"
+#include "kda_ckpt_layout.h"
 
 namespace kda {
 namespace {
@@ -41,41 +43,37 @@ __device__ __forceinline__ uint32_t lane_off(int qw) { return static_cast<uint32
 // [128][128] as the CM operand image) per (batch, head, chunk) unit, written by
 // bwd_seq and read by bwd_par, each with one bulk copy.
 constexpr size_t WS_UNIT = 32768;
-// Per-chunk factors the forward stores after the boundary states of its
-// checkpoint: T = (I + diag(beta) Akk)^-1, Aqk, Akk, bf16 [64][64] CM tiles.
-constexpr size_t FAC_UNIT = 24576, FAC_T = 0, FAC_AQ = 8192, FAC_AK = 16384;
-
-// cp.async `bytes` (multiple of 16 * NT) contiguous bytes.
-__device__ __forceinline__ void stage_bytes(unsigned char* dst, const unsigned char* src, int bytes) {
-  for (int i = threadIdx.x; i < bytes / 16; i += NT) cp_async16(dst + 16 * i, src + 16 * i, true);
-}
 
 // ===========================================================================
 // bwd_seq
 // ===========================================================================
-constexpr int Q_SQ = 0, Q_SK = 16384, Q_SG = 32768, Q_DO = 49152;
-constexpr int Q_A3 = 65536;              // [-W ; Gam Q ; Gam K] CM[192][128]
-constexpr int Q_KI = Q_A3 + 49152;       // K Gi            | T fp32 | G fp32 (slow, with TP)
-constexpr int Q_TP = Q_KI + 16384;       // T beta [64][64] | dU^T [128][64] | prep partials
-constexpr int Q_KL = Q_TP + 16384;       // lam K
-constexpr int Q_SB = Q_KL + 16384;       // dS' bf16 [128][128] (also stored to the workspace)
-constexpr int Q_AQB = Q_SB + 32768;      // Aqk bf16 [64][64]
-constexpr int Q_BETA = Q_AQB + 8192;
-constexpr int Q_GC = Q_BETA + 256;
-constexpr int Q_BAR = Q_GC + 512;
+// Chunk c works on operand set p = c & 1 while chunk c-1's set is loaded: the
+// forward's Q Gam, K Gam, lam K, Gam_C, T, Aqk (bulk copies from the
+// checkpoint) and dO (TMA tile, or cp.async).
+constexpr int Q_QG0 = 0, Q_KG0 = 16384, Q_KL0 = 32768, Q_DO0 = 49152;  // set 0
+constexpr int Q_A3 = 65536;              // [-W ; set 1: Q Gam ; K Gam] CM[192][128]
+constexpr int Q_QG1 = Q_A3 + 16384, Q_KG1 = Q_A3 + 32768;
+constexpr int Q_KL1 = Q_A3 + 49152;      // set 1 lam K
+constexpr int Q_TP = Q_KL1 + 16384;      // T beta [64][64] | dU^T [128][64]
+constexpr int Q_SB = Q_TP + 16384;       // dS' bf16 [128][128] (also stored to the workspace)
+constexpr int Q_TA0 = Q_SB + 32768;      // set 0: T, Aqk bf16 [64][64] (adjacent, as in the checkpoint)
+constexpr int Q_TA1 = Q_TA0 + 16384;     // set 1
+constexpr int Q_DO1 = Q_TA1 + 16384;     // set 1 dO
+constexpr int Q_BETA = Q_DO1 + 16384;
+constexpr int Q_GC0 = Q_BETA + 256, Q_GC1 = Q_GC0 + 512;  // Gam_C per set
+constexpr int Q_BAR = Q_GC1 + 512;
 constexpr int SEQ_SMEM = Q_BAR + 64;
 
 __global__ void __launch_bounds__(NT, 1)
-bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ g,
-               const bf16* __restrict__ beta, const bf16* __restrict__ dout,
+bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
                const unsigned char* __restrict__ factors, const float* __restrict__ dsT,
                float* __restrict__ ds0, bf16* __restrict__ dsw, int T, int H,
-               int* __restrict__ err) {
+               int* __restrict__ err, const __grid_constant__ CUtensorMap tm_do, int use_tma) {
   extern __shared__ __align__(1024) unsigned char sm[];
   float* beta_s = reinterpret_cast<float*>(sm + Q_BETA);
-  float* gamC = reinterpret_cast<float*>(sm + Q_GC);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + Q_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + Q_BAR + 8);
+  uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + Q_BAR + 16);  // [2]: one per operand set
   unsigned char* A3 = sm + Q_A3;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;
@@ -83,28 +81,50 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   const int n_chunks = (T + C - 1) / C;
   const size_t tok0 = static_cast<size_t>(b) * T;
   const size_t rstride = static_cast<size_t>(H) * DK;
-  const bf16* qh = q + static_cast<size_t>(h) * DK;
-  const bf16* kh = k + static_cast<size_t>(h) * DK;
-  const bf16* gh = g + static_cast<size_t>(h) * DK;
   const bf16* doh = dout + static_cast<size_t>(h) * DV;
   const size_t unit = static_cast<size_t>(b) * H + h;
+  // shared offsets of operand set ps
+  auto set_qg = [](int ps) { return ps ? Q_QG1 : Q_QG0; };
+  auto set_kg = [](int ps) { return ps ? Q_KG1 : Q_KG0; };
+  auto set_kl = [](int ps) { return ps ? Q_KL1 : Q_KL0; };
+  auto set_do = [](int ps) { return ps ? Q_DO1 : Q_DO0; };
+  auto set_ta = [](int ps) { return ps ? Q_TA1 : Q_TA0; };
+  auto set_gc = [](int ps) { return ps ? Q_GC1 : Q_GC0; };
+  uint32_t ld_par = 0u, ld_pending = 0u;  // bit ps: phase parity / loads in flight of set ps
 
-  if (tid == 0) { mbar_init(mbar, 1); mbar_fence_init(); }
-  if (warp == 0) { tmem_alloc(tslot, 512); tmem_relinquish(); }
-  {
-    const int c = n_chunks - 1, t0 = c * C, rv = min(C, T - t0);
-    stage_tile(sm + Q_SQ, qh + (tok0 + t0) * rstride, rv, rstride);
-    stage_tile(sm + Q_SK, kh + (tok0 + t0) * rstride, rv, rstride);
-    stage_tile(sm + Q_SG, gh + (tok0 + t0) * rstride, rv, rstride);
-    stage_tile(sm + Q_DO, doh + (tok0 + t0) * rstride, rv, rstride);
-    const unsigned char* fu = factors + ((unit * n_chunks) + c) * FAC_UNIT;
-    stage_bytes(sm + Q_TP + 8192, fu + FAC_T, 8192);
-    stage_bytes(sm + Q_AQB, fu + FAC_AQ, 8192);
-    cp_async_commit();
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_init(mbar_ld, 1);
+    mbar_init(mbar_ld + 1, 1);
+    mbar_fence_init();
   }
+  if (warp == 0) { tmem_alloc(tslot, 512); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Issues every load of chunk cc into its operand set (after the set's last
+  // reader has finished); the beta of chunk cc goes to a register.
+  float beta_nx = 0.f;
+  auto issue_chunk = [&](int cc) {
+    const int ps = cc & 1, t0 = cc * C, rv = min(C, T - t0);
+    if (!use_tma) {
+      stage_tile(sm + set_do(ps), doh + (tok0 + t0) * rstride, rv, rstride);
+      cp_async_commit();
+    }
+    if (tid == 0) {
+      const unsigned char* fu = factors + (unit * n_chunks + cc) * FAC_UNIT;
+      fence_async_smem();
+      mbar_expect_tx(mbar_ld + ps, 32768 + 16384 + 16384 + 512 + (use_tma ? 16384 : 0));
+      bulk_load(sm + set_qg(ps), fu + FAC_QG, 32768, mbar_ld + ps);  // Q Gam, K Gam
+      bulk_load(sm + set_kl(ps), fu + FAC_KL, 16384, mbar_ld + ps);
+      bulk_load(sm + set_ta(ps), fu + FAC_T, 16384, mbar_ld + ps);   // T, Aqk
+      bulk_load(sm + set_gc(ps), fu + FAC_GC, 512, mbar_ld + ps);
+      if (use_tma) tma_tile(sm + set_do(ps), &tm_do, h, cc, b, mbar_ld + ps);
+    }
+    ld_pending |= 1u << ps;
+    beta_nx = tid < rv ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
+  };
+  issue_chunk(n_chunks - 1);
   const uint32_t tbase = *tslot;
   const uint32_t T_DS = tbase, T_W = tbase + 256, T_U = tbase + 384;
   const uint32_t tl = lane_off(qw);
@@ -131,30 +151,26 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 
   KDA_PT_INIT();
   for (int c = n_chunks - 1; c >= 0; --c) {
-    const int t0 = c * C, rows_valid = min(C, T - t0);
+    const int p = c & 1;
     cp_async_wait<0>();
+    failed |= !mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
+    ld_par ^= 1u << p;
+    ld_pending &= ~(1u << p);
     if (tid == 0) bulk_wait_read();  // SB may be rewritten: the previous dS' image is stored
-    if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
-    __syncthreads();
+    if (tid < C) beta_s[tid] = beta_nx;
+    if (__syncthreads_or(failed)) break;
     KDA_PT(1, 0);
-    float G[4][8];
-    prep(sm + Q_SQ, sm + Q_SK, sm + Q_SG, A3 + cm_off(64, 0, DK), A3 + cm_off(128, 0, DK),
-         nullptr, sm + Q_KL, gamC, G);
-    const bool more = c > 0;
-    const int tp0 = (c - 1) * C;
+    const float* gamC = reinterpret_cast<const float*>(sm + set_gc(p));
+    const uint32_t qg = smem_u32(sm + set_qg(p)), kg = smem_u32(sm + set_kg(p));
+    const uint32_t kl = smem_u32(sm + set_kl(p)), dob = smem_u32(sm + set_do(p));
+    const uint32_t aqb = smem_u32(sm + set_ta(p) + 8192);
+    if (c > 0) issue_chunk(c - 1);  // the other set was last read by chunk c + 1
     KDA_PT(1, 1);
-    __syncthreads();
-    if (more) {  // next chunk's q, k, g into the free staging
-      stage_tile(sm + Q_SQ, qh + (tok0 + tp0) * rstride, C, rstride);
-      stage_tile(sm + Q_SK, kh + (tok0 + tp0) * rstride, C, rstride);
-      stage_tile(sm + Q_SG, gh + (tok0 + tp0) * rstride, C, rstride);
-      cp_async_commit();
-    }
     {  // T diag(beta) from the forward's bf16 T tile
       const int r = tid >> 2, c0 = (tid & 3) * 16;
       float tv[16];
-      unpack_bf16x8(ld16(sm + Q_TP + 8192, cm_off(r, c0, C)), tv);
-      unpack_bf16x8(ld16(sm + Q_TP + 8192, cm_off(r, c0 + 8, C)), tv + 8);
+      unpack_bf16x8(ld16(sm + set_ta(p), cm_off(r, c0, C)), tv);
+      unpack_bf16x8(ld16(sm + set_ta(p), cm_off(r, c0 + 8, C)), tv + 8);
 #pragma unroll
       for (int j = 0; j < 16; ++j) tv[j] *= beta_s[c0 + j];
       st16(sm + Q_TP, cm_off(r, c0, C), pack_bf16x8(tv));
@@ -168,9 +184,9 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       tc_fence_after();
       const uint32_t id = idesc_bf16(64, 128, false, true);
       const uint32_t tp = smem_u32(sm + Q_TP);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks)
-        mma_bf16(T_W, desc_kmajor(tp + ks * 256, C), desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), id, ks > 0);
+        mma_bf16(T_W, desc_kmajor(tp + ks * 256, C), desc_mnmajor(kg + ks * 4096, DK), id, ks > 0);
       mma_commit(mbar);
     }
     failed |= !mma_wait();
@@ -220,13 +236,12 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
                  WS_UNIT);
       bulk_commit();
       tc_fence_after();
-      const uint32_t sb = smem_u32(sm + Q_SB), kl = smem_u32(sm + Q_KL);
-      const uint32_t dob = smem_u32(sm + Q_DO), aqb = smem_u32(sm + Q_AQB);
+      const uint32_t sb = smem_u32(sm + Q_SB);
       const uint32_t id1 = idesc_bf16(128, 64, true, false), id2 = idesc_bf16(128, 64, true, true);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < DK / 16; ++ks)
         mma_bf16(T_U, desc_mnmajor(sb + ks * 4096, DV), desc_kmajor(kl + ks * 256, DK), id1, ks > 0);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks)
         mma_bf16(T_U, desc_mnmajor(dob + ks * 4096, DV), desc_mnmajor(aqb + ks * 2048, C), id2, 1u);
       mma_commit(mbar);
@@ -248,12 +263,12 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // dS += (Gam Q)^T dO + (-W)^T dU
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t dob = smem_u32(sm + Q_DO), dut = smem_u32(sm + Q_TP);
+      const uint32_t dut = smem_u32(sm + Q_TP);
       const uint32_t id1 = idesc_bf16(128, 128, true, true), id2 = idesc_bf16(128, 128, true, false);
-#pragma unroll
+#pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks)
-        mma_bf16(T_DS, desc_mnmajor(a3 + 64 * 256 + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id1, 1u);
-#pragma unroll
+        mma_bf16(T_DS, desc_mnmajor(qg + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id1, 1u);
+#pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks)
         mma_bf16(T_DS, desc_mnmajor(a3 + ks * 4096, DK), desc_kmajor(dut + ks * 256, C), id2, 1u);
       mma_commit(mbar);
@@ -261,13 +276,6 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
     KDA_PT(1, 6);
-    if (more) {
-      stage_tile(sm + Q_DO, doh + (tok0 + tp0) * rstride, C, rstride);
-      const unsigned char* fu = factors + ((unit * n_chunks) + c - 1) * FAC_UNIT;
-      stage_bytes(sm + Q_TP + 8192, fu + FAC_T, 8192);
-      stage_bytes(sm + Q_AQB, fu + FAC_AQ, 8192);
-      cp_async_commit();
-    }
   }
   if (!failed && ds0) {
     const int d = 32 * qw + lane;
@@ -281,6 +289,9 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   }
   if (failed && tid == 0 && err) atomicExch(err, 1);
   cp_async_wait<0>();
+  // a chunk abandoned on a timeout may leave loads in flight: wait (bounded)
+  for (int ps = 0; ps < 2; ++ps)
+    if ((ld_pending >> ps) & 1u) mbar_wait(mbar_ld + ps, (ld_par >> ps) & 1u);
   if (tid == 0) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
@@ -294,26 +305,37 @@ bwd_seq_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 // ===========================================================================
 constexpr int P_SQ = 0;                  // dO | raw q (exact path) | g^T [128][64]
 constexpr int P_SK = 16384;              // dS' (lo) | dW^T [128][64] | raw k (exact path) | v^T
-constexpr int P_SG = 32768;              // dS' (hi) | raw g
+constexpr int P_SG = 32768;              // dS' (hi) | raw g | KI^T [128][64]
 constexpr int P_V = 49152;               // v staging | U bf16 [64][128] | raw v
-constexpr int P_A3 = 65536;              // [W ; Gam Q ; Gam K] (q, k staged in place) | KG^T
-constexpr int P_KI = P_A3 + 49152;       // g staging | K Gi
-constexpr int P_KL = P_KI + 16384;       // lam K | dU^T [128][64] | [dAqk ; beta dL] [128][64] | KI^T
+constexpr int P_A3 = 65536;              // [W ; Gam Q ; Gam K] (the forward's images) | KG^T
+constexpr int P_KI = P_A3 + 49152;       // K Gi (the forward's image)
+constexpr int P_KL = P_KI + 16384;       // lam K | dU^T [128][64] | [dAqk ; beta dL] [128][64]
 constexpr int P_SB = P_KL + 16384;       // S_c bf16 [128][128] | Yw^T, Yu^T | dbeta partials
 constexpr int P_TP = P_SB + 32768;       // T beta [64][64] | v~ bf16 [64][128] | QG^T | G fp32 (exact path, with TB/AQB)
 constexpr int P_TB = P_TP + 16384;       // T bf16 [64][64]
 constexpr int P_AQB = P_TB + 8192;       // Aqk bf16
 constexpr int P_AKB = P_AQB + 8192;      // Akk bf16
 constexpr int P_BETA = P_AKB + 8192;     // beta fp32[64]
-constexpr int P_GC = P_BETA + 256;       // Gam_C fp32[128]
-constexpr int P_DGC = P_GC + 512;        // dGam_C partial fp32[128]
+constexpr int P_GF = P_BETA + 256;       // [2][544]: Gam_C fp32[128] + exact-path flag, per unit parity
+constexpr int P_DGC = P_GF + 2 * 544;    // dGam_C partial fp32[128]
 constexpr int P_DB = P_DGC + 512;        // dbeta accum fp32[64]
 constexpr int P_XCH = P_DB + 256;        // half-exchange fp32[2][2][128]
 constexpr int P_BAR = P_XCH + 2048;
-constexpr int PAR_SMEM = P_BAR + 64;
-// the factor block is copied in one piece: TB, AQB, AKB mirror FAC_T, FAC_AQ, FAC_AK
+constexpr int P_MMA = P_BAR + 64;         // MMA issue table (MmaOp[96])
+// issue-table groups: first entry, count
+constexpr int G_WU = 0, N_WU = 8;         // W, U
+constexpr int G_WS = 8, N_WS = 8;         // W S_c
+constexpr int G_DU = 16, N_DU = 20;       // dU^T, dKL^T
+constexpr int G_SD = 36, N_SD = 16;       // S_c [dO^T | dU^T]
+constexpr int G_Y = 52, N_Y = 8;          // Yw^T, Yu^T
+constexpr int G_DA = 60, N_DA = 24;       // dAqk, dL
+constexpr int G_VII = 84, N_VII = 12;     // [dQG^T | dKG^T] +=, dKI^T
+constexpr int PAR_SMEM = P_MMA + 96 * 32;
+// the checkpoint's adjacent tiles land with one bulk copy each: [T, Aqk, Akk] in
+// TB, AQB, AKB; [Q Gam, K Gam] in A3 rows 64..191; [K Gi, lam K] in KI, KL
 static_assert(P_AQB - P_TB == static_cast<int>(FAC_AQ) && P_AKB - P_TB == static_cast<int>(FAC_AK) &&
-                  P_BETA - P_TB == static_cast<int>(FAC_UNIT),
+                  FAC_QG == FAC_AK + 8192 && FAC_KG == FAC_QG + 16384 &&
+                  P_KL - P_KI == static_cast<int>(FAC_KL - FAC_KI) && FAC_KL == FAC_KI + 16384,
               "factor staging layout");
 
 // fp32 checkpoint state (row-major) -> bf16 CM operand tile.
@@ -335,17 +357,20 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
                const bf16* __restrict__ dsw,
                const bf16* __restrict__ dout, bf16* __restrict__ dq, bf16* __restrict__ dk,
                bf16* __restrict__ dv, bf16* __restrict__ dg, bf16* __restrict__ dbeta, int B,
-               int T, int H, int* __restrict__ err) {
+               int T, int H, int* __restrict__ err, const __grid_constant__ CUtensorMap tm_q,
+               const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_g,
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+               int use_tma) {
   extern __shared__ __align__(1024) unsigned char sm[];
   float* beta_s = reinterpret_cast<float*>(sm + P_BETA);
-  float* gamC = reinterpret_cast<float*>(sm + P_GC);
   float* dgc = reinterpret_cast<float*>(sm + P_DGC);
   float* dbs = reinterpret_cast<float*>(sm + P_DB);
   float* xch = reinterpret_cast<float*>(sm + P_XCH);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P_BAR + 8);
   uint64_t* mbar_fac = reinterpret_cast<uint64_t*>(sm + P_BAR + 16);   // T, Aqk, Akk bulk load
-  uint64_t* mbar_late = reinterpret_cast<uint64_t*>(sm + P_BAR + 24);  // dS', S_c bulk loads
+  uint64_t* mbar_late = reinterpret_cast<uint64_t*>(sm + P_BAR + 24);  // dS', S_c (+ dO) loads
+  uint64_t* mbar_rs = reinterpret_cast<uint64_t*>(sm + P_BAR + 32);    // restaged tiles (TMA)
   unsigned char* A3 = sm + P_A3;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;
@@ -357,6 +382,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     mbar_init(mbar, 1);
     mbar_init(mbar_fac, 1);
     mbar_init(mbar_late, 1);
+    mbar_init(mbar_rs, 1);
     mbar_fence_init();
   }
   if (warp == 0) { tmem_alloc(tslot, 512); tmem_relinquish(); }
@@ -383,15 +409,74 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   };
   const uint32_t a3 = smem_u32(A3);
 
-  // Unit inputs q, k, g, v and the forward's T, Aqk, Akk are staged where prep
-  // and the MMAs consume them: q, k into A3 rows 64..191 (prep scales them in
-  // place), g into KI (overwritten by K Gi).  They are issued one unit ahead,
-  // during the previous unit's epilogue: the tiles as one cp.async group, the
-  // contiguous 24 KB factor block (TB, AQB, AKB are adjacent) as one bulk load
-  // completing on mbar_fac.  Every bulk phase is waited before the CTA exits.
+  // The MMA issue table: every descriptor of the unit loop is fixed for the
+  // kernel's lifetime.  Only thread 0 builds and reads it.
+  MmaOp* tab = reinterpret_cast<MmaOp*>(sm + P_MMA);
+  if (tid == 0) {
+    const uint32_t tp = smem_u32(sm + P_TP), vb = smem_u32(sm + P_V), sb = smem_u32(sm + P_SB);
+    const uint32_t dsp = smem_u32(sm + P_SK), kl = smem_u32(sm + P_KL), dob = smem_u32(sm + P_SQ);
+    const uint32_t aqb = smem_u32(sm + P_AQB), tb = smem_u32(sm + P_TB), ki = smem_u32(sm + P_KI);
+    int n = G_WU;  // W = (T b)(Gam K), U = (T b) V   (M = 64)
+    for (int ks = 0; ks < C / 16; ++ks) {
+      const uint64_t ad = desc_kmajor(tp + ks * 256, C);
+      const uint32_t id = idesc_bf16(64, 128, false, true);
+      mma_op(tab, n++, T_IV, ad, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), id, ks > 0);
+      mma_op(tab, n++, T_UF, ad, desc_mnmajor(vb + ks * 4096, DV), id, ks > 0);
+    }
+    for (int ks = 0; ks < DK / 16; ++ks)  // W S_c   (M = 64)
+      mma_op(tab, n++, T_WS, desc_kmajor(a3 + ks * 256, DK), desc_mnmajor(sb + ks * 4096, DV),
+             idesc_bf16(64, 128, false, true), ks > 0);
+    // dU^T = dS'^T (lam K)^T + dO^T Aqk ;  dKL^T = dS' v~^T
+    for (int ks = 0; ks < DK / 16; ++ks)
+      mma_op(tab, n++, T_DU, desc_mnmajor(dsp + ks * 4096, DV), desc_kmajor(kl + ks * 256, DK),
+             idesc_bf16(128, 64, true, false), ks > 0);
+    for (int ks = 0; ks < C / 16; ++ks)
+      mma_op(tab, n++, T_DU, desc_mnmajor(dob + ks * 4096, DV), desc_mnmajor(aqb + ks * 2048, C),
+             idesc_bf16(128, 64, true, true), 1u);
+    for (int ks = 0; ks < DV / 16; ++ks)
+      mma_op(tab, n++, T_KL, desc_kmajor(dsp + ks * 256, DV), desc_kmajor(tp + ks * 256, DV),
+             idesc_bf16(128, 64, false, false), ks > 0);
+    for (int ks = 0; ks < DV / 16; ++ks) {  // S_c [dO^T | dU^T]
+      const uint64_t ad = desc_kmajor(sb + ks * 256, DV);
+      mma_op(tab, n++, T_IV, ad, desc_kmajor(dob + ks * 256, DV), idesc_bf16(128, 64, false, false), ks > 0);
+      mma_op(tab, n++, T_IV + 64, ad, desc_mnmajor(kl + ks * 2048, C), idesc_bf16(128, 64, false, true), ks > 0);
+    }
+    for (int ks = 0; ks < C / 16; ++ks) {  // Yw^T = dW^T T,  Yu^T = dU^T T
+      const uint64_t bd = desc_mnmajor(tb + ks * 2048, C);
+      const uint32_t id = idesc_bf16(128, 64, false, true);
+      mma_op(tab, n++, T_UF, desc_kmajor(dsp + ks * 256, C), bd, id, ks > 0);
+      mma_op(tab, n++, T_UF + 64, desc_kmajor(kl + ks * 256, C), bd, id, ks > 0);
+    }
+    // dAqk = dO v~^T, dL~ = Yu U^T + Yw W^T   (M = 64)
+    for (int ks = 0; ks < DV / 16; ++ks)
+      mma_op(tab, n++, T_SC, desc_kmajor(dob + ks * 256, DV), desc_kmajor(tp + ks * 256, DV),
+             idesc_bf16(64, 64, false, false), ks > 0);
+    for (int ks = 0; ks < DV / 16; ++ks)
+      mma_op(tab, n++, T_L, desc_mnmajor(sb + 16384 + ks * 2048, C), desc_kmajor(vb + ks * 256, DV),
+             idesc_bf16(64, 64, true, false), ks > 0);
+    for (int ks = 0; ks < DK / 16; ++ks)
+      mma_op(tab, n++, T_L, desc_mnmajor(sb + ks * 2048, C), desc_kmajor(a3 + ks * 256, DK),
+             idesc_bf16(64, 64, true, false), 1u);
+    // [dQG^T | dKG^T] += KI^T [dAqk ; beta dL]^T ;  dKI^T = QG^T dAqk + KG^T (beta dL)
+    for (int ks = 0; ks < C / 16; ++ks)
+      mma_op(tab, n++, T_IV, desc_mnmajor(ki + ks * 4096, DK), desc_kmajor(kl + ks * 256, C),
+             idesc_bf16(128, 128, true, false), 1u);
+    for (int ks = 0; ks < C / 16; ++ks)
+      mma_op(tab, n++, T_SC, desc_mnmajor(a3 + 64 * 256 + ks * 4096, DK), desc_mnmajor(kl + ks * 2048, C),
+             idesc_bf16(128, 64, true, true), ks > 0);
+    for (int ks = 0; ks < C / 16; ++ks)
+      mma_op(tab, n++, T_SC, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK),
+             desc_mnmajor(kl + 8192 + ks * 2048, C), idesc_bf16(128, 64, true, true), 1u);
+  }
+
+  // A unit's inputs are the forward's operand images (T, Aqk, Akk; Q Gam, K Gam;
+  // K Gi, lam K; Gam_C and the exact-path flag: bulk copies from the checkpoint)
+  // and v (TMA tile when use_tma, else one cp.async group of all threads).  They
+  // are issued one unit ahead, during the previous unit's epilogue, and complete
+  // on mbar_fac.  Every asynchronous phase is waited before the CTA exits.
   int it = 0;                                      // units processed by this CTA
-  bool fac_pending = false, late_pending = false;  // bulk loads issued, not yet waited
-  uint32_t fac_par = 0, late_par = 0;
+  bool fac_pending = false, late_pending = false, rs_pending = false;  // issued, not yet waited
+  uint32_t fac_par = 0, late_par = 0, rs_par = 0;
   auto issue_inputs = [&](long long uu, float& beta_nx) {
     const int cc = static_cast<int>(uu % n_chunks);
     const long long bhn = uu / n_chunks;
@@ -399,16 +484,20 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     const int rv = min(C, T - cc * C);
     const size_t tk = static_cast<size_t>(bn) * T + static_cast<size_t>(cc) * C;
     const size_t src = static_cast<size_t>(hn) * DK + tk * rstride;
-    stage_tile(A3 + cm_off(64, 0, DK), q + src, rv, rstride);
-    stage_tile(A3 + cm_off(128, 0, DK), k + src, rv, rstride);
-    stage_tile(sm + P_KI, g + src, rv, rstride);
-    stage_tile(sm + P_V, v + src, rv, rstride);
-    cp_async_commit();
+    if (!use_tma) {
+      stage_tile(sm + P_V, v + src, rv, rstride);
+      cp_async_commit();
+    }
     if (tid == 0) {
       const unsigned char* fu = factors + ((static_cast<size_t>(bn) * H + hn) * n_chunks + cc) * FAC_UNIT;
+      const int gf = P_GF + 544 * ((uu == blockIdx.x ? it : it + 1) & 1);
       fence_async_smem();
-      mbar_expect_tx(mbar_fac, FAC_UNIT);
-      bulk_load(sm + P_TB, fu, FAC_UNIT, mbar_fac);
+      mbar_expect_tx(mbar_fac, 24576 + 32768 + 32768 + FAC_GF_BYTES + (use_tma ? 16384 : 0));
+      bulk_load(sm + P_TB, fu + FAC_T, 24576, mbar_fac);                  // T, Aqk, Akk
+      bulk_load(A3 + cm_off(64, 0, DK), fu + FAC_QG, 32768, mbar_fac);    // Q Gam, K Gam
+      bulk_load(sm + P_KI, fu + FAC_KI, 32768, mbar_fac);                 // K Gi, lam K
+      bulk_load(sm + gf, fu + FAC_GC, FAC_GF_BYTES, mbar_fac);            // Gam_C, flag
+      if (use_tma) tma_tile(sm + P_V, &tm_v, hn, cc, bn, mbar_fac);
     }
     fac_pending = true;
     fac_par = static_cast<uint32_t>(uu == blockIdx.x ? it : it + 1) & 1u;
@@ -431,14 +520,17 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 
     // dO, dS' and S_c (bf16 checkpoint: the operand image) land while prep and
     // the W, U MMAs run
-    stage_tile(sm + P_SQ, dout + hoff + tok0 * rstride, rows_valid, rstride);
-    cp_async_commit();
+    if (!use_tma) {
+      stage_tile(sm + P_SQ, dout + hoff + tok0 * rstride, rows_valid, rstride);
+      cp_async_commit();
+    }
     if (tid == 0) {
       constexpr uint32_t late_bytes = WS_UNIT + (sizeof(Tc) == 2 ? DK * DV * 2 : 0);
       fence_async_smem();
-      mbar_expect_tx(mbar_late, late_bytes);
+      mbar_expect_tx(mbar_late, late_bytes + (use_tma ? 16384 : 0));
       bulk_load(sm + P_SK, reinterpret_cast<const unsigned char*>(dsw) + unit_sq * WS_UNIT, WS_UNIT, mbar_late);
       if constexpr (sizeof(Tc) == 2) bulk_load(sm + P_SB, s_ckpt + unit_sq * (DK * DV), DK * DV * 2, mbar_late);
+      if (use_tma) tma_tile(sm + P_SQ, &tm_do, h, c, b, mbar_late);
     }
     late_pending = true;
     late_par = static_cast<uint32_t>(it) & 1u;
@@ -453,13 +545,10 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     if (__syncthreads_or(failed)) break;
 
     KDA_PT(2, 0);
-    // ---- recompute: prep (T and the scores come from the forward), then W, U ----
-    float G[4][8];
-    unsigned char* qk = A3 + cm_off(64, 0, DK);
-    unsigned char* kk = A3 + cm_off(128, 0, DK);
-    const bool slow = prep(qk, kk, sm + P_KI, qk, kk, sm + P_KI, sm + P_KL, gamC, G);
+    // ---- W, U from the forward's T and K Gam (no recompute of the decay prep) ----
+    const float* gamC = reinterpret_cast<const float*>(sm + P_GF + 544 * (it & 1));
+    const bool slow = reinterpret_cast<const uint32_t*>(gamC)[128] != 0u;  // exact-path chunk
     KDA_PT(2, 1);
-    __syncthreads();
     {  // T diag(beta) from the bf16 T tile
       const int r = tid >> 2, c0 = (tid & 3) * 16;
       float tv[16];
@@ -476,14 +565,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // W = (T b)(Gam K), U = (T b) V   (M = 64)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t id = idesc_bf16(64, 128, false, true);
-      const uint32_t tp = smem_u32(sm + P_TP), vb = smem_u32(sm + P_V);
-#pragma unroll 1
-      for (int ks = 0; ks < C / 16; ++ks) {
-        const uint64_t ad = desc_kmajor(tp + ks * 256, C);
-        mma_bf16(T_IV, ad, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), id, ks > 0);
-        mma_bf16(T_UF, ad, desc_mnmajor(vb + ks * 4096, DV), id, ks > 0);
-      }
+      mma_run(tab, G_WU, N_WU);
       mma_commit(mbar);
     }
     failed |= !mma_wait();
@@ -517,11 +599,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // W S_c  (M = 64)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t id = idesc_bf16(64, 128, false, true);
-      const uint32_t sb = smem_u32(sm + P_SB);
-#pragma unroll 1
-      for (int ks = 0; ks < DK / 16; ++ks)
-        mma_bf16(T_WS, desc_kmajor(a3 + ks * 256, DK), desc_mnmajor(sb + ks * 4096, DV), id, ks > 0);
+      mma_run(tab, G_WS, N_WS);
       mma_commit(mbar);
     }
     {  // dGam_C partial sums: sum_j S_c[d][j] dS'[d][j]
@@ -562,19 +640,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // dU^T = dS'^T (lam K)^T + dO^T Aqk ;  dKL^T = dS' v~^T
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t dsp = smem_u32(sm + P_SK), kl = smem_u32(sm + P_KL);
-      const uint32_t dob = smem_u32(sm + P_SQ), aqb = smem_u32(sm + P_AQB), vt = smem_u32(sm + P_TP);
-      const uint32_t id1 = idesc_bf16(128, 64, true, false), id2 = idesc_bf16(128, 64, true, true);
-      const uint32_t id3 = idesc_bf16(128, 64, false, false);
-#pragma unroll 1
-      for (int ks = 0; ks < DK / 16; ++ks)
-        mma_bf16(T_DU, desc_mnmajor(dsp + ks * 4096, DV), desc_kmajor(kl + ks * 256, DK), id1, ks > 0);
-#pragma unroll 1
-      for (int ks = 0; ks < C / 16; ++ks)
-        mma_bf16(T_DU, desc_mnmajor(dob + ks * 4096, DV), desc_mnmajor(aqb + ks * 2048, C), id2, 1u);
-#pragma unroll 1
-      for (int ks = 0; ks < DV / 16; ++ks)
-        mma_bf16(T_KL, desc_kmajor(dsp + ks * 256, DV), desc_kmajor(vt + ks * 256, DV), id3, ks > 0);
+      mma_run(tab, G_DU, N_DU);
       mma_commit(mbar);
       KDA_PT(2, 20);
     }
@@ -583,8 +649,18 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     if (__syncthreads_or(failed)) break;
     KDA_PT(2, 7);
     // dS' is dead: restage g (for the epilogue) over its upper half
-    stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
-    cp_async_commit();
+    if (use_tma) {
+      if (tid == 0) {
+        fence_async_smem();
+        mbar_expect_tx(mbar_rs, slow ? 4 * 16384 : 2 * 16384);  // + v (and q, k) below
+        tma_tile(sm + P_SG, &tm_g, h, c, b, mbar_rs);
+      }
+      rs_pending = true;
+      rs_par = static_cast<uint32_t>(it) & 1u;
+    } else {
+      stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
+      cp_async_commit();
+    }
     {  // dU^T -> bf16 [j][c] (KL region)
       const int j = 32 * qw + lane;
       float vals[32];
@@ -600,14 +676,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // S_c [dO^T | dU^T] -> (dO S^T)^T | (dU S^T)^T
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t sb = smem_u32(sm + P_SB), dob = smem_u32(sm + P_SQ), dut = smem_u32(sm + P_KL);
-      const uint32_t id1 = idesc_bf16(128, 64, false, false), id2 = idesc_bf16(128, 64, false, true);
-#pragma unroll 1
-      for (int ks = 0; ks < DV / 16; ++ks) {
-        const uint64_t ad = desc_kmajor(sb + ks * 256, DV);
-        mma_bf16(T_IV, ad, desc_kmajor(dob + ks * 256, DV), id1, ks > 0);
-        mma_bf16(T_IV + 64, ad, desc_mnmajor(dut + ks * 2048, C), id2, ks > 0);
-      }
+      mma_run(tab, G_SD, N_SD);
       mma_commit(mbar);
       KDA_PT(2, 22);
     }
@@ -632,14 +701,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // Yw^T = dW^T T,  Yu^T = dU^T T
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t dwt = smem_u32(sm + P_SK), dut = smem_u32(sm + P_KL), tb = smem_u32(sm + P_TB);
-      const uint32_t id = idesc_bf16(128, 64, false, true);
-#pragma unroll 1
-      for (int ks = 0; ks < C / 16; ++ks) {
-        const uint64_t bd = desc_mnmajor(tb + ks * 2048, C);
-        mma_bf16(T_UF, desc_kmajor(dwt + ks * 256, C), bd, id, ks > 0);
-        mma_bf16(T_UF + 64, desc_kmajor(dut + ks * 256, C), bd, id, ks > 0);
-      }
+      mma_run(tab, G_Y, N_Y);
       mma_commit(mbar);
     }
     failed |= !mma_wait();
@@ -668,18 +730,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // dAqk = dO v~^T, dL~ = Yu U^T + Yw W^T   (M = 64)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t dob = smem_u32(sm + P_SQ), vt = smem_u32(sm + P_TP);
-      const uint32_t ywt = smem_u32(sm + P_SB), yut = smem_u32(sm + P_SB + 16384), ub = smem_u32(sm + P_V);
-      const uint32_t id1 = idesc_bf16(64, 64, false, false), id2 = idesc_bf16(64, 64, true, false);
-#pragma unroll 1
-      for (int ks = 0; ks < DV / 16; ++ks)
-        mma_bf16(T_SC, desc_kmajor(dob + ks * 256, DV), desc_kmajor(vt + ks * 256, DV), id1, ks > 0);
-#pragma unroll 1
-      for (int ks = 0; ks < DV / 16; ++ks)
-        mma_bf16(T_L, desc_mnmajor(yut + ks * 2048, C), desc_kmajor(ub + ks * 256, DV), id2, ks > 0);
-#pragma unroll 1
-      for (int ks = 0; ks < DK / 16; ++ks)
-        mma_bf16(T_L, desc_mnmajor(ywt + ks * 2048, C), desc_kmajor(a3 + ks * 256, DK), id2, 1u);
+      mma_run(tab, G_DA, N_DA);
       mma_commit(mbar);
       KDA_PT(2, 24);
     }
@@ -688,12 +739,23 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     if (__syncthreads_or(failed)) break;
     KDA_PT(2, 13);
     // U, dO and dW^T are dead: restage v (and raw q, k for the exact path)
-    stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
-    if (slow) {
-      stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
-      stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
+    if (use_tma) {
+      if (tid == 0) {
+        fence_async_smem();
+        tma_tile(sm + P_V, &tm_v, h, c, b, mbar_rs);
+        if (slow) {
+          tma_tile(sm + P_SQ, &tm_q, h, c, b, mbar_rs);
+          tma_tile(sm + P_SK, &tm_k, h, c, b, mbar_rs);
+        }
+      }
+    } else {
+      stage_tile(sm + P_V, v + hoff + tok0 * rstride, rows_valid, rstride);
+      if (slow) {
+        stage_tile(sm + P_SQ, q + hoff + tok0 * rstride, rows_valid, rstride);
+        stage_tile(sm + P_SK, k + hoff + tok0 * rstride, rows_valid, rstride);
+      }
+      cp_async_commit();
     }
-    cp_async_commit();
     {  // [dAqk ; beta dL] -> bf16 [128][64] (KL region); dbeta += rowsum(dL * Akk)
       const int r = 16 * qw + lane;
       float da[32], dl[32];
@@ -730,36 +792,39 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       // [dQG^T | dKG^T] += KI^T [dAqk ; beta dL]^T ;  dKI^T = QG^T dAqk + KG^T (beta dL)
       if (tid == 0) {
         tc_fence_after();
-        const uint32_t ki = smem_u32(sm + P_KI), da = smem_u32(sm + P_KL);
-        const uint32_t id1 = idesc_bf16(128, 128, true, false), id2 = idesc_bf16(128, 64, true, true);
-#pragma unroll 1
-        for (int ks = 0; ks < C / 16; ++ks)
-          mma_bf16(T_IV, desc_mnmajor(ki + ks * 4096, DK), desc_kmajor(da + ks * 256, C), id1, 1u);
-#pragma unroll 1
-        for (int ks = 0; ks < C / 16; ++ks)
-          mma_bf16(T_SC, desc_mnmajor(a3 + 64 * 256 + ks * 4096, DK), desc_mnmajor(da + ks * 2048, C), id2, ks > 0);
-#pragma unroll 1
-        for (int ks = 0; ks < C / 16; ++ks)
-          mma_bf16(T_SC, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), desc_mnmajor(da + 8192 + ks * 2048, C), id2, 1u);
+        mma_run(tab, G_VII, N_VII);
         mma_commit(mbar);
+        KDA_PT(2, 29);
       }
       // channel-major copies for the epilogue: QG -> TP, KG -> A3 rows 0..63 (W is dead;
       // the MMAs only read QG, KG)
       transpose_cm<64, 128>(smem_u32(sm + P_TP), a3 + 64 * 256, warp, lane, NT / 32);
       transpose_cm<64, 128>(a3, a3 + 128 * 256, warp, lane, NT / 32);
+      KDA_PT(2, 30);
       cp_async_wait<0>();
-      __syncthreads();
+      if (use_tma) {
+        failed |= !mbar_wait(mbar_rs, rs_par);
+        rs_pending = false;
+      }
+      if (__syncthreads_or(failed)) break;
+      KDA_PT(2, 31);
       transpose_cm<64, 128>(smem_u32(sm + P_SQ), smem_u32(sm + P_SG), warp, lane, NT / 32);  // g
       transpose_cm<64, 128>(smem_u32(sm + P_SK), smem_u32(sm + P_V), warp, lane, NT / 32);   // v
       failed |= !mma_wait();
       if (__syncthreads_or(failed)) break;
-      transpose_cm<64, 128>(smem_u32(sm + P_KL), smem_u32(sm + P_KI), warp, lane, NT / 32);  // KI
+      KDA_PT(2, 19);
+      transpose_cm<64, 128>(smem_u32(sm + P_SG), smem_u32(sm + P_KI), warp, lane, NT / 32);  // KI
       __syncthreads();
-      // A3 rows 64..191, KI, V, TB, AQB and AKB are free: stage the next unit
+      // A3 rows 64..191, KI, KL, V, TB, AQB, AKB and the other Gam_C slot are free:
+      // stage the next unit
       if (u_next < n_units) issue_inputs(u_next, beta_nx);
       prefetched = true;
     } else {
       cp_async_wait<0>();
+      if (use_tma) {
+        failed |= !mbar_wait(mbar_rs, rs_par);
+        rs_pending = false;
+      }
       if (__syncthreads_or(failed)) break;
     }
     KDA_PT(2, 15);
@@ -773,7 +838,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       float* TR = reinterpret_cast<float*>(sm + P_SB);  // dbeta partials [128][64], xor-swizzled
       const size_t gbase = hoff + tok0 * rstride + d;
       if (!slow) {
-        // channel-major tiles: g (SQ), v (SK), QG (TP), KG (A3), KI (KL), each [128][64]
+        // channel-major tiles: g (SQ), v (SK), QG (TP), KG (A3), KI (SG), each [128][64]
         float gm[32];
 #pragma unroll
         for (int j = 0; j < 4; ++j) unpack_bf16x8(ld16(sm + P_SQ, cm_off(d, cb + 8 * j, C)), gm + 8 * j);
@@ -799,7 +864,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           tmem_ld8(T_UF + 64 + tl + c8, yu);
           unpack_bf16x8(ld16(sm + P_TP, cm_off(d, c8, C)), qg);
           unpack_bf16x8(ld16(A3, cm_off(d, c8, C)), kg);
-          unpack_bf16x8(ld16(sm + P_KL, cm_off(d, c8, C)), ki);
+          unpack_bf16x8(ld16(sm + P_SG, cm_off(d, c8, C)), ki);
           unpack_bf16x8(ld16(sm + P_SK, cm_off(d, c8, C)), vv);
           tmem_wait_ld();
 #pragma unroll
@@ -923,6 +988,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   // for them before the shared memory is released
   if (fac_pending) mbar_wait(mbar_fac, fac_par);
   if (late_pending) mbar_wait(mbar_late, late_par);
+  if (rs_pending) mbar_wait(mbar_rs, rs_par);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -960,10 +1026,14 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
   const size_t n = (static_cast<size_t>(T) + C - 1) / C;
   const unsigned char* factors =
       static_cast<const unsigned char*>(s_ckpt) + static_cast<size_t>(B) * H * n * DK * DV * sizeof(Tc);
-  bwd_seq_kernel<<<B * H, NT, SEQ_SMEM, st>>>(
-      static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(g),
-      static_cast<const bf16*>(beta), static_cast<const bf16*>(dout), factors, dsT, ds0, dsw, T, H,
-      err);
+  // TMA tile maps of the inputs; any length or map the encoder refuses falls back
+  // to cp.async staging inside the kernels
+  CUtensorMap tm[5] = {};
+  const void* srcs[5] = {q, k, g, v, dout};
+  int use_tma = 1;
+  for (int i = 0; i < 5 && use_tma; ++i) use_tma = make_tile_map(&tm[i], srcs[i], B, T, H) ? 1 : 0;
+  bwd_seq_kernel<<<B * H, NT, SEQ_SMEM, st>>>(static_cast<const bf16*>(beta), static_cast<const bf16*>(dout),
+                                              factors, dsT, ds0, dsw, T, H, err, tm[4], use_tma);
   rc = launch_status();
   if (rc != KDA_OK) return rc;
   const long long units = static_cast<long long>(B) * H * ((T + C - 1) / C);
@@ -972,7 +1042,8 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
       static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v),
       static_cast<const bf16*>(g), static_cast<const bf16*>(beta), static_cast<const Tc*>(s_ckpt),
       factors, dsw, static_cast<const bf16*>(dout), static_cast<bf16*>(dq), static_cast<bf16*>(dk_),
-      static_cast<bf16*>(dv_), static_cast<bf16*>(dg), static_cast<bf16*>(dbeta), B, T, H, err);
+      static_cast<bf16*>(dv_), static_cast<bf16*>(dg), static_cast<bf16*>(dbeta), B, T, H, err,
+      tm[0], tm[1], tm[2], tm[3], tm[4], use_tma);
   return launch_status();
 }
 

@@ -2,6 +2,7 @@
 // closed, before any launch) and dispatch to the kernels.
 #include <cuda_runtime.h>
 
+#include "kda_ckpt_layout.h"
 #include "kda_common.cuh"
 
 namespace kda {
@@ -13,7 +14,7 @@ int simt_fwd_launch(const void* q, const void* k, const void* v, const void* g, 
                     const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
                     int dk, int dv, int C, int in_dt, int o_dt, int ck_dt, cudaStream_t st);
 bool tc_fwd_supported(int dk, int dv, int C_, int in_dt);
-constexpr size_t kTcFactorBytes = 3 * 64 * 64 * 2;  // T, Aqk, Akk (bf16) per chunk-head
+constexpr size_t kTcFactorBytes = FAC_UNIT;  // factor block per chunk-head (kda_ckpt_layout.h)
 int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                   const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
                   int o_dt, int ck_dt, cudaStream_t st);

@@ -18,6 +18,8 @@
 //   MMA_3  : S <- Gam_C * S + (lam K)^T v~   (accumulated in TMEM)
 // The chunk-boundary state (bf16 or fp32) is written for the backward.
 #include "kda_chunk.cuh"
+#include "kda_ckpt_layout.h"
+#include "kda_tma.cuh"
 
 namespace kda {
 namespace {
@@ -62,12 +64,15 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
               const bf16* __restrict__ g, const bf16* __restrict__ beta,
               const float* __restrict__ s0, To* __restrict__ o, float* __restrict__ s_out,
               Tc* __restrict__ s_ckpt, unsigned char* __restrict__ factors, int T, int H,
-              int* __restrict__ err) {
+              int* __restrict__ err, const __grid_constant__ CUtensorMap tm_q,
+              const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_g,
+              const __grid_constant__ CUtensorMap tm_v, int use_tma) {
   extern __shared__ __align__(1024) unsigned char sm[];
   float* beta_s = reinterpret_cast<float*>(sm + OFF_BETA);
   float* gamC = reinterpret_cast<float*>(sm + OFF_GC);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
+  uint64_t* mbar_in = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 16);  // TMA: a chunk's q, k, g, v
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;  // TMEM lane quarter, column half
@@ -82,15 +87,36 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
 
   if (tid == 0) {
     mbar_init(mbar, 1);
+    mbar_init(mbar_in, 1);
     mbar_fence_init();
   }
   if (warp == 0) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
-  // stage chunk 0
-  stage_chunk(sm, qh, kh, gh, vh, tok0, min(C, T), H, true);
-  stage_chunk(sm, qh, kh, gh, vh, tok0, min(C, T), H, false);
+  // Staging of chunk cc's q, k, g (qkg) or v: TMA tiles completing on mbar_in
+  // (armed for all four tiles with the q, k, g issue), else cp.async.
+  auto stage = [&](int cc, bool qkg) {
+    if (!use_tma) {
+      stage_chunk(sm, qh, kh, gh, vh, tok0 + static_cast<size_t>(cc) * C, min(C, T - cc * C), H, qkg);
+      return;
+    }
+    if (tid != 0) return;
+    fence_async_smem();
+    if (qkg) {
+      mbar_expect_tx(mbar_in, 4 * 16384);
+      tma_tile(sm + OFF_SQ, &tm_q, h, cc, b, mbar_in);
+      tma_tile(sm + OFF_SK, &tm_k, h, cc, b, mbar_in);
+      tma_tile(sm + OFF_SG, &tm_g, h, cc, b, mbar_in);
+    } else {
+      tma_tile(sm + OFF_V, &tm_v, h, cc, b, mbar_in);
+    }
+  };
+  __syncthreads();  // mbar_in initialised
+  stage(0, true);
+  stage(0, false);
+  bool in_pending = use_tma != 0;  // TMA loads issued and not yet waited, for chunk parity in_par
+  uint32_t in_par = 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -131,14 +157,35 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     const int t0 = c * C;
     const int rows_valid = min(C, T - t0);
     cp_async_wait<0>();
+    if (use_tma) {
+      failed |= !mbar_wait(mbar_in, static_cast<uint32_t>(c) & 1u);
+      in_pending = false;
+    }
     if (tid == 0) bulk_wait_read();  // the previous state image in SB has been stored
     if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
-    __syncthreads();
+    if (__syncthreads_or(failed)) break;
 
     KDA_PT(0, 0);
     // ---------------- prep: G, exponentials, operand tiles ----------------
     float* Aq = reinterpret_cast<float*>(sm + OFF_SB);
     float* Akk = Aq + 4096;
+    // the factor block of this chunk-head in the checkpoint (null when not training)
+    unsigned char* fu = factors ? factors + ((static_cast<size_t>(b) * H + h) * n_chunks + c) * FAC_UNIT
+                                : nullptr;
+    // prep's operand images (Q Gam, K Gam, K Gam^-1, lam K) and Gam_C go to the
+    // checkpoint with bulk copies; their shared sources stay untouched until the
+    // solve (KI) and E2 (Q Gam), before which the copies are waited for
+    // (two bulk groups: K Gam^-1 alone, which the solve overwrites first, then the rest)
+    auto store_prep = [&](bool slow_chunk) {
+      if (!fu) return;
+      if (!slow_chunk) bulk_store(fu + FAC_KI, sm + OFF_KI, 16384);
+      bulk_commit();
+      bulk_store(fu + FAC_QG, A3 + cm_off(64, 0, DK), 2 * 16384);  // Q Gam, K Gam (adjacent)
+      bulk_store(fu + FAC_KL, sm + OFF_KL, 16384);
+      bulk_store(fu + FAC_GC, gamC, 512);
+      bulk_commit();
+      *reinterpret_cast<uint32_t*>(fu + FAC_FLAG) = slow_chunk ? 1u : 0u;
+    };
     {
       float G[4][8];
       const bool slow = prep(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, A3 + cm_off(64, 0, DK),
@@ -155,9 +202,14 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
             mma_bf16(T_D, desc_kmajor(a3_addr + 64 * 256 + ks * 256, DK),
                      desc_kmajor(smem_u32(sm + OFF_KI) + ks * 256, DK), idesc, ks > 0);
           mma_commit(mbar);
+          store_prep(false);
         }
         // prefetch the next chunk's q, k, g (staging is free)
-        if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, true);
+        if (c + 1 < n_chunks) {
+          stage(c + 1, true);
+          in_pending = use_tma != 0;
+          in_par = static_cast<uint32_t>(c + 1) & 1u;
+        }
         failed |= !mma_wait();
         if (__syncthreads_or(failed)) break;
         KDA_PT(0, 2);
@@ -167,15 +219,22 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         // exact scores on the CUDA cores (strong decay: the single anchor would overflow)
         float* Gf = reinterpret_cast<float*>(sm + OFF_KI);  // [64][128] fp32 across KI|TP
         store_G(Gf, G);
+        fence_async_smem();
         __syncthreads();
+        if (tid == 0) store_prep(true);
         scores_exact(sm + OFF_SQ, sm + OFF_SK, Gf, Aq, Akk);
         __syncthreads();
-        if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, true);
+        if (c + 1 < n_chunks) {
+          stage(c + 1, true);
+          in_pending = use_tma != 0;
+          in_par = static_cast<uint32_t>(c + 1) & 1u;
+        }
       }
     }
     // ---------------- solve: T = (I + L)^-1, then P = Aqk T on the tensor cores ----------------
     {
       float* Tm = reinterpret_cast<float*>(sm + OFF_KI);
+      if (tid == 0) bulk_wait_read<1>();  // KI has been stored and may be overwritten
       __syncthreads();
       KDA_PT(0, 12);
       solve_T(Akk, beta_s, Tm, reinterpret_cast<float*>(sm + OFF_VT));
@@ -196,11 +255,10 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         mma_bf16(T_P, desc_kmajor(aqb + ks * 256, C), desc_mnmajor(tb + ks * 2048, C), idesc, ks > 0);
       mma_commit(mbar);
     }
-    if (factors) {  // T, Aqk, Akk (bf16 CM tiles) into the checkpoint for the backward
-      unsigned char* fu = factors + ((static_cast<size_t>(b) * H + h) * n_chunks + c) * 24576;
+    if (fu) {  // T, Aqk, Akk (bf16 CM tiles) into the checkpoint for the backward
       for (int i = tid; i < 1024; i += NT)
-        *reinterpret_cast<uint4*>(fu + 16 * i) = *reinterpret_cast<const uint4*>(sm + OFF_VT + 16 * i);
-      row16_to_cm(fu + 16384, tid >> 2, Akk, tid >> 2, (tid & 3) * 16, nullptr);
+        *reinterpret_cast<uint4*>(fu + FAC_T + 16 * i) = *reinterpret_cast<const uint4*>(sm + OFF_VT + 16 * i);
+      row16_to_cm(fu + FAC_AK, tid >> 2, Akk, tid >> 2, (tid & 3) * 16, nullptr);
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
@@ -233,8 +291,9 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       mma_commit(mbar);
     }
     failed |= !mma_wait();
+    if (tid == 0) bulk_wait_read();  // Q Gam has been stored: E2 overwrites it with Q~
     if (__syncthreads_or(failed)) break;
-    if (c + 1 < n_chunks) stage_chunk(sm, qh, kh, gh, vh, tok0 + t0 + C, min(C, T - t0 - C), H, false);
+    if (c + 1 < n_chunks) stage(c + 1, false);
     KDA_PT(0, 6);
     // ---------------- E2: W -> A3[0:64), Q~ = Gam Q - Aqk W -> A3[64:128) ----------------
     {
@@ -360,6 +419,8 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   }
   if (failed && tid == 0 && err) atomicExch(err, 1);
   cp_async_wait<0>();
+  // an abandoned chunk may leave tile loads in flight: wait (bounded) for them
+  if (in_pending) mbar_wait(mbar_in, in_par);
   if (tid == 0) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
@@ -385,10 +446,16 @@ int launch_t(const void* q, const void* k, const void* v, const void* g, const v
     const size_t n = (static_cast<size_t>(T) + C - 1) / C;
     factors = static_cast<unsigned char*>(s_ckpt) + static_cast<size_t>(B) * H * n * DK * DV * sizeof(Tc);
   }
+  // TMA tile maps of q, k, g, v; a length or map the encoder refuses falls back
+  // to cp.async staging inside the kernel
+  CUtensorMap tm[4] = {};
+  const void* srcs[4] = {q, k, g, v};
+  int use_tma = 1;
+  for (int i = 0; i < 4 && use_tma; ++i) use_tma = make_tile_map(&tm[i], srcs[i], B, T, H) ? 1 : 0;
   kern<<<B * H, NT, SMEM_BYTES, st>>>(
       static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v),
       static_cast<const bf16*>(g), static_cast<const bf16*>(beta), s0, static_cast<To*>(o), s_out,
-      static_cast<Tc*>(s_ckpt), factors, T, H, err);
+      static_cast<Tc*>(s_ckpt), factors, T, H, err, tm[0], tm[1], tm[2], tm[3], use_tma);
   return launch_status();
 }
 

@@ -89,6 +89,33 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
       :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
+// One MMA of a precomputed issue table (32 bytes, in shared memory).  A kernel
+// builds its table once; every MMA group is then issued by the same short loop,
+// which stays in the instruction cache (an unrolled issue block per group runs
+// once per work unit, cold, and costs about twice the tensor time).
+struct MmaOp {
+  uint64_t a, b;      // shared-memory descriptors
+  uint32_t d, id;     // TMEM accumulator address, instruction descriptor
+  uint32_t acc, pad;  // accumulate into d (else overwrite)
+};
+__device__ __forceinline__ void mma_op(MmaOp* t, int i, uint32_t d, uint64_t a, uint64_t b,
+                                       uint32_t id, uint32_t acc) {
+  t[i].a = a;
+  t[i].b = b;
+  t[i].d = d;
+  t[i].id = id;
+  t[i].acc = acc;
+  t[i].pad = 0;
+}
+// Issues table entries [i0, i0 + n); one thread.
+__device__ __forceinline__ void mma_run(const MmaOp* t, int i0, int n) {
+#pragma unroll 2
+  for (int i = i0; i < i0 + n; ++i) {
+    const MmaOp op = t[i];
+    mma_bf16(op.d, op.a, op.b, op.id, op.acc);
+  }
+}
+
 // Arrive on an mbarrier once all previously issued MMAs of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* mbar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
@@ -229,8 +256,11 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
                :: "l"(dst), "r"(smem_u32(src)), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// The shared source of every committed bulk store may be overwritten.
-__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// The shared source of every committed bulk store but the newest N may be overwritten.
+template <int N = 0>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory");
+}
 // Every committed bulk store has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
@@ -265,7 +295,7 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
 // 0's table to g_kda_phase[k] at the kernel's converged exit.
 #ifdef KDA_PHASE_TIMERS
 #define KDA_PT_INIT()                                                       \
-  __shared__ unsigned long long kda_pt_sm_[8][32];                          \
+  __shared__ unsigned int kda_pt_sm_[8][32];                          \
   for (int i_ = threadIdx.x; i_ < 256; i_ += blockDim.x) kda_pt_sm_[i_ >> 5][i_ & 31] = 0; \
   __syncthreads();                                                          \
   long long kda_pt_prev_ = clock64()
@@ -273,7 +303,7 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
   do {                                                                      \
     const long long kda_pt_now_ = clock64();                                \
     if ((threadIdx.x & 31) == 0)                                            \
-      kda_pt_sm_[threadIdx.x >> 5][i] += static_cast<unsigned long long>(kda_pt_now_ - kda_pt_prev_); \
+      kda_pt_sm_[threadIdx.x >> 5][i] += static_cast<unsigned int>(kda_pt_now_ - kda_pt_prev_); \
     kda_pt_prev_ = kda_pt_now_;                                             \
   } while (0)
 #define KDA_PT_FLUSH(k)                                                     \
