@@ -104,14 +104,14 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
   tc_fence_after();
   // Issues every load of chunk cc into its operand set (after the set's last
   // reader has finished); the beta of chunk cc goes to a register.
-  float beta_nx = 0.f;
+  unsigned short beta_nx = 0;  // raw bf16 of the next chunk's beta (prefetch)
   auto issue_chunk = [&](int cc) {
     const int ps = cc & 1, t0 = cc * C, rv = min(C, T - t0);
     if (!use_tma) {
       stage_tile(sm + set_do(ps), doh + (tok0 + t0) * rstride, rv, rstride);
       cp_async_commit();
     }
-    if (tid == 0) {
+    if (tid == kIoThread) {
       const unsigned char* fu = factors + (unit * n_chunks + cc) * FAC_UNIT;
       fence_async_smem();
       mbar_expect_tx(mbar_ld + ps, 32768 + 16384 + 16384 + 512 + (use_tma ? 16384 : 0));
@@ -122,7 +122,7 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
       if (use_tma) tma_tile(sm + set_do(ps), &tm_do, h, cc, b, mbar_ld + ps);
     }
     ld_pending |= 1u << ps;
-    beta_nx = tid < rv ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
+    beta_nx = ld_bf16_raw(beta + (tok0 + t0 + tid) * H + h, tid < rv);
   };
   issue_chunk(n_chunks - 1);
   const uint32_t tbase = *tslot;
@@ -156,8 +156,8 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     failed |= !mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
     ld_par ^= 1u << p;
     ld_pending &= ~(1u << p);
-    if (tid == 0) bulk_wait_read();  // SB may be rewritten: the previous dS' image is stored
-    if (tid < C) beta_s[tid] = beta_nx;
+    if (tid == kIoThread) bulk_wait_read();  // SB may be rewritten: the previous dS' image is stored
+    if (tid < C) beta_s[tid] = bf16_raw_to_float(beta_nx);
     if (__syncthreads_or(failed)) break;
     KDA_PT(1, 0);
     const float* gamC = reinterpret_cast<const float*>(sm + set_gc(p));
@@ -230,11 +230,12 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     tc_fence_before();
     __syncthreads();
     // dU^T = dS'^T (lam K)^T + dO^T Aqk
-    if (tid == 0) {
-      // the workspace entry of chunk c is the dS' operand image (one bulk copy)
+    if (tid == kIoThread) {  // the workspace entry of chunk c is the dS' operand image
       bulk_store(reinterpret_cast<unsigned char*>(dsw) + (unit * n_chunks + c) * WS_UNIT, sm + Q_SB,
                  WS_UNIT);
       bulk_commit();
+    }
+    if (tid == 0) {
       tc_fence_after();
       const uint32_t sb = smem_u32(sm + Q_SB);
       const uint32_t id1 = idesc_bf16(128, 64, true, false), id2 = idesc_bf16(128, 64, true, true);
@@ -292,7 +293,7 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
   // a chunk abandoned on a timeout may leave loads in flight: wait (bounded)
   for (int ps = 0; ps < 2; ++ps)
     if ((ld_pending >> ps) & 1u) mbar_wait(mbar_ld + ps, (ld_par >> ps) & 1u);
-  if (tid == 0) bulk_wait_all();
+  if (tid == kIoThread) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -477,7 +478,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   int it = 0;                                      // units processed by this CTA
   bool fac_pending = false, late_pending = false, rs_pending = false;  // issued, not yet waited
   uint32_t fac_par = 0, late_par = 0, rs_par = 0;
-  auto issue_inputs = [&](long long uu, float& beta_nx) {
+  auto issue_inputs = [&](long long uu, unsigned short& beta_nx) {
     const int cc = static_cast<int>(uu % n_chunks);
     const long long bhn = uu / n_chunks;
     const int hn = static_cast<int>(bhn % H), bn = static_cast<int>(bhn / H);
@@ -488,7 +489,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       stage_tile(sm + P_V, v + src, rv, rstride);
       cp_async_commit();
     }
-    if (tid == 0) {
+    if (tid == kIoThread) {
       const unsigned char* fu = factors + ((static_cast<size_t>(bn) * H + hn) * n_chunks + cc) * FAC_UNIT;
       const int gf = P_GF + 544 * ((uu == blockIdx.x ? it : it + 1) & 1);
       fence_async_smem();
@@ -501,9 +502,9 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     fac_pending = true;
     fac_par = static_cast<uint32_t>(uu == blockIdx.x ? it : it + 1) & 1u;
-    beta_nx = tid < rv ? __bfloat162float(beta[(tk + tid) * H + hn]) : 0.f;
+    beta_nx = ld_bf16_raw(beta + (tk + tid) * H + hn, tid < rv);
   };
-  float beta_nx = 0.f;
+  unsigned short beta_nx = 0;  // raw bf16 of the next unit's beta (prefetch)
   if (blockIdx.x < n_units) issue_inputs(blockIdx.x, beta_nx);
 
   KDA_PT_INIT();
@@ -524,7 +525,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       stage_tile(sm + P_SQ, dout + hoff + tok0 * rstride, rows_valid, rstride);
       cp_async_commit();
     }
-    if (tid == 0) {
+    if (tid == kIoThread) {
       constexpr uint32_t late_bytes = WS_UNIT + (sizeof(Tc) == 2 ? DK * DV * 2 : 0);
       fence_async_smem();
       mbar_expect_tx(mbar_late, late_bytes + (use_tma ? 16384 : 0));
@@ -534,7 +535,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     late_pending = true;
     late_par = static_cast<uint32_t>(it) & 1u;
-    if (tid < C) beta_s[tid] = beta_nx;
+    if (tid < C) beta_s[tid] = bf16_raw_to_float(beta_nx);
     if (tid < 128) dgc[tid] = 0.f;
     if (tid < 64) dbs[tid] = 0.f;
     KDA_PT(2, 26);
@@ -650,7 +651,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     KDA_PT(2, 7);
     // dS' is dead: restage g (for the epilogue) over its upper half
     if (use_tma) {
-      if (tid == 0) {
+      if (tid == kIoThread) {
         fence_async_smem();
         mbar_expect_tx(mbar_rs, slow ? 4 * 16384 : 2 * 16384);  // + v (and q, k) below
         tma_tile(sm + P_SG, &tm_g, h, c, b, mbar_rs);
@@ -740,7 +741,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     KDA_PT(2, 13);
     // U, dO and dW^T are dead: restage v (and raw q, k for the exact path)
     if (use_tma) {
-      if (tid == 0) {
+      if (tid == kIoThread) {
         fence_async_smem();
         tma_tile(sm + P_V, &tm_v, h, c, b, mbar_rs);
         if (slow) {

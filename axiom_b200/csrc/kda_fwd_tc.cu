@@ -101,7 +101,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       stage_chunk(sm, qh, kh, gh, vh, tok0 + static_cast<size_t>(cc) * C, min(C, T - cc * C), H, qkg);
       return;
     }
-    if (tid != 0) return;
+    if (tid != kIoThread) return;
     fence_async_smem();
     if (qkg) {
       mbar_expect_tx(mbar_in, 4 * 16384);
@@ -115,6 +115,8 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   __syncthreads();  // mbar_in initialised
   stage(0, true);
   stage(0, false);
+  // raw bf16 beta of the chunk to come, loaded one chunk ahead
+  unsigned short beta_nx = ld_bf16_raw(beta + tok0 * H + static_cast<size_t>(tid) * H + h, tid < min(C, T));
   bool in_pending = use_tma != 0;  // TMA loads issued and not yet waited, for chunk parity in_par
   uint32_t in_par = 0u;
   tc_fence_before();
@@ -161,8 +163,10 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       failed |= !mbar_wait(mbar_in, static_cast<uint32_t>(c) & 1u);
       in_pending = false;
     }
-    if (tid == 0) bulk_wait_read();  // the previous state image in SB has been stored
-    if (tid < C) beta_s[tid] = tid < rows_valid ? __bfloat162float(beta[(tok0 + t0 + tid) * H + h]) : 0.f;
+    if (tid == kIoThread) bulk_wait_read();  // the previous state image in SB has been stored
+    if (tid < C) beta_s[tid] = bf16_raw_to_float(beta_nx);
+    if (c + 1 < n_chunks)
+      beta_nx = ld_bf16_raw(beta + (tok0 + t0 + C + tid) * H + h, tid < min(C, T - t0 - C));
     if (__syncthreads_or(failed)) break;
 
     KDA_PT(0, 0);
@@ -202,8 +206,8 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
             mma_bf16(T_D, desc_kmajor(a3_addr + 64 * 256 + ks * 256, DK),
                      desc_kmajor(smem_u32(sm + OFF_KI) + ks * 256, DK), idesc, ks > 0);
           mma_commit(mbar);
-          store_prep(false);
         }
+        if (tid == kIoThread) store_prep(false);
         // prefetch the next chunk's q, k, g (staging is free)
         if (c + 1 < n_chunks) {
           stage(c + 1, true);
@@ -221,7 +225,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         store_G(Gf, G);
         fence_async_smem();
         __syncthreads();
-        if (tid == 0) store_prep(true);
+        if (tid == kIoThread) store_prep(true);
         scores_exact(sm + OFF_SQ, sm + OFF_SK, Gf, Aq, Akk);
         __syncthreads();
         if (c + 1 < n_chunks) {
@@ -234,7 +238,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     // ---------------- solve: T = (I + L)^-1, then P = Aqk T on the tensor cores ----------------
     {
       float* Tm = reinterpret_cast<float*>(sm + OFF_KI);
-      if (tid == 0) bulk_wait_read<1>();  // KI has been stored and may be overwritten
+      if (tid == kIoThread) bulk_wait_read<1>();  // KI has been stored and may be overwritten
       __syncthreads();
       KDA_PT(0, 12);
       solve_T(Akk, beta_s, Tm, reinterpret_cast<float*>(sm + OFF_VT));
@@ -291,7 +295,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       mma_commit(mbar);
     }
     failed |= !mma_wait();
-    if (tid == 0) bulk_wait_read();  // Q Gam has been stored: E2 overwrites it with Q~
+    if (tid == kIoThread) bulk_wait_read();  // Q Gam has been stored: E2 overwrites it with Q~
     if (__syncthreads_or(failed)) break;
     if (c + 1 < n_chunks) stage(c + 1, false);
     KDA_PT(0, 6);
@@ -347,11 +351,11 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     __syncthreads();
     KDA_PT(0, 8);
     // ---------------- MMA_1: [W ; Q~] S ----------------
+    if (tid == kIoThread && sizeof(Tc) == 2 && ck_unit) {
+      bulk_store(ck_unit, sm + OFF_SB, DK * DV * 2);
+      bulk_commit();
+    }
     if (tid == 0) {
-      if (sizeof(Tc) == 2 && ck_unit) {
-        bulk_store(ck_unit, sm + OFF_SB, DK * DV * 2);
-        bulk_commit();
-      }
       tc_fence_after();
       const uint32_t idesc = idesc_bf16(128, 128, false, true);
       const uint32_t sb = smem_u32(sm + OFF_SB);
@@ -421,7 +425,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   cp_async_wait<0>();
   // an abandoned chunk may leave tile loads in flight: wait (bounded) for them
   if (in_pending) mbar_wait(mbar_in, in_par);
-  if (tid == 0) bulk_wait_all();
+  if (tid == kIoThread) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

@@ -238,6 +238,10 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
 // ---- bulk copies (cp.async.bulk, contiguous, no tensor map) --------------------
+// Copies (bulk and TMA) are issued by this thread, lane 0 of warp 1, so that
+// they never queue behind thread 0's MMA issue (and the other way round).  The
+// bulk async-group waits are per thread and are made by it too.
+constexpr int kIoThread = 32;
 // Issued by one thread.  Both addresses 16-byte aligned, size a multiple of 16.
 // Arms `mbar` for one arrival plus `bytes` transaction bytes.
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
@@ -263,6 +267,17 @@ __device__ __forceinline__ void bulk_wait_read() {
 }
 // Every committed bulk store has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Raw bf16 load kept as 16 bits: the value is converted where it is consumed,
+// so no instruction waits on the load right after issuing it (a prefetch).
+__device__ __forceinline__ unsigned short ld_bf16_raw(const __nv_bfloat16* p, bool valid) {
+  unsigned short v = 0;
+  if (valid) v = *reinterpret_cast<const unsigned short*>(p);
+  return v;
+}
+__device__ __forceinline__ float bf16_raw_to_float(unsigned short v) {
+  return __uint_as_float(static_cast<uint32_t>(v) << 16);
+}
 
 // ---- bf16 packing ---------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
