@@ -39,6 +39,14 @@ CFG4 = dict(N=256 * 32, dk=128, dv=128)
 # backward adjoint 23.07 MFLOP (recompute excluded).
 FWD_FLOP_PER_CHUNK_HEAD = 11.62e6
 BWD_FLOP_PER_CHUNK_HEAD = 23.07e6
+# DRAM traffic per chunk-head (dram__bytes_read.sum + dram__bytes_write.sum from one
+# ncu capture per kernel of the reduced case B=1, T=8192, H=16 = 2,048 chunk-heads,
+# summarised in profiles/kda_kernels_small_case.md); a launch's traffic grows in
+# proportion to the chunk-heads it processes, so roofline.traffic = this x units.
+TRAFFIC_PER_CHUNK_HEAD = {
+    "kda_fwd": (134.711040e6 + 238.693376e6) / 2048,
+    "kda_bwd": (169.267456e6 + 44.406528e6 + 421.580544e6 + 111.635200e6) / 2048,  # bwd_seq + bwd_par
+}
 
 
 def _peaks():
@@ -323,7 +331,10 @@ def run_b200(args):
             "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": peaks["source"] + (" sustained" if peak == peaks["bf16_sustained"] else " burst"),
-                         "traffic": None},
+                         "traffic": TRAFFIC_PER_CHUNK_HEAD[dom] * units,
+                         "traffic_unit": "bytes per launch (ncu DRAM bytes per chunk-head x units)",
+                         "traffic_GBps": TRAFFIC_PER_CHUNK_HEAD[dom] * units / (dom_ms / 1e3) / 1e9,
+                         "hbm_peak_GBps": peaks["hbm"]},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "steps": e2e.get("steps"),
                     "overlap": e2e.get("overlap")},
