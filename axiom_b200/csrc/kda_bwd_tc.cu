@@ -339,6 +339,30 @@ static_assert(P_AQB - P_TB == static_cast<int>(FAC_AQ) && P_AKB - P_TB == static
                   P_KL - P_KI == static_cast<int>(FAC_KL - FAC_KI) && FAC_KL == FAC_KI + 16384,
               "factor staging layout");
 
+// Channel-major [128][64] CM tile (rows = channels, cols = tokens) -> [64][128]
+// token rows of 256 bytes whose 16-byte chunk j sits at position j ^ (row & 7)
+// (the XOR keeps the transposing stmatrix writes conflict-free).
+__device__ __forceinline__ void transpose_to_rows(uint32_t dst, uint32_t src, int warp, int lane) {
+  for (int j0 = 4 * warp; j0 < 128; j0 += 4 * (NT / 32)) {
+    const int j = j0 + (lane >> 3), row = lane & 7;
+    const int rg = j >> 3, cg = j & 7;  // channel block, token block
+    uint32_t f[4];
+    ldmatrix_x4(f, src + ((rg * 8 + cg) << 7) + (row << 4));
+    const int c = 8 * cg + row;  // token row this lane addresses
+    stmatrix_x4_trans(dst + (c << 8) + ((rg ^ (c & 7)) << 4), f);
+  }
+}
+// Token rows written by transpose_to_rows -> global rows (row r at dst + r*rstride),
+// 16 bytes per thread and store, rows >= rows_valid skipped.
+__device__ __forceinline__ void store_rows(bf16* dst, const unsigned char* rows, int rows_valid,
+                                           size_t rstride) {
+  for (int i = threadIdx.x; i < 64 * 16; i += NT) {
+    const int r = i >> 4, j = i & 15;
+    if (r < rows_valid)
+      *reinterpret_cast<uint4*>(dst + r * rstride + j * 8) = ld16(rows, (r << 8) + ((j ^ (r & 7)) << 4));
+  }
+}
+
 // fp32 checkpoint state (row-major) -> bf16 CM operand tile.
 __device__ __forceinline__ void stage_ckpt_f32(unsigned char* dst, const float* src) {
   for (int i = threadIdx.x; i < 128 * 16; i += NT) {
@@ -857,6 +881,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         for (int qq = 0; qq < 4; ++qq) {
           const int c8 = cb + 8 * qq;
           float dqg[8], dkg[8], dki[8], dkl[8], yw[8], yu[8], qg[8], kg[8], ki[8], vv[8];
+          float oq[8], ok[8], ov[8];
           tmem_ld8(T_IV + tl + c8, dqg);
           tmem_ld8(T_IV + 64 + tl + c8, dkg);
           tmem_ld8(T_SC + tl + c8, dki);
@@ -877,10 +902,23 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
             dG[8 * qq + i] = dqg[i] * qg[i] + dkg[i] * kg[i] - s2 * ki[i];
             klsum += gC * dkl[i] * ki[i];
             TR[d * 64 + (cc ^ (d & 63))] = yw[i] * kg[i] + yu[i] * vv[i];
-            if (cc < rows_valid) {
-              dq[gbase + cc * rstride] = __float2bfloat16_rn(dqg[i] * gam);
-              dk[gbase + cc * rstride] = __float2bfloat16_rn(dkg[i] * gam + s2 * gi);
-              dv[gbase + cc * rstride] = __float2bfloat16_rn(beta_s[cc] * yu[i]);
+            oq[i] = dqg[i] * gam;
+            ok[i] = dkg[i] * gam + s2 * gi;
+            ov[i] = beta_s[cc] * yu[i];
+          }
+          if (use_tma) {  // channel-major, over the tiles just read (stored below)
+            st16(sm + P_TP, cm_off(d, c8, C), pack_bf16x8(oq));
+            st16(A3, cm_off(d, c8, C), pack_bf16x8(ok));
+            st16(sm + P_SK, cm_off(d, c8, C), pack_bf16x8(ov));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int cc = c8 + i;
+              if (cc < rows_valid) {
+                dq[gbase + cc * rstride] = __float2bfloat16_rn(oq[i]);
+                dk[gbase + cc * rstride] = __float2bfloat16_rn(ok[i]);
+                dv[gbase + cc * rstride] = __float2bfloat16_rn(ov[i]);
+              }
             }
           }
         }
@@ -967,12 +1005,37 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       KDA_PT(2, 17);
       const float dGC = xch[(1 * 2 + 0) * 128 + d] + xch[(1 * 2 + 1) * 128 + d] + gC * dgc[d];
       float acc = dGC + (hh == 0 ? xch[(0 * 2 + 1) * 128 + d] : 0.f);
+      if (use_tma && !slow) {  // dg over g^T (consumed), channel-major
 #pragma unroll
-      for (int jj = 31; jj >= 0; --jj) {
-        acc += dG[jj];
-        const int cc = cb + jj;
-        if (cc < rows_valid) dg[gbase + cc * rstride] = __float2bfloat16_rn(acc);
+        for (int jj = 31; jj >= 0; --jj) {
+          acc += dG[jj];
+          dG[jj] = acc;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) st16(sm + P_SQ, cm_off(d, cb + 8 * j, C), pack_bf16x8(dG + 8 * j));
+      } else {
+#pragma unroll
+        for (int jj = 31; jj >= 0; --jj) {
+          acc += dG[jj];
+          const int cc = cb + jj;
+          if (cc < rows_valid) dg[gbase + cc * rstride] = __float2bfloat16_rn(acc);
+        }
       }
+    }
+    if (use_tma && !slow) {
+      // dq, dk, dv, dg: channel-major tiles -> token rows (swizzled) -> 16-byte stores
+      __syncthreads();
+      transpose_to_rows(smem_u32(sm + P_SG), smem_u32(sm + P_TP), warp, lane);         // dq
+      transpose_to_rows(smem_u32(sm + P_SB), a3, warp, lane);                          // dk
+      transpose_to_rows(smem_u32(sm + P_SB + 16384), smem_u32(sm + P_SK), warp, lane);  // dv
+      __syncthreads();
+      transpose_to_rows(smem_u32(sm + P_TP), smem_u32(sm + P_SQ), warp, lane);         // dg
+      const size_t obase = hoff + tok0 * rstride;
+      store_rows(dq + obase, sm + P_SG, rows_valid, rstride);
+      store_rows(dk + obase, sm + P_SB, rows_valid, rstride);
+      store_rows(dv + obase, sm + P_SB + 16384, rows_valid, rstride);
+      __syncthreads();
+      store_rows(dg + obase, sm + P_TP, rows_valid, rstride);
     }
     KDA_PT(2, 18);
     tc_fence_before();
