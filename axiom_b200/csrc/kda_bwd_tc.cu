@@ -323,13 +323,19 @@ constexpr int P_DB = P_DGC + 512;        // dbeta accum fp32[64]
 constexpr int P_XCH = P_DB + 256;        // half-exchange fp32[2][2][128]
 constexpr int P_BAR = P_XCH + 2048;
 constexpr int P_MMA = P_BAR + 64;         // MMA issue table (MmaOp[96])
-// issue-table groups: first entry, count
+// Issue-table groups (first entry, count).  A group's critical MMAs are
+// committed before its filler MMAs: the tensor core runs in issue order, so the
+// filler (needed only later) executes while the threads work on the critical
+// results, and the next group's commit implies it has completed.
 constexpr int G_WU = 0, N_WU = 8;         // W, U
 constexpr int G_WS = 8, N_WS = 8;         // W S_c
-constexpr int G_DU = 16, N_DU = 20;       // dU^T, dKL^T
-constexpr int G_SD = 36, N_SD = 16;       // S_c [dO^T | dU^T]
-constexpr int G_Y = 52, N_Y = 8;          // Yw^T, Yu^T
-constexpr int G_DA = 60, N_DA = 24;       // dAqk, dL
+constexpr int G_DU = 16, N_DU = 12;       // dU^T               | filler: dKL^T
+constexpr int F_DU = 28, NF_DU = 8;
+constexpr int G_SD = 36, N_SD = 8;        // (dU S_c^T)^T       | filler: Yu^T, (dO S_c^T)^T
+constexpr int F_SD = 44, NF_SD = 12;
+constexpr int G_YW = 56, N_YW = 4;        // Yw^T               | filler: dAqk
+constexpr int F_YW = 60, NF_YW = 8;
+constexpr int G_DL = 68, N_DL = 16;       // dL
 constexpr int G_VII = 84, N_VII = 12;     // [dQG^T | dKG^T] +=, dKI^T
 constexpr int PAR_SMEM = P_MMA + 96 * 32;
 // the checkpoint's adjacent tiles land with one bulk copy each: [T, Aqk, Akk] in
@@ -451,7 +457,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     for (int ks = 0; ks < DK / 16; ++ks)  // W S_c   (M = 64)
       mma_op(tab, n++, T_WS, desc_kmajor(a3 + ks * 256, DK), desc_mnmajor(sb + ks * 4096, DV),
              idesc_bf16(64, 128, false, true), ks > 0);
-    // dU^T = dS'^T (lam K)^T + dO^T Aqk ;  dKL^T = dS' v~^T
+    // G_DU: dU^T = dS'^T (lam K)^T + dO^T Aqk | F_DU: dKL^T = dS' v~^T
     for (int ks = 0; ks < DK / 16; ++ks)
       mma_op(tab, n++, T_DU, desc_mnmajor(dsp + ks * 4096, DV), desc_kmajor(kl + ks * 256, DK),
              idesc_bf16(128, 64, true, false), ks > 0);
@@ -461,21 +467,24 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     for (int ks = 0; ks < DV / 16; ++ks)
       mma_op(tab, n++, T_KL, desc_kmajor(dsp + ks * 256, DV), desc_kmajor(tp + ks * 256, DV),
              idesc_bf16(128, 64, false, false), ks > 0);
-    for (int ks = 0; ks < DV / 16; ++ks) {  // S_c [dO^T | dU^T]
-      const uint64_t ad = desc_kmajor(sb + ks * 256, DV);
-      mma_op(tab, n++, T_IV, ad, desc_kmajor(dob + ks * 256, DV), idesc_bf16(128, 64, false, false), ks > 0);
-      mma_op(tab, n++, T_IV + 64, ad, desc_mnmajor(kl + ks * 2048, C), idesc_bf16(128, 64, false, true), ks > 0);
-    }
-    for (int ks = 0; ks < C / 16; ++ks) {  // Yw^T = dW^T T,  Yu^T = dU^T T
-      const uint64_t bd = desc_mnmajor(tb + ks * 2048, C);
-      const uint32_t id = idesc_bf16(128, 64, false, true);
-      mma_op(tab, n++, T_UF, desc_kmajor(dsp + ks * 256, C), bd, id, ks > 0);
-      mma_op(tab, n++, T_UF + 64, desc_kmajor(kl + ks * 256, C), bd, id, ks > 0);
-    }
-    // dAqk = dO v~^T, dL~ = Yu U^T + Yw W^T   (M = 64)
+    // G_SD: (dU S_c^T)^T = S_c dU^T | F_SD: Yu^T = dU^T T, (dO S_c^T)^T = S_c dO^T
+    for (int ks = 0; ks < DV / 16; ++ks)
+      mma_op(tab, n++, T_IV + 64, desc_kmajor(sb + ks * 256, DV), desc_mnmajor(kl + ks * 2048, C),
+             idesc_bf16(128, 64, false, true), ks > 0);
+    for (int ks = 0; ks < C / 16; ++ks)
+      mma_op(tab, n++, T_UF + 64, desc_kmajor(kl + ks * 256, C), desc_mnmajor(tb + ks * 2048, C),
+             idesc_bf16(128, 64, false, true), ks > 0);
+    for (int ks = 0; ks < DV / 16; ++ks)
+      mma_op(tab, n++, T_IV, desc_kmajor(sb + ks * 256, DV), desc_kmajor(dob + ks * 256, DV),
+             idesc_bf16(128, 64, false, false), ks > 0);
+    // G_YW: Yw^T = dW^T T | F_YW: dAqk = dO v~^T   (M = 64)
+    for (int ks = 0; ks < C / 16; ++ks)
+      mma_op(tab, n++, T_UF, desc_kmajor(dsp + ks * 256, C), desc_mnmajor(tb + ks * 2048, C),
+             idesc_bf16(128, 64, false, true), ks > 0);
     for (int ks = 0; ks < DV / 16; ++ks)
       mma_op(tab, n++, T_SC, desc_kmajor(dob + ks * 256, DV), desc_kmajor(tp + ks * 256, DV),
              idesc_bf16(64, 64, false, false), ks > 0);
+    // G_DL: dL~ = Yu U^T + Yw W^T   (M = 64)
     for (int ks = 0; ks < DV / 16; ++ks)
       mma_op(tab, n++, T_L, desc_mnmajor(sb + 16384 + ks * 2048, C), desc_kmajor(vb + ks * 256, DV),
              idesc_bf16(64, 64, true, false), ks > 0);
@@ -667,25 +676,13 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       tc_fence_after();
       mma_run(tab, G_DU, N_DU);
       mma_commit(mbar);
+      mma_run(tab, F_DU, NF_DU);
       KDA_PT(2, 20);
     }
     failed |= !mma_wait();
     KDA_PT(2, 21);
     if (__syncthreads_or(failed)) break;
     KDA_PT(2, 7);
-    // dS' is dead: restage g (for the epilogue) over its upper half
-    if (use_tma) {
-      if (tid == kIoThread) {
-        fence_async_smem();
-        mbar_expect_tx(mbar_rs, slow ? 4 * 16384 : 2 * 16384);  // + v (and q, k) below
-        tma_tile(sm + P_SG, &tm_g, h, c, b, mbar_rs);
-      }
-      rs_pending = true;
-      rs_par = static_cast<uint32_t>(it) & 1u;
-    } else {
-      stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
-      cp_async_commit();
-    }
     {  // dU^T -> bf16 [j][c] (KL region)
       const int j = 32 * qw + lane;
       float vals[32];
@@ -703,12 +700,27 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       tc_fence_after();
       mma_run(tab, G_SD, N_SD);
       mma_commit(mbar);
+      mma_run(tab, F_SD, NF_SD);
       KDA_PT(2, 22);
     }
     failed |= !mma_wait();
     KDA_PT(2, 23);
     if (__syncthreads_or(failed)) break;
     KDA_PT(2, 9);
+    // dS' is dead (its last reader, the dKL^T filler, is done): restage g
+    // (for the epilogue) over its upper half
+    if (use_tma) {
+      if (tid == kIoThread) {
+        fence_async_smem();
+        mbar_expect_tx(mbar_rs, slow ? 4 * 16384 : 2 * 16384);  // + v (and q, k) below
+        tma_tile(sm + P_SG, &tm_g, h, c, b, mbar_rs);
+      }
+      rs_pending = true;
+      rs_par = static_cast<uint32_t>(it) & 1u;
+    } else {
+      stage_tile(sm + P_SG, g + hoff + tok0 * rstride, rows_valid, rstride);
+      cp_async_commit();
+    }
     {  // dW^T = -(dU S^T)^T -> bf16 [d][c] (SK region)
       const int d = 32 * qw + lane;
       float vals[32];
@@ -726,8 +738,9 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // Yw^T = dW^T T,  Yu^T = dU^T T
     if (tid == 0) {
       tc_fence_after();
-      mma_run(tab, G_Y, N_Y);
+      mma_run(tab, G_YW, N_YW);
       mma_commit(mbar);
+      mma_run(tab, F_YW, NF_YW);
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
@@ -755,7 +768,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     // dAqk = dO v~^T, dL~ = Yu U^T + Yw W^T   (M = 64)
     if (tid == 0) {
       tc_fence_after();
-      mma_run(tab, G_DA, N_DA);
+      mma_run(tab, G_DL, N_DL);
       mma_commit(mbar);
       KDA_PT(2, 24);
     }
