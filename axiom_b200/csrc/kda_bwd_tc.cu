@@ -48,18 +48,14 @@ constexpr size_t WS_UNIT = 32768;
 // bwd_seq
 // ===========================================================================
 // Chunk c works on operand set p = c & 1 while chunk c-1's set is loaded: the
-// forward's Q Gam, K Gam, lam K, Gam_C, T, Aqk (bulk copies from the
-// checkpoint) and dO (TMA tile, or cp.async).
-constexpr int Q_QG0 = 0, Q_KG0 = 16384, Q_KL0 = 32768, Q_DO0 = 49152;  // set 0
-constexpr int Q_A3 = 65536;              // [-W ; set 1: Q Gam ; K Gam] CM[192][128]
-constexpr int Q_QG1 = Q_A3 + 16384, Q_KG1 = Q_A3 + 32768;
-constexpr int Q_KL1 = Q_A3 + 49152;      // set 1 lam K
-constexpr int Q_TP = Q_KL1 + 16384;      // T beta [64][64] | dU^T [128][64]
+// forward's W, Q Gam, lam K, Aqk, Gam_C (bulk copies from the checkpoint) and
+// dO (TMA tile, or cp.async).  W, Q Gam are adjacent, in the set and in the
+// checkpoint.
+constexpr int Q_SET = 73728;             // bytes per operand set
+constexpr int Q_W = 0, Q_QG = 16384, Q_KL = 32768, Q_DO = 49152, Q_AQ = 65536;  // offsets in a set
+constexpr int Q_TP = 2 * Q_SET;          // -dU^T bf16 [128][64]
 constexpr int Q_SB = Q_TP + 16384;       // dS' bf16 [128][128] (also stored to the workspace)
-constexpr int Q_TA0 = Q_SB + 32768;      // set 0: T, Aqk bf16 [64][64] (adjacent, as in the checkpoint)
-constexpr int Q_TA1 = Q_TA0 + 16384;     // set 1
-constexpr int Q_DO1 = Q_TA1 + 16384;     // set 1 dO
-constexpr int Q_BETA = Q_DO1 + 16384;
+constexpr int Q_BETA = Q_SB + 32768;
 constexpr int Q_GC0 = Q_BETA + 256, Q_GC1 = Q_GC0 + 512;  // Gam_C per set
 constexpr int Q_BAR = Q_GC1 + 512;
 constexpr int SEQ_SMEM = Q_BAR + 64;
@@ -74,7 +70,6 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + Q_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + Q_BAR + 8);
   uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + Q_BAR + 16);  // [2]: one per operand set
-  unsigned char* A3 = sm + Q_A3;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;
   const int h = blockIdx.x % H, b = blockIdx.x / H;
@@ -83,12 +78,6 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
   const size_t rstride = static_cast<size_t>(H) * DK;
   const bf16* doh = dout + static_cast<size_t>(h) * DV;
   const size_t unit = static_cast<size_t>(b) * H + h;
-  // shared offsets of operand set ps
-  auto set_qg = [](int ps) { return ps ? Q_QG1 : Q_QG0; };
-  auto set_kg = [](int ps) { return ps ? Q_KG1 : Q_KG0; };
-  auto set_kl = [](int ps) { return ps ? Q_KL1 : Q_KL0; };
-  auto set_do = [](int ps) { return ps ? Q_DO1 : Q_DO0; };
-  auto set_ta = [](int ps) { return ps ? Q_TA1 : Q_TA0; };
   auto set_gc = [](int ps) { return ps ? Q_GC1 : Q_GC0; };
   uint32_t ld_par = 0u, ld_pending = 0u;  // bit ps: phase parity / loads in flight of set ps
 
@@ -107,26 +96,27 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
   unsigned short beta_nx = 0;  // raw bf16 of the next chunk's beta (prefetch)
   auto issue_chunk = [&](int cc) {
     const int ps = cc & 1, t0 = cc * C, rv = min(C, T - t0);
+    unsigned char* set = sm + ps * Q_SET;
     if (!use_tma) {
-      stage_tile(sm + set_do(ps), doh + (tok0 + t0) * rstride, rv, rstride);
+      stage_tile(set + Q_DO, doh + (tok0 + t0) * rstride, rv, rstride);
       cp_async_commit();
     }
     if (tid == kIoThread) {
       const unsigned char* fu = factors + (unit * n_chunks + cc) * FAC_UNIT;
       fence_async_smem();
-      mbar_expect_tx(mbar_ld + ps, 32768 + 16384 + 16384 + 512 + (use_tma ? 16384 : 0));
-      bulk_load(sm + set_qg(ps), fu + FAC_QG, 32768, mbar_ld + ps);  // Q Gam, K Gam
-      bulk_load(sm + set_kl(ps), fu + FAC_KL, 16384, mbar_ld + ps);
-      bulk_load(sm + set_ta(ps), fu + FAC_T, 16384, mbar_ld + ps);   // T, Aqk
+      mbar_expect_tx(mbar_ld + ps, 32768 + 16384 + 8192 + 512 + (use_tma ? 16384 : 0));
+      bulk_load(set + Q_W, fu + FAC_W, 32768, mbar_ld + ps);  // W, Q Gam
+      bulk_load(set + Q_KL, fu + FAC_KL, 16384, mbar_ld + ps);
+      bulk_load(set + Q_AQ, fu + FAC_AQ, 8192, mbar_ld + ps);
       bulk_load(sm + set_gc(ps), fu + FAC_GC, 512, mbar_ld + ps);
-      if (use_tma) tma_tile(sm + set_do(ps), &tm_do, h, cc, b, mbar_ld + ps);
+      if (use_tma) tma_tile(set + Q_DO, &tm_do, h, cc, b, mbar_ld + ps);
     }
     ld_pending |= 1u << ps;
     beta_nx = ld_bf16_raw(beta + (tok0 + t0 + tid) * H + h, tid < rv);
   };
   issue_chunk(n_chunks - 1);
   const uint32_t tbase = *tslot;
-  const uint32_t T_DS = tbase, T_W = tbase + 256, T_U = tbase + 384;
+  const uint32_t T_DS = tbase, T_U = tbase + 384;
   const uint32_t tl = lane_off(qw);
   uint32_t phase = 0;
   bool failed = false;
@@ -147,7 +137,6 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     }
     tmem_wait_st();
   }
-  const uint32_t a3 = smem_u32(A3);
 
   KDA_PT_INIT();
   for (int c = n_chunks - 1; c >= 0; --c) {
@@ -161,52 +150,9 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     if (__syncthreads_or(failed)) break;
     KDA_PT(1, 0);
     const float* gamC = reinterpret_cast<const float*>(sm + set_gc(p));
-    const uint32_t qg = smem_u32(sm + set_qg(p)), kg = smem_u32(sm + set_kg(p));
-    const uint32_t kl = smem_u32(sm + set_kl(p)), dob = smem_u32(sm + set_do(p));
-    const uint32_t aqb = smem_u32(sm + set_ta(p) + 8192);
+    const uint32_t set = smem_u32(sm + p * Q_SET);
     if (c > 0) issue_chunk(c - 1);  // the other set was last read by chunk c + 1
     KDA_PT(1, 1);
-    {  // T diag(beta) from the forward's bf16 T tile
-      const int r = tid >> 2, c0 = (tid & 3) * 16;
-      float tv[16];
-      unpack_bf16x8(ld16(sm + set_ta(p), cm_off(r, c0, C)), tv);
-      unpack_bf16x8(ld16(sm + set_ta(p), cm_off(r, c0 + 8, C)), tv + 8);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) tv[j] *= beta_s[c0 + j];
-      st16(sm + Q_TP, cm_off(r, c0, C), pack_bf16x8(tv));
-      st16(sm + Q_TP, cm_off(r, c0 + 8, C), pack_bf16x8(tv + 8));
-    }
-    KDA_PT(1, 2);
-    fence_async_smem();
-    __syncthreads();
-    // W = (T beta) (Gam K)   (M = 64: rows r at lanes 32(r/16) + r%16)
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t id = idesc_bf16(64, 128, false, true);
-      const uint32_t tp = smem_u32(sm + Q_TP);
-#pragma unroll 1
-      for (int ks = 0; ks < C / 16; ++ks)
-        mma_bf16(T_W, desc_kmajor(tp + ks * 256, C), desc_mnmajor(kg + ks * 4096, DK), id, ks > 0);
-      mma_commit(mbar);
-    }
-    failed |= !mma_wait();
-    if (__syncthreads_or(failed)) break;
-    KDA_PT(1, 3);
-    {  // -W -> A3 rows 0..63
-      const int r = 16 * qw + lane;
-      for (int half = 0; half < 2; ++half) {
-        const int c0 = hh * 64 + half * 32;
-        float vals[32];
-        tmem_ld32(T_W + tl + c0, vals);
-        tmem_wait_ld();
-        if (lane < 16) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) vals[j] = -vals[j];
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) st16(A3, cm_off(r, c0 + j, DK), pack_bf16x8(vals + j));
-        }
-      }
-    }
     {  // dS' pass: bf16 operand (stored to the workspace below), then dS *= Gam_C
       const int d = 32 * qw + lane;
       const float gcd = gamC[d];
@@ -216,9 +162,7 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
         tmem_ld32(T_DS + tl + c0, vals);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          st16(sm + Q_SB, cm_off(d, c0 + j, DV), pack_bf16x8(vals + j));
-        }
+        for (int j = 0; j < 32; j += 8) st16(sm + Q_SB, cm_off(d, c0 + j, DV), pack_bf16x8(vals + j));
 #pragma unroll
         for (int j = 0; j < 32; ++j) vals[j] *= gcd;
         tmem_st32(T_DS + tl + c0, vals);
@@ -229,15 +173,15 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // dU^T = dS'^T (lam K)^T + dO^T Aqk
     if (tid == kIoThread) {  // the workspace entry of chunk c is the dS' operand image
       bulk_store(reinterpret_cast<unsigned char*>(dsw) + (unit * n_chunks + c) * WS_UNIT, sm + Q_SB,
                  WS_UNIT);
       bulk_commit();
     }
+    // dU^T = dS'^T (lam K)^T + dO^T Aqk
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t sb = smem_u32(sm + Q_SB);
+      const uint32_t sb = smem_u32(sm + Q_SB), kl = set + Q_KL, dob = set + Q_DO, aqb = set + Q_AQ;
       const uint32_t id1 = idesc_bf16(128, 64, true, false), id2 = idesc_bf16(128, 64, true, true);
 #pragma unroll 1
       for (int ks = 0; ks < DK / 16; ++ks)
@@ -250,28 +194,30 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
     KDA_PT(1, 5);
-    {  // dU^T -> bf16 [j][c] (TP region)
+    {  // -dU^T -> bf16 [j][c] (TP region)
       const int j = 32 * qw + lane;
       float vals[32];
       tmem_ld32(T_U + tl + hh * 32, vals);
       tmem_wait_ld();
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) vals[jj] = -vals[jj];
 #pragma unroll
       for (int jj = 0; jj < 32; jj += 8) st16(sm + Q_TP, cm_off(j, hh * 32 + jj, C), pack_bf16x8(vals + jj));
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // dS += (Gam Q)^T dO + (-W)^T dU
+    // dS += (Gam Q)^T dO + W^T (-dU)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t dut = smem_u32(sm + Q_TP);
+      const uint32_t dut = smem_u32(sm + Q_TP), qg = set + Q_QG, dob = set + Q_DO, w = set + Q_W;
       const uint32_t id1 = idesc_bf16(128, 128, true, true), id2 = idesc_bf16(128, 128, true, false);
 #pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks)
         mma_bf16(T_DS, desc_mnmajor(qg + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id1, 1u);
 #pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks)
-        mma_bf16(T_DS, desc_mnmajor(a3 + ks * 4096, DK), desc_kmajor(dut + ks * 256, C), id2, 1u);
+        mma_bf16(T_DS, desc_mnmajor(w + ks * 4096, DK), desc_kmajor(dut + ks * 256, C), id2, 1u);
       mma_commit(mbar);
     }
     failed |= !mma_wait();
@@ -341,8 +287,7 @@ constexpr int PAR_SMEM = P_MMA + 96 * 32;
 // the checkpoint's adjacent tiles land with one bulk copy each: [T, Aqk, Akk] in
 // TB, AQB, AKB; [Q Gam, K Gam] in A3 rows 64..191; [K Gi, lam K] in KI, KL
 static_assert(P_AQB - P_TB == static_cast<int>(FAC_AQ) && P_AKB - P_TB == static_cast<int>(FAC_AK) &&
-                  FAC_QG == FAC_AK + 8192 && FAC_KG == FAC_QG + 16384 &&
-                  P_KL - P_KI == static_cast<int>(FAC_KL - FAC_KI) && FAC_KL == FAC_KI + 16384,
+                  FAC_KG == FAC_QG + 16384 && P_KL - P_KI == static_cast<int>(FAC_KL - FAC_KI),
               "factor staging layout");
 
 // Channel-major [128][64] CM tile (rows = channels, cols = tokens) -> [64][128]

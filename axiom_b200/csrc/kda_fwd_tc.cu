@@ -351,8 +351,9 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     __syncthreads();
     KDA_PT(0, 8);
     // ---------------- MMA_1: [W ; Q~] S ----------------
-    if (tid == kIoThread && sizeof(Tc) == 2 && ck_unit) {
-      bulk_store(ck_unit, sm + OFF_SB, DK * DV * 2);
+    if (tid == kIoThread && ((sizeof(Tc) == 2 && ck_unit) || fu)) {
+      if (sizeof(Tc) == 2 && ck_unit) bulk_store(ck_unit, sm + OFF_SB, DK * DV * 2);
+      if (fu) bulk_store(fu + FAC_W, A3, 16384);  // W (E2 wrote it to A3 rows 0..63)
       bulk_commit();
     }
     if (tid == 0) {
