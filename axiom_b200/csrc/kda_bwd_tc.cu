@@ -497,7 +497,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     const long long u_next = u + gridDim.x;
     bool prefetched = false;
 
-    // dO, dS' and S_c (bf16 checkpoint: the operand image) land while prep and
+    // dO, dS' and S_c (bf16 checkpoint: the operand image) land while T beta and
     // the W, U MMAs run
     if (!use_tma) {
       stage_tile(sm + P_SQ, dout + hoff + tok0 * rstride, rows_valid, rstride);

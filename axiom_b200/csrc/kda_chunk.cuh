@@ -1,8 +1,7 @@
 // Per-chunk building blocks shared by the tensor-core forward and backward
 // kernels (bf16 operands, dk = dv = 128, chunk C = 64, 256 threads):
-// staging of input tiles, the decay prep (G = cumsum(g) and the scaled operand
-// tiles), the score epilogue, the exact CUDA-core score fallback and the
-// blocked unit-triangular inverse T = (I + diag(beta) Akk)^-1.
+// staging of input tiles, the score epilogue, the exact CUDA-core score
+// fallback and the blocked unit-triangular inverse T = (I + diag(beta) Akk)^-1.
 #pragma once
 
 #include "kda_common.cuh"
@@ -70,99 +69,6 @@ __device__ __forceinline__ void stage_tile(unsigned char* dst, const bf16* src, 
   }
 }
 
-// Decay prep for one chunk.  Thread t owns channels 8(t>>4)..+7 and the rows
-// 8k + (t&7) for k in [4h, 4h+4), h = (t>>3)&1, so each group of 8 lanes reads
-// and writes whole core matrices (conflict-free).  G = cumsum(g) over the chunk
-// is formed with warp shuffles (no shared memory).  Writes the bf16 operand
-// tiles (CM, 128 columns):
-//   qg = q*Gam, kg = k*Gam, ki = k*exp(-G) (fast path only), kl = k*exp(G_C - G)
-// with Gam = exp(G); gamC[d] = exp(G_C[d]).  Any destination may be null.
-// Returns true ("slow") when some channel decays by more than kExpBudget over
-// the chunk; the caller must then use the exact score path.  G (fp32) for the
-// thread's 4 rows x 8 channels is returned in registers.
-__device__ __forceinline__ int prep_row(int k) {
-  const int t = threadIdx.x;
-  return 8 * (4 * ((t >> 3) & 1) + k) + (t & 7);
-}
-
-__device__ __forceinline__ bool prep(const unsigned char* sq, const unsigned char* sk,
-                                     const unsigned char* sg, unsigned char* qg_dst,
-                                     unsigned char* kg_dst, unsigned char* ki_dst,
-                                     unsigned char* kl_dst, float* gamC, float (&G)[4][8]) {
-  const int tid = threadIdx.x, cg = tid >> 4, half = (tid >> 3) & 1, rr = tid & 7;
-  const unsigned full = 0xffffffffu;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) unpack_bf16x8(ld16(sg, cm_off(prep_row(k), 8 * cg, 128)), G[k]);
-  float run[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) run[e] = 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float x = G[k][e];
-#pragma unroll
-      for (int off = 1; off < 8; off <<= 1) {
-        const float y = __shfl_up_sync(full, x, off, 8);
-        if (rr >= off) x += y;
-      }
-      const float grp = __shfl_sync(full, x, 7, 8);  // total of this 8-row group
-      G[k][e] = x + run[e];
-      run[e] += grp;
-    }
-  }
-  bool strong = false;
-  float tot[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float lo = __shfl_up_sync(full, run[e], 8);    // half 0's total, seen by half 1
-    const float hi = __shfl_down_sync(full, run[e], 8);  // half 1's total, seen by half 0
-    if (half) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) G[k][e] += lo;
-      tot[e] = lo + run[e];
-    } else {
-      tot[e] = run[e] + hi;
-    }
-    strong |= fabsf(tot[e]) > kExpBudget;
-  }
-  float gce[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) gce[e] = __expf(tot[e]);
-  if (half == 0 && rr == 0) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) gamC[8 * cg + e] = gce[e];
-  }
-  // one barrier publishes gamC and decides the path for the whole CTA
-  const bool slow = __syncthreads_or(strong) != 0;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t off = cm_off(prep_row(k), 8 * cg, 128);
-    float qv[8], kv[8], qg[8], kg[8], ki[8], kl[8];
-    unpack_bf16x8(ld16(sq, off), qv);
-    unpack_bf16x8(ld16(sk, off), kv);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float gam = __expf(G[k][e]);
-      qg[e] = qv[e] * gam;
-      kg[e] = kv[e] * gam;
-      if (!slow) {
-        const float gi = __expf(-G[k][e]);
-        ki[e] = kv[e] * gi;
-        kl[e] = kv[e] * (gi * gce[e]);
-      } else {
-        ki[e] = 0.f;
-        kl[e] = kv[e] * __expf(fminf(tot[e] - G[k][e], 0.f));
-      }
-    }
-    if (qg_dst) st16(qg_dst, off, pack_bf16x8(qg));
-    if (kg_dst) st16(kg_dst, off, pack_bf16x8(kg));
-    if (ki_dst && !slow) st16(ki_dst, off, pack_bf16x8(ki));
-    if (kl_dst) st16(kl_dst, off, pack_bf16x8(kl));
-  }
-  return slow;
-}
-
 // Score epilogue (fast path).  TMEM holds [Q*Gam ; K*Gam] (K*Gi)^T at `t_scores`
 // (128 lanes x 64 columns).  Writes Aqk (lower, inclusive) and Akk (strict)
 // as swizzled fp32 64x64 matrices.
@@ -214,14 +120,6 @@ __device__ __forceinline__ void scores_exact(const unsigned char* sq, const unsi
   }
 }
 
-// Store G (registers of prep) as fp32 [64][128] for scores_exact.
-__device__ __forceinline__ void store_G(float* Gf, const float (&G)[4][8]) {
-  const int cg = threadIdx.x >> 4;
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) Gf[prep_row(k) * DK + 8 * cg + e] = G[k][e];
-}
 
 // One merge step of the recursive-doubling inverse: for every pair of BS x BS
 // diagonal blocks already inverted (A^-1 above, B^-1 below), fill the block
@@ -331,6 +229,18 @@ __device__ __forceinline__ void solve_T(const float* Akk, const float* beta_s, f
 
 // Write row r, columns c0..c0+15 of a fp32 swizzled 64x64 matrix M (times
 // colscale[c] when given) as bf16 into a CM tile with 64 columns at row `dst_row`.
+// 16 consecutive fp32 values of row r of a swizzled 64 x 64 matrix (sw64),
+// columns c0..c0+15, read with explicit shared-memory vector loads.
+__device__ __forceinline__ void ld_row16_sw64(const float* M, int r, int c0, float* v) {
+  const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(M));
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) {
+    const uint32_t a = base + 4u * static_cast<uint32_t>(sw64(r, c0 + j));
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v[j]), "=f"(v[j + 1]), "=f"(v[j + 2]), "=f"(v[j + 3]) : "r"(a));
+  }
+}
+
 __device__ __forceinline__ void row16_to_cm(unsigned char* dst, int dst_row, const float* M, int r,
                                             int c0, const float* colscale) {
   float v[16];

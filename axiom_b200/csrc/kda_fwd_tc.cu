@@ -41,7 +41,9 @@ constexpr int OFF_VT = OFF_SB + 32768;          // v~ CM[64][128]      | T, Aqk 
 constexpr int OFF_BETA = OFF_VT + 16384;        // beta fp32[64]
 constexpr int OFF_GC = OFF_BETA + 256;          // Gam_C fp32[128]
 constexpr int OFF_BAR = OFF_GC + 512;           // mbarrier + tmem slot
-constexpr int SMEM_BYTES = OFF_BAR + 64;
+constexpr int OFF_TRI = OFF_BAR + 128;          // [L ; U'] bf16 CM[128][64] (0/1, built once)
+constexpr int OFF_GN = OFF_TRI + 16384;         // exp(-G_C) fp32[128] (G_C itself while staged)
+constexpr int SMEM_BYTES = OFF_GN + 512;
 
 // Issue the cp.async copies of one chunk's q, k, g (qkg = true) or v into CM tiles.
 __device__ __forceinline__ void stage_chunk(unsigned char* sm, const bf16* q, const bf16* k,
@@ -70,6 +72,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   extern __shared__ __align__(1024) unsigned char sm[];
   float* beta_s = reinterpret_cast<float*>(sm + OFF_BETA);
   float* gamC = reinterpret_cast<float*>(sm + OFF_GC);
+  float* gneg = reinterpret_cast<float*>(sm + OFF_GN);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 8);
   uint64_t* mbar_in = reinterpret_cast<uint64_t*>(sm + OFF_BAR + 16);  // TMA: a chunk's q, k, g, v
@@ -153,6 +156,22 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
 
   unsigned char* A3 = sm + OFF_A3;
   const uint32_t a3_addr = smem_u32(A3);
+  // The cumulative-sum operand of the decay prep: rows 0..63 L[i][j] = (j <= i),
+  // rows 64..127 U'[i][j] = (j > i - 64), so [L ; U'] g = [G ; G_C - G].
+  for (int i = tid; i < 128 * 8; i += NT) {
+    const int row = i >> 3, c8 = 8 * (i & 7);
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const int j0 = c8 + e, j1 = c8 + e + 1;
+      const bool b0 = row < 64 ? (j0 <= row) : (j0 > row - 64);
+      const bool b1 = row < 64 ? (j1 <= row) : (j1 > row - 64);
+      w[e >> 1] = (b0 ? 0x3F80u : 0u) | (b1 ? 0x3F800000u : 0u);
+    }
+    st16(sm + OFF_TRI, cm_off(row, c8, C), make_uint4(w[0], w[1], w[2], w[3]));
+  }
+  fence_async_smem();
+  __syncthreads();
 
   KDA_PT_INIT();
   for (int c = 0; c < n_chunks; ++c) {
@@ -191,9 +210,90 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       *reinterpret_cast<uint32_t*>(fu + FAC_FLAG) = slow_chunk ? 1u : 0u;
     };
     {
-      float G[4][8];
-      const bool slow = prep(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, A3 + cm_off(64, 0, DK),
-                             A3 + cm_off(128, 0, DK), sm + OFF_KI, sm + OFF_KL, gamC, G);
+      // ---- decay prep.  [G ; G_C - G] = [L ; U'] g on the tensor core (exact
+      // sums of the bf16 log-decays in fp32), then each thread takes TMEM lane R
+      // (token R % 64) and 64 channels: rows R < 64 give Q Gam, K Gam (Gam =
+      // exp(G)); rows R >= 64 give lam K = K exp(G_C - G) and K Gam^-1 = lam K
+      // exp(-G_C).  Row 63 of G is G_C, which decides the path (kExpBudget).
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t tri = smem_u32(sm + OFF_TRI), gt = smem_u32(sm + OFF_SG);
+        const uint32_t idesc = idesc_bf16(128, 128, false, true);
+#pragma unroll
+        for (int ks = 0; ks < C / 16; ++ks)
+          mma_bf16(T_D, desc_kmajor(tri + ks * 256, C), desc_mnmajor(gt + ks * 4096, DK), idesc, ks > 0);
+        mma_commit(mbar);
+      }
+      failed |= !mma_wait();
+      if (__syncthreads_or(failed)) break;
+      const int R = 32 * qw + lane;
+      bool strong = false;
+      if (qw == 1) {  // warps 1, 5 hold row 63 (lane 31): G_C of their 64 channels
+        for (int half = 0; half < 2; ++half) {  // whole-warp TMEM loads
+          float gv[32];
+          tmem_ld32(T_D + t_lane + hh * 64 + 32 * half, gv);
+          tmem_wait_ld();
+          if (lane == 31) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) gneg[hh * 64 + 32 * half + j] = gv[j];
+          }
+        }
+        __syncwarp();  // then Gam_C and exp(-G_C), two channels per lane
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int d = hh * 64 + 2 * lane + e;
+          const float gc = gneg[d];
+          gamC[d] = __expf(gc);
+          gneg[d] = __expf(-gc);
+          strong |= fabsf(gc) > kExpBudget;
+        }
+      }
+      const bool slow = __syncthreads_or(strong) != 0;
+      float* Gf = reinterpret_cast<float*>(sm + OFF_KI);  // exact path: G fp32 [64][128] across KI|TP
+      for (int half = 0; half < 2; ++half) {
+        const int c32 = hh * 64 + 32 * half;
+        float gv[32];
+        tmem_ld32(T_D + t_lane + c32, gv);
+        tmem_wait_ld();
+        if (R < 64) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            const uint32_t off = cm_off(R, c32 + j, DK);
+            float qv[8], kv[8], qg[8], kg[8];
+            unpack_bf16x8(ld16(sm + OFF_SQ, off), qv);
+            unpack_bf16x8(ld16(sm + OFF_SK, off), kv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float gam = __expf(gv[j + e]);
+              qg[e] = qv[e] * gam;
+              kg[e] = kv[e] * gam;
+            }
+            st16(A3, cm_off(64 + R, c32 + j, DK), pack_bf16x8(qg));
+            st16(A3, cm_off(128 + R, c32 + j, DK), pack_bf16x8(kg));
+            if (slow) {
+              *reinterpret_cast<float4*>(Gf + R * DK + c32 + j) = make_float4(gv[j], gv[j + 1], gv[j + 2], gv[j + 3]);
+              *reinterpret_cast<float4*>(Gf + R * DK + c32 + j + 4) =
+                  make_float4(gv[j + 4], gv[j + 5], gv[j + 6], gv[j + 7]);
+            }
+          }
+        } else {
+          const int r = R - 64;
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            const uint32_t off = cm_off(r, c32 + j, DK);
+            float kv[8], kl[8], ki[8];
+            unpack_bf16x8(ld16(sm + OFF_SK, off), kv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              kl[e] = kv[e] * __expf(slow ? fminf(gv[j + e], 0.f) : gv[j + e]);
+              ki[e] = kl[e] * gneg[c32 + j + e];
+            }
+            st16(sm + OFF_KL, off, pack_bf16x8(kl));
+            if (!slow) st16(sm + OFF_KI, off, pack_bf16x8(ki));
+          }
+        }
+      }
+      tc_fence_before();  // the TMEM reads above precede the score MMA's writes to T_D
       KDA_PT(0, 1);
       if (!slow) {
         fence_async_smem();
@@ -221,8 +321,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         KDA_PT(0, 3);
       } else {
         // exact scores on the CUDA cores (strong decay: the single anchor would overflow)
-        float* Gf = reinterpret_cast<float*>(sm + OFF_KI);  // [64][128] fp32 across KI|TP
-        store_G(Gf, G);
         fence_async_smem();
         __syncthreads();
         if (tid == kIoThread) store_prep(true);
@@ -244,12 +342,35 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       solve_T(Akk, beta_s, Tm, reinterpret_cast<float*>(sm + OFF_VT));
       KDA_PT(0, 4);
       const int r = tid >> 2, c0 = (tid & 3) * 16;
-      row16_to_cm(sm + OFF_TP, r, Tm, r, c0, beta_s);          // T diag(beta)
-      row16_to_cm(sm + OFF_VT, r, Tm, r, c0, nullptr);         // T      (bf16, K x N)
-      row16_to_cm(sm + OFF_VT + 8192, r, Aq, r, c0, nullptr);  // Aqk    (bf16, M x K)
+      float v[16], a[16], kk[16];
+      ld_row16_sw64(Tm, r, c0, v);
+      ld_row16_sw64(Aq, r, c0, a);
+      if (fu) ld_row16_sw64(Akk, r, c0, kk);
+      st16(sm + OFF_VT, cm_off(r, c0, C), pack_bf16x8(v));            // T      (bf16, K x N)
+      st16(sm + OFF_VT, cm_off(r, c0 + 8, C), pack_bf16x8(v + 8));
+      st16(sm + OFF_VT + 8192, cm_off(r, c0, C), pack_bf16x8(a));     // Aqk    (bf16, M x K)
+      st16(sm + OFF_VT + 8192, cm_off(r, c0 + 8, C), pack_bf16x8(a + 8));
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] *= beta_s[c0 + j];
+      st16(sm + OFF_TP, cm_off(r, c0, C), pack_bf16x8(v));            // T diag(beta)
+      st16(sm + OFF_TP, cm_off(r, c0 + 8, C), pack_bf16x8(v + 8));
+      // Akk bf16 for the checkpoint, over the fp32 Aqk just read (SB's first 16 KB)
+      KDA_PT(0, 16);
+      __syncthreads();
+      KDA_PT(0, 17);
+      if (fu) {
+        st16(sm + OFF_SB, cm_off(r, c0, C), pack_bf16x8(kk));
+        st16(sm + OFF_SB, cm_off(r, c0 + 8, C), pack_bf16x8(kk + 8));
+      }
     }
+    KDA_PT(0, 13);
     fence_async_smem();
     __syncthreads();
+    if (tid == kIoThread && fu) {  // T, Aqk (adjacent in VT) and Akk into the checkpoint
+      bulk_store(fu + FAC_T, sm + OFF_VT, 16384);
+      bulk_store(fu + FAC_AK, sm + OFF_SB, 8192);
+      bulk_commit();
+    }
     if (tid == 0) {  // P = Aqk T   (M = 64: row r at lane 32(r/16) + r%16)
       tc_fence_after();
       const uint32_t idesc = idesc_bf16(64, 64, false, true);
@@ -259,13 +380,10 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         mma_bf16(T_P, desc_kmajor(aqb + ks * 256, C), desc_mnmajor(tb + ks * 2048, C), idesc, ks > 0);
       mma_commit(mbar);
     }
-    if (fu) {  // T, Aqk, Akk (bf16 CM tiles) into the checkpoint for the backward
-      for (int i = tid; i < 1024; i += NT)
-        *reinterpret_cast<uint4*>(fu + FAC_T + 16 * i) = *reinterpret_cast<const uint4*>(sm + OFF_VT + 16 * i);
-      row16_to_cm(fu + FAC_AK, tid >> 2, Akk, tid >> 2, (tid & 3) * 16, nullptr);
-    }
     failed |= !mma_wait();
+    KDA_PT(0, 14);
     if (__syncthreads_or(failed)) break;
+    KDA_PT(0, 15);
     {  // P diag(beta) -> rows 64..127 of the [T b ; P b] operand
       float vals[32];
       tmem_ld32(T_P + t_lane + hh * 32, vals);
