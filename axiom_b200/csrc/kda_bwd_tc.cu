@@ -190,6 +190,11 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
       for (int ks = 0; ks < C / 16; ++ks)
         mma_bf16(T_U, desc_mnmajor(dob + ks * 4096, DV), desc_mnmajor(aqb + ks * 2048, C), id2, 1u);
       mma_commit(mbar);
+      // filler, independent of dU (runs under the -dU^T epilogue): dS += (Gam Q)^T dO
+      const uint32_t qg = set + Q_QG, id3 = idesc_bf16(128, 128, true, true);
+#pragma unroll 1
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_DS, desc_mnmajor(qg + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id3, 1u);
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
@@ -207,14 +212,11 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // dS += (Gam Q)^T dO + W^T (-dU)
+    // dS += W^T (-dU)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t dut = smem_u32(sm + Q_TP), qg = set + Q_QG, dob = set + Q_DO, w = set + Q_W;
-      const uint32_t id1 = idesc_bf16(128, 128, true, true), id2 = idesc_bf16(128, 128, true, false);
-#pragma unroll 1
-      for (int ks = 0; ks < C / 16; ++ks)
-        mma_bf16(T_DS, desc_mnmajor(qg + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id1, 1u);
+      const uint32_t dut = smem_u32(sm + Q_TP), w = set + Q_W;
+      const uint32_t id2 = idesc_bf16(128, 128, true, false);
 #pragma unroll 1
       for (int ks = 0; ks < C / 16; ++ks)
         mma_bf16(T_DS, desc_mnmajor(w + ks * 4096, DK), desc_kmajor(dut + ks * 256, C), id2, 1u);
