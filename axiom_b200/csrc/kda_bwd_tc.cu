@@ -316,6 +316,29 @@ __device__ __forceinline__ void store_rows(bf16* dst, const unsigned char* rows,
   }
 }
 
+// Column sums over the 32 lanes of a warp: every lane holds N consecutive
+// columns v[0..N-1] (N = 8 or 16); the result, on every lane, is column
+// (lane % N) summed over all 32 lanes.  Halving exchanges (N/2 + ... + 1
+// shuffles) leave lane l with column l % N summed over its group of N lanes;
+// log2(32 / N) more shuffles add the groups.
+template <int N>
+__device__ __forceinline__ float warp_colsum(float (&v)[N], int lane) {
+#pragma unroll
+  for (int off = N / 2; off >= 1; off >>= 1) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int j = 0; j < off; ++j) {
+      const float send = up ? v[j] : v[j + off];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, off);
+      v[j] = (up ? v[j + off] : v[j]) + recv;
+    }
+  }
+  float s = v[0];
+#pragma unroll
+  for (int off = N; off < 32; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  return s;
+}
+
 // fp32 checkpoint state (row-major) -> bf16 CM operand tile.
 __device__ __forceinline__ void stage_ckpt_f32(unsigned char* dst, const float* src) {
   for (int i = threadIdx.x; i < 128 * 16; i += NT) {
@@ -820,7 +843,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       const float gC = gamC[d];
       float dG[32];
       float klsum = 0.f;
-      float* TR = reinterpret_cast<float*>(sm + P_SB);  // dbeta partials [128][64], xor-swizzled
       const size_t gbase = hoff + tok0 * rstride + d;
       if (!slow) {
         // channel-major tiles: g (SQ), v (SK), QG (TP), KG (A3), KI (SG), each [128][64]
@@ -841,7 +863,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         for (int qq = 0; qq < 4; ++qq) {
           const int c8 = cb + 8 * qq;
           float dqg[8], dkg[8], dki[8], dkl[8], yw[8], yu[8], qg[8], kg[8], ki[8], vv[8];
-          float oq[8], ok[8], ov[8];
+          float oq[8], ok[8], ov[8], tb[8];
           tmem_ld8(T_IV + tl + c8, dqg);
           tmem_ld8(T_IV + 64 + tl + c8, dkg);
           tmem_ld8(T_SC + tl + c8, dki);
@@ -861,10 +883,14 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
             const float s2 = dki[i] + gC * dkl[i];
             dG[8 * qq + i] = dqg[i] * qg[i] + dkg[i] * kg[i] - s2 * ki[i];
             klsum += gC * dkl[i] * ki[i];
-            TR[d * 64 + (cc ^ (d & 63))] = yw[i] * kg[i] + yu[i] * vv[i];
+            tb[i] = yw[i] * kg[i] + yu[i] * vv[i];  // dbeta partial of token cc, channel d
             oq[i] = dqg[i] * gam;
             ok[i] = dkg[i] * gam + s2 * gi;
             ov[i] = beta_s[cc] * yu[i];
+          }
+          {  // dbeta partials: sum over this warp's 32 channels, 4 warps per token
+            const float sb = warp_colsum<8>(tb, lane);
+            if (lane < 8) atomicAdd(&dbs[c8 + lane], sb);
           }
           if (use_tma) {  // channel-major, over the tiles just read (stored below)
             st16(sm + P_TP, cm_off(d, c8, C), pack_bf16x8(oq));
@@ -903,7 +929,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
           const int c16 = cb + 16 * part;
-          float dqg[16], dkg[16], dkl[16], yw[16], yu[16];
+          float dqg[16], dkg[16], dkl[16], yw[16], yu[16], tb[16];
           tmem_ld16(T_IV + tl + c16, dqg);
           tmem_ld16(T_IV + 64 + tl + c16, dkg);
           tmem_ld16(T_KL + tl + c16, dkl);
@@ -939,13 +965,15 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
             dGv += dra * qv + drk * kv - (dca + dck) * kv;
             dG[16 * part + i] = dGv;
             const float vv = ldbf(sm + P_V, cm_off(cc, d, DV));
-            TR[d * 64 + (cc ^ (d & 63))] = yw[i] * kv * gam + yu[i] * vv;
+            tb[i] = yw[i] * kv * gam + yu[i] * vv;
             if (cc < rows_valid) {
               dq[gbase + cc * rstride] = __float2bfloat16_rn(dqv);
               dk[gbase + cc * rstride] = __float2bfloat16_rn(dkv);
               dv[gbase + cc * rstride] = __float2bfloat16_rn(beta_s[cc] * yu[i]);
             }
           }
+          const float sb = warp_colsum<16>(tb, lane);
+          if (lane < 16) atomicAdd(&dbs[c16 + lane], sb);
         }
       }
       float gsum = 0.f;
@@ -954,14 +982,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       xch[(0 * 2 + hh) * 128 + d] = gsum;
       xch[(1 * 2 + hh) * 128 + d] = klsum;
       KDA_PT(2, 16);
-      __syncthreads();
-      {  // dbeta: rowsum over the 128 channels of the partials, a quarter per thread
-        const int r = tid & 63, d0 = (tid >> 6) * 32;
-        float acc = 0.f;
-#pragma unroll 8
-        for (int dd = d0; dd < d0 + 32; ++dd) acc += TR[dd * 64 + (r ^ (dd & 63))];
-        atomicAdd(&dbs[r], acc);
-      }
+      __syncthreads();  // xch
       KDA_PT(2, 17);
       const float dGC = xch[(1 * 2 + 0) * 128 + d] + xch[(1 * 2 + 1) * 128 + d] + gC * dgc[d];
       float acc = dGC + (hh == 0 ? xch[(0 * 2 + 1) * 128 + d] : 0.f);
