@@ -252,15 +252,20 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
 // ===========================================================================
 // bwd_par
 // ===========================================================================
-constexpr int P_SQ = 0;                  // dO | raw q (exact path) | g^T [128][64]
-constexpr int P_SK = 16384;              // dS' (lo) | dW^T [128][64] | raw k (exact path) | v^T
+// Regions by phase.  Prefetched one unit ahead (during the previous epilogue):
+// A3 = [W ; Gam Q ; Gam K], KI, KL, V (U), TP (v~), TB, AQB, AKB, GF.  Loaded at
+// unit start: SQ (dO), SK|SG (dS'), SB (S_c).  Epilogue tiles (channel-major,
+// then the outputs in place): SQ (g^T -> dg), SK (v^T -> dv), SG (KI^T),
+// SB (QG^T -> dq, KG^T -> dk).
+constexpr int P_SQ = 0;                  // dO | raw q (exact path) | g^T -> dg
+constexpr int P_SK = 16384;              // dS' (lo) | dW^T [128][64] | raw k (exact path) | v^T -> dv
 constexpr int P_SG = 32768;              // dS' (hi) | raw g | KI^T [128][64]
-constexpr int P_V = 49152;               // v staging | U bf16 [64][128] | raw v
-constexpr int P_A3 = 65536;              // [W ; Gam Q ; Gam K] (the forward's images) | KG^T
+constexpr int P_V = 49152;               // U bf16 [64][128] | raw v
+constexpr int P_A3 = 65536;              // [W ; Gam Q ; Gam K] (the forward's images)
 constexpr int P_KI = P_A3 + 49152;       // K Gi (the forward's image)
 constexpr int P_KL = P_KI + 16384;       // lam K | dU^T [128][64] | [dAqk ; beta dL] [128][64]
-constexpr int P_SB = P_KL + 16384;       // S_c bf16 [128][128] | Yw^T, Yu^T | dbeta partials
-constexpr int P_TP = P_SB + 32768;       // T beta [64][64] | v~ bf16 [64][128] | QG^T | G fp32 (exact path, with TB/AQB)
+constexpr int P_SB = P_KL + 16384;       // S_c bf16 [128][128] | Yw^T, Yu^T | QG^T -> dq, KG^T -> dk
+constexpr int P_TP = P_SB + 32768;       // v~ bf16 [64][128] | G fp32 (exact path, with TB/AQB)
 constexpr int P_TB = P_TP + 16384;       // T bf16 [64][64]
 constexpr int P_AQB = P_TB + 8192;       // Aqk bf16
 constexpr int P_AKB = P_AQB + 8192;      // Akk bf16
@@ -270,42 +275,54 @@ constexpr int P_DGC = P_GF + 2 * 544;    // dGam_C partial fp32[128]
 constexpr int P_DB = P_DGC + 512;        // dbeta accum fp32[64]
 constexpr int P_XCH = P_DB + 256;        // half-exchange fp32[2][2][128]
 constexpr int P_BAR = P_XCH + 2048;
-constexpr int P_MMA = P_BAR + 64;         // MMA issue table (MmaOp[96])
+constexpr int P_MMA = P_BAR + 64;         // MMA issue table (MmaOp[N_MMA])
 // Issue-table groups (first entry, count).  A group's critical MMAs are
 // committed before its filler MMAs: the tensor core runs in issue order, so the
 // filler (needed only later) executes while the threads work on the critical
 // results, and the next group's commit implies it has completed.
-constexpr int G_WU = 0, N_WU = 8;         // W, U
-constexpr int G_WS = 8, N_WS = 8;         // W S_c
-constexpr int G_DU = 16, N_DU = 12;       // dU^T               | filler: dKL^T
-constexpr int F_DU = 28, NF_DU = 8;
-constexpr int G_SD = 36, N_SD = 8;        // (dU S_c^T)^T       | filler: Yu^T, (dO S_c^T)^T
-constexpr int F_SD = 44, NF_SD = 12;
-constexpr int G_YW = 56, N_YW = 4;        // Yw^T               | filler: dAqk
-constexpr int F_YW = 60, NF_YW = 8;
-constexpr int G_DL = 68, N_DL = 16;       // dL
-constexpr int G_VII = 84, N_VII = 12;     // [dQG^T | dKG^T] +=, dKI^T
-constexpr int PAR_SMEM = P_MMA + 96 * 32;
+constexpr int G_DU = 0, N_DU = 12;        // dU^T               | filler: dKL^T
+constexpr int F_DU = 12, NF_DU = 8;
+constexpr int G_SD = 20, N_SD = 8;        // (dU S_c^T)^T       | filler: Yu^T, (dO S_c^T)^T
+constexpr int F_SD = 28, NF_SD = 12;
+constexpr int G_YW = 40, N_YW = 4;        // Yw^T               | filler: dAqk
+constexpr int F_YW = 44, NF_YW = 8;
+constexpr int G_DL = 52, N_DL = 16;       // dL
+constexpr int G_VII = 68, N_VII = 12;     // [dQG^T | dKG^T] +=, dKI^T
+constexpr int N_MMA = 80;
+constexpr int PAR_SMEM = P_MMA + N_MMA * 32;
 // the checkpoint's adjacent tiles land with one bulk copy each: [T, Aqk, Akk] in
 // TB, AQB, AKB; [Q Gam, K Gam] in A3 rows 64..191; [K Gi, lam K] in KI, KL
 static_assert(P_AQB - P_TB == static_cast<int>(FAC_AQ) && P_AKB - P_TB == static_cast<int>(FAC_AK) &&
                   FAC_KG == FAC_QG + 16384 && P_KL - P_KI == static_cast<int>(FAC_KL - FAC_KI),
               "factor staging layout");
 
-// Channel-major [128][64] CM tile (rows = channels, cols = tokens) -> [64][128]
-// token rows of 256 bytes whose 16-byte chunk j sits at position j ^ (row & 7)
-// (the XOR keeps the transposing stmatrix writes conflict-free).
-__device__ __forceinline__ void transpose_to_rows(uint32_t dst, uint32_t src, int warp, int lane) {
-  for (int j0 = 4 * warp; j0 < 128; j0 += 4 * (NT / 32)) {
-    const int j = j0 + (lane >> 3), row = lane & 7;
-    const int rg = j >> 3, cg = j & 7;  // channel block, token block
-    uint32_t f[4];
-    ldmatrix_x4(f, src + ((rg * 8 + cg) << 7) + (row << 4));
-    const int c = 8 * cg + row;  // token row this lane addresses
-    stmatrix_x4_trans(dst + (c << 8) + ((rg ^ (c & 7)) << 4), f);
-  }
+// Four channel-major [128][64] CM tiles (rows = channels, cols = tokens) become,
+// each in place, [64][128] token rows of 256 bytes whose 16-byte chunk j sits at
+// position j ^ (row & 7) (the XOR keeps the transposing stmatrix writes
+// conflict-free): every warp loads its core matrices of all four tiles into
+// registers, a barrier, then the transposed writes; ends with a barrier.
+__device__ __forceinline__ void transpose4_to_rows_inplace(const uint32_t (&tile)[4], int warp, int lane) {
+  uint32_t f[4][4][4];
+  __syncthreads();  // every tile complete
+#pragma unroll
+  for (int t = 0; t < 4; ++t)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * warp + 32 * k + (lane >> 3), row = lane & 7;
+      ldmatrix_x4(f[t][k], tile[t] + (((j >> 3) * 8 + (j & 7)) << 7) + (row << 4));
+    }
+  __syncthreads();
+#pragma unroll
+  for (int t = 0; t < 4; ++t)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = 4 * warp + 32 * k + (lane >> 3), row = lane & 7;
+      const int rg = j >> 3, c = 8 * (j & 7) + row;
+      stmatrix_x4_trans(tile[t] + (c << 8) + ((rg ^ (c & 7)) << 4), f[t][k]);
+    }
+  __syncthreads();
 }
-// Token rows written by transpose_to_rows -> global rows (row r at dst + r*rstride),
+// Token rows (transpose4_to_rows_inplace) -> global rows (row r at dst + r*rstride),
 // 16 bytes per thread and store, rows >= rows_valid skipped.
 __device__ __forceinline__ void store_rows(bf16* dst, const unsigned char* rows, int rows_valid,
                                            size_t rstride) {
@@ -370,7 +387,8 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P_BAR + 8);
   uint64_t* mbar_fac = reinterpret_cast<uint64_t*>(sm + P_BAR + 16);   // T, Aqk, Akk bulk load
-  uint64_t* mbar_late = reinterpret_cast<uint64_t*>(sm + P_BAR + 24);  // dS', S_c (+ dO) loads
+  uint64_t* mbar_late = reinterpret_cast<uint64_t*>(sm + P_BAR + 24);  // dO, dS' (first needed)
+  uint64_t* mbar_sc = reinterpret_cast<uint64_t*>(sm + P_BAR + 40);    // S_c (needed from G_SD)
   uint64_t* mbar_rs = reinterpret_cast<uint64_t*>(sm + P_BAR + 32);    // restaged tiles (TMA)
   unsigned char* A3 = sm + P_A3;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -383,6 +401,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     mbar_init(mbar, 1);
     mbar_init(mbar_fac, 1);
     mbar_init(mbar_late, 1);
+    mbar_init(mbar_sc, 1);
     mbar_init(mbar_rs, 1);
     mbar_fence_init();
   }
@@ -392,10 +411,9 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   tc_fence_after();
   const uint32_t tbase = *tslot;
   // TMEM columns
-  const uint32_t T_IV = tbase;            // [0,128): W | (dO S^T)^T, dKG^T
-  const uint32_t T_UF = tbase + 128;      // [128,256): U (fp32) | Yw^T, Yu^T
-  const uint32_t T_SC = tbase + 256;      // [256,320): scores | W S (64..) | dAqk | dKI^T
-  const uint32_t T_WS = tbase + 256;      // [256,384): W S (M = 64)
+  const uint32_t T_IV = tbase;            // [0,128): (dO S^T)^T, dKG^T
+  const uint32_t T_UF = tbase + 128;      // [128,256): Yw^T, Yu^T
+  const uint32_t T_SC = tbase + 256;      // [256,320): dAqk | dKI^T
   const uint32_t T_L = tbase + 320;       // [320,384): dL (negated)
   const uint32_t T_DU = tbase + 384;      // [384,448): dU^T
   const uint32_t T_KL = tbase + 448;      // [448,512): dKL^T
@@ -417,16 +435,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     const uint32_t tp = smem_u32(sm + P_TP), vb = smem_u32(sm + P_V), sb = smem_u32(sm + P_SB);
     const uint32_t dsp = smem_u32(sm + P_SK), kl = smem_u32(sm + P_KL), dob = smem_u32(sm + P_SQ);
     const uint32_t aqb = smem_u32(sm + P_AQB), tb = smem_u32(sm + P_TB), ki = smem_u32(sm + P_KI);
-    int n = G_WU;  // W = (T b)(Gam K), U = (T b) V   (M = 64)
-    for (int ks = 0; ks < C / 16; ++ks) {
-      const uint64_t ad = desc_kmajor(tp + ks * 256, C);
-      const uint32_t id = idesc_bf16(64, 128, false, true);
-      mma_op(tab, n++, T_IV, ad, desc_mnmajor(a3 + 128 * 256 + ks * 4096, DK), id, ks > 0);
-      mma_op(tab, n++, T_UF, ad, desc_mnmajor(vb + ks * 4096, DV), id, ks > 0);
-    }
-    for (int ks = 0; ks < DK / 16; ++ks)  // W S_c   (M = 64)
-      mma_op(tab, n++, T_WS, desc_kmajor(a3 + ks * 256, DK), desc_mnmajor(sb + ks * 4096, DV),
-             idesc_bf16(64, 128, false, true), ks > 0);
+    int n = G_DU;
     // G_DU: dU^T = dS'^T (lam K)^T + dO^T Aqk | F_DU: dKL^T = dS' v~^T
     for (int ks = 0; ks < DK / 16; ++ks)
       mma_op(tab, n++, T_DU, desc_mnmajor(dsp + ks * 4096, DV), desc_kmajor(kl + ks * 256, DK),
@@ -479,29 +488,26 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   // are issued one unit ahead, during the previous unit's epilogue, and complete
   // on mbar_fac.  Every asynchronous phase is waited before the CTA exits.
   int it = 0;                                      // units processed by this CTA
-  bool fac_pending = false, late_pending = false, rs_pending = false;  // issued, not yet waited
-  uint32_t fac_par = 0, late_par = 0, rs_par = 0;
+  bool fac_pending = false, late_pending = false, sc_pending = false, rs_pending = false;  // issued, not waited
+  uint32_t fac_par = 0, late_par = 0, sc_par = 0, rs_par = 0;
   auto issue_inputs = [&](long long uu, unsigned short& beta_nx) {
     const int cc = static_cast<int>(uu % n_chunks);
     const long long bhn = uu / n_chunks;
     const int hn = static_cast<int>(bhn % H), bn = static_cast<int>(bhn / H);
     const int rv = min(C, T - cc * C);
     const size_t tk = static_cast<size_t>(bn) * T + static_cast<size_t>(cc) * C;
-    const size_t src = static_cast<size_t>(hn) * DK + tk * rstride;
-    if (!use_tma) {
-      stage_tile(sm + P_V, v + src, rv, rstride);
-      cp_async_commit();
-    }
     if (tid == kIoThread) {
       const unsigned char* fu = factors + ((static_cast<size_t>(bn) * H + hn) * n_chunks + cc) * FAC_UNIT;
       const int gf = P_GF + 544 * ((uu == blockIdx.x ? it : it + 1) & 1);
       fence_async_smem();
-      mbar_expect_tx(mbar_fac, 24576 + 32768 + 32768 + FAC_GF_BYTES + (use_tma ? 16384 : 0));
+      mbar_expect_tx(mbar_fac, 24576 + 32768 + 32768 + 3 * 16384 + FAC_GF_BYTES);
       bulk_load(sm + P_TB, fu + FAC_T, 24576, mbar_fac);                  // T, Aqk, Akk
       bulk_load(A3 + cm_off(64, 0, DK), fu + FAC_QG, 32768, mbar_fac);    // Q Gam, K Gam
       bulk_load(sm + P_KI, fu + FAC_KI, 32768, mbar_fac);                 // K Gi, lam K
+      bulk_load(A3, fu + FAC_W, 16384, mbar_fac);                         // W
+      bulk_load(sm + P_V, fu + FAC_U, 16384, mbar_fac);                   // U
+      bulk_load(sm + P_TP, fu + FAC_VT, 16384, mbar_fac);                 // v~
       bulk_load(sm + gf, fu + FAC_GC, FAC_GF_BYTES, mbar_fac);            // Gam_C, flag
-      if (use_tma) tma_tile(sm + P_V, &tm_v, hn, cc, bn, mbar_fac);
     }
     fac_pending = true;
     fac_par = static_cast<uint32_t>(uu == blockIdx.x ? it : it + 1) & 1u;
@@ -528,16 +534,20 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       stage_tile(sm + P_SQ, dout + hoff + tok0 * rstride, rows_valid, rstride);
       cp_async_commit();
     }
-    if (tid == kIoThread) {
-      constexpr uint32_t late_bytes = WS_UNIT + (sizeof(Tc) == 2 ? DK * DV * 2 : 0);
+    if (tid == kIoThread) {  // in the order they are needed: dO, dS' (dU group), then S_c
       fence_async_smem();
-      mbar_expect_tx(mbar_late, late_bytes + (use_tma ? 16384 : 0));
-      bulk_load(sm + P_SK, reinterpret_cast<const unsigned char*>(dsw) + unit_sq * WS_UNIT, WS_UNIT, mbar_late);
-      if constexpr (sizeof(Tc) == 2) bulk_load(sm + P_SB, s_ckpt + unit_sq * (DK * DV), DK * DV * 2, mbar_late);
+      mbar_expect_tx(mbar_late, WS_UNIT + (use_tma ? 16384 : 0));
       if (use_tma) tma_tile(sm + P_SQ, &tm_do, h, c, b, mbar_late);
+      bulk_load(sm + P_SK, reinterpret_cast<const unsigned char*>(dsw) + unit_sq * WS_UNIT, WS_UNIT, mbar_late);
+      if constexpr (sizeof(Tc) == 2) {
+        mbar_expect_tx(mbar_sc, DK * DV * 2);
+        bulk_load(sm + P_SB, s_ckpt + unit_sq * (DK * DV), DK * DV * 2, mbar_sc);
+      }
     }
     late_pending = true;
     late_par = static_cast<uint32_t>(it) & 1u;
+    sc_pending = sizeof(Tc) == 2;
+    sc_par = static_cast<uint32_t>(it) & 1u;
     if (tid < C) beta_s[tid] = bf16_raw_to_float(beta_nx);
     if (tid < 128) dgc[tid] = 0.f;
     if (tid < 64) dbs[tid] = 0.f;
@@ -549,97 +559,17 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     if (__syncthreads_or(failed)) break;
 
     KDA_PT(2, 0);
-    // ---- W, U from the forward's T and K Gam (no recompute of the decay prep) ----
+    // ---- the forward's W, U and v~ are resident: straight to the adjoint ----
     const float* gamC = reinterpret_cast<const float*>(sm + P_GF + 544 * (it & 1));
     const bool slow = reinterpret_cast<const uint32_t*>(gamC)[128] != 0u;  // exact-path chunk
     KDA_PT(2, 1);
-    {  // T diag(beta) from the bf16 T tile
-      const int r = tid >> 2, c0 = (tid & 3) * 16;
-      float tv[16];
-      unpack_bf16x8(ld16(sm + P_TB, cm_off(r, c0, C)), tv);
-      unpack_bf16x8(ld16(sm + P_TB, cm_off(r, c0 + 8, C)), tv + 8);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) tv[j] *= beta_s[c0 + j];
-      st16(sm + P_TP, cm_off(r, c0, C), pack_bf16x8(tv));
-      st16(sm + P_TP, cm_off(r, c0 + 8, C), pack_bf16x8(tv + 8));
-    }
-    fence_async_smem();
-    __syncthreads();
-    KDA_PT(2, 2);
-    // W = (T b)(Gam K), U = (T b) V   (M = 64)
-    if (tid == 0) {
-      tc_fence_after();
-      mma_run(tab, G_WU, N_WU);
-      mma_commit(mbar);
-    }
-    failed |= !mma_wait();
-    if (__syncthreads_or(failed)) break;
     if constexpr (sizeof(Tc) == 4) stage_ckpt_f32(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
-    KDA_PT(2, 3);
-    {  // W -> A3 rows 0..63, U -> bf16 (V region); U fp32 stays in TMEM
-      const int r = 16 * qw + lane;
-      for (int half = 0; half < 2; ++half) {
-        const int c0 = hh * 64 + half * 32;
-        float w[32], uu[32];
-        tmem_ld32(T_IV + tl + c0, w);
-        tmem_ld32(T_UF + tl + c0, uu);
-        tmem_wait_ld();
-        if (lane < 16) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            st16(A3, cm_off(r, c0 + j, DK), pack_bf16x8(w + j));
-            st16(sm + P_V, cm_off(r, c0 + j, DV), pack_bf16x8(uu + j));
-          }
-        }
-      }
-    }
     cp_async_wait<0>();
     failed |= !mbar_wait(mbar_late, late_par);
     late_pending = false;
     fence_async_smem();
     tc_fence_before();
     if (__syncthreads_or(failed)) break;
-    KDA_PT(2, 4);
-    // W S_c  (M = 64)
-    if (tid == 0) {
-      tc_fence_after();
-      mma_run(tab, G_WS, N_WS);
-      mma_commit(mbar);
-    }
-    {  // dGam_C partial sums: sum_j S_c[d][j] dS'[d][j]
-      const int d = tid >> 1, j0 = (tid & 1) * 64;
-      float acc = 0.f;
-      for (int j = j0; j < j0 + 64; j += 8) {
-        float a[8], bb[8];
-        unpack_bf16x8(ld16(sm + P_SB, cm_off(d, j, DV)), a);
-        unpack_bf16x8(ld16(sm + P_SK, cm_off(d, j, DV)), bb);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc += a[e] * bb[e];
-      }
-      atomicAdd(&dgc[d], acc);
-    }
-    failed |= !mma_wait();
-    if (__syncthreads_or(failed)) break;
-    KDA_PT(2, 5);
-    {  // v~ = U - W S -> bf16 (TP region)
-      const int r = 16 * qw + lane;
-      for (int half = 0; half < 2; ++half) {
-        const int c0 = hh * 64 + half * 32;
-        float ws[32], uu[32];
-        tmem_ld32(T_WS + tl + c0, ws);
-        tmem_ld32(T_UF + tl + c0, uu);
-        tmem_wait_ld();
-        if (lane < 16) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) uu[j] -= ws[j];
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) st16(sm + P_TP, cm_off(r, c0 + j, DV), pack_bf16x8(uu + j));
-        }
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
     KDA_PT(2, 6);
     // dU^T = dS'^T (lam K)^T + dO^T Aqk ;  dKL^T = dS' v~^T
     if (tid == 0) {
@@ -649,6 +579,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       mma_run(tab, F_DU, NF_DU);
       KDA_PT(2, 20);
     }
+
     failed |= !mma_wait();
     KDA_PT(2, 21);
     if (__syncthreads_or(failed)) break;
@@ -661,9 +592,13 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 #pragma unroll
       for (int jj = 0; jj < 32; jj += 8) st16(sm + P_KL, cm_off(j, hh * 32 + jj, C), pack_bf16x8(vals + jj));
     }
+    if constexpr (sizeof(Tc) == 2) {
+      failed |= !mbar_wait(mbar_sc, sc_par);
+      sc_pending = false;
+    }
     fence_async_smem();
     tc_fence_before();
-    __syncthreads();
+    if (__syncthreads_or(failed)) break;
     KDA_PT(2, 8);
     // S_c [dO^T | dU^T] -> (dO S^T)^T | (dU S^T)^T
     if (tid == 0) {
@@ -672,6 +607,18 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       mma_commit(mbar);
       mma_run(tab, F_SD, NF_SD);
       KDA_PT(2, 22);
+    }
+    {  // dGam_C partial sums: sum_j S_c[d][j] dS'[d][j]  (under the S_c MMAs; both only read)
+      const int d = tid >> 1, j0 = (tid & 1) * 64;
+      float acc = 0.f;
+      for (int j = j0; j < j0 + 64; j += 8) {
+        float a[8], bb[8];
+        unpack_bf16x8(ld16(sm + P_SB, cm_off(d, j, DV)), a);
+        unpack_bf16x8(ld16(sm + P_SK, cm_off(d, j, DV)), bb);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc += a[e] * bb[e];
+      }
+      atomicAdd(&dgc[d], acc);
     }
     failed |= !mma_wait();
     KDA_PT(2, 23);
@@ -804,10 +751,10 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         mma_commit(mbar);
         KDA_PT(2, 29);
       }
-      // channel-major copies for the epilogue: QG -> TP, KG -> A3 rows 0..63 (W is dead;
-      // the MMAs only read QG, KG)
-      transpose_cm<64, 128>(smem_u32(sm + P_TP), a3 + 64 * 256, warp, lane, NT / 32);
-      transpose_cm<64, 128>(a3, a3 + 128 * 256, warp, lane, NT / 32);
+      // channel-major copies for the epilogue: QG, KG -> SB (Yw^T, Yu^T are dead; the
+      // MMAs only read QG, KG)
+      transpose_cm<64, 128>(smem_u32(sm + P_SB), a3 + 64 * 256, warp, lane, NT / 32);
+      transpose_cm<64, 128>(smem_u32(sm + P_SB + 16384), a3 + 128 * 256, warp, lane, NT / 32);
       KDA_PT(2, 30);
       cp_async_wait<0>();
       if (use_tma) {
@@ -823,8 +770,8 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       KDA_PT(2, 19);
       transpose_cm<64, 128>(smem_u32(sm + P_SG), smem_u32(sm + P_KI), warp, lane, NT / 32);  // KI
       __syncthreads();
-      // A3 rows 64..191, KI, KL, V, TB, AQB, AKB and the other Gam_C slot are free:
-      // stage the next unit
+      // A3, KI, KL, V, TP, TB, AQB, AKB and the other Gam_C slot are free: stage the
+      // next unit
       if (u_next < n_units) issue_inputs(u_next, beta_nx);
       prefetched = true;
     } else {
@@ -845,7 +792,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       float klsum = 0.f;
       const size_t gbase = hoff + tok0 * rstride + d;
       if (!slow) {
-        // channel-major tiles: g (SQ), v (SK), QG (TP), KG (A3), KI (SG), each [128][64]
+        // channel-major tiles: g (SQ), v (SK), QG (SB), KG (SB + 16 KB), KI (SG), each [128][64]
         float gm[32];
 #pragma unroll
         for (int j = 0; j < 4; ++j) unpack_bf16x8(ld16(sm + P_SQ, cm_off(d, cb + 8 * j, C)), gm + 8 * j);
@@ -870,8 +817,8 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           tmem_ld8(T_KL + tl + c8, dkl);
           tmem_ld8(T_UF + tl + c8, yw);
           tmem_ld8(T_UF + 64 + tl + c8, yu);
-          unpack_bf16x8(ld16(sm + P_TP, cm_off(d, c8, C)), qg);
-          unpack_bf16x8(ld16(A3, cm_off(d, c8, C)), kg);
+          unpack_bf16x8(ld16(sm + P_SB, cm_off(d, c8, C)), qg);
+          unpack_bf16x8(ld16(sm + P_SB + 16384, cm_off(d, c8, C)), kg);
           unpack_bf16x8(ld16(sm + P_SG, cm_off(d, c8, C)), ki);
           unpack_bf16x8(ld16(sm + P_SK, cm_off(d, c8, C)), vv);
           tmem_wait_ld();
@@ -893,8 +840,8 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
             if (lane < 8) atomicAdd(&dbs[c8 + lane], sb);
           }
           if (use_tma) {  // channel-major, over the tiles just read (stored below)
-            st16(sm + P_TP, cm_off(d, c8, C), pack_bf16x8(oq));
-            st16(A3, cm_off(d, c8, C), pack_bf16x8(ok));
+            st16(sm + P_SB, cm_off(d, c8, C), pack_bf16x8(oq));
+            st16(sm + P_SB + 16384, cm_off(d, c8, C), pack_bf16x8(ok));
             st16(sm + P_SK, cm_off(d, c8, C), pack_bf16x8(ov));
           } else {
 #pragma unroll
@@ -1004,19 +951,16 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       }
     }
     if (use_tma && !slow) {
-      // dq, dk, dv, dg: channel-major tiles -> token rows (swizzled) -> 16-byte stores
-      __syncthreads();
-      transpose_to_rows(smem_u32(sm + P_SG), smem_u32(sm + P_TP), warp, lane);         // dq
-      transpose_to_rows(smem_u32(sm + P_SB), a3, warp, lane);                          // dk
-      transpose_to_rows(smem_u32(sm + P_SB + 16384), smem_u32(sm + P_SK), warp, lane);  // dv
-      __syncthreads();
-      transpose_to_rows(smem_u32(sm + P_TP), smem_u32(sm + P_SQ), warp, lane);         // dg
+      // dq, dk, dv, dg: channel-major tiles -> token rows (swizzled, in place) ->
+      // 16-byte stores
+      const uint32_t tiles[4] = {smem_u32(sm + P_SB), smem_u32(sm + P_SB + 16384), smem_u32(sm + P_SK),
+                                 smem_u32(sm + P_SQ)};
+      transpose4_to_rows_inplace(tiles, warp, lane);
       const size_t obase = hoff + tok0 * rstride;
-      store_rows(dq + obase, sm + P_SG, rows_valid, rstride);
-      store_rows(dk + obase, sm + P_SB, rows_valid, rstride);
-      store_rows(dv + obase, sm + P_SB + 16384, rows_valid, rstride);
-      __syncthreads();
-      store_rows(dg + obase, sm + P_TP, rows_valid, rstride);
+      store_rows(dq + obase, sm + P_SB, rows_valid, rstride);
+      store_rows(dk + obase, sm + P_SB + 16384, rows_valid, rstride);
+      store_rows(dv + obase, sm + P_SK, rows_valid, rstride);
+      store_rows(dg + obase, sm + P_SQ, rows_valid, rstride);
     }
     KDA_PT(2, 18);
     tc_fence_before();
@@ -1033,6 +977,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   // for them before the shared memory is released
   if (fac_pending) mbar_wait(mbar_fac, fac_par);
   if (late_pending) mbar_wait(mbar_late, late_par);
+  if (sc_pending) mbar_wait(mbar_sc, sc_par);
   if (rs_pending) mbar_wait(mbar_rs, rs_par);
   tc_fence_before();
   __syncthreads();

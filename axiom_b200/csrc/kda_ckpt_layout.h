@@ -16,10 +16,12 @@ constexpr size_t FAC_QG = 40960;     // Q Gam                                bf1
 constexpr size_t FAC_KG = 57344;     // K Gam                                bf16 CM [64][128]
 constexpr size_t FAC_KI = 73728;     // K Gam^-1 (fast-path chunks only)     bf16 CM [64][128]
 constexpr size_t FAC_KL = 90112;     // lam K = K Gam^-1 Gam_C               bf16 CM [64][128]
-constexpr size_t FAC_GC = 106496;    // Gam_C                                fp32 [128]
-constexpr size_t FAC_FLAG = 107008;  // u32: 1 if the chunk took the exact (strong-decay) path
+constexpr size_t FAC_VT = 106496;    // v~ = U - W S_c                       bf16 CM [64][128]
+constexpr size_t FAC_U = 122880;     // U = T diag(beta) V                   bf16 CM [64][128]
+constexpr size_t FAC_GC = 139264;    // Gam_C                                fp32 [128]
+constexpr size_t FAC_FLAG = 139776;  // u32: 1 if the chunk took the exact (strong-decay) path
 constexpr size_t FAC_GF_BYTES = 528; // Gam_C + flag, copied together
-constexpr size_t FAC_UNIT = 107520;  // bytes per chunk-head (16-byte multiple)
+constexpr size_t FAC_UNIT = 140288;  // bytes per chunk-head (16-byte multiple)
 
 static_assert(FAC_FLAG == FAC_GC + 512 && FAC_UNIT % 16 == 0 && FAC_GF_BYTES % 16 == 0 &&
                   FAC_QG == FAC_W + 16384 && FAC_KG == FAC_QG + 16384 && FAC_KL == FAC_KI + 16384,

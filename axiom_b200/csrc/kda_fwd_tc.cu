@@ -496,6 +496,11 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         tmem_ld32(T_D + t_lane + 128 + c0, u);
         tmem_wait_ld();
         if (R < 64) {
+          if (fu) {  // U (bf16 image) into the checkpoint
+#pragma unroll
+            for (int j = 0; j < 32; j += 8)
+              *reinterpret_cast<uint4*>(fu + FAC_U + cm_off(R, c0 + j, DV)) = pack_bf16x8(u + j);
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) u[j] -= ws[j];
 #pragma unroll
@@ -513,6 +518,10 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    if (tid == kIoThread && fu) {  // v~ (bf16 image) into the checkpoint
+      bulk_store(fu + FAC_VT, sm + OFF_VT, 16384);
+      bulk_commit();
+    }
     KDA_PT(0, 10);
     // ---------------- MMA_3: S += (lam K)^T v~ ----------------
     if (tid == 0) {
