@@ -79,6 +79,11 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> str:
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
     os.replace(tmp, LIB)
+    # objects of earlier source versions are never reused once a source changes
+    keep = {os.path.basename(o) for o in objs}
+    for name in os.listdir(BUILD):
+        if name.endswith(".o") and name not in keep:
+            os.remove(os.path.join(BUILD, name))
     return LIB
 
 

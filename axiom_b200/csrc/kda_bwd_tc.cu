@@ -297,10 +297,12 @@ static_assert(P_AQB - P_TB == static_cast<int>(FAC_AQ) && P_AKB - P_TB == static
               "factor staging layout");
 
 // Four channel-major [128][64] CM tiles (rows = channels, cols = tokens) become,
-// each in place, [64][128] token rows of 256 bytes whose 16-byte chunk j sits at
-// position j ^ (row & 7) (the XOR keeps the transposing stmatrix writes
-// conflict-free): every warp loads its core matrices of all four tiles into
-// registers, a barrier, then the transposed writes; ends with a barrier.
+// each in place, two 8 KB halves (channels 0..63, 64..127) of 64 token rows of
+// 128 bytes, 16-byte chunk j of row r at position j ^ (r & 7): the SWIZZLE_128B
+// image of an output store box (make_out_map), and conflict-free for the
+// transposing stmatrix writes.  Every warp loads its core matrices of all four
+// tiles into registers, a barrier, then the transposed writes and a proxy fence
+// (the tiles are read by TMA next); ends with a barrier.
 __device__ __forceinline__ void transpose4_to_rows_inplace(const uint32_t (&tile)[4], int warp, int lane) {
   uint32_t f[4][4][4];
   __syncthreads();  // every tile complete
@@ -318,18 +320,22 @@ __device__ __forceinline__ void transpose4_to_rows_inplace(const uint32_t (&tile
     for (int k = 0; k < 4; ++k) {
       const int j = 4 * warp + 32 * k + (lane >> 3), row = lane & 7;
       const int rg = j >> 3, c = 8 * (j & 7) + row;
-      stmatrix_x4_trans(tile[t] + (c << 8) + ((rg ^ (c & 7)) << 4), f[t][k]);
+      stmatrix_x4_trans(tile[t] + ((rg >> 3) << 13) + (c << 7) + (((rg & 7) ^ (c & 7)) << 4), f[t][k]);
     }
+  fence_async_smem();
   __syncthreads();
 }
 // Token rows (transpose4_to_rows_inplace) -> global rows (row r at dst + r*rstride),
-// 16 bytes per thread and store, rows >= rows_valid skipped.
+// 16 bytes per thread and store, rows >= rows_valid skipped: the path taken when
+// the shared memory is not 1024-byte aligned (the swizzle of a TMA store box
+// follows the absolute address).
 __device__ __forceinline__ void store_rows(bf16* dst, const unsigned char* rows, int rows_valid,
                                            size_t rstride) {
   for (int i = threadIdx.x; i < 64 * 16; i += NT) {
     const int r = i >> 4, j = i & 15;
     if (r < rows_valid)
-      *reinterpret_cast<uint4*>(dst + r * rstride + j * 8) = ld16(rows, (r << 8) + ((j ^ (r & 7)) << 4));
+      *reinterpret_cast<uint4*>(dst + r * rstride + j * 8) =
+          ld16(rows, ((j >> 3) << 13) + (r << 7) + (((j & 7) ^ (r & 7)) << 4));
   }
 }
 
@@ -378,8 +384,13 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
                int T, int H, int* __restrict__ err, const __grid_constant__ CUtensorMap tm_q,
                const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_g,
                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+               const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
+               const __grid_constant__ CUtensorMap tm_dv, const __grid_constant__ CUtensorMap tm_dg,
                int use_tma) {
   extern __shared__ __align__(1024) unsigned char sm[];
+  // dq, dk, dv, dg leave as TMA stores of 128-byte-swizzled boxes (issued by the
+  // copy thread, drained before the next unit's loads reuse the tiles)
+  const bool out_tma = use_tma && (smem_u32(sm) & 1023u) == 0u;
   float* beta_s = reinterpret_cast<float*>(sm + P_BETA);
   float* dgc = reinterpret_cast<float*>(sm + P_DGC);
   float* dbs = reinterpret_cast<float*>(sm + P_DB);
@@ -535,6 +546,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       cp_async_commit();
     }
     if (tid == kIoThread) {  // in the order they are needed: dO, dS' (dU group), then S_c
+      if (out_tma) bulk_wait_read();  // the previous unit's output stores read SQ, SK, SB
       fence_async_smem();
       mbar_expect_tx(mbar_late, WS_UNIT + (use_tma ? 16384 : 0));
       if (use_tma) tma_tile(sm + P_SQ, &tm_do, h, c, b, mbar_late);
@@ -956,11 +968,24 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       const uint32_t tiles[4] = {smem_u32(sm + P_SB), smem_u32(sm + P_SB + 16384), smem_u32(sm + P_SK),
                                  smem_u32(sm + P_SQ)};
       transpose4_to_rows_inplace(tiles, warp, lane);
-      const size_t obase = hoff + tok0 * rstride;
-      store_rows(dq + obase, sm + P_SB, rows_valid, rstride);
-      store_rows(dk + obase, sm + P_SB + 16384, rows_valid, rstride);
-      store_rows(dv + obase, sm + P_SK, rows_valid, rstride);
-      store_rows(dg + obase, sm + P_SQ, rows_valid, rstride);
+      if (out_tma) {
+        if (tid == kIoThread) {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            tma_out_store(&tm_dq, sm + P_SB + hf * 8192, 64 * hf, h, t0, b);
+            tma_out_store(&tm_dk, sm + P_SB + 16384 + hf * 8192, 64 * hf, h, t0, b);
+            tma_out_store(&tm_dv, sm + P_SK + hf * 8192, 64 * hf, h, t0, b);
+            tma_out_store(&tm_dg, sm + P_SQ + hf * 8192, 64 * hf, h, t0, b);
+          }
+          bulk_commit();
+        }
+      } else {
+        const size_t obase = hoff + tok0 * rstride;
+        store_rows(dq + obase, sm + P_SB, rows_valid, rstride);
+        store_rows(dk + obase, sm + P_SB + 16384, rows_valid, rstride);
+        store_rows(dv + obase, sm + P_SK, rows_valid, rstride);
+        store_rows(dg + obase, sm + P_SQ, rows_valid, rstride);
+      }
     }
     KDA_PT(2, 18);
     tc_fence_before();
@@ -979,6 +1004,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   if (late_pending) mbar_wait(mbar_late, late_par);
   if (sc_pending) mbar_wait(mbar_sc, sc_par);
   if (rs_pending) mbar_wait(mbar_rs, rs_par);
+  if (tid == kIoThread) bulk_wait_all();  // output stores
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1018,10 +1044,12 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
       static_cast<const unsigned char*>(s_ckpt) + static_cast<size_t>(B) * H * n * DK * DV * sizeof(Tc);
   // TMA tile maps of the inputs; any length or map the encoder refuses falls back
   // to cp.async staging inside the kernels
-  CUtensorMap tm[5] = {};
+  CUtensorMap tm[5] = {}, to[4] = {};
   const void* srcs[5] = {q, k, g, v, dout};
+  const void* outs[4] = {dq, dk_, dv_, dg};
   int use_tma = 1;
   for (int i = 0; i < 5 && use_tma; ++i) use_tma = make_tile_map(&tm[i], srcs[i], B, T, H) ? 1 : 0;
+  for (int i = 0; i < 4 && use_tma; ++i) use_tma = make_out_map(&to[i], outs[i], B, T, H) ? 1 : 0;
   bwd_seq_kernel<<<B * H, NT, SEQ_SMEM, st>>>(static_cast<const bf16*>(beta), static_cast<const bf16*>(dout),
                                               factors, dsT, ds0, dsw, T, H, err, tm[4], use_tma);
   rc = launch_status();
@@ -1033,7 +1061,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
       static_cast<const bf16*>(g), static_cast<const bf16*>(beta), static_cast<const Tc*>(s_ckpt),
       factors, dsw, static_cast<const bf16*>(dout), static_cast<bf16*>(dq), static_cast<bf16*>(dk_),
       static_cast<bf16*>(dv_), static_cast<bf16*>(dg), static_cast<bf16*>(dbeta), B, T, H, err,
-      tm[0], tm[1], tm[2], tm[3], tm[4], use_tma);
+      tm[0], tm[1], tm[2], tm[3], tm[4], to[0], to[1], to[2], to[3], use_tma);
   return launch_status();
 }
 

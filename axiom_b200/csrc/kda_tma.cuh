@@ -27,6 +27,13 @@ namespace kda {
 // encoder is unavailable or rejects the map.
 bool make_tile_map(CUtensorMap* map, const void* base, int B, int T, int H);
 
+// Store map of a [B, T, H, 128] bf16 output: 4-D (channel, head, token, batch),
+// box {64, 1, 64, 1} = 64 tokens x 64 channels of one head, SWIZZLE_128B: the
+// shared source is 64 rows of 128 bytes whose 16-byte chunk j sits at position
+// j ^ (row & 7).  Tokens past T are not written (any T).  Returns false when
+// the encoder is unavailable or rejects the map.
+bool make_out_map(CUtensorMap* map, const void* base, int B, int T, int H);
+
 namespace tc {
 // One [64][128] tile (16384 bytes) of head h, chunk c, batch b into `dst`
 // (1024-byte aligned shared memory); completes 16384 transaction bytes on `mbar`.
@@ -38,6 +45,16 @@ __device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, int 
       " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
       :: "r"(smem_u32(dst)), "l"(map), "r"(0), "r"(0), "r"(16 * h), "r"(8 * c), "r"(b),
          "r"(smem_u32(mbar))
+      : "memory");
+}
+// 64 tokens x 64 channels (8 KB, 1024-byte aligned shared memory, the
+// make_out_map layout) to channels [d0, d0 + 64) of head h, tokens [t0, t0 + 64)
+// of batch b.  Tracked by the issuing thread's bulk async-groups.
+__device__ __forceinline__ void tma_out_store(const CUtensorMap* map, const void* src, int d0, int h,
+                                              int t0, int b) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];"
+      :: "l"(map), "r"(d0), "r"(h), "r"(t0), "r"(b), "r"(smem_u32(src))
       : "memory");
 }
 }  // namespace tc
