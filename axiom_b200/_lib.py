@@ -1,4 +1,5 @@
-"""ctypes binding of ``libkda_b200.so`` (the C ABI declared in ``include/kda_b200.h``).
+"""ctypes binding of ``libkda_b200.so`` (the C ABI declared in ``include/kda_b200.h`` and
+``include/kda_mixer.h``).
 
 There is no fallback: if the library is missing or cannot be loaded, every
 entry point raises ``RuntimeError``.  Build it with ``python -m axiom_b200.build``.
@@ -17,6 +18,7 @@ KDA_BF16 = 1
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _Z = ctypes.c_size_t
+_F = ctypes.c_float
 
 #: every symbol the header declares, with its ctypes signature
 SIGNATURES = {
@@ -28,6 +30,13 @@ SIGNATURES = {
     "kda_bwd": ([_P] * 14 + [_P, _Z] + [_I] * 9 + [_P], _I),
     "kda_decode": ([_P] * 7 + [_I] * 5 + [_P], _I),
     "kda_bwd_noalloc": ([_P] * 14 + [_I] * 9 + [_P], _I),
+    # include/kda_mixer.h
+    "kda_prologue_fwd": ([_P] * 10 + [_F, _I] + [_P] * 3 + [_I] + [_P] * 5 + [_I] * 8 + [_P], _I),
+    "kda_prologue_bwd_workspace_bytes": ([_I] * 6, _Z),
+    "kda_prologue_bwd": ([_P] * 10 + [_F, _I, _P, _P, _I] + [_P] * 17 + [_Z] + [_I] * 8 + [_P], _I),
+    "kda_gated_rmsnorm_fwd": ([_P] * 3 + [_I] * 3 + [_F] + [_I] * 3 + [_P], _I),
+    "kda_gated_rmsnorm_bwd": ([_P] * 5 + [_I] * 3 + [_F] + [_I] * 3 + [_P], _I),
+    "kda_decode_fused": ([_P] * 13 + [_F, _I, _F, _P] + [_I] * 7 + [_P], _I),
 }
 
 _lib = None

@@ -1,0 +1,1051 @@
+// Per-token work around the KDA core (all HBM-bandwidth bound):
+//
+//   * prologue fwd/bwd: causal depthwise short conv + Swish + L2 norm (q, k),
+//     conv + Swish (v), sigmoid(beta), decay gate  (net/shortconv.py:14-30,
+//     net/kda.py:169-180, :194-203, net/norm.py:15-61);
+//   * output gate fwd/bwd: sigmoid(gate) * headwise_rms_norm(o)
+//     (net/kda.py:206-214, net/norm.py:70-73);
+//   * fused decode step: recurrent_step without the projection GEMMs
+//     (net/kda.py:277-295, net/shortconv.py:33-53).
+//
+// Prologue mapping: a warp owns a strip of 64 consecutive tokens of one head
+// and one tensor (block = 8 warps of the same head and tensor; blockIdx.z
+// picks q, k, v or the gates), each lane 2 or 4 adjacent channels, so a row of
+// the head (128 or 256 bytes) is one coalesced warp access and the L2 norm is
+// a warp reduction.  The conv window lives in registers: every input is read
+// once, plus K-1 halo rows per strip (L2 hits).  Loads of 8 tokens are issued
+// before their use to keep enough bytes in flight.  The backward sweeps each
+// strip from its end (plus K-1 halo tokens whose conv cotangents its inputs
+// need) to its start, so dx[t] = sum_i w[i] dc[t+i] is complete when t is
+// reached; weight gradients are reduced per block (4 warps) in shared
+// memory, then over blocks in a fixed order by a second kernel (deterministic).
+#include <climits>
+#include <type_traits>
+
+#include "kda_common.cuh"
+#include "kda_mixer.h"
+
+namespace kda {
+namespace {
+
+constexpr int kStrip = 64;   // tokens per warp strip
+constexpr int kWarps = 8;    // warps per prologue forward block
+constexpr int kBwdWarps = 4; // warps per backward block (more registers per thread)
+constexpr int kPre = 8;      // tokens whose loads are issued together
+constexpr float kL2Eps = 1e-12f;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+__device__ __forceinline__ float softplusf_(float x) { return fmaxf(x, 0.f) + log1pf(__expf(-fabsf(x))); }
+
+// CPL (2 or 4) consecutive elements <-> floats, one vector access
+template <int CPL>
+__device__ __forceinline__ void ldv(const float* p, float (&x)[CPL]) {
+  if constexpr (CPL == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    x[0] = t.x; x[1] = t.y; x[2] = t.z; x[3] = t.w;
+  } else {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    x[0] = t.x; x[1] = t.y;
+  }
+}
+template <int CPL>
+__device__ __forceinline__ void ldv(const bf16* p, float (&x)[CPL]) {
+  if constexpr (CPL == 4) {
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&t.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&t.y);
+    x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
+  } else {
+    const uint32_t t = *reinterpret_cast<const uint32_t*>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&t);
+    x[0] = __low2float(a); x[1] = __high2float(a);
+  }
+}
+template <int CPL>
+__device__ __forceinline__ void stv(float* p, const float (&x)[CPL]) {
+  if constexpr (CPL == 4) *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+  else *reinterpret_cast<float2*>(p) = make_float2(x[0], x[1]);
+}
+template <int CPL>
+__device__ __forceinline__ void stv(bf16* p, const float (&x)[CPL]) {
+  if constexpr (CPL == 4) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]), b = __floats2bfloat162_rn(x[2], x[3]);
+    uint2 t;
+    t.x = *reinterpret_cast<const uint32_t*>(&a);
+    t.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = t;
+  } else {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]);
+    *reinterpret_cast<uint32_t*>(p) = *reinterpret_cast<const uint32_t*>(&a);
+  }
+}
+
+// A row slice of CPL elements as loaded (packed bf16 pairs or floats), kept
+// packed while in flight and converted at use.
+template <typename T, int CPL> struct Raw;
+template <> struct Raw<bf16, 4> { uint2 v; };
+template <> struct Raw<bf16, 2> { uint32_t v; };
+template <> struct Raw<float, 4> { float4 v; };
+template <> struct Raw<float, 2> { float2 v; };
+template <int CPL, typename T>
+__device__ __forceinline__ Raw<T, CPL> ldr(const T* p) {
+  Raw<T, CPL> r;
+  r.v = *reinterpret_cast<const decltype(r.v)*>(p);
+  return r;
+}
+template <int CPL, typename T>
+__device__ __forceinline__ void cvt(const Raw<T, CPL>& r, float (&x)[CPL]) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float* f = reinterpret_cast<const float*>(&r.v);
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) x[c] = f[c];
+  } else {
+    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&r.v);
+#pragma unroll
+    for (int c = 0; c < CPL / 2; ++c) {
+      x[2 * c] = __low2float(p[c]);
+      x[2 * c + 1] = __high2float(p[c]);
+    }
+  }
+}
+
+struct ProArgs {
+  const void* x[4];  // qp, kp, vp, z
+  const void* beta_logit;
+  const float* w[3];  // conv_q, conv_k, conv_v
+  const float* b_gate;
+  const float* A;
+  float g_min;
+  int gate_kind;
+  const float* st_in;
+  float* st_out;
+  const int* cu;
+  int n_seqs;
+  void* y[4];  // q, k, v, g
+  void* beta;
+  // backward
+  const void* dy[4];  // dq, dk, dv, dg
+  const void* dbeta;
+  void* dx[4];  // dqp, dkp, dvp, dz
+  void* dbeta_logit;
+  float* dst;   // dconv_state_in
+  float* ws;    // per-block partial sums
+  int ws_stride;
+  int B, T, H, dk, dv, K;
+  int spb;      // strips per batch row
+  int n_strips;
+  int roles;    // tensor of each blockIdx.z, 4 bits each
+};
+
+// Element r (0..3) of a 4-pointer parameter array by selects: indexing the
+// kernel-parameter array with a runtime index would copy it to local memory.
+template <typename P>
+__device__ __forceinline__ P pick(const P (&p)[4], int r) {
+  return r == 0 ? p[0] : r == 1 ? p[1] : r == 2 ? p[2] : p[3];
+}
+template <typename P>
+__device__ __forceinline__ P pick(const P (&p)[3], int r) {
+  return r == 0 ? p[0] : r == 1 ? p[1] : p[2];
+}
+
+// Index of the packed sequence holding token t (cu_seqlens[i] <= t < cu_seqlens[i+1]).
+__device__ __forceinline__ int seq_of(const int* cu, int n, int t) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(cu + mid) <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// fp32 conv-state column of (role, head) and row width
+__device__ __forceinline__ int state_col(const ProArgs& a, int role) {
+  return role == 0 ? 0 : role == 1 ? a.H * a.dk : 2 * a.H * a.dk;
+}
+
+// The input x[t] of a strip's sequence for token t (t may be negative: the
+// conv state, or zero).  Rows are loaded only inside [0, T).
+template <int CPL, typename Tin>
+__device__ __forceinline__ void load_x(const ProArgs& a, const Tin* x, size_t row0, int HD, int ch, int b,
+                                       int role, int t, float (&v)[CPL]) {
+  if (t >= 0 && t < a.T) {
+    ldv<CPL>(x + (row0 + t) * HD + ch, v);
+  } else if (t < 0 && a.st_in && t >= -(a.K - 1)) {
+    const int sw = a.H * (2 * a.dk + a.dv);
+    ldv<CPL>(a.st_in + (static_cast<size_t>(b) * (a.K - 1) + t + a.K - 1) * sw + state_col(a, role) + ch, v);
+  } else {
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) v[c] = 0.f;
+  }
+}
+
+// ---------------------------------------------------------------- forward ----
+
+template <int CPL, typename Tin, typename Tout>
+__device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, int h, int lane) {
+  constexpr int D = CPL * 32;
+  const int HD = a.H * D;
+  const int ch = h * D + lane * CPL;
+  const size_t row0 = static_cast<size_t>(b) * a.T;
+  const Tin* x = static_cast<const Tin*>(pick(a.x, role));
+  Tout* y = static_cast<Tout*>(pick(a.y, role));
+  float wt[4][CPL];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) wt[i][c] = i < a.K ? pick(a.w, role)[i * HD + ch + c] : 0.f;
+  int si = 0, lb = 0, nb = INT_MAX;
+  if (a.cu) {
+    si = seq_of(a.cu, a.n_seqs, t0);
+    lb = __ldg(a.cu + si);
+    nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+  }
+  float hw[3][CPL];  // x[t-1], x[t-2], x[t-3]
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int t = t0 - 1 - j;
+    if (a.cu && t < lb) {
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
+    } else {
+      load_x<CPL>(a, x, row0, HD, ch, b, role, t, hw[j]);
+    }
+  }
+  for (int tb = t0; tb < t1; tb += kPre) {
+    Raw<Tin, CPL> xr[kPre];
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      if (tb + u < t1) xr[u] = ldr<CPL>(x + (row0 + tb + u) * HD + ch);
+    }
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      const int t = tb + u;
+      if (t < t1) {
+        float xv[CPL];
+        cvt<CPL>(xr[u], xv);
+        if (t == nb) {  // a packed sequence starts: the window restarts from zeros
+#pragma unroll
+          for (int j = 0; j < 3; ++j)
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
+          ++si;
+          nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+        }
+        float s[CPL];
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const float cv = wt[0][c] * xv[c] + wt[1][c] * hw[0][c] + wt[2][c] * hw[1][c] + wt[3][c] * hw[2][c];
+          hw[2][c] = hw[1][c];
+          hw[1][c] = hw[0][c];
+          hw[0][c] = xv[c];
+          s[c] = cv * sigmoidf_(cv);
+          ss += s[c] * s[c];
+        }
+        if (role < 2) {  // q, k: x / (|x| + eps)
+          const float inv = 1.f / (sqrtf(warp_sum(ss)) + kL2Eps);
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) s[c] *= inv;
+        }
+        stv<CPL>(y + (row0 + t) * HD + ch, s);
+      }
+    }
+  }
+  if (a.st_out && t1 == a.T) {  // this strip ends the sequence: its last K-1 inputs
+    const int sw = a.H * (2 * a.dk + a.dv);
+    for (int j = 0; j < a.K - 1; ++j) {
+      float v[CPL];
+      load_x<CPL>(a, x, row0, HD, ch, b, role, a.T - (a.K - 1) + j, v);
+      stv<CPL>(a.st_out + (static_cast<size_t>(b) * (a.K - 1) + j) * sw + state_col(a, role) + ch, v);
+    }
+  }
+}
+
+template <int CPL, typename Tin, typename Tout>
+__device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane) {
+  constexpr int D = CPL * 32;
+  const int HD = a.H * D;
+  const int ch = h * D + lane * CPL;
+  const size_t row0 = static_cast<size_t>(b) * a.T;
+  const Tin* z = static_cast<const Tin*>(a.x[3]);
+  Tout* g = static_cast<Tout*>(a.y[3]);
+  float bias[CPL];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) bias[c] = a.b_gate ? a.b_gate[ch + c] : 0.f;
+  const float ea = __expf(a.A[h]);
+  for (int tb = t0; tb < t1; tb += kPre) {
+    Raw<Tin, CPL> zr[kPre];
+#pragma unroll
+    for (int u = 0; u < kPre; ++u)
+      if (tb + u < t1) zr[u] = ldr<CPL>(z + (row0 + tb + u) * HD + ch);
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      if (tb + u < t1) {
+        float o[CPL], zv[CPL];
+        cvt<CPL>(zr[u], zv);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const float uu = zv[c] + bias[c];
+          o[c] = a.gate_kind == KDA_GATE_SIGMOID_MIN ? a.g_min * sigmoidf_(ea * uu) : -ea * softplusf_(uu);
+        }
+        stv<CPL>(g + (row0 + tb + u) * HD + ch, o);
+      }
+    }
+  }
+  const Tin* bl = static_cast<const Tin*>(a.beta_logit);
+  Tout* beta = static_cast<Tout*>(a.beta);
+  for (int t = t0 + lane; t < t1; t += 32) {
+    const size_t i = (row0 + t) * a.H + h;
+    stf(beta + i, sigmoidf_(ldf(bl + i)));
+  }
+}
+
+// blockIdx.z selects the tensor: role = 4-bit field z of a.roles (0 q, 1 k,
+// 2 v, 3 gates), so one launch covers the tensors of one width D = 32 CPL.
+template <int CPL, typename Tin, typename Tout>
+__global__ void __launch_bounds__(kWarps * 32) prologue_fwd_kernel(const ProArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s = blockIdx.x * kWarps + warp;
+  if (s >= a.n_strips) return;
+  const int h = blockIdx.y, role = (a.roles >> (4 * blockIdx.z)) & 15;
+  const int b = s / a.spb;
+  const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
+  if (role < 3) pro_fwd_conv<CPL, Tin, Tout>(a, role, b, t0, t1, h, lane);
+  else pro_fwd_gate<CPL, Tin, Tout>(a, b, t0, t1, h, lane);
+}
+
+// --------------------------------------------------------------- backward ----
+
+template <int CPL, typename Tin, typename Tout>
+__device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, int h, int lane,
+                             float (&dw)[4][4]) {
+  constexpr int D = CPL * 32;
+  const int HD = a.H * D;
+  const int ch = h * D + lane * CPL;
+  const size_t row0 = static_cast<size_t>(b) * a.T;
+  const Tin* x = static_cast<const Tin*>(pick(a.x, role));
+  const Tout* dy = static_cast<const Tout*>(pick(a.dy, role));
+  Tin* dx = static_cast<Tin*>(pick(a.dx, role));
+  const int K = a.K;
+  float wt[4][CPL];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) wt[i][c] = i < K ? pick(a.w, role)[i * HD + ch + c] : 0.f;
+  // sweep tau from hi (the last token whose conv cotangent the strip's inputs
+  // need) down to lo (t0, or -(K-1) when the strip writes the state's cotangent)
+  const int hi = min(t1 + K - 1, a.T) - 1;
+  const int lo = (t0 == 0 && a.dst && !a.cu) ? -(K - 1) : t0;
+  int si = 0, lb = INT_MIN;
+  if (a.cu) {
+    si = seq_of(a.cu, a.n_seqs, hi);
+    lb = __ldg(a.cu + si);
+  }
+  float xw[4][CPL];  // x[tau], x[tau-1], x[tau-2], x[tau-3]
+#pragma unroll
+  for (int i = 0; i < 4; ++i) load_x<CPL>(a, x, row0, HD, ch, b, role, hi - i, xw[i]);
+  float dcw[3][CPL];  // dc[tau+1], dc[tau+2], dc[tau+3]
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) dcw[j][c] = 0.f;
+  const int sw = a.H * (2 * a.dk + a.dv);
+  for (int base = hi; base >= lo; base -= kPre) {
+    Raw<Tin, CPL> xr[kPre];
+    Raw<Tout, CPL> dr[kPre];
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      const int tau = base - u;
+      if (tau - 4 >= 0) xr[u] = ldr<CPL>(x + (row0 + tau - 4) * HD + ch);
+      if (tau >= 0 && tau >= lo) dr[u] = ldr<CPL>(dy + (row0 + tau) * HD + ch);
+    }
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      const int tau = base - u;
+      if (tau >= lo) {
+        float xn[CPL], dv[CPL];
+        if (tau - 4 >= 0) cvt<CPL>(xr[u], xn);
+        else load_x<CPL>(a, x, row0, HD, ch, b, role, tau - 4, xn);  // the conv state, or zero
+        if (tau >= 0) cvt<CPL>(dr[u], dv);
+        float xm[4][CPL];  // window masked at the sequence start
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const bool ok = tau - i >= lb;
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) xm[i][c] = ok ? xw[i][c] : 0.f;
+        }
+        float dc[CPL];
+        if (tau >= 0) {
+          float cv[CPL], s[CPL], sg[CPL];
+          float ss = 0.f, sd = 0.f;
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) {
+            cv[c] = wt[0][c] * xm[0][c] + wt[1][c] * xm[1][c] + wt[2][c] * xm[2][c] + wt[3][c] * xm[3][c];
+            const float sig = sigmoidf_(cv[c]);
+            s[c] = cv[c] * sig;
+            sg[c] = sig * (1.f + cv[c] * (1.f - sig));
+            ss += s[c] * s[c];
+            sd += s[c] * dv[c];
+          }
+          if (role < 2) {  // cotangent of x / (|x| + eps); zero at x = 0
+            const float n = sqrtf(warp_sum(ss));
+            const float p = warp_sum(sd);
+            const float den = n + kL2Eps;
+            const float pr = n > 0.f ? p / n : 0.f;
+#pragma unroll
+            for (int c = 0; c < CPL; ++c)
+              dc[c] = (n > 0.f ? (dv[c] - s[c] * pr / den) / den : 0.f) * sg[c];
+          } else {
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) dc[c] = dv[c] * sg[c];
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) dc[c] = 0.f;
+        }
+        if (tau < t1) {
+          float o[CPL];
+#pragma unroll
+          for (int c = 0; c < CPL; ++c)
+            o[c] = wt[0][c] * dc[c] + wt[1][c] * dcw[0][c] + wt[2][c] * dcw[1][c] + wt[3][c] * dcw[2][c];
+          if (tau >= t0) {
+            stv<CPL>(dx + (row0 + tau) * HD + ch, o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int c = 0; c < CPL; ++c) dw[i][c] += dc[c] * xm[i][c];
+          } else {  // tau < 0: cotangent of the conv state row
+            stv<CPL>(a.dst + (static_cast<size_t>(b) * (K - 1) + tau + K - 1) * sw + state_col(a, role) + ch, o);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          dcw[2][c] = dcw[1][c];
+          dcw[1][c] = dcw[0][c];
+          dcw[0][c] = dc[c];
+          xw[0][c] = xw[1][c];
+          xw[1][c] = xw[2][c];
+          xw[2][c] = xw[3][c];
+          xw[3][c] = xn[c];
+        }
+        if (a.cu && tau == lb && si > 0) {  // below tau lies the previous sequence
+#pragma unroll
+          for (int j = 0; j < 3; ++j)
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) dcw[j][c] = 0.f;
+          --si;
+          lb = __ldg(a.cu + si);
+        }
+      }
+    }
+  }
+}
+
+template <int CPL, typename Tin, typename Tout>
+__device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane, float (&db)[4],
+                             float& dA) {
+  constexpr int D = CPL * 32;
+  const int HD = a.H * D;
+  const int ch = h * D + lane * CPL;
+  const size_t row0 = static_cast<size_t>(b) * a.T;
+  const Tin* z = static_cast<const Tin*>(a.x[3]);
+  const Tout* dg = static_cast<const Tout*>(a.dy[3]);
+  Tin* dz = static_cast<Tin*>(a.dx[3]);
+  float bias[CPL];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) bias[c] = a.b_gate ? a.b_gate[ch + c] : 0.f;
+  const float ea = __expf(a.A[h]);
+  for (int tb = t0; tb < t1; tb += kPre) {
+    Raw<Tin, CPL> zr[kPre];
+    Raw<Tout, CPL> gr[kPre];
+#pragma unroll
+    for (int u = 0; u < kPre; ++u)
+      if (tb + u < t1) {
+        zr[u] = ldr<CPL>(z + (row0 + tb + u) * HD + ch);
+        gr[u] = ldr<CPL>(dg + (row0 + tb + u) * HD + ch);
+      }
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      if (tb + u < t1) {
+        float o[CPL], zv[CPL], gv[CPL];
+        cvt<CPL>(zr[u], zv);
+        cvt<CPL>(gr[u], gv);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const float uu = zv[c] + bias[c];
+          if (a.gate_kind == KDA_GATE_SIGMOID_MIN) {
+            const float sg = sigmoidf_(ea * uu);
+            const float t = gv[c] * a.g_min * sg * (1.f - sg) * ea;
+            o[c] = t;
+            dA += t * uu;
+          } else {
+            o[c] = -gv[c] * ea * sigmoidf_(uu);
+            dA -= gv[c] * ea * softplusf_(uu);
+          }
+          db[c] += o[c];
+        }
+        stv<CPL>(dz + (row0 + tb + u) * HD + ch, o);
+      }
+    }
+  }
+  const Tin* bl = static_cast<const Tin*>(a.beta_logit);
+  const Tout* dbt = static_cast<const Tout*>(a.dbeta);
+  Tin* dbl = static_cast<Tin*>(a.dbeta_logit);
+  for (int t = t0 + lane; t < t1; t += 32) {
+    const size_t i = (row0 + t) * a.H + h;
+    const float s = sigmoidf_(ldf(bl + i));
+    stf(dbl + i, ldf(dbt + i) * s * (1.f - s));
+  }
+}
+
+// Partial-sum slab of one block group: [q taps K x H*dk | k taps | v taps K x H*dv | db H*dk | dA H]
+__host__ __device__ inline int slab_off(int role, int H, int dk, int K) {
+  return role == 0 ? 0 : role == 1 ? K * H * dk : role == 2 ? 2 * K * H * dk : -1;
+}
+
+template <int CPL, typename Tin, typename Tout>
+__global__ void __launch_bounds__(kBwdWarps * 32) prologue_bwd_kernel(const ProArgs a) {
+  __shared__ float red[kBwdWarps][4][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s = blockIdx.x * kBwdWarps + warp;
+  const int h = blockIdx.y, role = (a.roles >> (4 * blockIdx.z)) & 15;
+  constexpr int D = CPL * 32;
+  float acc[4][4] = {};
+  float dA = 0.f;
+  if (s < a.n_strips) {
+    const int b = s / a.spb;
+    const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
+    if (role < 3) pro_bwd_conv<CPL, Tin, Tout>(a, role, b, t0, t1, h, lane, acc);
+    else pro_bwd_gate<CPL, Tin, Tout>(a, b, t0, t1, h, lane, acc[0], dA);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if (c < CPL) red[warp][i][lane * CPL + c] = acc[i][c];
+  dA = warp_sum(dA);
+  if (role == 3 && lane == 0) red[warp][1][0] = dA;
+  __syncthreads();
+  float* slab = a.ws + static_cast<size_t>(blockIdx.x) * a.ws_stride;
+  if (role < 3) {
+    const int HD = a.H * D;
+    for (int e = threadIdx.x; e < a.K * D; e += blockDim.x) {
+      const int i = e / D, c = e % D;
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kBwdWarps; ++w) sum += red[w][i][c];
+      slab[slab_off(role, a.H, a.dk, a.K) + i * HD + h * D + c] = sum;
+    }
+  } else {
+    const int db_off = 2 * a.K * a.H * a.dk + a.K * a.H * a.dv;
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kBwdWarps; ++w) sum += red[w][0][c];
+      slab[db_off + h * D + c] = sum;
+    }
+    if (threadIdx.x == 0) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kBwdWarps; ++w) sum += red[w][1][0];
+      slab[db_off + a.H * a.dk + h] = sum;
+    }
+  }
+}
+
+// Sum the per-group slabs (fixed order) into the weight gradients.
+__global__ void prologue_reduce_kernel(const float* __restrict__ ws, int groups, int stride, int H, int dk,
+                                       int dv, int K, float* dwq, float* dwk, float* dwv, float* db,
+                                       float* dA) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= stride) return;
+  float sum = 0.f;
+  for (int g = 0; g < groups; ++g) sum += ws[static_cast<size_t>(g) * stride + e];
+  const int nq = K * H * dk, nv = K * H * dv;
+  if (e < nq) dwq[e] = sum;
+  else if (e < 2 * nq) dwk[e - nq] = sum;
+  else if (e < 2 * nq + nv) dwv[e - 2 * nq] = sum;
+  else if (e < 2 * nq + nv + H * dk) db[e - 2 * nq - nv] = sum;
+  else dA[e - 2 * nq - nv - H * dk] = sum;
+}
+
+// ------------------------------------------------------------ output gate ----
+
+template <int CPL, typename To, typename Tg, typename Ty>
+__global__ void __launch_bounds__(256) gated_rms_fwd_kernel(const To* __restrict__ o, const Tg* __restrict__ gate,
+                                                            Ty* __restrict__ y, long long rows, float eps) {
+  constexpr int D = CPL * 32;
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += nw) {
+    const size_t off = static_cast<size_t>(r) * D + lane * CPL;
+    float ov[CPL], gv[CPL];
+    ldv<CPL>(o + off, ov);
+    ldv<CPL>(gate + off, gv);
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) ss += ov[c] * ov[c];
+    const float rr = 1.f / sqrtf(warp_sum(ss) / D + eps);
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) ov[c] = sigmoidf_(gv[c]) * ov[c] * rr;
+    stv<CPL>(y + off, ov);
+  }
+}
+
+template <int CPL, typename To, typename Tg, typename Ty>
+__global__ void __launch_bounds__(256) gated_rms_bwd_kernel(const To* __restrict__ o, const Tg* __restrict__ gate,
+                                                            const Ty* __restrict__ dy, To* __restrict__ dout,
+                                                            Tg* __restrict__ dgate, long long rows, float eps) {
+  constexpr int D = CPL * 32;
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += nw) {
+    const size_t off = static_cast<size_t>(r) * D + lane * CPL;
+    float ov[CPL], gv[CPL], dv[CPL];
+    ldv<CPL>(o + off, ov);
+    ldv<CPL>(gate + off, gv);
+    ldv<CPL>(dy + off, dv);
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) ss += ov[c] * ov[c];
+    const float rr = 1.f / sqrtf(warp_sum(ss) / D + eps);
+    float dn[CPL], dg[CPL], m = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      const float n = ov[c] * rr, s = sigmoidf_(gv[c]);
+      dg[c] = dv[c] * n * s * (1.f - s);
+      dn[c] = dv[c] * s;
+      m += dn[c] * n;
+    }
+    m = warp_sum(m) / D;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) dn[c] = rr * (dn[c] - ov[c] * rr * m);
+    stv<CPL>(dout + off, dn);
+    stv<CPL>(dgate + off, dg);
+  }
+}
+
+// ------------------------------------------------------------ fused decode ----
+
+struct DecArgs {
+  float* S;
+  float* buf;
+  const void* qp;
+  const void* kp;
+  const void* vp;
+  const void* z;
+  const void* beta_logit;
+  const void* gate;
+  const float* w[3];
+  const float* b_gate;
+  const float* A;
+  float g_min;
+  int gate_kind;
+  float rms_eps;
+  void* out;
+  int H, K;
+};
+
+constexpr int kDecThreads = 256;
+
+// One CTA per (sequence, head).  The state read is issued first; meanwhile
+// threads [0, DK) form q, k, g of channel d and threads [DK, DK + DV) v of
+// channel d - DK from the projections and the conv buffer (shifted in place,
+// each thread its own channel); then the delta-rule update of the decode step
+// (r = (alpha k)^T S, S' = alpha S + beta k (v - r)^T, o = S'^T q).
+template <int DK, int DV, typename Tin, typename To>
+__global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecArgs a) {
+  static_assert(DK + DV <= kDecThreads, "one thread per q/k/g and per v channel");
+  constexpr int TPR = DV / 4;
+  constexpr int RPP = kDecThreads / TPR;
+  constexpr int NR = DK / RPP;
+  __shared__ float s_ak[DK], s_a[DK], s_bk[DK], s_q[DK], s_v[DV];
+  __shared__ float s_red[RPP][DV];
+  __shared__ float s_nrm[2][8];
+  __shared__ float s_beta;
+  const int n = blockIdx.x / a.H, h = blockIdx.x % a.H;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int col = (tid % TPR) * 4, row0 = tid / TPR;
+  float4* Sn = reinterpret_cast<float4*>(a.S + static_cast<size_t>(blockIdx.x) * DK * DV);
+  float4 s[NR];
+#pragma unroll
+  for (int m = 0; m < NR; ++m) s[m] = Sn[((row0 + m * RPP) * DV + col) / 4];
+
+  // ---- prologue of this token: conv step, Swish, gates ----
+  const int HK = a.H * DK, HV = a.H * DV;
+  const int sw = 2 * HK + HV;
+  float* bufn = a.buf ? a.buf + static_cast<size_t>(n) * (a.K - 1) * sw : nullptr;
+  auto conv_step = [&](const Tin* xp, const float* w, int stride_x, int col_buf, int c) -> float {
+    const float xt = ldf(xp + static_cast<size_t>(n) * stride_x + c);
+    float acc = w[c] * xt;  // w[0] x_t + sum_j w[K-1-j] buf[j]
+    float prev = xt;
+    for (int j = a.K - 2; j >= 0; --j) {  // newest first; shift the rows up in place
+      float* p = bufn + static_cast<size_t>(j) * sw + col_buf + c;
+      const float bj = *p;
+      acc += w[(a.K - 1 - j) * stride_x + c] * bj;
+      *p = prev;
+      prev = bj;
+    }
+    return acc;
+  };
+  float qv = 0.f, kv = 0.f;
+  if (tid < DK) {
+    const int c = h * DK + tid;
+    const float cq = conv_step(static_cast<const Tin*>(a.qp), a.w[0], HK, 0, c);
+    const float ck = conv_step(static_cast<const Tin*>(a.kp), a.w[1], HK, HK, c);
+    qv = cq * sigmoidf_(cq);
+    kv = ck * sigmoidf_(ck);
+    const float u = ldf(static_cast<const Tin*>(a.z) + static_cast<size_t>(n) * HK + c) + (a.b_gate ? a.b_gate[c] : 0.f);
+    const float ea = __expf(a.A[h]);
+    const float g = a.gate_kind == KDA_GATE_SIGMOID_MIN ? a.g_min * sigmoidf_(ea * u) : -ea * softplusf_(u);
+    s_a[tid] = __expf(g);
+    const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
+    if (lane == 0) {
+      s_nrm[0][warp] = sq;
+      s_nrm[1][warp] = sk;
+    }
+  } else if (tid < DK + DV) {
+    const int c = h * DV + tid - DK;
+    const float cv = conv_step(static_cast<const Tin*>(a.vp), a.w[2], HV, 2 * HK, c);
+    s_v[tid - DK] = cv * sigmoidf_(cv);
+  }
+  if (tid == kDecThreads - 1)
+    s_beta = sigmoidf_(ldf(static_cast<const Tin*>(a.beta_logit) + static_cast<size_t>(n) * a.H + h));
+  __syncthreads();
+  if (tid < DK) {
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int w = 0; w < DK / 32; ++w) {
+      sq += s_nrm[0][w];
+      sk += s_nrm[1][w];
+    }
+    const float q = qv / (sqrtf(sq) + kL2Eps), k = kv / (sqrtf(sk) + kL2Eps);
+    s_q[tid] = q;
+    s_ak[tid] = s_a[tid] * k;
+    s_bk[tid] = s_beta * k;
+  }
+  __syncthreads();
+
+  // ---- delta-rule update ----
+  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int m = 0; m < NR; ++m) {
+    const float w = s_ak[row0 + m * RPP];
+    r.x += w * s[m].x; r.y += w * s[m].y; r.z += w * s[m].z; r.w += w * s[m].w;
+  }
+  *reinterpret_cast<float4*>(&s_red[row0][col]) = r;
+  __syncthreads();
+  r = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int p = 0; p < RPP; ++p) {
+    const float4 t = *reinterpret_cast<const float4*>(&s_red[p][col]);
+    r.x += t.x; r.y += t.y; r.z += t.z; r.w += t.w;
+  }
+  const float4 u = make_float4(s_v[col] - r.x, s_v[col + 1] - r.y, s_v[col + 2] - r.z, s_v[col + 3] - r.w);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int m = 0; m < NR; ++m) {
+    const int d = row0 + m * RPP;
+    const float al = s_a[d], bk = s_bk[d], qd = s_q[d];
+    float4 t;
+    t.x = al * s[m].x + bk * u.x; t.y = al * s[m].y + bk * u.y;
+    t.z = al * s[m].z + bk * u.z; t.w = al * s[m].w + bk * u.w;
+    Sn[(d * DV + col) / 4] = t;
+    acc.x += qd * t.x; acc.y += qd * t.y; acc.z += qd * t.z; acc.w += qd * t.w;
+  }
+  __syncthreads();
+  *reinterpret_cast<float4*>(&s_red[row0][col]) = acc;
+  __syncthreads();
+  if (tid < TPR) {  // one warp (DV = 128) or half a warp (DV = 64) holds o
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int p = 0; p < RPP; ++p) {
+      const float4 x = *reinterpret_cast<const float4*>(&s_red[p][col]);
+      o[0] += x.x; o[1] += x.y; o[2] += x.z; o[3] += x.w;
+    }
+    if (a.gate) {  // sigmoid(gate) * o / sqrt(mean(o^2) + eps)
+      float ss = o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3];
+#pragma unroll
+      for (int off = TPR / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(TPR == 32 ? 0xffffffffu : 0xffffu, ss, off);
+      const float rr = 1.f / sqrtf(ss / DV + a.rms_eps);
+      const Tin* gp = static_cast<const Tin*>(a.gate) + static_cast<size_t>(n) * HV + h * DV + col;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = sigmoidf_(ldf(gp + j)) * o[j] * rr;
+    }
+    To* on = static_cast<To*>(a.out) + static_cast<size_t>(blockIdx.x) * DV + col;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) stf(on + j, o[j]);
+  }
+}
+
+template <int CPL, typename Tin, typename Tout>
+int launch_prologue_d(ProArgs& a, int roles, int n_roles, bool bwd, cudaStream_t st) {
+  a.roles = roles;
+  const int w = bwd ? kBwdWarps : kWarps;
+  const dim3 grid((a.n_strips + w - 1) / w, a.H, n_roles);
+  if (bwd) prologue_bwd_kernel<CPL, Tin, Tout><<<grid, w * 32, 0, st>>>(a);
+  else prologue_fwd_kernel<CPL, Tin, Tout><<<grid, w * 32, 0, st>>>(a);
+  return launch_status();
+}
+
+// q, k and the gates have width dk, v has dv: one launch when they agree.
+template <typename Tin, typename Tout>
+int launch_prologue(ProArgs& a, bool bwd, cudaStream_t st) {
+  auto launch = [&](int D, int roles, int n) {
+    return D == 128 ? launch_prologue_d<4, Tin, Tout>(a, roles, n, bwd, st)
+                    : launch_prologue_d<2, Tin, Tout>(a, roles, n, bwd, st);
+  };
+  if (a.dk == a.dv) return launch(a.dk, 0x3210, 4);
+  const int rc = launch(a.dk, 0x310, 3);
+  return rc != KDA_OK ? rc : launch(a.dv, 0x2, 1);
+}
+
+template <int CPL, typename To, typename Tg, typename Ty>
+int launch_grms(const void* o, const void* gate, const void* dy, void* y, void* dout, void* dgate,
+                long long rows, float eps, bool bwd, cudaStream_t st) {
+  const long long want = (rows + 7) / 8;
+  const int grid = static_cast<int>(want < 148LL * 16 ? want : 148LL * 16);
+  if (bwd)
+    gated_rms_bwd_kernel<CPL, To, Tg, Ty><<<grid, 256, 0, st>>>(
+        static_cast<const To*>(o), static_cast<const Tg*>(gate), static_cast<const Ty*>(dy),
+        static_cast<To*>(dout), static_cast<Tg*>(dgate), rows, eps);
+  else
+    gated_rms_fwd_kernel<CPL, To, Tg, Ty><<<grid, 256, 0, st>>>(
+        static_cast<const To*>(o), static_cast<const Tg*>(gate), static_cast<Ty*>(y), rows, eps);
+  return launch_status();
+}
+
+template <int CPL>
+int grms_types(const void* o, const void* gate, const void* dy, void* y, void* dout, void* dgate, long long rows,
+               float eps, int odt, int gdt, int ydt, bool bwd, cudaStream_t st) {
+  // o and y in either type; the gate logits in either type
+#define KDA_GRMS(TO, TG, TY)                                                                               \
+  if (odt == (std::is_same<TO, float>::value ? KDA_F32 : KDA_BF16) &&                                      \
+      gdt == (std::is_same<TG, float>::value ? KDA_F32 : KDA_BF16) &&                                      \
+      ydt == (std::is_same<TY, float>::value ? KDA_F32 : KDA_BF16))                                        \
+    return launch_grms<CPL, TO, TG, TY>(o, gate, dy, y, dout, dgate, rows, eps, bwd, st);
+  KDA_GRMS(float, float, float)
+  KDA_GRMS(float, float, bf16)
+  KDA_GRMS(float, bf16, float)
+  KDA_GRMS(float, bf16, bf16)
+  KDA_GRMS(bf16, float, float)
+  KDA_GRMS(bf16, float, bf16)
+  KDA_GRMS(bf16, bf16, float)
+  KDA_GRMS(bf16, bf16, bf16)
+#undef KDA_GRMS
+  return KDA_ERR_DTYPE;
+}
+
+template <int DK, int DV>
+int dec_types(const DecArgs& a, int N, int in_dt, int o_dt, cudaStream_t st) {
+  const int grid = N * a.H;
+  if (in_dt == KDA_BF16 && o_dt == KDA_BF16) decode_fused_kernel<DK, DV, bf16, bf16><<<grid, kDecThreads, 0, st>>>(a);
+  else if (in_dt == KDA_BF16 && o_dt == KDA_F32) decode_fused_kernel<DK, DV, bf16, float><<<grid, kDecThreads, 0, st>>>(a);
+  else if (in_dt == KDA_F32 && o_dt == KDA_F32) decode_fused_kernel<DK, DV, float, float><<<grid, kDecThreads, 0, st>>>(a);
+  else if (in_dt == KDA_F32 && o_dt == KDA_BF16) decode_fused_kernel<DK, DV, float, bf16><<<grid, kDecThreads, 0, st>>>(a);
+  else return KDA_ERR_DTYPE;
+  return launch_status();
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- entry points ----
+
+int prologue_launch(ProArgs& a, int in_dt, int out_dt, bool bwd, cudaStream_t st) {
+  if (in_dt == KDA_BF16 && out_dt == KDA_BF16) return launch_prologue<bf16, bf16>(a, bwd, st);
+  if (in_dt == KDA_BF16 && out_dt == KDA_F32) return launch_prologue<bf16, float>(a, bwd, st);
+  if (in_dt == KDA_F32 && out_dt == KDA_F32) return launch_prologue<float, float>(a, bwd, st);
+  if (in_dt == KDA_F32 && out_dt == KDA_BF16) return launch_prologue<float, bf16>(a, bwd, st);
+  return KDA_ERR_DTYPE;
+}
+
+}  // namespace kda
+
+namespace {
+
+bool valid_dt(int d) { return d == KDA_F32 || d == KDA_BF16; }
+bool d_ok(int d) { return d == 64 || d == 128; }
+
+// Shared validation of the prologue's dimensions and pointers.
+int prologue_check(const void* qp, const void* kp, const void* vp, const void* z, const void* bl,
+                   const float* cq, const float* ck, const float* cv, const float* A, int kind,
+                   const float* st_in, const float* st_out, const int* cu, int n_seqs, int B, int T, int H,
+                   int dk, int dv, int K, int in_dt, int out_dt) {
+  if (B < 0 || T < 0 || H < 0 || H > 65535 || K < 1 || K > 4 || !d_ok(dk) || !d_ok(dv)) return KDA_ERR_SHAPE;
+  if (!valid_dt(in_dt) || !valid_dt(out_dt)) return KDA_ERR_DTYPE;
+  if (kind != KDA_GATE_SIGMOID_MIN && kind != KDA_GATE_SOFTPLUS) return KDA_ERR_SHAPE;
+  if (cu && (B != 1 || n_seqs < 1 || st_in || st_out)) return KDA_ERR_SHAPE;
+  if (B == 0 || T == 0 || H == 0) return KDA_OK;
+  if (!qp || !kp || !vp || !z || !bl || !cq || !ck || !cv || !A) return KDA_ERR_NULL;
+  const void* al[] = {qp, kp, vp, z, st_in, st_out};
+  for (const void* p : al)
+    if (p && !kda::aligned16(p)) return KDA_ERR_ALIGN;
+  const long long strips = static_cast<long long>(B) * ((T + kda::kStrip - 1) / kda::kStrip);
+  if (strips > 0x7fffffffLL) return KDA_ERR_SHAPE;
+  return KDA_OK;
+}
+
+kda::ProArgs base_args(const void* qp, const void* kp, const void* vp, const void* z, const void* bl,
+                       const float* cq, const float* ck, const float* cv, const float* b_gate,
+                       const float* A, float g_min, int kind, const float* st_in, const int* cu,
+                       int n_seqs, int B, int T, int H, int dk, int dv, int K) {
+  kda::ProArgs a{};
+  a.x[0] = qp; a.x[1] = kp; a.x[2] = vp; a.x[3] = z;
+  a.beta_logit = bl;
+  a.w[0] = cq; a.w[1] = ck; a.w[2] = cv;
+  a.b_gate = b_gate; a.A = A; a.g_min = g_min; a.gate_kind = kind;
+  a.st_in = st_in; a.cu = cu; a.n_seqs = n_seqs;
+  a.B = B; a.T = T; a.H = H; a.dk = dk; a.dv = dv; a.K = K;
+  a.spb = (T + kda::kStrip - 1) / kda::kStrip;
+  a.n_strips = B * a.spb;
+  return a;
+}
+
+int ws_stride(int H, int dk, int dv, int K) { return 2 * K * H * dk + K * H * dv + H * dk + H; }
+size_t ws_groups(int B, int T) {
+  const size_t strips = static_cast<size_t>(B) * ((static_cast<size_t>(T) + kda::kStrip - 1) / kda::kStrip);
+  return (strips + kda::kBwdWarps - 1) / kda::kBwdWarps;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kda_prologue_fwd(const void* qp, const void* kp, const void* vp, const void* z, const void* beta_logit,
+                     const float* conv_q, const float* conv_k, const float* conv_v, const float* b_gate,
+                     const float* A, float g_min, int gate_kind, const float* conv_state_in,
+                     float* conv_state_out, const int* cu_seqlens, int n_seqs, void* q, void* k, void* v,
+                     void* g, void* beta, int B, int T, int H, int dk, int dv, int K, int in_dtype,
+                     int out_dtype, kda_stream_t stream) {
+  int rc = prologue_check(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, gate_kind, conv_state_in,
+                          conv_state_out, cu_seqlens, n_seqs, B, T, H, dk, dv, K, in_dtype, out_dtype);
+  if (rc != KDA_OK || B == 0 || T == 0 || H == 0) return rc;
+  if (!q || !k || !v || !g || !beta) return KDA_ERR_NULL;
+  const void* al[] = {q, k, v, g};
+  for (const void* p : al)
+    if (!kda::aligned16(p)) return KDA_ERR_ALIGN;
+  kda::ProArgs a = base_args(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, b_gate, A, g_min, gate_kind,
+                             conv_state_in, cu_seqlens, n_seqs, B, T, H, dk, dv, K);
+  a.st_out = conv_state_out;
+  a.y[0] = q; a.y[1] = k; a.y[2] = v; a.y[3] = g;
+  a.beta = beta;
+  return kda::prologue_launch(a, in_dtype, out_dtype, false, stream);
+}
+
+size_t kda_prologue_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int K) {
+  if (B < 0 || T < 0 || H < 0 || K < 1 || K > 4 || !d_ok(dk) || !d_ok(dv)) return 0;
+  return ws_groups(B, T) * static_cast<size_t>(ws_stride(H, dk, dv, K)) * sizeof(float);
+}
+
+int kda_prologue_bwd(const void* qp, const void* kp, const void* vp, const void* z, const void* beta_logit,
+                     const float* conv_q, const float* conv_k, const float* conv_v, const float* b_gate,
+                     const float* A, float g_min, int gate_kind, const float* conv_state_in,
+                     const int* cu_seqlens, int n_seqs, const void* dq, const void* dk_, const void* dv_,
+                     const void* dg, const void* dbeta, void* dqp, void* dkp, void* dvp, void* dz,
+                     void* dbeta_logit, float* dconv_q, float* dconv_k, float* dconv_v, float* db_gate,
+                     float* dA, float* dconv_state_in, void* workspace, size_t workspace_bytes, int B, int T,
+                     int H, int dk, int dv, int K, int in_dtype, int out_dtype, kda_stream_t stream) {
+  int rc = prologue_check(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, gate_kind, conv_state_in,
+                          dconv_state_in, cu_seqlens, n_seqs, B, T, H, dk, dv, K, in_dtype, out_dtype);
+  if (rc != KDA_OK) return rc;
+  if (!dconv_q || !dconv_k || !dconv_v || !db_gate || !dA) return KDA_ERR_NULL;
+  const size_t nq = static_cast<size_t>(K) * H * dk, nv = static_cast<size_t>(K) * H * dv;
+  if (B == 0 || T == 0 || H == 0) {  // no tokens: zero gradients
+    cudaError_t e = cudaMemsetAsync(dconv_q, 0, nq * 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dconv_k, 0, nq * 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dconv_v, 0, nv * 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(db_gate, 0, static_cast<size_t>(H) * dk * 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dA, 0, static_cast<size_t>(H) * 4, stream);
+    if (e == cudaSuccess && dconv_state_in && B > 0 && K > 1)
+      e = cudaMemsetAsync(dconv_state_in, 0, static_cast<size_t>(B) * (K - 1) * H * (2 * dk + dv) * 4, stream);
+    return e == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+  }
+  if (!dq || !dk_ || !dv_ || !dg || !dbeta || !dqp || !dkp || !dvp || !dz || !dbeta_logit) return KDA_ERR_NULL;
+  const void* al[] = {dq, dk_, dv_, dg, dqp, dkp, dvp, dz, dconv_state_in};
+  for (const void* p : al)
+    if (p && !kda::aligned16(p)) return KDA_ERR_ALIGN;
+  const size_t need = kda_prologue_bwd_workspace_bytes(B, T, H, dk, dv, K);
+  if (!workspace || workspace_bytes < need) return KDA_ERR_WORKSPACE;
+  kda::ProArgs a = base_args(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, b_gate, A, g_min, gate_kind,
+                             conv_state_in, cu_seqlens, n_seqs, B, T, H, dk, dv, K);
+  a.dy[0] = dq; a.dy[1] = dk_; a.dy[2] = dv_; a.dy[3] = dg;
+  a.dbeta = dbeta;
+  a.dx[0] = dqp; a.dx[1] = dkp; a.dx[2] = dvp; a.dx[3] = dz;
+  a.dbeta_logit = dbeta_logit;
+  a.dst = K > 1 ? dconv_state_in : nullptr;
+  a.ws = static_cast<float*>(workspace);
+  a.ws_stride = ws_stride(H, dk, dv, K);
+  if (dconv_state_in && K == 1) {
+    // K = 1 has no conv state; nothing to write
+  }
+  rc = kda::prologue_launch(a, in_dtype, out_dtype, true, stream);
+  if (rc != KDA_OK) return rc;
+  const int groups = static_cast<int>(ws_groups(B, T));
+  kda::prologue_reduce_kernel<<<(a.ws_stride + 255) / 256, 256, 0, stream>>>(
+      a.ws, groups, a.ws_stride, H, dk, dv, K, dconv_q, dconv_k, dconv_v, db_gate, dA);
+  return kda::launch_status();
+}
+
+int kda_gated_rmsnorm_fwd(const void* o, const void* gate, void* y, int N, int H, int dv, float eps, int o_dtype,
+                          int gate_dtype, int y_dtype, kda_stream_t stream) {
+  if (N < 0 || H < 0 || !d_ok(dv)) return KDA_ERR_SHAPE;
+  if (!valid_dt(o_dtype) || !valid_dt(gate_dtype) || !valid_dt(y_dtype)) return KDA_ERR_DTYPE;
+  if (N == 0 || H == 0) return KDA_OK;
+  if (!o || !gate || !y) return KDA_ERR_NULL;
+  if (!kda::aligned16(o) || !kda::aligned16(gate) || !kda::aligned16(y)) return KDA_ERR_ALIGN;
+  const long long rows = static_cast<long long>(N) * H;
+  return dv == 128 ? kda::grms_types<4>(o, gate, nullptr, y, nullptr, nullptr, rows, eps, o_dtype, gate_dtype,
+                                        y_dtype, false, stream)
+                   : kda::grms_types<2>(o, gate, nullptr, y, nullptr, nullptr, rows, eps, o_dtype, gate_dtype,
+                                        y_dtype, false, stream);
+}
+
+int kda_gated_rmsnorm_bwd(const void* o, const void* gate, const void* dy, void* do_, void* dgate, int N, int H,
+                          int dv, float eps, int o_dtype, int gate_dtype, int y_dtype, kda_stream_t stream) {
+  if (N < 0 || H < 0 || !d_ok(dv)) return KDA_ERR_SHAPE;
+  if (!valid_dt(o_dtype) || !valid_dt(gate_dtype) || !valid_dt(y_dtype)) return KDA_ERR_DTYPE;
+  if (N == 0 || H == 0) return KDA_OK;
+  if (!o || !gate || !dy || !do_ || !dgate) return KDA_ERR_NULL;
+  const void* al[] = {o, gate, dy, do_, dgate};
+  for (const void* p : al)
+    if (!kda::aligned16(p)) return KDA_ERR_ALIGN;
+  const long long rows = static_cast<long long>(N) * H;
+  return dv == 128 ? kda::grms_types<4>(o, gate, dy, nullptr, do_, dgate, rows, eps, o_dtype, gate_dtype,
+                                        y_dtype, true, stream)
+                   : kda::grms_types<2>(o, gate, dy, nullptr, do_, dgate, rows, eps, o_dtype, gate_dtype,
+                                        y_dtype, true, stream);
+}
+
+int kda_decode_fused(float* S, float* conv_buf, const void* qp, const void* kp, const void* vp, const void* z,
+                     const void* beta_logit, const void* gate_logit, const float* conv_q, const float* conv_k,
+                     const float* conv_v, const float* b_gate, const float* A, float g_min, int gate_kind,
+                     float rms_eps, void* out, int N, int H, int dk, int dv, int K, int in_dtype, int out_dtype,
+                     kda_stream_t stream) {
+  if (N < 0 || H < 0 || H > 65535 || K < 1 || K > 4 || !d_ok(dk) || !d_ok(dv)) return KDA_ERR_SHAPE;
+  if (!valid_dt(in_dtype) || !valid_dt(out_dtype)) return KDA_ERR_DTYPE;
+  if (gate_kind != KDA_GATE_SIGMOID_MIN && gate_kind != KDA_GATE_SOFTPLUS) return KDA_ERR_SHAPE;
+  if (N == 0 || H == 0) return KDA_OK;
+  if (static_cast<long long>(N) * H > 0x7fffffffLL) return KDA_ERR_SHAPE;
+  if (!S || !qp || !kp || !vp || !z || !beta_logit || !conv_q || !conv_k || !conv_v || !A || !out)
+    return KDA_ERR_NULL;
+  if (K > 1 && !conv_buf) return KDA_ERR_NULL;
+  if (!kda::aligned16(S)) return KDA_ERR_ALIGN;
+  kda::DecArgs a{};
+  a.S = S; a.buf = K > 1 ? conv_buf : nullptr;
+  a.qp = qp; a.kp = kp; a.vp = vp; a.z = z; a.beta_logit = beta_logit; a.gate = gate_logit;
+  a.w[0] = conv_q; a.w[1] = conv_k; a.w[2] = conv_v;
+  a.b_gate = b_gate; a.A = A; a.g_min = g_min; a.gate_kind = gate_kind; a.rms_eps = rms_eps;
+  a.out = out; a.H = H; a.K = K;
+  if (dk == 128 && dv == 128) return kda::dec_types<128, 128>(a, N, in_dtype, out_dtype, stream);
+  if (dk == 64 && dv == 128) return kda::dec_types<64, 128>(a, N, in_dtype, out_dtype, stream);
+  if (dk == 128 && dv == 64) return kda::dec_types<128, 64>(a, N, in_dtype, out_dtype, stream);
+  return kda::dec_types<64, 64>(a, N, in_dtype, out_dtype, stream);
+}
+
+}  // extern "C"

@@ -2,11 +2,12 @@
 reference functions use, so that those functions can be *executed* from the
 reference's own source files in a container that has no JAX.
 
-Used only by ``make_golden.py`` (fixture generation); nothing at test or run
-time imports it.  It covers exactly what the generating script calls:
-``jax.numpy`` (delegated to NumPy, with the ``x.at[idx].set/add`` functional
-update JAX arrays have), ``jax.lax.scan`` (a Python loop), ``jax.custom_vjp``
-and ``jax.jit`` as pass-throughs.  The arithmetic is NumPy's; the algorithm --
+Used only by ``make_golden.py`` and ``make_golden_mixer.py`` (fixture
+generation); nothing at test or run time imports it.  It covers exactly what
+the generating scripts call: ``jax.numpy`` (delegated to NumPy, with the
+``x.at[idx].set/add`` functional update JAX arrays have), ``jax.lax.scan`` (a
+Python loop), ``jax.custom_vjp`` and ``jax.jit`` as pass-throughs, and
+``jax.custom_jvp``, which keeps the registered derivative rule callable.  The arithmetic is NumPy's; the algorithm --
 operation order, tiling, clamps, dtype casts -- is the reference's own code.
 """
 
@@ -82,6 +83,7 @@ def _make_jnp():
     linalg = types.ModuleType("jax.numpy.linalg")
     linalg.inv = _wrapfn(np.linalg.inv)
     linalg.solve = _wrapfn(np.linalg.solve)
+    linalg.norm = _wrapfn(np.linalg.norm)
     jnp.linalg = linalg
 
     def asarray(x, dtype=None):
@@ -121,6 +123,24 @@ def _scan(f, init, xs, length=None, reverse=False):
     return carry, stacked
 
 
+class _CustomJvp:
+    """``jax.custom_jvp`` stand-in: calling it runs the primal; ``defjvp``
+    records the rule, which ``jvp_rule`` exposes so that a fixture can evaluate
+    the reference's own derivative."""
+
+    def __init__(self, fn, nondiff_argnums=()):
+        self.fn = fn
+        self.nondiff_argnums = tuple(nondiff_argnums)
+        self.jvp_rule = None
+
+    def __call__(self, *a, **k):
+        return self.fn(*a, **k)
+
+    def defjvp(self, rule):
+        self.jvp_rule = rule
+        return rule
+
+
 def install():
     """Register the stand-in as ``jax`` / ``jax.numpy`` / ``jax.lax`` / ``jax.nn``."""
     jax = types.ModuleType("jax")
@@ -134,6 +154,7 @@ def install():
     jax.nn = nn
     jax.jit = lambda f, *a, **k: f
     jax.custom_vjp = lambda f, *a, **k: f
+    jax.custom_jvp = _CustomJvp
     jax.devices = lambda *a, **k: []
     sys.modules["jax"] = jax
     sys.modules["jax.numpy"] = jnp

@@ -1,6 +1,6 @@
 """Host-side checks of the C ABI and the Python mirror (no GPU needed).
 
-* the library loads and exports every function ``include/kda_b200.h`` declares;
+* the library loads and exports every function ``include/*.h`` declares;
 * argument validation fails closed before any launch (typed error codes);
 * the implementation switch fails closed on unknown values
   (``net/kda.py:708-729``) and the operators refuse a GPU-less host with a
@@ -8,6 +8,7 @@
 """
 
 import ctypes
+import glob
 import os
 import re
 
@@ -18,22 +19,24 @@ from axiom_b200 import _lib
 from axiom_b200 import kda as K
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "kda_b200.h")
+HEADERS = sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
-def _declared_functions():
-    src = open(HEADER).read()
+def _declared_functions(header):
+    src = open(header).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(kda_\w+)\s*\(", src, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
-    names = _declared_functions()
-    assert names, "no declarations parsed from the header"
-    for name in names:
-        assert hasattr(lib, name), f"{name} declared in kda_b200.h but not exported"
-        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert len(HEADERS) >= 2
+    for header in HEADERS:
+        names = _declared_functions(header)
+        assert names, f"no declarations parsed from {header}"
+        for name in names:
+            assert hasattr(lib, name), f"{name} declared in {os.path.basename(header)} but not exported"
+            assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
 
 
 def test_version_and_strerror():
@@ -119,6 +122,50 @@ def test_decode_validation():
     assert lib.kda_decode(*([None] * 7), 0, 128, 128, 1, 1, None) == 0
     odd = ctypes.c_void_p(8)
     assert lib.kda_decode(odd, *([ctypes.c_void_p(16)] * 6), 4, 128, 128, 1, 1, None) == -3
+
+
+def test_prologue_validation():
+    lib = _lib.lib()
+    w = [None] * 10
+    outs = [None] * 5
+
+    def fwd(*, kind=0, st=(None, None), cu=None, n_seqs=0, dims=(1, 64, 2, 128, 128, 4), dt=(1, 1), ptrs=None,
+            o=None):
+        return lib.kda_prologue_fwd(*(ptrs or w), -5.0, kind, st[0], st[1], cu, n_seqs, *(o or outs), *dims, *dt,
+                                    None)
+
+    assert fwd(dims=(1, 64, 2, 96, 128, 4)) == -1       # dk not 64/128
+    assert fwd(dims=(1, 64, 2, 128, 128, 5)) == -1      # K > 4
+    assert fwd(dims=(1, 64, 2, 128, 128, 0)) == -1      # K < 1
+    assert fwd(kind=7) == -1                              # unknown gate form
+    assert fwd(dt=(1, 9)) == -2
+    assert fwd(dims=(0, 64, 2, 128, 128, 4)) == 0        # nothing to do
+    assert fwd() == -4                                    # null inputs
+    fake, odd = ctypes.c_void_p(16), ctypes.c_void_p(8)
+    # packed sequences need B = 1 and no conv state
+    assert fwd(cu=fake, n_seqs=2, dims=(2, 64, 2, 128, 128, 4)) == -1
+    assert fwd(cu=fake, n_seqs=2, st=(fake, None)) == -1
+    assert fwd(ptrs=[odd] + [fake] * 9, o=[fake] * 5) == -3
+    assert lib.kda_prologue_bwd_workspace_bytes(1, 64, 2, 128, 128, 4) > 0
+    assert lib.kda_prologue_bwd_workspace_bytes(1, 64, 2, 100, 128, 4) == 0
+    bw = lib.kda_prologue_bwd(*([fake] * 10), -5.0, 0, None, None, 0, *([fake] * 10), *([fake] * 5), None,
+                              None, 0, 1, 64, 2, 128, 128, 4, 1, 1, None)
+    assert bw == -6                                       # workspace missing
+
+
+def test_gated_rmsnorm_and_fused_decode_validation():
+    lib = _lib.lib()
+    assert lib.kda_gated_rmsnorm_fwd(None, None, None, 4, 2, 96, 1e-6, 1, 1, 1, None) == -1
+    assert lib.kda_gated_rmsnorm_fwd(None, None, None, 0, 2, 128, 1e-6, 1, 1, 1, None) == 0
+    assert lib.kda_gated_rmsnorm_fwd(None, None, None, 4, 2, 128, 1e-6, 1, 1, 1, None) == -4
+    assert lib.kda_gated_rmsnorm_bwd(*([None] * 5), 4, 2, 128, 1e-6, 3, 1, 1, None) == -2
+    fake = ctypes.c_void_p(16)
+    args = [fake, fake] + [fake] * 11
+    assert lib.kda_decode_fused(*args, -5.0, 0, 1e-6, fake, 4, 2, 96, 128, 4, 1, 1, None) == -1
+    assert lib.kda_decode_fused(*args, -5.0, 2, 1e-6, fake, 4, 2, 128, 128, 4, 1, 1, None) == -1
+    no_buf = [fake, None] + [fake] * 11
+    assert lib.kda_decode_fused(*no_buf, -5.0, 0, 1e-6, fake, 4, 2, 128, 128, 4, 1, 1, None) == -4
+    assert lib.kda_decode_fused(*args, -5.0, 0, 1e-6, fake, 0, 2, 128, 128, 4, 1, 1, None) == 0
 
 
 def test_impl_switch_fails_closed(monkeypatch):
