@@ -339,29 +339,6 @@ __device__ __forceinline__ void store_rows(bf16* dst, const unsigned char* rows,
   }
 }
 
-// Column sums over the 32 lanes of a warp: every lane holds N consecutive
-// columns v[0..N-1] (N = 8 or 16); the result, on every lane, is column
-// (lane % N) summed over all 32 lanes.  Halving exchanges (N/2 + ... + 1
-// shuffles) leave lane l with column l % N summed over its group of N lanes;
-// log2(32 / N) more shuffles add the groups.
-template <int N>
-__device__ __forceinline__ float warp_colsum(float (&v)[N], int lane) {
-#pragma unroll
-  for (int off = N / 2; off >= 1; off >>= 1) {
-    const bool up = (lane & off) != 0;
-#pragma unroll
-    for (int j = 0; j < off; ++j) {
-      const float send = up ? v[j] : v[j + off];
-      const float recv = __shfl_xor_sync(0xffffffffu, send, off);
-      v[j] = (up ? v[j + off] : v[j]) + recv;
-    }
-  }
-  float s = v[0];
-#pragma unroll
-  for (int off = N; off < 32; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  return s;
-}
-
 // fp32 checkpoint state (row-major) -> bf16 CM operand tile.
 __device__ __forceinline__ void stage_ckpt_f32(unsigned char* dst, const float* src) {
   for (int i = threadIdx.x; i < 128 * 16; i += NT) {

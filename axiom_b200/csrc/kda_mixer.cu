@@ -8,30 +8,36 @@
 //   * fused decode step: recurrent_step without the projection GEMMs
 //     (net/kda.py:277-295, net/shortconv.py:33-53).
 //
-// Prologue mapping: a warp owns a strip of 64 consecutive tokens of one head
-// and one tensor (block = 8 warps of the same head and tensor; blockIdx.z
-// picks q, k, v or the gates), each lane 2 or 4 adjacent channels, so a row of
-// the head (128 or 256 bytes) is one coalesced warp access and the L2 norm is
-// a warp reduction.  The conv window lives in registers: every input is read
-// once, plus K-1 halo rows per strip (L2 hits).  Loads of 8 tokens are issued
-// before their use to keep enough bytes in flight.  The backward sweeps each
-// strip from its end (plus K-1 halo tokens whose conv cotangents its inputs
-// need) to its start, so dx[t] = sum_i w[i] dc[t+i] is complete when t is
-// reached; weight gradients are reduced per block (4 warps) in shared
-// memory, then over blocks in a fixed order by a second kernel (deterministic).
+// Prologue mapping: a warp owns a strip of 256 consecutive tokens of one head
+// and one tensor (a block's warps share the head and tensor; blockIdx.z picks
+// q, k, v or the gates), each lane 2 or 4 adjacent channels, so a row of the
+// head (128 or 256 bytes) is one coalesced warp access and the L2 norm is a
+// warp reduction.  The strip's rows stream through a per-warp shared-memory
+// ring filled by cp.async (several batches in flight without holding
+// registers); the conv window lives in registers, so every input is read once
+// plus K-1 halo rows per strip (L2 hits).  The L2 norms of a batch of tokens
+// are one column-sum reduction.  The backward sweeps each strip from its end
+// (plus K-1 halo tokens whose conv cotangents its inputs need) to its start,
+// so dx[t] = sum_i w[i] dc[t+i] is complete when t is reached; weight
+// gradients are reduced per block in shared memory, then over blocks in a
+// fixed order by a second kernel (deterministic).
 #include <climits>
 #include <type_traits>
 
 #include "kda_common.cuh"
 #include "kda_mixer.h"
+#include "kda_tc.cuh"
 
 namespace kda {
 namespace {
 
-constexpr int kStrip = 64;   // tokens per warp strip
+constexpr int kStrip = 256;  // tokens per warp strip (a long sweep amortises the ring fill)
 constexpr int kWarps = 8;    // warps per prologue forward block
 constexpr int kBwdWarps = 4; // warps per backward block (more registers per thread)
-constexpr int kPre = 8;      // tokens whose loads are issued together
+constexpr int kPre = 8;      // tokens per forward batch
+constexpr int kStages = 4;   // forward ring stages per warp (3 batches in flight)
+constexpr int kBwStages = 6; // backward ring stages per warp
+constexpr int kBw = 4;       // tokens per backward batch
 constexpr float kL2Eps = 1e-12f;
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -40,6 +46,19 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Sigmoid at the precision its consumer keeps: with FAST (results rounded to
+// bf16) one tanh.approx, sigmoid(x) = (1 + tanh(x / 2)) / 2, whose absolute
+// error (below 2^-11) is under bf16's resolution; else exp and reciprocal.
+template <bool FAST>
+__device__ __forceinline__ float sigm(float x) {
+  if constexpr (FAST) return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f);
+  else return sigmoidf_(x);
+}
 __device__ __forceinline__ float softplusf_(float x) { return fmaxf(x, 0.f) + log1pf(__expf(-fabsf(x))); }
 
 // CPL (2 or 4) consecutive elements <-> floats, one vector access
@@ -112,6 +131,32 @@ __device__ __forceinline__ void cvt(const Raw<T, CPL>& r, float (&x)[CPL]) {
       x[2 * c + 1] = __high2float(p[c]);
     }
   }
+}
+
+// One stage of a warp's shared-memory ring: NROWS rows of RB bytes, row r
+// copied from src(r) with cp.async (16 bytes per lane and copy), or
+// zero-filled when src(r) is null.  Rows in flight cost no registers, so a
+// warp keeps several batches of its strip in flight.
+template <int RB, int NROWS, typename Src>
+__device__ __forceinline__ void ring_fill(unsigned char* dst, int lane, const void* any_valid, Src src) {
+  constexpr int CPR = RB / 16;
+  constexpr int N = NROWS * CPR;
+  static_assert(N % 32 == 0, "whole warp copies");
+#pragma unroll
+  for (int it = 0; it < N / 32; ++it) {
+    const int j = lane + 32 * it;
+    const int r = j / CPR, c = j % CPR;
+    const unsigned char* p = static_cast<const unsigned char*>(src(r));
+    tc::cp_async16(dst + r * RB + c * 16, p ? p + c * 16 : any_valid, p != nullptr);
+  }
+}
+
+// CPL elements of this lane from a staged row (lane l holds elements [l CPL, l CPL + CPL)).
+template <int CPL, typename T>
+__device__ __forceinline__ void ld_row(const unsigned char* row, int lane, float (&x)[CPL]) {
+  Raw<T, CPL> r;
+  r.v = *reinterpret_cast<const decltype(r.v)*>(row + lane * CPL * sizeof(T));
+  cvt<CPL>(r, x);
 }
 
 struct ProArgs {
@@ -187,321 +232,445 @@ __device__ __forceinline__ void load_x(const ProArgs& a, const Tin* x, size_t ro
 
 // ---------------------------------------------------------------- forward ----
 
+// Bytes of one warp's ring in the forward and backward kernels.
+template <int CPL, typename Tin>
+__host__ __device__ constexpr int fwd_ring_bytes() { return kStages * kPre * CPL * 32 * static_cast<int>(sizeof(Tin)); }
 template <int CPL, typename Tin, typename Tout>
-__device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, int h, int lane) {
-  constexpr int D = CPL * 32;
+__host__ __device__ constexpr int bwd_ring_bytes() {
+  return kBwStages * kBw * CPL * 32 * static_cast<int>(sizeof(Tin) + sizeof(Tout));
+}
+
+// q, k, v of one strip.  Batches of kPre tokens stream through the warp's
+// ring (kStages - 1 batches in flight); a batch's L2 norms are one column-sum
+// reduction (warp_colsum) instead of kPre serial ones.
+template <int CPL, bool VARLEN, typename Tin, typename Tout>
+__device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, int h, int lane,
+                             unsigned char* ring) {
+  constexpr bool FAST = std::is_same<Tout, bf16>::value;
+  constexpr int D = CPL * 32, RB = D * static_cast<int>(sizeof(Tin)), STG = kPre * RB;
   const int HD = a.H * D;
   const int ch = h * D + lane * CPL;
   const size_t row0 = static_cast<size_t>(b) * a.T;
-  const Tin* x = static_cast<const Tin*>(pick(a.x, role));
-  Tout* y = static_cast<Tout*>(pick(a.y, role));
+  const Tin* xb = static_cast<const Tin*>(pick(a.x, role));
+  const Tin* xh = xb + row0 * HD + h * D;  // token t of this head at xh + t * HD
+  Tout* y = static_cast<Tout*>(pick(a.y, role)) + row0 * HD + ch;
   float wt[4][CPL];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int c = 0; c < CPL; ++c) wt[i][c] = i < a.K ? pick(a.w, role)[i * HD + ch + c] : 0.f;
   int si = 0, lb = 0, nb = INT_MAX;
-  if (a.cu) {
+  if constexpr (VARLEN) {
     si = seq_of(a.cu, a.n_seqs, t0);
     lb = __ldg(a.cu + si);
     nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+  }
+  const int nbat = (t1 - t0 + kPre - 1) / kPre;
+  auto fill = [&](int bi) {
+    const int tb = t0 + bi * kPre;
+    ring_fill<RB, kPre>(ring + (bi % kStages) * STG, lane, xh, [&](int r) -> const void* {
+      return tb + r < t1 ? xh + static_cast<size_t>(tb + r) * HD : nullptr;
+    });
+  };
+#pragma unroll
+  for (int bi = 0; bi < kStages - 1; ++bi) {
+    if (bi < nbat) fill(bi);
+    tc::cp_async_commit();
   }
   float hw[3][CPL];  // x[t-1], x[t-2], x[t-3]
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
     const int t = t0 - 1 - j;
-    if (a.cu && t < lb) {
+    if (VARLEN && t < lb) {
 #pragma unroll
       for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
     } else {
-      load_x<CPL>(a, x, row0, HD, ch, b, role, t, hw[j]);
+      load_x<CPL>(a, xb, row0, HD, ch, b, role, t, hw[j]);
     }
   }
-  for (int tb = t0; tb < t1; tb += kPre) {
-    Raw<Tin, CPL> xr[kPre];
+  for (int bi = 0; bi < nbat; ++bi) {
+    tc::cp_async_wait<kStages - 2>();
+    __syncwarp();
+    if (bi + kStages - 1 < nbat) fill(bi + kStages - 1);
+    tc::cp_async_commit();
+    const unsigned char* st = ring + (bi % kStages) * STG;
+    const int tb = t0 + bi * kPre;
+    float s[kPre][CPL], ss[kPre];
 #pragma unroll
     for (int u = 0; u < kPre; ++u) {
-      if (tb + u < t1) xr[u] = ldr<CPL>(x + (row0 + tb + u) * HD + ch);
-    }
+      float xv[CPL];
+      ld_row<CPL, Tin>(st + u * RB, lane, xv);
+      if (VARLEN && tb + u == nb) {  // a packed sequence starts: the window restarts from zeros
 #pragma unroll
-    for (int u = 0; u < kPre; ++u) {
-      const int t = tb + u;
-      if (t < t1) {
-        float xv[CPL];
-        cvt<CPL>(xr[u], xv);
-        if (t == nb) {  // a packed sequence starts: the window restarts from zeros
+        for (int j = 0; j < 3; ++j)
 #pragma unroll
-          for (int j = 0; j < 3; ++j)
+          for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
+        ++si;
+        nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+      }
+      ss[u] = 0.f;
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
-          ++si;
-          nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
-        }
-        float s[CPL];
-        float ss = 0.f;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          const float cv = wt[0][c] * xv[c] + wt[1][c] * hw[0][c] + wt[2][c] * hw[1][c] + wt[3][c] * hw[2][c];
-          hw[2][c] = hw[1][c];
-          hw[1][c] = hw[0][c];
-          hw[0][c] = xv[c];
-          s[c] = cv * sigmoidf_(cv);
-          ss += s[c] * s[c];
-        }
-        if (role < 2) {  // q, k: x / (|x| + eps)
-          const float inv = 1.f / (sqrtf(warp_sum(ss)) + kL2Eps);
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) s[c] *= inv;
-        }
-        stv<CPL>(y + (row0 + t) * HD + ch, s);
+      for (int c = 0; c < CPL; ++c) {
+        const float cv = wt[0][c] * xv[c] + wt[1][c] * hw[0][c] + wt[2][c] * hw[1][c] + wt[3][c] * hw[2][c];
+        hw[2][c] = hw[1][c];
+        hw[1][c] = hw[0][c];
+        hw[0][c] = xv[c];
+        s[u][c] = cv * sigm<FAST>(cv);
+        ss[u] += s[u][c] * s[u][c];
       }
     }
+    if (role < 2) {  // q, k: x / (|x| + eps), the batch's norms in one reduction
+      const float tot = warp_colsum<kPre>(ss, lane);  // lane l: token l % kPre
+#pragma unroll
+      for (int u = 0; u < kPre; ++u) {
+        const float inv = 1.f / (sqrtf(__shfl_sync(0xffffffffu, tot, u)) + kL2Eps);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) s[u][c] *= inv;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kPre; ++u)
+      if (tb + u < t1) stv<CPL>(y + static_cast<size_t>(tb + u) * HD, s[u]);
   }
+  tc::cp_async_wait<0>();
+  __syncwarp();
   if (a.st_out && t1 == a.T) {  // this strip ends the sequence: its last K-1 inputs
     const int sw = a.H * (2 * a.dk + a.dv);
     for (int j = 0; j < a.K - 1; ++j) {
       float v[CPL];
-      load_x<CPL>(a, x, row0, HD, ch, b, role, a.T - (a.K - 1) + j, v);
+      load_x<CPL>(a, xb, row0, HD, ch, b, role, a.T - (a.K - 1) + j, v);
       stv<CPL>(a.st_out + (static_cast<size_t>(b) * (a.K - 1) + j) * sw + state_col(a, role) + ch, v);
     }
   }
 }
 
+template <bool FAST>
+__device__ __forceinline__ float gate_fwd(float u, float ea, float g_min, int kind) {
+  return kind == KDA_GATE_SIGMOID_MIN ? g_min * sigm<FAST>(ea * u) : -ea * softplusf_(u);
+}
+
 template <int CPL, typename Tin, typename Tout>
-__device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane) {
-  constexpr int D = CPL * 32;
+__device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane, unsigned char* ring) {
+  constexpr bool FAST = std::is_same<Tout, bf16>::value;
+  constexpr int D = CPL * 32, RB = D * static_cast<int>(sizeof(Tin)), STG = kPre * RB;
   const int HD = a.H * D;
   const int ch = h * D + lane * CPL;
   const size_t row0 = static_cast<size_t>(b) * a.T;
-  const Tin* z = static_cast<const Tin*>(a.x[3]);
-  Tout* g = static_cast<Tout*>(a.y[3]);
+  const Tin* zh = static_cast<const Tin*>(a.x[3]) + row0 * HD + h * D;
+  Tout* g = static_cast<Tout*>(a.y[3]) + row0 * HD + ch;
   float bias[CPL];
 #pragma unroll
   for (int c = 0; c < CPL; ++c) bias[c] = a.b_gate ? a.b_gate[ch + c] : 0.f;
   const float ea = __expf(a.A[h]);
-  for (int tb = t0; tb < t1; tb += kPre) {
-    Raw<Tin, CPL> zr[kPre];
+  const int nbat = (t1 - t0 + kPre - 1) / kPre;
+  auto fill = [&](int bi) {
+    const int tb = t0 + bi * kPre;
+    ring_fill<RB, kPre>(ring + (bi % kStages) * STG, lane, zh, [&](int r) -> const void* {
+      return tb + r < t1 ? zh + static_cast<size_t>(tb + r) * HD : nullptr;
+    });
+  };
 #pragma unroll
-    for (int u = 0; u < kPre; ++u)
-      if (tb + u < t1) zr[u] = ldr<CPL>(z + (row0 + tb + u) * HD + ch);
-#pragma unroll
-    for (int u = 0; u < kPre; ++u) {
-      if (tb + u < t1) {
-        float o[CPL], zv[CPL];
-        cvt<CPL>(zr[u], zv);
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          const float uu = zv[c] + bias[c];
-          o[c] = a.gate_kind == KDA_GATE_SIGMOID_MIN ? a.g_min * sigmoidf_(ea * uu) : -ea * softplusf_(uu);
-        }
-        stv<CPL>(g + (row0 + tb + u) * HD + ch, o);
-      }
-    }
+  for (int bi = 0; bi < kStages - 1; ++bi) {
+    if (bi < nbat) fill(bi);
+    tc::cp_async_commit();
   }
   const Tin* bl = static_cast<const Tin*>(a.beta_logit);
   Tout* beta = static_cast<Tout*>(a.beta);
-  for (int t = t0 + lane; t < t1; t += 32) {
+  for (int t = t0 + lane; t < t1; t += 32) {  // beta while the first batches land
     const size_t i = (row0 + t) * a.H + h;
     stf(beta + i, sigmoidf_(ldf(bl + i)));
   }
+  for (int bi = 0; bi < nbat; ++bi) {
+    tc::cp_async_wait<kStages - 2>();
+    __syncwarp();
+    if (bi + kStages - 1 < nbat) fill(bi + kStages - 1);
+    tc::cp_async_commit();
+    const unsigned char* st = ring + (bi % kStages) * STG;
+    const int tb = t0 + bi * kPre;
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      if (tb + u < t1) {
+        float o[CPL];
+        ld_row<CPL, Tin>(st + u * RB, lane, o);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) o[c] = gate_fwd<FAST>(o[c] + bias[c], ea, a.g_min, a.gate_kind);
+        stv<CPL>(g + static_cast<size_t>(tb + u) * HD, o);
+      }
+    }
+  }
+  tc::cp_async_wait<0>();
+  __syncwarp();
 }
 
 // blockIdx.z selects the tensor: role = 4-bit field z of a.roles (0 q, 1 k,
 // 2 v, 3 gates), so one launch covers the tensors of one width D = 32 CPL.
-template <int CPL, typename Tin, typename Tout>
+template <int CPL, bool VARLEN, typename Tin, typename Tout>
 __global__ void __launch_bounds__(kWarps * 32) prologue_fwd_kernel(const ProArgs a) {
+  extern __shared__ __align__(16) unsigned char pro_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int s = blockIdx.x * kWarps + warp;
   if (s >= a.n_strips) return;
+  unsigned char* ring = pro_smem + warp * fwd_ring_bytes<CPL, Tin>();
   const int h = blockIdx.y, role = (a.roles >> (4 * blockIdx.z)) & 15;
   const int b = s / a.spb;
   const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
-  if (role < 3) pro_fwd_conv<CPL, Tin, Tout>(a, role, b, t0, t1, h, lane);
-  else pro_fwd_gate<CPL, Tin, Tout>(a, b, t0, t1, h, lane);
+  if (role < 3) pro_fwd_conv<CPL, VARLEN, Tin, Tout>(a, role, b, t0, t1, h, lane, ring);
+  else pro_fwd_gate<CPL, Tin, Tout>(a, b, t0, t1, h, lane, ring);
 }
 
 // --------------------------------------------------------------- backward ----
 
-template <int CPL, typename Tin, typename Tout>
+// q, k, v of one strip, swept from its end (hi: the last token whose conv
+// cotangent the strip's inputs need) down to its start, kBw tokens a batch:
+// X[j] holds x[base - j] (j < kBw + 3: every tap of every token of the batch),
+// dcw the conv cotangents of the three tokens above the batch.  A batch's
+// cotangent rows and the input rows the window slides onto stream through the
+// warp's ring.  The L2-norm cotangent needs two sums per token; a batch's
+// 2 kBw sums are one column-sum reduction.
+template <int CPL, bool VARLEN, typename Tin, typename Tout>
 __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, int h, int lane,
-                             float (&dw)[4][4]) {
-  constexpr int D = CPL * 32;
+                             float (&dw)[4][4], unsigned char* ring) {
+  constexpr bool FAST = std::is_same<Tin, bf16>::value;  // the cotangents leave as Tin
+  constexpr int D = CPL * 32, NX = kBw + 3;
+  constexpr int RBX = D * static_cast<int>(sizeof(Tin)), RBY = D * static_cast<int>(sizeof(Tout));
+  constexpr int STG = kBw * (RBX + RBY);
   const int HD = a.H * D;
   const int ch = h * D + lane * CPL;
   const size_t row0 = static_cast<size_t>(b) * a.T;
-  const Tin* x = static_cast<const Tin*>(pick(a.x, role));
-  const Tout* dy = static_cast<const Tout*>(pick(a.dy, role));
-  Tin* dx = static_cast<Tin*>(pick(a.dx, role));
+  const Tin* xb = static_cast<const Tin*>(pick(a.x, role));
+  const Tin* xh = xb + row0 * HD + h * D;
+  const Tout* dyh = static_cast<const Tout*>(pick(a.dy, role)) + row0 * HD + h * D;
+  Tin* dx = static_cast<Tin*>(pick(a.dx, role)) + row0 * HD + ch;
   const int K = a.K;
   float wt[4][CPL];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int c = 0; c < CPL; ++c) wt[i][c] = i < K ? pick(a.w, role)[i * HD + ch + c] : 0.f;
-  // sweep tau from hi (the last token whose conv cotangent the strip's inputs
-  // need) down to lo (t0, or -(K-1) when the strip writes the state's cotangent)
   const int hi = min(t1 + K - 1, a.T) - 1;
   const int lo = (t0 == 0 && a.dst && !a.cu) ? -(K - 1) : t0;
-  int si = 0, lb = INT_MIN;
-  if (a.cu) {
+  const int nbat = (hi - lo) / kBw + 1;
+  // stage bi: the input rows base - NX - u (the window's next rows), then the
+  // cotangent rows base - u, u < kBw, base = hi - bi kBw
+  auto fill = [&](int bi) {
+    const int base = hi - bi * kBw;
+    unsigned char* st = ring + (bi % kBwStages) * STG;
+    ring_fill<RBX, kBw>(st, lane, xh, [&](int r) -> const void* {
+      const int t = base - NX - r;
+      return t >= 0 ? xh + static_cast<size_t>(t) * HD : nullptr;
+    });
+    ring_fill<RBY, kBw>(st + kBw * RBX, lane, dyh, [&](int r) -> const void* {
+      const int t = base - r;
+      return t >= 0 && t >= lo ? dyh + static_cast<size_t>(t) * HD : nullptr;
+    });
+  };
+#pragma unroll
+  for (int bi = 0; bi < kBwStages - 1; ++bi) {
+    if (bi < nbat) fill(bi);
+    tc::cp_async_commit();
+  }
+  int si = 0, lb = INT_MIN, ub = INT_MAX;  // the packed sequence [lb, ub) of the current token
+  if constexpr (VARLEN) {
     si = seq_of(a.cu, a.n_seqs, hi);
     lb = __ldg(a.cu + si);
+    ub = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
   }
-  float xw[4][CPL];  // x[tau], x[tau-1], x[tau-2], x[tau-3]
+  float X[NX][CPL];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) load_x<CPL>(a, x, row0, HD, ch, b, role, hi - i, xw[i]);
-  float dcw[3][CPL];  // dc[tau+1], dc[tau+2], dc[tau+3]
+  for (int j = 0; j < NX; ++j) load_x<CPL>(a, xb, row0, HD, ch, b, role, hi - j, X[j]);
+  float dcw[3][CPL];
 #pragma unroll
   for (int j = 0; j < 3; ++j)
 #pragma unroll
     for (int c = 0; c < CPL; ++c) dcw[j][c] = 0.f;
   const int sw = a.H * (2 * a.dk + a.dv);
-  for (int base = hi; base >= lo; base -= kPre) {
-    Raw<Tin, CPL> xr[kPre];
-    Raw<Tout, CPL> dr[kPre];
+  for (int bi = 0; bi < nbat; ++bi) {
+    tc::cp_async_wait<kBwStages - 2>();
+    __syncwarp();
+    if (bi + kBwStages - 1 < nbat) fill(bi + kBwStages - 1);
+    tc::cp_async_commit();
+    const unsigned char* st = ring + (bi % kBwStages) * STG;
+    const int base = hi - bi * kBw;
+    int lbu[kBw], ubu[kBw];
 #pragma unroll
-    for (int u = 0; u < kPre; ++u) {
+    for (int u = 0; u < kBw; ++u) {
       const int tau = base - u;
-      if (tau - 4 >= 0) xr[u] = ldr<CPL>(x + (row0 + tau - 4) * HD + ch);
-      if (tau >= 0 && tau >= lo) dr[u] = ldr<CPL>(dy + (row0 + tau) * HD + ch);
-    }
-#pragma unroll
-    for (int u = 0; u < kPre; ++u) {
-      const int tau = base - u;
-      if (tau >= lo) {
-        float xn[CPL], dv[CPL];
-        if (tau - 4 >= 0) cvt<CPL>(xr[u], xn);
-        else load_x<CPL>(a, x, row0, HD, ch, b, role, tau - 4, xn);  // the conv state, or zero
-        if (tau >= 0) cvt<CPL>(dr[u], dv);
-        float xm[4][CPL];  // window masked at the sequence start
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const bool ok = tau - i >= lb;
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) xm[i][c] = ok ? xw[i][c] : 0.f;
-        }
-        float dc[CPL];
-        if (tau >= 0) {
-          float cv[CPL], s[CPL], sg[CPL];
-          float ss = 0.f, sd = 0.f;
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) {
-            cv[c] = wt[0][c] * xm[0][c] + wt[1][c] * xm[1][c] + wt[2][c] * xm[2][c] + wt[3][c] * xm[3][c];
-            const float sig = sigmoidf_(cv[c]);
-            s[c] = cv[c] * sig;
-            sg[c] = sig * (1.f + cv[c] * (1.f - sig));
-            ss += s[c] * s[c];
-            sd += s[c] * dv[c];
-          }
-          if (role < 2) {  // cotangent of x / (|x| + eps); zero at x = 0
-            const float n = sqrtf(warp_sum(ss));
-            const float p = warp_sum(sd);
-            const float den = n + kL2Eps;
-            const float pr = n > 0.f ? p / n : 0.f;
-#pragma unroll
-            for (int c = 0; c < CPL; ++c)
-              dc[c] = (n > 0.f ? (dv[c] - s[c] * pr / den) / den : 0.f) * sg[c];
-          } else {
-#pragma unroll
-            for (int c = 0; c < CPL; ++c) dc[c] = dv[c] * sg[c];
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) dc[c] = 0.f;
-        }
-        if (tau < t1) {
-          float o[CPL];
-#pragma unroll
-          for (int c = 0; c < CPL; ++c)
-            o[c] = wt[0][c] * dc[c] + wt[1][c] * dcw[0][c] + wt[2][c] * dcw[1][c] + wt[3][c] * dcw[2][c];
-          if (tau >= t0) {
-            stv<CPL>(dx + (row0 + tau) * HD + ch, o);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-              for (int c = 0; c < CPL; ++c) dw[i][c] += dc[c] * xm[i][c];
-          } else {  // tau < 0: cotangent of the conv state row
-            stv<CPL>(a.dst + (static_cast<size_t>(b) * (K - 1) + tau + K - 1) * sw + state_col(a, role) + ch, o);
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          dcw[2][c] = dcw[1][c];
-          dcw[1][c] = dcw[0][c];
-          dcw[0][c] = dc[c];
-          xw[0][c] = xw[1][c];
-          xw[1][c] = xw[2][c];
-          xw[2][c] = xw[3][c];
-          xw[3][c] = xn[c];
-        }
-        if (a.cu && tau == lb && si > 0) {  // below tau lies the previous sequence
-#pragma unroll
-          for (int j = 0; j < 3; ++j)
-#pragma unroll
-            for (int c = 0; c < CPL; ++c) dcw[j][c] = 0.f;
+      if constexpr (VARLEN) {
+        while (tau < lb && si > 0) {  // below lb lies the previous sequence
+          ub = lb;
           --si;
           lb = __ldg(a.cu + si);
         }
       }
+      lbu[u] = lb;
+      ubu[u] = ub;
+    }
+    float s[kBw][CPL], sg[kBw][CPL], dv[kBw][CPL], sums[2 * kBw];
+#pragma unroll
+    for (int u = 0; u < kBw; ++u) {
+      const int tau = base - u;
+      ld_row<CPL, Tout>(st + kBw * RBX + u * RBY, lane, dv[u]);
+      float ss = 0.f, sd = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        float cv = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) cv += !VARLEN || tau - i >= lbu[u] ? wt[i][c] * X[u + i][c] : 0.f;
+        const float sig = sigm<FAST>(cv);
+        s[u][c] = cv * sig;
+        sg[u][c] = sig * (1.f + cv * (1.f - sig));
+        ss += s[u][c] * s[u][c];
+        sd += s[u][c] * dv[u][c];
+      }
+      sums[u] = ss;
+      sums[kBw + u] = sd;
+    }
+    float dc[kBw][CPL];
+    if (role < 2) {  // cotangent of x / (|x| + eps); zero at x = 0
+      const float tot = warp_colsum<2 * kBw>(sums, lane);  // lane l: sum l % (2 kBw)
+#pragma unroll
+      for (int u = 0; u < kBw; ++u) {
+        const float n = sqrtf(__shfl_sync(0xffffffffu, tot, u));
+        const float p = __shfl_sync(0xffffffffu, tot, kBw + u);
+        const float den = n + kL2Eps;
+        const float pr = n > 0.f ? p / n : 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) dc[u][c] = n > 0.f ? (dv[u][c] - s[u][c] * pr / den) / den * sg[u][c] : 0.f;
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < kBw; ++u)
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) dc[u][c] = dv[u][c] * sg[u][c];
+    }
+#pragma unroll
+    for (int u = 0; u < kBw; ++u) {
+      if (base - u < 0) {
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) dc[u][c] = 0.f;
+      }
+    }
+    // dx[tau] = sum_i w[i] dc[tau + i] (same sequence); dw[i] += dc[tau] x[tau - i]
+#pragma unroll
+    for (int u = 0; u < kBw; ++u) {
+      const int tau = base - u;
+      if (tau >= lo && tau < t1) {
+        float o[CPL];
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          float acc = wt[0][c] * dc[u][c];
+#pragma unroll
+          for (int i = 1; i < 4; ++i) {
+            const float d = i <= u ? dc[u - i][c] : dcw[i - u - 1][c];
+            acc += !VARLEN || tau + i < ubu[u] ? wt[i][c] * d : 0.f;
+          }
+          o[c] = acc;
+        }
+        if (tau >= t0) {
+          stv<CPL>(dx + static_cast<size_t>(tau) * HD, o);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) dw[i][c] += !VARLEN || tau - i >= lbu[u] ? dc[u][c] * X[u + i][c] : 0.f;
+        } else {  // tau < 0: cotangent of the conv state row
+          stv<CPL>(a.dst + (static_cast<size_t>(b) * (K - 1) + tau + K - 1) * sw + state_col(a, role) + ch, o);
+        }
+      }
+    }
+    // slide down by kBw tokens
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) dcw[j][c] = dc[kBw - 1 - j][c];
+#pragma unroll
+    for (int j = 0; j < NX - kBw; ++j)
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) X[j][c] = X[j + kBw][c];
+#pragma unroll
+    for (int u = 0; u < kBw; ++u) {
+      const int t = base - NX - u;  // row of X[NX - kBw + u] after the slide
+      if (t >= 0) ld_row<CPL, Tin>(st + u * RBX, lane, X[NX - kBw + u]);
+      else load_x<CPL>(a, xb, row0, HD, ch, b, role, t, X[NX - kBw + u]);
     }
   }
+  tc::cp_async_wait<0>();
+  __syncwarp();
 }
 
 template <int CPL, typename Tin, typename Tout>
 __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane, float (&db)[4],
-                             float& dA) {
+                             float& dA, unsigned char* ring) {
+  constexpr bool FAST = std::is_same<Tin, bf16>::value;
   constexpr int D = CPL * 32;
+  constexpr int RBX = D * static_cast<int>(sizeof(Tin)), RBY = D * static_cast<int>(sizeof(Tout));
+  constexpr int STG = kBw * (RBX + RBY);
   const int HD = a.H * D;
   const int ch = h * D + lane * CPL;
   const size_t row0 = static_cast<size_t>(b) * a.T;
-  const Tin* z = static_cast<const Tin*>(a.x[3]);
-  const Tout* dg = static_cast<const Tout*>(a.dy[3]);
-  Tin* dz = static_cast<Tin*>(a.dx[3]);
+  const Tin* zh = static_cast<const Tin*>(a.x[3]) + row0 * HD + h * D;
+  const Tout* dgh = static_cast<const Tout*>(a.dy[3]) + row0 * HD + h * D;
+  Tin* dz = static_cast<Tin*>(a.dx[3]) + row0 * HD + ch;
   float bias[CPL];
 #pragma unroll
   for (int c = 0; c < CPL; ++c) bias[c] = a.b_gate ? a.b_gate[ch + c] : 0.f;
   const float ea = __expf(a.A[h]);
-  for (int tb = t0; tb < t1; tb += kPre) {
-    Raw<Tin, CPL> zr[kPre];
-    Raw<Tout, CPL> gr[kPre];
+  const int nbat = (t1 - t0 + kBw - 1) / kBw;
+  auto fill = [&](int bi) {
+    const int tb = t0 + bi * kBw;
+    unsigned char* st = ring + (bi % kBwStages) * STG;
+    ring_fill<RBX, kBw>(st, lane, zh, [&](int r) -> const void* {
+      return tb + r < t1 ? zh + static_cast<size_t>(tb + r) * HD : nullptr;
+    });
+    ring_fill<RBY, kBw>(st + kBw * RBX, lane, dgh, [&](int r) -> const void* {
+      return tb + r < t1 ? dgh + static_cast<size_t>(tb + r) * HD : nullptr;
+    });
+  };
 #pragma unroll
-    for (int u = 0; u < kPre; ++u)
-      if (tb + u < t1) {
-        zr[u] = ldr<CPL>(z + (row0 + tb + u) * HD + ch);
-        gr[u] = ldr<CPL>(dg + (row0 + tb + u) * HD + ch);
-      }
-#pragma unroll
-    for (int u = 0; u < kPre; ++u) {
-      if (tb + u < t1) {
-        float o[CPL], zv[CPL], gv[CPL];
-        cvt<CPL>(zr[u], zv);
-        cvt<CPL>(gr[u], gv);
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          const float uu = zv[c] + bias[c];
-          if (a.gate_kind == KDA_GATE_SIGMOID_MIN) {
-            const float sg = sigmoidf_(ea * uu);
-            const float t = gv[c] * a.g_min * sg * (1.f - sg) * ea;
-            o[c] = t;
-            dA += t * uu;
-          } else {
-            o[c] = -gv[c] * ea * sigmoidf_(uu);
-            dA -= gv[c] * ea * softplusf_(uu);
-          }
-          db[c] += o[c];
-        }
-        stv<CPL>(dz + (row0 + tb + u) * HD + ch, o);
-      }
-    }
+  for (int bi = 0; bi < kBwStages - 1; ++bi) {
+    if (bi < nbat) fill(bi);
+    tc::cp_async_commit();
   }
   const Tin* bl = static_cast<const Tin*>(a.beta_logit);
   const Tout* dbt = static_cast<const Tout*>(a.dbeta);
   Tin* dbl = static_cast<Tin*>(a.dbeta_logit);
-  for (int t = t0 + lane; t < t1; t += 32) {
+  for (int t = t0 + lane; t < t1; t += 32) {  // beta while the first batches land
     const size_t i = (row0 + t) * a.H + h;
     const float s = sigmoidf_(ldf(bl + i));
     stf(dbl + i, ldf(dbt + i) * s * (1.f - s));
   }
+  for (int bi = 0; bi < nbat; ++bi) {
+    tc::cp_async_wait<kBwStages - 2>();
+    __syncwarp();
+    if (bi + kBwStages - 1 < nbat) fill(bi + kBwStages - 1);
+    tc::cp_async_commit();
+    const unsigned char* st = ring + (bi % kBwStages) * STG;
+    const int tb = t0 + bi * kBw;
+#pragma unroll
+    for (int u = 0; u < kBw; ++u) {
+      if (tb + u < t1) {
+        float o[CPL], zv[CPL], gv[CPL];
+        ld_row<CPL, Tin>(st + u * RBX, lane, zv);
+        ld_row<CPL, Tout>(st + kBw * RBX + u * RBY, lane, gv);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          const float uu = zv[c] + bias[c];
+          if (a.gate_kind == KDA_GATE_SIGMOID_MIN) {
+            const float sg = sigm<FAST>(ea * uu);
+            const float t = gv[c] * a.g_min * sg * (1.f - sg) * ea;
+            o[c] = t;
+            dA += t * uu;
+          } else {
+            o[c] = -gv[c] * ea * sigm<FAST>(uu);
+            dA -= gv[c] * ea * softplusf_(uu);
+          }
+          db[c] += o[c];
+        }
+        stv<CPL>(dz + static_cast<size_t>(tb + u) * HD, o);
+      }
+    }
+  }
+  tc::cp_async_wait<0>();
+  __syncwarp();
 }
 
 // Partial-sum slab of one block group: [q taps K x H*dk | k taps | v taps K x H*dv | db H*dk | dA H]
@@ -509,10 +678,12 @@ __host__ __device__ inline int slab_off(int role, int H, int dk, int K) {
   return role == 0 ? 0 : role == 1 ? K * H * dk : role == 2 ? 2 * K * H * dk : -1;
 }
 
-template <int CPL, typename Tin, typename Tout>
+template <int CPL, bool VARLEN, typename Tin, typename Tout>
 __global__ void __launch_bounds__(kBwdWarps * 32) prologue_bwd_kernel(const ProArgs a) {
   __shared__ float red[kBwdWarps][4][128];
+  extern __shared__ __align__(16) unsigned char pro_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned char* ring = pro_smem + warp * bwd_ring_bytes<CPL, Tin, Tout>();
   const int s = blockIdx.x * kBwdWarps + warp;
   const int h = blockIdx.y, role = (a.roles >> (4 * blockIdx.z)) & 15;
   constexpr int D = CPL * 32;
@@ -521,8 +692,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32) prologue_bwd_kernel(const ProA
   if (s < a.n_strips) {
     const int b = s / a.spb;
     const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
-    if (role < 3) pro_bwd_conv<CPL, Tin, Tout>(a, role, b, t0, t1, h, lane, acc);
-    else pro_bwd_gate<CPL, Tin, Tout>(a, b, t0, t1, h, lane, acc[0], dA);
+    if (role < 3) pro_bwd_conv<CPL, VARLEN, Tin, Tout>(a, role, b, t0, t1, h, lane, acc, ring);
+    else pro_bwd_gate<CPL, Tin, Tout>(a, b, t0, t1, h, lane, acc[0], dA, ring);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -784,14 +955,30 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecA
   }
 }
 
-template <int CPL, typename Tin, typename Tout>
-int launch_prologue_d(ProArgs& a, int roles, int n_roles, bool bwd, cudaStream_t st) {
+template <int CPL, bool VARLEN, typename Tin, typename Tout>
+int launch_prologue_v(ProArgs& a, int roles, int n_roles, bool bwd, cudaStream_t st) {
   a.roles = roles;
   const int w = bwd ? kBwdWarps : kWarps;
   const dim3 grid((a.n_strips + w - 1) / w, a.H, n_roles);
-  if (bwd) prologue_bwd_kernel<CPL, Tin, Tout><<<grid, w * 32, 0, st>>>(a);
-  else prologue_fwd_kernel<CPL, Tin, Tout><<<grid, w * 32, 0, st>>>(a);
+  static bool done_f[64] = {false}, done_b[64] = {false};
+  if (bwd) {
+    constexpr int smem = kBwdWarps * bwd_ring_bytes<CPL, Tin, Tout>();
+    const int rc = ensure_smem(prologue_bwd_kernel<CPL, VARLEN, Tin, Tout>, smem, done_b);
+    if (rc != KDA_OK) return rc;
+    prologue_bwd_kernel<CPL, VARLEN, Tin, Tout><<<grid, w * 32, smem, st>>>(a);
+  } else {
+    constexpr int smem = kWarps * fwd_ring_bytes<CPL, Tin>();
+    const int rc = ensure_smem(prologue_fwd_kernel<CPL, VARLEN, Tin, Tout>, smem, done_f);
+    if (rc != KDA_OK) return rc;
+    prologue_fwd_kernel<CPL, VARLEN, Tin, Tout><<<grid, w * 32, smem, st>>>(a);
+  }
   return launch_status();
+}
+
+template <int CPL, typename Tin, typename Tout>
+int launch_prologue_d(ProArgs& a, int roles, int n_roles, bool bwd, cudaStream_t st) {
+  return a.cu ? launch_prologue_v<CPL, true, Tin, Tout>(a, roles, n_roles, bwd, st)
+              : launch_prologue_v<CPL, false, Tin, Tout>(a, roles, n_roles, bwd, st);
 }
 
 // q, k and the gates have width dk, v has dv: one launch when they agree.
