@@ -30,12 +30,15 @@ SIGNATURES = {
     "kda_bwd": ([_P] * 14 + [_P, _Z] + [_I] * 9 + [_P], _I),
     "kda_decode": ([_P] * 7 + [_I] * 5 + [_P], _I),
     "kda_bwd_noalloc": ([_P] * 14 + [_I] * 9 + [_P], _I),
+    "kda_fwd_varlen": ([_P] * 10 + [_I] * 9 + [_P], _I),
+    "kda_bwd_varlen_workspace_bytes": ([_I] * 7, _Z),
+    "kda_bwd_varlen": ([_P] * 15 + [_Z, _P] + [_I] * 9 + [_P], _I),
     # include/kda_mixer.h
-    "kda_prologue_fwd": ([_P] * 10 + [_F, _I] + [_P] * 3 + [_I] + [_P] * 5 + [_I] * 8 + [_P], _I),
+    "kda_prologue_fwd": ([_P] * 10 + [_F, _I] + [_P] * 3 + [_I] + [_P] * 6 + [_I] * 8 + [_P], _I),
     "kda_prologue_bwd_workspace_bytes": ([_I] * 6, _Z),
-    "kda_prologue_bwd": ([_P] * 10 + [_F, _I, _P, _P, _I] + [_P] * 17 + [_Z] + [_I] * 8 + [_P], _I),
-    "kda_gated_rmsnorm_fwd": ([_P] * 3 + [_I] * 3 + [_F] + [_I] * 3 + [_P], _I),
-    "kda_gated_rmsnorm_bwd": ([_P] * 5 + [_I] * 3 + [_F] + [_I] * 3 + [_P], _I),
+    "kda_prologue_bwd": ([_P] * 10 + [_F, _I, _P, _P, _I] + [_P] * 18 + [_Z] + [_I] * 8 + [_P], _I),
+    "kda_gated_rmsnorm_fwd": ([_P] * 5 + [_I] * 4 + [_F] + [_I] * 3 + [_P], _I),
+    "kda_gated_rmsnorm_bwd": ([_P] * 7 + [_I] * 4 + [_F] + [_I] * 3 + [_P], _I),
     "kda_decode_fused": ([_P] * 13 + [_F, _I, _F, _P] + [_I] * 7 + [_P], _I),
 }
 

@@ -63,7 +63,7 @@ constexpr int SEQ_SMEM = Q_BAR + 64;
 __global__ void __launch_bounds__(NT, 1)
 bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
                const unsigned char* __restrict__ factors, const float* __restrict__ dsT,
-               float* __restrict__ ds0, bf16* __restrict__ dsw, int T, int H,
+               float* __restrict__ ds0, bf16* __restrict__ dsw, int T, int H, const int* __restrict__ cs,
                int* __restrict__ err, const __grid_constant__ CUtensorMap tm_do, int use_tma) {
   extern __shared__ __align__(1024) unsigned char sm[];
   float* beta_s = reinterpret_cast<float*>(sm + Q_BETA);
@@ -72,12 +72,18 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
   uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + Q_BAR + 16);  // [2]: one per operand set
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;
-  const int h = blockIdx.x % H, b = blockIdx.x / H;
+  // CTA (seq, h) walks the chunks [c_beg, c_end) of batch row b in reverse: the
+  // whole row, or with packed sequences (cs: chunk offsets, B = 1) the sequence's range
+  const int h = blockIdx.x % H, seq = blockIdx.x / H;
+  const int b = cs ? 0 : seq;
   const int n_chunks = (T + C - 1) / C;
+  const int c_beg = cs ? min(max(cs[seq], 0), n_chunks) : 0;  // clamped like the forward's
+  const int c_end = cs ? min(max(cs[seq + 1], c_beg), n_chunks) : n_chunks;
   const size_t tok0 = static_cast<size_t>(b) * T;
   const size_t rstride = static_cast<size_t>(H) * DK;
   const bf16* doh = dout + static_cast<size_t>(h) * DV;
-  const size_t unit = static_cast<size_t>(b) * H + h;
+  const size_t unit = static_cast<size_t>(b) * H + h;   // checkpoint row
+  const size_t sunit = static_cast<size_t>(seq) * H + h;  // state (dS_T, dS_0) row
   auto set_gc = [](int ps) { return ps ? Q_GC1 : Q_GC0; };
   uint32_t ld_par = 0u, ld_pending = 0u;  // bit ps: phase parity / loads in flight of set ps
 
@@ -114,7 +120,7 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     ld_pending |= 1u << ps;
     beta_nx = ld_bf16_raw(beta + (tok0 + t0 + tid) * H + h, tid < rv);
   };
-  issue_chunk(n_chunks - 1);
+  if (c_beg < c_end) issue_chunk(c_end - 1);
   const uint32_t tbase = *tslot;
   const uint32_t T_DS = tbase, T_U = tbase + 384;
   const uint32_t tl = lane_off(qw);
@@ -132,14 +138,14 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
       const int c0 = hh * 64 + half * 32;
       float vals[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) vals[j] = dsT ? dsT[(unit * DK + d) * DV + c0 + j] : 0.f;
+      for (int j = 0; j < 32; ++j) vals[j] = dsT ? dsT[(sunit * DK + d) * DV + c0 + j] : 0.f;
       tmem_st32(T_DS + tl + c0, vals);
     }
     tmem_wait_st();
   }
 
   KDA_PT_INIT();
-  for (int c = n_chunks - 1; c >= 0; --c) {
+  for (int c = c_end - 1; c >= c_beg; --c) {
     const int p = c & 1;
     cp_async_wait<0>();
     failed |= !mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
@@ -151,7 +157,7 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     KDA_PT(1, 0);
     const float* gamC = reinterpret_cast<const float*>(sm + set_gc(p));
     const uint32_t set = smem_u32(sm + p * Q_SET);
-    if (c > 0) issue_chunk(c - 1);  // the other set was last read by chunk c + 1
+    if (c > c_beg) issue_chunk(c - 1);  // the other set was last read by chunk c + 1
     KDA_PT(1, 1);
     {  // dS' pass: bf16 operand (stored to the workspace below), then dS *= Gam_C
       const int d = 32 * qw + lane;
@@ -233,7 +239,7 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
       float vals[32];
       tmem_ld32(T_DS + tl + c0, vals);
       tmem_wait_ld();
-      store_row32<float>(ds0 + (unit * DK + d) * DV + c0, vals);
+      store_row32<float>(ds0 + (sunit * DK + d) * DV + c0, vals);
     }
   }
   if (failed && tid == 0 && err) atomicExch(err, 1);
@@ -1007,7 +1013,7 @@ template <typename Tc>
 int launch_bwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
                const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
-               cudaStream_t st) {
+               const int* cs, int n_seqs, cudaStream_t st) {
   static bool done_seq[64] = {false}, done_par[64] = {false};
   int rc = ensure_smem(bwd_seq_kernel, SEQ_SMEM, done_seq);
   if (rc != KDA_OK) return rc;
@@ -1027,8 +1033,11 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
   int use_tma = 1;
   for (int i = 0; i < 5 && use_tma; ++i) use_tma = make_tile_map(&tm[i], srcs[i], B, T, H) ? 1 : 0;
   for (int i = 0; i < 4 && use_tma; ++i) use_tma = make_out_map(&to[i], outs[i], B, T, H) ? 1 : 0;
-  bwd_seq_kernel<<<B * H, NT, SEQ_SMEM, st>>>(static_cast<const bf16*>(beta), static_cast<const bf16*>(dout),
-                                              factors, dsT, ds0, dsw, T, H, err, tm[4], use_tma);
+  // the reverse state chain per sequence (batch row, or packed sequence); the
+  // chunks themselves are then independent units of one launch
+  bwd_seq_kernel<<<(cs ? n_seqs : B) * H, NT, SEQ_SMEM, st>>>(
+      static_cast<const bf16*>(beta), static_cast<const bf16*>(dout), factors, dsT, ds0, dsw, T, H, cs, err,
+      tm[4], use_tma);
   rc = launch_status();
   if (rc != KDA_OK) return rc;
   const long long units = static_cast<long long>(B) * H * ((T + C - 1) / C);
@@ -1056,11 +1065,13 @@ size_t tc_bwd_workspace_bytes(int B, int T, int H) {
 int tc_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                   const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                   void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
-                  int ck_dt, cudaStream_t st) {
+                  int ck_dt, const int* cs, int n_seqs, cudaStream_t st) {
   if (ck_dt == KDA_BF16)
-    return launch_bwd<bf16>(q, k, v, g, beta, s_ckpt, dout, dsT, dq, dk_, dv_, dg, dbeta, ds0, work, B, T, H, st);
+    return launch_bwd<bf16>(q, k, v, g, beta, s_ckpt, dout, dsT, dq, dk_, dv_, dg, dbeta, ds0, work, B, T, H,
+                            cs, n_seqs, st);
   if (ck_dt == KDA_F32)
-    return launch_bwd<float>(q, k, v, g, beta, s_ckpt, dout, dsT, dq, dk_, dv_, dg, dbeta, ds0, work, B, T, H, st);
+    return launch_bwd<float>(q, k, v, g, beta, s_ckpt, dout, dsT, dq, dk_, dv_, dg, dbeta, ds0, work, B, T, H,
+                             cs, n_seqs, st);
   return KDA_ERR_DTYPE;
 }
 

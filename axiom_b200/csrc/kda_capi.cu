@@ -12,23 +12,24 @@ int decode_launch(float* S, const void* q, const void* k, const void* v, const v
 size_t simt_bwd_workspace_bytes(int B, int H, int dk, int dv, int C);
 int simt_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                     const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
-                    int dk, int dv, int C, int in_dt, int o_dt, int ck_dt, cudaStream_t st);
+                    int dk, int dv, int C, int in_dt, int o_dt, int ck_dt, const int* cs, int n_seqs,
+                    cudaStream_t st);
 bool tc_fwd_supported(int dk, int dv, int C_, int in_dt);
 constexpr size_t kTcFactorBytes = FAC_UNIT;  // factor block per chunk-head (kda_ckpt_layout.h)
 int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                   const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
-                  int o_dt, int ck_dt, cudaStream_t st);
+                  int o_dt, int ck_dt, const int* cs, int n_seqs, cudaStream_t st);
 bool tc_bwd_supported(int dk, int dv, int C_, int in_dt, int do_dt);
 size_t tc_bwd_workspace_bytes(int B, int T, int H);
 int tc_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                   const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                   void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
-                  int ck_dt, cudaStream_t st);
+                  int ck_dt, const int* cs, int n_seqs, cudaStream_t st);
 int simt_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                     const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                     void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T,
                     int H, int dk, int dv, int C, int in_dt, int do_dt, int ck_dt,
-                    int states_cm, cudaStream_t st);
+                    int states_cm, const int* cs, int n_seqs, cudaStream_t st);
 }  // namespace kda
 
 namespace {
@@ -78,9 +79,14 @@ size_t kda_ckpt_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dty
   return bytes;
 }
 
-int kda_fwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
-            const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H, int dk,
-            int dv, int chunk, int in_dtype, int o_dtype, int ckpt_dtype, kda_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+int fwd_impl(const void* q, const void* k, const void* v, const void* g, const void* beta,
+             const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H, int dk,
+             int dv, int chunk, int in_dtype, int o_dtype, int ckpt_dtype, const int* cs, int n_seqs,
+             kda_stream_t stream) {
   int rc = check_dims(B, T, H, dk, dv, chunk);
   if (rc != KDA_OK) return rc;
   if (!valid_dtype(in_dtype) || !valid_dtype(o_dtype) || !valid_dtype(ckpt_dtype))
@@ -101,16 +107,16 @@ int kda_fwd(const void* q, const void* k, const void* v, const void* g, const vo
         !kda::aligned16(o) || (s_ckpt && !kda::aligned16(s_ckpt)) || (s_out && !kda::aligned16(s_out)) ||
         (s0 && !kda::aligned16(s0)))
       return KDA_ERR_ALIGN;
-    return kda::tc_fwd_launch(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, o_dtype, ckpt_dtype,
-                              stream);
+    return kda::tc_fwd_launch(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, o_dtype, ckpt_dtype, cs,
+                              n_seqs, stream);
   }
   return kda::simt_fwd_launch(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, dk, dv, chunk,
-                              in_dtype, o_dtype, ckpt_dtype, stream);
+                              in_dtype, o_dtype, ckpt_dtype, cs, n_seqs, stream);
 }
 
-size_t kda_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dtype) {
+size_t bwd_ws_impl(int B, int n_state_rows, int T, int H, int dk, int dv, int chunk, int in_dtype) {
   if (check_dims(B, T, H, dk, dv, chunk) != KDA_OK) return 0;
-  size_t n = kda::simt_bwd_workspace_bytes(B, H, dk, dv, chunk);
+  size_t n = kda::simt_bwd_workspace_bytes(n_state_rows, H, dk, dv, chunk);
   if (kda::tc_bwd_supported(dk, dv, chunk, in_dtype, KDA_BF16)) {
     const size_t t = kda::tc_bwd_workspace_bytes(B, T, H);
     if (t > n) n = t;
@@ -118,11 +124,11 @@ size_t kda_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, i
   return n;
 }
 
-int kda_bwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
-            const void* s_ckpt, const void* do_, const float* dsT, void* dq, void* dk_, void* dv_,
-            void* dg, void* dbeta, float* ds0, void* workspace, size_t workspace_bytes, int B,
-            int T, int H, int dk, int dv, int chunk, int in_dtype, int do_dtype, int ckpt_dtype,
-            kda_stream_t stream) {
+int bwd_impl(const void* q, const void* k, const void* v, const void* g, const void* beta,
+             const void* s_ckpt, const void* do_, const float* dsT, void* dq, void* dk_, void* dv_,
+             void* dg, void* dbeta, float* ds0, void* workspace, size_t workspace_bytes, int B,
+             int T, int H, int dk, int dv, int chunk, int in_dtype, int do_dtype, int ckpt_dtype,
+             const int* cs, int n_seqs, kda_stream_t stream) {
   int rc = check_dims(B, T, H, dk, dv, chunk);
   if (rc != KDA_OK) return rc;
   if (!valid_dtype(in_dtype) || !valid_dtype(do_dtype) || !valid_dtype(ckpt_dtype))
@@ -146,15 +152,95 @@ int kda_bwd(const void* q, const void* k, const void* v, const void* g, const vo
     for (const void* p : ptrs)
       if (!kda::aligned16(p)) return KDA_ERR_ALIGN;
     return kda::tc_bwd_launch(q, k, v, g, beta, s_ckpt, do_, dsT, dq, dk_, dv_, dg, dbeta, ds0,
-                              workspace, B, T, H, ckpt_dtype, stream);
+                              workspace, B, T, H, ckpt_dtype, cs, n_seqs, stream);
   }
-  const size_t need = kda::simt_bwd_workspace_bytes(B, H, dk, dv, chunk);
+  const size_t need = kda::simt_bwd_workspace_bytes(cs ? n_seqs : B, H, dk, dv, chunk);
   if (need && (!workspace || workspace_bytes < need)) return KDA_ERR_WORKSPACE;
   // a bf16 checkpoint written by the tensor-core forward holds operand images
   const int states_cm = kda::tc_fwd_supported(dk, dv, chunk, in_dtype) && ckpt_dtype == KDA_BF16;
   return kda::simt_bwd_launch(q, k, v, g, beta, s_ckpt, do_, dsT, dq, dk_, dv_, dg, dbeta, ds0,
                               workspace, B, T, H, dk, dv, chunk, in_dtype, do_dtype, ckpt_dtype,
-                              states_cm, stream);
+                              states_cm, cs, n_seqs, stream);
+}
+
+// Packed sequences: row 0 of a B = 1 batch holds n_seqs chunk-aligned sequences.
+int check_packing(const int* cs, int n_seqs, int T, int chunk) {
+  if (n_seqs < 0 || n_seqs > 65535 * 256) return KDA_ERR_SHAPE;
+  if (chunk <= 0 || T < 0 || T % chunk != 0) return KDA_ERR_SHAPE;
+  if (n_seqs > 0 && !cs) return KDA_ERR_NULL;
+  return KDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kda_fwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
+            const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H, int dk,
+            int dv, int chunk, int in_dtype, int o_dtype, int ckpt_dtype, kda_stream_t stream) {
+  return fwd_impl(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, dk, dv, chunk, in_dtype, o_dtype,
+                  ckpt_dtype, nullptr, 0, stream);
+}
+
+int kda_fwd_varlen(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                   const float* s0, void* o, float* s_out, void* s_ckpt, const int* chunk_offsets,
+                   int n_seqs, int T, int H, int dk, int dv, int chunk, int in_dtype, int o_dtype,
+                   int ckpt_dtype, kda_stream_t stream) {
+  int rc = check_packing(chunk_offsets, n_seqs, T, chunk);
+  if (rc != KDA_OK) return rc;
+  rc = check_dims(1, T, H, dk, dv, chunk);
+  if (rc != KDA_OK || n_seqs == 0 || H == 0) return rc;
+  if (T == 0) {  // empty sequences: S_T = S0
+    if (!s_out) return KDA_OK;
+    const size_t bytes = static_cast<size_t>(n_seqs) * H * dk * dv * sizeof(float);
+    cudaError_t e = s0 ? cudaMemcpyAsync(s_out, s0, bytes, cudaMemcpyDeviceToDevice, stream)
+                       : cudaMemsetAsync(s_out, 0, bytes, stream);
+    return e == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+  }
+  return fwd_impl(q, k, v, g, beta, s0, o, s_out, s_ckpt, 1, T, H, dk, dv, chunk, in_dtype, o_dtype,
+                  ckpt_dtype, chunk_offsets, n_seqs, stream);
+}
+
+size_t kda_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dtype) {
+  return bwd_ws_impl(B, B, T, H, dk, dv, chunk, in_dtype);
+}
+
+size_t kda_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv, int chunk,
+                                      int in_dtype) {
+  if (n_seqs < 0) return 0;
+  return bwd_ws_impl(1, n_seqs, T, H, dk, dv, chunk, in_dtype);
+}
+
+int kda_bwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
+            const void* s_ckpt, const void* do_, const float* dsT, void* dq, void* dk_, void* dv_,
+            void* dg, void* dbeta, float* ds0, void* workspace, size_t workspace_bytes, int B,
+            int T, int H, int dk, int dv, int chunk, int in_dtype, int do_dtype, int ckpt_dtype,
+            kda_stream_t stream) {
+  return bwd_impl(q, k, v, g, beta, s_ckpt, do_, dsT, dq, dk_, dv_, dg, dbeta, ds0, workspace,
+                  workspace_bytes, B, T, H, dk, dv, chunk, in_dtype, do_dtype, ckpt_dtype, nullptr, 0,
+                  stream);
+}
+
+int kda_bwd_varlen(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                   const void* s_ckpt, const void* do_, const float* dsT, void* dq, void* dk_,
+                   void* dv_, void* dg, void* dbeta, float* ds0, void* workspace,
+                   size_t workspace_bytes, const int* chunk_offsets, int n_seqs, int T, int H,
+                   int dk, int dv, int chunk, int in_dtype, int do_dtype, int ckpt_dtype,
+                   kda_stream_t stream) {
+  int rc = check_packing(chunk_offsets, n_seqs, T, chunk);
+  if (rc != KDA_OK) return rc;
+  rc = check_dims(1, T, H, dk, dv, chunk);
+  if (rc != KDA_OK || n_seqs == 0 || H == 0) return rc;
+  if (T == 0) {  // empty sequences: dS0 = dS_T
+    if (!ds0) return KDA_OK;
+    const size_t bytes = static_cast<size_t>(n_seqs) * H * dk * dv * sizeof(float);
+    cudaError_t e = dsT ? cudaMemcpyAsync(ds0, dsT, bytes, cudaMemcpyDeviceToDevice, stream)
+                        : cudaMemsetAsync(ds0, 0, bytes, stream);
+    return e == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+  }
+  return bwd_impl(q, k, v, g, beta, s_ckpt, do_, dsT, dq, dk_, dv_, dg, dbeta, ds0, workspace,
+                  workspace_bytes, 1, T, H, dk, dv, chunk, in_dtype, do_dtype, ckpt_dtype, chunk_offsets,
+                  n_seqs, stream);
 }
 
 int kda_decode(float* S, const void* q, const void* k, const void* v, const void* g,

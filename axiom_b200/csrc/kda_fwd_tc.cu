@@ -66,7 +66,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
               const bf16* __restrict__ g, const bf16* __restrict__ beta,
               const float* __restrict__ s0, To* __restrict__ o, float* __restrict__ s_out,
               Tc* __restrict__ s_ckpt, unsigned char* __restrict__ factors, int T, int H,
-              int* __restrict__ err, const __grid_constant__ CUtensorMap tm_q,
+              const int* __restrict__ cs, int* __restrict__ err, const __grid_constant__ CUtensorMap tm_q,
               const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_g,
               const __grid_constant__ CUtensorMap tm_v, int use_tma) {
   extern __shared__ __align__(1024) unsigned char sm[];
@@ -79,9 +79,15 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;  // TMEM lane quarter, column half
-  const int h = blockIdx.x % H, b = blockIdx.x / H;
+  // CTA (seq, h) walks the chunks [c_beg, c_end) of batch row b: the whole row,
+  // or with packed sequences (cs: chunk offsets, B = 1) the sequence's range
+  const int h = blockIdx.x % H, seq = blockIdx.x / H;
+  const int b = cs ? 0 : seq;
   const int n_chunks = (T + C - 1) / C;
-  const size_t tok0 = static_cast<size_t>(b) * T;   // first token row of this sequence
+  // (clamped: a malformed table cannot take a chunk outside the tensors)
+  const int c_beg = cs ? min(max(cs[seq], 0), n_chunks) : 0;
+  const int c_end = cs ? min(max(cs[seq + 1], c_beg), n_chunks) : n_chunks;
+  const size_t tok0 = static_cast<size_t>(b) * T;   // first token row of batch row b
   const size_t head_off = static_cast<size_t>(h) * DK;
   const bf16* qh = q + head_off;
   const bf16* kh = k + head_off;
@@ -116,11 +122,15 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     }
   };
   __syncthreads();  // mbar_in initialised
-  stage(0, true);
-  stage(0, false);
+  const bool any = c_beg < c_end;
+  if (any) {
+    stage(c_beg, true);
+    stage(c_beg, false);
+  }
   // raw bf16 beta of the chunk to come, loaded one chunk ahead
-  unsigned short beta_nx = ld_bf16_raw(beta + tok0 * H + static_cast<size_t>(tid) * H + h, tid < min(C, T));
-  bool in_pending = use_tma != 0;  // TMA loads issued and not yet waited, for chunk parity in_par
+  const size_t t_beg = static_cast<size_t>(c_beg) * C;
+  unsigned short beta_nx = ld_bf16_raw(beta + (tok0 + t_beg + tid) * H + h, any && tid < min(C, T - static_cast<int>(t_beg)));
+  bool in_pending = use_tma != 0 && any;  // TMA loads issued and not yet waited, for chunk parity in_par
   uint32_t in_par = 0u;
   tc_fence_before();
   __syncthreads();
@@ -136,7 +146,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   // S0 -> TMEM (row d = lane, 64 columns per warp)
   {
     const int d = 32 * qw + lane;
-    const size_t sb = ((static_cast<size_t>(b) * H + h) * DK + d) * DV;
+    const size_t sb = ((static_cast<size_t>(seq) * H + h) * DK + d) * DV;
     for (int half = 0; half < 2; ++half) {
       float vals[32];
       const int c0 = hh * 64 + half * 32;
@@ -174,17 +184,17 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   __syncthreads();
 
   KDA_PT_INIT();
-  for (int c = 0; c < n_chunks; ++c) {
+  for (int c = c_beg; c < c_end; ++c) {
     const int t0 = c * C;
     const int rows_valid = min(C, T - t0);
     cp_async_wait<0>();
     if (use_tma) {
-      failed |= !mbar_wait(mbar_in, static_cast<uint32_t>(c) & 1u);
+      failed |= !mbar_wait(mbar_in, static_cast<uint32_t>(c - c_beg) & 1u);
       in_pending = false;
     }
     if (tid == kIoThread) bulk_wait_read();  // the previous state image in SB has been stored
     if (tid < C) beta_s[tid] = bf16_raw_to_float(beta_nx);
-    if (c + 1 < n_chunks)
+    if (c + 1 < c_end)
       beta_nx = ld_bf16_raw(beta + (tok0 + t0 + C + tid) * H + h, tid < min(C, T - t0 - C));
     if (__syncthreads_or(failed)) break;
 
@@ -309,10 +319,10 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         }
         if (tid == kIoThread) store_prep(false);
         // prefetch the next chunk's q, k, g (staging is free)
-        if (c + 1 < n_chunks) {
+        if (c + 1 < c_end) {
           stage(c + 1, true);
           in_pending = use_tma != 0;
-          in_par = static_cast<uint32_t>(c + 1) & 1u;
+          in_par = static_cast<uint32_t>(c + 1 - c_beg) & 1u;
         }
         failed |= !mma_wait();
         if (__syncthreads_or(failed)) break;
@@ -326,10 +336,10 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         if (tid == kIoThread) store_prep(true);
         scores_exact(sm + OFF_SQ, sm + OFF_SK, Gf, Aq, Akk);
         __syncthreads();
-        if (c + 1 < n_chunks) {
+        if (c + 1 < c_end) {
           stage(c + 1, true);
           in_pending = use_tma != 0;
-          in_par = static_cast<uint32_t>(c + 1) & 1u;
+          in_par = static_cast<uint32_t>(c + 1 - c_beg) & 1u;
         }
       }
     }
@@ -415,7 +425,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     failed |= !mma_wait();
     if (tid == kIoThread) bulk_wait_read();  // Q Gam has been stored: E2 overwrites it with Q~
     if (__syncthreads_or(failed)) break;
-    if (c + 1 < n_chunks) stage(c + 1, false);
+    if (c + 1 < c_end) stage(c + 1, false);
     KDA_PT(0, 6);
     // ---------------- E2: W -> A3[0:64), Q~ = Gam Q - Aqk W -> A3[64:128) ----------------
     {
@@ -540,7 +550,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
 
   if (!failed && s_out) {
     const int d = 32 * qw + lane;
-    float* so = s_out + ((static_cast<size_t>(b) * H + h) * DK + d) * DV;
+    float* so = s_out + ((static_cast<size_t>(seq) * H + h) * DK + d) * DV;
     for (int half = 0; half < 2; ++half) {
       const int c0 = hh * 64 + half * 32;
       float vals[32];
@@ -566,7 +576,7 @@ __device__ int g_fwd_tc_error = 0;
 template <typename To, typename Tc>
 int launch_t(const void* q, const void* k, const void* v, const void* g, const void* beta,
              const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
-             cudaStream_t st) {
+             const int* cs, int n_seqs, cudaStream_t st) {
   static bool done[64] = {false};
   auto kern = fwd_tc_kernel<To, Tc>;
   int rc = ensure_smem(kern, SMEM_BYTES, done);
@@ -584,10 +594,10 @@ int launch_t(const void* q, const void* k, const void* v, const void* g, const v
   const void* srcs[4] = {q, k, g, v};
   int use_tma = 1;
   for (int i = 0; i < 4 && use_tma; ++i) use_tma = make_tile_map(&tm[i], srcs[i], B, T, H) ? 1 : 0;
-  kern<<<B * H, NT, SMEM_BYTES, st>>>(
+  kern<<<(cs ? n_seqs : B) * H, NT, SMEM_BYTES, st>>>(
       static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v),
       static_cast<const bf16*>(g), static_cast<const bf16*>(beta), s0, static_cast<To*>(o), s_out,
-      static_cast<Tc*>(s_ckpt), factors, T, H, err, tm[0], tm[1], tm[2], tm[3], use_tma);
+      static_cast<Tc*>(s_ckpt), factors, T, H, cs, err, tm[0], tm[1], tm[2], tm[3], use_tma);
   return launch_status();
 }
 
@@ -599,12 +609,12 @@ bool tc_fwd_supported(int dk, int dv, int C_, int in_dt) {
 
 int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                   const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
-                  int o_dt, int ck_dt, cudaStream_t st) {
-  if (static_cast<long long>(B) * H > 0x7fffffffLL) return KDA_ERR_SHAPE;
-  if (o_dt == KDA_BF16 && ck_dt == KDA_BF16) return launch_t<bf16, bf16>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, st);
-  if (o_dt == KDA_BF16 && ck_dt == KDA_F32) return launch_t<bf16, float>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, st);
-  if (o_dt == KDA_F32 && ck_dt == KDA_BF16) return launch_t<float, bf16>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, st);
-  if (o_dt == KDA_F32 && ck_dt == KDA_F32) return launch_t<float, float>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, st);
+                  int o_dt, int ck_dt, const int* cs, int n_seqs, cudaStream_t st) {
+  if (static_cast<long long>(cs ? n_seqs : B) * H > 0x7fffffffLL) return KDA_ERR_SHAPE;
+  if (o_dt == KDA_BF16 && ck_dt == KDA_BF16) return launch_t<bf16, bf16>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, cs, n_seqs, st);
+  if (o_dt == KDA_BF16 && ck_dt == KDA_F32) return launch_t<bf16, float>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, cs, n_seqs, st);
+  if (o_dt == KDA_F32 && ck_dt == KDA_BF16) return launch_t<float, bf16>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, cs, n_seqs, st);
+  if (o_dt == KDA_F32 && ck_dt == KDA_F32) return launch_t<float, float>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, cs, n_seqs, st);
   return KDA_ERR_DTYPE;
 }
 

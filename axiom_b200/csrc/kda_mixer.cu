@@ -171,6 +171,7 @@ struct ProArgs {
   float* st_out;
   const int* cu;
   int n_seqs;
+  const int* out_rows;  // packed: row of each sequence's first token in q, k, v, g (and their cotangents)
   void* y[4];  // q, k, v, g
   void* beta;
   // backward
@@ -207,6 +208,29 @@ __device__ __forceinline__ int seq_of(const int* cu, int n, int t) {
     else hi = mid - 1;
   }
   return lo;
+}
+
+// Row of packed token t in the outputs (and, backward, the output cotangents):
+// t itself, or with out_rows the chunk-aligned row of its sequence.
+__device__ __forceinline__ int out_row(const ProArgs& a, int t) {
+  if (!a.out_rows) return t;
+  const int s = seq_of(a.cu, a.n_seqs, t);
+  return t + __ldg(a.out_rows + s) - __ldg(a.cu + s);
+}
+
+// Zeroes this lane's channels of the pad rows of every sequence ending in
+// (t0, t1]: the rows between its last token and the next sequence's first row.
+template <int CPL, typename T>
+__device__ void zero_pads(const ProArgs& a, T* base, int HD, int t0, int t1) {
+  if (!a.out_rows) return;
+  const float z[CPL] = {};
+  for (int s = seq_of(a.cu, a.n_seqs, t0); s < a.n_seqs; ++s) {
+    const int e = __ldg(a.cu + s + 1);
+    if (e > t1) break;
+    const int r1 = __ldg(a.out_rows + s + 1);
+    for (int r = __ldg(a.out_rows + s) + e - __ldg(a.cu + s); r < r1; ++r)
+      stv<CPL>(base + static_cast<size_t>(r) * HD, z);
+  }
 }
 
 // fp32 conv-state column of (role, head) and row width
@@ -259,11 +283,12 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int c = 0; c < CPL; ++c) wt[i][c] = i < a.K ? pick(a.w, role)[i * HD + ch + c] : 0.f;
-  int si = 0, lb = 0, nb = INT_MAX;
+  int si = 0, lb = 0, nb = INT_MAX, shift = 0;  // shift: output row - token of this sequence
   if constexpr (VARLEN) {
     si = seq_of(a.cu, a.n_seqs, t0);
     lb = __ldg(a.cu + si);
     nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+    shift = a.out_rows ? __ldg(a.out_rows + si) - lb : 0;
   }
   const int nbat = (t1 - t0 + kPre - 1) / kPre;
   auto fill = [&](int bi) {
@@ -296,6 +321,7 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     const unsigned char* st = ring + (bi % kStages) * STG;
     const int tb = t0 + bi * kPre;
     float s[kPre][CPL], ss[kPre];
+    int sh[kPre];
 #pragma unroll
     for (int u = 0; u < kPre; ++u) {
       float xv[CPL];
@@ -307,7 +333,9 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
           for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
         ++si;
         nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+        shift = a.out_rows ? __ldg(a.out_rows + si) - __ldg(a.cu + si) : 0;
       }
+      sh[u] = shift;
       ss[u] = 0.f;
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {
@@ -330,10 +358,11 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     }
 #pragma unroll
     for (int u = 0; u < kPre; ++u)
-      if (tb + u < t1) stv<CPL>(y + static_cast<size_t>(tb + u) * HD, s[u]);
+      if (tb + u < t1) stv<CPL>(y + static_cast<size_t>(tb + u + sh[u]) * HD, s[u]);
   }
   tc::cp_async_wait<0>();
   __syncwarp();
+  if constexpr (VARLEN) zero_pads<CPL>(a, y, HD, t0, t1);
   if (a.st_out && t1 == a.T) {  // this strip ends the sequence: its last K-1 inputs
     const int sw = a.H * (2 * a.dk + a.dv);
     for (int j = 0; j < a.K - 1; ++j) {
@@ -349,7 +378,7 @@ __device__ __forceinline__ float gate_fwd(float u, float ea, float g_min, int ki
   return kind == KDA_GATE_SIGMOID_MIN ? g_min * sigm<FAST>(ea * u) : -ea * softplusf_(u);
 }
 
-template <int CPL, typename Tin, typename Tout>
+template <int CPL, bool VARLEN, typename Tin, typename Tout>
 __device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane, unsigned char* ring) {
   constexpr bool FAST = std::is_same<Tout, bf16>::value;
   constexpr int D = CPL * 32, RB = D * static_cast<int>(sizeof(Tin)), STG = kPre * RB;
@@ -378,7 +407,17 @@ __device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
   Tout* beta = static_cast<Tout*>(a.beta);
   for (int t = t0 + lane; t < t1; t += 32) {  // beta while the first batches land
     const size_t i = (row0 + t) * a.H + h;
-    stf(beta + i, sigmoidf_(ldf(bl + i)));
+    const int r = VARLEN ? out_row(a, t) : t;
+    stf(beta + (row0 + r) * a.H + h, sigmoidf_(ldf(bl + i)));
+  }
+  if (VARLEN && a.out_rows && lane == 0) {  // beta of the pad rows
+    for (int s = seq_of(a.cu, a.n_seqs, t0); s < a.n_seqs; ++s) {
+      const int e = __ldg(a.cu + s + 1);
+      if (e > t1) break;
+      const int r1 = __ldg(a.out_rows + s + 1);
+      for (int r = __ldg(a.out_rows + s) + e - __ldg(a.cu + s); r < r1; ++r)
+        stf(beta + static_cast<size_t>(r) * a.H + h, 0.f);
+    }
   }
   for (int bi = 0; bi < nbat; ++bi) {
     tc::cp_async_wait<kStages - 2>();
@@ -394,12 +433,14 @@ __device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
         ld_row<CPL, Tin>(st + u * RB, lane, o);
 #pragma unroll
         for (int c = 0; c < CPL; ++c) o[c] = gate_fwd<FAST>(o[c] + bias[c], ea, a.g_min, a.gate_kind);
-        stv<CPL>(g + static_cast<size_t>(tb + u) * HD, o);
+        const int r = VARLEN ? out_row(a, tb + u) : tb + u;
+        stv<CPL>(g + static_cast<size_t>(r) * HD, o);
       }
     }
   }
   tc::cp_async_wait<0>();
   __syncwarp();
+  if constexpr (VARLEN) zero_pads<CPL>(a, g, HD, t0, t1);
 }
 
 // blockIdx.z selects the tensor: role = 4-bit field z of a.roles (0 q, 1 k,
@@ -415,7 +456,7 @@ __global__ void __launch_bounds__(kWarps * 32) prologue_fwd_kernel(const ProArgs
   const int b = s / a.spb;
   const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
   if (role < 3) pro_fwd_conv<CPL, VARLEN, Tin, Tout>(a, role, b, t0, t1, h, lane, ring);
-  else pro_fwd_gate<CPL, Tin, Tout>(a, b, t0, t1, h, lane, ring);
+  else pro_fwd_gate<CPL, VARLEN, Tin, Tout>(a, b, t0, t1, h, lane, ring);
 }
 
 // --------------------------------------------------------------- backward ----
@@ -459,9 +500,13 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
       const int t = base - NX - r;
       return t >= 0 ? xh + static_cast<size_t>(t) * HD : nullptr;
     });
+    int rw[kBw];  // cotangent row of token base - u
+#pragma unroll
+    for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && base - u >= 0 ? out_row(a, base - u) : base - u;
     ring_fill<RBY, kBw>(st + kBw * RBX, lane, dyh, [&](int r) -> const void* {
       const int t = base - r;
-      return t >= 0 && t >= lo ? dyh + static_cast<size_t>(t) * HD : nullptr;
+      const int row = r == 0 ? rw[0] : r == 1 ? rw[1] : r == 2 ? rw[2] : rw[3];
+      return t >= 0 && t >= lo ? dyh + static_cast<size_t>(row) * HD : nullptr;
     });
   };
 #pragma unroll
@@ -597,7 +642,7 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
   __syncwarp();
 }
 
-template <int CPL, typename Tin, typename Tout>
+template <int CPL, bool VARLEN, typename Tin, typename Tout>
 __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane, float (&db)[4],
                              float& dA, unsigned char* ring) {
   constexpr bool FAST = std::is_same<Tin, bf16>::value;
@@ -621,8 +666,12 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
     ring_fill<RBX, kBw>(st, lane, zh, [&](int r) -> const void* {
       return tb + r < t1 ? zh + static_cast<size_t>(tb + r) * HD : nullptr;
     });
+    int rw[kBw];  // cotangent row of token tb + u
+#pragma unroll
+    for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && tb + u < t1 ? out_row(a, tb + u) : tb + u;
     ring_fill<RBY, kBw>(st + kBw * RBX, lane, dgh, [&](int r) -> const void* {
-      return tb + r < t1 ? dgh + static_cast<size_t>(tb + r) * HD : nullptr;
+      const int row = r == 0 ? rw[0] : r == 1 ? rw[1] : r == 2 ? rw[2] : rw[3];
+      return tb + r < t1 ? dgh + static_cast<size_t>(row) * HD : nullptr;
     });
   };
 #pragma unroll
@@ -636,7 +685,8 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
   for (int t = t0 + lane; t < t1; t += 32) {  // beta while the first batches land
     const size_t i = (row0 + t) * a.H + h;
     const float s = sigmoidf_(ldf(bl + i));
-    stf(dbl + i, ldf(dbt + i) * s * (1.f - s));
+    const int r = VARLEN ? out_row(a, t) : t;
+    stf(dbl + i, ldf(dbt + (row0 + r) * a.H + h) * s * (1.f - s));
   }
   for (int bi = 0; bi < nbat; ++bi) {
     tc::cp_async_wait<kBwStages - 2>();
@@ -693,7 +743,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32) prologue_bwd_kernel(const ProA
     const int b = s / a.spb;
     const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
     if (role < 3) pro_bwd_conv<CPL, VARLEN, Tin, Tout>(a, role, b, t0, t1, h, lane, acc, ring);
-    else pro_bwd_gate<CPL, Tin, Tout>(a, b, t0, t1, h, lane, acc[0], dA, ring);
+    else pro_bwd_gate<CPL, VARLEN, Tin, Tout>(a, b, t0, t1, h, lane, acc[0], dA, ring);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -748,16 +798,42 @@ __global__ void prologue_reduce_kernel(const float* __restrict__ ws, int groups,
 
 // ------------------------------------------------------------ output gate ----
 
+// Rows of o (and do) for the packed rows r = t H + h of y: the same row, or with
+// out_rows that of token t in the chunk-aligned layout (sequence s from row
+// out_rows[s]).
+struct RowMap {
+  const int* cu;
+  const int* out_rows;
+  int n_seqs;
+  int H;
+};
+__device__ __forceinline__ long long o_row(const RowMap& m, long long r) {
+  if (!m.out_rows) return r;
+  const int t = static_cast<int>(r / m.H), h = static_cast<int>(r % m.H);
+  const int s = seq_of(m.cu, m.n_seqs, t);
+  return static_cast<long long>(t + __ldg(m.out_rows + s) - __ldg(m.cu + s)) * m.H + h;
+}
+
+// Zeroes the pad rows of sequence blockIdx.x (row_elems elements per token row).
+template <typename T>
+__global__ void zero_pad_rows_kernel(T* __restrict__ x, RowMap m, int row_elems) {
+  const int s = blockIdx.x;
+  const long long r0 = __ldg(m.out_rows + s) + (__ldg(m.cu + s + 1) - __ldg(m.cu + s));
+  const long long r1 = __ldg(m.out_rows + s + 1);
+  for (long long i = r0 * row_elems + threadIdx.x; i < r1 * row_elems; i += blockDim.x) stf(x + i, 0.f);
+}
+
 template <int CPL, typename To, typename Tg, typename Ty>
 __global__ void __launch_bounds__(256) gated_rms_fwd_kernel(const To* __restrict__ o, const Tg* __restrict__ gate,
-                                                            Ty* __restrict__ y, long long rows, float eps) {
+                                                            Ty* __restrict__ y, long long rows, float eps,
+                                                            const RowMap m) {
   constexpr int D = CPL * 32;
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += nw) {
     const size_t off = static_cast<size_t>(r) * D + lane * CPL;
     float ov[CPL], gv[CPL];
-    ldv<CPL>(o + off, ov);
+    ldv<CPL>(o + static_cast<size_t>(o_row(m, r)) * D + lane * CPL, ov);
     ldv<CPL>(gate + off, gv);
     float ss = 0.f;
 #pragma unroll
@@ -772,14 +848,16 @@ __global__ void __launch_bounds__(256) gated_rms_fwd_kernel(const To* __restrict
 template <int CPL, typename To, typename Tg, typename Ty>
 __global__ void __launch_bounds__(256) gated_rms_bwd_kernel(const To* __restrict__ o, const Tg* __restrict__ gate,
                                                             const Ty* __restrict__ dy, To* __restrict__ dout,
-                                                            Tg* __restrict__ dgate, long long rows, float eps) {
+                                                            Tg* __restrict__ dgate, long long rows, float eps,
+                                                            const RowMap m) {
   constexpr int D = CPL * 32;
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += nw) {
     const size_t off = static_cast<size_t>(r) * D + lane * CPL;
+    const size_t ooff = static_cast<size_t>(o_row(m, r)) * D + lane * CPL;
     float ov[CPL], gv[CPL], dv[CPL];
-    ldv<CPL>(o + off, ov);
+    ldv<CPL>(o + ooff, ov);
     ldv<CPL>(gate + off, gv);
     ldv<CPL>(dy + off, dv);
     float ss = 0.f;
@@ -797,7 +875,7 @@ __global__ void __launch_bounds__(256) gated_rms_bwd_kernel(const To* __restrict
     m = warp_sum(m) / D;
 #pragma unroll
     for (int c = 0; c < CPL; ++c) dn[c] = rr * (dn[c] - ov[c] * rr * m);
-    stv<CPL>(dout + off, dn);
+    stv<CPL>(dout + ooff, dn);
     stv<CPL>(dgate + off, dg);
   }
 }
@@ -995,28 +1073,31 @@ int launch_prologue(ProArgs& a, bool bwd, cudaStream_t st) {
 
 template <int CPL, typename To, typename Tg, typename Ty>
 int launch_grms(const void* o, const void* gate, const void* dy, void* y, void* dout, void* dgate,
-                long long rows, float eps, bool bwd, cudaStream_t st) {
+                long long rows, float eps, bool bwd, const RowMap& m, cudaStream_t st) {
   const long long want = (rows + 7) / 8;
   const int grid = static_cast<int>(want < 148LL * 16 ? want : 148LL * 16);
-  if (bwd)
+  if (bwd) {
     gated_rms_bwd_kernel<CPL, To, Tg, Ty><<<grid, 256, 0, st>>>(
         static_cast<const To*>(o), static_cast<const Tg*>(gate), static_cast<const Ty*>(dy),
-        static_cast<To*>(dout), static_cast<Tg*>(dgate), rows, eps);
-  else
+        static_cast<To*>(dout), static_cast<Tg*>(dgate), rows, eps, m);
+    if (m.out_rows && m.n_seqs > 0)  // do's pad rows: zero cotangents for the core
+      zero_pad_rows_kernel<To><<<m.n_seqs, 256, 0, st>>>(static_cast<To*>(dout), m, m.H * CPL * 32);
+  } else {
     gated_rms_fwd_kernel<CPL, To, Tg, Ty><<<grid, 256, 0, st>>>(
-        static_cast<const To*>(o), static_cast<const Tg*>(gate), static_cast<Ty*>(y), rows, eps);
+        static_cast<const To*>(o), static_cast<const Tg*>(gate), static_cast<Ty*>(y), rows, eps, m);
+  }
   return launch_status();
 }
 
 template <int CPL>
 int grms_types(const void* o, const void* gate, const void* dy, void* y, void* dout, void* dgate, long long rows,
-               float eps, int odt, int gdt, int ydt, bool bwd, cudaStream_t st) {
+               float eps, int odt, int gdt, int ydt, bool bwd, const RowMap& m, cudaStream_t st) {
   // o and y in either type; the gate logits in either type
 #define KDA_GRMS(TO, TG, TY)                                                                               \
   if (odt == (std::is_same<TO, float>::value ? KDA_F32 : KDA_BF16) &&                                      \
       gdt == (std::is_same<TG, float>::value ? KDA_F32 : KDA_BF16) &&                                      \
       ydt == (std::is_same<TY, float>::value ? KDA_F32 : KDA_BF16))                                        \
-    return launch_grms<CPL, TO, TG, TY>(o, gate, dy, y, dout, dgate, rows, eps, bwd, st);
+    return launch_grms<CPL, TO, TG, TY>(o, gate, dy, y, dout, dgate, rows, eps, bwd, m, st);
   KDA_GRMS(float, float, float)
   KDA_GRMS(float, float, bf16)
   KDA_GRMS(float, bf16, float)
@@ -1081,13 +1162,13 @@ int prologue_check(const void* qp, const void* kp, const void* vp, const void* z
 kda::ProArgs base_args(const void* qp, const void* kp, const void* vp, const void* z, const void* bl,
                        const float* cq, const float* ck, const float* cv, const float* b_gate,
                        const float* A, float g_min, int kind, const float* st_in, const int* cu,
-                       int n_seqs, int B, int T, int H, int dk, int dv, int K) {
+                       int n_seqs, const int* out_rows, int B, int T, int H, int dk, int dv, int K) {
   kda::ProArgs a{};
   a.x[0] = qp; a.x[1] = kp; a.x[2] = vp; a.x[3] = z;
   a.beta_logit = bl;
   a.w[0] = cq; a.w[1] = ck; a.w[2] = cv;
   a.b_gate = b_gate; a.A = A; a.g_min = g_min; a.gate_kind = kind;
-  a.st_in = st_in; a.cu = cu; a.n_seqs = n_seqs;
+  a.st_in = st_in; a.cu = cu; a.n_seqs = n_seqs; a.out_rows = out_rows;
   a.B = B; a.T = T; a.H = H; a.dk = dk; a.dv = dv; a.K = K;
   a.spb = (T + kda::kStrip - 1) / kda::kStrip;
   a.n_strips = B * a.spb;
@@ -1107,18 +1188,19 @@ extern "C" {
 int kda_prologue_fwd(const void* qp, const void* kp, const void* vp, const void* z, const void* beta_logit,
                      const float* conv_q, const float* conv_k, const float* conv_v, const float* b_gate,
                      const float* A, float g_min, int gate_kind, const float* conv_state_in,
-                     float* conv_state_out, const int* cu_seqlens, int n_seqs, void* q, void* k, void* v,
-                     void* g, void* beta, int B, int T, int H, int dk, int dv, int K, int in_dtype,
-                     int out_dtype, kda_stream_t stream) {
+                     float* conv_state_out, const int* cu_seqlens, int n_seqs, const int* out_rows, void* q,
+                     void* k, void* v, void* g, void* beta, int B, int T, int H, int dk, int dv, int K,
+                     int in_dtype, int out_dtype, kda_stream_t stream) {
   int rc = prologue_check(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, gate_kind, conv_state_in,
                           conv_state_out, cu_seqlens, n_seqs, B, T, H, dk, dv, K, in_dtype, out_dtype);
+  if (rc == KDA_OK && out_rows && !cu_seqlens) rc = KDA_ERR_SHAPE;
   if (rc != KDA_OK || B == 0 || T == 0 || H == 0) return rc;
   if (!q || !k || !v || !g || !beta) return KDA_ERR_NULL;
   const void* al[] = {q, k, v, g};
   for (const void* p : al)
     if (!kda::aligned16(p)) return KDA_ERR_ALIGN;
   kda::ProArgs a = base_args(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, b_gate, A, g_min, gate_kind,
-                             conv_state_in, cu_seqlens, n_seqs, B, T, H, dk, dv, K);
+                             conv_state_in, cu_seqlens, n_seqs, out_rows, B, T, H, dk, dv, K);
   a.st_out = conv_state_out;
   a.y[0] = q; a.y[1] = k; a.y[2] = v; a.y[3] = g;
   a.beta = beta;
@@ -1133,13 +1215,15 @@ size_t kda_prologue_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int
 int kda_prologue_bwd(const void* qp, const void* kp, const void* vp, const void* z, const void* beta_logit,
                      const float* conv_q, const float* conv_k, const float* conv_v, const float* b_gate,
                      const float* A, float g_min, int gate_kind, const float* conv_state_in,
-                     const int* cu_seqlens, int n_seqs, const void* dq, const void* dk_, const void* dv_,
+                     const int* cu_seqlens, int n_seqs, const int* out_rows, const void* dq, const void* dk_,
+                     const void* dv_,
                      const void* dg, const void* dbeta, void* dqp, void* dkp, void* dvp, void* dz,
                      void* dbeta_logit, float* dconv_q, float* dconv_k, float* dconv_v, float* db_gate,
                      float* dA, float* dconv_state_in, void* workspace, size_t workspace_bytes, int B, int T,
                      int H, int dk, int dv, int K, int in_dtype, int out_dtype, kda_stream_t stream) {
   int rc = prologue_check(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, gate_kind, conv_state_in,
                           dconv_state_in, cu_seqlens, n_seqs, B, T, H, dk, dv, K, in_dtype, out_dtype);
+  if (rc == KDA_OK && out_rows && !cu_seqlens) rc = KDA_ERR_SHAPE;
   if (rc != KDA_OK) return rc;
   if (!dconv_q || !dconv_k || !dconv_v || !db_gate || !dA) return KDA_ERR_NULL;
   const size_t nq = static_cast<size_t>(K) * H * dk, nv = static_cast<size_t>(K) * H * dv;
@@ -1160,7 +1244,7 @@ int kda_prologue_bwd(const void* qp, const void* kp, const void* vp, const void*
   const size_t need = kda_prologue_bwd_workspace_bytes(B, T, H, dk, dv, K);
   if (!workspace || workspace_bytes < need) return KDA_ERR_WORKSPACE;
   kda::ProArgs a = base_args(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, b_gate, A, g_min, gate_kind,
-                             conv_state_in, cu_seqlens, n_seqs, B, T, H, dk, dv, K);
+                             conv_state_in, cu_seqlens, n_seqs, out_rows, B, T, H, dk, dv, K);
   a.dy[0] = dq; a.dy[1] = dk_; a.dy[2] = dv_; a.dy[3] = dg;
   a.dbeta = dbeta;
   a.dx[0] = dqp; a.dx[1] = dkp; a.dx[2] = dvp; a.dx[3] = dz;
@@ -1179,34 +1263,40 @@ int kda_prologue_bwd(const void* qp, const void* kp, const void* vp, const void*
   return kda::launch_status();
 }
 
-int kda_gated_rmsnorm_fwd(const void* o, const void* gate, void* y, int N, int H, int dv, float eps, int o_dtype,
-                          int gate_dtype, int y_dtype, kda_stream_t stream) {
+int kda_gated_rmsnorm_fwd(const void* o, const void* gate, void* y, const int* cu_seqlens, const int* out_rows,
+                          int n_seqs, int N, int H, int dv, float eps, int o_dtype, int gate_dtype, int y_dtype,
+                          kda_stream_t stream) {
   if (N < 0 || H < 0 || !d_ok(dv)) return KDA_ERR_SHAPE;
   if (!valid_dt(o_dtype) || !valid_dt(gate_dtype) || !valid_dt(y_dtype)) return KDA_ERR_DTYPE;
+  if (out_rows && (!cu_seqlens || n_seqs < 1)) return KDA_ERR_SHAPE;
   if (N == 0 || H == 0) return KDA_OK;
   if (!o || !gate || !y) return KDA_ERR_NULL;
   if (!kda::aligned16(o) || !kda::aligned16(gate) || !kda::aligned16(y)) return KDA_ERR_ALIGN;
   const long long rows = static_cast<long long>(N) * H;
+  const kda::RowMap m{cu_seqlens, out_rows, n_seqs, H};
   return dv == 128 ? kda::grms_types<4>(o, gate, nullptr, y, nullptr, nullptr, rows, eps, o_dtype, gate_dtype,
-                                        y_dtype, false, stream)
+                                        y_dtype, false, m, stream)
                    : kda::grms_types<2>(o, gate, nullptr, y, nullptr, nullptr, rows, eps, o_dtype, gate_dtype,
-                                        y_dtype, false, stream);
+                                        y_dtype, false, m, stream);
 }
 
-int kda_gated_rmsnorm_bwd(const void* o, const void* gate, const void* dy, void* do_, void* dgate, int N, int H,
-                          int dv, float eps, int o_dtype, int gate_dtype, int y_dtype, kda_stream_t stream) {
+int kda_gated_rmsnorm_bwd(const void* o, const void* gate, const void* dy, void* do_, void* dgate,
+                          const int* cu_seqlens, const int* out_rows, int n_seqs, int N, int H, int dv, float eps,
+                          int o_dtype, int gate_dtype, int y_dtype, kda_stream_t stream) {
   if (N < 0 || H < 0 || !d_ok(dv)) return KDA_ERR_SHAPE;
   if (!valid_dt(o_dtype) || !valid_dt(gate_dtype) || !valid_dt(y_dtype)) return KDA_ERR_DTYPE;
+  if (out_rows && (!cu_seqlens || n_seqs < 1)) return KDA_ERR_SHAPE;
   if (N == 0 || H == 0) return KDA_OK;
   if (!o || !gate || !dy || !do_ || !dgate) return KDA_ERR_NULL;
   const void* al[] = {o, gate, dy, do_, dgate};
   for (const void* p : al)
     if (!kda::aligned16(p)) return KDA_ERR_ALIGN;
   const long long rows = static_cast<long long>(N) * H;
+  const kda::RowMap m{cu_seqlens, out_rows, n_seqs, H};
   return dv == 128 ? kda::grms_types<4>(o, gate, dy, nullptr, do_, dgate, rows, eps, o_dtype, gate_dtype,
-                                        y_dtype, true, stream)
+                                        y_dtype, true, m, stream)
                    : kda::grms_types<2>(o, gate, dy, nullptr, do_, dgate, rows, eps, o_dtype, gate_dtype,
-                                        y_dtype, true, stream);
+                                        y_dtype, true, m, stream);
 }
 
 int kda_decode_fused(float* S, float* conv_buf, const void* qp, const void* kp, const void* vp, const void* z,

@@ -28,10 +28,14 @@ __global__ void __launch_bounds__(kFwdThreads)
 fwd_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin* __restrict__ v,
                 const Tin* __restrict__ g, const Tin* __restrict__ beta,
                 const float* __restrict__ s0, To* __restrict__ o, float* __restrict__ s_out,
-                Tc* __restrict__ s_ckpt, int T, int H, int dk, int dv, int C) {
+                Tc* __restrict__ s_ckpt, int T, int H, int dk, int dv, int C,
+                const int* __restrict__ cs) {
   const int j0 = blockIdx.x * kFwdSlice;
   const int nj = min(kFwdSlice, dv - j0);
-  const int h = blockIdx.y, b = blockIdx.z;
+  // (seq, h): batch row seq, or with packed sequences (cs: chunk offsets, B = 1)
+  // the chunk range [cs[seq], cs[seq + 1]) of row 0
+  const int h = blockIdx.y, seq = blockIdx.z;
+  const int b = cs ? 0 : seq;
   const int tid = threadIdx.x, nt = blockDim.x;
   const int ldk = dk + 1, ldc = C + 1, ldj = kFwdSlice;
   extern __shared__ float sm[];
@@ -46,13 +50,15 @@ fwd_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin*
   float* Bs = Ss + dk * ldj;       // C
   float* gC = Bs + C;              // dk : Gamma_C
 
-  const size_t sbase = (static_cast<size_t>(b) * H + h) * dk * dv;
+  const size_t sbase = (static_cast<size_t>(seq) * H + h) * dk * dv;
   for (int idx = tid; idx < dk * nj; idx += nt) {
     const int d = idx / nj, j = idx % nj;
     Ss[d * ldj + j] = s0 ? s0[sbase + static_cast<size_t>(d) * dv + j0 + j] : 0.f;
   }
   const int n_chunks = (T + C - 1) / C;
-  for (int c = 0; c < n_chunks; ++c) {
+  const int c_beg = cs ? min(max(cs[seq], 0), n_chunks) : 0;  // clamped to the tensors
+  const int c_end = cs ? min(max(cs[seq + 1], c_beg), n_chunks) : n_chunks;
+  for (int c = c_beg; c < c_end; ++c) {
     const int t0 = c * C;
     __syncthreads();
     if (s_ckpt) {
@@ -196,16 +202,20 @@ bwd_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin*
                 const float* __restrict__ dsT, Tin* __restrict__ dq, Tin* __restrict__ dkout,
                 Tin* __restrict__ dvout, Tin* __restrict__ dg, Tin* __restrict__ dbeta,
                 float* __restrict__ ds0, float* __restrict__ work, int T, int H, int dk, int dv,
-                int C, int states_cm) {
-  const int h = blockIdx.x, b = blockIdx.y;
+                int C, int states_cm, const int* __restrict__ cs) {
+  const int h = blockIdx.x, seq = blockIdx.y;
+  const int b = cs ? 0 : seq;
   const int tid = threadIdx.x, nt = blockDim.x;
-  const size_t unit = static_cast<size_t>(b) * H + h;
-  BwdScratch s = carve(work + unit * bwd_scratch_floats(C, dk, dv), C, dk, dv);
+  const size_t unit = static_cast<size_t>(b) * H + h;     // checkpoint row
+  const size_t sunit = static_cast<size_t>(seq) * H + h;  // state and scratch row
+  BwdScratch s = carve(work + sunit * bwd_scratch_floats(C, dk, dv), C, dk, dv);
   const int n_chunks = (T + C - 1) / C;
-  const size_t sbase = unit * dk * dv;
+  const int c_beg = cs ? min(max(cs[seq], 0), n_chunks) : 0;  // clamped to the tensors
+  const int c_end = cs ? min(max(cs[seq + 1], c_beg), n_chunks) : n_chunks;
+  const size_t sbase = sunit * dk * dv;
   for (int idx = tid; idx < dk * dv; idx += nt) s.dS[idx] = dsT ? dsT[sbase + idx] : 0.f;
 
-  for (int c = n_chunks - 1; c >= 0; --c) {
+  for (int c = c_end - 1; c >= c_beg; --c) {
     const int t0 = c * C;
     __syncthreads();
     // (1) loads
@@ -451,18 +461,18 @@ bwd_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin*
 template <typename Tin, typename To, typename Tc>
 int fwd_launch_t(const void* q, const void* k, const void* v, const void* g, const void* beta,
                  const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
-                 int dk, int dv, int C, cudaStream_t st) {
+                 int dk, int dv, int C, const int* cs, int n_seqs, cudaStream_t st) {
   static bool done[64] = {false};
   const int bytes = static_cast<int>(sizeof(float)) *
                     (4 * C * (dk + 1) + C * kFwdSlice + 2 * C * (C + 1) + dk * kFwdSlice + C + dk);
   auto kern = fwd_simt_kernel<Tin, To, Tc>;
   int rc = ensure_smem(kern, 227 * 1024, done);
   if (rc != KDA_OK) return rc;
-  dim3 grid((dv + kFwdSlice - 1) / kFwdSlice, H, B);
+  dim3 grid((dv + kFwdSlice - 1) / kFwdSlice, H, cs ? n_seqs : B);
   kern<<<grid, kFwdThreads, bytes, st>>>(
       static_cast<const Tin*>(q), static_cast<const Tin*>(k), static_cast<const Tin*>(v),
       static_cast<const Tin*>(g), static_cast<const Tin*>(beta), s0, static_cast<To*>(o), s_out,
-      static_cast<Tc*>(s_ckpt), T, H, dk, dv, C);
+      static_cast<Tc*>(s_ckpt), T, H, dk, dv, C, cs);
   return launch_status();
 }
 
@@ -470,14 +480,14 @@ template <typename Tin, typename Td, typename Tc>
 int bwd_launch_t(const void* q, const void* k, const void* v, const void* g, const void* beta,
                  const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                  void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
-                 int dk, int dv, int C, int states_cm, cudaStream_t st) {
-  dim3 grid(H, B);
+                 int dk, int dv, int C, int states_cm, const int* cs, int n_seqs, cudaStream_t st) {
+  dim3 grid(H, cs ? n_seqs : B);
   bwd_simt_kernel<Tin, Td, Tc><<<grid, kBwdThreads, 0, st>>>(
       static_cast<const Tin*>(q), static_cast<const Tin*>(k), static_cast<const Tin*>(v),
       static_cast<const Tin*>(g), static_cast<const Tin*>(beta), static_cast<const Tc*>(s_ckpt),
       static_cast<const Td*>(dout), dsT, static_cast<Tin*>(dq), static_cast<Tin*>(dk_),
       static_cast<Tin*>(dv_), static_cast<Tin*>(dg), static_cast<Tin*>(dbeta), ds0,
-      static_cast<float*>(work), T, H, dk, dv, C, states_cm);
+      static_cast<float*>(work), T, H, dk, dv, C, states_cm, cs);
   return launch_status();
 }
 
@@ -489,10 +499,11 @@ size_t simt_bwd_workspace_bytes(int B, int H, int dk, int dv, int C) {
 
 int simt_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                     const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
-                    int dk, int dv, int C, int in_dt, int o_dt, int ck_dt, cudaStream_t st) {
+                    int dk, int dv, int C, int in_dt, int o_dt, int ck_dt, const int* cs, int n_seqs,
+                    cudaStream_t st) {
 #define KDA_FWD_CASE(I, O, K, TI, TO, TK)                                                     \
   if (in_dt == I && o_dt == O && ck_dt == K)                                                 \
-    return fwd_launch_t<TI, TO, TK>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, dk, dv, C, st);
+    return fwd_launch_t<TI, TO, TK>(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, dk, dv, C, cs, n_seqs, st);
   KDA_FWD_CASE(KDA_F32, KDA_F32, KDA_F32, float, float, float)
   KDA_FWD_CASE(KDA_F32, KDA_F32, KDA_BF16, float, float, bf16)
   KDA_FWD_CASE(KDA_F32, KDA_BF16, KDA_F32, float, bf16, float)
@@ -509,11 +520,11 @@ int simt_bwd_launch(const void* q, const void* k, const void* v, const void* g, 
                     const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                     void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T,
                     int H, int dk, int dv, int C, int in_dt, int do_dt, int ck_dt,
-                    int states_cm, cudaStream_t st) {
+                    int states_cm, const int* cs, int n_seqs, cudaStream_t st) {
 #define KDA_BWD_CASE(I, D, K, TI, TD, TK)                                                     \
   if (in_dt == I && do_dt == D && ck_dt == K)                                                \
     return bwd_launch_t<TI, TD, TK>(q, k, v, g, beta, s_ckpt, dout, dsT, dq, dk_, dv_, dg,   \
-                                    dbeta, ds0, work, B, T, H, dk, dv, C, states_cm, st);
+                                    dbeta, ds0, work, B, T, H, dk, dv, C, states_cm, cs, n_seqs, st);
   KDA_BWD_CASE(KDA_F32, KDA_F32, KDA_F32, float, float, float)
   KDA_BWD_CASE(KDA_F32, KDA_F32, KDA_BF16, float, float, bf16)
   KDA_BWD_CASE(KDA_F32, KDA_BF16, KDA_F32, float, bf16, float)

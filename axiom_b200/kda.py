@@ -180,6 +180,101 @@ def kda_bwd(q, k, v, g, beta, ckpt, do, dST=None, *, chunk=CHUNK, need_ds0=True)
     return dq, dk_, dv_, dg, dbeta, ds0
 
 
+# ---------------------------------------------------------------------------
+# packed (variable-length) sequences
+# ---------------------------------------------------------------------------
+
+
+def packing(cu_seqlens, chunk=CHUNK):
+    """Chunk-aligned packing of the sequences ``cu_seqlens`` delimits (host
+    integers, or a tensor read back once): ``(chunk_offsets, out_rows, T_pad)``
+    with ``chunk_offsets[s]`` the first chunk of sequence ``s`` (last entry: the
+    total), ``out_rows = chunk * chunk_offsets`` (the rows
+    :func:`axiom_b200.mixer.prologue_fwd` writes each sequence from) and
+    ``T_pad`` the packed length.  Each sequence is padded to its next chunk
+    boundary (at most ``chunk - 1`` rows)."""
+    cu = [int(x) for x in (cu_seqlens.tolist() if isinstance(cu_seqlens, torch.Tensor) else cu_seqlens)]
+    if not cu or cu[0] != 0 or any(b < a for a, b in zip(cu[:-1], cu[1:])):
+        raise ValueError("cu_seqlens must start at 0 and be non-decreasing")
+    offs = [0]
+    for a, b in zip(cu[:-1], cu[1:]):
+        offs.append(offs[-1] + -(-(b - a) // chunk))
+    return offs, [chunk * o for o in offs], chunk * offs[-1]
+
+
+def _offsets_tensor(chunk_offsets, device):
+    if isinstance(chunk_offsets, torch.Tensor):
+        return chunk_offsets.to(device=device, dtype=torch.int32).contiguous()
+    return torch.tensor(list(chunk_offsets), dtype=torch.int32, device=device)
+
+
+def kda_fwd_varlen(q, k, v, g, beta, chunk_offsets, S0=None, *, chunk=CHUNK, o_dtype=None,
+                   need_ckpt=False, ckpt_dtype=None):
+    """Chunked forward over packed sequences; returns ``(o, S_T, ckpt)``.
+
+    ``q, k, g``: ``[1, T, H, dk]``, ``v``: ``[1, T, H, dv]``, ``beta``: ``[1, T, H]``
+    in the chunk-aligned packed layout (see :func:`packing`); ``chunk_offsets``:
+    ``[n + 1]`` (device int32 tensor or host integers); ``S0`` and ``S_T``:
+    ``[n, H, dk, dv]`` fp32, one state per sequence.
+    """
+    _require_device("kda_fwd_varlen")
+    B, T, H, dk = q.shape
+    dv = v.shape[-1]
+    dt = q.dtype
+    if B != 1:
+        raise ValueError("kda_fwd_varlen: packed sequences share one batch row (B = 1)")
+    for x, n, s in ((q, "q", (1, T, H, dk)), (k, "k", (1, T, H, dk)), (v, "v", (1, T, H, dv)),
+                    (g, "g", (1, T, H, dk)), (beta, "beta", (1, T, H))):
+        _check_tensor(x, n, s, dt)
+    cs = _offsets_tensor(chunk_offsets, q.device)
+    n_seqs = cs.numel() - 1
+    if S0 is not None:
+        _check_tensor(S0, "S0", (n_seqs, H, dk, dv), torch.float32)
+    o_dtype = dt if o_dtype is None else o_dtype
+    ckpt_dtype = (torch.float32 if dt == torch.float32 else torch.bfloat16) if ckpt_dtype is None else ckpt_dtype
+    o = torch.empty((1, T, H, dv), dtype=o_dtype, device=q.device)
+    s_out = torch.empty((n_seqs, H, dk, dv), dtype=torch.float32, device=q.device)
+    ckpt = None
+    if need_ckpt:
+        nbytes = lib().kda_ckpt_bytes(1, T, H, dk, dv, chunk, _dt(q, "q"), _DT[ckpt_dtype])
+        esz = 4 if ckpt_dtype == torch.float32 else 2
+        ckpt = torch.empty(max(-(-nbytes // esz), 1), dtype=ckpt_dtype, device=q.device)
+    rc = lib().kda_fwd_varlen(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(S0), _ptr(o),
+                              _ptr(s_out), _ptr(ckpt), _ptr(cs), n_seqs, T, H, dk, dv, int(chunk),
+                              _dt(q, "q"), _DT[o_dtype], _DT[ckpt_dtype], _stream())
+    check("kda_fwd_varlen", rc)
+    return o, s_out, ckpt
+
+
+def kda_bwd_varlen(q, k, v, g, beta, ckpt, do, chunk_offsets, dST=None, *, chunk=CHUNK, need_ds0=True):
+    """Fused backward over packed sequences; returns ``(dq, dk, dv, dg, dbeta, dS0)``
+    (``dS0``: ``[n, H, dk, dv]``).  ``do``'s pad rows must be zero."""
+    _require_device("kda_bwd_varlen")
+    B, T, H, dk = q.shape
+    dv = v.shape[-1]
+    dt = q.dtype
+    for x, n, s in ((q, "q", (1, T, H, dk)), (k, "k", (1, T, H, dk)), (v, "v", (1, T, H, dv)),
+                    (g, "g", (1, T, H, dk)), (beta, "beta", (1, T, H))):
+        _check_tensor(x, n, s, dt)
+    _check_tensor(do, "do", (1, T, H, dv))
+    cs = _offsets_tensor(chunk_offsets, q.device)
+    n_seqs = cs.numel() - 1
+    if dST is not None:
+        _check_tensor(dST, "dST", (n_seqs, H, dk, dv), torch.float32)
+    if ckpt is None or ckpt.dtype not in _DT or not ckpt.is_contiguous():
+        raise ValueError("kda_bwd_varlen: ckpt must be the forward's checkpoint")
+    dq, dk_, dv_, dg, dbeta = (torch.empty_like(x) for x in (q, k, v, g, beta))
+    ds0 = torch.empty((n_seqs, H, dk, dv), dtype=torch.float32, device=q.device) if need_ds0 else None
+    wbytes = lib().kda_bwd_varlen_workspace_bytes(n_seqs, T, H, dk, dv, int(chunk), _dt(q, "q"))
+    work = torch.empty(max(wbytes, 1), dtype=torch.uint8, device=q.device)
+    rc = lib().kda_bwd_varlen(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(ckpt), _ptr(do),
+                              _ptr(dST), _ptr(dq), _ptr(dk_), _ptr(dv_), _ptr(dg), _ptr(dbeta),
+                              _ptr(ds0), _ptr(work), wbytes, _ptr(cs), n_seqs, T, H, dk, dv, int(chunk),
+                              _dt(q, "q"), _dt(do, "do"), _dt(ckpt, "ckpt"), _stream())
+    check("kda_bwd_varlen", rc)
+    return dq, dk_, dv_, dg, dbeta, ds0
+
+
 def decode_step(S, q, k, v, g, beta, *, o_dtype=None):
     """One recurrent token for ``N`` states; updates ``S`` in place, returns ``o``.
 
@@ -234,6 +329,36 @@ class _ChunkKDA(torch.autograd.Function):
 def chunk_kda(q, k, v, g, beta, S0=None, chunk=CHUNK):
     """Differentiable chunked KDA core: ``(o, S_T)``; gradients via the fused backward."""
     return _ChunkKDA.apply(q, k, v, g, beta, S0, int(chunk))
+
+
+class _ChunkKDAVarlen(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, cs, S0, chunk):
+        o, s_t, ckpt = kda_fwd_varlen(q, k, v, g, beta, cs, S0, chunk=chunk, need_ckpt=True)
+        ctx.save_for_backward(q, k, v, g, beta, ckpt, cs)
+        ctx.chunk = chunk
+        ctx.has_s0 = S0 is not None
+        return o, s_t
+
+    @staticmethod
+    def backward(ctx, do, dst):
+        q, k, v, g, beta, ckpt, cs = ctx.saved_tensors
+        if do is None:
+            do = torch.zeros(q.shape[:-1] + (v.shape[-1],), dtype=q.dtype, device=q.device)
+        do = do.to(q.dtype).contiguous()
+        dst = None if dst is None else dst.to(torch.float32).contiguous()
+        dq, dk, dv, dg, dbeta, ds0 = kda_bwd_varlen(q, k, v, g, beta, ckpt, do, cs, dst, chunk=ctx.chunk,
+                                                    need_ds0=ctx.has_s0)
+        return dq, dk, dv, dg, dbeta, None, (ds0 if ctx.has_s0 else None), None
+
+
+def chunk_kda_varlen(q, k, v, g, beta, chunk_offsets, S0=None, chunk=CHUNK):
+    """Differentiable chunked KDA core over packed sequences (``[1, T, H, *]`` in
+    the chunk-aligned layout of :func:`packing`): ``(o, S_T)``, one state per
+    sequence.  The pad rows of ``o``'s cotangent must be zero (the output gate's
+    backward writes them so)."""
+    cs = _offsets_tensor(chunk_offsets, q.device)
+    return _ChunkKDAVarlen.apply(q, k, v, g, beta, cs, S0, int(chunk))
 
 
 # ---------------------------------------------------------------------------

@@ -50,22 +50,37 @@ def _cu(cu_seqlens, B, device):
     return cu, cu.numel() - 1
 
 
+def _rows(out_rows, cu, n_seqs, T, device):
+    """``(device int32 rows or None, output length)``."""
+    if out_rows is None:
+        return None, T
+    if cu is None:
+        raise ValueError("out_rows places packed sequences: cu_seqlens is required")
+    host = [int(x) for x in (out_rows.tolist() if isinstance(out_rows, torch.Tensor) else out_rows)]
+    if len(host) != n_seqs + 1:
+        raise ValueError("out_rows needs one entry per sequence plus the total")
+    return torch.tensor(host, dtype=torch.int32, device=device), host[-1]
+
+
 def _state_width(H, dk, dv):
     return H * (2 * dk + dv)
 
 
 def prologue_fwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, *, H, b_gate=None, g_min=G_MIN,
                  gate_kind="sigmoid_min", conv_state=None, return_state=False, cu_seqlens=None,
-                 out_dtype=None):
+                 out_rows=None, out_dtype=None):
     """The KDA core's inputs from the layer's projections.
 
     ``qp, kp, z``: ``[B, T, H*dk]``; ``vp``: ``[B, T, H*dv]``; ``beta_logit``:
     ``[B, T, H]`` (one dtype, bf16 or fp32); ``conv_q, conv_k``: ``[K, H*dk]``,
     ``conv_v``: ``[K, H*dv]``, ``b_gate``: ``[H*dk]``, ``A``: ``[H]`` (fp32).
     ``conv_state``: ``[B, K-1, H*(2dk+dv)]`` fp32 (the q, k, v buffers of
-    ``KDAState``) or None.  Returns ``q, k, v, g, beta`` in the core's layout
-    (``[B, T, H, d]``, ``[B, T, H]``), plus the next conv state when
-    ``return_state``.
+    ``KDAState``) or None.  ``cu_seqlens`` (``[n + 1]``) packs sequences along T
+    (B = 1; each restarts the convolution); ``out_rows`` (``[n + 1]``, e.g.
+    :func:`axiom_b200.kda.packing`'s) then places sequence ``s`` from output row
+    ``out_rows[s]`` with zero rows up to the next.  Returns ``q, k, v, g, beta``
+    in the core's layout (``[B, T', H, d]``, ``[B, T', H]``, ``T' = T`` or
+    ``out_rows[-1]``), plus the next conv state when ``return_state``.
     """
     _require_device("prologue_fwd")
     B, T, HK = qp.shape
@@ -83,19 +98,20 @@ def prologue_fwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, *, H, b_g
         _check_tensor(conv_state, "conv_state", (B, K - 1, _state_width(H, dk, dv)), torch.float32)
     out_dtype = dt if out_dtype is None else out_dtype
     dev = qp.device
-    q = torch.empty((B, T, H, dk), dtype=out_dtype, device=dev)
+    cu, n_seqs = _cu(cu_seqlens, B, dev)
+    rows, To = _rows(out_rows, cu, n_seqs, T, dev)
+    q = torch.empty((B, To, H, dk), dtype=out_dtype, device=dev)
     k = torch.empty_like(q)
     g = torch.empty_like(q)
-    v = torch.empty((B, T, H, dv), dtype=out_dtype, device=dev)
-    beta = torch.empty((B, T, H), dtype=out_dtype, device=dev)
+    v = torch.empty((B, To, H, dv), dtype=out_dtype, device=dev)
+    beta = torch.empty((B, To, H), dtype=out_dtype, device=dev)
     st_out = None
     if return_state and K > 1:
         st_out = torch.empty((B, K - 1, _state_width(H, dk, dv)), dtype=torch.float32, device=dev)
-    cu, n_seqs = _cu(cu_seqlens, B, dev)
     rc = lib().kda_prologue_fwd(
         _ptr(qp), _ptr(kp), _ptr(vp), _ptr(z), _ptr(beta_logit), _ptr(conv_q), _ptr(conv_k), _ptr(conv_v),
         _ptr(b_gate), _ptr(A), float(g_min), _gate_kind(gate_kind), _ptr(conv_state), _ptr(st_out), _ptr(cu),
-        n_seqs, _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), B, T, H, dk, dv, K, _dt(qp, "qp"),
+        n_seqs, _ptr(rows), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), B, T, H, dk, dv, K, _dt(qp, "qp"),
         _dt(q, "out"), _stream())
     check("kda_prologue_fwd", rc)
     if return_state:
@@ -104,7 +120,8 @@ def prologue_fwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, *, H, b_g
 
 
 def prologue_bwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, dq, dk, dv, dg, dbeta, *, H,
-                 b_gate=None, g_min=G_MIN, gate_kind="sigmoid_min", conv_state=None, cu_seqlens=None):
+                 b_gate=None, g_min=G_MIN, gate_kind="sigmoid_min", conv_state=None, cu_seqlens=None,
+                 out_rows=None):
     """Cotangents of :func:`prologue_fwd`'s inputs; returns a dict with
     ``dqp, dkp, dvp, dz, dbeta_logit`` (input dtype), ``dconv_q, dconv_k,
     dconv_v, db_gate, dA`` (fp32) and ``dconv_state`` (fp32, or None)."""
@@ -112,10 +129,12 @@ def prologue_bwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, dq, dk, d
     B, T, HK = qp.shape
     dk_, dv_, K = HK // H, vp.shape[-1] // H, conv_q.shape[0]
     odt = dq.dtype
-    for x, n, s in ((dq, "dq", (B, T, H, dk_)), (dk, "dk", (B, T, H, dk_)), (dv, "dv", (B, T, H, dv_)),
-                    (dg, "dg", (B, T, H, dk_)), (dbeta, "dbeta", (B, T, H))):
-        _check_tensor(x, n, s, odt)
     dev = qp.device
+    cu, n_seqs = _cu(cu_seqlens, B, dev)
+    rows, To = _rows(out_rows, cu, n_seqs, T, dev)
+    for x, n, s in ((dq, "dq", (B, To, H, dk_)), (dk, "dk", (B, To, H, dk_)), (dv, "dv", (B, To, H, dv_)),
+                    (dg, "dg", (B, To, H, dk_)), (dbeta, "dbeta", (B, To, H))):
+        _check_tensor(x, n, s, odt)
     out = {
         "dqp": torch.empty_like(qp), "dkp": torch.empty_like(kp), "dvp": torch.empty_like(vp),
         "dz": torch.empty_like(z), "dbeta_logit": torch.empty_like(beta_logit),
@@ -127,10 +146,9 @@ def prologue_bwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, dq, dk, d
         out["dconv_state"] = torch.empty_like(conv_state)
     ws_bytes = lib().kda_prologue_bwd_workspace_bytes(B, T, H, dk_, dv_, K)
     ws = torch.empty((max(ws_bytes, 16),), dtype=torch.uint8, device=dev)
-    cu, n_seqs = _cu(cu_seqlens, B, dev)
     rc = lib().kda_prologue_bwd(
         _ptr(qp), _ptr(kp), _ptr(vp), _ptr(z), _ptr(beta_logit), _ptr(conv_q), _ptr(conv_k), _ptr(conv_v),
-        _ptr(b_gate), _ptr(A), float(g_min), _gate_kind(gate_kind), _ptr(conv_state), _ptr(cu), n_seqs,
+        _ptr(b_gate), _ptr(A), float(g_min), _gate_kind(gate_kind), _ptr(conv_state), _ptr(cu), n_seqs, _ptr(rows),
         _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dg), _ptr(dbeta), _ptr(out["dqp"]), _ptr(out["dkp"]),
         _ptr(out["dvp"]), _ptr(out["dz"]), _ptr(out["dbeta_logit"]), _ptr(out["dconv_q"]),
         _ptr(out["dconv_k"]), _ptr(out["dconv_v"]), _ptr(out["db_gate"]), _ptr(out["dA"]),
@@ -143,84 +161,106 @@ def prologue_bwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, dq, dk, d
 class _Prologue(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, b_gate, H, g_min, gate_kind,
-                cu_seqlens):
+                cu_seqlens, out_rows):
         q, k, v, g, beta = prologue_fwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, H=H,
-                                        b_gate=b_gate, g_min=g_min, gate_kind=gate_kind, cu_seqlens=cu_seqlens)
+                                        b_gate=b_gate, g_min=g_min, gate_kind=gate_kind, cu_seqlens=cu_seqlens,
+                                        out_rows=out_rows)
         ctx.save_for_backward(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, b_gate, cu_seqlens)
-        ctx.cfg = (H, g_min, gate_kind)
+        ctx.cfg = (H, g_min, gate_kind, out_rows, q.shape[1])
         return q, k, v, g, beta
 
     @staticmethod
     def backward(ctx, dq, dk, dv, dg, dbeta):
         qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, b_gate, cu = ctx.saved_tensors
-        H, g_min, gate_kind = ctx.cfg
+        H, g_min, gate_kind, out_rows, To = ctx.cfg
         grads = [dq, dk, dv, dg, dbeta]
         ref = (dq if dq is not None else dk)
         odt = qp.dtype if ref is None else ref.dtype
-        shapes = ((qp.shape[0], qp.shape[1], H, qp.shape[2] // H),) * 2 + (
-            (vp.shape[0], vp.shape[1], H, vp.shape[2] // H), (z.shape[0], z.shape[1], H, z.shape[2] // H),
-            tuple(beta_logit.shape))
+        B = qp.shape[0]
+        shapes = ((B, To, H, qp.shape[2] // H),) * 2 + (
+            (B, To, H, vp.shape[2] // H), (B, To, H, z.shape[2] // H), (B, To, H))
         grads = [torch.zeros(s, dtype=odt, device=qp.device) if x is None else x.to(odt).contiguous()
                  for x, s in zip(grads, shapes)]
         r = prologue_bwd(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, *grads, H=H, b_gate=b_gate,
-                         g_min=g_min, gate_kind=gate_kind, cu_seqlens=cu)
+                         g_min=g_min, gate_kind=gate_kind, cu_seqlens=cu, out_rows=out_rows)
         return (r["dqp"], r["dkp"], r["dvp"], r["dz"], r["dbeta_logit"], r["dconv_q"], r["dconv_k"],
-                r["dconv_v"], r["dA"], None if b_gate is None else r["db_gate"], None, None, None, None)
+                r["dconv_v"], r["dA"], None if b_gate is None else r["db_gate"], None, None, None, None, None)
 
 
 def kda_prologue(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, *, H, b_gate=None, g_min=G_MIN,
-                 gate_kind="sigmoid_min", cu_seqlens=None):
+                 gate_kind="sigmoid_min", cu_seqlens=None, out_rows=None):
     """Differentiable :func:`prologue_fwd` (no conv state): ``q, k, v, g, beta``."""
+    if cu_seqlens is not None:
+        cu_seqlens = cu_seqlens.to(device=qp.device, dtype=torch.int32)
     return _Prologue.apply(qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, b_gate, H, g_min, gate_kind,
-                           cu_seqlens)
+                           cu_seqlens, out_rows)
 
 
-def gated_rmsnorm_fwd(o, gate, *, eps=RMS_EPS, out_dtype=None):
-    """``sigmoid(gate) * o / sqrt(mean(o^2) + eps)`` per head: ``o [..., H, dv]``,
-    ``gate`` logits ``[..., H*dv]``; returns ``[..., H*dv]``."""
+def _map(cu_seqlens, out_rows, device):
+    if out_rows is None:
+        return None, None, 0
+    if cu_seqlens is None:
+        raise ValueError("out_rows places packed sequences: cu_seqlens is required")
+    cu = cu_seqlens.to(device=device, dtype=torch.int32).contiguous()
+    rows, _ = _rows(out_rows, cu, cu.numel() - 1, 0, device)
+    return cu, rows, cu.numel() - 1
+
+
+def gated_rmsnorm_fwd(o, gate, *, eps=RMS_EPS, out_dtype=None, cu_seqlens=None, out_rows=None):
+    """``sigmoid(gate) * o / sqrt(mean(o^2) + eps)`` per head: ``gate`` logits
+    ``[..., N, H*dv]``, ``o [..., N, H, dv]`` -- or, with ``cu_seqlens`` and
+    ``out_rows``, ``o`` in the chunk-aligned packed layout (``[1, T', H, dv]``)
+    and ``gate`` packed (``[1, N, H*dv]``); returns the gate's shape."""
     _require_device("gated_rmsnorm")
     H, dv = o.shape[-2], o.shape[-1]
-    N = o.numel() // (H * dv)
+    N = gate.numel() // (H * dv)
     _check_tensor(o, "o", o.shape)
-    _check_tensor(gate, "gate", tuple(o.shape[:-2]) + (H * dv,))
-    y = torch.empty(tuple(o.shape[:-2]) + (H * dv,), dtype=out_dtype or gate.dtype, device=o.device)
-    rc = lib().kda_gated_rmsnorm_fwd(_ptr(o), _ptr(gate), _ptr(y), N, H, dv, float(eps), _dt(o, "o"),
-                                     _dt(gate, "gate"), _dt(y, "y"), _stream())
+    if out_rows is None:
+        _check_tensor(gate, "gate", tuple(o.shape[:-2]) + (H * dv,))
+    cu, rows, n = _map(cu_seqlens, out_rows, o.device)
+    y = torch.empty(gate.shape, dtype=out_dtype or gate.dtype, device=o.device)
+    rc = lib().kda_gated_rmsnorm_fwd(_ptr(o), _ptr(gate), _ptr(y), _ptr(cu), _ptr(rows), n, N, H, dv, float(eps),
+                                     _dt(o, "o"), _dt(gate, "gate"), _dt(y, "y"), _stream())
     check("kda_gated_rmsnorm_fwd", rc)
     return y
 
 
-def gated_rmsnorm_bwd(o, gate, dy, *, eps=RMS_EPS):
-    """``(do, dgate)`` of :func:`gated_rmsnorm_fwd` (dtypes of ``o`` and ``gate``)."""
+def gated_rmsnorm_bwd(o, gate, dy, *, eps=RMS_EPS, cu_seqlens=None, out_rows=None):
+    """``(do, dgate)`` of :func:`gated_rmsnorm_fwd` (dtypes of ``o`` and ``gate``;
+    ``do`` in ``o``'s rows, zero on the pad rows of a packed layout)."""
     _require_device("gated_rmsnorm_bwd")
     H, dv = o.shape[-2], o.shape[-1]
-    N = o.numel() // (H * dv)
-    _check_tensor(dy, "dy", tuple(o.shape[:-2]) + (H * dv,))
+    N = gate.numel() // (H * dv)
+    _check_tensor(dy, "dy", tuple(gate.shape))
+    cu, rows, n = _map(cu_seqlens, out_rows, o.device)
     do = torch.empty_like(o)
     dgate = torch.empty_like(gate)
-    rc = lib().kda_gated_rmsnorm_bwd(_ptr(o), _ptr(gate), _ptr(dy), _ptr(do), _ptr(dgate), N, H, dv, float(eps),
-                                     _dt(o, "o"), _dt(gate, "gate"), _dt(dy, "dy"), _stream())
+    rc = lib().kda_gated_rmsnorm_bwd(_ptr(o), _ptr(gate), _ptr(dy), _ptr(do), _ptr(dgate), _ptr(cu), _ptr(rows), n,
+                                     N, H, dv, float(eps), _dt(o, "o"), _dt(gate, "gate"), _dt(dy, "dy"), _stream())
     check("kda_gated_rmsnorm_bwd", rc)
     return do, dgate
 
 
 class _GatedRMSNorm(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, o, gate, eps):
-        ctx.save_for_backward(o, gate)
-        ctx.eps = eps
-        return gated_rmsnorm_fwd(o, gate, eps=eps)
+    def forward(ctx, o, gate, eps, cu_seqlens, out_rows):
+        ctx.save_for_backward(o, gate, cu_seqlens)
+        ctx.eps, ctx.out_rows = eps, out_rows
+        return gated_rmsnorm_fwd(o, gate, eps=eps, cu_seqlens=cu_seqlens, out_rows=out_rows)
 
     @staticmethod
     def backward(ctx, dy):
-        o, gate = ctx.saved_tensors
-        do, dgate = gated_rmsnorm_bwd(o, gate, dy.to(gate.dtype).contiguous(), eps=ctx.eps)
-        return do, dgate, None
+        o, gate, cu = ctx.saved_tensors
+        do, dgate = gated_rmsnorm_bwd(o, gate, dy.to(gate.dtype).contiguous(), eps=ctx.eps, cu_seqlens=cu,
+                                      out_rows=ctx.out_rows)
+        return do, dgate, None, None, None
 
 
-def gated_rmsnorm(o, gate, *, eps=RMS_EPS):
+def gated_rmsnorm(o, gate, *, eps=RMS_EPS, cu_seqlens=None, out_rows=None):
     """Differentiable output gate (``_output_gate`` up to ``W_o``)."""
-    return _GatedRMSNorm.apply(o, gate, eps)
+    if cu_seqlens is not None:
+        cu_seqlens = cu_seqlens.to(device=o.device, dtype=torch.int32)
+    return _GatedRMSNorm.apply(o, gate, eps, cu_seqlens, out_rows)
 
 
 def decode_fused(S, conv_buf, qp, kp, vp, z, beta_logit, conv_q, conv_k, conv_v, A, *, H, b_gate=None,

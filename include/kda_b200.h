@@ -122,6 +122,38 @@ int kda_bwd(const void* q, const void* k, const void* v, const void* g,
             int B, int T, int H, int dk, int dv, int chunk, int in_dtype,
             int do_dtype, int ckpt_dtype, kda_stream_t stream);
 
+/* Packed (variable-length) sequences.  No counterpart in the reference, which
+ * pads every sequence of a batch to one length (net/kda.py:824-830); the
+ * mixer's packed batches (cu_seqlens) need it.  The tensors hold n_seqs
+ * sequences one after another in a single batch row (B = 1) of T tokens,
+ * every sequence starting on a chunk boundary: rows padding a sequence to the
+ * next boundary are zero (q = k = v = g = 0, beta = 0), which leaves the
+ * state unchanged, so the states and every real row are those of the
+ * unpadded sequences.  kda_prologue_fwd with out_rows = chunk * chunk_offsets
+ * writes this layout from packed projections.
+ *   chunk_offsets : device int32 [n_seqs + 1], the first chunk of each
+ *                   sequence: chunk_offsets[0] = 0, non-decreasing,
+ *                   chunk_offsets[n_seqs] = T / chunk
+ *   s0, s_out, dsT, ds0 : [n_seqs, H, dk, dv] fp32 (per sequence)
+ *   s_ckpt        : kda_ckpt_bytes(1, T, H, ...) bytes
+ * T must be a multiple of chunk; everything else as kda_fwd / kda_bwd. */
+int kda_fwd_varlen(const void* q, const void* k, const void* v, const void* g,
+                   const void* beta, const float* s0, void* o, float* s_out,
+                   void* s_ckpt, const int* chunk_offsets, int n_seqs, int T, int H,
+                   int dk, int dv, int chunk, int in_dtype, int o_dtype, int ckpt_dtype,
+                   kda_stream_t stream);
+
+size_t kda_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv,
+                                      int chunk, int in_dtype);
+
+int kda_bwd_varlen(const void* q, const void* k, const void* v, const void* g,
+                   const void* beta, const void* s_ckpt, const void* do_,
+                   const float* dsT, void* dq, void* dk_, void* dv_, void* dg,
+                   void* dbeta, float* ds0, void* workspace, size_t workspace_bytes,
+                   const int* chunk_offsets, int n_seqs, int T, int H, int dk, int dv,
+                   int chunk, int in_dtype, int do_dtype, int ckpt_dtype,
+                   kda_stream_t stream);
+
 /* Size of the fixed device scratch array used by kda_bwd_noalloc (32 MiB). */
 #define KDA_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -44,9 +44,17 @@ enum {
  *   conv_state_in  : fp32 conv state or NULL (zeros): inputs before t = 0
  *   conv_state_out : fp32 conv state or NULL: the last K-1 inputs (the next
  *                    call's conv_state_in); must not overlap conv_state_in
- *   cu_seqlens     : int32 [n_seqs + 1] or NULL: packed sequences (B must be 1,
- *                    conv states NULL); every sequence starts from zeros
- *   q, k, g : [B,T,H,dk];  v : [B,T,H,dv];  beta : [B,T,H]   (out_dtype)
+ *   cu_seqlens     : device int32 [n_seqs + 1] or NULL: packed sequences (B must
+ *                    be 1, conv states NULL); every sequence starts from zeros
+ *   out_rows       : device int32 [n_seqs + 1] or NULL (needs cu_seqlens): the
+ *                    outputs' row of each sequence's first token; token t of
+ *                    sequence s goes to row t - cu_seqlens[s] + out_rows[s] and
+ *                    the rows after a sequence's last token up to
+ *                    out_rows[s + 1] are written as zeros -- with
+ *                    out_rows = chunk * chunk_offsets this is the packed layout
+ *                    of kda_fwd_varlen
+ *   q, k, g : [B,T',H,dk];  v : [B,T',H,dv];  beta : [B,T',H]   (out_dtype;
+ *   T' = T, or out_rows[n_seqs])
  * Supported: dk, dv in {64, 128}; inputs in_dtype, outputs out_dtype
  * (KDA_BF16 or KDA_F32); every tensor pointer 16-byte aligned except beta
  * and beta_logit. */
@@ -54,17 +62,17 @@ int kda_prologue_fwd(const void* qp, const void* kp, const void* vp, const void*
                      const void* beta_logit, const float* conv_q, const float* conv_k,
                      const float* conv_v, const float* b_gate, const float* A, float g_min,
                      int gate_kind, const float* conv_state_in, float* conv_state_out,
-                     const int* cu_seqlens, int n_seqs, void* q, void* k, void* v, void* g,
-                     void* beta, int B, int T, int H, int dk, int dv, int K, int in_dtype,
-                     int out_dtype, kda_stream_t stream);
+                     const int* cu_seqlens, int n_seqs, const int* out_rows, void* q, void* k,
+                     void* v, void* g, void* beta, int B, int T, int H, int dk, int dv, int K,
+                     int in_dtype, int out_dtype, kda_stream_t stream);
 
 /* Scratch bytes kda_prologue_bwd needs (per-block partial sums of the weight
  * gradients, reduced in a fixed order: the result is deterministic). */
 size_t kda_prologue_bwd_workspace_bytes(int B, int T, int H, int dk, int dv, int K);
 
 /* Fused prologue, backward: the same inputs, the cotangents of the forward's
- * outputs (dq, dk_, dg [B,T,H,dk], dv_ [B,T,H,dv], dbeta [B,T,H], out_dtype),
- * and produces
+ * outputs (dq, dk_, dg [B,T',H,dk], dv_ [B,T',H,dv], dbeta [B,T',H], out_dtype,
+ * rows as the forward's outputs), and produces
  *   dqp, dkp, dz [B,T,H*dk], dvp [B,T,H*dv], dbeta_logit [B,T,H]   (in_dtype)
  *   dconv_q, dconv_k [K,H*dk], dconv_v [K,H*dv], db_gate [H*dk], dA [H]   (fp32,
  *   overwritten), dconv_state_in (fp32 conv state, or NULL).
@@ -73,7 +81,7 @@ int kda_prologue_bwd(const void* qp, const void* kp, const void* vp, const void*
                      const void* beta_logit, const float* conv_q, const float* conv_k,
                      const float* conv_v, const float* b_gate, const float* A, float g_min,
                      int gate_kind, const float* conv_state_in, const int* cu_seqlens,
-                     int n_seqs, const void* dq, const void* dk_, const void* dv_,
+                     int n_seqs, const int* out_rows, const void* dq, const void* dk_, const void* dv_,
                      const void* dg, const void* dbeta, void* dqp, void* dkp, void* dvp,
                      void* dz, void* dbeta_logit, float* dconv_q, float* dconv_k,
                      float* dconv_v, float* db_gate, float* dA, float* dconv_state_in,
@@ -81,16 +89,20 @@ int kda_prologue_bwd(const void* qp, const void* kp, const void* vp, const void*
                      int dv, int K, int in_dtype, int out_dtype, kda_stream_t stream);
 
 /* Output gate, forward: y = sigmoid(gate) * o / sqrt(mean_dv(o^2) + eps) per
- * (row, head) for N rows: o [N, H, dv], gate logits and y [N, H*dv].
+ * (row, head) for N rows: gate logits and y [N, H*dv], o [N', H, dv] with row
+ * t of y at row t of o, or (cu_seqlens and out_rows as kda_prologue_fwd's,
+ * else NULL) at the packed layout's row of token t.
  * Supported: dv in {64, 128}; o, gate, y 16-byte aligned. */
-int kda_gated_rmsnorm_fwd(const void* o, const void* gate, void* y, int N, int H, int dv,
-                          float eps, int o_dtype, int gate_dtype, int y_dtype,
-                          kda_stream_t stream);
+int kda_gated_rmsnorm_fwd(const void* o, const void* gate, void* y, const int* cu_seqlens,
+                          const int* out_rows, int n_seqs, int N, int H, int dv, float eps,
+                          int o_dtype, int gate_dtype, int y_dtype, kda_stream_t stream);
 
-/* Output gate, backward: do_ (o_dtype) and dgate (gate_dtype) from dy (y_dtype). */
+/* Output gate, backward: do_ (o_dtype, o's rows; with out_rows its pad rows
+ * are written as zeros) and dgate (gate_dtype) from dy (y_dtype). */
 int kda_gated_rmsnorm_bwd(const void* o, const void* gate, const void* dy, void* do_,
-                          void* dgate, int N, int H, int dv, float eps, int o_dtype,
-                          int gate_dtype, int y_dtype, kda_stream_t stream);
+                          void* dgate, const int* cu_seqlens, const int* out_rows, int n_seqs,
+                          int N, int H, int dv, float eps, int o_dtype, int gate_dtype,
+                          int y_dtype, kda_stream_t stream);
 
 /* One streaming decode token for N sequences, H heads (recurrent_step
  * without the projection GEMMs): ShortConv steps over conv_buf (updated in

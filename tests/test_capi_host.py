@@ -129,10 +129,10 @@ def test_prologue_validation():
     w = [None] * 10
     outs = [None] * 5
 
-    def fwd(*, kind=0, st=(None, None), cu=None, n_seqs=0, dims=(1, 64, 2, 128, 128, 4), dt=(1, 1), ptrs=None,
-            o=None):
-        return lib.kda_prologue_fwd(*(ptrs or w), -5.0, kind, st[0], st[1], cu, n_seqs, *(o or outs), *dims, *dt,
-                                    None)
+    def fwd(*, kind=0, st=(None, None), cu=None, n_seqs=0, rows=None, dims=(1, 64, 2, 128, 128, 4), dt=(1, 1),
+            ptrs=None, o=None):
+        return lib.kda_prologue_fwd(*(ptrs or w), -5.0, kind, st[0], st[1], cu, n_seqs, rows, *(o or outs), *dims,
+                                    *dt, None)
 
     assert fwd(dims=(1, 64, 2, 96, 128, 4)) == -1       # dk not 64/128
     assert fwd(dims=(1, 64, 2, 128, 128, 5)) == -1      # K > 4
@@ -146,26 +146,47 @@ def test_prologue_validation():
     assert fwd(cu=fake, n_seqs=2, dims=(2, 64, 2, 128, 128, 4)) == -1
     assert fwd(cu=fake, n_seqs=2, st=(fake, None)) == -1
     assert fwd(ptrs=[odd] + [fake] * 9, o=[fake] * 5) == -3
+    assert fwd(rows=fake, ptrs=[fake] * 10, o=[fake] * 5) == -1  # out_rows without cu_seqlens
     assert lib.kda_prologue_bwd_workspace_bytes(1, 64, 2, 128, 128, 4) > 0
     assert lib.kda_prologue_bwd_workspace_bytes(1, 64, 2, 100, 128, 4) == 0
-    bw = lib.kda_prologue_bwd(*([fake] * 10), -5.0, 0, None, None, 0, *([fake] * 10), *([fake] * 5), None,
+    bw = lib.kda_prologue_bwd(*([fake] * 10), -5.0, 0, None, None, 0, None, *([fake] * 10), *([fake] * 5), None,
                               None, 0, 1, 64, 2, 128, 128, 4, 1, 1, None)
     assert bw == -6                                       # workspace missing
 
 
 def test_gated_rmsnorm_and_fused_decode_validation():
     lib = _lib.lib()
-    assert lib.kda_gated_rmsnorm_fwd(None, None, None, 4, 2, 96, 1e-6, 1, 1, 1, None) == -1
-    assert lib.kda_gated_rmsnorm_fwd(None, None, None, 0, 2, 128, 1e-6, 1, 1, 1, None) == 0
-    assert lib.kda_gated_rmsnorm_fwd(None, None, None, 4, 2, 128, 1e-6, 1, 1, 1, None) == -4
-    assert lib.kda_gated_rmsnorm_bwd(*([None] * 5), 4, 2, 128, 1e-6, 3, 1, 1, None) == -2
+    nomap = (None, None, 0)
+    assert lib.kda_gated_rmsnorm_fwd(None, None, None, *nomap, 4, 2, 96, 1e-6, 1, 1, 1, None) == -1
+    assert lib.kda_gated_rmsnorm_fwd(None, None, None, *nomap, 0, 2, 128, 1e-6, 1, 1, 1, None) == 0
+    assert lib.kda_gated_rmsnorm_fwd(None, None, None, *nomap, 4, 2, 128, 1e-6, 1, 1, 1, None) == -4
+    assert lib.kda_gated_rmsnorm_bwd(*([None] * 5), *nomap, 4, 2, 128, 1e-6, 3, 1, 1, None) == -2
     fake = ctypes.c_void_p(16)
+    # a row map needs the sequence offsets
+    assert lib.kda_gated_rmsnorm_fwd(fake, fake, fake, None, fake, 2, 4, 2, 128, 1e-6, 1, 1, 1, None) == -1
     args = [fake, fake] + [fake] * 11
     assert lib.kda_decode_fused(*args, -5.0, 0, 1e-6, fake, 4, 2, 96, 128, 4, 1, 1, None) == -1
     assert lib.kda_decode_fused(*args, -5.0, 2, 1e-6, fake, 4, 2, 128, 128, 4, 1, 1, None) == -1
     no_buf = [fake, None] + [fake] * 11
     assert lib.kda_decode_fused(*no_buf, -5.0, 0, 1e-6, fake, 4, 2, 128, 128, 4, 1, 1, None) == -4
     assert lib.kda_decode_fused(*args, -5.0, 0, 1e-6, fake, 0, 2, 128, 128, 4, 1, 1, None) == 0
+
+
+def test_varlen_core_validation():
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(16)
+    # T must be a multiple of the chunk; the chunk offsets are required
+    assert lib.kda_fwd_varlen(*([fake] * 9), fake, 2, 100, 2, 128, 128, 64, 1, 1, 1, None) == -1
+    assert lib.kda_fwd_varlen(*([fake] * 9), None, 2, 128, 2, 128, 128, 64, 1, 1, 1, None) == -4
+    assert lib.kda_fwd_varlen(*([fake] * 9), fake, -1, 128, 2, 128, 128, 64, 1, 1, 1, None) == -1
+    assert lib.kda_fwd_varlen(*([None] * 10), 0, 128, 2, 128, 128, 64, 1, 1, 1, None) == 0
+    args = [fake] * 14 + [None, 0]
+    assert lib.kda_bwd_varlen(*args, fake, 2, 128, 2, 128, 128, 64, 1, 1, 1, None) == -6  # workspace missing
+    assert lib.kda_bwd_varlen_workspace_bytes(2, 128, 2, 128, 128, 64, 1) >= \
+        lib.kda_bwd_workspace_bytes(1, 128, 2, 128, 128, 64, 1)
+    # the CUDA-core path's scratch is per sequence
+    assert lib.kda_bwd_varlen_workspace_bytes(3, 96, 2, 32, 32, 32, 0) == \
+        lib.kda_bwd_workspace_bytes(3, 96, 2, 32, 32, 32, 0)
 
 
 def test_impl_switch_fails_closed(monkeypatch):
