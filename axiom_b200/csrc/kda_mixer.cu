@@ -930,27 +930,36 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecA
   const int HK = a.H * DK, HV = a.H * DV;
   const int sw = 2 * HK + HV;
   float* bufn = a.buf ? a.buf + static_cast<size_t>(n) * (a.K - 1) * sw : nullptr;
-  auto conv_step = [&](const Tin* xp, const float* w, int stride_x, int col_buf, int c) -> float {
-    const float xt = ldf(xp + static_cast<size_t>(n) * stride_x + c);
+  // Every load of this token's prologue is issued before any store (the conv
+  // rows are shifted in place only at the end), so the round trips overlap.
+  auto load_taps = [&](const Tin* xp, int stride_x, int col_buf, int c, float (&bj)[3]) -> float {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) bj[j] = j < a.K - 1 ? bufn[static_cast<size_t>(j) * sw + col_buf + c] : 0.f;
+    return ldf(xp + static_cast<size_t>(n) * stride_x + c);
+  };
+  auto conv = [&](const float* w, int stride_x, int c, float xt, const float (&bj)[3]) -> float {
     float acc = w[c] * xt;  // w[0] x_t + sum_j w[K-1-j] buf[j]
-    float prev = xt;
-    for (int j = a.K - 2; j >= 0; --j) {  // newest first; shift the rows up in place
-      float* p = bufn + static_cast<size_t>(j) * sw + col_buf + c;
-      const float bj = *p;
-      acc += w[(a.K - 1 - j) * stride_x + c] * bj;
-      *p = prev;
-      prev = bj;
-    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      if (j < a.K - 1) acc += w[(a.K - 1 - j) * stride_x + c] * bj[j];
     return acc;
+  };
+  auto shift = [&](int col_buf, int c, float xt, const float (&bj)[3]) {  // oldest row out, x_t in
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      if (j < a.K - 1) bufn[static_cast<size_t>(j) * sw + col_buf + c] = j + 1 < a.K - 1 ? bj[j + 1] : xt;
   };
   float qv = 0.f, kv = 0.f;
   if (tid < DK) {
     const int c = h * DK + tid;
-    const float cq = conv_step(static_cast<const Tin*>(a.qp), a.w[0], HK, 0, c);
-    const float ck = conv_step(static_cast<const Tin*>(a.kp), a.w[1], HK, HK, c);
+    float bq[3], bk[3];
+    const float xq = load_taps(static_cast<const Tin*>(a.qp), HK, 0, c, bq);
+    const float xk = load_taps(static_cast<const Tin*>(a.kp), HK, HK, c, bk);
+    const float u = ldf(static_cast<const Tin*>(a.z) + static_cast<size_t>(n) * HK + c) + (a.b_gate ? a.b_gate[c] : 0.f);
+    const float cq = conv(a.w[0], HK, c, xq, bq);
+    const float ck = conv(a.w[1], HK, c, xk, bk);
     qv = cq * sigmoidf_(cq);
     kv = ck * sigmoidf_(ck);
-    const float u = ldf(static_cast<const Tin*>(a.z) + static_cast<size_t>(n) * HK + c) + (a.b_gate ? a.b_gate[c] : 0.f);
     const float ea = __expf(a.A[h]);
     const float g = a.gate_kind == KDA_GATE_SIGMOID_MIN ? a.g_min * sigmoidf_(ea * u) : -ea * softplusf_(u);
     s_a[tid] = __expf(g);
@@ -959,10 +968,15 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecA
       s_nrm[0][warp] = sq;
       s_nrm[1][warp] = sk;
     }
+    shift(0, c, xq, bq);
+    shift(HK, c, xk, bk);
   } else if (tid < DK + DV) {
     const int c = h * DV + tid - DK;
-    const float cv = conv_step(static_cast<const Tin*>(a.vp), a.w[2], HV, 2 * HK, c);
+    float bv[3];
+    const float xv = load_taps(static_cast<const Tin*>(a.vp), HV, 2 * HK, c, bv);
+    const float cv = conv(a.w[2], HV, c, xv, bv);
     s_v[tid - DK] = cv * sigmoidf_(cv);
+    shift(2 * HK, c, xv, bv);
   }
   if (tid == kDecThreads - 1)
     s_beta = sigmoidf_(ldf(static_cast<const Tin*>(a.beta_logit) + static_cast<size_t>(n) * a.H + h));

@@ -1,0 +1,116 @@
+"""The KDA mixer layer on the B200 kernels: projections, fused prologue, KDA
+core, output gate and output projection, differentiable end to end.
+
+Mirrors the reference's layer function ``apply_kda(params, cfg, x,
+chunk_size)`` (AXIOM ``net/kda.py:929-946``; ``_project`` :157-191,
+``_postprocess`` :194-203, ``_output_gate`` :206-214), with two additions the
+mixer configuration needs: packed variable-length batches (``cu_seqlens``) and
+the decay gate ``g = -exp(A_log) * softplus(z + b)`` beside the reference's
+``g = g_min * sigmoid(exp(A) z)``.  The projection GEMMs are plain library
+GEMMs (``torch.matmul``: cuBLAS); the per-token work and the KDA core run in
+``libkda_b200.so``.  The reference's sliding-window branch (``_with_window``
+:261-269) is outside this layer.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, fields
+
+import torch
+
+from . import mixer
+from .kda import CHUNK, chunk_kda, chunk_kda_varlen, packing
+
+
+@dataclass
+class KDALayerParams:
+    """Weights of one layer (the reference's ``KDAParams``, ``net/kda.py:63-80``;
+    ``b_gate`` is its ``b_alpha``, ``A`` its ``A`` or the mixer's ``A_log``)."""
+
+    W_q: torch.Tensor       # [d_model, H*dk]
+    W_k: torch.Tensor       # [d_model, H*dk]
+    W_v: torch.Tensor       # [d_model, H*dv]
+    W_g: torch.Tensor       # [d_model, H*dv]   output gate
+    W_beta: torch.Tensor    # [d_model, H]
+    W_a_down: torch.Tensor  # [d_model, rank]
+    W_a_up: torch.Tensor    # [rank, H*dk]
+    b_gate: torch.Tensor    # [H*dk] fp32
+    A: torch.Tensor         # [H] fp32
+    conv_q: torch.Tensor    # [K, H*dk] fp32
+    conv_k: torch.Tensor    # [K, H*dk] fp32
+    conv_v: torch.Tensor    # [K, H*dv] fp32
+    W_o: torch.Tensor       # [H*dv, d_model]
+
+    def tensors(self):
+        return [getattr(self, f.name) for f in fields(self)]
+
+
+def init_params(d_model, H, dk, dv, *, rank=128, K=4, gate_kind="softplus", gate_bias="dt",
+                dtype=torch.bfloat16, device="cuda", seed=0) -> KDALayerParams:
+    """Random-init weights: projections N(0, 0.02) (the reference's ``_rand``
+    scale, ``net/kda.py:110-127``), conv taps N(0, 0.1), ``A`` zero for the
+    reference's gate (with ``b_alpha`` zero, ``net/kda.py:124-125``) or
+    ``A_log ~ U(log 1, log 16)`` for the softplus gate.  The softplus gate's
+    bias: ``gate_bias="dt"`` sets ``softplus(b)`` log-uniform in
+    ``[1e-3, 1e-1]`` per channel (the usual time-step bias of this gate form),
+    ``"zero"`` sets ``b = 0`` (per-token decay up to ``16 log 2``: every chunk
+    then exceeds the tensor-core path's exponent budget).  Every tensor
+    requires grad."""
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+
+    def rnd(*shape, scale, dt=dtype):
+        return (torch.randn(*shape, generator=gen) * scale).to(device=device, dtype=dt).requires_grad_(True)
+
+    b = torch.zeros(H * dk)
+    if gate_kind == "softplus":
+        A = torch.empty(H).uniform_(0.0, float(torch.log(torch.tensor(16.0))), generator=gen)
+        if gate_bias == "dt":
+            lo, hi = float(torch.log(torch.tensor(1e-3))), float(torch.log(torch.tensor(1e-1)))
+            dt_ = torch.exp(torch.empty(H * dk).uniform_(lo, hi, generator=gen))
+            b = dt_ + torch.log(-torch.expm1(-dt_))  # softplus^-1(dt)
+        elif gate_bias != "zero":
+            raise ValueError(f"gate_bias={gate_bias!r}: expected 'dt' or 'zero'")
+    else:
+        A = torch.zeros(H)
+    return KDALayerParams(
+        W_q=rnd(d_model, H * dk, scale=0.02), W_k=rnd(d_model, H * dk, scale=0.02),
+        W_v=rnd(d_model, H * dv, scale=0.02), W_g=rnd(d_model, H * dv, scale=0.02),
+        W_beta=rnd(d_model, H, scale=0.02), W_a_down=rnd(d_model, rank, scale=0.02),
+        W_a_up=rnd(rank, H * dk, scale=0.02), b_gate=b.to(device).requires_grad_(True),
+        A=A.to(device).requires_grad_(True), conv_q=rnd(K, H * dk, scale=0.1, dt=torch.float32),
+        conv_k=rnd(K, H * dk, scale=0.1, dt=torch.float32), conv_v=rnd(K, H * dv, scale=0.1, dt=torch.float32),
+        W_o=rnd(H * dv, d_model, scale=0.02))
+
+
+def kda_layer(p: KDALayerParams, x, *, H, cu_seqlens=None, gate_kind="softplus", g_min=mixer.G_MIN,
+              chunk=CHUNK, S0=None, return_state=False):
+    """One KDA mixer layer: ``x [T, d_model]`` (one sequence, or the packed
+    sequences ``cu_seqlens`` delimits) -> ``[T, d_model]``.
+
+    ``S0``/``S_T``: ``[n, H, dk, dv]`` fp32 (one state per sequence).
+    """
+    T, _ = x.shape
+    dk = p.W_q.shape[1] // H
+    dv = p.W_v.shape[1] // H
+    # projections (_project, net/kda.py:157-191)
+    qp, kp, vp = x @ p.W_q, x @ p.W_k, x @ p.W_v
+    z = (x @ p.W_a_down) @ p.W_a_up
+    bl = x @ p.W_beta
+    gl = x @ p.W_g
+    if cu_seqlens is None:
+        q, k, v, g, beta = mixer.kda_prologue(qp[None], kp[None], vp[None], z[None], bl[None], p.conv_q, p.conv_k,
+                                              p.conv_v, p.A, H=H, b_gate=p.b_gate, g_min=g_min,
+                                              gate_kind=gate_kind)
+        o, s_t = chunk_kda(q, k, v, g, beta, S0, chunk=chunk)
+        y = mixer.gated_rmsnorm(o, gl[None])
+    else:
+        offs, rows, _ = packing(cu_seqlens, chunk)
+        cu = cu_seqlens if isinstance(cu_seqlens, torch.Tensor) else torch.tensor(list(cu_seqlens))
+        cu = cu.to(device=x.device, dtype=torch.int32)
+        q, k, v, g, beta = mixer.kda_prologue(qp[None], kp[None], vp[None], z[None], bl[None], p.conv_q, p.conv_k,
+                                              p.conv_v, p.A, H=H, b_gate=p.b_gate, g_min=g_min,
+                                              gate_kind=gate_kind, cu_seqlens=cu, out_rows=rows)
+        o, s_t = chunk_kda_varlen(q, k, v, g, beta, offs, S0, chunk=chunk)
+        y = mixer.gated_rmsnorm(o, gl[None], cu_seqlens=cu, out_rows=rows)
+    out = y[0] @ p.W_o
+    return (out, s_t) if return_state else out

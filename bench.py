@@ -303,6 +303,9 @@ def run_b200(args):
     if rank == 0 and not args.no_extra:
         extra["decode"] = run_decode(torch, KD, dev, peaks)
         extra["prefill"] = run_prefill(torch, KD, dev, peaks)
+        extra["mixer_kernels"] = run_mixer_kernels(torch, dev, peaks)
+        extra["mixer_cfg5"] = run_mixer_layer(torch, dev, peaks)
+        extra["mixer_cfg5_strong_decay"] = run_mixer_layer(torch, dev, peaks, gate_bias="zero")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(sample_heads=args.cpu_heads, cfg=cfg)
@@ -438,6 +441,112 @@ def run_decode(torch, KD, dev, peaks, steps=64, warmup=8):
             "frac": gbs / peaks["hbm"], "bytes_per_step": state_bytes + in_bytes, "steps": steps}
 
 
+def _time(torch, fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def run_mixer_kernels(torch, dev, peaks, steps=10, warmup=3, B=4):
+    """The per-token kernels around the core at cfg3 shapes (B=4, T=8192, H=32,
+    d=128, conv K=4, bf16), HBM-bound: achieved GB/s of their algorithmic bytes
+    (every input read once, every output written once).  Plus the fused decode
+    step (cfg4: 256 sequences x 32 heads) with the conv buffers and output gate."""
+    from axiom_b200 import mixer
+
+    T, H, D, K = 8192, 32, 128, 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    bf = torch.bfloat16
+
+    def rn(*shape, scale=1.0, dt=bf):
+        return (torch.randn(*shape, generator=gen, device=dev) * scale).to(dt)
+
+    qp, kp, vp, z = (rn(B, T, H * D) for _ in range(4))
+    bl = rn(B, T, H)
+    w = [rn(K, H * D, scale=0.5, dt=torch.float32) for _ in range(3)]
+    A = rn(H, scale=0.3, dt=torch.float32)
+    bg = rn(H * D, scale=0.3, dt=torch.float32)
+    outs = mixer.prologue_fwd(qp, kp, vp, z, bl, *w, A, H=H, b_gate=bg, gate_kind="softplus")
+    cots = [torch.randn_like(o) for o in outs]
+    rows = B * T * H
+    res = {}
+    t_f = _time(torch, lambda: mixer.prologue_fwd(qp, kp, vp, z, bl, *w, A, H=H, b_gate=bg, gate_kind="softplus"),
+                steps, warmup)
+    t_b = _time(torch, lambda: mixer.prologue_bwd(qp, kp, vp, z, bl, *w, A, *cots, H=H, b_gate=bg,
+                                                  gate_kind="softplus"), steps, warmup)
+    row_b = 4 * D * 2 + 2  # q, k, v, g rows + beta, bf16
+    for name, ms, nbytes in (("prologue_fwd", t_f, rows * row_b * 2), ("prologue_bwd", t_b, rows * row_b * 3)):
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"ms": ms, "bytes": nbytes, "GB/s": gbs, "frac": gbs / peaks["hbm"]}
+    o = torch.randn(B * T, H, D, generator=gen, device=dev)
+    gl = rn(B * T, H * D)
+    dy = torch.randn_like(gl)
+    t_gf = _time(torch, lambda: mixer.gated_rmsnorm_fwd(o, gl), steps, warmup)
+    t_gb = _time(torch, lambda: mixer.gated_rmsnorm_bwd(o, gl, dy), steps, warmup)
+    for name, ms, nbytes in (("gated_rmsnorm_fwd", t_gf, rows * D * (4 + 2 + 2)),
+                             ("gated_rmsnorm_bwd", t_gb, rows * D * (4 + 2 + 2 + 4 + 2))):
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"ms": ms, "bytes": nbytes, "GB/s": gbs, "frac": gbs / peaks["hbm"]}
+    # fused decode: one token of 256 sequences x 32 heads (conv step, gates, update, output gate)
+    N, Hd = CFG4["N"] // 32, 32
+    S = torch.randn(N, Hd, D, D, generator=gen, device=dev) * 0.02
+    buf = torch.randn(N, K - 1, Hd * 3 * D, generator=gen, device=dev)
+    wd = [rn(K, Hd * D, scale=0.5, dt=torch.float32) for _ in range(3)]
+    Ad = rn(Hd, scale=0.3, dt=torch.float32)
+    xs = [rn(N, Hd * D) for _ in range(5)]
+    bd = rn(N, Hd)
+    t_d = _time(torch, lambda: mixer.decode_fused(S, buf, xs[0], xs[1], xs[2], xs[3], bd, *wd, Ad, H=Hd,
+                                                  gate_logit=xs[4], gate_kind="softplus"),
+                max(steps, 1) * 8, max(warmup, 1))
+    nbytes = 2 * N * Hd * D * D * 4 + 2 * N * (K - 1) * Hd * 3 * D * 4 + N * Hd * D * 2 * 6 + N * Hd * 2
+    gbs = nbytes / (t_d / 1e3) / 1e9
+    res["decode_fused"] = {"workload": "cfg4 decode token with conv buffers and output gate", "us": t_d * 1e3,
+                           "bytes": nbytes, "GB/s": gbs, "frac": gbs / peaks["hbm"]}
+    res["config"] = f"B={B} T=8192 H=32 d=128 K=4 bf16 (cfg3 shapes at B=4); decode: cfg4"
+    return res
+
+
+def run_mixer_layer(torch, dev, peaks, steps=3, warmup=2, gate_bias="dt"):
+    """BASELINE's mixer configuration (cfg5): one KDA layer, d_model=2048, H=16,
+    dk=dv=128, rank-128 softplus gate, conv K=4, 16 packed sequences (lengths
+    U[512, 8192] rescaled to T=65536), bf16, forward + backward of every
+    weight and the input, on one GPU."""
+    import numpy as np
+
+    from axiom_b200 import layer
+
+    rng = np.random.default_rng(5)
+    L = rng.uniform(512, 8192, 16)
+    L = np.floor(L / L.sum() * 65536).astype(int)
+    L[-1] += 65536 - int(L.sum())
+    cu = [0] + np.cumsum(L).tolist()
+    p = layer.init_params(2048, 16, 128, 128, rank=128, K=4, gate_kind="softplus", gate_bias=gate_bias,
+                          dtype=torch.bfloat16, device=dev, seed=5)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(12)
+    x = torch.randn(65536, 2048, generator=gen, device=dev).to(torch.bfloat16).requires_grad_(True)
+    dout = torch.randn(65536, 2048, generator=gen, device=dev).to(torch.bfloat16)
+
+    def step():
+        for t in p.tensors() + [x]:
+            t.grad = None
+        layer.kda_layer(p, x, H=16, cu_seqlens=cu, gate_kind="softplus").backward(dout)
+
+    ms = _time(torch, step, steps, warmup)
+    del p, x, dout
+    torch.cuda.empty_cache()
+    return {"workload": f"cfg5 KDA mixer layer fwd+bwd, 16 packed seqs, T=65536, d_model=2048, H=16, gate bias {gate_bias}",
+            "ms_per_step": ms, "tokens/s": 65536 / (ms / 1e3), "steps": steps}
+
+
 def run_prefill(torch, KD, dev, peaks, steps=5, warmup=3):
     """forward only, B=8, T=4096, H=16, S0 ~ N(0, 0.02)."""
     cfg = dict(CFG2)
@@ -535,8 +644,18 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override B per rank (profiling cases)")
     ap.add_argument("--seqlen", type=int, default=0, help="override T (profiling cases)")
     ap.add_argument("--heads", type=int, default=0, help="override H (profiling cases)")
+    ap.add_argument("--mixer-only", action="store_true",
+                    help="time only the mixer kernels (prologue, output gate, fused decode); --batch sets B")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # the timing contract needs >= 3 untimed warm-up steps
+    if args.mixer_only:
+        import torch
+
+        torch.cuda.set_device(0)
+        res = run_mixer_kernels(torch, torch.device("cuda", 0), _peaks(), steps=args.steps,
+                                warmup=args.warmup, B=args.batch or 4)
+        print(json.dumps({"mixer_kernels": res}), flush=True)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

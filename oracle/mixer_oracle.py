@@ -335,3 +335,70 @@ def decode_fused_step(S, conv_buf, qp, kp, vp, z, beta_logit, wq, wk, wv, b_gate
         Sn[n] = s_new
         out[n] = o if gate_logit is None else gated_rmsnorm(o, np.asarray(gate_logit[n], np.float64).reshape(H, dv))
     return Sn, bufn, out
+
+
+# ---------------------------------------------------------------------------
+# the whole layer: projections -> prologue -> core -> output gate -> W_o
+# ---------------------------------------------------------------------------
+
+
+def layer_fwd(P, x, H, cu_seqlens=None, kind=GATE_SOFTPLUS, g_min=G_MIN, chunk=64):
+    """``apply_kda`` of one layer (``net/kda.py:929-946`` with ``_project``
+    :157-191, ``_postprocess`` :194-203 and ``_output_gate`` :206-214) over
+    ``x [T, d_model]``, float64.  ``P`` maps the weight names of
+    ``axiom_b200.layer.KDALayerParams`` to arrays.  Returns ``(out, cache)``;
+    ``cache`` feeds :func:`layer_bwd`."""
+    from oracle.kda_oracle import chunk_fwd
+
+    x = np.asarray(x, np.float64)
+    T = x.shape[0]
+    dk = P["W_q"].shape[1] // H
+    dv = P["W_v"].shape[1] // H
+    a_down = x @ P["W_a_down"]
+    proj = dict(qp=x @ P["W_q"], kp=x @ P["W_k"], vp=x @ P["W_v"], z=a_down @ P["W_a_up"], bl=x @ P["W_beta"],
+                gl=x @ P["W_g"])
+    pro = prologue_fwd(proj["qp"][None], proj["kp"][None], proj["vp"][None], proj["z"][None], proj["bl"][None],
+                       P["conv_q"], P["conv_k"], P["conv_v"], P["b_gate"], P["A"], H, dk, dv, g_min=g_min, kind=kind,
+                       cu_seqlens=cu_seqlens)
+    cu = [0, T] if cu_seqlens is None else [int(c) for c in cu_seqlens]
+    o = np.zeros((T, H, dv))
+    for a, b in zip(cu[:-1], cu[1:]):
+        if b > a:
+            o[a:b] = chunk_fwd(*(pro[n][:, a:b] for n in ("q", "k", "v", "g", "beta")), None, chunk=chunk)[0][0]
+    y = gated_rmsnorm(o, proj["gl"].reshape(T, H, dv)).reshape(T, H * dv)
+    cache = dict(x=x, a_down=a_down, proj=proj, pro=pro, o=o, y=y, cu=cu, H=H, dk=dk, dv=dv, kind=kind,
+                 g_min=g_min, chunk=chunk, cu_seqlens=cu_seqlens)
+    return y @ P["W_o"], cache
+
+
+def layer_bwd(P, cache, dout):
+    """Cotangents of :func:`layer_fwd`'s input and weights for ``dout``:
+    ``{"x": ..., <weight name>: ...}`` -- the VJPs of the pieces composed."""
+    from oracle.kda_oracle import chunk_bwd
+
+    x, proj, pro, o, y, cu = (cache[n] for n in ("x", "proj", "pro", "o", "y", "cu"))
+    H, dk, dv = cache["H"], cache["dk"], cache["dv"]
+    T = x.shape[0]
+    dout = np.asarray(dout, np.float64)
+    g = {"W_o": y.T @ dout}
+    dy = (dout @ P["W_o"].T).reshape(T, H, dv)
+    do, dgl = gated_rmsnorm_bwd(o, proj["gl"].reshape(T, H, dv), dy)
+    c = {n: np.zeros_like(pro[n]) for n in ("q", "k", "v", "g", "beta")}
+    for a, b in zip(cu[:-1], cu[1:]):
+        if b > a:
+            r = chunk_bwd(*(pro[n][:, a:b] for n in ("q", "k", "v", "g", "beta")), None, do[a:b][None], None,
+                          chunk=cache["chunk"])
+            for n, d in zip(("q", "k", "v", "g", "beta"), r[:5]):
+                c[n][:, a:b] = d
+    pb = prologue_bwd(proj["qp"][None], proj["kp"][None], proj["vp"][None], proj["z"][None], proj["bl"][None],
+                      P["conv_q"], P["conv_k"], P["conv_v"], P["b_gate"], P["A"], H, dk, dv, c["q"], c["k"], c["v"],
+                      c["g"], c["beta"], g_min=cache["g_min"], kind=cache["kind"], cu_seqlens=cache["cu_seqlens"])
+    d = dict(qp=pb["dqp"][0], kp=pb["dkp"][0], vp=pb["dvp"][0], z=pb["dz"][0], bl=pb["dbeta_logit"][0],
+             gl=dgl.reshape(T, H * dv))
+    da_down = d["z"] @ P["W_a_up"].T
+    g.update(W_q=x.T @ d["qp"], W_k=x.T @ d["kp"], W_v=x.T @ d["vp"], W_g=x.T @ d["gl"], W_beta=x.T @ d["bl"],
+             W_a_up=cache["a_down"].T @ d["z"], W_a_down=x.T @ da_down, conv_q=pb["dwq"], conv_k=pb["dwk"],
+             conv_v=pb["dwv"], b_gate=pb["db_gate"], A=pb["dA"])
+    g["x"] = (d["qp"] @ P["W_q"].T + d["kp"] @ P["W_k"].T + d["vp"] @ P["W_v"].T + d["gl"] @ P["W_g"].T
+              + d["bl"] @ P["W_beta"].T + da_down @ P["W_a_down"].T)
+    return g

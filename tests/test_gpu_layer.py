@@ -1,0 +1,51 @@
+"""The whole KDA mixer layer (``axiom_b200.layer.kda_layer``: projections,
+prologue, core, output gate, output projection) against the oracle's
+composition (``oracle.mixer_oracle.layer_fwd`` / ``layer_bwd``, whose VJPs
+``tests/test_mixer_oracle.py`` checks by finite differences), forward and every
+gradient, packed and unpacked.  fp32 runs the CUDA-core KDA path (bound 1e-3
+over the chain of eight GEMMs and four kernels); bf16 with dk = dv = 128 runs
+the tensor-core path and its bf16 intermediates (bound 5e-2)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mixer_oracle as M
+from oracle.kda_oracle import scale_rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dt,dk,cu,kind", [
+    (torch.float32, 64, [0, 70, 103, 103, 233], "softplus"),
+    (torch.float32, 64, None, "sigmoid_min"),
+    (torch.bfloat16, 128, [0, 130, 131, 300], "softplus"),
+])
+def test_layer_matches_oracle(dt, dk, cu, kind):
+    from axiom_b200 import layer
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    d_model, H, dv = 96, 2, dk
+    T = 233 if cu is None else cu[-1]
+    p = layer.init_params(d_model, H, dk, dv, rank=16, K=4, gate_kind=kind, dtype=dt, seed=3)
+    with torch.no_grad():  # non-trivial gate bias, conv taps and A
+        p.b_gate.normal_(0.0, 0.3)
+        p.A.normal_(0.0, 0.3)
+    gen = torch.Generator(device="cpu").manual_seed(4)
+    x = torch.randn(T, d_model, generator=gen).to("cuda", dt).requires_grad_(True)
+    dout = torch.randn(T, d_model, generator=gen).to("cuda", dt)
+    out = layer.kda_layer(p, x, H=H, cu_seqlens=cu, gate_kind=kind)
+    out.backward(dout)
+    P = {f: getattr(p, f).detach().double().cpu().numpy() for f in
+         ("W_q", "W_k", "W_v", "W_g", "W_beta", "W_a_down", "W_a_up", "b_gate", "A", "conv_q", "conv_k", "conv_v",
+          "W_o")}
+    xk = {"softplus": M.GATE_SOFTPLUS, "sigmoid_min": M.GATE_SIGMOID_MIN}[kind]
+    ref, cache = M.layer_fwd(P, x.detach().double().cpu().numpy(), H, cu, kind=xk)
+    g = M.layer_bwd(P, cache, dout.double().cpu().numpy())
+    tol = 1e-3 if dt == torch.float32 else 5e-2
+    assert scale_rel_err(out.detach().double().cpu().numpy(), ref) <= tol
+    assert scale_rel_err(x.grad.double().cpu().numpy(), g["x"]) <= tol
+    for name in P:
+        got = getattr(p, name).grad
+        assert got is not None, name
+        assert scale_rel_err(got.double().cpu().numpy(), g[name]) <= tol, name

@@ -183,3 +183,41 @@ def test_gated_rmsnorm_bwd_matches_finite_differences():
                 lambda a: np.sum(M.gated_rmsnorm(o, a) * dy))
             fd = (f(p) - f(m)) / (2 * eps)
             assert abs(fd - grad[idx]) < 1e-7 * max(1.0, abs(fd))
+
+
+def _layer_case(seed):
+    rng = np.random.default_rng(seed)
+    d, H, dk, dv, r, K, T = 12, 2, 8, 4, 3, 4, 11
+    P = dict(W_q=rng.standard_normal((d, H * dk)) * 0.3, W_k=rng.standard_normal((d, H * dk)) * 0.3,
+             W_v=rng.standard_normal((d, H * dv)) * 0.3, W_g=rng.standard_normal((d, H * dv)) * 0.3,
+             W_beta=rng.standard_normal((d, H)) * 0.3, W_a_down=rng.standard_normal((d, r)) * 0.3,
+             W_a_up=rng.standard_normal((r, H * dk)) * 0.3, b_gate=rng.standard_normal(H * dk) * 0.2,
+             A=rng.standard_normal(H) * 0.2, conv_q=rng.standard_normal((K, H * dk)) * 0.4,
+             conv_k=rng.standard_normal((K, H * dk)) * 0.4, conv_v=rng.standard_normal((K, H * dv)) * 0.4,
+             W_o=rng.standard_normal((H * dv, d)) * 0.3)
+    return P, rng.standard_normal((T, d)), rng.standard_normal((T, d)), H
+
+
+@pytest.mark.parametrize("cu,kind", [([0, 4, 4, 11], M.GATE_SOFTPLUS), (None, M.GATE_SIGMOID_MIN)])
+def test_layer_bwd_matches_finite_differences(cu, kind):
+    P, x, dout, H = _layer_case(0)
+    out, cache = M.layer_fwd(P, x, H, cu, kind=kind, chunk=4)
+    g = M.layer_bwd(P, cache, dout)
+
+    def loss(P2, x2):
+        return float(np.sum(M.layer_fwd(P2, x2, H, cu, kind=kind, chunk=4)[0] * dout))
+
+    rng = np.random.default_rng(1)
+    eps = 1e-6
+    for name in list(P) + ["x"]:
+        arr = x if name == "x" else P[name]
+        for _ in range(2):
+            idx = tuple(int(rng.integers(0, n)) for n in arr.shape)
+            p, m = arr.copy(), arr.copy()
+            p[idx] += eps
+            m[idx] -= eps
+            if name == "x":
+                fd = (loss(P, p) - loss(P, m)) / (2 * eps)
+            else:
+                fd = (loss({**P, name: p}, x) - loss({**P, name: m}, x)) / (2 * eps)
+            assert abs(fd - g[name][idx]) < 1e-6 * max(1.0, abs(fd)), (name, idx)
