@@ -1,13 +1,18 @@
-"""B200-native (sm_100a) Kimi Delta Attention core: chunked forward, fused
-backward and recurrent decode, behind the C ABI in ``include/kda_b200.h``."""
+"""B200-native (sm_100a) Kimi Delta Attention: chunked forward, fused backward
+and recurrent decode behind the C ABI in ``include/kda_b200.h``, and the
+per-token work around them (prologue, output gate, fused decode step, packed
+sequences) behind ``include/kda_mixer.h``; ``layer`` wires a whole mixer
+layer."""
 
+from . import layer, mixer  # noqa: F401
 from .kda import (  # noqa: F401
-    CHUNK, KDA_CC_IMPLS, TILE, cc_scan, chunk_kda, ckpt_states, decode_step, device_available,
-    kda_bwd, kda_cc_impl, kda_fwd, kernel, kernel_bwd,
+    CHUNK, KDA_CC_IMPLS, TILE, cc_scan, chunk_kda, chunk_kda_varlen, ckpt_states, decode_step,
+    device_available, kda_bwd, kda_bwd_varlen, kda_cc_impl, kda_fwd, kda_fwd_varlen, kernel, kernel_bwd,
+    packing,
 )
 
 __all__ = [
-    "CHUNK", "TILE", "KDA_CC_IMPLS", "cc_scan", "chunk_kda", "ckpt_states", "decode_step",
-    "device_available",
-    "kda_bwd", "kda_cc_impl", "kda_fwd", "kernel", "kernel_bwd",
+    "CHUNK", "TILE", "KDA_CC_IMPLS", "cc_scan", "chunk_kda", "chunk_kda_varlen", "ckpt_states",
+    "decode_step", "device_available", "kda_bwd", "kda_bwd_varlen", "kda_cc_impl", "kda_fwd",
+    "kda_fwd_varlen", "kernel", "kernel_bwd", "layer", "mixer", "packing",
 ]
