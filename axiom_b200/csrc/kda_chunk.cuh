@@ -94,30 +94,104 @@ __device__ __forceinline__ void scores_epilogue(uint32_t t_scores, float* Aq, fl
   }
 }
 
-// Exact scores on the CUDA cores (strong-decay chunks): Aqk and Akk with the
-// direct ratio exp(min(G_c - G_i, 0)).  Gf is G as fp32 [64][128].
-__device__ __forceinline__ void scores_exact(const unsigned char* sq, const unsigned char* sk,
-                                             const float* Gf, float* Aq, float* Akk) {
-  for (int idx = threadIdx.x; idx < C * C; idx += NT) {
+// Exact scores for chunks whose summed decay is beyond the single anchor's
+// budget: Aq[r][i] = sum_d q_r k_i exp(G_r - G_i) (i <= r) and Akk likewise
+// with k_r (i < r), from G (fp32 [64][128], row-major).  With blocks of 16
+// tokens, for row r of block I and column i of block J < I
+//   exp(G_r - G_i) = a_r * m_IJ * b_i,   a_r = exp(G_r - G_{16I}),
+//   m_IJ = exp(G_{16I} - G_{16J+15}),   b_i = exp(G_{16J+15} - G_i),
+// and each factor is <= 1 (G is non-increasing), so nothing overflows and the
+// O(C^2 dk) part needs no exponentials; pairs inside one block take exact
+// exponentials.  q (sq) and k (sk) are overwritten with q a and k b (bf16 CM),
+// k a goes to `ka` (CM [64][128]) and m to `m` (fp32 [6][128]).
+__device__ __forceinline__ void scores_exact(unsigned char* sq, unsigned char* sk, unsigned char* ka,
+                                             float* m, const float* Gf, float* Aq, float* Akk) {
+  const int tid = threadIdx.x;
+  // zeros above the diagonal
+  for (int idx = tid; idx < C * C; idx += NT) {
     const int r = idx >> 6, i = idx & 63;
+    if (i > r) {
+      Aq[sw64(r, i)] = 0.f;
+      Akk[sw64(r, i)] = 0.f;
+    }
+  }
+  // (1) pairs inside a 16-token block: exact exponentials on the raw q, k
+  for (int p = tid; p < 4 * 136; p += NT) {
+    const int blk = p / 136, t = p % 136;
+    int rr = static_cast<int>((sqrtf(8.f * t + 1.f) - 1.f) * 0.5f);
+    if ((rr + 1) * (rr + 2) / 2 <= t) ++rr;
+    if (rr * (rr + 1) / 2 > t) --rr;
+    const int ii = t - rr * (rr + 1) / 2;
+    const int r = 16 * blk + rr, i = 16 * blk + ii;
     float a = 0.f, l = 0.f;
-    if (i <= r) {
-      for (int d8 = 0; d8 < DK; d8 += 8) {
-        float qr[8], kr[8], ki8[8];
-        unpack_bf16x8(ld16(sq, cm_off(r, d8, DK)), qr);
-        unpack_bf16x8(ld16(sk, cm_off(r, d8, DK)), kr);
-        unpack_bf16x8(ld16(sk, cm_off(i, d8, DK)), ki8);
+    for (int d8 = 0; d8 < DK; d8 += 8) {
+      float qr[8], kr[8], ki8[8];
+      unpack_bf16x8(ld16(sq, cm_off(r, d8, DK)), qr);
+      unpack_bf16x8(ld16(sk, cm_off(r, d8, DK)), kr);
+      unpack_bf16x8(ld16(sk, cm_off(i, d8, DK)), ki8);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float ex = __expf(fminf(Gf[r * DK + d8 + e] - Gf[i * DK + d8 + e], 0.f));
-          a += qr[e] * ki8[e] * ex;
-          l += kr[e] * ki8[e] * ex;
-        }
+      for (int e = 0; e < 8; ++e) {
+        const float ex = __expf(fminf(Gf[r * DK + d8 + e] - Gf[i * DK + d8 + e], 0.f));
+        a += qr[e] * ki8[e] * ex;
+        l += kr[e] * ki8[e] * ex;
       }
     }
     Aq[sw64(r, i)] = a;
     Akk[sw64(r, i)] = (i < r) ? l : 0.f;
   }
+  __syncthreads();  // the raw q, k are read: replace them with the factored rows
+  // (2) a_t, b_t per (token, channel): q a -> sq, k a -> ka, k b -> sk; m per block pair
+  for (int idx = tid; idx < C * (DK / 8); idx += NT) {
+    const int t = idx >> 4, d8 = (idx & 15) * 8, I = t >> 4;
+    const uint32_t off = cm_off(t, d8, DK);
+    float qv[8], kv[8], qa[8], kav[8], kb[8];
+    unpack_bf16x8(ld16(sq, off), qv);
+    unpack_bf16x8(ld16(sk, off), kv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float g = Gf[t * DK + d8 + e];
+      const float av = __expf(fminf(g - Gf[16 * I * DK + d8 + e], 0.f));
+      const float bv = __expf(fminf(Gf[(16 * I + 15) * DK + d8 + e] - g, 0.f));
+      qa[e] = qv[e] * av;
+      kav[e] = kv[e] * av;
+      kb[e] = kv[e] * bv;
+    }
+    st16(sq, off, pack_bf16x8(qa));
+    st16(ka, off, pack_bf16x8(kav));
+    st16(sk, off, pack_bf16x8(kb));
+  }
+  for (int idx = tid; idx < 6 * DK; idx += NT) {
+    const int p = idx / DK, d = idx % DK;
+    const int I = p < 3 ? p + 1 : (p < 5 ? p - 1 : 3), J = p < 3 ? 0 : (p < 5 ? 1 : 2);
+    m[idx] = __expf(fminf(Gf[16 * I * DK + d] - Gf[(16 * J + 15) * DK + d], 0.f));
+  }
+  __syncthreads();
+  // (3) block pairs I > J: (1,0) (2,0) (3,0) (2,1) (3,1) (3,2), multiply-adds only
+  for (int idx = tid; idx < 6 * 256; idx += NT) {
+    const int p = idx >> 8, w = idx & 255;
+    const int I = p < 3 ? p + 1 : (p < 5 ? p - 1 : 3), J = p < 3 ? 0 : (p < 5 ? 1 : 2);
+    const int r = 16 * I + (w >> 4), i = 16 * J + (w & 15);
+    const float* mp = m + p * DK;
+    float a = 0.f, l = 0.f;
+    for (int d8 = 0; d8 < DK; d8 += 8) {
+      float qa[8], kav[8], kb[8];
+      unpack_bf16x8(ld16(sq, cm_off(r, d8, DK)), qa);
+      unpack_bf16x8(ld16(ka, cm_off(r, d8, DK)), kav);
+      unpack_bf16x8(ld16(sk, cm_off(i, d8, DK)), kb);
+      const float4 m0 = *reinterpret_cast<const float4*>(mp + d8);
+      const float4 m1 = *reinterpret_cast<const float4*>(mp + d8 + 4);
+      const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float kbm = kb[e] * mv[e];
+        a += qa[e] * kbm;
+        l += kav[e] * kbm;
+      }
+    }
+    Aq[sw64(r, i)] = a;
+    Akk[sw64(r, i)] = l;
+  }
+  fence_async_smem();  // sq, sk, ka are the next chunk's TMA destinations
 }
 
 

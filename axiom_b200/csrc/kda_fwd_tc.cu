@@ -334,7 +334,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         fence_async_smem();
         __syncthreads();
         if (tid == kIoThread) store_prep(true);
-        scores_exact(sm + OFF_SQ, sm + OFF_SK, Gf, Aq, Akk);
+        scores_exact(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, reinterpret_cast<float*>(sm + OFF_VT), Gf, Aq, Akk);
         __syncthreads();
         if (c + 1 < c_end) {
           stage(c + 1, true);

@@ -151,9 +151,15 @@ def cc_scores(row, col, G, tile=TILE, strict=False):
     column exponent is clamped at ``COL_EXP_BUDGET`` as the persistent kernel
     does (``net/kernels/kda_cc_fused_persist.py:482``; inert in-tile).
     Shapes ``[..., C, D]`` -> ``[..., C, C]``; mask keeps ``c >= i``
-    (``strict``: ``c > i``).
+    (``strict``: ``c > i``).  ``tile=None`` takes the direct ratio instead,
+    exact for any decay (the reference's anchor and clamp lose accuracy once a
+    tile's summed decay passes the budget).
     """
     C = row.shape[-2]
+    if tile is None:  # the direct ratio, exact for any decay (no anchor, no clamp)
+        E = np.exp(np.minimum(G[..., :, None, :] - G[..., None, :, :], 0.0))
+        mask = np.tril(np.ones((C, C), row.dtype), -1 if strict else 0)
+        return mask * np.einsum("...cid,...cd,...id->...ci", E, row, col)
     out = np.zeros(row.shape[:-1] + (C,), row.dtype)
     for p in range(0, C, tile):
         b = min(tile, C - p)
@@ -319,12 +325,13 @@ def _chunk_backward(qc, kc, vc, gc, bc, S, do, dSn):
     return dq, dk, dv, dla, db, dS
 
 
-def chunk_bwd(q, k, v, g, beta, S0, do, dST=None, chunk=64, dtype=np.float64):
+def chunk_bwd(q, k, v, g, beta, S0, do, dST=None, chunk=64, dtype=np.float64, tile=TILE):
     """Reverse chunk scan of the adjoint; returns ``(dq, dk, dv, dg, dbeta, dS0)``.
 
     ``reference_bwd_scan`` (``net/kernels/kda_cc_fused_persist.py:794-849``):
-    a forward pass recomputes the incoming state of every chunk, then the
-    chunks are walked in reverse carrying the state cotangent.
+    a forward pass recomputes the incoming state of every chunk (``tile`` as in
+    :func:`chunk_fwd`), then the chunks are walked in reverse carrying the state
+    cotangent.
     """
     B, T, H, dk = q.shape
     dv = v.shape[-1]
@@ -343,7 +350,7 @@ def chunk_bwd(q, k, v, g, beta, S0, do, dST=None, chunk=64, dtype=np.float64):
         sl = slice(c * C, (c + 1) * C)
         s_ins.append(S)
         S = _chunk_forward_parts(Q[:, :, sl], K[:, :, sl], V[:, :, sl],
-                                 Gl[:, :, sl], Bt[:, :, sl], S)["S_new"]
+                                 Gl[:, :, sl], Bt[:, :, sl], S, tile)["S_new"]
     dS = np.zeros((B, H, dk, dv), dtype) if dST is None else np.asarray(dST, dtype)
     dQ, dK, dV, dGl = (np.zeros_like(a) for a in (Q, K, V, Gl))
     dB = np.zeros_like(Bt)

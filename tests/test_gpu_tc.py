@@ -126,3 +126,33 @@ def test_tc_forward_checkpoint_feeds_the_exact_backward():
     for name, ge, gt, rf in zip(GRADS, exact, tc, ref):
         assert K.scale_rel_err(_np(ge), rf) <= TOL, name
         assert K.scale_rel_err(_np(gt), rf) <= TOL, name
+
+
+def test_tc_extreme_decay_is_exact():
+    """Per-token decay up to 11 (BASELINE's mixer gate with b = 0): every chunk
+    takes the exact score path.  The reference's tile-anchored chunk algorithm
+    loses accuracy here (its column clamp binds inside a tile), so the forward is
+    checked against the direct-ratio oracle and the token recurrence, the
+    backward against the direct-ratio adjoint."""
+    from axiom_b200 import chunk_kda
+
+    B, T, H = 1, 200, 2
+    x = K.make_inputs(B, T, H, 128, 128, seed=31, s0_std=0.05, decay="strong")
+    x["g"] = x["g"] * 2.2
+    xr = {k: (K.bf16_round(v) if k != "S0" else v) for k, v in x.items()}
+    d = {k: _dev(v, torch.bfloat16 if k != "S0" else torch.float32) for k, v in xr.items()}
+    rng = np.random.default_rng(32)
+    do = K.bf16_round(rng.standard_normal((B, T, H, 128)))
+    dST = rng.standard_normal((B, H, 128, 128)).astype(np.float32)
+    leaves = {n: d[n].clone().requires_grad_() for n in ("q", "k", "v", "g", "beta", "S0")}
+    o, s_t = chunk_kda(*(leaves[n] for n in ("q", "k", "v", "g", "beta", "S0")))
+    o_rec, s_rec = K.recurrent(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"])
+    o_ex, s_ex = K.chunk_fwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], chunk=64, tile=None)
+    assert K.scale_rel_err(o_ex, o_rec) <= 1e-10
+    assert K.scale_rel_err(_np(o), o_rec) <= TOL
+    assert K.scale_rel_err(_np(s_t), s_rec) <= TOL
+    (o.float() * _dev(do, torch.float32)).sum().backward(retain_graph=True)
+    (s_t * _dev(dST, torch.float32)).sum().backward()
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64, tile=None)
+    for name, leaf, rf in zip(GRADS, ("q", "k", "v", "g", "beta", "S0"), ref):
+        assert K.scale_rel_err(_np(leaves[leaf].grad), rf) <= TOL, name
