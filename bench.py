@@ -300,7 +300,7 @@ def run_b200(args):
     e2e_value = None if args.no_e2e else tokens_per_step / (e2e["ms"] / 1e3)
 
     extra = {}
-    if rank == 0 and not args.no_extra:
+    if rank == 0 and world == 1 and not args.no_extra:  # single-GPU measurements
         extra["decode"] = run_decode(torch, KD, dev, peaks)
         extra["prefill"] = run_prefill(torch, KD, dev, peaks)
         extra["mixer_kernels"] = run_mixer_kernels(torch, dev, peaks)
