@@ -898,18 +898,23 @@ struct DecArgs {
   int gate_kind;
   float rms_eps;
   void* out;
+  int* err;
   int H, K;
 };
 
 constexpr int kDecThreads = 256;
 
-// One CTA per (sequence, head).  The state read is issued first; meanwhile
-// threads [0, DK) form q, k, g of channel d and threads [DK, DK + DV) v of
-// channel d - DK from the projections and the conv buffer (shifted in place,
-// each thread its own channel); then the delta-rule update of the decode step
-// (r = (alpha k)^T S, S' = alpha S + beta k (v - r)^T, o = S'^T q).
+// One CTA per (sequence, head).  The state (DK x DV fp32) comes into shared
+// memory with one bulk copy issued first, so it is in flight without holding
+// registers (three CTAs per SM); meanwhile threads [0, DK) form q, k, g of
+// channel d and threads [DK, DK + DV) v of channel d - DK from the projections
+// and the conv buffer (shifted in place, each thread its own channel); then
+// the delta-rule update of the decode step (r = (alpha k)^T S,
+// S' = alpha S + beta k (v - r)^T, o = S'^T q) reads the rows from shared
+// memory and writes S' to HBM.  The copy's wait is bounded: on a timeout the
+// CTA raises `err`, waits (bounded) once more and returns.
 template <int DK, int DV, typename Tin, typename To>
-__global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecArgs a) {
+__global__ void __launch_bounds__(kDecThreads, 3) decode_fused_kernel(const DecArgs a) {
   static_assert(DK + DV <= kDecThreads, "one thread per q/k/g and per v channel");
   constexpr int TPR = DV / 4;
   constexpr int RPP = kDecThreads / TPR;
@@ -918,13 +923,21 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecA
   __shared__ float s_red[RPP][DV];
   __shared__ float s_nrm[2][8];
   __shared__ float s_beta;
+  __shared__ __align__(8) uint64_t s_mbar;
+  extern __shared__ __align__(128) float s_state[];  // DK x DV
   const int n = blockIdx.x / a.H, h = blockIdx.x % a.H;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int col = (tid % TPR) * 4, row0 = tid / TPR;
   float4* Sn = reinterpret_cast<float4*>(a.S + static_cast<size_t>(blockIdx.x) * DK * DV);
-  float4 s[NR];
-#pragma unroll
-  for (int m = 0; m < NR; ++m) s[m] = Sn[((row0 + m * RPP) * DV + col) / 4];
+  if (tid == 0) {
+    tc::mbar_init(&s_mbar, 1);
+    tc::mbar_fence_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    tc::mbar_expect_tx(&s_mbar, DK * DV * 4);
+    tc::bulk_load(s_state, Sn, DK * DV * 4, &s_mbar);
+  }
 
   // ---- prologue of this token: conv step, Swish, gates ----
   const int HK = a.H * DK, HV = a.H * DV;
@@ -996,11 +1009,18 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecA
   __syncthreads();
 
   // ---- delta-rule update ----
+  if (!__syncthreads_and(tc::mbar_wait(&s_mbar, 0))) {
+    if (tid == 0 && a.err) atomicExch(a.err, 1);
+    tc::mbar_wait(&s_mbar, 0);  // the copy may still land: wait (bounded) before leaving
+    return;
+  }
+  auto srow = [&](int m) { return *reinterpret_cast<const float4*>(&s_state[(row0 + m * RPP) * DV + col]); };
   float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int m = 0; m < NR; ++m) {
     const float w = s_ak[row0 + m * RPP];
-    r.x += w * s[m].x; r.y += w * s[m].y; r.z += w * s[m].z; r.w += w * s[m].w;
+    const float4 sv = srow(m);
+    r.x += w * sv.x; r.y += w * sv.y; r.z += w * sv.z; r.w += w * sv.w;
   }
   *reinterpret_cast<float4*>(&s_red[row0][col]) = r;
   __syncthreads();
@@ -1016,9 +1036,10 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecA
   for (int m = 0; m < NR; ++m) {
     const int d = row0 + m * RPP;
     const float al = s_a[d], bk = s_bk[d], qd = s_q[d];
+    const float4 sv = srow(m);
     float4 t;
-    t.x = al * s[m].x + bk * u.x; t.y = al * s[m].y + bk * u.y;
-    t.z = al * s[m].z + bk * u.z; t.w = al * s[m].w + bk * u.w;
+    t.x = al * sv.x + bk * u.x; t.y = al * sv.y + bk * u.y;
+    t.z = al * sv.z + bk * u.z; t.w = al * sv.w + bk * u.w;
     Sn[(d * DV + col) / 4] = t;
     acc.x += qd * t.x; acc.y += qd * t.y; acc.z += qd * t.z; acc.w += qd * t.w;
   }
@@ -1046,6 +1067,12 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_fused_kernel(const DecA
     for (int j = 0; j < 4; ++j) stf(on + j, o[j]);
   }
 }
+
+}  // namespace
+
+__device__ int g_decode_fused_error = 0;  // set when a state copy's wait timed out
+
+namespace {
 
 template <int CPL, bool VARLEN, typename Tin, typename Tout>
 int launch_prologue_v(ProArgs& a, int roles, int n_roles, bool bwd, cudaStream_t st) {
@@ -1124,15 +1151,23 @@ int grms_types(const void* o, const void* gate, const void* dy, void* y, void* d
   return KDA_ERR_DTYPE;
 }
 
+template <int DK, int DV, typename Tin, typename To>
+int dec_launch(const DecArgs& a, int N, cudaStream_t st) {
+  static bool done[64] = {false};
+  constexpr int smem = DK * DV * 4;
+  const int rc = ensure_smem(decode_fused_kernel<DK, DV, Tin, To>, smem, done);
+  if (rc != KDA_OK) return rc;
+  decode_fused_kernel<DK, DV, Tin, To><<<N * a.H, kDecThreads, smem, st>>>(a);
+  return launch_status();
+}
+
 template <int DK, int DV>
 int dec_types(const DecArgs& a, int N, int in_dt, int o_dt, cudaStream_t st) {
-  const int grid = N * a.H;
-  if (in_dt == KDA_BF16 && o_dt == KDA_BF16) decode_fused_kernel<DK, DV, bf16, bf16><<<grid, kDecThreads, 0, st>>>(a);
-  else if (in_dt == KDA_BF16 && o_dt == KDA_F32) decode_fused_kernel<DK, DV, bf16, float><<<grid, kDecThreads, 0, st>>>(a);
-  else if (in_dt == KDA_F32 && o_dt == KDA_F32) decode_fused_kernel<DK, DV, float, float><<<grid, kDecThreads, 0, st>>>(a);
-  else if (in_dt == KDA_F32 && o_dt == KDA_BF16) decode_fused_kernel<DK, DV, float, bf16><<<grid, kDecThreads, 0, st>>>(a);
-  else return KDA_ERR_DTYPE;
-  return launch_status();
+  if (in_dt == KDA_BF16 && o_dt == KDA_BF16) return dec_launch<DK, DV, bf16, bf16>(a, N, st);
+  if (in_dt == KDA_BF16 && o_dt == KDA_F32) return dec_launch<DK, DV, bf16, float>(a, N, st);
+  if (in_dt == KDA_F32 && o_dt == KDA_F32) return dec_launch<DK, DV, float, float>(a, N, st);
+  if (in_dt == KDA_F32 && o_dt == KDA_BF16) return dec_launch<DK, DV, float, bf16>(a, N, st);
+  return KDA_ERR_DTYPE;
 }
 
 }  // namespace
@@ -1333,6 +1368,8 @@ int kda_decode_fused(float* S, float* conv_buf, const void* qp, const void* kp, 
   a.w[0] = conv_q; a.w[1] = conv_k; a.w[2] = conv_v;
   a.b_gate = b_gate; a.A = A; a.g_min = g_min; a.gate_kind = gate_kind; a.rms_eps = rms_eps;
   a.out = out; a.H = H; a.K = K;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&a.err), kda::g_decode_fused_error) != cudaSuccess)
+    return KDA_ERR_LAUNCH;
   if (dk == 128 && dv == 128) return kda::dec_types<128, 128>(a, N, in_dtype, out_dtype, stream);
   if (dk == 64 && dv == 128) return kda::dec_types<64, 128>(a, N, in_dtype, out_dtype, stream);
   if (dk == 128 && dv == 64) return kda::dec_types<128, 64>(a, N, in_dtype, out_dtype, stream);
