@@ -60,6 +60,32 @@ __device__ __forceinline__ float sigm(float x) {
   else return sigmoidf_(x);
 }
 __device__ __forceinline__ float softplusf_(float x) { return fmaxf(x, 0.f) + log1pf(__expf(-fabsf(x))); }
+// Softplus at the precision its consumer keeps: with FAST (bf16 results)
+// log(1 + e^-|x|) through the fast logarithm; its error (absolute, below
+// e^-|x| ulp-scale) is under bf16's resolution of the result.
+template <bool FAST>
+__device__ __forceinline__ float softp(float x) {
+  if constexpr (FAST) return fmaxf(x, 0.f) + __logf(1.f + __expf(-fabsf(x)));
+  else return softplusf_(x);
+}
+
+// Two fp32 lanes per instruction (sm_100 packed f32x2 arithmetic).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
 
 // CPL (2 or 4) consecutive elements <-> floats, one vector access
 template <int CPL>
@@ -338,13 +364,20 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
       sh[u] = shift;
       ss[u] = 0.f;
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        const float cv = wt[0][c] * xv[c] + wt[1][c] * hw[0][c] + wt[2][c] * hw[1][c] + wt[3][c] * hw[2][c];
-        hw[2][c] = hw[1][c];
-        hw[1][c] = hw[0][c];
-        hw[0][c] = xv[c];
-        s[u][c] = cv * sigm<FAST>(cv);
-        ss[u] += s[u][c] * s[u][c];
+      for (int c = 0; c < CPL; c += 2) {
+        float2 cv = fmul2(make_float2(wt[0][c], wt[0][c + 1]), make_float2(xv[c], xv[c + 1]));
+#pragma unroll
+        for (int j = 0; j < 3; ++j)
+          cv = ffma2(make_float2(wt[j + 1][c], wt[j + 1][c + 1]), make_float2(hw[j][c], hw[j][c + 1]), cv);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          hw[2][c + e] = hw[1][c + e];
+          hw[1][c + e] = hw[0][c + e];
+          hw[0][c + e] = xv[c + e];
+        }
+        s[u][c] = cv.x * sigm<FAST>(cv.x);
+        s[u][c + 1] = cv.y * sigm<FAST>(cv.y);
+        ss[u] += s[u][c] * s[u][c] + s[u][c + 1] * s[u][c + 1];
       }
     }
     if (role < 2) {  // q, k: x / (|x| + eps), the batch's norms in one reduction
@@ -375,7 +408,7 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
 
 template <bool FAST>
 __device__ __forceinline__ float gate_fwd(float u, float ea, float g_min, int kind) {
-  return kind == KDA_GATE_SIGMOID_MIN ? g_min * sigm<FAST>(ea * u) : -ea * softplusf_(u);
+  return kind == KDA_GATE_SIGMOID_MIN ? g_min * sigm<FAST>(ea * u) : -ea * softp<FAST>(u);
 }
 
 template <int CPL, bool VARLEN, typename Tin, typename Tout>
@@ -557,15 +590,29 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
       ld_row<CPL, Tout>(st + kBw * RBX + u * RBY, lane, dv[u]);
       float ss = 0.f, sd = 0.f;
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        float cv = 0.f;
+      for (int c = 0; c < CPL; c += 2) {
+        float2 cv2;
+        if constexpr (VARLEN) {
+          cv2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) cv += !VARLEN || tau - i >= lbu[u] ? wt[i][c] * X[u + i][c] : 0.f;
-        const float sig = sigm<FAST>(cv);
-        s[u][c] = cv * sig;
-        sg[u][c] = sig * (1.f + cv * (1.f - sig));
-        ss += s[u][c] * s[u][c];
-        sd += s[u][c] * dv[u][c];
+          for (int i = 0; i < 4; ++i)
+            if (tau - i >= lbu[u])
+              cv2 = ffma2(make_float2(wt[i][c], wt[i][c + 1]), make_float2(X[u + i][c], X[u + i][c + 1]), cv2);
+        } else {
+          cv2 = fmul2(make_float2(wt[0][c], wt[0][c + 1]), make_float2(X[u][c], X[u][c + 1]));
+#pragma unroll
+          for (int i = 1; i < 4; ++i)
+            cv2 = ffma2(make_float2(wt[i][c], wt[i][c + 1]), make_float2(X[u + i][c], X[u + i][c + 1]), cv2);
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float cv = e ? cv2.y : cv2.x;
+          const float sig = sigm<FAST>(cv);
+          s[u][c + e] = cv * sig;
+          sg[u][c + e] = sig * (1.f + cv * (1.f - sig));
+          ss += s[u][c + e] * s[u][c + e];
+          sd += s[u][c + e] * dv[u][c + e];
+        }
       }
       sums[u] = ss;
       sums[kBw + u] = sd;
@@ -602,21 +649,31 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
       if (tau >= lo && tau < t1) {
         float o[CPL];
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          float acc = wt[0][c] * dc[u][c];
+        for (int c = 0; c < CPL; c += 2) {
+          float2 acc = fmul2(make_float2(wt[0][c], wt[0][c + 1]), make_float2(dc[u][c], dc[u][c + 1]));
 #pragma unroll
           for (int i = 1; i < 4; ++i) {
-            const float d = i <= u ? dc[u - i][c] : dcw[i - u - 1][c];
-            acc += !VARLEN || tau + i < ubu[u] ? wt[i][c] * d : 0.f;
+            const float2 d = i <= u ? make_float2(dc[u - i][c], dc[u - i][c + 1])
+                                    : make_float2(dcw[i - u - 1][c], dcw[i - u - 1][c + 1]);
+            if (!VARLEN || tau + i < ubu[u]) acc = ffma2(make_float2(wt[i][c], wt[i][c + 1]), d, acc);
           }
-          o[c] = acc;
+          o[c] = acc.x;
+          o[c + 1] = acc.y;
         }
         if (tau >= t0) {
           stv<CPL>(dx + static_cast<size_t>(tau) * HD, o);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < 4; ++i) {
+            if (!VARLEN || tau - i >= lbu[u]) {
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) dw[i][c] += !VARLEN || tau - i >= lbu[u] ? dc[u][c] * X[u + i][c] : 0.f;
+              for (int c = 0; c < CPL; c += 2) {
+                const float2 w2 = ffma2(make_float2(dc[u][c], dc[u][c + 1]), make_float2(X[u + i][c], X[u + i][c + 1]),
+                                        make_float2(dw[i][c], dw[i][c + 1]));
+                dw[i][c] = w2.x;
+                dw[i][c + 1] = w2.y;
+              }
+            }
+          }
         } else {  // tau < 0: cotangent of the conv state row
           stv<CPL>(a.dst + (static_cast<size_t>(b) * (K - 1) + tau + K - 1) * sw + state_col(a, role) + ch, o);
         }
@@ -711,7 +768,7 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
             dA += t * uu;
           } else {
             o[c] = -gv[c] * ea * sigm<FAST>(uu);
-            dA -= gv[c] * ea * softplusf_(uu);
+            dA -= gv[c] * ea * softp<FAST>(uu);
           }
           db[c] += o[c];
         }
