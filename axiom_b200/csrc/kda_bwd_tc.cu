@@ -867,17 +867,95 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           }
         }
         __syncthreads();
+        // Score adjoints with 16-token block anchors (every exponent <= 0).  For
+        // token r of block I and i of an earlier block: exp(G_r - G_i) =
+        // exp(G_r - G_16I) exp(G_16I - G_i), so the row sums
+        //   sum_{i<16I} dAqk[r][i] k_i exp(G_r - G_i)   (and beta dL with k)
+        // are exp(G_r - G_16I) times MMAs over kbm_I = k exp(G_16I - G_i); the
+        // column sums over later blocks use qa_J, ka_J = (q, k) exp(G_r - G_e)
+        // with e = 16J + 15 and the factor exp(G_e - G_c).  Pairs inside one
+        // block take exact exponentials below.  Operands: kbm_I (I = 1..3) in
+        // SB, qa_J / ka_J (J = 0..2) in A3 (both free in a slow unit's epilogue);
+        // sums in the free TMEM columns T_SC, T_L, T_DU.
+        unsigned char* kbm = sm + P_SB;
+        unsigned char* qa = A3;
+        unsigned char* ka = A3 + 24576;
+        auto kbm_off = [](int I) { return I == 1 ? 0 : (I == 2 ? 4096 : 12288); };  // 16I rows each
+        auto qa_off = [](int J) { return J == 0 ? 0 : (J == 1 ? 12288 : 20480); };   // 48 - 16J rows each
+        auto t_row = [&](int I) { return I == 1 ? T_SC : (I == 2 ? T_SC + 32 : T_L); };          // [dra | drk]
+        auto t_col = [&](int J) { return J == 0 ? T_L + 32 : (J == 1 ? T_L + 48 : T_DU); };      // dca + dck
+        for (int idx = tid; idx < 96 * 16; idx += NT) {
+          const int pr = idx >> 4, d8 = (idx & 15) * 8;
+          {  // kbm: (I, i) for i < 16 I
+            const int I = pr < 16 ? 1 : (pr < 48 ? 2 : 3);
+            const int i = pr - (I == 1 ? 0 : (I == 2 ? 16 : 48));
+            float kv[8], o[8];
+            unpack_bf16x8(ld16(sm + P_SK, cm_off(i, d8, DK)), kv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              o[e] = kv[e] * __expf(fminf(Gs[16 * I * DK + d8 + e] - Gs[i * DK + d8 + e], 0.f));
+            st16(kbm + kbm_off(I), cm_off(i, d8, DK), pack_bf16x8(o));
+          }
+          {  // qa, ka: (J, r) for r > 16 J + 15
+            const int J = pr < 48 ? 0 : (pr < 80 ? 1 : 2);
+            const int rr = pr - (J == 0 ? 0 : (J == 1 ? 48 : 80));
+            const int r = 16 * (J + 1) + rr;
+            float qv[8], kv[8], oq[8], ok[8];
+            unpack_bf16x8(ld16(sm + P_SQ, cm_off(r, d8, DK)), qv);
+            unpack_bf16x8(ld16(sm + P_SK, cm_off(r, d8, DK)), kv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float f = __expf(fminf(Gs[r * DK + d8 + e] - Gs[(16 * J + 15) * DK + d8 + e], 0.f));
+              oq[e] = qv[e] * f;
+              ok[e] = kv[e] * f;
+            }
+            st16(qa + qa_off(J), cm_off(rr, d8, DK), pack_bf16x8(oq));
+            st16(ka + qa_off(J), cm_off(rr, d8, DK), pack_bf16x8(ok));
+          }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+          tc_fence_after();
+          const uint32_t kl = smem_u32(sm + P_KL), kb0 = smem_u32(kbm), qa0 = smem_u32(qa), ka0 = smem_u32(ka);
+          const uint32_t idr = idesc_bf16(128, 16, true, false), idc = idesc_bf16(128, 16, true, true);
+          for (int I = 1; I <= 3; ++I)
+            for (int ks = 0; ks < I; ++ks) {
+              const uint64_t Ad = desc_mnmajor(kb0 + kbm_off(I) + ks * 4096, DK);
+              mma_bf16(t_row(I), Ad, desc_kmajor(kl + 2048 * I + ks * 256, C), idr, ks > 0);
+              mma_bf16(t_row(I) + 16, Ad, desc_kmajor(kl + 8192 + 2048 * I + ks * 256, C), idr, ks > 0);
+            }
+          for (int J = 0; J <= 2; ++J)
+            for (int Ip = J + 1; Ip <= 3; ++Ip) {
+              const int ks = Ip - J - 1;
+              mma_bf16(t_col(J), desc_mnmajor(qa0 + qa_off(J) + ks * 4096, DK),
+                       desc_mnmajor(kl + 2048 * Ip + 256 * J, C), idc, ks > 0);
+              mma_bf16(t_col(J), desc_mnmajor(ka0 + qa_off(J) + ks * 4096, DK),
+                       desc_mnmajor(kl + 8192 + 2048 * Ip + 256 * J, C), idc, 1u);
+            }
+          mma_commit(mbar);
+        }
+        failed |= !mma_wait();
+        if (__syncthreads_or(failed)) break;
         float run = pre;
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
           const int c16 = cb + 16 * part;
-          float dqg[16], dkg[16], dkl[16], yw[16], yu[16], tb[16];
+          const int I = c16 >> 4;  // this part's 16-token block (warp-uniform)
+          float dqg[16], dkg[16], dkl[16], yw[16], yu[16], tb[16], offr[16], offk[16], offc[16];
           tmem_ld16(T_IV + tl + c16, dqg);
           tmem_ld16(T_IV + 64 + tl + c16, dkg);
           tmem_ld16(T_KL + tl + c16, dkl);
           tmem_ld16(T_UF + tl + c16, yw);
           tmem_ld16(T_UF + 64 + tl + c16, yu);
+          if (I >= 1) {
+            tmem_ld16(t_row(I) + tl, offr);
+            tmem_ld16(t_row(I) + 16 + tl, offk);
+          }
+          if (I <= 2) tmem_ld16(t_col(I) + tl, offc);
           tmem_wait_ld();
+          const float g_s = Gs[16 * I * DK + d], g_e = Gs[(16 * I + 15) * DK + d];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int cc = c16 + i;
@@ -890,21 +968,24 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
             float dkv = dkg[i] * gam + dkl[i] * lam;
             float dGv = dqg[i] * qv * gam + dkg[i] * kv * gam - dkl[i] * kv * lam;
             klsum += dkl[i] * kv * lam;
-            // exact score adjoints (direct decay ratio)
-            float dra = 0.f, drk = 0.f, dca = 0.f, dck = 0.f;
-            for (int i2 = 0; i2 <= cc; ++i2) {
+            // score adjoints: earlier / later blocks from the MMAs, this block exact
+            const float ar = I >= 1 ? __expf(fminf(run - g_s, 0.f)) : 0.f;
+            const float bc = I <= 2 ? __expf(fminf(g_e - run, 0.f)) : 0.f;
+            float dra = I >= 1 ? ar * offr[i] : 0.f, drk = I >= 1 ? ar * offk[i] : 0.f;
+            float dcc = I <= 2 ? bc * offc[i] : 0.f;
+            for (int i2 = 16 * I; i2 <= cc; ++i2) {
               const float ke = ldbf(sm + P_SK, cm_off(i2, d, DK)) * __expf(fminf(run - Gs[i2 * DK + d], 0.f));
               dra += ldbf(sm + P_KL, cm_off(cc, i2, C)) * ke;
               drk += ldbf(sm + P_KL, cm_off(64 + cc, i2, C)) * ke;
             }
-            for (int r2 = cc; r2 < C; ++r2) {
+            for (int r2 = cc; r2 < 16 * I + 16; ++r2) {
               const float e = __expf(fminf(Gs[r2 * DK + d] - run, 0.f));
-              dca += ldbf(sm + P_KL, cm_off(r2, cc, C)) * ldbf(sm + P_SQ, cm_off(r2, d, DK)) * e;
-              dck += ldbf(sm + P_KL, cm_off(64 + r2, cc, C)) * ldbf(sm + P_SK, cm_off(r2, d, DK)) * e;
+              dcc += (ldbf(sm + P_KL, cm_off(r2, cc, C)) * ldbf(sm + P_SQ, cm_off(r2, d, DK)) +
+                      ldbf(sm + P_KL, cm_off(64 + r2, cc, C)) * ldbf(sm + P_SK, cm_off(r2, d, DK))) * e;
             }
             dqv += dra;
-            dkv += drk + dca + dck;
-            dGv += dra * qv + drk * kv - (dca + dck) * kv;
+            dkv += drk + dcc;
+            dGv += dra * qv + drk * kv - dcc * kv;
             dG[16 * part + i] = dGv;
             const float vv = ldbf(sm + P_V, cm_off(cc, d, DV));
             tb[i] = yw[i] * kv * gam + yu[i] * vv;
