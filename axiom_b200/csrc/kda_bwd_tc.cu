@@ -858,15 +858,16 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           pre += (cc < cb) ? x : 0.f;
           gtot += x;
         }
-        float* Gs = reinterpret_cast<float*>(sm + P_TP);  // exact path: G fp32 [64][128]
+        float* Gs = reinterpret_cast<float*>(sm + P_TP);  // exact path: G fp32 [64][128] (gsw layout)
         {
           float run2 = pre;
           for (int jj = 0; jj < 32; ++jj) {
             run2 += ldbf(sgt, cm_off(cb + jj, d, DK));
-            Gs[(cb + jj) * DK + d] = run2;
+            Gs[gsw(cb + jj, d)] = run2;
           }
         }
         __syncthreads();
+        KDA_PT(2, 2);
         // Score adjoints with 16-token block anchors (every exponent <= 0).  For
         // token r of block I and i of an earlier block: exp(G_r - G_i) =
         // exp(G_r - G_16I) exp(G_16I - G_i), so the row sums
@@ -885,27 +886,32 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         auto t_row = [&](int I) { return I == 1 ? T_SC : (I == 2 ? T_SC + 32 : T_L); };          // [dra | drk]
         auto t_col = [&](int J) { return J == 0 ? T_L + 32 : (J == 1 ? T_L + 48 : T_DU); };      // dca + dck
         for (int idx = tid; idx < 96 * 16; idx += NT) {
-          const int pr = idx >> 4, d8 = (idx & 15) * 8;
+          // eight consecutive threads take the eight rows of one core matrix (conflict-free
+          // 16-byte accesses); blocks I, J start on multiples of 8 rows
+          const int pr = ((idx >> 7) << 3) + (idx & 7), d8 = ((idx >> 3) & 15) * 8;
           {  // kbm: (I, i) for i < 16 I
             const int I = pr < 16 ? 1 : (pr < 48 ? 2 : 3);
             const int i = pr - (I == 1 ? 0 : (I == 2 ? 16 : 48));
-            float kv[8], o[8];
+            float kv[8], o[8], ga[8], gb[8];
             unpack_bf16x8(ld16(sm + P_SK, cm_off(i, d8, DK)), kv);
+            ld8g(Gs, 16 * I, d8, ga);
+            ld8g(Gs, i, d8, gb);
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              o[e] = kv[e] * __expf(fminf(Gs[16 * I * DK + d8 + e] - Gs[i * DK + d8 + e], 0.f));
+            for (int e = 0; e < 8; ++e) o[e] = kv[e] * __expf(fminf(ga[e] - gb[e], 0.f));
             st16(kbm + kbm_off(I), cm_off(i, d8, DK), pack_bf16x8(o));
           }
           {  // qa, ka: (J, r) for r > 16 J + 15
             const int J = pr < 48 ? 0 : (pr < 80 ? 1 : 2);
             const int rr = pr - (J == 0 ? 0 : (J == 1 ? 48 : 80));
             const int r = 16 * (J + 1) + rr;
-            float qv[8], kv[8], oq[8], ok[8];
+            float qv[8], kv[8], oq[8], ok[8], ga[8], gb[8];
             unpack_bf16x8(ld16(sm + P_SQ, cm_off(r, d8, DK)), qv);
             unpack_bf16x8(ld16(sm + P_SK, cm_off(r, d8, DK)), kv);
+            ld8g(Gs, r, d8, ga);
+            ld8g(Gs, 16 * J + 15, d8, gb);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float f = __expf(fminf(Gs[r * DK + d8 + e] - Gs[(16 * J + 15) * DK + d8 + e], 0.f));
+              const float f = __expf(fminf(ga[e] - gb[e], 0.f));
               oq[e] = qv[e] * f;
               ok[e] = kv[e] * f;
             }
@@ -916,6 +922,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
+        KDA_PT(2, 3);
         if (tid == 0) {
           tc_fence_after();
           const uint32_t kl = smem_u32(sm + P_KL), kb0 = smem_u32(kbm), qa0 = smem_u32(qa), ka0 = smem_u32(ka);
@@ -938,24 +945,73 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         }
         failed |= !mma_wait();
         if (__syncthreads_or(failed)) break;
+        KDA_PT(2, 4);
+        float* dGs = reinterpret_cast<float*>(sm + P_SB);  // dG fp32 [64][128] (kbm is dead now)
         float run = pre;
-#pragma unroll
+#pragma unroll 1
         for (int part = 0; part < 2; ++part) {
           const int c16 = cb + 16 * part;
           const int I = c16 >> 4;  // this part's 16-token block (warp-uniform)
-          float dqg[16], dkg[16], dkl[16], yw[16], yu[16], tb[16], offr[16], offk[16], offc[16];
+          // score adjoints of this block's tokens: dra / drk (row sums with k over
+          // earlier tokens) and dcc (column sums with q, k over later tokens)
+          float dra[16], drk[16], dcc[16];
+          {  // earlier / later blocks: the MMA sums times their anchor factors
+            float offr[16], offk[16], offc[16];
+            if (I >= 1) {
+              tmem_ld16(t_row(I) + tl, offr);
+              tmem_ld16(t_row(I) + 16 + tl, offk);
+            }
+            if (I <= 2) tmem_ld16(t_col(I) + tl, offc);
+            tmem_wait_ld();
+            const float g_s = Gs[gsw(c16, d)], g_e = Gs[gsw(c16 + 15, d)];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float gi = Gs[gsw(c16 + i, d)];
+              const float ar = __expf(fminf(gi - g_s, 0.f)), bc = __expf(fminf(g_e - gi, 0.f));
+              dra[i] = I >= 1 ? ar * offr[i] : 0.f;
+              drk[i] = I >= 1 ? ar * offk[i] : 0.f;
+              dcc[i] = I <= 2 ? bc * offc[i] : 0.f;
+            }
+          }
+          {  // pairs inside the block (r >= i): exp(G_r - G_i) is the running product of
+             // the per-token decays exp(g_t), t = i+1 .. r (each <= 1), shared by row r's
+             // sums and column i's sum
+            float kd[16], ad[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              kd[j] = ldbf(sm + P_SK, cm_off(c16 + j, d, DK));
+              ad[j] = __expf(ldbf(sgt, cm_off(c16 + j, d, DK)));
+            }
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+              float kla[16], klb[16];  // dAqk[r][16I + i], (beta dL)[r][16I + i]
+              unpack_bf16x8(ld16(sm + P_KL, cm_off(c16 + r, c16, C)), kla);
+              unpack_bf16x8(ld16(sm + P_KL, cm_off(64 + c16 + r, c16, C)), klb);
+              if (r >= 8) {
+                unpack_bf16x8(ld16(sm + P_KL, cm_off(c16 + r, c16 + 8, C)), kla + 8);
+                unpack_bf16x8(ld16(sm + P_KL, cm_off(64 + c16 + r, c16 + 8, C)), klb + 8);
+              }
+              const float qr = ldbf(sm + P_SQ, cm_off(c16 + r, d, DK)), kr = kd[r];
+              float sa = 0.f, sk = 0.f, e = 1.f;
+#pragma unroll
+              for (int i = r; i >= 0; --i) {
+                if (i < r) e *= ad[i + 1];
+                const float ke = kd[i] * e;
+                sa = fmaf(kla[i], ke, sa);
+                sk = fmaf(klb[i], ke, sk);
+                dcc[i] = fmaf(fmaf(kla[i], qr, klb[i] * kr), e, dcc[i]);
+              }
+              dra[r] += sa;
+              drk[r] += sk;
+            }
+          }
+          float dqg[16], dkg[16], dkl[16], yw[16], yu[16], tb[16];
           tmem_ld16(T_IV + tl + c16, dqg);
           tmem_ld16(T_IV + 64 + tl + c16, dkg);
           tmem_ld16(T_KL + tl + c16, dkl);
           tmem_ld16(T_UF + tl + c16, yw);
           tmem_ld16(T_UF + 64 + tl + c16, yu);
-          if (I >= 1) {
-            tmem_ld16(t_row(I) + tl, offr);
-            tmem_ld16(t_row(I) + 16 + tl, offk);
-          }
-          if (I <= 2) tmem_ld16(t_col(I) + tl, offc);
           tmem_wait_ld();
-          const float g_s = Gs[16 * I * DK + d], g_e = Gs[(16 * I + 15) * DK + d];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int cc = c16 + i;
@@ -964,29 +1020,11 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
             const float qv = ldbf(sm + P_SQ, cm_off(cc, d, DK));
             const float kv = ldbf(sm + P_SK, cm_off(cc, d, DK));
             const float lam = __expf(fminf(gtot - run, 0.f));
-            float dqv = dqg[i] * gam;
-            float dkv = dkg[i] * gam + dkl[i] * lam;
-            float dGv = dqg[i] * qv * gam + dkg[i] * kv * gam - dkl[i] * kv * lam;
+            const float dqv = dqg[i] * gam + dra[i];
+            const float dkv = dkg[i] * gam + dkl[i] * lam + drk[i] + dcc[i];
+            dGs[cc * DK + d] = dqg[i] * qv * gam + dkg[i] * kv * gam - dkl[i] * kv * lam + dra[i] * qv +
+                               drk[i] * kv - dcc[i] * kv;
             klsum += dkl[i] * kv * lam;
-            // score adjoints: earlier / later blocks from the MMAs, this block exact
-            const float ar = I >= 1 ? __expf(fminf(run - g_s, 0.f)) : 0.f;
-            const float bc = I <= 2 ? __expf(fminf(g_e - run, 0.f)) : 0.f;
-            float dra = I >= 1 ? ar * offr[i] : 0.f, drk = I >= 1 ? ar * offk[i] : 0.f;
-            float dcc = I <= 2 ? bc * offc[i] : 0.f;
-            for (int i2 = 16 * I; i2 <= cc; ++i2) {
-              const float ke = ldbf(sm + P_SK, cm_off(i2, d, DK)) * __expf(fminf(run - Gs[i2 * DK + d], 0.f));
-              dra += ldbf(sm + P_KL, cm_off(cc, i2, C)) * ke;
-              drk += ldbf(sm + P_KL, cm_off(64 + cc, i2, C)) * ke;
-            }
-            for (int r2 = cc; r2 < 16 * I + 16; ++r2) {
-              const float e = __expf(fminf(Gs[r2 * DK + d] - run, 0.f));
-              dcc += (ldbf(sm + P_KL, cm_off(r2, cc, C)) * ldbf(sm + P_SQ, cm_off(r2, d, DK)) +
-                      ldbf(sm + P_KL, cm_off(64 + r2, cc, C)) * ldbf(sm + P_SK, cm_off(r2, d, DK))) * e;
-            }
-            dqv += dra;
-            dkv += drk + dcc;
-            dGv += dra * qv + drk * kv - dcc * kv;
-            dG[16 * part + i] = dGv;
             const float vv = ldbf(sm + P_V, cm_off(cc, d, DV));
             tb[i] = yw[i] * kv * gam + yu[i] * vv;
             if (cc < rows_valid) {
@@ -998,6 +1036,8 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           const float sb = warp_colsum<16>(tb, lane);
           if (lane < 16) atomicAdd(&dbs[c16 + lane], sb);
         }
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) dG[jj] = dGs[(cb + jj) * DK + d];
       }
       float gsum = 0.f;
 #pragma unroll

@@ -94,104 +94,181 @@ __device__ __forceinline__ void scores_epilogue(uint32_t t_scores, float* Aq, fl
   }
 }
 
+// G fp32 [64][128] of the exact path: the 16-byte chunks of row r are
+// XOR-swizzled by (r & 7), so eight rows' same chunk lie in distinct banks.
+__device__ __forceinline__ int gsw(int r, int d) {
+  return r * DK + ((((d >> 2) ^ r) & 7) | ((d >> 2) & ~7)) * 4 + (d & 3);
+}
+__device__ __forceinline__ void ld8g(const float* G, int r, int d8, float* o) {  // G[r][d8 .. d8 + 8)
+  const float4 x = *reinterpret_cast<const float4*>(G + gsw(r, d8));
+  const float4 y = *reinterpret_cast<const float4*>(G + gsw(r, d8 + 4));
+  o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w; o[4] = y.x; o[5] = y.y; o[6] = y.z; o[7] = y.w;
+}
+
+// One row r of a diagonal block for the exact scores (two channels per lane):
+// v[VQ + i] = sum_c q_r k_i exp(G_r - G_i), v[VK + i] = the same with k_r (i < r),
+// exp(G_r - G_i) as the running product of the decays a_t = exp(g_t).
+template <int R, int VQ, int VK>
+__device__ __forceinline__ void exact_diag_row(const float (&q0)[16], const float (&q1)[16], const float (&k0)[16],
+                                               const float (&k1)[16], const float (&a0)[16], const float (&a1)[16],
+                                               float (&v)[32]) {
+  float e0 = 1.f, e1 = 1.f;
+#pragma unroll
+  for (int i = R; i >= 0; --i) {
+    if (i < R) {
+      e0 *= a0[i + 1];
+      e1 *= a1[i + 1];
+    }
+    const float x0 = k0[i] * e0, x1 = k1[i] * e1;
+    v[VQ + i] = fmaf(q0[R], x0, q1[R] * x1);
+    if (i < R) v[VK + i] = fmaf(k0[R], x0, k1[R] * x1);
+  }
+}
+
+// Rows RP and 15 - RP of diagonal block `blk`: 17 Aq and 15 Akk sums, 32 in
+// all, which one batched warp reduction spreads one per lane; each lane adds
+// its sum (this warp's 64 channels) into Aq / Akk.
+template <int RP>
+__device__ __forceinline__ void exact_diag_pair(const float (&q0)[16], const float (&q1)[16], const float (&k0)[16],
+                                                const float (&k1)[16], const float (&a0)[16], const float (&a1)[16],
+                                                int lane, int blk, float* Aq, float* Akk) {
+  float v[32];
+  exact_diag_row<RP, 0, 17>(q0, q1, k0, k1, a0, a1, v);
+  exact_diag_row<15 - RP, RP + 1, 17 + RP>(q0, q1, k0, k1, a0, a1, v);
+  const float sum = warp_colsum<32>(v, lane);  // lane j: entry j
+  int r, i;
+  float* dst;
+  if (lane <= RP) {
+    dst = Aq; r = RP; i = lane;
+  } else if (lane < 17) {
+    dst = Aq; r = 15 - RP; i = lane - RP - 1;
+  } else if (lane < 17 + RP) {
+    dst = Akk; r = RP; i = lane - 17;
+  } else {
+    dst = Akk; r = 15 - RP; i = lane - 17 - RP;
+  }
+  atomicAdd(dst + sw64(16 * blk + r, 16 * blk + i), sum);
+}
+
 // Exact scores for chunks whose summed decay is beyond the single anchor's
 // budget: Aq[r][i] = sum_d q_r k_i exp(G_r - G_i) (i <= r) and Akk likewise
-// with k_r (i < r), from G (fp32 [64][128], row-major).  With blocks of 16
-// tokens, for row r of block I and column i of block J < I
-//   exp(G_r - G_i) = a_r * m_IJ * b_i,   a_r = exp(G_r - G_{16I}),
-//   m_IJ = exp(G_{16I} - G_{16J+15}),   b_i = exp(G_{16J+15} - G_i),
-// and each factor is <= 1 (G is non-increasing), so nothing overflows and the
-// O(C^2 dk) part needs no exponentials; pairs inside one block take exact
-// exponentials.  q (sq) and k (sk) are overwritten with q a and k b (bf16 CM),
-// k a goes to `ka` (CM [64][128]) and m to `m` (fp32 [6][128]).
-__device__ __forceinline__ void scores_exact(unsigned char* sq, unsigned char* sk, unsigned char* ka,
-                                             float* m, const float* Gf, float* Aq, float* Akk) {
-  const int tid = threadIdx.x;
-  // zeros above the diagonal
+// with k_r (i < r).  With blocks of 16 tokens, for row r of block I and column
+// i of block J < I
+//   exp(G_r - G_i) = exp(G_r - G_{16I}) * exp(G_{16I} - G_i),
+// both factors <= 1 (G is non-increasing), so the block pairs are tensor-core
+// products [q a ; k a] kbm_I^T with a_r = exp(G_r - G_{16I}) and
+// kbm_I[i] = k_i exp(G_{16I} - G_i) (i < 16 I), N = 16 I.  This part, on the
+// CUDA cores, fills the pairs inside each block (exact, fp32) and writes those
+// operands: q a -> sq, k a -> sk (in place, so [sq ; sk] is the 128-row A
+// operand) and kbm_1..3 (bf16 CM [16 I][128]).  Inputs: raw q, k, g (sq, sk,
+// sg; bf16 CM [64][128]) and G (fp32, gsw layout).
+__device__ __forceinline__ void scores_exact_prep(unsigned char* sq, unsigned char* sk, const unsigned char* sg,
+                                                  unsigned char* kbm1, unsigned char* kbm2, unsigned char* kbm3,
+                                                  const float* Gf, float* Aq, float* Akk) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // zeros above the diagonal and in the diagonal blocks (accumulated below)
   for (int idx = tid; idx < C * C; idx += NT) {
     const int r = idx >> 6, i = idx & 63;
-    if (i > r) {
+    if (i > r || (i >> 4) == (r >> 4)) {
       Aq[sw64(r, i)] = 0.f;
       Akk[sw64(r, i)] = 0.f;
     }
   }
-  // (1) pairs inside a 16-token block: exact exponentials on the raw q, k
-  for (int p = tid; p < 4 * 136; p += NT) {
-    const int blk = p / 136, t = p % 136;
-    int rr = static_cast<int>((sqrtf(8.f * t + 1.f) - 1.f) * 0.5f);
-    if ((rr + 1) * (rr + 2) / 2 <= t) ++rr;
-    if (rr * (rr + 1) / 2 > t) --rr;
-    const int ii = t - rr * (rr + 1) / 2;
-    const int r = 16 * blk + rr, i = 16 * blk + ii;
-    float a = 0.f, l = 0.f;
-    for (int d8 = 0; d8 < DK; d8 += 8) {
-      float qr[8], kr[8], ki8[8];
-      unpack_bf16x8(ld16(sq, cm_off(r, d8, DK)), qr);
-      unpack_bf16x8(ld16(sk, cm_off(r, d8, DK)), kr);
-      unpack_bf16x8(ld16(sk, cm_off(i, d8, DK)), ki8);
+  __syncthreads();
+  {
+    // Pairs inside a block: warp w takes block w / 2 and 64 channels (two per
+    // lane); the two channel halves meet in a shared-memory add onto zero
+    // (two addends: order-free).
+    const int blk = warp >> 1, d0 = 64 * (warp & 1) + 2 * lane;
+    float q0[16], q1[16], k0[16], k1[16], a0[16], a1[16];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float ex = __expf(fminf(Gf[r * DK + d8 + e] - Gf[i * DK + d8 + e], 0.f));
-        a += qr[e] * ki8[e] * ex;
-        l += kr[e] * ki8[e] * ex;
-      }
+    for (int t = 0; t < 16; ++t) {
+      const uint32_t off = cm_off(16 * blk + t, d0, DK);
+      const float2 qv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sq + off));
+      const float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sk + off));
+      const float2 gv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sg + off));
+      q0[t] = qv.x; q1[t] = qv.y; k0[t] = kv.x; k1[t] = kv.y;
+      a0[t] = __expf(gv.x); a1[t] = __expf(gv.y);
     }
-    Aq[sw64(r, i)] = a;
-    Akk[sw64(r, i)] = (i < r) ? l : 0.f;
+    exact_diag_pair<0>(q0, q1, k0, k1, a0, a1, lane, blk, Aq, Akk);
+    exact_diag_pair<1>(q0, q1, k0, k1, a0, a1, lane, blk, Aq, Akk);
+    exact_diag_pair<2>(q0, q1, k0, k1, a0, a1, lane, blk, Aq, Akk);
+    exact_diag_pair<3>(q0, q1, k0, k1, a0, a1, lane, blk, Aq, Akk);
+    exact_diag_pair<4>(q0, q1, k0, k1, a0, a1, lane, blk, Aq, Akk);
+    exact_diag_pair<5>(q0, q1, k0, k1, a0, a1, lane, blk, Aq, Akk);
+    exact_diag_pair<6>(q0, q1, k0, k1, a0, a1, lane, blk, Aq, Akk);
+    exact_diag_pair<7>(q0, q1, k0, k1, a0, a1, lane, blk, Aq, Akk);
   }
   __syncthreads();  // the raw q, k are read: replace them with the factored rows
-  // (2) a_t, b_t per (token, channel): q a -> sq, k a -> ka, k b -> sk; m per block pair
+  // Operands: eight consecutive threads take the eight rows of one core matrix
+  // (conflict-free 16-byte accesses); warps are uniform in the block I.
   for (int idx = tid; idx < C * (DK / 8); idx += NT) {
-    const int t = idx >> 4, d8 = (idx & 15) * 8, I = t >> 4;
+    const int t = ((idx >> 7) << 3) + (idx & 7), d8 = ((idx >> 3) & 15) * 8, I = t >> 4;
     const uint32_t off = cm_off(t, d8, DK);
-    float qv[8], kv[8], qa[8], kav[8], kb[8];
+    float qv[8], kv[8], gt[8], ga[8], o1[8], o2[8];
     unpack_bf16x8(ld16(sq, off), qv);
     unpack_bf16x8(ld16(sk, off), kv);
+    ld8g(Gf, t, d8, gt);
+    ld8g(Gf, 16 * I, d8, ga);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float g = Gf[t * DK + d8 + e];
-      const float av = __expf(fminf(g - Gf[16 * I * DK + d8 + e], 0.f));
-      const float bv = __expf(fminf(Gf[(16 * I + 15) * DK + d8 + e] - g, 0.f));
-      qa[e] = qv[e] * av;
-      kav[e] = kv[e] * av;
-      kb[e] = kv[e] * bv;
+      const float av = __expf(fminf(gt[e] - ga[e], 0.f));
+      o1[e] = qv[e] * av;
+      o2[e] = kv[e] * av;
     }
-    st16(sq, off, pack_bf16x8(qa));
-    st16(ka, off, pack_bf16x8(kav));
-    st16(sk, off, pack_bf16x8(kb));
-  }
-  for (int idx = tid; idx < 6 * DK; idx += NT) {
-    const int p = idx / DK, d = idx % DK;
-    const int I = p < 3 ? p + 1 : (p < 5 ? p - 1 : 3), J = p < 3 ? 0 : (p < 5 ? 1 : 2);
-    m[idx] = __expf(fminf(Gf[16 * I * DK + d] - Gf[(16 * J + 15) * DK + d], 0.f));
-  }
-  __syncthreads();
-  // (3) block pairs I > J: (1,0) (2,0) (3,0) (2,1) (3,1) (3,2), multiply-adds only
-  for (int idx = tid; idx < 6 * 256; idx += NT) {
-    const int p = idx >> 8, w = idx & 255;
-    const int I = p < 3 ? p + 1 : (p < 5 ? p - 1 : 3), J = p < 3 ? 0 : (p < 5 ? 1 : 2);
-    const int r = 16 * I + (w >> 4), i = 16 * J + (w & 15);
-    const float* mp = m + p * DK;
-    float a = 0.f, l = 0.f;
-    for (int d8 = 0; d8 < DK; d8 += 8) {
-      float qa[8], kav[8], kb[8];
-      unpack_bf16x8(ld16(sq, cm_off(r, d8, DK)), qa);
-      unpack_bf16x8(ld16(ka, cm_off(r, d8, DK)), kav);
-      unpack_bf16x8(ld16(sk, cm_off(i, d8, DK)), kb);
-      const float4 m0 = *reinterpret_cast<const float4*>(mp + d8);
-      const float4 m1 = *reinterpret_cast<const float4*>(mp + d8 + 4);
-      const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+    st16(sq, off, pack_bf16x8(o1));
+    st16(sk, off, pack_bf16x8(o2));
+    for (int I2 = I + 1; I2 < 4; ++I2) {
+      ld8g(Gf, 16 * I2, d8, ga);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float kbm = kb[e] * mv[e];
-        a += qa[e] * kbm;
-        l += kav[e] * kbm;
+      for (int e = 0; e < 8; ++e) o1[e] = kv[e] * __expf(fminf(ga[e] - gt[e], 0.f));
+      st16(I2 == 1 ? kbm1 : (I2 == 2 ? kbm2 : kbm3), off, pack_bf16x8(o1));
+    }
+  }
+  fence_async_smem();  // generic writes -> the tensor core's reads
+}
+
+// Column of kbm_I's products in the score TMEM block: I = 1, 2, 3 -> 0, 16, 48.
+__device__ __forceinline__ int exact_col(int I) { return 8 * I * (I - 1); }
+
+// Issue of the block-pair products (one thread): D[:, col(I) .. col(I) + 16 I)
+// = [q a ; k a] kbm_I^T, K = dk.
+__device__ __forceinline__ void scores_exact_mma(uint32_t tmem, uint32_t a_qk, uint32_t kbm1, uint32_t kbm2,
+                                                 uint32_t kbm3) {
+#pragma unroll
+  for (int I = 1; I <= 3; ++I) {
+    const uint32_t idesc = idesc_bf16(128, 16 * I, false, false), kb = I == 1 ? kbm1 : (I == 2 ? kbm2 : kbm3);
+#pragma unroll
+    for (int ks = 0; ks < DK / 16; ++ks)
+      mma_bf16(tmem + exact_col(I), desc_kmajor(a_qk + ks * 256, DK), desc_kmajor(kb + ks * 256, DK), idesc,
+               ks > 0);
+  }
+}
+
+// TMEM -> Aq (lanes 0..63) / Akk (lanes 64..127) for the block pairs I > J.
+// Warp w reads TMEM lanes 32 (w % 4) .. +31 (rows of blocks 2 (w % 2) and
+// 2 (w % 2) + 1) and the column blocks J of parity w / 4.
+__device__ __forceinline__ void scores_exact_epilogue(uint32_t tmem, float* Aq, float* Akk) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qw = warp & 3, hh = warp >> 2;
+  const int R = 32 * qw + lane, r = R & 63;
+  float* dst = R < 64 ? Aq : Akk;
+  const uint32_t tl = static_cast<uint32_t>(32 * qw) << 16;
+  const int Ib = 2 * (qw & 1);  // rows of blocks Ib (lanes 0..15) and Ib + 1 (lanes 16..31)
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    const int I = Ib + s;
+    for (int J = hh; J < I; J += 2) {  // warp-uniform
+      float x[16];
+      tmem_ld16(tmem + tl + exact_col(I) + 16 * J, x);
+      tmem_wait_ld();
+      if ((r >> 4) == I) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(dst + sw64(r, 16 * J + j)) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
       }
     }
-    Aq[sw64(r, i)] = a;
-    Akk[sw64(r, i)] = l;
   }
-  fence_async_smem();  // sq, sk, ka are the next chunk's TMA destinations
+  tc_fence_before();  // the TMEM reads precede later MMAs into these columns
 }
 
 

@@ -281,8 +281,8 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
             st16(A3, cm_off(64 + R, c32 + j, DK), pack_bf16x8(qg));
             st16(A3, cm_off(128 + R, c32 + j, DK), pack_bf16x8(kg));
             if (slow) {
-              *reinterpret_cast<float4*>(Gf + R * DK + c32 + j) = make_float4(gv[j], gv[j + 1], gv[j + 2], gv[j + 3]);
-              *reinterpret_cast<float4*>(Gf + R * DK + c32 + j + 4) =
+              *reinterpret_cast<float4*>(Gf + gsw(R, c32 + j)) = make_float4(gv[j], gv[j + 1], gv[j + 2], gv[j + 3]);
+              *reinterpret_cast<float4*>(Gf + gsw(R, c32 + j + 4)) =
                   make_float4(gv[j + 4], gv[j + 5], gv[j + 6], gv[j + 7]);
             }
           }
@@ -330,11 +330,25 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         scores_epilogue(T_D, Aq, Akk);
         KDA_PT(0, 3);
       } else {
-        // exact scores on the CUDA cores (strong decay: the single anchor would overflow)
+        // exact scores (strong decay: the single anchor would overflow): 16-token
+        // block anchors, block pairs on the tensor cores, pairs inside a block exact
         fence_async_smem();
         __syncthreads();
         if (tid == kIoThread) store_prep(true);
-        scores_exact(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, reinterpret_cast<float*>(sm + OFF_VT), Gf, Aq, Akk);
+        // kbm_1 (4 KB), kbm_2 (8 KB), kbm_3 (12 KB) in A3 rows 0..63 (W comes later) and VT
+        unsigned char *kbm1 = A3 + 12288, *kbm2 = sm + OFF_VT, *kbm3 = A3;
+        scores_exact_prep(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, kbm1, kbm2, kbm3, Gf, Aq, Akk);
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+          tc_fence_after();
+          scores_exact_mma(T_D, smem_u32(sm + OFF_SQ), smem_u32(kbm1), smem_u32(kbm2), smem_u32(kbm3));
+          mma_commit(mbar);
+        }
+        failed |= !mma_wait();
+        if (__syncthreads_or(failed)) break;
+        KDA_PT(0, 2);
+        scores_exact_epilogue(T_D, Aq, Akk);
         __syncthreads();
         if (c + 1 < c_end) {
           stage(c + 1, true);
