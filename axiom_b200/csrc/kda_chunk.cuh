@@ -162,7 +162,7 @@ __device__ __forceinline__ void exact_diag_pair(const float (&q0)[16], const flo
 // operands: q a -> sq, k a -> sk (in place, so [sq ; sk] is the 128-row A
 // operand) and kbm_1..3 (bf16 CM [16 I][128]).  Inputs: raw q, k, g (sq, sk,
 // sg; bf16 CM [64][128]) and G (fp32, gsw layout).
-__device__ __forceinline__ void scores_exact_prep(unsigned char* sq, unsigned char* sk, const unsigned char* sg,
+static __device__ __noinline__ void scores_exact_prep(unsigned char* sq, unsigned char* sk, const unsigned char* sg,
                                                   unsigned char* kbm1, unsigned char* kbm2, unsigned char* kbm3,
                                                   const float* Gf, float* Aq, float* Akk) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
