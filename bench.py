@@ -44,8 +44,8 @@ BWD_FLOP_PER_CHUNK_HEAD = 23.07e6
 # summarised in profiles/kda_kernels_small_case.md); a launch's traffic grows in
 # proportion to the chunk-heads it processes, so roofline.traffic = this x units.
 TRAFFIC_PER_CHUNK_HEAD = {
-    "kda_fwd": (134.634240e6 + 267.665920e6) / 2048,
-    "kda_bwd": (152.344832e6 + 43.242752e6 + 421.613056e6 + 110.059264e6) / 2048,  # bwd_seq + bwd_par
+    "kda_fwd": (134.819584e6 + 331.858432e6) / 2048,
+    "kda_bwd": (152.345600e6 + 43.184640e6 + 522.276608e6 + 111.698944e6) / 2048,  # bwd_seq + bwd_par
 }
 
 
