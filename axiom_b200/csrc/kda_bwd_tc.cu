@@ -295,7 +295,8 @@ constexpr int F_YW = 44, NF_YW = 8;
 constexpr int G_DL = 52, N_DL = 16;       // dL
 constexpr int G_VII = 68, N_VII = 12;     // [dQG^T | dKG^T] +=, dKI^T
 constexpr int N_MMA = 80;
-constexpr int PAR_SMEM = P_MMA + N_MMA * 32;
+constexpr int P_DBQ = P_MMA + N_MMA * 32;  // dbeta partials per channel quarter fp32[4][64]
+constexpr int PAR_SMEM = P_DBQ + 1024;
 // the checkpoint's adjacent tiles land with one bulk copy each: [T, Aqk, Akk] in
 // TB, AQB, AKB; [Q Gam, K Gam] in A3 rows 64..191; [K Gi, lam K] in KI, KL
 static_assert(P_AQB - P_TB == static_cast<int>(FAC_AQ) && P_AKB - P_TB == static_cast<int>(FAC_AK) &&
@@ -377,6 +378,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   float* beta_s = reinterpret_cast<float*>(sm + P_BETA);
   float* dgc = reinterpret_cast<float*>(sm + P_DGC);
   float* dbs = reinterpret_cast<float*>(sm + P_DB);
+  float* dbq = reinterpret_cast<float*>(sm + P_DBQ);  // one writer per entry: summed in a fixed order
   float* xch = reinterpret_cast<float*>(sm + P_XCH);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P_BAR + 8);
@@ -832,7 +834,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           }
           {  // dbeta partials: sum over this warp's 32 channels, 4 warps per token
             const float sb = warp_colsum<8>(tb, lane);
-            if (lane < 8) atomicAdd(&dbs[c8 + lane], sb);
+            if (lane < 8) dbq[qw * 64 + c8 + lane] = sb;
           }
           if (use_tma) {  // channel-major, over the tiles just read (stored below)
             st16(sm + P_SB, cm_off(d, c8, C), pack_bf16x8(oq));
@@ -1034,7 +1036,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
             }
           }
           const float sb = warp_colsum<16>(tb, lane);
-          if (lane < 16) atomicAdd(&dbs[c16 + lane], sb);
+          if (lane < 16) dbq[qw * 64 + c16 + lane] = sb;
         }
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) dG[jj] = dGs[(cb + jj) * DK + d];
@@ -1096,7 +1098,9 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     __syncthreads();
     tc_fence_after();
     KDA_PT(2, 28);
-    if (tid < rows_valid) dbeta[(tok0 + tid) * H + h] = __float2bfloat16_rn(dbs[tid]);
+    if (tid < rows_valid)
+      dbeta[(tok0 + tid) * H + h] =
+          __float2bfloat16_rn(dbs[tid] + dbq[tid] + dbq[64 + tid] + dbq[128 + tid] + dbq[192 + tid]);
     if (!prefetched && u_next < n_units) issue_inputs(u_next, beta_nx);
     ++it;
   }

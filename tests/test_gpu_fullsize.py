@@ -1,0 +1,124 @@
+"""BASELINE's full sizes on the GPU, through the C ABI.
+
+cfg3 (B=4, T=8192, H=32, dk=dv=128, bf16, S0=0) and cfg2 (B=8, T=4096, H=16,
+S0 ~ N(0, 0.02)) run whole.  (batch, head) units are independent, so sampled
+units are checked against the oracle run on those units alone, and two
+size-independent properties are checked over every unit:
+
+* a sequence split at a chunk boundary, with the fp32 state carried from the
+  first call into the second, gives the same O and S_T as one call;
+* the backward's input-state cotangent dS0 of a call whose S_T cotangent is
+  dST equals the chain through two half calls.
+
+Inputs follow BASELINE's distributions (q, k ~ N(0, 1) L2-normalised per
+token-head, v ~ N(0, 1), beta = sigmoid(N(0, 1)), g = logsigmoid(N(3, 1)));
+the oracle reads the same bf16-rounded values in float64.  Tolerance: the bf16
+bar, scale-relative 1e-2, against the oracle; 1e-5 between the split and the
+whole calls (the same arithmetic on the same fp32 state).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import kda_oracle as K
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+TOL_SPLIT = 1e-5
+
+
+def _inputs(B, T, H, seed, s0_std=None):
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+
+    def rn(*shape):
+        return torch.randn(*shape, generator=gen, device=dev)
+
+    q = torch.nn.functional.normalize(rn(B, T, H, 128), dim=-1).to(torch.bfloat16)
+    k = torch.nn.functional.normalize(rn(B, T, H, 128), dim=-1).to(torch.bfloat16)
+    v = rn(B, T, H, 128).to(torch.bfloat16)
+    g = torch.nn.functional.logsigmoid(rn(B, T, H, 128) + 3.0).to(torch.bfloat16)
+    beta = torch.sigmoid(rn(B, T, H)).to(torch.bfloat16)
+    S0 = (rn(B, H, 128, 128) * s0_std).contiguous() if s0_std else None
+    return q, k, v, g, beta, S0
+
+
+def _unit(x, b, h):
+    """(b, h) slice of a [B, T, H, ...] tensor as float64 [1, T, 1, ...]."""
+    return x[b:b + 1, :, h:h + 1].double().cpu().numpy()
+
+
+def _np(x):
+    return x.detach().double().cpu().numpy()
+
+
+def test_cfg3_full_size_units_match_oracle_and_split_is_exact():
+    from axiom_b200 import kda_bwd, kda_fwd
+
+    B, T, H = 4, 8192, 32
+    q, k, v, g, beta, _ = _inputs(B, T, H, seed=3)
+    do = torch.randn(B, T, H, 128, device="cuda", generator=torch.Generator("cuda").manual_seed(4)).to(torch.bfloat16)
+    o, s_t, ckpt = kda_fwd(q, k, v, g, beta, None, chunk=64, o_dtype=torch.float32, need_ckpt=True)
+    grads = kda_bwd(q, k, v, g, beta, ckpt, do, None, chunk=64, need_ds0=False)
+    torch.cuda.synchronize()
+    for b, h in ((0, 0), (1, 17), (3, 31)):
+        xs = [_unit(t, b, h) for t in (q, k, v, g)] + [beta[b:b + 1, :, h:h + 1].double().cpu().numpy()]
+        o_ref, s_ref = K.chunk_fwd(*xs, None, chunk=64)
+        assert K.scale_rel_err(_np(o[b:b + 1, :, h:h + 1]), o_ref) <= TOL, (b, h)
+        assert K.scale_rel_err(_np(s_t[b:b + 1, h:h + 1]), s_ref) <= TOL, (b, h)
+        ref = K.chunk_bwd(*xs, None, _unit(do, b, h), None, chunk=64)
+        for name, gr, rf in zip(("dq", "dk", "dv", "dg"), grads[:4], ref[:4]):
+            assert K.scale_rel_err(_np(gr[b:b + 1, :, h:h + 1]), rf) <= TOL, (name, b, h)
+        assert K.scale_rel_err(_np(grads[4][b:b + 1, :, h:h + 1]), ref[4]) <= TOL, ("dbeta", b, h)
+    del ckpt, grads
+    # the same sequences in two calls at the chunk boundary T/2, state carried in fp32
+    m = T // 2
+    halves = [[t[:, :m].contiguous() for t in (q, k, v, g, beta)], [t[:, m:].contiguous() for t in (q, k, v, g, beta)]]
+    o1, s_mid, _ = kda_fwd(*halves[0], None, chunk=64, o_dtype=torch.float32)
+    o2, s_end, _ = kda_fwd(*halves[1], s_mid, chunk=64, o_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert K.scale_rel_err(_np(o1), _np(o[:, :m])) <= TOL_SPLIT
+    assert K.scale_rel_err(_np(o2), _np(o[:, m:])) <= TOL_SPLIT
+    assert K.scale_rel_err(_np(s_end), _np(s_t)) <= TOL_SPLIT
+
+
+def test_cfg3_full_size_ds0_chains_through_a_split():
+    from axiom_b200 import kda_bwd, kda_fwd
+
+    B, T, H = 4, 8192, 32
+    q, k, v, g, beta, S0 = _inputs(B, T, H, seed=5, s0_std=0.02)
+    gen = torch.Generator("cuda").manual_seed(6)
+    do = torch.randn(B, T, H, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    dST = torch.randn(B, H, 128, 128, device="cuda", generator=gen) * 0.1
+    _, _, ckpt = kda_fwd(q, k, v, g, beta, S0, chunk=64, need_ckpt=True)
+    whole = kda_bwd(q, k, v, g, beta, ckpt, do, dST, chunk=64)
+    del ckpt
+    m = T // 2
+    a = [t[:, :m].contiguous() for t in (q, k, v, g, beta)]
+    z = [t[:, m:].contiguous() for t in (q, k, v, g, beta)]
+    _, s_mid, ck_a = kda_fwd(*a, S0, chunk=64, need_ckpt=True)
+    _, _, ck_z = kda_fwd(*z, s_mid, chunk=64, need_ckpt=True)
+    gz = kda_bwd(*z, ck_z, do[:, m:].contiguous(), dST, chunk=64)
+    ga = kda_bwd(*a, ck_a, do[:, :m].contiguous(), gz[5], chunk=64)
+    torch.cuda.synchronize()
+    assert K.scale_rel_err(_np(ga[5]), _np(whole[5])) <= TOL_SPLIT
+    for i, name in enumerate(("dq", "dk", "dv", "dg", "dbeta")):
+        got = torch.cat([ga[i], gz[i]], dim=1)
+        assert K.scale_rel_err(_np(got), _np(whole[i])) <= TOL_SPLIT, name
+
+
+def test_cfg2_full_size_prefill_units_match_oracle():
+    from axiom_b200 import kda_fwd
+
+    B, T, H = 8, 4096, 16
+    q, k, v, g, beta, S0 = _inputs(B, T, H, seed=7, s0_std=0.02)
+    o, s_t, _ = kda_fwd(q, k, v, g, beta, S0, chunk=64, o_dtype=torch.float32)
+    torch.cuda.synchronize()
+    for b, h in ((0, 3), (7, 15)):
+        xs = [_unit(t, b, h) for t in (q, k, v, g)] + [beta[b:b + 1, :, h:h + 1].double().cpu().numpy()]
+        o_ref, s_ref = K.chunk_fwd(*xs, S0[b:b + 1, h:h + 1].double().cpu().numpy(), chunk=64)
+        assert K.scale_rel_err(_np(o[b:b + 1, :, h:h + 1]), o_ref) <= TOL, (b, h)
+        assert K.scale_rel_err(_np(s_t[b:b + 1, h:h + 1]), s_ref) <= TOL, (b, h)
