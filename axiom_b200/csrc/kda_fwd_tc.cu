@@ -365,7 +365,9 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       KDA_PT(0, 12);
       solve_T(Akk, beta_s, Tm, reinterpret_cast<float*>(sm + OFF_VT));
       KDA_PT(0, 4);
-      const int r = tid >> 2, c0 = (tid & 3) * 16;
+      // eight consecutive threads take eight rows of one column block: conflict-free
+      // swizzled fp32 reads and core-matrix bf16 writes
+      const int r = 8 * (tid >> 5) + (tid & 7), c0 = 16 * ((tid >> 3) & 3);
       float v[16], a[16], kk[16];
       ld_row16_sw64(Tm, r, c0, v);
       ld_row16_sw64(Aq, r, c0, a);
