@@ -9,7 +9,10 @@ the decay gate ``g = -exp(A_log) * softplus(z + b)`` beside the reference's
 ``g = g_min * sigmoid(exp(A) z)``.  The projection GEMMs are plain library
 GEMMs (``torch.matmul``: cuBLAS); the per-token work and the KDA core run in
 ``libkda_b200.so``.  The reference's sliding-window branch (``_with_window``
-:261-269) is outside this layer.
+:261-269) is outside this layer.  For inference, ``kda_layer_prefill`` runs N
+prompts and returns a ``KDADecodeCache`` (recurrent state and short-conv
+buffers, the reference's ``KDAState``) that ``kda_layer_decode`` advances one
+token per call with the fused decode kernel.
 """
 
 from __future__ import annotations
@@ -19,7 +22,7 @@ from dataclasses import dataclass, fields
 import torch
 
 from . import mixer
-from .kda import CHUNK, chunk_kda, chunk_kda_varlen, packing
+from .kda import CHUNK, chunk_kda, chunk_kda_varlen, kda_fwd, packing
 
 
 @dataclass
@@ -114,3 +117,52 @@ def kda_layer(p: KDALayerParams, x, *, H, cu_seqlens=None, gate_kind="softplus",
         y = mixer.gated_rmsnorm(o, gl[None], cu_seqlens=cu, out_rows=rows)
     out = y[0] @ p.W_o
     return (out, s_t) if return_state else out
+
+
+@dataclass
+class KDADecodeCache:
+    """Per-layer streaming state of N sequences (the reference's ``KDAState``,
+    ``net/kda.py:54-60``): the fp32 recurrent state and the short-conv buffers
+    of the q, k, v projections (the last K-1 rows, side by side)."""
+
+    S: torch.Tensor     # [N, H, dk, dv] fp32
+    conv: torch.Tensor  # [N, K-1, H*(2dk+dv)] fp32
+
+
+def _projections(p: KDALayerParams, x):
+    return x @ p.W_q, x @ p.W_k, x @ p.W_v, (x @ p.W_a_down) @ p.W_a_up, x @ p.W_beta, x @ p.W_g
+
+
+def kda_layer_prefill(p: KDALayerParams, x, *, H, gate_kind="softplus", g_min=mixer.G_MIN, chunk=CHUNK):
+    """Inference over N prompts of one length: ``x [N, T, d_model]`` ->
+    ``(out [N, T, d_model], cache)``.  The same kernels as :func:`kda_layer`
+    (prologue with its conv state out, chunked core with its final state,
+    output gate); the cache continues each sequence with
+    :func:`kda_layer_decode`.  (The reference's ``generate``, ``net/infer.py``,
+    re-runs the whole forward for every new token; this is the state cache
+    that replaces that.)"""
+    with torch.no_grad():
+        qp, kp, vp, z, bl, gl = _projections(p, x)
+        q, k, v, g, beta, conv = mixer.prologue_fwd(qp, kp, vp, z, bl, p.conv_q, p.conv_k, p.conv_v, p.A, H=H,
+                                                    b_gate=p.b_gate, g_min=g_min, gate_kind=gate_kind,
+                                                    return_state=True)
+        o, S, _ = kda_fwd(q, k, v, g, beta, None, chunk=chunk)
+        y = mixer.gated_rmsnorm_fwd(o, gl)
+        out = y @ p.W_o
+    if conv is None:  # K = 1: no buffers
+        conv = torch.empty((x.shape[0], 0, 0), dtype=torch.float32, device=x.device)
+    return out, KDADecodeCache(S=S, conv=conv)
+
+
+def kda_layer_decode(p: KDALayerParams, x, cache: KDADecodeCache, *, H, gate_kind="softplus",
+                     g_min=mixer.G_MIN):
+    """One new token for each of the N cached sequences: ``x [N, d_model]`` ->
+    ``[N, d_model]``; ``cache`` is updated in place.  The token's prologue, the
+    recurrent step and the output gate are one kernel
+    (``kda_decode_fused``); the projections are library GEMMs."""
+    with torch.no_grad():
+        qp, kp, vp, z, bl, gl = _projections(p, x)
+        y = mixer.decode_fused(cache.S, cache.conv, qp, kp, vp, z, bl, p.conv_q, p.conv_k, p.conv_v, p.A, H=H,
+                               b_gate=p.b_gate, gate_logit=gl, g_min=g_min, gate_kind=gate_kind)
+        return y.reshape(x.shape[0], -1) @ p.W_o
+

@@ -49,3 +49,34 @@ def test_layer_matches_oracle(dt, dk, cu, kind):
         got = getattr(p, name).grad
         assert got is not None, name
         assert scale_rel_err(got.double().cpu().numpy(), g[name]) <= tol, name
+
+
+@pytest.mark.parametrize("dt,dk,kind", [(torch.bfloat16, 128, "softplus"), (torch.float32, 64, "sigmoid_min")])
+def test_prefill_then_decode_matches_the_full_layer(dt, dk, kind):
+    """Streaming: prefill N prompts of length T (chunked kernels, conv and
+    recurrent state out), then decode n tokens one at a time through the cache
+    (``kda_decode_fused``); outputs and the final state equal the whole layer
+    run over the T + n tokens of each sequence.  Bounds: 5e-2 bf16 (the two
+    routes round different bf16 intermediates), 1e-3 fp32."""
+    from axiom_b200 import layer
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    d_model, H, dv, N, T, n = 96, 2, dk, 3, 100, 6
+    p = layer.init_params(d_model, H, dk, dv, rank=16, K=4, gate_kind=kind, dtype=dt, seed=5)
+    with torch.no_grad():
+        p.b_gate.normal_(0.0, 0.3)
+        p.A.normal_(0.0, 0.3)
+    gen = torch.Generator(device="cpu").manual_seed(6)
+    x = torch.randn(N, T + n, d_model, generator=gen).to("cuda", dt)
+    tol = 1e-3 if dt == torch.float32 else 5e-2
+    with torch.no_grad():
+        full = [layer.kda_layer(p, x[i], H=H, gate_kind=kind, return_state=True) for i in range(N)]
+    out, cache = layer.kda_layer_prefill(p, x[:, :T].contiguous(), H=H, gate_kind=kind)
+    for i in range(N):
+        assert scale_rel_err(out[i].double().cpu().numpy(), full[i][0][:T].double().cpu().numpy()) <= tol, i
+    for t in range(T, T + n):
+        y = layer.kda_layer_decode(p, x[:, t].contiguous(), cache, H=H, gate_kind=kind)
+        for i in range(N):
+            assert scale_rel_err(y[i].double().cpu().numpy(), full[i][0][t].double().cpu().numpy()) <= tol, (t, i)
+    for i in range(N):
+        assert scale_rel_err(cache.S[i].double().cpu().numpy(), full[i][1][0].double().cpu().numpy()) <= tol, i
