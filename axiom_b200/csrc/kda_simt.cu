@@ -385,18 +385,20 @@ bwd_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin*
       }
       s.L[idx] = -acc;
     }
+    __syncthreads();  // (13) read Yw, Yu of every row; (14) overwrites them with dbeta terms
     // (14) Yw / Yu terms; dv = Yu beta
     for (int idx = tid; idx < C * dk; idx += nt) {
       const int r = idx / dk;
       const float yw = s.X[idx], gam = expf(s.G[idx]), kk = s.K[idx], bb = s.Bs[r];
       s.dKa[idx] += yw * gam * bb;
       s.dGa[idx] += yw * kk * bb * gam;
-      atomicAdd(&s.dBa[r], yw * gam * kk);
+      s.X[idx] = yw * gam * kk;  // dbeta term (Yw is dead after this)
     }
     for (int idx = tid; idx < C * dv; idx += nt) {
       const int r = idx / dv, j = idx % dv, t = t0 + r;
-      atomicAdd(&s.dBa[r], s.dVt[idx] * s.V[idx]);
-      if (t < T) stf(dvout + row_off(b, t, h, T, H, dv) + j, s.dVt[idx] * s.Bs[r]);
+      const float dvt = s.dVt[idx];
+      if (t < T) stf(dvout + row_off(b, t, h, T, H, dv) + j, dvt * s.Bs[r]);
+      s.dVt[idx] = dvt * s.V[idx];  // dbeta term (dV~ is dead after this)
     }
     __syncthreads();
     // (15) score adjoints (row side then column side), direct decay ratio
@@ -413,9 +415,16 @@ bwd_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin*
       s.dQa[idx] += dra;
       s.dKa[idx] += drk * bb;
       s.dGa[idx] += dra * s.Q[idx] + drk * kk * bb;
-      atomicAdd(&s.dBa[r], drk * kk);
+      s.X[idx] += drk * kk;
     }
     __syncthreads();
+    // dbeta: each row's terms summed by one thread in a fixed order (deterministic)
+    for (int r = tid; r < C; r += nt) {
+      float acc = 0.f;
+      for (int d = 0; d < dk; ++d) acc += s.X[r * dk + d];
+      for (int j = 0; j < dv; ++j) acc += s.dVt[r * dv + j];
+      s.dBa[r] = acc;
+    }
     for (int idx = tid; idx < C * dk; idx += nt) {
       const int i = idx / dk, d = idx % dk;
       const float Gi = s.G[idx];
