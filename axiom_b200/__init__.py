@@ -6,13 +6,13 @@ layer."""
 
 from . import layer, mixer  # noqa: F401
 from .kda import (  # noqa: F401
-    CHUNK, KDA_CC_IMPLS, TILE, cc_scan, chunk_kda, chunk_kda_varlen, ckpt_states, decode_step,
-    device_available, kda_bwd, kda_bwd_varlen, kda_cc_impl, kda_fwd, kda_fwd_varlen, kernel, kernel_bwd,
-    packing,
+    CHUNK, KDA_CC_IMPLS, TILE, cc_scan, check_device, chunk_kda, chunk_kda_varlen, ckpt_states, decode_step,
+    device_available, device_status, kda_bwd, kda_bwd_varlen, kda_cc_impl, kda_fwd, kda_fwd_varlen, kernel,
+    kernel_bwd, packing, selftest_wait_timeout,
 )
 
 __all__ = [
-    "CHUNK", "TILE", "KDA_CC_IMPLS", "cc_scan", "chunk_kda", "chunk_kda_varlen", "ckpt_states",
-    "decode_step", "device_available", "kda_bwd", "kda_bwd_varlen", "kda_cc_impl", "kda_fwd",
-    "kda_fwd_varlen", "kernel", "kernel_bwd", "layer", "mixer", "packing",
+    "CHUNK", "TILE", "KDA_CC_IMPLS", "cc_scan", "check_device", "chunk_kda", "chunk_kda_varlen", "ckpt_states",
+    "decode_step", "device_available", "device_status", "kda_bwd", "kda_bwd_varlen", "kda_cc_impl", "kda_fwd",
+    "kda_fwd_varlen", "kernel", "kernel_bwd", "layer", "mixer", "packing", "selftest_wait_timeout",
 ]

@@ -40,6 +40,8 @@ SIGNATURES = {
     "kda_gated_rmsnorm_fwd": ([_P] * 5 + [_I] * 4 + [_F] + [_I] * 3 + [_P], _I),
     "kda_gated_rmsnorm_bwd": ([_P] * 7 + [_I] * 4 + [_F] + [_I] * 3 + [_P], _I),
     "kda_decode_fused": ([_P] * 13 + [_F, _I, _F, _P] + [_I] * 7 + [_P], _I),
+    "kda_device_status": ([_P, _I, _P], _I),
+    "kda_selftest_wait_timeout": ([ctypes.c_uint, _P], _I),
 }
 
 _lib = None

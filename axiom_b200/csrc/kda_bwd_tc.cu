@@ -1200,4 +1200,13 @@ int tc_bwd_launch(const void* q, const void* k, const void* v, const void* g, co
   return KDA_ERR_DTYPE;
 }
 
+int tc_bwd_error_flag(int* value, bool clear, cudaStream_t st) {
+  static const int zero = 0;
+  if (cudaMemcpyFromSymbolAsync(value, g_bwd_tc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return KDA_ERR_LAUNCH;
+  if (clear && cudaMemcpyToSymbolAsync(g_bwd_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return KDA_ERR_LAUNCH;
+  return KDA_OK;
+}
+
 }  // namespace kda

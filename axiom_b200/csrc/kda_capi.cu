@@ -63,6 +63,7 @@ const char* kda_strerror(int status) {
     case KDA_ERR_DEVICE: return "no usable CUDA device";
     case KDA_ERR_SCRATCH_LIMIT:
       return "problem needs more scratch than kda_bwd_noalloc's fixed array (KDA_NOALLOC_SCRATCH_BYTES)";
+    case KDA_ERR_TIMEOUT: return "a kernel's bounded wait gave up (device status)";
     default: return "unknown status";
   }
 }

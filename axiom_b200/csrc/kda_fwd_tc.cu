@@ -634,8 +634,13 @@ int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, co
   return KDA_ERR_DTYPE;
 }
 
-int tc_fwd_poll_error(int* value) {
-  return cudaMemcpyFromSymbol(value, g_fwd_tc_error, sizeof(int)) == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+int tc_fwd_error_flag(int* value, bool clear, cudaStream_t st) {
+  static const int zero = 0;
+  if (cudaMemcpyFromSymbolAsync(value, g_fwd_tc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return KDA_ERR_LAUNCH;
+  if (clear && cudaMemcpyToSymbolAsync(g_fwd_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return KDA_ERR_LAUNCH;
+  return KDA_OK;
 }
 
 }  // namespace kda

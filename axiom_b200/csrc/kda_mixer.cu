@@ -1129,6 +1129,17 @@ __global__ void __launch_bounds__(kDecThreads, 3) decode_fused_kernel(const DecA
 
 __device__ int g_decode_fused_error = 0;  // set when a state copy's wait timed out
 
+int decode_fused_error_flag(int* value, bool clear, cudaStream_t st) {
+  static const int zero = 0;
+  if (cudaMemcpyFromSymbolAsync(value, g_decode_fused_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st) !=
+      cudaSuccess)
+    return KDA_ERR_LAUNCH;
+  if (clear &&
+      cudaMemcpyToSymbolAsync(g_decode_fused_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return KDA_ERR_LAUNCH;
+  return KDA_OK;
+}
+
 namespace {
 
 template <int CPL, bool VARLEN, typename Tin, typename Tout>

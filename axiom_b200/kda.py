@@ -21,11 +21,12 @@ computation runs in ``libkda_b200.so`` and there is no eager or CPU fallback.
 
 from __future__ import annotations
 
+import ctypes
 import os
 
 import torch
 
-from ._lib import KDA_BF16, KDA_F32, check, lib
+from ._lib import KDA_BF16, KDA_F32, KDAError, check, lib
 
 #: Chunk width of the tensor-core path (the reference's persistent kernel uses 32
 #: because of the GB10 SMEM budget, ``kda_cc_fused_persist.py:228``; B200 runs 64).
@@ -73,6 +74,34 @@ def _ptr(x):
 
 def _stream():
     return torch.cuda.current_stream().cuda_stream
+
+
+STATUS_BITS = {"fwd": 1, "bwd": 2, "decode_fused": 4, "selftest": 8}  # KDA_STATUS_* (kda_b200.h)
+
+
+def device_status(clear=False) -> dict:
+    """Which kernel families had a bounded wait give up since the last clear
+    (``kda_device_status``; synchronises the current stream).  A kernel that
+    gives up skips its remaining work, so its outputs are not valid."""
+    _require_device("device_status")
+    flags = ctypes.c_int(0)
+    check("kda_device_status", lib().kda_device_status(ctypes.byref(flags), int(bool(clear)), _stream()))
+    return {name: bool(flags.value & bit) for name, bit in STATUS_BITS.items()}
+
+
+def check_device(clear=True) -> None:
+    """Raise ``KDAError`` (``KDA_ERR_TIMEOUT``) if any kernel's wait gave up."""
+    st = device_status(clear=clear)
+    bad = [name for name, hit in st.items() if hit]
+    if bad:
+        raise KDAError("check_device", -9, "bounded wait gave up in: " + ", ".join(bad))
+
+
+def selftest_wait_timeout(polls=4096) -> None:
+    """Run the bounded-wait failure path once (``kda_selftest_wait_timeout``):
+    a wait that nothing completes gives up and sets the ``selftest`` bit."""
+    _require_device("selftest_wait_timeout")
+    check("kda_selftest_wait_timeout", lib().kda_selftest_wait_timeout(int(polls), _stream()))
 
 
 def _check_tensor(x: torch.Tensor, name: str, shape, dtype=None):

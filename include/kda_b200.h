@@ -59,7 +59,16 @@ enum {
   KDA_ERR_LAUNCH = -5,  /* the CUDA launch itself failed */
   KDA_ERR_WORKSPACE = -6, /* workspace missing or too small */
   KDA_ERR_DEVICE = -7,  /* no sm_100 device / device query failed */
-  KDA_ERR_SCRATCH_LIMIT = -8 /* problem needs more than kda_bwd_noalloc's fixed scratch */
+  KDA_ERR_SCRATCH_LIMIT = -8, /* problem needs more than kda_bwd_noalloc's fixed scratch */
+  KDA_ERR_TIMEOUT = -9  /* a kernel's bounded wait gave up (see kda_device_status) */
+};
+
+/* Device-side status bits (kda_device_status). */
+enum {
+  KDA_STATUS_FWD = 1,           /* tensor-core kda_fwd / kda_fwd_varlen */
+  KDA_STATUS_BWD = 2,           /* tensor-core kda_bwd / kda_bwd_varlen / kda_bwd_noalloc */
+  KDA_STATUS_DECODE_FUSED = 4,  /* kda_decode_fused */
+  KDA_STATUS_SELFTEST = 8       /* kda_selftest_wait_timeout */
 };
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -186,6 +195,22 @@ int kda_bwd_noalloc(const void* q, const void* k, const void* v, const void* g,
 int kda_decode(float* S, const void* q, const void* k, const void* v,
                const void* g, const void* beta, void* o, int N, int dk, int dv,
                int in_dtype, int o_dtype, kda_stream_t stream);
+
+/* Every wait of a kernel on its own copies or MMAs (an mbarrier) is bounded:
+ * when one gives up, the CTA records it in a device flag, skips its remaining
+ * work, waits (again bounded) for its copies in flight, frees its tensor
+ * memory and returns, so the context stays usable.  This reads those flags
+ * as KDA_STATUS_* bits into *flags (0: no wait gave up since the last clear)
+ * and, with clear != 0, resets them.  Unlike the compute entry points it
+ * synchronises `stream` (the flags are read after its work).  Returns KDA_OK,
+ * or KDA_ERR_LAUNCH if a copy fails. */
+int kda_device_status(int* flags, int clear, kda_stream_t stream);
+
+/* Exercises the bounded wait the kernels share: one CTA waits on an mbarrier
+ * that nothing completes, gives up after `polls` polls (each ~0.1 us after
+ * the first 64) and sets KDA_STATUS_SELFTEST.  For tests of the failure path;
+ * it faults nothing. */
+int kda_selftest_wait_timeout(unsigned int polls, kda_stream_t stream);
 
 #ifdef __cplusplus
 }

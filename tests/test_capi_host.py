@@ -213,3 +213,10 @@ def test_missing_library_raises(monkeypatch):
     monkeypatch.setattr(_lib, "LIB_PATH", os.path.join(ROOT, "does_not_exist.so"))
     with pytest.raises(RuntimeError, match="not built"):
         _lib.lib()
+
+
+def test_device_status_entry_points_validate_before_any_cuda_call():
+    lib = _lib.lib()
+    assert lib.kda_device_status(None, 0, None) == -4  # KDA_ERR_NULL
+    assert lib.kda_selftest_wait_timeout(0, None) == -1  # KDA_ERR_SHAPE: zero polls
+    assert b"bounded wait" in lib.kda_strerror(-9)
