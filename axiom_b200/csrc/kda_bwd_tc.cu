@@ -74,9 +74,11 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
   const int qw = warp & 3, hh = warp >> 2;
   // CTA (seq, h) walks the chunks [c_beg, c_end) of batch row b in reverse: the
   // whole row, or with packed sequences (cs: chunk offsets, B = 1) the sequence's range
-  const int h = blockIdx.x % H, seq = blockIdx.x / H;
-  const int b = cs ? 0 : seq;
   const int n_chunks = (T + C - 1) / C;
+  const int h = blockIdx.x % H;
+  const int seq = cs ? longest_first(cs, gridDim.x / H, blockIdx.x / H, n_chunks, reinterpret_cast<int*>(sm))
+                     : blockIdx.x / H;
+  const int b = cs ? 0 : seq;
   const int c_beg = cs ? min(max(cs[seq], 0), n_chunks) : 0;  // clamped like the forward's
   const int c_end = cs ? min(max(cs[seq + 1], c_beg), n_chunks) : n_chunks;
   const size_t tok0 = static_cast<size_t>(b) * T;

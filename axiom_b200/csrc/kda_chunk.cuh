@@ -94,6 +94,35 @@ __device__ __forceinline__ void scores_epilogue(uint32_t t_scores, float* Aq, fl
   }
 }
 
+// Packed sequences, longest first: the per-(sequence, head) kernels walk one
+// sequence's chunks in order, so a long sequence scheduled late sets the
+// kernel's end.  CTA rank r (blockIdx / H) takes the sequence with the r-th
+// largest chunk count (ties by index) when there are at most NT sequences;
+// else rank = sequence.  `scratch`: NT + 1 ints of shared memory, free on
+// entry and on exit.  All threads call it.
+__device__ __forceinline__ int longest_first(const int* cs, int n, int r, int n_chunks, int* scratch) {
+  if (n > NT) return r;
+  const int tid = threadIdx.x;
+  if (tid < n) {
+    const int c0 = min(max(cs[tid], 0), n_chunks);
+    scratch[tid] = min(max(cs[tid + 1], c0), n_chunks) - c0;  // clamped like the ranges themselves
+  }
+  __syncthreads();
+  if (tid < n) {
+    const int len = scratch[tid];
+    int rank = 0;
+    for (int s2 = 0; s2 < n; ++s2) {
+      const int l2 = scratch[s2];
+      rank += (l2 > len) || (l2 == len && s2 < tid);
+    }
+    if (rank == r) scratch[NT] = tid;
+  }
+  __syncthreads();
+  const int seq = scratch[NT];
+  __syncthreads();
+  return seq;
+}
+
 // G fp32 [64][128] of the exact path: the 16-byte chunks of row r are
 // XOR-swizzled by (r & 7), so eight rows' same chunk lie in distinct banks.
 __device__ __forceinline__ int gsw(int r, int d) {

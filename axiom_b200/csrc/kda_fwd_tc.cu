@@ -81,9 +81,11 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   const int qw = warp & 3, hh = warp >> 2;  // TMEM lane quarter, column half
   // CTA (seq, h) walks the chunks [c_beg, c_end) of batch row b: the whole row,
   // or with packed sequences (cs: chunk offsets, B = 1) the sequence's range
-  const int h = blockIdx.x % H, seq = blockIdx.x / H;
-  const int b = cs ? 0 : seq;
   const int n_chunks = (T + C - 1) / C;
+  const int h = blockIdx.x % H;
+  const int seq = cs ? longest_first(cs, gridDim.x / H, blockIdx.x / H, n_chunks, reinterpret_cast<int*>(sm + OFF_SQ))
+                     : blockIdx.x / H;
+  const int b = cs ? 0 : seq;
   // (clamped: a malformed table cannot take a chunk outside the tensors)
   const int c_beg = cs ? min(max(cs[seq], 0), n_chunks) : 0;
   const int c_end = cs ? min(max(cs[seq + 1], c_beg), n_chunks) : n_chunks;

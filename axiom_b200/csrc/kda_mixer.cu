@@ -244,6 +244,41 @@ __device__ __forceinline__ int out_row(const ProArgs& a, int t) {
   return t + __ldg(a.out_rows + s) - __ldg(a.cu + s);
 }
 
+// out_row for tokens visited in increasing (UP) or decreasing order: the
+// sequence and its row shift change only at sequence boundaries, so a call is
+// a compare, with a reload when a boundary is crossed (no search per token).
+template <bool UP>
+struct RowWalk {
+  const int* cu;
+  const int* rows;
+  int n, s, edge, shift;
+  __device__ void init(const ProArgs& a, int t) {
+    cu = a.cu;
+    rows = a.out_rows;
+    n = a.n_seqs;
+    s = seq_of(cu, n, t);
+    set();
+  }
+  __device__ void set() {
+    edge = UP ? __ldg(cu + s + 1) : __ldg(cu + s);  // first token of the next / this sequence
+    shift = rows ? __ldg(rows + s) - __ldg(cu + s) : 0;
+  }
+  __device__ int operator()(int t) {
+    if (UP) {
+      while (t >= edge && s < n - 1) {
+        ++s;
+        set();
+      }
+    } else {
+      while (t < edge && s > 0) {
+        --s;
+        set();
+      }
+    }
+    return t + shift;
+  }
+};
+
 // Zeroes this lane's channels of the pad rows of every sequence ending in
 // (t0, t1]: the rows between its last token and the next sequence's first row.
 template <int CPL, typename T>
@@ -438,9 +473,14 @@ __device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
   }
   const Tin* bl = static_cast<const Tin*>(a.beta_logit);
   Tout* beta = static_cast<Tout*>(a.beta);
+  RowWalk<true> rwb, rwm;  // rows of this lane's beta tokens, of the gate rows
+  if (VARLEN) {
+    rwb.init(a, min(t0 + lane, a.T - 1));
+    rwm.init(a, t0);
+  }
   for (int t = t0 + lane; t < t1; t += 32) {  // beta while the first batches land
     const size_t i = (row0 + t) * a.H + h;
-    const int r = VARLEN ? out_row(a, t) : t;
+    const int r = VARLEN ? rwb(t) : t;
     stf(beta + (row0 + r) * a.H + h, sigmoidf_(ldf(bl + i)));
   }
   if (VARLEN && a.out_rows && lane == 0) {  // beta of the pad rows
@@ -466,7 +506,7 @@ __device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
         ld_row<CPL, Tin>(st + u * RB, lane, o);
 #pragma unroll
         for (int c = 0; c < CPL; ++c) o[c] = gate_fwd<FAST>(o[c] + bias[c], ea, a.g_min, a.gate_kind);
-        const int r = VARLEN ? out_row(a, tb + u) : tb + u;
+        const int r = VARLEN ? rwm(tb + u) : tb + u;
         stv<CPL>(g + static_cast<size_t>(r) * HD, o);
       }
     }
@@ -526,6 +566,8 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
   const int nbat = (hi - lo) / kBw + 1;
   // stage bi: the input rows base - NX - u (the window's next rows), then the
   // cotangent rows base - u, u < kBw, base = hi - bi kBw
+  RowWalk<false> rwf;  // rows of the cotangent tokens the fills walk down
+  if (VARLEN) rwf.init(a, max(hi, 0));
   auto fill = [&](int bi) {
     const int base = hi - bi * kBw;
     unsigned char* st = ring + (bi % kBwStages) * STG;
@@ -535,7 +577,7 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     });
     int rw[kBw];  // cotangent row of token base - u
 #pragma unroll
-    for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && base - u >= 0 ? out_row(a, base - u) : base - u;
+    for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && base - u >= 0 ? rwf(base - u) : base - u;
     ring_fill<RBY, kBw>(st + kBw * RBX, lane, dyh, [&](int r) -> const void* {
       const int t = base - r;
       const int row = r == 0 ? rw[0] : r == 1 ? rw[1] : r == 2 ? rw[2] : rw[3];
@@ -717,6 +759,11 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
   for (int c = 0; c < CPL; ++c) bias[c] = a.b_gate ? a.b_gate[ch + c] : 0.f;
   const float ea = __expf(a.A[h]);
   const int nbat = (t1 - t0 + kBw - 1) / kBw;
+  RowWalk<true> rwf, rwb;  // rows of the cotangent tokens the fills walk up, of this lane's beta tokens
+  if (VARLEN) {
+    rwf.init(a, t0);
+    rwb.init(a, min(t0 + lane, a.T - 1));
+  }
   auto fill = [&](int bi) {
     const int tb = t0 + bi * kBw;
     unsigned char* st = ring + (bi % kBwStages) * STG;
@@ -725,7 +772,7 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
     });
     int rw[kBw];  // cotangent row of token tb + u
 #pragma unroll
-    for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && tb + u < t1 ? out_row(a, tb + u) : tb + u;
+    for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && tb + u < t1 ? rwf(tb + u) : tb + u;
     ring_fill<RBY, kBw>(st + kBw * RBX, lane, dgh, [&](int r) -> const void* {
       const int row = r == 0 ? rw[0] : r == 1 ? rw[1] : r == 2 ? rw[2] : rw[3];
       return tb + r < t1 ? dgh + static_cast<size_t>(row) * HD : nullptr;
@@ -742,7 +789,7 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
   for (int t = t0 + lane; t < t1; t += 32) {  // beta while the first batches land
     const size_t i = (row0 + t) * a.H + h;
     const float s = sigmoidf_(ldf(bl + i));
-    const int r = VARLEN ? out_row(a, t) : t;
+    const int r = VARLEN ? rwb(t) : t;
     stf(dbl + i, ldf(dbt + (row0 + r) * a.H + h) * s * (1.f - s));
   }
   for (int bi = 0; bi < nbat; ++bi) {

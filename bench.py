@@ -306,6 +306,7 @@ def run_b200(args):
         extra["mixer_kernels"] = run_mixer_kernels(torch, dev, peaks)
         extra["mixer_cfg5"] = run_mixer_layer(torch, dev, peaks)
         extra["mixer_cfg5_strong_decay"] = run_mixer_layer(torch, dev, peaks, gate_bias="zero")
+        extra["mixer_decode"] = run_mixer_decode(torch, dev)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(sample_heads=args.cpu_heads, cfg=cfg)
@@ -547,6 +548,37 @@ def run_mixer_layer(torch, dev, peaks, steps=3, warmup=2, gate_bias="dt"):
     torch.cuda.empty_cache()
     return {"workload": f"cfg5 KDA mixer layer fwd+bwd, 16 packed seqs, T=65536, d_model=2048, H=16, gate bias {gate_bias}",
             "ms_per_step": ms, "tokens/s": 65536 / (ms / 1e3), "steps": steps}
+
+
+def run_mixer_decode(torch, dev, steps=32, warmup=4):
+    """Streaming generation through the layer cache at cfg4's batch: 256
+    sequences, cfg5's layer (d_model=2048, H=16, dk=dv=128, conv K=4, softplus
+    gate), prompts of 256 tokens prefilled, then one token per sequence per
+    step (six projection GEMMs, the fused decode kernel, W_o)."""
+    from axiom_b200 import layer
+
+    N, d_model, H = 256, 2048, 16
+    p = layer.init_params(d_model, H, 128, 128, rank=128, K=4, gate_kind="softplus", dtype=torch.bfloat16,
+                          device=dev, seed=7)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    prompts = torch.randn(N, 256, d_model, generator=gen, device=dev).to(torch.bfloat16)
+    toks = torch.randn(steps + warmup, N, d_model, generator=gen, device=dev).to(torch.bfloat16)
+    _, cache = layer.kda_layer_prefill(p, prompts, H=H)
+    for i in range(warmup):
+        layer.kda_layer_decode(p, toks[i], cache, H=H)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(warmup, warmup + steps):
+        layer.kda_layer_decode(p, toks[i], cache, H=H)
+    e.record()
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1e3 / steps
+    del p, prompts, toks, cache
+    torch.cuda.empty_cache()
+    return {"workload": "layer decode via the cache: 256 seqs, d_model=2048, H=16, 1 token per seq per step",
+            "us_per_step": us, "tokens/s": N / (us / 1e6), "steps": steps}
 
 
 def run_prefill(torch, KD, dev, peaks, steps=5, warmup=3):
