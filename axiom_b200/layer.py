@@ -48,6 +48,33 @@ class KDALayerParams:
         return [getattr(self, f.name) for f in fields(self)]
 
 
+class _Projections(torch.autograd.Function):
+    """``x @ W`` for several weights sharing the input ``x``.  The backward
+    accumulates ``dx = sum_i dY_i W_i^T`` inside the GEMMs (``addmm_``, beta =
+    1) instead of one GEMM per weight plus an elementwise add each."""
+
+    @staticmethod
+    def forward(ctx, x, *Ws):
+        ctx.save_for_backward(x, *Ws)
+        return tuple(x @ W for W in Ws)
+
+    @staticmethod
+    def backward(ctx, *dYs):
+        x, *Ws = ctx.saved_tensors
+        dx = None
+        if ctx.needs_input_grad[0]:
+            for dY, W in zip(dYs, Ws):
+                if dY is None:
+                    continue
+                if dx is None:
+                    dx = dY @ W.t()
+                else:
+                    dx.addmm_(dY, W.t())
+        dWs = [(x.t() @ dY) if (dY is not None and ctx.needs_input_grad[1 + i]) else None
+               for i, dY in enumerate(dYs)]
+        return (dx, *dWs)
+
+
 def init_params(d_model, H, dk, dv, *, rank=128, K=4, gate_kind="softplus", gate_bias="dt",
                 dtype=torch.bfloat16, device="cuda", seed=0) -> KDALayerParams:
     """Random-init weights: projections N(0, 0.02) (the reference's ``_rand``
@@ -96,10 +123,8 @@ def kda_layer(p: KDALayerParams, x, *, H, cu_seqlens=None, gate_kind="softplus",
     dk = p.W_q.shape[1] // H
     dv = p.W_v.shape[1] // H
     # projections (_project, net/kda.py:157-191)
-    qp, kp, vp = x @ p.W_q, x @ p.W_k, x @ p.W_v
-    z = (x @ p.W_a_down) @ p.W_a_up
-    bl = x @ p.W_beta
-    gl = x @ p.W_g
+    qp, kp, vp, zd, bl, gl = _Projections.apply(x, p.W_q, p.W_k, p.W_v, p.W_a_down, p.W_beta, p.W_g)
+    z = zd @ p.W_a_up
     if cu_seqlens is None:
         q, k, v, g, beta = mixer.kda_prologue(qp[None], kp[None], vp[None], z[None], bl[None], p.conv_q, p.conv_k,
                                               p.conv_v, p.A, H=H, b_gate=p.b_gate, g_min=g_min,
