@@ -146,3 +146,52 @@ def test_prologue_writes_the_packed_layout_and_gate_reads_it():
     for s in range(len(LENS)):
         pad[rows[s]:rows[s] + LENS[s]] = False
     assert np.all(do_np[0][pad] == 0.0)
+
+
+@pytest.mark.parametrize("n_seqs", [40, 300])
+def test_varlen_many_sequences_any_order(n_seqs):
+    """Many packed sequences with repeated lengths (ties) and empty ones: the
+    per-sequence kernels take them longest first when there are at most 256,
+    in order otherwise; every sequence must still equal the oracle run alone.
+    O, S_T and dS0 are compared per sequence; the token gradients over all
+    sampled sequences together (the bound's scale is the tensor's: a 1-token
+    sequence with no state cotangent has dv = beta (q.k) do, whose score carries
+    the bf16-operand rounding of q.k, ~1 % of a small number)."""
+    from axiom_b200 import kda as KD
+
+    H, dk, dv, chunk = 1, 128, 128, 64
+    rng = np.random.default_rng(n_seqs)
+    lens = rng.choice([0, 1, 17, 64, 65, 130], size=n_seqs).tolist()
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    n_tok = int(cu[-1])
+    x = K.make_inputs(1, n_tok, H, dk, dv, seed=n_seqs, s0_std=None)
+    x = {k: (K.bf16_round(v) if k != "S0" else v) for k, v in x.items()}
+    S0 = (rng.standard_normal((n_seqs, H, dk, dv)) * 0.05).astype(np.float32)
+    offs, rows, T_pad = KD.packing(cu.tolist(), chunk)
+    t = {k: torch.as_tensor(_pack(x[k][0], cu, rows, T_pad)[None]).to(DEV).to(torch.bfloat16).contiguous()
+         for k in ("q", "k", "v", "g", "beta")}
+    do_np = K.bf16_round(rng.standard_normal((n_tok, H, dv)).astype(np.float32))
+    do_t = torch.as_tensor(_pack(do_np, cu, rows, T_pad)[None]).to(DEV).to(torch.bfloat16).contiguous()
+    o, s_t, ckpt = KD.kda_fwd_varlen(t["q"], t["k"], t["v"], t["g"], t["beta"], offs, torch.as_tensor(S0).to(DEV),
+                                     chunk=chunk, o_dtype=torch.float32, need_ckpt=True)
+    grads = KD.kda_bwd_varlen(t["q"], t["k"], t["v"], t["g"], t["beta"], ckpt, do_t, offs, None, chunk=chunk)
+    o_np = o[0].float().cpu().numpy()
+    g_np = [g_[0].float().cpu().numpy() for g_ in grads[:5]]
+    ds0 = grads[5].cpu().numpy()
+    got_rows = {n: [] for n in ("dq", "dk", "dv", "dg", "dbeta")}
+    ref_rows = {n: [] for n in got_rows}
+    for s in rng.choice(n_seqs, size=min(n_seqs, 24), replace=False):
+        a, b = int(cu[s]), int(cu[s + 1])
+        r0 = rows[s]
+        xs = [x[k][:, a:b] for k in ("q", "k", "v", "g", "beta")]
+        ref_o, ref_s = K.chunk_fwd(*xs, S0[s][None], chunk=chunk)
+        assert K.scale_rel_err(s_t[s].cpu().numpy(), ref_s[0]) <= 1e-2, ("S_T", s)
+        ref = K.chunk_bwd(*xs, S0[s][None], do_np[a:b][None], None, chunk=chunk)
+        assert K.scale_rel_err(ds0[s], ref[5][0]) <= 1e-2, ("dS0", s)
+        if b > a:
+            assert K.scale_rel_err(o_np[r0:r0 + b - a], ref_o[0]) <= 1e-2, ("o", s)
+            for name, gg, rf in zip(got_rows, g_np, ref[:5]):
+                got_rows[name].append(gg[r0:r0 + b - a])
+                ref_rows[name].append(rf[0])
+    for name in got_rows:
+        assert K.scale_rel_err(np.concatenate(got_rows[name]), np.concatenate(ref_rows[name])) <= 1e-2, name
