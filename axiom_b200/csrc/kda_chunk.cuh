@@ -257,6 +257,106 @@ static __device__ __noinline__ void scores_exact_prep(unsigned char* sq, unsigne
   fence_async_smem();  // generic writes -> the tensor core's reads
 }
 
+// Scores for chunks whose summed decay passes the single anchor's budget while
+// each 32-token half stays within it (per channel: -G_31 <= 80 and
+// G_31 - G_63 <= 80).  Half J is anchored at A_0 = 0 (before the chunk) and
+// A_1 = G_31 (before token 32):
+//   pairs inside half J:           exp(G_r - G_i) = exp(G_r - A_J) exp(A_J - G_i)
+//   r in half 1, i in half 0:      exp(G_r - G_31) exp(G_31 - G_i), both <= 1,
+// so two tensor-core products give every pair with no exact exponentials:
+// D_diag = [q a ; k a] bd^T (N = 64) and D_cross = [q a ; k a] bc^T (N = 32),
+// a_r = exp(G_r - A_J(r)) <= 1, bd_i = k_i exp(A_J(i) - G_i) <= exp(80),
+// bc_i = k_i exp(G_31 - G_i) <= 1 (i < 32).
+__device__ __forceinline__ bool halves_within_budget(const float* Gf) {  // this thread's channel
+  const int d = threadIdx.x;
+  if (d >= DK) return true;
+  const float g31 = Gf[gsw(31, d)], g63 = Gf[gsw(63, d)];
+  return -g31 <= kExpBudget && g31 - g63 <= kExpBudget;
+}
+
+// Operands of the two-half scores: q a -> sq, k a -> sk (in place, the 128-row A
+// operand), bd -> CM [64][128], bc -> CM [32][128].  Inputs: raw q, k (sq, sk)
+// and G (fp32, gsw layout).
+static __device__ __noinline__ void scores_halves_prep(unsigned char* sq, unsigned char* sk, unsigned char* bd,
+                                                       unsigned char* bc, const float* Gf) {
+  for (int idx = threadIdx.x; idx < C * (DK / 8); idx += NT) {
+    // eight consecutive threads take the eight rows of one core matrix; warps are
+    // uniform in the half
+    const int t = ((idx >> 7) << 3) + (idx & 7), d8 = ((idx >> 3) & 15) * 8, J = t >> 5;
+    const uint32_t off = cm_off(t, d8, DK);
+    float qv[8], kv[8], gt[8], ga[8], o1[8], o2[8];
+    unpack_bf16x8(ld16(sq, off), qv);
+    unpack_bf16x8(ld16(sk, off), kv);
+    ld8g(Gf, t, d8, gt);
+    if (J) {
+      ld8g(Gf, 31, d8, ga);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ga[e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float av = __expf(fminf(gt[e] - ga[e], 0.f));
+      o1[e] = qv[e] * av;
+      o2[e] = kv[e] * av;
+    }
+    st16(sq, off, pack_bf16x8(o1));
+    st16(sk, off, pack_bf16x8(o2));
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o1[e] = kv[e] * __expf(ga[e] - gt[e]);
+    st16(bd, off, pack_bf16x8(o1));
+    if (!J) {
+      ld8g(Gf, 31, d8, ga);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o2[e] = kv[e] * __expf(fminf(ga[e] - gt[e], 0.f));
+      st16(bc, off, pack_bf16x8(o2));
+    }
+  }
+  fence_async_smem();  // generic writes -> the tensor core's reads
+}
+
+// Issue (one thread): D_diag -> columns [0, 64), D_cross -> [64, 96).
+__device__ __forceinline__ void scores_halves_mma(uint32_t tmem, uint32_t a_qk, uint32_t bd, uint32_t bc) {
+  const uint32_t id64 = idesc_bf16(128, 64, false, false), id32 = idesc_bf16(128, 32, false, false);
+#pragma unroll
+  for (int ks = 0; ks < DK / 16; ++ks)
+    mma_bf16(tmem, desc_kmajor(a_qk + ks * 256, DK), desc_kmajor(bd + ks * 256, DK), id64, ks > 0);
+#pragma unroll
+  for (int ks = 0; ks < DK / 16; ++ks)
+    mma_bf16(tmem + 64, desc_kmajor(a_qk + ks * 256, DK), desc_kmajor(bc + ks * 256, DK), id32, ks > 0);
+}
+
+// TMEM -> Aq (lanes 0..63) / Akk (lanes 64..127), masked (i <= r, i < r).  Warp w
+// takes TMEM lanes 32 (w % 4) .. +31 (one half of the rows) and the columns of
+// half w / 4: the same half comes from D_diag, half 0 under rows of half 1 from
+// D_cross, half 1 above rows of half 0 is zero.
+__device__ __forceinline__ void scores_halves_epilogue(uint32_t tmem, float* Aq, float* Akk) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qw = warp & 3, hh = warp >> 2;
+  const int R = 32 * qw + lane, r = R & 63, Jr = qw & 1;
+  const bool is_q = R < 64;
+  float* dst = is_q ? Aq : Akk;
+  const uint32_t tl = static_cast<uint32_t>(32 * qw) << 16;
+  float vals[32];
+  if (hh == Jr || hh == 0) {
+    tmem_ld32(tmem + tl + (hh == Jr ? 32 * hh : 64), vals);
+    tmem_wait_ld();
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) vals[j] = 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const int i0 = hh * 32 + j;
+    float4 w4;
+    w4.x = (is_q ? (i0 + 0 <= r) : (i0 + 0 < r)) ? vals[j + 0] : 0.f;
+    w4.y = (is_q ? (i0 + 1 <= r) : (i0 + 1 < r)) ? vals[j + 1] : 0.f;
+    w4.z = (is_q ? (i0 + 2 <= r) : (i0 + 2 < r)) ? vals[j + 2] : 0.f;
+    w4.w = (is_q ? (i0 + 3 <= r) : (i0 + 3 < r)) ? vals[j + 3] : 0.f;
+    *reinterpret_cast<float4*>(dst + sw64(r, i0)) = w4;
+  }
+  tc_fence_before();  // the TMEM reads precede later MMAs into these columns
+}
+
 // Column of kbm_I's products in the score TMEM block: I = 1, 2, 3 -> 0, 16, 48.
 __device__ __forceinline__ int exact_col(int I) { return 8 * I * (I - 1); }
 

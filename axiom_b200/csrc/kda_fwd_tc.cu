@@ -332,25 +332,43 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         scores_epilogue(T_D, Aq, Akk);
         KDA_PT(0, 3);
       } else {
-        // exact scores (strong decay: the single anchor would overflow): 16-token
-        // block anchors, block pairs on the tensor cores, pairs inside a block exact
+        // past the single anchor's budget: two-half anchors on the tensor cores while
+        // each half is within it, else exact scores (16-token block anchors, block
+        // pairs on the tensor cores, pairs inside a block exact)
         fence_async_smem();
         __syncthreads();
         if (tid == kIoThread) store_prep(true);
-        // kbm_1 (4 KB), kbm_2 (8 KB), kbm_3 (12 KB) in A3 rows 0..63 (W comes later) and VT
-        unsigned char *kbm1 = A3 + 12288, *kbm2 = sm + OFF_VT, *kbm3 = A3;
-        scores_exact_prep(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, kbm1, kbm2, kbm3, Gf, Aq, Akk);
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-          tc_fence_after();
-          scores_exact_mma(T_D, smem_u32(sm + OFF_SQ), smem_u32(kbm1), smem_u32(kbm2), smem_u32(kbm3));
-          mma_commit(mbar);
+        const bool halves = __syncthreads_or(!halves_within_budget(Gf)) == 0;
+        if (halves) {
+          unsigned char *bd = A3, *bc = sm + OFF_VT;  // A3 rows 0..63 (W comes later), VT
+          scores_halves_prep(sm + OFF_SQ, sm + OFF_SK, bd, bc, Gf);
+          tc_fence_before();
+          __syncthreads();
+          if (tid == 0) {
+            tc_fence_after();
+            scores_halves_mma(T_D, smem_u32(sm + OFF_SQ), smem_u32(bd), smem_u32(bc));
+            mma_commit(mbar);
+          }
+          failed |= !mma_wait();
+          if (__syncthreads_or(failed)) break;
+          KDA_PT(0, 2);
+          scores_halves_epilogue(T_D, Aq, Akk);
+        } else {
+          // kbm_1 (4 KB), kbm_2 (8 KB), kbm_3 (12 KB) in A3 rows 0..63 (W comes later) and VT
+          unsigned char *kbm1 = A3 + 12288, *kbm2 = sm + OFF_VT, *kbm3 = A3;
+          scores_exact_prep(sm + OFF_SQ, sm + OFF_SK, sm + OFF_SG, kbm1, kbm2, kbm3, Gf, Aq, Akk);
+          tc_fence_before();
+          __syncthreads();
+          if (tid == 0) {
+            tc_fence_after();
+            scores_exact_mma(T_D, smem_u32(sm + OFF_SQ), smem_u32(kbm1), smem_u32(kbm2), smem_u32(kbm3));
+            mma_commit(mbar);
+          }
+          failed |= !mma_wait();
+          if (__syncthreads_or(failed)) break;
+          KDA_PT(0, 2);
+          scores_exact_epilogue(T_D, Aq, Akk);
         }
-        failed |= !mma_wait();
-        if (__syncthreads_or(failed)) break;
-        KDA_PT(0, 2);
-        scores_exact_epilogue(T_D, Aq, Akk);
         __syncthreads();
         if (c + 1 < c_end) {
           stage(c + 1, true);

@@ -66,7 +66,9 @@ def make_inputs(B, T, H, dk, dv, seed=0, s0_std=None, decay="baseline"):
     beta = sigmoid(N(0,1)); g = logsigmoid(N(3,1)) per key channel
     (``decay="strong"``: g = -5 sigmoid(3 N(0,1)), the reference's
     strong-decay test range ``net/tests/test_kda_chunked_cc.py:231``;
-    ``decay="medium"``: g = -sigmoid(2 N(0,1))).
+    ``decay="medium"``: g = -sigmoid(2 N(0,1)); ``decay="half_budget"``:
+    g = -(1.6 + 0.4 sigmoid(N(0,1))), so a 64-token chunk sums past 80 while
+    each 32-token half stays below it).
     S0 ~ N(0, s0_std) or zeros.  Returns float32 arrays.
     """
     rng = np.random.default_rng(seed)
@@ -83,6 +85,8 @@ def make_inputs(B, T, H, dk, dv, seed=0, s0_std=None, decay="baseline"):
         g = -5.0 / (1.0 + np.exp(-3.0 * z))
     elif decay == "medium":
         g = -1.0 / (1.0 + np.exp(-2.0 * rng.standard_normal((B, T, H, dk))))
+    elif decay == "half_budget":
+        g = -(1.6 + 0.4 / (1.0 + np.exp(-rng.standard_normal((B, T, H, dk)))))
     else:
         raise ValueError(f"unknown decay {decay!r}")
     if s0_std is None:

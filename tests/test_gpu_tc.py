@@ -36,7 +36,8 @@ def _bf16_inputs(B, T, H, seed, s0_std=None, decay="baseline"):
     (2, 512, 4, 0.02, "baseline"),    # config-2 distributions at reduced size
     (1, 200, 2, 0.1, "baseline"),     # ragged tail
     (1, 5, 3, 0.1, "baseline"),       # shorter than one chunk
-    (1, 256, 2, 0.1, "strong"),       # strong decay: exact CUDA-core score path
+    (1, 256, 2, 0.1, "strong"),       # strong decay: exact score path (16-token block anchors)
+    (1, 320, 2, 0.1, "half_budget"),  # chunk sums past 80, halves below: two-half anchored scores
     (1, 320, 2, 0.0, "medium"),
 ])
 def test_tc_forward_matches_oracle(B, T, H, s0, decay):
@@ -70,7 +71,7 @@ def test_tc_forward_bf16_output_and_repeatability():
     assert K.scale_rel_err(_np(o1), o_ref) <= TOL
 
 
-@pytest.mark.parametrize("T,decay", [(256, "baseline"), (130, "strong")])
+@pytest.mark.parametrize("T,decay", [(256, "baseline"), (130, "strong"), (200, "half_budget")])
 def test_tc_training_step_matches_oracle(T, decay):
     from axiom_b200 import chunk_kda
 
