@@ -607,8 +607,9 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       mma_run(tab, F_SD, NF_SD);
       KDA_PT(2, 22);
     }
-    {  // dGam_C partial sums: sum_j S_c[d][j] dS'[d][j]  (under the S_c MMAs; both only read)
-      const int d = tid >> 1, j0 = (tid & 1) * 64;
+    {  // dGam_C partial sums: sum_j S_c[d][j] dS'[d][j]  (under the S_c MMAs; both only read);
+       // eight consecutive threads read eight rows of one core matrix (conflict-free)
+      const int d = tid & 127, j0 = (tid >> 7) * 64;
       float acc = 0.f;
       for (int j = j0; j < j0 + 64; j += 8) {
         float a[8], bb[8];
