@@ -176,3 +176,32 @@ def test_tc_backward_is_bitwise_repeatable():
         again = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, do, dST)
         for name, a, b in zip(GRADS, first, again):
             assert torch.equal(a, b), name
+
+
+@pytest.mark.parametrize("decay", ["baseline", "strong"])
+def test_tc_fp32_checkpoint_states(decay):
+    """The chunk-boundary states stored in fp32 (ckpt_dtype=float32) instead of
+    their bf16 operand images: the backward reads them row-major and builds its
+    operands itself.  Gradients against the oracle, at the bf16 bar."""
+    from axiom_b200 import kda_bwd, kda_fwd
+    from axiom_b200.kda import ckpt_states
+
+    B, T, H = 1, 192, 2
+    xr, d = _bf16_inputs(B, T, H, seed=51, s0_std=0.05, decay=decay)
+    rng = np.random.default_rng(52)
+    do = K.bf16_round(rng.standard_normal((B, T, H, 128)))
+    dST = rng.standard_normal((B, H, 128, 128)).astype(np.float32)
+    o, s_t, ckpt = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], need_ckpt=True,
+                           ckpt_dtype=torch.float32, o_dtype=torch.float32)
+    grads = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, _dev(do, torch.bfloat16),
+                    _dev(dST, torch.float32))
+    torch.cuda.synchronize()
+    o_ref, s_ref, states = K.chunk_fwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], chunk=64,
+                                       return_states=True, tile=None)
+    assert K.scale_rel_err(_np(o), o_ref) <= TOL
+    assert ckpt.dtype == torch.float32
+    st = _np(ckpt_states(ckpt, B, T, H, 128, 128, chunk=64))
+    assert K.scale_rel_err(st, states) <= TOL
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64, tile=None)
+    for name, gr, rf in zip(GRADS, grads, ref):
+        assert K.scale_rel_err(_np(gr), rf) <= TOL, name
