@@ -205,3 +205,34 @@ def test_tc_fp32_checkpoint_states(decay):
     ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64, tile=None)
     for name, gr, rf in zip(GRADS, grads, ref):
         assert K.scale_rel_err(_np(gr), rf) <= TOL, name
+
+
+def test_tc_mixed_decay_regimes_in_one_call():
+    """Heads in one launch on three score paths at once: head 0 within the single
+    anchor's budget, head 1 past it with each 32-token half within it (two-half
+    anchors), head 2 past both (16-token block anchors).  Forward and backward
+    against the direct-ratio oracle."""
+    from axiom_b200 import kda_bwd, kda_fwd
+
+    B, T = 1, 256
+    parts = [K.make_inputs(B, T, 1, 128, 128, seed=61 + i, s0_std=0.05, decay=dcy)
+             for i, dcy in enumerate(("baseline", "half_budget", "strong"))]
+    x = {k: np.concatenate([p_[k] for p_ in parts], axis=2 if k != "S0" else 1) for k in parts[0]}
+    xr = {k: (K.bf16_round(v) if k != "S0" else v) for k, v in x.items()}
+    d = {k: _dev(v, torch.bfloat16 if k != "S0" else torch.float32) for k, v in x.items()}
+    rng = np.random.default_rng(64)
+    do = K.bf16_round(rng.standard_normal((B, T, 3, 128)))
+    dST = rng.standard_normal((B, 3, 128, 128)).astype(np.float32)
+    o, s_t, ckpt = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], need_ckpt=True,
+                           o_dtype=torch.float32)
+    grads = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, _dev(do, torch.bfloat16),
+                    _dev(dST, torch.float32))
+    torch.cuda.synchronize()
+    o_ref, s_ref = K.chunk_fwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], chunk=64, tile=None)
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64, tile=None)
+    for h in range(3):
+        assert K.scale_rel_err(_np(o)[:, :, h], o_ref[:, :, h]) <= TOL, ("o", h)
+        assert K.scale_rel_err(_np(s_t)[:, h], s_ref[:, h]) <= TOL, ("S_T", h)
+        for name, gr, rf in zip(GRADS, grads, ref):
+            g_, r_ = (_np(gr)[:, h], rf[:, h]) if name == "dS0" else (_np(gr)[:, :, h], rf[:, :, h])
+            assert K.scale_rel_err(g_, r_) <= TOL, (name, h)
