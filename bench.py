@@ -196,6 +196,9 @@ def pci_bus_id(torch, index):
 
 
 def make_train_inputs(torch, cfg, seed, device):
+    """BASELINE's distributions; ``cfg["decay"]`` (profiling cases only) swaps g for
+    per-token decays in [1.6, 2.0] ("half_budget": chunk sums past the single
+    anchor's 80, halves within it) or 11 sigmoid(3 N(0,1)) ("strong")."""
     B, T, H, dk, dv = cfg["B"], cfg["T"], cfg["H"], cfg["dk"], cfg["dv"]
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
@@ -208,6 +211,11 @@ def make_train_inputs(torch, cfg, seed, device):
     k = torch.nn.functional.normalize(normal(B, T, H, dk), dim=-1).to(bf)
     v = normal(B, T, H, dv).to(bf)
     g = torch.nn.functional.logsigmoid(normal(B, T, H, dk) + 3.0).to(bf)
+    decay = cfg.get("decay", "baseline")
+    if decay == "half_budget":
+        g = (-(1.6 + 0.4 * torch.sigmoid(g.float()))).to(bf)
+    elif decay == "strong":
+        g = (-11.0 * torch.sigmoid(3.0 * normal(B, T, H, dk))).to(bf)
     beta = torch.sigmoid(normal(B, T, H)).to(bf)
     do = normal(B, T, H, dv).to(bf)
     return q, k, v, g, beta, do
@@ -238,6 +246,8 @@ def run_b200(args):
     for key, val in (("B", args.batch), ("T", args.seqlen), ("H", args.heads)):
         if val:
             cfg[key] = val
+    if args.decay != "baseline":
+        cfg["decay"] = args.decay
     B, T, H, dk, dv, C = (cfg[k] for k in ("B", "T", "H", "dk", "dv", "chunk"))
     n_chunks = (T + C - 1) // C
     q, k, v, g, beta, do = make_train_inputs(torch, cfg, seed=1234 + rank, device=dev)
@@ -326,7 +336,7 @@ def run_b200(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (BASELINE distributions, seeded per rank)",
-            "config": {"workload": "cfg3 KDA chunked fwd+bwd" if cfg == CFG3 else "reduced profiling case", "B_per_rank": B, "T": T, "H": H,
+            "config": {"workload": "cfg3 KDA chunked fwd+bwd" if cfg == CFG3 else "reduced profiling case", "decay": cfg.get("decay", "baseline"), "B_per_rank": B, "T": T, "H": H,
                        "dk": dk, "dv": dv, "chunk": C, "global_batch": B * world,
                        "parallelism": f"batch-sharded x{world}, no collective",
                        "l2": "inputs larger than L2 (no flush)",
@@ -678,6 +688,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override B per rank (profiling cases)")
     ap.add_argument("--seqlen", type=int, default=0, help="override T (profiling cases)")
     ap.add_argument("--heads", type=int, default=0, help="override H (profiling cases)")
+    ap.add_argument("--decay", choices=["baseline", "half_budget", "strong"], default="baseline",
+                    help="log-decay distribution (profiling cases; the headline is baseline)")
     ap.add_argument("--mixer-only", action="store_true",
                     help="time only the mixer kernels (prologue, output gate, fused decode); --batch sets B")
     args = ap.parse_args()
