@@ -37,15 +37,23 @@ def _sources():
     return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
 
 
+def _headers():
+    """Every header a source can include: csrc/*.cuh|*.h and include/*.h."""
+    out = []
+    for d in (CSRC, INCLUDE):
+        out += sorted(os.path.join(d, f) for f in os.listdir(d) if f.endswith((".cuh", ".h")))
+    return out
+
+
 def _digest(path: str, extra: str) -> str:
+    """Object key: the source, every header (an edit to any of them rebuilds) and the flags."""
     h = hashlib.sha256(extra.encode())
     with open(path, "rb") as f:
         h.update(f.read())
-    for hdr in sorted(os.listdir(CSRC)) + ["kda_b200.h"]:
-        p = os.path.join(CSRC, hdr) if hdr != "kda_b200.h" else os.path.join(INCLUDE, hdr)
-        if p.endswith((".cuh", ".h")) and os.path.exists(p):
-            with open(p, "rb") as f:
-                h.update(f.read())
+    for p in _headers():
+        h.update(os.path.basename(p).encode())
+        with open(p, "rb") as f:
+            h.update(f.read())
     return h.hexdigest()[:16]
 
 

@@ -146,7 +146,6 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     tmem_wait_st();
   }
 
-  KDA_PT_INIT();
   for (int c = c_end - 1; c >= c_beg; --c) {
     const int p = c & 1;
     cp_async_wait<0>();
@@ -156,11 +155,9 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     if (tid == kIoThread) bulk_wait_read();  // SB may be rewritten: the previous dS' image is stored
     if (tid < C) beta_s[tid] = bf16_raw_to_float(beta_nx);
     if (__syncthreads_or(failed)) break;
-    KDA_PT(1, 0);
     const float* gamC = reinterpret_cast<const float*>(sm + set_gc(p));
     const uint32_t set = smem_u32(sm + p * Q_SET);
     if (c > c_beg) issue_chunk(c - 1);  // the other set was last read by chunk c + 1
-    KDA_PT(1, 1);
     {  // dS' pass: bf16 operand (stored to the workspace below), then dS *= Gam_C
       const int d = 32 * qw + lane;
       const float gcd = gamC[d];
@@ -177,7 +174,6 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
       }
       tmem_wait_st();
     }
-    KDA_PT(1, 4);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -206,7 +202,6 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
-    KDA_PT(1, 5);
     {  // -dU^T -> bf16 [j][c] (TP region)
       const int j = 32 * qw + lane;
       float vals[32];
@@ -232,7 +227,6 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
-    KDA_PT(1, 6);
   }
   if (!failed && ds0) {
     const int d = 32 * qw + lane;
@@ -254,7 +248,6 @@ bwd_seq_kernel(const bf16* __restrict__ beta, const bf16* __restrict__ dout,
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);
-  KDA_PT_FLUSH(1);
 }
 
 // ===========================================================================
@@ -514,7 +507,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   unsigned short beta_nx = 0;  // raw bf16 of the next unit's beta (prefetch)
   if (blockIdx.x < n_units) issue_inputs(blockIdx.x, beta_nx);
 
-  KDA_PT_INIT();
   for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
     const int c = static_cast<int>(u % n_chunks);
     const long long bh = u / n_chunks;
@@ -550,18 +542,14 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     if (tid < C) beta_s[tid] = bf16_raw_to_float(beta_nx);
     if (tid < 128) dgc[tid] = 0.f;
     if (tid < 64) dbs[tid] = 0.f;
-    KDA_PT(2, 26);
     cp_async_wait<1>();
     failed |= !mbar_wait(mbar_fac, fac_par);
     fac_pending = false;
-    KDA_PT(2, 27);
     if (__syncthreads_or(failed)) break;
 
-    KDA_PT(2, 0);
     // ---- the forward's W, U and v~ are resident: straight to the adjoint ----
     const float* gamC = reinterpret_cast<const float*>(sm + P_GF + 544 * (it & 1));
     const bool slow = reinterpret_cast<const uint32_t*>(gamC)[128] != 0u;  // exact-path chunk
-    KDA_PT(2, 1);
     if constexpr (sizeof(Tc) == 4) stage_ckpt_f32(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
     cp_async_wait<0>();
     failed |= !mbar_wait(mbar_late, late_par);
@@ -569,20 +557,16 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     if (__syncthreads_or(failed)) break;
-    KDA_PT(2, 6);
     // dU^T = dS'^T (lam K)^T + dO^T Aqk ;  dKL^T = dS' v~^T
     if (tid == 0) {
       tc_fence_after();
       mma_run(tab, G_DU, N_DU);
       mma_commit(mbar);
       mma_run(tab, F_DU, NF_DU);
-      KDA_PT(2, 20);
     }
 
     failed |= !mma_wait();
-    KDA_PT(2, 21);
     if (__syncthreads_or(failed)) break;
-    KDA_PT(2, 7);
     {  // dU^T -> bf16 [j][c] (KL region)
       const int j = 32 * qw + lane;
       float vals[32];
@@ -598,14 +582,12 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     if (__syncthreads_or(failed)) break;
-    KDA_PT(2, 8);
     // S_c [dO^T | dU^T] -> (dO S^T)^T | (dU S^T)^T
     if (tid == 0) {
       tc_fence_after();
       mma_run(tab, G_SD, N_SD);
       mma_commit(mbar);
       mma_run(tab, F_SD, NF_SD);
-      KDA_PT(2, 22);
     }
     {  // dGam_C partial sums: sum_j S_c[d][j] dS'[d][j]  (under the S_c MMAs; both only read);
        // eight consecutive threads read eight rows of one core matrix (conflict-free)
@@ -621,9 +603,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       atomicAdd(&dgc[d], acc);
     }
     failed |= !mma_wait();
-    KDA_PT(2, 23);
     if (__syncthreads_or(failed)) break;
-    KDA_PT(2, 9);
     // dS' is dead (its last reader, the dKL^T filler, is done): restage g
     // (for the epilogue) over its upper half
     if (use_tma) {
@@ -651,7 +631,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    KDA_PT(2, 10);
     // Yw^T = dW^T T,  Yu^T = dU^T T
     if (tid == 0) {
       tc_fence_after();
@@ -661,7 +640,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
-    KDA_PT(2, 11);
     {  // Yw^T, Yu^T -> bf16 (SB region); beta_c Yw^T -> TMEM [64,128)
       const int d = 32 * qw + lane;
       float yw[32], yu[32];
@@ -681,18 +659,14 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    KDA_PT(2, 12);
     // dAqk = dO v~^T, dL~ = Yu U^T + Yw W^T   (M = 64)
     if (tid == 0) {
       tc_fence_after();
       mma_run(tab, G_DL, N_DL);
       mma_commit(mbar);
-      KDA_PT(2, 24);
     }
     failed |= !mma_wait();
-    KDA_PT(2, 25);
     if (__syncthreads_or(failed)) break;
-    KDA_PT(2, 13);
     // U, dO and dW^T are dead: restage v (and raw q, k for the exact path)
     if (use_tma) {
       if (tid == kIoThread) {
@@ -742,32 +716,27 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    KDA_PT(2, 14);
     if (!slow) {
       // [dQG^T | dKG^T] += KI^T [dAqk ; beta dL]^T ;  dKI^T = QG^T dAqk + KG^T (beta dL)
       if (tid == 0) {
         tc_fence_after();
         mma_run(tab, G_VII, N_VII);
         mma_commit(mbar);
-        KDA_PT(2, 29);
       }
       // channel-major copies for the epilogue: QG, KG -> SB (Yw^T, Yu^T are dead; the
       // MMAs only read QG, KG)
       transpose_cm<64, 128>(smem_u32(sm + P_SB), a3 + 64 * 256, warp, lane, NT / 32);
       transpose_cm<64, 128>(smem_u32(sm + P_SB + 16384), a3 + 128 * 256, warp, lane, NT / 32);
-      KDA_PT(2, 30);
       cp_async_wait<0>();
       if (use_tma) {
         failed |= !mbar_wait(mbar_rs, rs_par);
         rs_pending = false;
       }
       if (__syncthreads_or(failed)) break;
-      KDA_PT(2, 31);
       transpose_cm<64, 128>(smem_u32(sm + P_SQ), smem_u32(sm + P_SG), warp, lane, NT / 32);  // g
       transpose_cm<64, 128>(smem_u32(sm + P_SK), smem_u32(sm + P_V), warp, lane, NT / 32);   // v
       failed |= !mma_wait();
       if (__syncthreads_or(failed)) break;
-      KDA_PT(2, 19);
       transpose_cm<64, 128>(smem_u32(sm + P_SG), smem_u32(sm + P_KI), warp, lane, NT / 32);  // KI
       __syncthreads();
       // A3, KI, KL, V, TP, TB, AQB, AKB and the other Gam_C slot are free: stage the
@@ -782,7 +751,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       }
       if (__syncthreads_or(failed)) break;
     }
-    KDA_PT(2, 15);
     // ---- final epilogue: thread = channel d (lane), columns c in [32 hh, 32 hh + 32) ----
     {
       const int d = 32 * qw + lane;
@@ -872,7 +840,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
           }
         }
         __syncthreads();
-        KDA_PT(2, 2);
         // Score adjoints with 16-token block anchors (every exponent <= 0).  For
         // token r of block I and i of an earlier block: exp(G_r - G_i) =
         // exp(G_r - G_16I) exp(G_16I - G_i), so the row sums
@@ -927,7 +894,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        KDA_PT(2, 3);
         if (tid == 0) {
           tc_fence_after();
           const uint32_t kl = smem_u32(sm + P_KL), kb0 = smem_u32(kbm), qa0 = smem_u32(qa), ka0 = smem_u32(ka);
@@ -950,7 +916,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         }
         failed |= !mma_wait();
         if (__syncthreads_or(failed)) break;
-        KDA_PT(2, 4);
         float* dGs = reinterpret_cast<float*>(sm + P_SB);  // dG fp32 [64][128] (kbm is dead now)
         float run = pre;
 #pragma unroll 1
@@ -1049,9 +1014,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
       for (int jj = 0; jj < 32; ++jj) gsum += dG[jj];
       xch[(0 * 2 + hh) * 128 + d] = gsum;
       xch[(1 * 2 + hh) * 128 + d] = klsum;
-      KDA_PT(2, 16);
       __syncthreads();  // xch
-      KDA_PT(2, 17);
       const float dGC = xch[(1 * 2 + 0) * 128 + d] + xch[(1 * 2 + 1) * 128 + d] + gC * dgc[d];
       float acc = dGC + (hh == 0 ? xch[(0 * 2 + 1) * 128 + d] : 0.f);
       if (use_tma && !slow) {  // dg over g^T (consumed), channel-major
@@ -1096,11 +1059,9 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
         store_rows(dg + obase, sm + P_SQ, rows_valid, rstride);
       }
     }
-    KDA_PT(2, 18);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    KDA_PT(2, 28);
     if (tid < rows_valid)
       dbeta[(tok0 + tid) * H + h] =
           __float2bfloat16_rn(dbs[tid] + dbq[tid] + dbq[64 + tid] + dbq[128 + tid] + dbq[192 + tid]);
@@ -1120,7 +1081,6 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);
-  KDA_PT_FLUSH(2);
 }
 
 __device__ int g_bwd_tc_error = 0;

@@ -185,7 +185,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   fence_async_smem();
   __syncthreads();
 
-  KDA_PT_INIT();
   for (int c = c_beg; c < c_end; ++c) {
     const int t0 = c * C;
     const int rows_valid = min(C, T - t0);
@@ -200,7 +199,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       beta_nx = ld_bf16_raw(beta + (tok0 + t0 + C + tid) * H + h, tid < min(C, T - t0 - C));
     if (__syncthreads_or(failed)) break;
 
-    KDA_PT(0, 0);
     // ---------------- prep: G, exponentials, operand tiles ----------------
     float* Aq = reinterpret_cast<float*>(sm + OFF_SB);
     float* Akk = Aq + 4096;
@@ -306,7 +304,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         }
       }
       tc_fence_before();  // the TMEM reads above precede the score MMA's writes to T_D
-      KDA_PT(0, 1);
       if (!slow) {
         fence_async_smem();
         __syncthreads();
@@ -328,9 +325,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         }
         failed |= !mma_wait();
         if (__syncthreads_or(failed)) break;
-        KDA_PT(0, 2);
         scores_epilogue(T_D, Aq, Akk);
-        KDA_PT(0, 3);
       } else {
         // past the single anchor's budget: two-half anchors on the tensor cores while
         // each half is within it, else exact scores (16-token block anchors, block
@@ -351,7 +346,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
           }
           failed |= !mma_wait();
           if (__syncthreads_or(failed)) break;
-          KDA_PT(0, 2);
           scores_halves_epilogue(T_D, Aq, Akk);
         } else {
           // kbm_1 (4 KB), kbm_2 (8 KB), kbm_3 (12 KB) in A3 rows 0..63 (W comes later) and VT
@@ -366,7 +360,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
           }
           failed |= !mma_wait();
           if (__syncthreads_or(failed)) break;
-          KDA_PT(0, 2);
           scores_exact_epilogue(T_D, Aq, Akk);
         }
         __syncthreads();
@@ -382,9 +375,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       float* Tm = reinterpret_cast<float*>(sm + OFF_KI);
       if (tid == kIoThread) bulk_wait_read<1>();  // KI has been stored and may be overwritten
       __syncthreads();
-      KDA_PT(0, 12);
       solve_T(Akk, beta_s, Tm, reinterpret_cast<float*>(sm + OFF_VT));
-      KDA_PT(0, 4);
       // eight consecutive threads take eight rows of one column block: conflict-free
       // swizzled fp32 reads and core-matrix bf16 writes
       const int r = 8 * (tid >> 5) + (tid & 7), c0 = 16 * ((tid >> 3) & 3);
@@ -401,15 +392,12 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       st16(sm + OFF_TP, cm_off(r, c0, C), pack_bf16x8(v));            // T diag(beta)
       st16(sm + OFF_TP, cm_off(r, c0 + 8, C), pack_bf16x8(v + 8));
       // Akk bf16 for the checkpoint, over the fp32 Aqk just read (SB's first 16 KB)
-      KDA_PT(0, 16);
       __syncthreads();
-      KDA_PT(0, 17);
       if (fu) {
         st16(sm + OFF_SB, cm_off(r, c0, C), pack_bf16x8(kk));
         st16(sm + OFF_SB, cm_off(r, c0 + 8, C), pack_bf16x8(kk + 8));
       }
     }
-    KDA_PT(0, 13);
     fence_async_smem();
     __syncthreads();
     if (tid == kIoThread && fu) {  // T, Aqk (adjacent in VT) and Akk into the checkpoint
@@ -427,9 +415,7 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       mma_commit(mbar);
     }
     failed |= !mma_wait();
-    KDA_PT(0, 14);
     if (__syncthreads_or(failed)) break;
-    KDA_PT(0, 15);
     {  // P diag(beta) -> rows 64..127 of the [T b ; P b] operand
       float vals[32];
       tmem_ld32(T_P + t_lane + hh * 32, vals);
@@ -442,7 +428,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         for (int j = 0; j < 32; j += 8) st16(sm + OFF_TP, cm_off(64 + r, hh * 32 + j, C), pack_bf16x8(vals + j));
       }
     }
-    KDA_PT(0, 5);
     fence_async_smem();
     __syncthreads();
     // ---------------- MMA_wu: [Tb ; Pb] [K*Gam | V] ----------------
@@ -462,7 +447,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     if (tid == kIoThread) bulk_wait_read();  // Q Gam has been stored: E2 overwrites it with Q~
     if (__syncthreads_or(failed)) break;
     if (c + 1 < c_end) stage(c + 1, false);
-    KDA_PT(0, 6);
     // ---------------- E2: W -> A3[0:64), Q~ = Gam Q - Aqk W -> A3[64:128) ----------------
     {
       const int R = 32 * qw + lane;
@@ -487,7 +471,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         }
       }
     }
-    KDA_PT(0, 7);
     // ---------------- S pass: S_c -> bf16 operand (+ checkpoint), S *= Gam_C ----------------
     // A bf16 checkpoint entry is the operand image itself, stored below with one
     // bulk copy; an fp32 checkpoint is written row-major here.
@@ -513,7 +496,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    KDA_PT(0, 8);
     // ---------------- MMA_1: [W ; Q~] S ----------------
     if (tid == kIoThread && ((sizeof(Tc) == 2 && ck_unit) || fu)) {
       if (sizeof(Tc) == 2 && ck_unit) bulk_store(ck_unit, sm + OFF_SB, DK * DV * 2);
@@ -531,7 +513,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
-    KDA_PT(0, 9);
     // ---------------- E3: v~ = U - W S -> bf16 ; O = Q~ S + Aqk U -> global ----------------
     {
       const int R = 32 * qw + lane;
@@ -568,7 +549,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       bulk_store(fu + FAC_VT, sm + OFF_VT, 16384);
       bulk_commit();
     }
-    KDA_PT(0, 10);
     // ---------------- MMA_3: S += (lam K)^T v~ ----------------
     if (tid == 0) {
       tc_fence_after();
@@ -581,7 +561,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     }
     failed |= !mma_wait();
     if (__syncthreads_or(failed)) break;
-    KDA_PT(0, 11);
   }
 
   if (!failed && s_out) {
@@ -604,7 +583,6 @@ fwd_tc_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tbase, 512);
-  KDA_PT_FLUSH(0);
 }
 
 __device__ int g_fwd_tc_error = 0;

@@ -19,7 +19,11 @@
 //   are rejected with KDA_ERR_SCRATCH_LIMIT before anything is launched.
 // * The first call on a device looks up the device address of the array
 //   (cudaGetSymbolAddress, with that device current).  Make that first call
-//   before any stream capture on the device.
+//   before any stream capture on the device.  The address is cached for the
+//   life of the process and is valid for as long as the device's primary
+//   context lives: after cudaDeviceReset (or anything else that destroys that
+//   context) the cached address is stale, so such a process must not call this
+//   entry point again.
 // * Every call uses the same array.  Nothing in it needs to start at zero: the
 //   backward writes every scratch byte it reads earlier in the same call, so the
 //   leftovers of the previous call are harmless.  Two calls whose kernels

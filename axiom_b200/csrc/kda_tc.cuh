@@ -300,36 +300,3 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
 
 }  // namespace tc
 }  // namespace kda
-
-// Optional per-phase cycle counters for performance work: compiled only with
-// -DKDA_PHASE_TIMERS (never in the shipped library), in a single-translation-
-// unit build that defines `__device__ unsigned long long g_kda_phase[3][8][32]`
-// before including this header.  Lane 0 of each warp adds the cycles since its
-// previous mark to slot i of a shared-memory table (one shared load per mark,
-// so the counters barely perturb what they measure); KDA_PT_FLUSH copies CTA
-// 0's table to g_kda_phase[k] at the kernel's converged exit.
-#ifdef KDA_PHASE_TIMERS
-#define KDA_PT_INIT()                                                       \
-  __shared__ unsigned int kda_pt_sm_[8][32];                          \
-  for (int i_ = threadIdx.x; i_ < 256; i_ += blockDim.x) kda_pt_sm_[i_ >> 5][i_ & 31] = 0; \
-  __syncthreads();                                                          \
-  long long kda_pt_prev_ = clock64()
-#define KDA_PT(k, i)                                                        \
-  do {                                                                      \
-    const long long kda_pt_now_ = clock64();                                \
-    if ((threadIdx.x & 31) == 0)                                            \
-      kda_pt_sm_[threadIdx.x >> 5][i] += static_cast<unsigned int>(kda_pt_now_ - kda_pt_prev_); \
-    kda_pt_prev_ = kda_pt_now_;                                             \
-  } while (0)
-#define KDA_PT_FLUSH(k)                                                     \
-  do {                                                                      \
-    __syncthreads();                                                        \
-    if (blockIdx.x == 0)                                                    \
-      for (int i_ = threadIdx.x; i_ < 256; i_ += blockDim.x)                \
-        g_kda_phase[k][i_ >> 5][i_ & 31] += kda_pt_sm_[i_ >> 5][i_ & 31];   \
-  } while (0)
-#else
-#define KDA_PT_INIT() do {} while (0)
-#define KDA_PT(k, i) do {} while (0)
-#define KDA_PT_FLUSH(k) do {} while (0)
-#endif

@@ -39,10 +39,18 @@ CFG4 = dict(N=256 * 32, dk=128, dv=128)
 # backward adjoint 23.07 MFLOP (recompute excluded).
 FWD_FLOP_PER_CHUNK_HEAD = 11.62e6
 BWD_FLOP_PER_CHUNK_HEAD = 23.07e6
+# Algorithmic HBM bytes per chunk-head (64 tokens of one head, bf16 tensors, dk = dv = 128):
+# forward reads q, k, v, g (4 x 256 B per token) and beta (2 B), writes o (256 B) and
+# the bf16 boundary state the backward needs (128 x 128 x 2 B per chunk-head); the
+# backward reads q, k, v, g, dO, beta and that state, writes dq, dk, dv, dg, dbeta.
+ALGO_BYTES_PER_CHUNK_HEAD = {
+    "kda_fwd": 64 * (4 * 256 + 2 + 256) + 128 * 128 * 2,
+    "kda_bwd": 64 * (5 * 256 + 2 + 4 * 256 + 2) + 128 * 128 * 2,
+}
 # DRAM traffic per chunk-head (dram__bytes_read.sum + dram__bytes_write.sum from one
-# ncu capture per kernel of the reduced case B=1, T=8192, H=16 = 2,048 chunk-heads,
-# summarised in profiles/kda_kernels_small_case.md); a launch's traffic grows in
-# proportion to the chunk-heads it processes, so roofline.traffic = this x units.
+# ncu capture per kernel of the reduced case B=1, T=8192, H=16 = 2,048 chunk-heads);
+# a launch's traffic grows in proportion to the chunk-heads it processes, so
+# roofline.traffic = this x units.
 TRAFFIC_PER_CHUNK_HEAD = {
     "kda_fwd": (134.819584e6 + 331.858432e6) / 2048,
     "kda_bwd": (152.345600e6 + 43.184640e6 + 522.276608e6 + 111.698944e6) / 2048,  # bwd_seq + bwd_par
@@ -295,11 +303,11 @@ def run_b200(args):
     tokens_per_step = world * B * T
     value = tokens_per_step * args.steps / (ms / 1e3)
     units = B * H * n_chunks
-    fwd_flop = FWD_FLOP_PER_CHUNK_HEAD * units
-    bwd_flop = BWD_FLOP_PER_CHUNK_HEAD * units
-    dom_ms, dom_flop, dom = (bwd_ms, bwd_flop, "kda_bwd") if bwd_ms >= fwd_ms else (fwd_ms, fwd_flop, "kda_fwd")
-    achieved = dom_flop / (dom_ms / 1e3) / 1e12
-    peak = peaks["bf16_sustained"] if ms * args.steps > 1000.0 else peaks["bf16"]
+    # `ms` is the whole timed region (all K steps): a region under a second is a
+    # burst, so the burst GEMM peak is the denominator, else the sustained one
+    peak_kind = "sustained" if ms > 1000.0 else "burst"
+    kern = kernel_rooflines({"kda_fwd": fwd_ms, "kda_bwd": bwd_ms}, units, peaks, peak_kind)
+    dom = "kda_bwd" if bwd_ms >= fwd_ms else "kda_fwd"
 
     # e2e through the public API with host buffers (rank-local), after the device timing
     e2e = run_e2e(torch, KD, q, k, v, g, beta, do, C, args, dev) if not args.no_e2e else {"ms": float("nan"), "h2d": 0, "d2h": 0}
@@ -341,14 +349,11 @@ def run_b200(args):
                        "parallelism": f"batch-sharded x{world}, no collective",
                        "l2": "inputs larger than L2 (no flush)",
                        "value_is": "whole-job tokens/s over all GPUs"},
+            "tokens_per_s_whole_job": value,
+            "tokens_per_s_per_gpu": value / world,
             "kernels_ms": {"kda_fwd": fwd_ms, "kda_bwd": bwd_ms},
-            "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
-                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": peaks["source"] + (" sustained" if peak == peaks["bf16_sustained"] else " burst"),
-                         "traffic": TRAFFIC_PER_CHUNK_HEAD[dom] * units,
-                         "traffic_unit": "bytes per launch (ncu DRAM bytes per chunk-head x units)",
-                         "traffic_GBps": TRAFFIC_PER_CHUNK_HEAD[dom] * units / (dom_ms / 1e3) / 1e9,
-                         "hbm_peak_GBps": peaks["hbm"]},
+            "roofline": dict(kern[dom], kernel=dom),
+            "roofline_kernels": kern,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "steps": e2e.get("steps"),
                     "overlap": e2e.get("overlap")},
@@ -362,6 +367,38 @@ def run_b200(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def kernel_rooflines(kernels_ms, units, peaks, peak_kind):
+    """Roofline entry per kernel from its average CUDA-event time per launch:
+    algorithmic FLOP/s against the measured bf16 GEMM peak (burst or sustained,
+    by the timed region's length), and the HBM side (algorithmic bytes, and the
+    ncu-measured DRAM traffic scaled to this launch) against the measured copy
+    bandwidth.  ``frac`` = achieved / peak can be recomputed from kernels_ms,
+    the per-chunk-head constants above and MEASURED_PEAKS.json."""
+    peak = peaks["bf16_sustained"] if peak_kind == "sustained" else peaks["bf16"]
+    flop = {"kda_fwd": FWD_FLOP_PER_CHUNK_HEAD, "kda_bwd": BWD_FLOP_PER_CHUNK_HEAD}
+    out = {}
+    for name, ms in kernels_ms.items():
+        sec = ms / 1e3
+        achieved = flop[name] * units / sec / 1e12
+        algo = ALGO_BYTES_PER_CHUNK_HEAD[name] * units
+        traffic = TRAFFIC_PER_CHUNK_HEAD[name] * units
+        out[name] = {
+            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak,
+            "peak_source": f"{peaks['source']} bf16 {peak_kind} (MEASURED_PEAKS.json)",
+            "ms_per_launch": ms, "flop_per_launch": flop[name] * units,
+            "traffic": traffic,
+            "traffic_unit": "bytes per launch (ncu DRAM read+write per chunk-head x units)",
+            "algorithmic_bytes": algo,
+            "traffic_over_algorithmic": traffic / algo,
+            "hbm_GBps_algorithmic": algo / sec / 1e9,
+            "hbm_GBps_traffic": traffic / sec / 1e9,
+            "hbm_peak_GBps": peaks["hbm"],
+            "hbm_frac_traffic": traffic / sec / 1e9 / peaks["hbm"],
+        }
+    return out
 
 
 def run_e2e(torch, KD, q, k, v, g, beta, do, C, args, dev):
@@ -423,8 +460,9 @@ def run_e2e(torch, KD, q, k, v, g, beta, do, C, args, dev):
             "overlap": "H2D of step i+1 and D2H of step i-1 overlap step i's compute"}
 
 
-def run_decode(torch, KD, dev, peaks, steps=64, warmup=8):
-    """256 sequences x 32 heads, fp32 128x128 states, one token per step."""
+def run_decode(torch, KD, dev, peaks, steps=1024, warmup=8):
+    """256 sequences x 32 heads, fp32 128x128 states, one token per step,
+    1024 consecutive steps (new q, k, v, g, beta every step from 16 cycled batches)."""
     N, dk, dv = CFG4["N"], CFG4["dk"], CFG4["dv"]
     gen = torch.Generator(device=dev)
     gen.manual_seed(7)
@@ -634,12 +672,15 @@ def cpu_baseline(sample_heads, cfg, T=None):
     K.chunk_bwd(x["q"], x["k"], x["v"], x["g"], x["beta"], None, do, None, chunk=cfg["chunk"],
                 dtype=np.float32)
     dt = time.perf_counter() - t0
-    full_step_s = dt * (cfg["B"] * cfg["H"] / sample_heads) * (cfg["T"] / T)
+    scale = (cfg["B"] * cfg["H"] / sample_heads) * (cfg["T"] / T)
+    full_step_s = dt * scale
     tokens = cfg["B"] * cfg["T"]
     return {"value": tokens / full_step_s, "unit": "tokens/s", "cores": os.cpu_count(),
             "kind": "port",
             "sample": f"{sample_heads} (b,h) units x T={T} fwd+bwd in {dt:.2f} s, NumPy fp32 "
                       f"restatement of the reference JAX path (JAX absent), scaled by B*H",
+            "sample_seconds": dt, "sample_tokens": sample_heads * T,
+            "scale_factor": scale, "extrapolated_step_seconds": full_step_s,
             "threads": "OpenBLAS default (all host cores)"}
 
 
@@ -649,18 +690,22 @@ def run_reference(args):
     if rank != 0:
         return
     cfg = dict(CFG3)
-    vals = []
     for _ in range(args.warmup):
         cpu_baseline(sample_heads=1, cfg=cfg, T=1024)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        vals.append(cpu_baseline(sample_heads=args.cpu_heads, cfg=cfg)["value"])
+    runs = [cpu_baseline(sample_heads=args.cpu_heads, cfg=cfg) for _ in range(args.steps)]
     wall = time.perf_counter() - t0
+    vals = [r["value"] for r in runs]
     value = statistics.median(vals)
+    sample_s = statistics.median(r["sample_seconds"] for r in runs)
+    scale = runs[0]["scale_factor"]
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": cfg["B"] * cfg["T"] / value * 1e3, "higher_is_better": True,
+        "ms_per_step": cfg["B"] * cfg["T"] / value * 1e3,
+        "ms_per_step_is": "extrapolated: the measured sample time x scale_factor (units are independent)",
+        "sample_ms_per_step": sample_s * 1e3, "scale_factor": scale,
+        "wall_s_all_steps": wall, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "cfg3 KDA chunked fwd+bwd", "B_per_rank": cfg["B"], "T": cfg["T"],
                    "H": cfg["H"], "dk": cfg["dk"], "dv": cfg["dv"], "chunk": cfg["chunk"]},
@@ -669,7 +714,8 @@ def run_reference(args):
                          "kind": "port",
                          "sample": f"per step {args.cpu_heads} (b,h) units x T={cfg['T']} fwd+bwd, "
                                    "NumPy fp32 restatement (reference JAX not installed), "
-                                   f"scaled by B*H; {wall:.1f} s wall"},
+                                   f"scaled by B*H; {wall:.1f} s wall",
+                         "sample_seconds": sample_s, "scale_factor": scale},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

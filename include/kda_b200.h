@@ -176,9 +176,13 @@ int kda_bwd_varlen(const void* q, const void* k, const void* v, const void* g,
  * instead, which every GPU that loads the library holds until exit.  It
  * allocates nothing.  Problems whose kda_bwd_workspace_bytes exceeds the
  * array are rejected with KDA_ERR_SCRATCH_LIMIT.  The first call on a device
- * looks up the array's device address (make it before any stream capture).
- * All calls share the array: calls whose kernels overlap on the GPU race and
- * must be serialised; no scratch content needs clearing between calls. */
+ * looks up the array's device address (make it before any stream capture) and
+ * keeps it for the life of the process: it stays valid while the device's
+ * primary context lives, so a caller that resets the device (cudaDeviceReset)
+ * or otherwise destroys that context must not call this entry point again in
+ * the same process.  All calls share the array: calls whose kernels overlap on
+ * the GPU race and must be serialised; no scratch content needs clearing
+ * between calls. */
 int kda_bwd_noalloc(const void* q, const void* k, const void* v, const void* g,
                     const void* beta, const void* s_ckpt, const void* do_,
                     const float* dsT, void* dq, void* dk_, void* dv_, void* dg,

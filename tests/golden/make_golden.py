@@ -12,6 +12,10 @@ the reference checkout given by ``--reference``:
 * ``net/kda.py:298-310``                          ``_delta_step``    (the recurrence), ``o = S^T q`` :293
 * ``net/kda.py:588-631``                          ``_cc_scores``     (tile-anchored scores)
 
+The ``tc_*`` cases run the scan and its reverse scan at the tensor-core shape
+(dk = dv = 128, C = 64) on inputs that are exactly representable in bfloat16,
+so the bf16 kernels can be checked against the reference's own outputs.
+
 The reference's operand-form replica (``kda_cc_fused.reference``) builds the
 column factor ``exp(anchor - G)`` over the whole chunk before masking it, which
 overflows to ``inf * 0 = nan`` once the decay summed over a chunk passes ~88
@@ -97,6 +101,21 @@ def _inputs(rng, T, H, dk, dv, decay, s0_std):
     f = np.float32
     return dict(q=q.astype(f), k=k.astype(f), v=v.astype(f), alpha=alpha,
                 beta=beta.astype(f), S=S)
+
+
+def _bf16(a):
+    """Round to the nearest bfloat16 (ties to even), returned as float32."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def _bf16_inputs(x):
+    """The same draw made bf16-representable: q, k, v, beta rounded; alpha = exp(g)
+    of the rounded log-decay (so log(alpha) rounds back to it); S stays fp32."""
+    g = _bf16(np.log(x["alpha"].astype(np.float64)))
+    return dict(q=_bf16(x["q"]), k=_bf16(x["k"]), v=_bf16(x["v"]),
+                alpha=np.exp(g.astype(np.float64)).astype(np.float32), beta=_bf16(x["beta"]), S=x["S"])
 
 
 def _ref_form(x):
@@ -205,6 +224,36 @@ def main():
                                G.view(jaxshim.Arr), 16, strict)
         out[f"scores/{'strict' if strict else 'lower'}"] = np.asarray(sc)
     out["scores/row"], out["scores/col"], out["scores/G"] = row, col, G
+
+    # 7. the tensor-core shape (dk = dv = 128, C = 64) on bf16-representable inputs:
+    # q, k, v, beta, dO and the log-decay are rounded to bf16 before the reference
+    # sees them (alpha = exp of the rounded g, in fp32), so a bf16 caller passes
+    # exactly the values the reference computed with.
+    for name, (T, H, decay, s0, seed, bwd) in {
+        "tc_scan_baseline": (192, 1, "baseline", 0.02, 13, False),
+        "tc_scan_medium": (192, 1, "medium", 0.1, 14, False),
+        "tc_bwd_scan_baseline": (128, 1, "baseline", 0.02, 15, True),
+        "tc_bwd_scan_medium": (128, 1, "medium", 0.1, 16, True),
+    }.items():
+        rng = np.random.default_rng(seed)
+        x = _bf16_inputs(_inputs(rng, T, H, 128, 128, decay, s0))
+        ref = _ref_form(x)
+        put(name, _our_inputs(x))
+        if not bwd:
+            o, s_new = persist.reference(*ref, tile=16, chunk=64)
+            put(name, dict(o=np.asarray(o).reshape(1, T, H, 128), S_T=np.asarray(s_new)[None],
+                           chunk=np.array(64)))
+            continue
+        do = _bf16(rng.standard_normal((T, H * 128)))
+        dS = rng.standard_normal((H, 128, 128)).astype(np.float32)
+        dq, dk_, dv_, dalpha, dbeta32, dS_in = (np.asarray(r) for r in persist.reference_bwd_scan(
+            *ref, do.view(jaxshim.Arr), dS.view(jaxshim.Arr), tile=16, chunk=64))
+        put(name, dict(
+            do=do.reshape(1, T, H, 128), dST=dS[None], chunk=np.array(64),
+            dq=dq.reshape(1, T, H, 128), dk=dk_.reshape(1, T, H, 128), dv=dv_.reshape(1, T, H, 128),
+            dg=(dalpha.astype(np.float64) * x["alpha"].reshape(T, H * 128)).reshape(1, T, H, 128),
+            dbeta=dbeta32.astype(np.float64).reshape(T, H, 32).sum(-1)[None],
+            dS0=dS_in[None]))
 
     path = os.path.join(args.out, "reference_kda.npz")
     np.savez_compressed(path, **out)

@@ -80,3 +80,41 @@ def test_prefill_then_decode_matches_the_full_layer(dt, dk, kind):
             assert scale_rel_err(y[i].double().cpu().numpy(), full[i][0][t].double().cpu().numpy()) <= tol, (t, i)
     for i in range(N):
         assert scale_rel_err(cache.S[i].double().cpu().numpy(), full[i][1][0].double().cpu().numpy()) <= tol, i
+
+
+@pytest.mark.parametrize("gate_bias", ["dt", "zero"])
+def test_layer_at_config5_width_matches_oracle(gate_bias):
+    """BASELINE config 5's layer at its full width: d_model = 2048, H = 16,
+    dk = dv = 128, rank-128 softplus gate with A_log ~ U(log 1, log 16), conv K = 4,
+    bf16 weights N(0, 0.02) and inputs N(0, 1), three packed sequences (a ragged
+    mix of lengths, 683 tokens in all instead of cfg5's 65,536).  Forward, input
+    gradient and every weight gradient against the oracle's float64 layer; gate
+    bias "dt" (the bench's time-step bias) and "zero" (BASELINE's b = 0: every
+    chunk past the single-anchor exponent budget, the exact score path).
+    Bound 5e-2 as for the other bf16 layer cases."""
+    from axiom_b200 import layer
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    d_model, H, dk, rank = 2048, 16, 128, 128
+    cu = [0, 200, 533, 683]
+    T = cu[-1]
+    p = layer.init_params(d_model, H, dk, dk, rank=rank, K=4, gate_kind="softplus", gate_bias=gate_bias,
+                          dtype=torch.bfloat16, seed=21)
+    gen = torch.Generator(device="cpu").manual_seed(22)
+    x = torch.randn(T, d_model, generator=gen).to("cuda", torch.bfloat16).requires_grad_(True)
+    dout = torch.randn(T, d_model, generator=gen).to("cuda", torch.bfloat16)
+    out = layer.kda_layer(p, x, H=H, cu_seqlens=cu, gate_kind="softplus")
+    out.backward(dout)
+    torch.cuda.synchronize()
+    P = {f: getattr(p, f).detach().double().cpu().numpy() for f in
+         ("W_q", "W_k", "W_v", "W_g", "W_beta", "W_a_down", "W_a_up", "b_gate", "A", "conv_q", "conv_k", "conv_v",
+          "W_o")}
+    ref, cache = M.layer_fwd(P, x.detach().double().cpu().numpy(), H, cu, kind=M.GATE_SOFTPLUS)
+    g = M.layer_bwd(P, cache, dout.double().cpu().numpy())
+    tol = 5e-2
+    assert scale_rel_err(out.detach().double().cpu().numpy(), ref) <= tol
+    assert scale_rel_err(x.grad.double().cpu().numpy(), g["x"]) <= tol
+    for name in P:
+        got = getattr(p, name).grad
+        assert got is not None, name
+        assert scale_rel_err(got.double().cpu().numpy(), g[name]) <= tol, name

@@ -67,6 +67,43 @@ def test_decode_step_matches_recurrence(dk, dv, dtype):
     assert K.scale_rel_err(_np(S), s_ref) <= 1e-5
 
 
+def test_decode_1024_consecutive_steps_cfg4():
+    """BASELINE config 4 over its full 1024 consecutive steps: cfg4's distributions
+    and state shape (fp32 128 x 128 per head, seeded N(0, 0.02)), new bf16 q, k, v,
+    g, beta every step, 4 sequences x 32 heads (128 states; cfg4 has 256 x 32 of the
+    same independent per-head recurrence, the kernel runs one CTA per state).  The
+    kernel's fp32 state is carried on the device through all steps and compared
+    with the float64 recurrence (net/kda.py:298-310, :293) on the same bf16-rounded
+    inputs: o at every 128th step and the last, and S after the last."""
+    from axiom_b200 import decode_step
+
+    n_seq, H, D, steps = 4, 32, 128, 1024
+    rng = np.random.default_rng(4000)
+    S0 = rng.normal(0.0, 0.02, (n_seq, H, D, D)).astype(np.float32)
+    S = _dev(S0)
+    s_ref = S0.astype(np.float64)
+    worst_o = 0.0
+
+    def unit(x):
+        return x / (np.linalg.norm(x, axis=-1, keepdims=True) + 1e-12)
+
+    for t in range(steps):
+        x = {"q": unit(rng.standard_normal((n_seq, H, D))), "k": unit(rng.standard_normal((n_seq, H, D))),
+             "v": rng.standard_normal((n_seq, H, D)),
+             "g": -np.logaddexp(0.0, -rng.normal(3.0, 1.0, (n_seq, H, D))),
+             "beta": 1.0 / (1.0 + np.exp(-rng.standard_normal((n_seq, H))))}
+        xr = {n: K.bf16_round(a.astype(np.float32)) for n, a in x.items()}
+        args = [_dev(xr[n], torch.bfloat16) for n in ("q", "k", "v", "g", "beta")]
+        o = decode_step(S, *args, o_dtype=torch.float32)
+        o_ref, s_ref = K.decode_step(s_ref, *(xr[n] for n in ("q", "k", "v", "g", "beta")))
+        if t % 128 == 127 or t == steps - 1:
+            worst_o = max(worst_o, K.scale_rel_err(_np(o), o_ref))
+    err_s = K.scale_rel_err(_np(S), s_ref)
+    # the bf16 bar is 1e-2; an fp32 state carried over 1024 steps stays far inside it
+    assert worst_o <= 1e-4, worst_o
+    assert err_s <= 1e-4, err_s
+
+
 def test_decode_many_states_in_place():
     """cfg4-shaped step at reduced batch: 64 sequences x 32 heads, fp32 state."""
     from axiom_b200 import decode_step

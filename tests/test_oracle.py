@@ -14,8 +14,10 @@ import pytest
 
 from oracle import kda_oracle as K
 
-FWD_CASES = ["chunk_a", "chunk_b", "chunk_c", "scan_a", "scan_b", "scan_c", "scan_d"]
-BWD_CASES = ["bwd_chunk", "bwd_scan", "bwd_scan_strong", "bwd_scan_medium"]
+FWD_CASES = ["chunk_a", "chunk_b", "chunk_c", "scan_a", "scan_b", "scan_c", "scan_d",
+             "tc_scan_baseline", "tc_scan_medium"]
+BWD_CASES = ["bwd_chunk", "bwd_scan", "bwd_scan_strong", "bwd_scan_medium",
+             "tc_bwd_scan_baseline", "tc_bwd_scan_medium"]
 GRADS = ["dq", "dk", "dv", "dg", "dbeta", "dS0"]
 
 
