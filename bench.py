@@ -10,6 +10,14 @@ checkpoint) plus one fused backward from a bf16 upstream cotangent.  Inputs
 (268 MB per q/k/v/g tensor) are larger than the 126 MB L2, so no flush is
 needed between steps.  Rank 0 prints ONE JSON line.
 
+Beside the headline (weak scaling), every run also measures, on all its ranks:
+``strong`` -- one fixed global cfg3 problem split over the ranks by (batch,
+head), with the NCCL all-gathers of the outputs and gradients inside the timed
+step; and ``mixer_cfg5_sharded`` -- BASELINE config 5 (the mixer layer over 16
+packed sequences, T = 65,536) sharded by sequence x head with its gradient
+all-reduces.  Single-GPU extras (N = 1 only): decode (cfg4, 1024 steps),
+prefill (cfg2), the mixer kernels and the cfg5 layer on one GPU.
+
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 NumPy restatement in ``oracle/``; the reference itself is JAX, which is not
 installed) on the host cores over a bounded sample and prints the same line
@@ -318,6 +326,12 @@ def run_b200(args):
     e2e_value = None if args.no_e2e else tokens_per_step / (e2e["ms"] / 1e3)
 
     extra = {}
+    if not args.no_extra:  # every rank takes part (collectives)
+        strong = run_strong(torch, dist, KD, world, rank, dev, peaks, args)
+        mix = run_mixer_sharded(torch, dist, world, rank, dev)
+        if rank == 0:
+            extra["strong"] = strong
+            extra["mixer_cfg5_sharded"] = mix
     if rank == 0 and world == 1 and not args.no_extra:  # single-GPU measurements
         extra["decode"] = run_decode(torch, KD, dev, peaks)
         extra["prefill"] = run_prefill(torch, KD, dev, peaks)
@@ -367,6 +381,144 @@ def run_b200(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _max_over_ranks(torch, dist, world, dev, vals):
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def run_strong(torch, dist, KD, world, rank, dev, peaks, args, steps=10, warmup=3):
+    """Strong scaling of the north star's partitioned workload: ONE global cfg3
+    problem (B=4, T=8192, H=32) whatever the number of GPUs, its (batch, head)
+    units split over the ranks by ``axiom_b200.dist.core_shard`` (batch while it
+    divides, else heads).  Every rank generates the global inputs from one seed
+    and keeps its slice (outside the timed region).  A timed step: forward on
+    the slice, the all-gather of O and S_T (NCCL, overlapped with the backward),
+    the backward, and the all-gather of dq, dk, dv, dg and dbeta, so every rank
+    ends the step holding the full outputs and gradients.  Device-timed, max
+    over ranks; also timed: the same step without the gathers (compute only)."""
+    from axiom_b200 import dist as D
+
+    cfg = dict(CFG3)
+    B, T, H, C = cfg["B"], cfg["T"], cfg["H"], cfg["chunk"]
+    full = make_train_inputs(torch, cfg, seed=4321, device=dev)
+    sh = D.core_shard(B, H)
+    loc = [sh.take(t) for t in full]
+    del full
+    torch.cuda.empty_cache()
+    q, k, v, g, beta, do = loc
+
+    def step(gather):
+        o, s_t, ck = KD.kda_fwd(q, k, v, g, beta, None, chunk=C, need_ckpt=True)
+        if gather:
+            fo, _ = D._gather(o, sh.axis, async_op=True)
+            fs, _ = D._gather(s_t, sh.s_axis, async_op=True)
+        grads = KD.kda_bwd(q, k, v, g, beta, ck, do, None, chunk=C, need_ds0=False)
+        if gather:
+            out = [fo(), fs()] + [D._gather(x, sh.axis) for x in grads[:5]]
+            return out
+        return grads
+
+    def timed(gather):
+        for _ in range(warmup):
+            step(gather)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step(gather)
+        e1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        return e0.elapsed_time(e1) / steps
+
+    ms_full, ms_compute = _max_over_ranks(torch, dist, world, dev, [timed(True), timed(False)])
+    units = q.shape[0] * q.shape[2]
+    el = 2  # bf16
+    gathered = (B * T * H * 128 * el * 5 + B * T * H * el + B * H * 128 * 128 * 4) if world > 1 else 0
+    del loc, q, k, v, g, beta, do
+    torch.cuda.empty_cache()
+    return {"workload": "cfg3 global problem (B=4, T=8192, H=32) fixed, (batch, head) units split over the ranks",
+            "scaling": "strong", "n_gpus": world, "shard_axis": "batch" if sh.axis == 0 else "head",
+            "units_per_rank": units, "ms_per_step": ms_full, "tokens_per_s": B * T / (ms_full / 1e3),
+            "ms_per_step_compute_only": ms_compute, "tokens_per_s_compute_only": B * T / (ms_compute / 1e3),
+            "gather_ms_per_step": ms_full - ms_compute, "gathered_bytes_per_step": gathered,
+            "gathers": "O and S_T (overlapping the backward), then dq, dk, dv, dg, dbeta: NCCL all-gather",
+            "steps": steps, "timing": "CUDA events, max over ranks"}
+
+
+def run_mixer_sharded(torch, dist, world, rank, dev, steps=5, warmup=3):
+    """BASELINE config 5 as specified: the mixer layer's forward + backward over
+    16 packed sequences (T = 65,536), sharded by sequence x head over the ranks.
+    The mesh (sequence groups x head groups) is the one whose busiest rank has
+    the least work (``axiom_b200.dist.choose_head_groups``); whole sequences go
+    to sequence groups longest first; weight gradients are all-reduced (NCCL) in
+    the timed step.  Device-timed, max over ranks; tokens/s over the whole job."""
+    import numpy as np
+
+    from axiom_b200 import dist as D
+    from axiom_b200 import layer
+
+    H, d_model = 16, 2048
+    rng = np.random.default_rng(5)
+    L = rng.uniform(512, 8192, 16)
+    L = np.floor(L / L.sum() * 65536).astype(int)
+    L[-1] += 65536 - int(L.sum())
+    cu = [0] + np.cumsum(L).tolist()
+    hg = D.choose_head_groups(L.tolist(), world, H)
+    mesh = D.layer_mesh(hg)
+    p = layer.init_params(d_model, H, 128, 128, rank=128, K=4, gate_kind="softplus", dtype=torch.bfloat16,
+                          device=dev, seed=5)
+    pl, Hl = D.shard_layer_params(p, H, mesh)
+    del p
+    ids = D.assign_sequences(L.tolist(), mesh.n_seq_groups)[mesh.seq_index]
+    rows, cu_loc = D.local_packing(cu, ids)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(12)
+    x_all = torch.randn(65536, d_model, generator=gen, device=dev).to(torch.bfloat16)
+    d_all = torch.randn(65536, d_model, generator=gen, device=dev).to(torch.bfloat16)
+    ridx = torch.tensor(rows, device=dev, dtype=torch.long)
+    x = x_all[ridx].contiguous().requires_grad_(True)
+    dout = d_all[ridx].contiguous()
+    del x_all, d_all
+
+    def step():
+        for t in pl.tensors() + [x]:
+            t.grad = None
+        D.kda_layer_sharded(pl, x, mesh, H_local=Hl, cu_seqlens=cu_loc, gate_kind="softplus").backward(dout)
+        D.allreduce_layer_grads(pl, mesh)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    (ms,) = _max_over_ranks(torch, dist, world, dev, [e0.elapsed_time(e1) / steps])
+    tok_rank = len(rows)
+    (tok_max,) = _max_over_ranks(torch, dist, world, dev, [float(tok_rank)])
+    del pl, x, dout
+    torch.cuda.empty_cache()
+    return {"workload": "cfg5 KDA mixer layer fwd+bwd, 16 packed seqs, T=65536, d_model=2048, H=16, "
+                        "sharded by sequence x head",
+            "n_gpus": world, "mesh": f"{mesh.n_seq_groups} sequence groups x {mesh.n_head_groups} head groups",
+            "ms_per_step": ms, "tokens_per_s": 65536 / (ms / 1e3), "max_tokens_per_sequence_group": tok_max,
+            "heads_per_rank": Hl, "collectives": "NCCL all-reduce: W_o partial outputs and input cotangent "
+                                                 "(head groups > 1), weight gradients (sequence groups > 1)",
+            "steps": steps, "timing": "CUDA events, max over ranks"}
 
 
 def kernel_rooflines(kernels_ms, units, peaks, peak_kind):
