@@ -1,5 +1,8 @@
 // extern "C" entry points of libkda_b200.so: argument validation (fail
 // closed, before any launch) and dispatch to the kernels.
+#include <cstdlib>
+#include <cstring>
+
 #include <cuda_runtime.h>
 
 #include "kda_ckpt_layout.h"
@@ -19,6 +22,10 @@ constexpr size_t kTcFactorBytes = FAC_UNIT;  // factor block per chunk-head (kda
 int tc_fwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
                   const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
                   int o_dt, int ck_dt, const int* cs, int n_seqs, cudaStream_t st);
+int tc_fwd_split_slices(long long heads);
+int tc_fwd_split_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                        const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H, int o_dt,
+                        int ck_dt, const int* cs, int n_seqs, int slices, cudaStream_t st);
 bool tc_bwd_supported(int dk, int dv, int C_, int in_dt, int do_dt);
 size_t tc_bwd_workspace_bytes(int B, int T, int H);
 int tc_bwd_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,
@@ -35,6 +42,23 @@ int simt_bwd_launch(const void* q, const void* k, const void* v, const void* g, 
 namespace {
 
 bool valid_dtype(int d) { return d == KDA_F32 || d == KDA_BF16; }
+
+// Schedule of the tensor-core forward when a checkpoint is written (training):
+// "split" (chunk-parallel prep + column-sliced state scan, kda_fwd_split.cu) or
+// "fused" (one CTA per (sequence, head), kda_fwd_tc.cu).  The fused kernel's time
+// is one head's chain of chunks, whatever the head count up to one CTA per SM;
+// the split schedule's grows with the units but spreads a head over 2 to 8 SMs.
+// By default the split one runs while the heads fill at most half the SMs (its
+// state scan then takes two or more slices per head), the fused one otherwise;
+// the environment variable KDA_FWD_SCHEDULE ("split" or "fused") overrides it.
+// Without a checkpoint the fused kernel runs (the split schedule hands its
+// work over in the checkpoint).
+bool use_split_forward(long long heads) {
+  const char* e = std::getenv("KDA_FWD_SCHEDULE");
+  if (e && std::strcmp(e, "fused") == 0) return false;
+  if (e && std::strcmp(e, "split") == 0) return true;
+  return kda::tc_fwd_split_slices(heads) >= 2;
+}
 
 int check_dims(int B, int T, int H, int dk, int dv, int chunk) {
   if (B < 0 || T < 0 || H < 0) return KDA_ERR_SHAPE;
@@ -108,6 +132,12 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* g, const v
         !kda::aligned16(o) || (s_ckpt && !kda::aligned16(s_ckpt)) || (s_out && !kda::aligned16(s_out)) ||
         (s0 && !kda::aligned16(s0)))
       return KDA_ERR_ALIGN;
+    const long long heads = static_cast<long long>(cs ? n_seqs : B) * H;
+    if (s_ckpt && use_split_forward(heads)) {
+      const int slices = kda::tc_fwd_split_slices(heads);
+      return kda::tc_fwd_split_launch(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, o_dtype, ckpt_dtype, cs,
+                                      n_seqs, slices, stream);
+    }
     return kda::tc_fwd_launch(q, k, v, g, beta, s0, o, s_out, s_ckpt, B, T, H, o_dtype, ckpt_dtype, cs,
                               n_seqs, stream);
   }

@@ -8,6 +8,7 @@
 namespace kda {
 
 int tc_fwd_error_flag(int* value, bool clear, cudaStream_t st);
+int tc_fwd_split_error_flag(int* value, bool clear, cudaStream_t st);
 int tc_bwd_error_flag(int* value, bool clear, cudaStream_t st);
 int decode_fused_error_flag(int* value, bool clear, cudaStream_t st);
 
@@ -44,15 +45,16 @@ int selftest_error_flag(int* value, bool clear, cudaStream_t st) {
 extern "C" int kda_device_status(int* flags, int clear, kda_stream_t stream) {
   if (!flags) return KDA_ERR_NULL;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  int v[4] = {0, 0, 0, 0};
+  int v[5] = {0, 0, 0, 0, 0};
   const bool c = clear != 0;
   int rc = kda::tc_fwd_error_flag(&v[0], c, st);
+  if (rc == KDA_OK) rc = kda::tc_fwd_split_error_flag(&v[4], c, st);
   if (rc == KDA_OK) rc = kda::tc_bwd_error_flag(&v[1], c, st);
   if (rc == KDA_OK) rc = kda::decode_fused_error_flag(&v[2], c, st);
   if (rc == KDA_OK) rc = kda::selftest_error_flag(&v[3], c, st);
   if (cudaStreamSynchronize(st) != cudaSuccess) rc = KDA_ERR_LAUNCH;
   if (rc != KDA_OK) return rc;
-  *flags = (v[0] ? KDA_STATUS_FWD : 0) | (v[1] ? KDA_STATUS_BWD : 0) | (v[2] ? KDA_STATUS_DECODE_FUSED : 0) |
+  *flags = ((v[0] || v[4]) ? KDA_STATUS_FWD : 0) | (v[1] ? KDA_STATUS_BWD : 0) | (v[2] ? KDA_STATUS_DECODE_FUSED : 0) |
            (v[3] ? KDA_STATUS_SELFTEST : 0);
   return KDA_OK;
 }

@@ -342,13 +342,19 @@ def decode_fused_step(S, conv_buf, qp, kp, vp, z, beta_logit, wq, wk, wv, b_gate
 # ---------------------------------------------------------------------------
 
 
-def layer_fwd(P, x, H, cu_seqlens=None, kind=GATE_SOFTPLUS, g_min=G_MIN, chunk=64):
+def layer_fwd(P, x, H, cu_seqlens=None, kind=GATE_SOFTPLUS, g_min=G_MIN, chunk=64, tile="reference"):
     """``apply_kda`` of one layer (``net/kda.py:929-946`` with ``_project``
     :157-191, ``_postprocess`` :194-203 and ``_output_gate`` :206-214) over
     ``x [T, d_model]``, float64.  ``P`` maps the weight names of
     ``axiom_b200.layer.KDALayerParams`` to arrays.  Returns ``(out, cache)``;
-    ``cache`` feeds :func:`layer_bwd`."""
-    from oracle.kda_oracle import chunk_fwd
+    ``cache`` feeds :func:`layer_bwd`.  ``tile``: the core's score evaluation,
+    the reference's tile-anchored one with its exponent clamp (default) or
+    ``None`` for the direct decay ratio, exact for any decay (the clamp binds
+    once a 16-token tile's summed decay passes 80, e.g. per-token decays of
+    ~5 and more)."""
+    from oracle.kda_oracle import TILE, chunk_fwd
+
+    tile = TILE if tile == "reference" else tile
 
     x = np.asarray(x, np.float64)
     T = x.shape[0]
@@ -364,10 +370,11 @@ def layer_fwd(P, x, H, cu_seqlens=None, kind=GATE_SOFTPLUS, g_min=G_MIN, chunk=6
     o = np.zeros((T, H, dv))
     for a, b in zip(cu[:-1], cu[1:]):
         if b > a:
-            o[a:b] = chunk_fwd(*(pro[n][:, a:b] for n in ("q", "k", "v", "g", "beta")), None, chunk=chunk)[0][0]
+            o[a:b] = chunk_fwd(*(pro[n][:, a:b] for n in ("q", "k", "v", "g", "beta")), None, chunk=chunk,
+                               tile=tile)[0][0]
     y = gated_rmsnorm(o, proj["gl"].reshape(T, H, dv)).reshape(T, H * dv)
     cache = dict(x=x, a_down=a_down, proj=proj, pro=pro, o=o, y=y, cu=cu, H=H, dk=dk, dv=dv, kind=kind,
-                 g_min=g_min, chunk=chunk, cu_seqlens=cu_seqlens)
+                 g_min=g_min, chunk=chunk, tile=tile, cu_seqlens=cu_seqlens)
     return y @ P["W_o"], cache
 
 
@@ -387,7 +394,7 @@ def layer_bwd(P, cache, dout):
     for a, b in zip(cu[:-1], cu[1:]):
         if b > a:
             r = chunk_bwd(*(pro[n][:, a:b] for n in ("q", "k", "v", "g", "beta")), None, do[a:b][None], None,
-                          chunk=cache["chunk"])
+                          chunk=cache["chunk"], tile=cache["tile"])
             for n, d in zip(("q", "k", "v", "g", "beta"), r[:5]):
                 c[n][:, a:b] = d
     pb = prologue_bwd(proj["qp"][None], proj["kp"][None], proj["vp"][None], proj["z"][None], proj["bl"][None],

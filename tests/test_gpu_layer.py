@@ -109,7 +109,10 @@ def test_layer_at_config5_width_matches_oracle(gate_bias):
     P = {f: getattr(p, f).detach().double().cpu().numpy() for f in
          ("W_q", "W_k", "W_v", "W_g", "W_beta", "W_a_down", "W_a_up", "b_gate", "A", "conv_q", "conv_k", "conv_v",
           "W_o")}
-    ref, cache = M.layer_fwd(P, x.detach().double().cpu().numpy(), H, cu, kind=M.GATE_SOFTPLUS)
+    # b = 0 gives per-token decays up to ~20: past the reference's tile-anchored
+    # clamp, so the oracle evaluates the direct decay ratio (exact) there
+    ref, cache = M.layer_fwd(P, x.detach().double().cpu().numpy(), H, cu, kind=M.GATE_SOFTPLUS,
+                             tile=None if gate_bias == "zero" else "reference")
     g = M.layer_bwd(P, cache, dout.double().cpu().numpy())
     tol = 5e-2
     assert scale_rel_err(out.detach().double().cpu().numpy(), ref) <= tol

@@ -269,3 +269,36 @@ def test_tc_mixed_decay_regimes_in_one_call():
         for name, gr, rf in zip(GRADS, grads, ref):
             g_, r_ = (_np(gr)[:, h], rf[:, h]) if name == "dS0" else (_np(gr)[:, :, h], rf[:, :, h])
             assert K.scale_rel_err(g_, r_) <= TOL, (name, h)
+
+
+@pytest.mark.parametrize("schedule", ["split", "fused"])
+@pytest.mark.parametrize("B,T,H,ck", [
+    (1, 200, 2, torch.bfloat16),    # 2 (sequence, head) pairs: 8 state slices of 16 columns
+    (1, 130, 32, torch.bfloat16),   # 32 pairs: 4 slices of 32 columns
+    (2, 128, 32, torch.float32),    # 64 pairs: 2 slices of 64 columns, fp32 checkpoint
+    (2, 64, 64, torch.bfloat16),    # 128 pairs: one CTA per pair, whole state
+])
+def test_tc_training_forward_schedules_match_oracle(monkeypatch, schedule, B, T, H, ck):
+    """The training forward (checkpoint written) on both schedules: the split
+    one (chunk-parallel prep + state scan sliced by columns, the slice count
+    following the number of (sequence, head) pairs) and the fused one; outputs,
+    states and the backward from each checkpoint against the oracle."""
+    from axiom_b200 import kda_bwd, kda_fwd
+    from axiom_b200.kda import ckpt_states
+
+    monkeypatch.setenv("KDA_FWD_SCHEDULE", schedule)
+    xr, d = _bf16_inputs(B, T, H, seed=B * 1000 + T + H, s0_std=0.05)
+    rng = np.random.default_rng(T + H)
+    do = K.bf16_round(rng.standard_normal((B, T, H, 128)))
+    o, s_t, ckpt = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], chunk=64,
+                           o_dtype=torch.float32, need_ckpt=True, ckpt_dtype=ck)
+    grads = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, _dev(do, torch.bfloat16), None, chunk=64)
+    torch.cuda.synchronize()
+    o_ref, s_ref, states = K.chunk_fwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], chunk=64,
+                                       return_states=True)
+    assert K.scale_rel_err(_np(o), o_ref) <= TOL
+    assert K.scale_rel_err(_np(s_t), s_ref) <= TOL
+    assert K.scale_rel_err(_np(ckpt_states(ckpt, B, T, H, 128, 128, chunk=64)), states) <= TOL
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, None, chunk=64)
+    for name, gr, rf in zip(GRADS, grads, ref):
+        assert K.scale_rel_err(_np(gr), rf) <= TOL, name
