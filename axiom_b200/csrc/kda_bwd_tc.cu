@@ -1083,6 +1083,265 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
   if (warp == 0) tmem_dealloc(tbase, 512);
 }
 
+// ===========================================================================
+// bwd_seq, column-sliced (fewer (sequence, head) pairs than SMs)
+// ===========================================================================
+// The same reverse recurrence on a slice dS'_s = dS'[:, col0 + DVS) of the
+// state cotangent: the columns never mix (lam K, Aqk, Gam Q and W act on the
+// rows), so 2 to 8 CTAs walk one head's chunks side by side.  Per chunk, in the
+// untransposed form (M = 64 for the chunk-row products):
+//   dU_s  = (lam K) dS'_s + Aqk^T dO_s               (M = 64, N = DVS)
+//   dS_s  = Gam_C dS'_s + (Gam Q)^T dO_s - W^T dU_s  (M = 128, N = DVS)
+// and the slice of each chunk's dS' image goes to the workspace for bwd_par.
+template <int DVS>
+struct SeqSliceMap {
+  static constexpr int W = 0, QG = 16384, KL = 32768, DO = 49152, AQ = 65536, GC = 73728;
+  static constexpr int SET = GC + 512;
+  static constexpr int SB = 2 * SET;          // dS'_s bf16 CM[128][DVS]
+  static constexpr int DU = SB + 256 * DVS;   // -dU_s bf16 CM[64][DVS]
+  static constexpr int BAR = DU + 128 * DVS;
+  static constexpr int SMEM = BAR + 64;
+  static constexpr int TCOLS = 2 * DVS <= 32 ? 32 : (2 * DVS <= 64 ? 64 : 128);
+};
+
+template <int N>
+__device__ __forceinline__ void tmem_ldn_s(uint32_t taddr, float* v) {
+  if constexpr (N == 32) tmem_ld32(taddr, v);
+  else if constexpr (N == 16) tmem_ld16(taddr, v);
+  else tmem_ld8(taddr, v);
+}
+template <int N>
+__device__ __forceinline__ void tmem_stn_s(uint32_t taddr, const float* v) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  if constexpr (N == 32) {
+    tmem_st32(taddr, v);
+  } else if constexpr (N == 16) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+           "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+           "r"(r[15])
+        : "memory");
+  } else {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+                    "r"(r[6]), "r"(r[7])
+                 : "memory");
+  }
+}
+
+template <int DVS>
+__global__ void __launch_bounds__(NT, 1)
+bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __restrict__ factors,
+                      const float* __restrict__ dsT, float* __restrict__ ds0, bf16* __restrict__ dsw, int T,
+                      int H, const int* __restrict__ cs, int* __restrict__ err,
+                      const __grid_constant__ CUtensorMap tm_do, int use_tma) {
+  using M = SeqSliceMap<DVS>;
+  constexpr int NS = DV / DVS;
+  constexpr int CW = DVS / 2;              // columns per warp (one lane quarter, one column half)
+  constexpr int CB = CW < 32 ? CW : 32;    // columns per TMEM access
+  extern __shared__ __align__(1024) unsigned char sm[];
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + M::BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + M::BAR + 8);
+  uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + M::BAR + 16);  // [2]: one per operand set
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qw = warp & 3, hh = warp >> 2;
+  const int n_chunks = (T + C - 1) / C;
+  const int s = blockIdx.x % NS;
+  const int bh = blockIdx.x / NS;
+  const int h = bh % H;
+  const int seq = cs ? longest_first(cs, gridDim.x / (H * NS), bh / H, n_chunks, reinterpret_cast<int*>(sm))
+                     : bh / H;
+  const int b = cs ? 0 : seq;
+  const int c_beg = cs ? min(max(cs[seq], 0), n_chunks) : 0;
+  const int c_end = cs ? min(max(cs[seq + 1], c_beg), n_chunks) : n_chunks;
+  const size_t tok0 = static_cast<size_t>(b) * T;
+  const size_t rstride = static_cast<size_t>(H) * DK;
+  const bf16* doh = dout + static_cast<size_t>(h) * DV;
+  const size_t unit = static_cast<size_t>(b) * H + h;      // checkpoint row
+  const size_t sunit = static_cast<size_t>(seq) * H + h;   // state (dS_T, dS_0) row
+  const int col0 = s * DVS, cg0 = col0 / 8;
+  uint32_t ld_par = 0u, ld_pending = 0u;
+
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_init(mbar_ld, 1);
+    mbar_init(mbar_ld + 1, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) { tmem_alloc(tslot, M::TCOLS); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  auto issue_chunk = [&](int cc) {
+    const int ps = cc & 1, t0 = cc * C, rv = min(C, T - t0);
+    unsigned char* set = sm + ps * M::SET;
+    if (!use_tma) {
+      stage_tile(set + M::DO, doh + (tok0 + t0) * rstride, rv, rstride);
+      cp_async_commit();
+    }
+    if (tid == kIoThread) {
+      const unsigned char* fu = factors + (unit * n_chunks + cc) * FAC_UNIT;
+      fence_async_smem();
+      mbar_expect_tx(mbar_ld + ps, 32768 + 16384 + 8192 + 512 + (use_tma ? 16384 : 0));
+      bulk_load(set + M::W, fu + FAC_W, 32768, mbar_ld + ps);  // W, Q Gam
+      bulk_load(set + M::KL, fu + FAC_KL, 16384, mbar_ld + ps);
+      bulk_load(set + M::AQ, fu + FAC_AQ, 8192, mbar_ld + ps);
+      bulk_load(set + M::GC, fu + FAC_GC, 512, mbar_ld + ps);
+      if (use_tma) tma_tile(set + M::DO, &tm_do, h, cc, b, mbar_ld + ps);
+    }
+    ld_pending |= 1u << ps;
+  };
+  if (c_beg < c_end) issue_chunk(c_end - 1);
+  const uint32_t tbase = *tslot;
+  const uint32_t T_DS = tbase, T_U = tbase + DVS;
+  const uint32_t tl = static_cast<uint32_t>(32 * qw) << 16;
+  uint32_t phase = 0;
+  bool failed = false;
+  auto mma_wait = [&]() -> bool {
+    const bool ok = mbar_wait(mbar, phase);
+    phase ^= 1u;
+    tc_fence_after();
+    return ok;
+  };
+  const int d = 32 * qw + lane, cw0 = hh * CW;
+  {  // dS_T -> TMEM (this slice)
+#pragma unroll
+    for (int j = 0; j < CW; j += CB) {
+      float vals[CB];
+#pragma unroll
+      for (int e = 0; e < CB; ++e) vals[e] = dsT ? dsT[(sunit * DK + d) * DV + col0 + cw0 + j + e] : 0.f;
+      tmem_stn_s<CB>(T_DS + tl + cw0 + j, vals);
+    }
+    tmem_wait_st();
+  }
+
+  for (int c = c_end - 1; c >= c_beg; --c) {
+    const int p = c & 1;
+    cp_async_wait<0>();
+    failed |= !mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
+    ld_par ^= 1u << p;
+    ld_pending &= ~(1u << p);
+    if (tid == kIoThread) bulk_wait_read();  // SB may be rewritten: the previous dS' slice is stored
+    if (__syncthreads_or(failed)) break;
+    const unsigned char* setp = sm + p * M::SET;
+    const uint32_t set = smem_u32(setp);
+    const float* gamC = reinterpret_cast<const float*>(setp + M::GC);
+    if (c > c_beg) issue_chunk(c - 1);  // the other set was last read by chunk c + 1
+    {  // dS' pass: bf16 operand (stored to the workspace below), then dS *= Gam_C
+      const float gcd = gamC[d];
+#pragma unroll
+      for (int j = 0; j < CW; j += CB) {
+        float vals[CB];
+        tmem_ldn_s<CB>(T_DS + tl + cw0 + j, vals);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < CB; e += 8) st16(sm + M::SB, cm_off(d, cw0 + j + e, DVS), pack_bf16x8(vals + e));
+#pragma unroll
+        for (int e = 0; e < CB; ++e) vals[e] *= gcd;
+        tmem_stn_s<CB>(T_DS + tl + cw0 + j, vals);
+      }
+      tmem_wait_st();
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == kIoThread) {  // this slice of chunk c's dS' image
+      unsigned char* img = reinterpret_cast<unsigned char*>(dsw) + (unit * n_chunks + c) * WS_UNIT;
+#pragma unroll 1
+      for (int rg = 0; rg < 16; ++rg)
+        bulk_store(img + (rg * 16 + cg0) * 128, sm + M::SB + rg * (16 * DVS), 16 * DVS);
+      bulk_commit();
+    }
+    // dU_s = (lam K) dS'_s + Aqk^T dO_s  (M = 64); filler: dS_s += (Gam Q)^T dO_s
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t sb = smem_u32(sm + M::SB), kl = set + M::KL, dob = set + M::DO + cg0 * 128,
+                     aqb = set + M::AQ, qg = set + M::QG;
+      const uint32_t id1 = idesc_bf16(64, DVS, false, true), id2 = idesc_bf16(64, DVS, true, true);
+      const uint32_t id3 = idesc_bf16(128, DVS, true, true);
+#pragma unroll 1
+      for (int ks = 0; ks < DK / 16; ++ks)
+        mma_bf16(T_U, desc_kmajor(kl + ks * 256, DK), desc_mnmajor(sb + ks * (32 * DVS), DVS), id1, ks > 0);
+#pragma unroll 1
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_U, desc_mnmajor(aqb + ks * 2048, C), desc_mnmajor(dob + ks * 4096, DV), id2, 1u);
+      mma_commit(mbar);
+#pragma unroll 1
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_DS, desc_mnmajor(qg + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id3, 1u);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // -dU_s -> bf16 CM[64][DVS] (M = 64 layout: row r at lane 32 (r / 16) + r % 16)
+      const int r = 16 * qw + lane;
+#pragma unroll
+      for (int j = 0; j < CW; j += CB) {
+        float vals[CB];
+        tmem_ldn_s<CB>(T_U + tl + cw0 + j, vals);
+        tmem_wait_ld();
+        if (lane < 16) {
+#pragma unroll
+          for (int e = 0; e < CB; ++e) vals[e] = -vals[e];
+#pragma unroll
+          for (int e = 0; e < CB; e += 8) st16(sm + M::DU, cm_off(r, cw0 + j + e, DVS), pack_bf16x8(vals + e));
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // dS_s += W^T (-dU_s)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t du = smem_u32(sm + M::DU), w = set + M::W;
+      const uint32_t id = idesc_bf16(128, DVS, true, true);
+#pragma unroll 1
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_DS, desc_mnmajor(w + ks * 4096, DK), desc_mnmajor(du + ks * (32 * DVS), DVS), id, 1u);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+  }
+  if (!failed && ds0) {
+#pragma unroll
+    for (int j = 0; j < CW; j += CB) {
+      float vals[CB];
+      tmem_ldn_s<CB>(T_DS + tl + cw0 + j, vals);
+      tmem_wait_ld();
+      float* dst = ds0 + (sunit * DK + d) * DV + col0 + cw0 + j;
+#pragma unroll
+      for (int e = 0; e < CB; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(vals[e], vals[e + 1], vals[e + 2], vals[e + 3]);
+    }
+  }
+  if (failed && tid == 0 && err) atomicExch(err, 1);
+  cp_async_wait<0>();
+  for (int ps = 0; ps < 2; ++ps)
+    if ((ld_pending >> ps) & 1u) mbar_wait(mbar_ld + ps, (ld_par >> ps) & 1u);
+  if (tid == kIoThread) bulk_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, M::TCOLS);
+}
+
+template <int DVS>
+int launch_seq_sliced(const void* dout, const unsigned char* factors, const float* dsT, float* ds0, bf16* dsw,
+                      int B, int T, int H, const int* cs, int n_seqs, int* err, const CUtensorMap& tm_do,
+                      int use_tma, cudaStream_t st) {
+  static bool done[64] = {false};
+  auto kern = bwd_seq_sliced_kernel<DVS>;
+  int rc = ensure_smem(kern, SeqSliceMap<DVS>::SMEM, done);
+  if (rc != KDA_OK) return rc;
+  const long long grid = static_cast<long long>(cs ? n_seqs : B) * H * (DV / DVS);
+  if (grid > 0x7fffffffLL) return KDA_ERR_SHAPE;
+  kern<<<static_cast<unsigned>(grid), NT, SeqSliceMap<DVS>::SMEM, st>>>(
+      static_cast<const bf16*>(dout), factors, dsT, ds0, dsw, T, H, cs, err, tm_do, use_tma);
+  return launch_status();
+}
+
 __device__ int g_bwd_tc_error = 0;
 
 int sm_count() {
@@ -1121,12 +1380,22 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
   int use_tma = 1;
   for (int i = 0; i < 5 && use_tma; ++i) use_tma = make_tile_map(&tm[i], srcs[i], B, T, H) ? 1 : 0;
   for (int i = 0; i < 4 && use_tma; ++i) use_tma = make_out_map(&to[i], outs[i], B, T, H) ? 1 : 0;
-  // the reverse state chain per sequence (batch row, or packed sequence); the
-  // chunks themselves are then independent units of one launch
-  bwd_seq_kernel<<<(cs ? n_seqs : B) * H, NT, SEQ_SMEM, st>>>(
-      static_cast<const bf16*>(beta), static_cast<const bf16*>(dout), factors, dsT, ds0, dsw, T, H, cs, err,
-      tm[4], use_tma);
-  rc = launch_status();
+  // the reverse state chain per sequence (batch row, or packed sequence), split
+  // into column slices while the (sequence, head) pairs fill at most half the
+  // SMs; the chunks themselves are then independent units of one launch
+  const long long heads = static_cast<long long>(cs ? n_seqs : B) * H;
+  int slices = 1;
+  while (slices < 8 && heads * slices * 2 <= sm_count()) slices *= 2;
+  switch (slices) {
+    case 2: rc = launch_seq_sliced<64>(dout, factors, dsT, ds0, dsw, B, T, H, cs, n_seqs, err, tm[4], use_tma, st); break;
+    case 4: rc = launch_seq_sliced<32>(dout, factors, dsT, ds0, dsw, B, T, H, cs, n_seqs, err, tm[4], use_tma, st); break;
+    case 8: rc = launch_seq_sliced<16>(dout, factors, dsT, ds0, dsw, B, T, H, cs, n_seqs, err, tm[4], use_tma, st); break;
+    default:
+      bwd_seq_kernel<<<(cs ? n_seqs : B) * H, NT, SEQ_SMEM, st>>>(
+          static_cast<const bf16*>(beta), static_cast<const bf16*>(dout), factors, dsT, ds0, dsw, T, H, cs, err,
+          tm[4], use_tma);
+      rc = launch_status();
+  }
   if (rc != KDA_OK) return rc;
   const long long units = static_cast<long long>(B) * H * ((T + C - 1) / C);
   const int grid = static_cast<int>(units < sm_count() ? units : sm_count());

@@ -290,15 +290,18 @@ def test_tc_training_forward_schedules_match_oracle(monkeypatch, schedule, B, T,
     xr, d = _bf16_inputs(B, T, H, seed=B * 1000 + T + H, s0_std=0.05)
     rng = np.random.default_rng(T + H)
     do = K.bf16_round(rng.standard_normal((B, T, H, 128)))
+    dST = rng.standard_normal((B, H, 128, 128)).astype(np.float32)
     o, s_t, ckpt = kda_fwd(d["q"], d["k"], d["v"], d["g"], d["beta"], d["S0"], chunk=64,
                            o_dtype=torch.float32, need_ckpt=True, ckpt_dtype=ck)
-    grads = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, _dev(do, torch.bfloat16), None, chunk=64)
+    # the backward's state-cotangent scan is sliced the same way (2, 4, 8 slices here)
+    grads = kda_bwd(d["q"], d["k"], d["v"], d["g"], d["beta"], ckpt, _dev(do, torch.bfloat16),
+                    _dev(dST, torch.float32), chunk=64)
     torch.cuda.synchronize()
     o_ref, s_ref, states = K.chunk_fwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], chunk=64,
                                        return_states=True)
     assert K.scale_rel_err(_np(o), o_ref) <= TOL
     assert K.scale_rel_err(_np(s_t), s_ref) <= TOL
     assert K.scale_rel_err(_np(ckpt_states(ckpt, B, T, H, 128, 128, chunk=64)), states) <= TOL
-    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, None, chunk=64)
+    ref = K.chunk_bwd(xr["q"], xr["k"], xr["v"], xr["g"], xr["beta"], xr["S0"], do, dST, chunk=64)
     for name, gr, rf in zip(GRADS, grads, ref):
         assert K.scale_rel_err(_np(gr), rf) <= TOL, name
