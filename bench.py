@@ -890,6 +890,8 @@ def main():
                     help="log-decay distribution (profiling cases; the headline is baseline)")
     ap.add_argument("--mixer-only", action="store_true",
                     help="time only the mixer kernels (prologue, output gate, fused decode); --batch sets B")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="time only the cfg4 decode step (--steps consecutive steps; profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # the timing contract needs >= 3 untimed warm-up steps
     if args.mixer_only:
@@ -899,6 +901,15 @@ def main():
         res = run_mixer_kernels(torch, torch.device("cuda", 0), _peaks(), steps=args.steps,
                                 warmup=args.warmup, B=args.batch or 4)
         print(json.dumps({"mixer_kernels": res}), flush=True)
+        return
+    if args.decode_only:
+        import torch
+
+        from axiom_b200 import kda as KD
+
+        torch.cuda.set_device(0)
+        res = run_decode(torch, KD, torch.device("cuda", 0), _peaks(), steps=args.steps, warmup=args.warmup)
+        print(json.dumps({"decode": res}), flush=True)
         return
     if args.impl == "reference":
         run_reference(args)
