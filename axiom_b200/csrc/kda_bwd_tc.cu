@@ -549,7 +549,7 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 
     // ---- the forward's W, U and v~ are resident: straight to the adjoint ----
     const float* gamC = reinterpret_cast<const float*>(sm + P_GF + 544 * (it & 1));
-    const bool slow = reinterpret_cast<const uint32_t*>(gamC)[128] != 0u;  // exact-path chunk
+    const bool slow = (reinterpret_cast<const uint32_t*>(gamC)[128] & 1u) != 0u;  // exact-path chunk (bit 0)
     if constexpr (sizeof(Tc) == 4) stage_ckpt_f32(sm + P_SB, s_ckpt + unit_sq * (DK * DV));
     cp_async_wait<0>();
     failed |= !mbar_wait(mbar_late, late_par);
@@ -1093,9 +1093,15 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 //   dU_s  = (lam K) dS'_s + Aqk^T dO_s               (M = 64, N = DVS)
 //   dS_s  = Gam_C dS'_s + (Gam Q)^T dO_s - W^T dU_s  (M = 128, N = DVS)
 // and the slice of each chunk's dS' image goes to the workspace for bwd_par.
+// When the forward's prep wrote the chain operands (FLAG_CHAIN: NP = -(lam K)^T W
+// and Q~ = Q Gam - Aqk W), the two products fold into one MMA round trip,
+//   dS_s  = Gam_C dS'_s + NP^T dS'_s + Q~^T dO_s.
 template <int DVS>
 struct SeqSliceMap {
+  // per operand set: W, Q Gam, lam K, dO, Aqk, Gam_C; with the prep's chain
+  // operands (FLAG_CHAIN) NP takes W|Q Gam and Q~ takes lam K's place
   static constexpr int W = 0, QG = 16384, KL = 32768, DO = 49152, AQ = 65536, GC = 73728;
+  static constexpr int NP = 0, QT = 32768;
   static constexpr int SET = GC + 512;
   static constexpr int SB = 2 * SET;          // dS'_s bf16 CM[128][DVS]
   static constexpr int DU = SB + 256 * DVS;   // -dU_s bf16 CM[64][DVS]
@@ -1163,6 +1169,11 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
   const size_t sunit = static_cast<size_t>(seq) * H + h;   // state (dS_T, dS_0) row
   const int col0 = s * DVS, cg0 = col0 / 8;
   uint32_t ld_par = 0u, ld_pending = 0u;
+  // every chunk of a checkpoint comes from one forward schedule: the last
+  // chunk's flags decide the form for the whole walk
+  const bool chain = c_beg < c_end &&
+                     (*reinterpret_cast<const uint32_t*>(factors + (unit * n_chunks + c_end - 1) * FAC_UNIT +
+                                                         FAC_FLAG) & FLAG_CHAIN) != 0u;
 
   if (tid == 0) {
     mbar_init(mbar, 1);
@@ -1184,10 +1195,16 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
     if (tid == kIoThread) {
       const unsigned char* fu = factors + (unit * n_chunks + cc) * FAC_UNIT;
       fence_async_smem();
-      mbar_expect_tx(mbar_ld + ps, 32768 + 16384 + 8192 + 512 + (use_tma ? 16384 : 0));
-      bulk_load(set + M::W, fu + FAC_W, 32768, mbar_ld + ps);  // W, Q Gam
-      bulk_load(set + M::KL, fu + FAC_KL, 16384, mbar_ld + ps);
-      bulk_load(set + M::AQ, fu + FAC_AQ, 8192, mbar_ld + ps);
+      if (chain) {
+        mbar_expect_tx(mbar_ld + ps, 32768 + 16384 + 512 + (use_tma ? 16384 : 0));
+        bulk_load(set + M::NP, fu + FAC_NP, 32768, mbar_ld + ps);
+        bulk_load(set + M::QT, fu + FAC_QT, 16384, mbar_ld + ps);
+      } else {
+        mbar_expect_tx(mbar_ld + ps, 32768 + 16384 + 8192 + 512 + (use_tma ? 16384 : 0));
+        bulk_load(set + M::W, fu + FAC_W, 32768, mbar_ld + ps);  // W, Q Gam
+        bulk_load(set + M::KL, fu + FAC_KL, 16384, mbar_ld + ps);
+        bulk_load(set + M::AQ, fu + FAC_AQ, 8192, mbar_ld + ps);
+      }
       bulk_load(set + M::GC, fu + FAC_GC, 512, mbar_ld + ps);
       if (use_tma) tma_tile(set + M::DO, &tm_do, h, cc, b, mbar_ld + ps);
     }
@@ -1253,6 +1270,24 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
       for (int rg = 0; rg < 16; ++rg)
         bulk_store(img + (rg * 16 + cg0) * 128, sm + M::SB + rg * (16 * DVS), 16 * DVS);
       bulk_commit();
+    }
+    if (chain) {  // dS_s += NP^T dS'_s + Q~^T dO_s: one round trip
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t sb = smem_u32(sm + M::SB), np = set + M::NP, qt = set + M::QT,
+                       dob = set + M::DO + cg0 * 128;
+        const uint32_t id = idesc_bf16(128, DVS, true, true);
+#pragma unroll 1
+        for (int ks = 0; ks < DK / 16; ++ks)
+          mma_bf16(T_DS, desc_mnmajor(np + ks * 4096, DK), desc_mnmajor(sb + ks * (32 * DVS), DVS), id, 1u);
+#pragma unroll 1
+        for (int ks = 0; ks < C / 16; ++ks)
+          mma_bf16(T_DS, desc_mnmajor(qt + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id, 1u);
+        mma_commit(mbar);
+      }
+      failed |= !mma_wait();
+      if (__syncthreads_or(failed)) break;
+      continue;
     }
     // dU_s = (lam K) dS'_s + Aqk^T dO_s  (M = 64); filler: dS_s += (Gam Q)^T dO_s
     if (tid == 0) {

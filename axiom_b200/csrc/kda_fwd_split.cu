@@ -198,7 +198,7 @@ fwd_prep_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf
       bulk_store(fu + FAC_KL, sm + R_KL, 16384);
       bulk_store(fu + FAC_GC, gamC, 512);
       bulk_commit();
-      *reinterpret_cast<uint32_t*>(fu + FAC_FLAG) = slow_chunk ? 1u : 0u;
+      *reinterpret_cast<uint32_t*>(fu + FAC_FLAG) = (slow_chunk ? FLAG_EXACT : 0u) | FLAG_CHAIN;
     };
     // ---- decay prep: [G ; G_C - G] = [L ; U'] g on the tensor core
     if (tid == 0) {
@@ -370,10 +370,37 @@ fwd_prep_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf
       bulk_store(fu + FAC_AK, sm + R_SB, 8192);
       bulk_commit();
     }
-    // ---- W = (T beta) (K Gam), U = (T beta) V: M = 64 (row r at TMEM lane 32 (r / 16) + r % 16)
+    // ---- P = Aqk T  (M = 64: row r at TMEM lane 32 (r / 16) + r % 16)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t idesc = idesc_bf16(64, 128, false, true);
+      const uint32_t idesc = idesc_bf16(64, 64, false, true);
+      const uint32_t tb = smem_u32(sm + R_VT), aqb = smem_u32(sm + R_VT + 8192);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_D, desc_kmajor(aqb + ks * 256, C), desc_mnmajor(tb + ks * 2048, C), idesc, ks > 0);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (__syncthreads_or(failed)) break;
+    {  // P diag(beta) -> rows 64..127 of the [T b ; P b] operand
+      float vals[32];
+      tmem_ld32(T_D + t_lane + hh * 32, vals);
+      tmem_wait_ld();
+      if (lane < 16) {
+        const int r = 16 * qw + lane;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) vals[j] *= beta_s[hh * 32 + j];
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) st16(sm + R_TP, cm_off(64 + r, hh * 32 + j, C), pack_bf16x8(vals + j));
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- [T b ; P b] [K Gam | V] -> W, U (rows 0..63), Aqk W, Aqk U (rows 64..127)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16(128, 128, false, true);
       const uint32_t tp = smem_u32(sm + R_TP);
 #pragma unroll
       for (int ks = 0; ks < C / 16; ++ks) {
@@ -384,32 +411,75 @@ fwd_prep_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf
       mma_commit(mbar);
     }
     failed |= !mma_wait();
+    if (tid == kIoThread) bulk_wait_read<1>();  // Q Gam, K Gam have left A3 (E2 overwrites Q Gam)
     if (__syncthreads_or(failed)) break;
     if (has_nx) stage(u_nx, false);  // V has been consumed
-    // ---- W -> A3 rows 0..63 (stored below), U -> the checkpoint.  The TMEM loads
-    // are warp-collective; lanes 16..31 read lanes that hold no row and store nothing.
+    // ---- E2: W -> A3 rows 0..63, U -> the checkpoint; Q~ = Q Gam - Aqk W -> A3 rows
+    // 64..127, Aqk U -> the checkpoint
     {
-      const int r = 16 * qw + lane;
+      const int R = 32 * qw + lane;
       for (int half = 0; half < 2; ++half) {
         const int c0 = hh * 64 + half * 32;
-        float w[32], uu[32];
-        tmem_ld32(T_D + t_lane + c0, w);
+        float wv[32], uu[32];
+        tmem_ld32(T_D + t_lane + c0, wv);
         tmem_ld32(T_D + t_lane + 128 + c0, uu);
         tmem_wait_ld();
-        if (lane < 16) {
+        const size_t fo = R < 64 ? FAC_U : FAC_AU;
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            st16(A3, cm_off(r, c0 + j, DK), pack_bf16x8(w + j));
-            *reinterpret_cast<uint4*>(fu + FAC_U + cm_off(r, c0 + j, DV)) = pack_bf16x8(uu + j);
+        for (int j = 0; j < 32; j += 8) {
+          const uint32_t off = cm_off(R, c0 + j, DK);  // rows 64..127 of A3 hold Q Gam
+          if (R < 64) {
+            st16(A3, off, pack_bf16x8(wv + j));
+          } else {
+            float qg[8];
+            unpack_bf16x8(ld16(A3, off), qg);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qg[e] -= wv[j + e];
+            st16(A3, off, pack_bf16x8(qg));
           }
+          *reinterpret_cast<uint4*>(fu + fo + cm_off(R & 63, c0 + j, DV)) = pack_bf16x8(uu + j);
         }
       }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (tid == kIoThread) {
+    if (tid == kIoThread) {  // W, then Q~
       bulk_store(fu + FAC_W, A3, 16384);
+      bulk_store(fu + FAC_QT, A3 + 16384, 16384);
+      bulk_commit();
+    }
+    // ---- NP = -(lam K)^T W  (M = dk = 128, N = dk, K = C)
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16(128, 128, true, true);
+      const uint32_t kl = smem_u32(sm + R_KL);
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_D, desc_mnmajor(kl + ks * 4096, DK), desc_mnmajor(a3_addr + ks * 4096, DK), idesc, ks > 0);
+      mma_commit(mbar);
+    }
+    failed |= !mma_wait();
+    if (tid == kIoThread) bulk_wait_read<1>();  // T, Aqk, Akk have left VT and SB
+    if (__syncthreads_or(failed)) break;
+    {  // row i of NP = TMEM lane i -> bf16 CM [128][128] in SB (32 KB)
+      const int i = 32 * qw + lane;
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float pv[32];
+        tmem_ld32(T_D + t_lane + c0, pv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pv[j] = -pv[j];
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) st16(sm + R_SB, cm_off(i, c0 + j, DK), pack_bf16x8(pv + j));
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == kIoThread) {
+      bulk_store(fu + FAC_NP, sm + R_SB, 32768);
       bulk_commit();
     }
   }
@@ -424,25 +494,24 @@ fwd_prep_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf
 }
 
 // ===========================================================================
-// fwd_scan
+// fwd_scan: the state chain only
 // ===========================================================================
-// Chunk c's operands land in set (c - c_beg) & 1 while chunk c - 1 runs on the
-// other: [W ; Q Gam] (adjacent in the factor block), lam K, Aqk, the slice of
-// U and Gam_C, all bulk copies from the factor block.
+// S_{c+1} = Gam_C S_c + (lam K)^T U + NP S_c with NP = -(lam K)^T W (the prep's
+// FAC_NP): one MMA round trip per chunk.  Chunk c's operands (NP, lam K, the
+// slice of U, Gam_C) land in set (c - c_beg) & 1 while chunk c - 1 runs.
 template <int DVS>
 struct ScanMap {
-  static constexpr int WQ = 0, KL = 32768, AQ = 49152, US = 57344;
+  static constexpr int NP = 0, KL = 32768, US = 49152;
   static constexpr int GC = US + 128 * DVS;
   static constexpr int SET = GC + 512;
   static constexpr int SB = 2 * SET;          // S_s bf16 CM[128][DVS] (the MMA operand and checkpoint image)
-  static constexpr int VT = SB + 256 * DVS;   // v~_s bf16 CM[64][DVS]
-  static constexpr int BAR = VT + 128 * DVS;
+  static constexpr int BAR = SB + 256 * DVS;
   static constexpr int SMEM = BAR + 64;
-  static constexpr uint32_t TX = 32768 + 16384 + 8192 + 128 * DVS + 512;
-  static constexpr int TCOLS = 3 * DVS <= 32 ? 32 : (3 * DVS <= 64 ? 64 : (3 * DVS <= 128 ? 128 : (3 * DVS <= 256 ? 256 : 512)));
+  static constexpr uint32_t TX = 32768 + 16384 + 128 * DVS + 512;
+  static constexpr int TCOLS = DVS <= 32 ? 32 : DVS;
 };
 
-// TMEM loads of N columns (8, 16 or 32) of this warp's 32 lanes.
+// TMEM loads / stores of N columns (8, 16 or 32) of this warp's 32 lanes.
 template <int N>
 __device__ __forceinline__ void tmem_ldn(uint32_t taddr, float* v) {
   if constexpr (N == 32) tmem_ld32(taddr, v);
@@ -484,15 +553,15 @@ __device__ __forceinline__ void store_cols<bf16>(bf16* dst, const float* v, int 
   for (int j = 0; j < n; j += 8) *reinterpret_cast<uint4*>(dst + j) = pack_bf16x8(v + j);
 }
 
-template <typename To, typename Tc, int DVS>
+template <typename Tc, int DVS>
 __global__ void __launch_bounds__(NT, 1)
-fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restrict__ s0, To* __restrict__ o,
+fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restrict__ s0,
                 float* __restrict__ s_out, Tc* __restrict__ s_ckpt, int T, int H, const int* __restrict__ cs,
                 int* __restrict__ err) {
   using M = ScanMap<DVS>;
   constexpr int NS = DV / DVS;     // slices per head
   constexpr int CW = DVS / 2;      // columns per thread (each warp: one lane quarter, one column half)
-  constexpr int CB = CW < 32 ? CW : 32;  // columns per TMEM load
+  constexpr int CB = CW < 32 ? CW : 32;  // columns per TMEM access
   extern __shared__ __align__(1024) unsigned char sm[];
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + M::BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + M::BAR + 8);
@@ -508,7 +577,6 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
   const int b = cs ? 0 : seq;
   const int c_beg = cs ? min(max(cs[seq], 0), n_chunks) : 0;
   const int c_end = cs ? min(max(cs[seq + 1], c_beg), n_chunks) : n_chunks;
-  const size_t tok0 = static_cast<size_t>(b) * T;
   const size_t unit0 = (static_cast<size_t>(b) * H + h) * n_chunks;  // factor / checkpoint row
   const int col0 = s * DVS;           // this CTA's state columns [col0, col0 + DVS)
   const int cg0 = col0 / 8;           // ... as core-matrix columns
@@ -531,9 +599,8 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
       const unsigned char* fu = factors + (unit0 + cc) * FAC_UNIT;
       fence_async_smem();  // the set's generic reads (chunk cc - 2) precede the copies' writes
       mbar_expect_tx(mbar_ld + p, M::TX);
-      bulk_load(set + M::WQ, fu + FAC_W, 32768, mbar_ld + p);  // W, Q Gam
+      bulk_load(set + M::NP, fu + FAC_NP, 32768, mbar_ld + p);
       bulk_load(set + M::KL, fu + FAC_KL, 16384, mbar_ld + p);
-      bulk_load(set + M::AQ, fu + FAC_AQ, 8192, mbar_ld + p);
 #pragma unroll 1
       for (int rg = 0; rg < 8; ++rg)
         bulk_load(set + M::US + rg * (16 * DVS), fu + FAC_U + (rg * 16 + cg0) * 128, 16 * DVS, mbar_ld + p);
@@ -548,15 +615,9 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
   tc_fence_after();
   const uint32_t tbase = *tslot;
   const uint32_t tl = static_cast<uint32_t>(32 * qw) << 16;
-  const uint32_t T_S = tbase, T_W = tbase + DVS, T_Q = tbase + 2 * DVS;
+  const uint32_t T_S = tbase;
   uint32_t phase = 0;
   bool failed = false;
-  auto mma_wait = [&]() -> bool {
-    const bool ok = mbar_wait(mbar, phase);
-    phase ^= 1u;
-    tc_fence_after();
-    return ok;
-  };
   const int d = 32 * qw + lane;  // the state row this thread moves
   const int cw0 = hh * CW;       // its first column within the slice
   {  // S0 -> TMEM
@@ -570,18 +631,6 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
     }
     tmem_wait_st();
   }
-  // O of chunk cc from T_Q (M = 64 layout: row r at lane 32 (r / 16) + r % 16)
-  auto store_o = [&](int cc) {
-    float vals[CB];
-    const int r = 16 * qw + lane, rv = min(C, T - cc * C);
-#pragma unroll
-    for (int j = 0; j < CW; j += CB) {
-      tmem_ldn<CB>(T_Q + tl + cw0 + j, vals);
-      tmem_wait_ld();
-      if (lane < 16 && r < rv)
-        store_cols<To>(o + ((tok0 + static_cast<size_t>(cc) * C + r) * H + h) * DV + col0 + cw0 + j, vals, CB);
-    }
-  };
 
   for (int c = c_beg; c < c_end; ++c) {
     const int p = (c - c_beg) & 1;
@@ -589,12 +638,11 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
     failed |= !mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
     ld_par ^= 1u << p;
     ld_pending &= ~(1u << p);
-    if (tid == kIoThread) bulk_wait_read<1>();  // the previous S_s image has been stored (v~ may pend)
+    if (tid == kIoThread) bulk_wait_read();  // the previous S_s image has been stored
     if (__syncthreads_or(failed)) break;
     if (c + 1 < c_end) issue(c + 1);  // the other set's last reader, chunk c - 1, has completed
-    if (c > c_beg) store_o(c - 1);
     // ---- S pass: S_s -> bf16 operand (+ checkpoint), S_s *= Gam_C
-    Tc* ck = s_ckpt ? s_ckpt + (unit0 + c) * (DK * DV) : nullptr;
+    Tc* ck = s_ckpt + (unit0 + c) * (DK * DV);
     {
       const float gcd = reinterpret_cast<const float*>(set + M::GC)[d];
 #pragma unroll
@@ -604,7 +652,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < CB; e += 8) st16(sm + M::SB, cm_off(d, cw0 + j + e, DVS), pack_bf16x8(vals + e));
-        if (sizeof(Tc) == 4 && ck) store_cols<float>(reinterpret_cast<float*>(ck) + d * DV + col0 + cw0 + j, vals, CB);
+        if (sizeof(Tc) == 4) store_cols<float>(reinterpret_cast<float*>(ck) + d * DV + col0 + cw0 + j, vals, CB);
 #pragma unroll
         for (int e = 0; e < CB; ++e) vals[e] *= gcd;
         tmem_stn<CB>(T_S + tl + cw0 + j, vals);
@@ -615,7 +663,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
     tc_fence_before();
     __syncthreads();
     if (tid == kIoThread) {  // the slice of the bf16 state image (one bulk group per chunk, maybe empty)
-      if (sizeof(Tc) == 2 && ck) {
+      if (sizeof(Tc) == 2) {
         unsigned char* img = reinterpret_cast<unsigned char*>(ck);
 #pragma unroll 1
         for (int rg = 0; rg < 16; ++rg)
@@ -623,70 +671,25 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
       }
       bulk_commit();
     }
-    // ---- W S_s and (Q Gam) S_s  (M = 64 each, K = dk)
+    // ---- S_s += (lam K)^T U_s + NP S_s  (M = dk, N = DVS)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t idesc = idesc_bf16(64, DVS, false, true);
-      const uint32_t wq = smem_u32(set + M::WQ), sb = smem_u32(sm + M::SB);
+      const uint32_t id = idesc_bf16(128, DVS, true, true), id_np = idesc_bf16(128, DVS, false, true);
+      const uint32_t kl = smem_u32(set + M::KL), us = smem_u32(set + M::US), np = smem_u32(set + M::NP);
+      const uint32_t sb = smem_u32(sm + M::SB);
 #pragma unroll
-      for (int ks = 0; ks < DK / 16; ++ks) {
-        const uint64_t bd = desc_mnmajor(sb + ks * (32 * DVS), DVS);
-        mma_bf16(T_W, desc_kmajor(wq + ks * 256, DK), bd, idesc, ks > 0);
-        mma_bf16(T_Q, desc_kmajor(wq + 16384 + ks * 256, DK), bd, idesc, ks > 0);
-      }
+      for (int ks = 0; ks < C / 16; ++ks)
+        mma_bf16(T_S, desc_mnmajor(kl + ks * 4096, DK), desc_mnmajor(us + ks * (32 * DVS), DVS), id, 1u);
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks)
+        mma_bf16(T_S, desc_kmajor(np + ks * 256, DK), desc_mnmajor(sb + ks * (32 * DVS), DVS), id_np, 1u);
       mma_commit(mbar);
     }
-    failed |= !mma_wait();
-    if (tid == kIoThread) bulk_wait_read<1>();  // the previous v~ image has been stored
-    if (__syncthreads_or(failed)) break;
-    // ---- v~_s = U_s - W S_s  (bf16, the MMA operand and the checkpoint's image)
-    {
-      const int r = 16 * qw + lane;
-#pragma unroll
-      for (int j = 0; j < CW; j += CB) {
-        float ws[CB];
-        tmem_ldn<CB>(T_W + tl + cw0 + j, ws);
-        tmem_wait_ld();
-        if (lane < 16) {
-#pragma unroll
-          for (int e = 0; e < CB; e += 8) {
-            float u[8];
-            const uint32_t off = cm_off(r, cw0 + j + e, DVS);
-            unpack_bf16x8(ld16(set + M::US, off), u);
-#pragma unroll
-            for (int x = 0; x < 8; ++x) u[x] -= ws[e + x];
-            st16(sm + M::VT, off, pack_bf16x8(u));
-          }
-        }
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == kIoThread) {  // the slice of v~ (one bulk group per chunk)
-      unsigned char* fu = const_cast<unsigned char*>(factors) + (unit0 + c) * FAC_UNIT;
-#pragma unroll 1
-      for (int rg = 0; rg < 8; ++rg)
-        bulk_store(fu + FAC_VT + (rg * 16 + cg0) * 128, sm + M::VT + rg * (16 * DVS), 16 * DVS);
-      bulk_commit();
-    }
-    // ---- O_s += Aqk v~_s (M = 64, onto (Q Gam) S_s);  S_s += (lam K)^T v~_s (M = 128)
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t vt = smem_u32(sm + M::VT), aq = smem_u32(set + M::AQ), kl = smem_u32(set + M::KL);
-      const uint32_t id_o = idesc_bf16(64, DVS, false, true), id_s = idesc_bf16(128, DVS, true, true);
-#pragma unroll
-      for (int ks = 0; ks < C / 16; ++ks) {
-        const uint64_t bd = desc_mnmajor(vt + ks * (32 * DVS), DVS);
-        mma_bf16(T_Q, desc_kmajor(aq + ks * 256, C), bd, id_o, 1u);
-        mma_bf16(T_S, desc_mnmajor(kl + ks * 4096, DK), bd, id_s, 1u);
-      }
-      mma_commit(mbar);
-    }
-    failed |= !mma_wait();
+    failed |= !mbar_wait(mbar, phase);
+    phase ^= 1u;
+    tc_fence_after();
     if (__syncthreads_or(failed)) break;
   }
-  if (!failed && c_beg < c_end) store_o(c_end - 1);
   if (!failed && s_out) {
     float* so = s_out + ((static_cast<size_t>(seq) * H + h) * DK + d) * DV + col0 + cw0;
 #pragma unroll
@@ -707,17 +710,155 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
   if (warp == 0) tmem_dealloc(tbase, M::TCOLS);
 }
 
-template <typename To, typename Tc, int DVS>
-int launch_scan(const unsigned char* factors, const float* s0, void* o, float* s_out, void* s_ckpt, int B,
-                int T, int H, const int* cs, int n_seqs, int* err, cudaStream_t st) {
+// ===========================================================================
+// fwd_out: the chunk outputs, chunk-parallel
+// ===========================================================================
+// With every chunk's entering state in the checkpoint, each unit is
+// independent: [W ; Q~] S_c (one M = 128 MMA) gives W S_c and Q~ S_c, then
+//   v~ = U - W S_c  (bf16, the backward's FAC_VT)     O = Q~ S_c + Aqk U.
+// Persistent over the units; a unit's operands (S_c, [W ; Q~], U, Aqk U) land in
+// set it & 1 while the previous unit runs.
+constexpr int O_SC = 0, O_WQ = 32768, O_U = 65536, O_AU = 81920, O_SET = 98304;
+constexpr int O_VT = 2 * O_SET;       // v~ bf16 CM [64][128] (stored to the checkpoint)
+constexpr int O_BAR = O_VT + 16384;
+constexpr int OUT_SMEM = O_BAR + 64;
+
+template <typename To, typename Tc>
+__global__ void __launch_bounds__(NT, 1)
+fwd_out_kernel(unsigned char* __restrict__ factors, const Tc* __restrict__ s_ckpt, To* __restrict__ o, int B,
+               int T, int H, int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + O_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + O_BAR + 8);
+  uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + O_BAR + 16);  // [2]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qw = warp & 3, hh = warp >> 2;
+  const int n_chunks = (T + C - 1) / C;
+  const long long n_units = static_cast<long long>(B) * H * n_chunks;
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_init(mbar_ld, 1);
+    mbar_init(mbar_ld + 1, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 256);
+    tmem_relinquish();
+  }
+  uint32_t ld_par = 0u, ld_pending = 0u;
+  // (fp32 checkpoint states are converted by all threads when the unit starts)
+  auto issue = [&](long long uu, int p) {
+    unsigned char* set = sm + p * O_SET;
+    if (tid == kIoThread) {
+      const unsigned char* fu = factors + static_cast<size_t>(uu) * FAC_UNIT;
+      fence_async_smem();
+      mbar_expect_tx(mbar_ld + p, 16384 * 4 + (sizeof(Tc) == 2 ? 32768 : 0));  // one arrival per phase
+      if (sizeof(Tc) == 2)
+        bulk_load(set + O_SC, s_ckpt + static_cast<size_t>(uu) * (DK * DV), 32768, mbar_ld + p);
+      bulk_load(set + O_WQ, fu + FAC_W, 16384, mbar_ld + p);
+      bulk_load(set + O_WQ + 16384, fu + FAC_QT, 16384, mbar_ld + p);
+      bulk_load(set + O_U, fu + FAC_U, 16384, mbar_ld + p);
+      bulk_load(set + O_AU, fu + FAC_AU, 16384, mbar_ld + p);
+    }
+    ld_pending |= 1u << p;
+  };
+  __syncthreads();
+  const long long u0 = blockIdx.x;
+  if (u0 < n_units) issue(u0, 0);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t tl = static_cast<uint32_t>(32 * qw) << 16;
+  uint32_t phase = 0;
+  bool failed = false;
+  int it = 0;
+  for (long long u = u0; u < n_units; u += gridDim.x, ++it) {
+    const int p = it & 1;
+    unsigned char* set = sm + p * O_SET;
+    int b, h, c;
+    unit_coords(u, n_chunks, H, b, h, c);
+    if (sizeof(Tc) == 4) {  // fp32 checkpoint states (row-major) -> bf16 CM operand
+      const float* src = reinterpret_cast<const float*>(s_ckpt) + static_cast<size_t>(u) * (DK * DV);
+      for (int i = tid; i < 128 * 16; i += NT) {
+        const int r = i >> 4, cg = i & 15;
+        const float4 x0 = *reinterpret_cast<const float4*>(src + r * 128 + cg * 8);
+        const float4 x1 = *reinterpret_cast<const float4*>(src + r * 128 + cg * 8 + 4);
+        const float f[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        st16(set + O_SC, cm_off(r, cg * 8, DV), pack_bf16x8(f));
+      }
+      fence_async_smem();
+    }
+    failed |= !mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
+    ld_par ^= 1u << p;
+    ld_pending &= ~(1u << p);
+    if (tid == kIoThread) bulk_wait_read();  // the previous unit's v~ has been stored
+    if (__syncthreads_or(failed)) break;
+    if (u + gridDim.x < n_units) issue(u + gridDim.x, p ^ 1);  // the other set's unit has completed
+    if (tid == 0) {  // [W ; Q~] S_c
+      tc_fence_after();
+      const uint32_t id = idesc_bf16(128, 128, false, true);
+      const uint32_t wq = smem_u32(set + O_WQ), sc = smem_u32(set + O_SC);
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks)
+        mma_bf16(tbase, desc_kmajor(wq + ks * 256, DK), desc_mnmajor(sc + ks * 4096, DV), id, ks > 0);
+      mma_commit(mbar);
+    }
+    failed |= !mbar_wait(mbar, phase);
+    phase ^= 1u;
+    tc_fence_after();
+    if (__syncthreads_or(failed)) break;
+    {
+      const int R = 32 * qw + lane, r = R & 63, rv = min(C, T - c * C);
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = hh * 64 + half * 32;
+        float x[32];
+        tmem_ld32(tbase + tl + c0, x);
+        tmem_wait_ld();
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) unpack_bf16x8(ld16(set + (R < 64 ? O_U : O_AU), cm_off(r, c0 + j, DV)), y + j);
+        if (R < 64) {  // v~ = U - W S_c
+#pragma unroll
+          for (int j = 0; j < 32; ++j) y[j] -= x[j];
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) st16(sm + O_VT, cm_off(r, c0 + j, DV), pack_bf16x8(y + j));
+        } else if (r < rv) {  // O = Q~ S_c + Aqk U
+#pragma unroll
+          for (int j = 0; j < 32; ++j) y[j] += x[j];
+          store_cols<To>(o + ((static_cast<size_t>(b) * T + static_cast<size_t>(c) * C + r) * H + h) * DV + c0, y, 32);
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == kIoThread) {
+      bulk_store(factors + static_cast<size_t>(u) * FAC_UNIT + FAC_VT, sm + O_VT, 16384);
+      bulk_commit();
+    }
+  }
+  if (failed && tid == 0 && err) atomicExch(err, 1);
+  for (int p = 0; p < 2; ++p)
+    if ((ld_pending >> p) & 1u) mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
+  if (tid == kIoThread) bulk_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tbase, 256);
+}
+
+template <typename Tc, int DVS>
+int launch_scan(const unsigned char* factors, const float* s0, float* s_out, void* s_ckpt, int B, int T, int H,
+                const int* cs, int n_seqs, int* err, cudaStream_t st) {
   static bool done[64] = {false};
-  auto kern = fwd_scan_kernel<To, Tc, DVS>;
+  auto kern = fwd_scan_kernel<Tc, DVS>;
   int rc = ensure_smem(kern, ScanMap<DVS>::SMEM, done);
   if (rc != KDA_OK) return rc;
   const long long grid = static_cast<long long>(cs ? n_seqs : B) * H * (DV / DVS);
   if (grid > 0x7fffffffLL) return KDA_ERR_SHAPE;
-  kern<<<static_cast<unsigned>(grid), NT, ScanMap<DVS>::SMEM, st>>>(
-      factors, s0, static_cast<To*>(o), s_out, static_cast<Tc*>(s_ckpt), T, H, cs, err);
+  kern<<<static_cast<unsigned>(grid), NT, ScanMap<DVS>::SMEM, st>>>(factors, s0, s_out, static_cast<Tc*>(s_ckpt),
+                                                                   T, H, cs, err);
   return launch_status();
 }
 
@@ -750,12 +891,19 @@ int launch_split(const void* q, const void* k, const void* v, const void* g, con
   rc = launch_status();
   if (rc != KDA_OK) return rc;
   switch (slices) {
-    case 1: return launch_scan<To, Tc, 128>(factors, s0, o, s_out, s_ckpt, B, T, H, cs, n_seqs, err, st);
-    case 2: return launch_scan<To, Tc, 64>(factors, s0, o, s_out, s_ckpt, B, T, H, cs, n_seqs, err, st);
-    case 4: return launch_scan<To, Tc, 32>(factors, s0, o, s_out, s_ckpt, B, T, H, cs, n_seqs, err, st);
-    case 8: return launch_scan<To, Tc, 16>(factors, s0, o, s_out, s_ckpt, B, T, H, cs, n_seqs, err, st);
+    case 1: rc = launch_scan<Tc, 128>(factors, s0, s_out, s_ckpt, B, T, H, cs, n_seqs, err, st); break;
+    case 2: rc = launch_scan<Tc, 64>(factors, s0, s_out, s_ckpt, B, T, H, cs, n_seqs, err, st); break;
+    case 4: rc = launch_scan<Tc, 32>(factors, s0, s_out, s_ckpt, B, T, H, cs, n_seqs, err, st); break;
+    case 8: rc = launch_scan<Tc, 16>(factors, s0, s_out, s_ckpt, B, T, H, cs, n_seqs, err, st); break;
     default: return KDA_ERR_SHAPE;
   }
+  if (rc != KDA_OK) return rc;
+  static bool done_out[64] = {false};
+  auto out = fwd_out_kernel<To, Tc>;
+  rc = ensure_smem(out, OUT_SMEM, done_out);
+  if (rc != KDA_OK) return rc;
+  out<<<grid, NT, OUT_SMEM, st>>>(factors, static_cast<const Tc*>(s_ckpt), static_cast<To*>(o), B, T, H, err);
+  return launch_status();
 }
 
 }  // namespace

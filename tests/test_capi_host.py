@@ -51,9 +51,10 @@ def test_ckpt_bytes():
     units = 4 * 32 * 128
     # tensor-core path: states, then per chunk-head T, Aqk, Akk (3 x 64 x 64 bf16),
     # W, Q Gam, K Gam, K Gam^-1, lam K, v~, U (7 x 64 x 128 bf16), Gam_C (128 fp32)
-    # and a flag, padded to a 16-byte multiple
-    factors = 3 * 64 * 64 * 2 + 7 * 64 * 128 * 2 + 128 * 4 + 512
-    assert factors == 140288
+    # and the flags (padded to 16 bytes), then the state-chain operands of the
+    # split forward: NP (128 x 128 bf16), Q~ and Aqk U (2 x 64 x 128 bf16)
+    factors = 3 * 64 * 64 * 2 + 7 * 64 * 128 * 2 + 128 * 4 + 512 + 128 * 128 * 2 + 2 * 64 * 128 * 2
+    assert factors == 205824
     assert lib.kda_ckpt_bytes(4, 8192, 32, 128, 128, 64, 1, 1) == units * (128 * 128 * 2 + factors)
     assert lib.kda_ckpt_bytes(4, 8192, 32, 128, 128, 64, 1, 0) == units * (128 * 128 * 4 + factors)
     # exact path: states only
