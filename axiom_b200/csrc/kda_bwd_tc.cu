@@ -1378,6 +1378,9 @@ int launch_seq_sliced(const void* dout, const unsigned char* factors, const floa
 }
 
 __device__ int g_bwd_tc_error = 0;
+}  // namespace
+int tc_scan_slices(long long heads, int n_sm);  // kda_fwd_split.cu
+namespace {
 
 int sm_count() {
   static int cached[64] = {0};
@@ -1419,8 +1422,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
   // into column slices while the (sequence, head) pairs fill at most half the
   // SMs; the chunks themselves are then independent units of one launch
   const long long heads = static_cast<long long>(cs ? n_seqs : B) * H;
-  int slices = 1;
-  while (slices < 8 && heads * slices * 2 <= sm_count()) slices *= 2;
+  const int slices = tc_scan_slices(heads, sm_count());
   switch (slices) {
     case 2: rc = launch_seq_sliced<64>(dout, factors, dsT, ds0, dsw, B, T, H, cs, n_seqs, err, tm[4], use_tma, st); break;
     case 4: rc = launch_seq_sliced<32>(dout, factors, dsT, ds0, dsw, B, T, H, cs, n_seqs, err, tm[4], use_tma, st); break;

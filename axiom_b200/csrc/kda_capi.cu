@@ -57,7 +57,9 @@ bool use_split_forward(long long heads) {
   const char* e = std::getenv("KDA_FWD_SCHEDULE");
   if (e && std::strcmp(e, "fused") == 0) return false;
   if (e && std::strcmp(e, "split") == 0) return true;
-  return kda::tc_fwd_split_slices(heads) >= 2;
+  int dev = 0, n_sm = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  return 2 * heads <= n_sm;
 }
 
 int check_dims(int B, int T, int H, int dk, int dv, int chunk) {

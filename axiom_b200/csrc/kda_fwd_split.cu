@@ -23,6 +23,8 @@
 // The fused kernel (kda_fwd_tc.cu) does both in one CTA per head; it stays the
 // path without a checkpoint (inference), where there is no factor block to hand
 // the work over in.
+#include <cstdlib>
+
 #include "kda_chunk.cuh"
 #include "kda_ckpt_layout.h"
 #include "kda_tma.cuh"
@@ -909,13 +911,24 @@ int launch_split(const void* q, const void* k, const void* v, const void* g, con
 }  // namespace
 
 // The number of column slices per head for `heads` (sequence, head) pairs: the
-// largest of 1, 2, 4, 8 that keeps the scan's CTAs within one per SM.
-int tc_fwd_split_slices(long long heads) {
-  int dev = 0, n_sm = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+// largest of 1, 2, 4, 8 that keeps the scans' CTAs within one per SM, or the
+// value of the environment variable KDA_SCAN_SLICES (1, 2, 4 or 8) when set.
+// Used by the forward's and the backward's state scans alike.
+int tc_scan_slices(long long heads, int n_sm) {
+  const char* e = std::getenv("KDA_SCAN_SLICES");
+  if (e) {
+    const int v = std::atoi(e);
+    if (v == 1 || v == 2 || v == 4 || v == 8) return v;
+  }
   int s = 1;
   while (s < 8 && heads * s * 2 <= n_sm) s *= 2;
   return s;
+}
+
+int tc_fwd_split_slices(long long heads) {
+  int dev = 0, n_sm = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  return tc_scan_slices(heads, n_sm);
 }
 
 int tc_fwd_split_launch(const void* q, const void* k, const void* v, const void* g, const void* beta,

@@ -279,20 +279,21 @@ def layer_mesh(n_head_groups: int = 1, group=None) -> LayerMesh:
     return LayerMesh(n_seq, n_head_groups, s_idx, h_idx, head_groups[s_idx], dp_groups[h_idx])
 
 
-def choose_head_groups(lengths: Sequence[int], world: int, H: int) -> int:
-    """Head-group count for a ``world``-rank mesh that minimises the busiest
-    rank's work, (tokens of its sequence group) x (heads per rank), over the
-    divisors of ``world`` that also divide ``H``; ties go to fewer head groups
-    (less communication)."""
-    best, best_cost = 1, None
+def choose_head_groups(lengths: Sequence[int], world: int, H: int, slack: float = 0.10) -> int:
+    """Head-group count for a ``world``-rank mesh.  The busiest rank's work is
+    (tokens of its sequence group) x (heads per rank); splitting heads balances
+    it perfectly but all-reduces a ``[tokens, d_model]`` activation twice per
+    step, while splitting sequences only all-reduces the weight gradients.  So
+    the fewest head groups (over the divisors of ``world`` that also divide
+    ``H``) whose busiest rank is within ``slack`` of the best balance wins."""
+    costs = {}
     for hg in range(1, world + 1):
         if world % hg or H % hg:
             continue
         groups = assign_sequences(lengths, world // hg)
-        cost = max(sum(int(lengths[i]) for i in gr) for gr in groups) * (H // hg)
-        if best_cost is None or cost < best_cost:
-            best, best_cost = hg, cost
-    return best
+        costs[hg] = max(sum(int(lengths[i]) for i in gr) for gr in groups) * (H // hg)
+    best = min(costs.values())
+    return min(hg for hg, c in costs.items() if c <= (1.0 + slack) * best)
 
 
 class _CopyToHeadGroup(torch.autograd.Function):

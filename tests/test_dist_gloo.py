@@ -131,12 +131,17 @@ def test_sequence_assignment_balances_whole_sequences():
     L = rng.uniform(512, 8192, 16)
     L = np.floor(L / L.sum() * 65536).astype(int)
     L[-1] += 65536 - int(L.sum())
-    hg = D.choose_head_groups(L.tolist(), 8, 16)
-    assert hg in (1, 2, 4, 8)
-    cost = max(sum(L[i] for i in gr) for gr in D.assign_sequences(L.tolist(), 8 // hg)) * (16 // hg)
-    for h2 in (1, 2, 4, 8):
-        c2 = max(sum(L[i] for i in gr) for gr in D.assign_sequences(L.tolist(), 8 // h2)) * (16 // h2)
-        assert cost <= c2
+    def cost(w, h2):
+        return max(sum(L[i] for i in gr) for gr in D.assign_sequences(L.tolist(), w // h2)) * (16 // h2)
+
+    for world in (2, 4, 8):
+        hg = D.choose_head_groups(L.tolist(), world, 16)
+        best = min(cost(world, h2) for h2 in (1, 2, 4, 8) if world % h2 == 0)
+        # the fewest head groups within 10 % of the best-balanced mesh
+        assert cost(world, hg) <= 1.1 * best
+        assert all(cost(world, h2) > 1.1 * best for h2 in (1, 2, 4) if h2 < hg)
+    assert D.choose_head_groups(L.tolist(), 2, 16) == 1      # sequences balance two ranks
+    assert D.choose_head_groups(L.tolist(), 8, 16) == 2      # ... but not eight
 
 
 def _mesh_worker(rank, world, port, n_head_groups, out_path):
