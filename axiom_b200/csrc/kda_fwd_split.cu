@@ -911,9 +911,12 @@ int launch_split(const void* q, const void* k, const void* v, const void* g, con
 }  // namespace
 
 // The number of column slices per head for `heads` (sequence, head) pairs: the
-// largest of 1, 2, 4, 8 that keeps the scans' CTAs within one per SM, or the
-// value of the environment variable KDA_SCAN_SLICES (1, 2, 4 or 8) when set.
-// Used by the forward's and the backward's state scans alike.
+// largest of 1, 2, 4 that keeps the scans' CTAs within one per SM, or the value
+// of the environment variable KDA_SCAN_SLICES (1, 2, 4 or 8) when set.  Used by
+// the forward's and the backward's state scans alike.  Measured (B200, T = 8192,
+// fwd + bwd): at 16 pairs 1 / 2 / 4 / 8 slices take 0.94 / 0.84 / 0.82 / 0.86 ms,
+// at 32 pairs 1.33 / 1.23 / 1.22 / 1.53 ms: past 4 slices every slice CTA still
+// loads the whole chunk operands, and the chain per chunk no longer shortens.
 int tc_scan_slices(long long heads, int n_sm) {
   const char* e = std::getenv("KDA_SCAN_SLICES");
   if (e) {
@@ -921,7 +924,7 @@ int tc_scan_slices(long long heads, int n_sm) {
     if (v == 1 || v == 2 || v == 4 || v == 8) return v;
   }
   int s = 1;
-  while (s < 8 && heads * s * 2 <= n_sm) s *= 2;
+  while (s < 4 && heads * s * 2 <= n_sm) s *= 2;
   return s;
 }
 

@@ -272,21 +272,24 @@ def test_tc_mixed_decay_regimes_in_one_call():
 
 
 @pytest.mark.parametrize("schedule", ["split", "fused"])
-@pytest.mark.parametrize("B,T,H,ck", [
-    (1, 200, 2, torch.bfloat16),    # 2 (sequence, head) pairs: 8 state slices of 16 columns
-    (1, 130, 32, torch.bfloat16),   # 32 pairs: 4 slices of 32 columns
-    (2, 128, 32, torch.float32),    # 64 pairs: 2 slices of 64 columns, fp32 checkpoint
-    (2, 64, 64, torch.bfloat16),    # 128 pairs: one CTA per pair, whole state
+@pytest.mark.parametrize("B,T,H,ck,slices", [
+    (1, 200, 2, torch.bfloat16, "8"),   # 2 (sequence, head) pairs, forced 8 state slices of 16 columns
+    (1, 130, 32, torch.bfloat16, None),  # 32 pairs: 4 slices of 32 columns
+    (2, 128, 32, torch.float32, None),   # 64 pairs: 2 slices of 64 columns, fp32 checkpoint
+    (2, 64, 64, torch.bfloat16, "1"),   # 128 pairs, forced: one CTA per pair, whole state
 ])
-def test_tc_training_forward_schedules_match_oracle(monkeypatch, schedule, B, T, H, ck):
+def test_tc_training_forward_schedules_match_oracle(monkeypatch, schedule, B, T, H, ck, slices):
     """The training forward (checkpoint written) on both schedules: the split
     one (chunk-parallel prep + state scan sliced by columns, the slice count
-    following the number of (sequence, head) pairs) and the fused one; outputs,
-    states and the backward from each checkpoint against the oracle."""
+    following the number of (sequence, head) pairs or KDA_SCAN_SLICES) and the
+    fused one; outputs, states and the backward (whose state-cotangent scan is
+    sliced the same way) from each checkpoint against the oracle."""
     from axiom_b200 import kda_bwd, kda_fwd
     from axiom_b200.kda import ckpt_states
 
     monkeypatch.setenv("KDA_FWD_SCHEDULE", schedule)
+    if slices:
+        monkeypatch.setenv("KDA_SCAN_SLICES", slices)
     xr, d = _bf16_inputs(B, T, H, seed=B * 1000 + T + H, s0_std=0.05)
     rng = np.random.default_rng(T + H)
     do = K.bf16_round(rng.standard_normal((B, T, H, 128)))
