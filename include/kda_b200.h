@@ -83,11 +83,12 @@ const char* kda_strerror(int status);
  * entering chunk c (the reference's pass-A state chain,
  * net/kernels/kda_cc_fused_persist.py:1282-1370).  On the tensor-core path
  * (bf16 inputs, dk = dv = 128, chunk = 64) it continues with a per-chunk
- * block of what the backward would otherwise recompute (137 KB per
- * chunk-head): T = (I + diag(beta) Akk)^-1, Aqk, Akk (bf16 64 x 64 each),
+ * block (201 KB per chunk-head) of what the backward would otherwise
+ * recompute: T = (I + diag(beta) Akk)^-1, Aqk, Akk (bf16 64 x 64 each),
  * W, Q Gam, K Gam, K Gam^-1, lam K, v~ = U - W S, U = T diag(beta) V (bf16
- * 64 x 128 each), Gam_C (fp32 x 128) and
- * a flag for chunks that took the exact strong-decay path.  The checkpoint is
+ * 64 x 128 each), Gam_C (fp32 x 128) and flags, then the state-chain
+ * operands the split training forward hands from its chunk-parallel part to
+ * its state scan (-(lam K)^T W, Q Gam - Aqk W, Aqk U).  The checkpoint is
  * an opaque blob passed from kda_fwd to kda_bwd: on the tensor-core path with
  * a bf16 checkpoint each state is stored as the shared-memory operand image
  * the kernels copy in one bulk transfer (8 x 8 core matrices of 128 bytes,
