@@ -411,46 +411,75 @@ def run_strong(torch, dist, KD, world, rank, dev, peaks, args, steps=10, warmup=
     torch.cuda.empty_cache()
     q, k, v, g, beta, do = loc
 
-    def step(gather):
+    kern = []
+
+    def step(mode, record=False):
+        """mode: "all" (outputs and gradients gathered), "outputs" (O and S_T
+        only, the north star's "NCCL only to gather outputs") or "none"."""
+        if record:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
         o, s_t, ck = KD.kda_fwd(q, k, v, g, beta, None, chunk=C, need_ckpt=True)
-        if gather:
+        if record:
+            ev[1].record()
+        if mode != "none":
             fo, _ = D._gather(o, sh.axis, async_op=True)
             fs, _ = D._gather(s_t, sh.s_axis, async_op=True)
         grads = KD.kda_bwd(q, k, v, g, beta, ck, do, None, chunk=C, need_ds0=False)
-        if gather:
-            out = [fo(), fs()] + [D._gather(x, sh.axis) for x in grads[:5]]
-            return out
-        return grads
+        if record:
+            ev[2].record()
+            kern.append(ev)
+        if mode == "none":
+            return grads
+        out = [fo(), fs()]
+        if mode == "all":
+            out += [D._gather(x, sh.axis) for x in grads[:5]]
+        return out
 
-    def timed(gather):
+    def timed(mode):
         for _ in range(warmup):
-            step(gather)
+            step(mode)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            step(gather)
+            step(mode, record=mode == "none")
         e1.record()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         return e0.elapsed_time(e1) / steps
 
-    ms_full, ms_compute = _max_over_ranks(torch, dist, world, dev, [timed(True), timed(False)])
+    t_all, t_out, t_none = timed("all"), timed("outputs"), timed("none")
+    fwd_ms = sum(a.elapsed_time(b) for a, b, _ in kern) / len(kern)
+    bwd_ms = sum(b.elapsed_time(c) for _, b, c in kern) / len(kern)
+    ms_full, ms_out, ms_compute, fwd_ms, bwd_ms = _max_over_ranks(
+        torch, dist, world, dev, [t_all, t_out, t_none, fwd_ms, bwd_ms])
     units = q.shape[0] * q.shape[2]
     el = 2  # bf16
-    gathered = (B * T * H * 128 * el * 5 + B * T * H * el + B * H * 128 * 128 * 4) if world > 1 else 0
+    out_bytes = B * T * H * 128 * el + B * H * 128 * 128 * 4
+    grad_bytes = B * T * H * 128 * el * 4 + B * T * H * el
+    recv = (world - 1) / world  # share of a gathered tensor each rank receives
+    gather_ms = ms_full - ms_compute
     del loc, q, k, v, g, beta, do
     torch.cuda.empty_cache()
+    limiter = ("the NCCL all-gathers of the gradients (every rank receives (N-1)/N of 1.35 GB per step)"
+               if world > 1 and gather_ms > ms_compute else
+               "compute: the forward's and the backward's per-head state scans (one chunk after another)")
     return {"workload": "cfg3 global problem (B=4, T=8192, H=32) fixed, (batch, head) units split over the ranks",
             "scaling": "strong", "n_gpus": world, "shard_axis": "batch" if sh.axis == 0 else "head",
             "units_per_rank": units, "ms_per_step": ms_full, "tokens_per_s": B * T / (ms_full / 1e3),
+            "ms_per_step_outputs_gathered": ms_out, "tokens_per_s_outputs_gathered": B * T / (ms_out / 1e3),
             "ms_per_step_compute_only": ms_compute, "tokens_per_s_compute_only": B * T / (ms_compute / 1e3),
-            "gather_ms_per_step": ms_full - ms_compute, "gathered_bytes_per_step": gathered,
+            "kernels_ms_compute_only": {"kda_fwd": fwd_ms, "kda_bwd": bwd_ms},
+            "gather_ms_per_step": gather_ms,
+            "gathered_bytes_per_step": (out_bytes + grad_bytes) if world > 1 else 0,
+            "received_GBps_per_rank": (recv * (out_bytes + grad_bytes) / (gather_ms / 1e3) / 1e9)
+            if world > 1 and gather_ms > 0 else None,
             "gathers": "O and S_T (overlapping the backward), then dq, dk, dv, dg, dbeta: NCCL all-gather",
-            "steps": steps, "timing": "CUDA events, max over ranks"}
+            "limiter": limiter, "steps": steps, "timing": "CUDA events, max over ranks"}
 
 
 def run_mixer_sharded(torch, dist, world, rank, dev, steps=5, warmup=3):
