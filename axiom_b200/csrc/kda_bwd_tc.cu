@@ -1285,8 +1285,7 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
           mma_bf16(T_DS, desc_mnmajor(qt + ks * 4096, DK), desc_mnmajor(dob + ks * 4096, DV), id, 1u);
         mma_commit(mbar);
       }
-      failed |= !mma_wait();
-      if (__syncthreads_or(failed)) break;
+      failed |= !mma_wait();  // the next chunk's barrier shares failures
       continue;
     }
     // dU_s = (lam K) dS'_s + Aqk^T dO_s  (M = 64); filler: dS_s += (Gam Q)^T dO_s
@@ -1337,9 +1336,9 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
         mma_bf16(T_DS, desc_mnmajor(w + ks * 4096, DK), desc_mnmajor(du + ks * (32 * DVS), DVS), id, 1u);
       mma_commit(mbar);
     }
-    failed |= !mma_wait();
-    if (__syncthreads_or(failed)) break;
+    failed |= !mma_wait();  // the next chunk's barrier shares failures
   }
+  failed = __syncthreads_or(failed) != 0;
   if (!failed && ds0) {
 #pragma unroll
     for (int j = 0; j < CW; j += CB) {

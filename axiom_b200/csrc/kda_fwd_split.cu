@@ -687,11 +687,13 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
         mma_bf16(T_S, desc_kmajor(np + ks * 256, DK), desc_mnmajor(sb + ks * (32 * DVS), DVS), id_np, 1u);
       mma_commit(mbar);
     }
+    // every thread sees the commit itself; the next chunk's barrier (after its
+    // load wait) is the first one that needs all threads, and it shares failures
     failed |= !mbar_wait(mbar, phase);
     phase ^= 1u;
     tc_fence_after();
-    if (__syncthreads_or(failed)) break;
   }
+  failed = __syncthreads_or(failed) != 0;
   if (!failed && s_out) {
     float* so = s_out + ((static_cast<size_t>(seq) * H + h) * DK + d) * DV + col0 + cw0;
 #pragma unroll
