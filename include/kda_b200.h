@@ -106,7 +106,13 @@ size_t kda_ckpt_bytes(int B, int T, int H, int dk, int dv, int chunk, int in_dty
  *   s_ckpt     : the checkpoint for the backward (kda_ckpt_bytes bytes),
  *                or NULL when not training.
  * Supported: 1 <= dk, dv <= 128 (multiples of 8), chunk in {16, 32, 64}.
- * bf16 inputs with dk = dv = 128, chunk = 64 take the tensor-core path. */
+ * bf16 inputs with dk = dv = 128, chunk = 64 take the tensor-core path: one
+ * kernel with one CTA per (batch, head) or, when s_ckpt is given and the
+ * (batch, head) pairs fill at most half the SMs, three launches (chunk-parallel
+ * prep, state scan sliced by state columns, chunk-parallel outputs) that meet
+ * in the checkpoint.  The environment variables KDA_FWD_SCHEDULE
+ * (split | fused) and KDA_SCAN_SLICES (1, 2, 4, 8) override the choice; the
+ * results agree within the bf16 tolerance either way. */
 int kda_fwd(const void* q, const void* k, const void* v, const void* g,
             const void* beta, const float* s0, void* o, float* s_out,
             void* s_ckpt, int B, int T, int H, int dk, int dv, int chunk,
