@@ -1245,6 +1245,7 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
     const unsigned char* setp = sm + p * M::SET;
     const uint32_t set = smem_u32(setp);
     const float* gamC = reinterpret_cast<const float*>(setp + M::GC);
+    if (c > c_beg) issue_chunk(c - 1);  // the other set was last read by chunk c + 1
     {  // dS' pass: bf16 operand (stored to the workspace below), then dS *= Gam_C
       const float gcd = gamC[d];
 #pragma unroll
@@ -1263,11 +1264,7 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // the copy thread's work runs beside the MMA issue (another warp): the next
-    // chunk's operands into the other set (last read by chunk c + 1), then this
-    // slice of chunk c's dS' image
-    if (c > c_beg) issue_chunk(c - 1);
-    if (tid == kIoThread) {
+    if (tid == kIoThread) {  // this slice of chunk c's dS' image
       unsigned char* img = reinterpret_cast<unsigned char*>(dsw) + (unit * n_chunks + c) * WS_UNIT;
 #pragma unroll 1
       for (int rg = 0; rg < 16; ++rg)

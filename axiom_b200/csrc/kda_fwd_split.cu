@@ -642,6 +642,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
     ld_pending &= ~(1u << p);
     if (tid == kIoThread) bulk_wait_read();  // the previous S_s image has been stored
     if (__syncthreads_or(failed)) break;
+    if (c + 1 < c_end) issue(c + 1);  // the other set's last reader, chunk c - 1, has completed
     // ---- S pass: S_s -> bf16 operand (+ checkpoint), S_s *= Gam_C
     Tc* ck = s_ckpt + (unit0 + c) * (DK * DV);
     {
@@ -663,12 +664,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // the copy thread's work runs beside the MMA issue (another warp): the next
-    // chunk's operands into the other set (its last reader, chunk c - 1, has
-    // completed), then the slice of the bf16 state image (one bulk group per
-    // chunk, maybe empty)
-    if (c + 1 < c_end) issue(c + 1);
-    if (tid == kIoThread) {
+    if (tid == kIoThread) {  // the slice of the bf16 state image (one bulk group per chunk, maybe empty)
       if (sizeof(Tc) == 2) {
         unsigned char* img = reinterpret_cast<unsigned char*>(ck);
 #pragma unroll 1
