@@ -1098,12 +1098,15 @@ bwd_par_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf1
 //   dS_s  = Gam_C dS'_s + NP^T dS'_s + Q~^T dO_s.
 template <int DVS>
 struct SeqSliceMap {
-  // per operand set: W, Q Gam, lam K, dO, Aqk, Gam_C; with the prep's chain
-  // operands (FLAG_CHAIN) NP takes W|Q Gam and Q~ takes lam K's place
+  // per operand set: W, Q Gam, lam K, dO, Aqk, Gam_C (two sets in flight); with
+  // the prep's chain operands (FLAG_CHAIN) a set is NP, Q~, dO, Gam_C and three
+  // sets fit, so loads are issued two chunks ahead
   static constexpr int W = 0, QG = 16384, KL = 32768, DO = 49152, AQ = 65536, GC = 73728;
-  static constexpr int NP = 0, QT = 32768;
   static constexpr int SET = GC + 512;
-  static constexpr int SB = 2 * SET;          // dS'_s bf16 CM[128][DVS]
+  static constexpr int NP = 0, QT = 32768, CGC = 65536;
+  static constexpr int CSET = CGC + 512;
+  static constexpr int RING = 3 * CSET > 2 * SET ? 3 * CSET : 2 * SET;
+  static constexpr int SB = RING;             // dS'_s bf16 CM[128][DVS]
   static constexpr int DU = SB + 256 * DVS;   // -dU_s bf16 CM[64][DVS]
   static constexpr int BAR = DU + 128 * DVS;
   static constexpr int SMEM = BAR + 64;
@@ -1150,7 +1153,7 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
   extern __shared__ __align__(1024) unsigned char sm[];
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + M::BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + M::BAR + 8);
-  uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + M::BAR + 16);  // [2]: one per operand set
+  uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + M::BAR + 16);  // [3]: one per operand set
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;
   const int n_chunks = (T + C - 1) / C;
@@ -1174,11 +1177,14 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
   const bool chain = c_beg < c_end &&
                      (*reinterpret_cast<const uint32_t*>(factors + (unit * n_chunks + c_end - 1) * FAC_UNIT +
                                                          FAC_FLAG) & FLAG_CHAIN) != 0u;
+  // the operand ring: chunk cc (walked in reverse) uses set (c_end - 1 - cc) % nset
+  const int nset = chain && use_tma ? 3 : 2;
+  const int set_bytes = chain ? M::CSET : M::SET, gc_off = chain ? M::CGC : M::GC;
+  auto set_of = [&](int cc) { return (c_end - 1 - cc) % nset; };
 
   if (tid == 0) {
     mbar_init(mbar, 1);
-    mbar_init(mbar_ld, 1);
-    mbar_init(mbar_ld + 1, 1);
+    for (int p = 0; p < 3; ++p) mbar_init(mbar_ld + p, 1);
     mbar_fence_init();
   }
   if (warp == 0) { tmem_alloc(tslot, M::TCOLS); tmem_relinquish(); }
@@ -1186,8 +1192,8 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
   __syncthreads();
   tc_fence_after();
   auto issue_chunk = [&](int cc) {
-    const int ps = cc & 1, t0 = cc * C, rv = min(C, T - t0);
-    unsigned char* set = sm + ps * M::SET;
+    const int ps = set_of(cc), t0 = cc * C, rv = min(C, T - t0);
+    unsigned char* set = sm + ps * set_bytes;
     if (!use_tma) {
       stage_tile(set + M::DO, doh + (tok0 + t0) * rstride, rv, rstride);
       cp_async_commit();
@@ -1205,12 +1211,12 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
         bulk_load(set + M::KL, fu + FAC_KL, 16384, mbar_ld + ps);
         bulk_load(set + M::AQ, fu + FAC_AQ, 8192, mbar_ld + ps);
       }
-      bulk_load(set + M::GC, fu + FAC_GC, 512, mbar_ld + ps);
+      bulk_load(set + gc_off, fu + FAC_GC, 512, mbar_ld + ps);
       if (use_tma) tma_tile(set + M::DO, &tm_do, h, cc, b, mbar_ld + ps);
     }
     ld_pending |= 1u << ps;
   };
-  if (c_beg < c_end) issue_chunk(c_end - 1);
+  for (int cc = c_end - 1; cc >= max(c_beg, c_end - (nset - 1)); --cc) issue_chunk(cc);
   const uint32_t tbase = *tslot;
   const uint32_t T_DS = tbase, T_U = tbase + DVS;
   const uint32_t tl = static_cast<uint32_t>(32 * qw) << 16;
@@ -1235,17 +1241,18 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
   }
 
   for (int c = c_end - 1; c >= c_beg; --c) {
-    const int p = c & 1;
+    const int p = set_of(c);
     cp_async_wait<0>();
     failed |= !mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
     ld_par ^= 1u << p;
     ld_pending &= ~(1u << p);
     if (tid == kIoThread) bulk_wait_read();  // SB may be rewritten: the previous dS' slice is stored
     if (__syncthreads_or(failed)) break;
-    const unsigned char* setp = sm + p * M::SET;
+    const unsigned char* setp = sm + p * set_bytes;
     const uint32_t set = smem_u32(setp);
-    const float* gamC = reinterpret_cast<const float*>(setp + M::GC);
-    if (c > c_beg) issue_chunk(c - 1);  // the other set was last read by chunk c + 1
+    const float* gamC = reinterpret_cast<const float*>(setp + gc_off);
+    // chunk c - nset + 1 goes into the set of chunk c + 1, which has completed
+    if (c - (nset - 1) >= c_beg) issue_chunk(c - (nset - 1));
     {  // dS' pass: bf16 operand (stored to the workspace below), then dS *= Gam_C
       const float gcd = gamC[d];
 #pragma unroll
@@ -1352,7 +1359,7 @@ bwd_seq_sliced_kernel(const bf16* __restrict__ dout, const unsigned char* __rest
   }
   if (failed && tid == 0 && err) atomicExch(err, 1);
   cp_async_wait<0>();
-  for (int ps = 0; ps < 2; ++ps)
+  for (int ps = 0; ps < 3; ++ps)
     if ((ld_pending >> ps) & 1u) mbar_wait(mbar_ld + ps, (ld_par >> ps) & 1u);
   if (tid == kIoThread) bulk_wait_all();
   tc_fence_before();

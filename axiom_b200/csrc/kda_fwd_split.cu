@@ -500,13 +500,17 @@ fwd_prep_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf
 // ===========================================================================
 // S_{c+1} = Gam_C S_c + (lam K)^T U + NP S_c with NP = -(lam K)^T W (the prep's
 // FAC_NP): one MMA round trip per chunk.  Chunk c's operands (NP, lam K, the
-// slice of U, Gam_C) land in set (c - c_beg) & 1 while chunk c - 1 runs.
+// slice of U, Gam_C) land in set (c - c_beg) % NSET, issued NSET - 1 chunks
+// ahead.
 template <int DVS>
 struct ScanMap {
   static constexpr int NP = 0, KL = 32768, US = 49152;
   static constexpr int GC = US + 128 * DVS;
   static constexpr int SET = GC + 512;
-  static constexpr int SB = 2 * SET;          // S_s bf16 CM[128][DVS] (the MMA operand and checkpoint image)
+  // operand sets in flight: loads are issued NSET - 1 chunks ahead (three sets
+  // fit beside the state image up to 64 columns, two at 128)
+  static constexpr int NSET = DVS == 128 ? 2 : 3;
+  static constexpr int SB = NSET * SET;       // S_s bf16 CM[128][DVS] (the MMA operand and checkpoint image)
   static constexpr int BAR = SB + 256 * DVS;
   static constexpr int SMEM = BAR + 64;
   static constexpr uint32_t TX = 32768 + 16384 + 128 * DVS + 512;
@@ -567,7 +571,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
   extern __shared__ __align__(1024) unsigned char sm[];
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + M::BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + M::BAR + 8);
-  uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + M::BAR + 16);  // [2]: one per operand set
+  uint64_t* mbar_ld = reinterpret_cast<uint64_t*>(sm + M::BAR + 16);  // [NSET]: one per operand set
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qw = warp & 3, hh = warp >> 2;
   const int n_chunks = (T + C - 1) / C;
@@ -585,8 +589,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
 
   if (tid == 0) {
     mbar_init(mbar, 1);
-    mbar_init(mbar_ld, 1);
-    mbar_init(mbar_ld + 1, 1);
+    for (int p = 0; p < M::NSET; ++p) mbar_init(mbar_ld + p, 1);
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -595,7 +598,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
   }
   uint32_t ld_par = 0u, ld_pending = 0u;  // bit p: phase parity / loads in flight of set p
   auto issue = [&](int cc) {
-    const int p = (cc - c_beg) & 1;
+    const int p = (cc - c_beg) % M::NSET;
     if (tid == kIoThread) {
       unsigned char* set = sm + p * M::SET;
       const unsigned char* fu = factors + (unit0 + cc) * FAC_UNIT;
@@ -611,7 +614,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
     ld_pending |= 1u << p;
   };
   __syncthreads();  // barriers initialised
-  if (c_beg < c_end) issue(c_beg);
+  for (int cc = c_beg; cc < min(c_end, c_beg + M::NSET - 1); ++cc) issue(cc);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -635,14 +638,15 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
   }
 
   for (int c = c_beg; c < c_end; ++c) {
-    const int p = (c - c_beg) & 1;
+    const int p = (c - c_beg) % M::NSET;
     unsigned char* set = sm + p * M::SET;
     failed |= !mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
     ld_par ^= 1u << p;
     ld_pending &= ~(1u << p);
     if (tid == kIoThread) bulk_wait_read();  // the previous S_s image has been stored
     if (__syncthreads_or(failed)) break;
-    if (c + 1 < c_end) issue(c + 1);  // the other set's last reader, chunk c - 1, has completed
+    // the set of chunk c + NSET - 1 was last read by chunk c - 1, which has completed
+    if (c + M::NSET - 1 < c_end) issue(c + M::NSET - 1);
     // ---- S pass: S_s -> bf16 operand (+ checkpoint), S_s *= Gam_C
     Tc* ck = s_ckpt + (unit0 + c) * (DK * DV);
     {
@@ -705,7 +709,7 @@ fwd_scan_kernel(const unsigned char* __restrict__ factors, const float* __restri
     }
   }
   if (failed && tid == 0 && err) atomicExch(err, 1);
-  for (int p = 0; p < 2; ++p)
+  for (int p = 0; p < M::NSET; ++p)
     if ((ld_pending >> p) & 1u) mbar_wait(mbar_ld + p, (ld_par >> p) & 1u);
   if (tid == kIoThread) bulk_wait_all();
   tc_fence_before();
