@@ -465,9 +465,15 @@ def run_strong(torch, dist, KD, world, rank, dev, peaks, args, steps=10, warmup=
     gather_ms = ms_full - ms_compute
     del loc, q, k, v, g, beta, do
     torch.cuda.empty_cache()
-    limiter = ("the NCCL all-gathers of the gradients (every rank receives (N-1)/N of 1.35 GB per step)"
-               if world > 1 and gather_ms > ms_compute else
-               "compute: the forward's and the backward's per-head state scans (one chunk after another)")
+    compute_txt = ("compute (%.3f ms): the forward's and the backward's per-head state scans walk one chunk "
+                   "after another, the chunk-parallel kernels scale with the units" % ms_compute)
+    if world > 1:
+        limiter = (("the NCCL all-gathers (%.3f ms; every rank receives (N-1)/N of 1.35 GB per step), then "
+                    % gather_ms) + compute_txt) if gather_ms > ms_compute else \
+            (compute_txt + ("; the all-gathers add %.3f ms (every rank receives (N-1)/N of 1.35 GB per step)"
+                            % gather_ms))
+    else:
+        limiter = compute_txt
     return {"workload": "cfg3 global problem (B=4, T=8192, H=32) fixed, (batch, head) units split over the ranks",
             "scaling": "strong", "n_gpus": world, "shard_axis": "batch" if sh.axis == 0 else "head",
             "units_per_rank": units, "ms_per_step": ms_full, "tokens_per_s": B * T / (ms_full / 1e3),

@@ -186,10 +186,11 @@ def _mesh_worker(rank, world, port, n_head_groups, out_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("n_head_groups", [1, 2])  # 2 x 1: by sequence; 1 x 2: by head
-def test_layer_mesh_collectives_equal_unsharded(tmp_path, n_head_groups):
+@pytest.mark.parametrize("world,n_head_groups", [(2, 1), (2, 2), (4, 2)])  # 2 x 1, 1 x 2, 2 x 2 meshes
+def test_layer_mesh_collectives_equal_unsharded(tmp_path, world, n_head_groups):
     out = str(tmp_path / "mesh.npz")
-    _spawn(_mesh_worker, n_head_groups, out)
+    mp.start_processes(_mesh_worker, args=(world, _free_port(), n_head_groups, out), nprocs=world, join=True,
+                       start_method="spawn")
     g = torch.Generator().manual_seed(0)
     d, H, dh, T = 6, 4, 2, 5
     shapes = (("W_q", (d, H * dh)), ("W_k", (d, H * dh)), ("W_v", (d, H * dh)), ("W_g", (d, H * dh)),
@@ -200,19 +201,18 @@ def test_layer_mesh_collectives_equal_unsharded(tmp_path, n_head_groups):
     x = torch.randn(2 * T, d, generator=g, dtype=torch.float64).requires_grad_(True)
     y = ((x @ full["W_q"]) * ((x @ full["W_a_down"]) @ full["W_a_up"])) @ full["W_o"]
     y.backward(torch.ones_like(y))
-    r = [np.load(out.replace(".npz", f"_{i}.npz")) for i in range(2)]
-    if n_head_groups == 1:  # rank i holds sequence rows [i T, (i + 1) T) and every head
-        assert np.allclose(np.concatenate([r[0]["y"], r[1]["y"]]), y.detach().numpy())
-        assert np.allclose(np.concatenate([r[0]["dx"], r[1]["dx"]]), x.grad.numpy())
-        for n in ("W_q", "W_a_down", "W_a_up", "W_o"):
-            for i in range(2):
-                assert np.allclose(r[i][n], full[n].grad.numpy()), n
-    else:  # both ranks hold every row; rank i holds heads [2 i, 2 i + 2)
-        for i in range(2):
-            assert np.allclose(r[i]["y"], y.detach().numpy())
-            assert np.allclose(r[i]["dx"], x.grad.numpy())
-            assert np.allclose(r[i]["W_a_down"], full["W_a_down"].grad.numpy())
-            cols = slice(i * 4, (i + 1) * 4)
-            assert np.allclose(r[i]["W_q"], full["W_q"].grad.numpy()[:, cols])
-            assert np.allclose(r[i]["W_a_up"], full["W_a_up"].grad.numpy()[:, cols])
-            assert np.allclose(r[i]["W_o"], full["W_o"].grad.numpy()[cols, :])
+    n_seq = world // n_head_groups
+    width = H * dh // n_head_groups  # columns of one head shard
+    for r in range(world):
+        got = np.load(out.replace(".npz", f"_{r}.npz"))
+        s_idx, j = divmod(r, n_head_groups)
+        rows = slice(0, 2 * T) if n_seq == 1 else slice(s_idx * T, (s_idx + 1) * T)
+        cols = slice(j * width, (j + 1) * width)
+        assert np.allclose(got["y"], y.detach().numpy()[rows]), r
+        assert np.allclose(got["dx"], x.grad.numpy()[rows]), r
+        # every gradient is the whole batch's: summed over the sequence groups, and
+        # W_a_down's also over the head group
+        assert np.allclose(got["W_a_down"], full["W_a_down"].grad.numpy()), r
+        assert np.allclose(got["W_q"], full["W_q"].grad.numpy()[:, cols]), r
+        assert np.allclose(got["W_a_up"], full["W_a_up"].grad.numpy()[:, cols]), r
+        assert np.allclose(got["W_o"], full["W_o"].grad.numpy()[cols, :]), r
