@@ -86,6 +86,44 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
       : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
+
+// Swish x sigmoid(x) of two lanes.  FAST (bf16 consumers): with h = x / 2,
+// x sigmoid(x) = h + h tanh(h), one tanh.approx per element (absolute error of
+// the sigmoid factor below 2^-12, as in sigm<true>).
+template <bool FAST>
+__device__ __forceinline__ float2 swish2(float2 x) {
+  if constexpr (FAST) {
+    const float2 h = fmul2(x, f2(0.5f));
+    return ffma2(h, make_float2(tanh_approx(h.x), tanh_approx(h.y)), h);
+  } else {
+    return make_float2(x.x * sigmoidf_(x.x), x.y * sigmoidf_(x.y));
+  }
+}
+// Swish and its derivative d/dx [x sigmoid(x)] = sigmoid(x) (1 + x (1 - sigmoid(x))).
+template <bool FAST>
+__device__ __forceinline__ void swish_grad2(float2 x, float2& s, float2& ds) {
+  float2 sig;
+  if constexpr (FAST) {
+    const float2 h = fmul2(x, f2(0.5f));
+    const float2 th = make_float2(tanh_approx(h.x), tanh_approx(h.y));
+    s = ffma2(h, th, h);
+    sig = ffma2(th, f2(0.5f), f2(0.5f));
+  } else {
+    sig = make_float2(sigmoidf_(x.x), sigmoidf_(x.y));
+    s = fmul2(x, sig);
+  }
+  const float2 om = ffma2(sig, f2(-1.f), f2(1.f));
+  ds = fmul2(sig, ffma2(x, om, f2(1.f)));
+}
 
 // CPL (2 or 4) consecutive elements <-> floats, one vector access
 template <int CPL>
@@ -177,6 +215,26 @@ __device__ __forceinline__ void ring_fill(unsigned char* dst, int lane, const vo
   }
 }
 
+// The same for NROWS rows all in range, `stride` bytes apart (negative: rows
+// descending): `first` is this lane's chunk of row 0 (the row's address plus
+// lane_src_off), `dst` its chunk in the stage (the stage's shared address plus
+// lane_dst_off).  Lane l copies chunk l % CPR of rows l / CPR + RSTEP i.
+template <int RB, int NROWS>
+__device__ __forceinline__ void ring_fill_rows(uint32_t dst, const unsigned char* first, long long stride) {
+  constexpr int CPR = RB / 16, RSTEP = 32 / CPR;
+  static_assert(32 % CPR == 0 && NROWS % RSTEP == 0, "whole warp copies");
+#pragma unroll
+  for (int i = 0; i < NROWS / RSTEP; ++i) tc::cp_async16_s(dst + i * RSTEP * RB, first + i * RSTEP * stride);
+}
+template <int RB>
+__device__ __forceinline__ long long lane_src_off(int lane, long long stride) {
+  return (lane / (RB / 16)) * stride + (lane % (RB / 16)) * 16;
+}
+template <int RB>
+__device__ __forceinline__ uint32_t lane_dst_off(int lane) {
+  return (lane / (RB / 16)) * RB + (lane % (RB / 16)) * 16;
+}
+
 // CPL elements of this lane from a staged row (lane l holds elements [l CPL, l CPL + CPL)).
 template <int CPL, typename T>
 __device__ __forceinline__ void ld_row(const unsigned char* row, int lane, float (&x)[CPL]) {
@@ -237,16 +295,10 @@ __device__ __forceinline__ int seq_of(const int* cu, int n, int t) {
 }
 
 // Row of packed token t in the outputs (and, backward, the output cotangents):
-// t itself, or with out_rows the chunk-aligned row of its sequence.
-__device__ __forceinline__ int out_row(const ProArgs& a, int t) {
-  if (!a.out_rows) return t;
-  const int s = seq_of(a.cu, a.n_seqs, t);
-  return t + __ldg(a.out_rows + s) - __ldg(a.cu + s);
-}
-
-// out_row for tokens visited in increasing (UP) or decreasing order: the
-// sequence and its row shift change only at sequence boundaries, so a call is
-// a compare, with a reload when a boundary is crossed (no search per token).
+// t itself, or with out_rows the chunk-aligned row of its sequence, for tokens
+// visited in increasing (UP) or decreasing order.  The sequence and its row
+// shift change only at sequence boundaries, so a call is a compare, with a
+// reload when a boundary is crossed (no search per token).
 template <bool UP>
 struct RowWalk {
   const int* cu;
@@ -327,8 +379,12 @@ __host__ __device__ constexpr int bwd_ring_bytes() {
 
 // q, k, v of one strip.  Batches of kPre tokens stream through the warp's
 // ring (kStages - 1 batches in flight); a batch's L2 norms are one column-sum
-// reduction (warp_colsum) instead of kPre serial ones.
-template <int CPL, bool VARLEN, typename Tin, typename Tout>
+// reduction (warp_colsum) instead of kPre serial ones.  A batch whose rows are
+// all in the strip and in one packed sequence takes the plain path: rows
+// copied by running offsets, outputs stored through a running pointer, no
+// per-token test; the others (a strip's ragged end, a sequence start inside
+// the batch) test every token.
+template <int CPL, bool VARLEN, bool NORM, typename Tin, typename Tout>
 __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, int h, int lane,
                              unsigned char* ring) {
   constexpr bool FAST = std::is_same<Tout, bf16>::value;
@@ -338,7 +394,7 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
   const size_t row0 = static_cast<size_t>(b) * a.T;
   const Tin* xb = static_cast<const Tin*>(pick(a.x, role));
   const Tin* xh = xb + row0 * HD + h * D;  // token t of this head at xh + t * HD
-  Tout* y = static_cast<Tout*>(pick(a.y, role)) + row0 * HD + ch;
+  Tout* const y = static_cast<Tout*>(pick(a.y, role)) + row0 * HD + ch;
   float wt[4][CPL];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -352,11 +408,19 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     shift = a.out_rows ? __ldg(a.out_rows + si) - lb : 0;
   }
   const int nbat = (t1 - t0 + kPre - 1) / kPre;
+  const long long stride = static_cast<long long>(HD) * sizeof(Tin);
+  const unsigned char* src = reinterpret_cast<const unsigned char*>(xh + static_cast<size_t>(t0) * HD) +
+                             lane_src_off<RB>(lane, stride);  // this lane's chunk of the strip's first row
+  const uint32_t dst = tc::smem_u32(ring) + lane_dst_off<RB>(lane);
   auto fill = [&](int bi) {
     const int tb = t0 + bi * kPre;
-    ring_fill<RB, kPre>(ring + (bi % kStages) * STG, lane, xh, [&](int r) -> const void* {
-      return tb + r < t1 ? xh + static_cast<size_t>(tb + r) * HD : nullptr;
-    });
+    if (tb + kPre <= t1) {
+      ring_fill_rows<RB, kPre>(dst + (bi % kStages) * STG, src + static_cast<long long>(bi) * kPre * stride, stride);
+    } else {
+      ring_fill<RB, kPre>(ring + (bi % kStages) * STG, lane, xh, [&](int r) -> const void* {
+        return tb + r < t1 ? xh + static_cast<size_t>(tb + r) * HD : nullptr;
+      });
+    }
   };
 #pragma unroll
   for (int bi = 0; bi < kStages - 1; ++bi) {
@@ -374,30 +438,29 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
       load_x<CPL>(a, xb, row0, HD, ch, b, role, t, hw[j]);
     }
   }
-  for (int bi = 0; bi < nbat; ++bi) {
-    tc::cp_async_wait<kStages - 2>();
-    __syncwarp();
-    if (bi + kStages - 1 < nbat) fill(bi + kStages - 1);
-    tc::cp_async_commit();
-    const unsigned char* st = ring + (bi % kStages) * STG;
-    const int tb = t0 + bi * kPre;
+  Tout* yp = y + static_cast<size_t>(t0 + shift) * HD;  // output row of the batch's first token
+  // One batch; CHECK: tokens past t1 are skipped and a sequence may start inside.
+  auto batch = [&](const unsigned char* st, int tb, auto check) {
+    constexpr bool CHECK = decltype(check)::value;
     float s[kPre][CPL], ss[kPre];
-    int sh[kPre];
+    int sh[CHECK ? kPre : 1];
 #pragma unroll
     for (int u = 0; u < kPre; ++u) {
       float xv[CPL];
       ld_row<CPL, Tin>(st + u * RB, lane, xv);
-      if (VARLEN && tb + u == nb) {  // a packed sequence starts: the window restarts from zeros
+      if constexpr (CHECK && VARLEN) {
+        if (tb + u == nb) {  // a packed sequence starts: the window restarts from zeros
 #pragma unroll
-        for (int j = 0; j < 3; ++j)
+          for (int j = 0; j < 3; ++j)
 #pragma unroll
-          for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
-        ++si;
-        nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
-        shift = a.out_rows ? __ldg(a.out_rows + si) - __ldg(a.cu + si) : 0;
+            for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
+          ++si;
+          nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+          shift = a.out_rows ? __ldg(a.out_rows + si) - __ldg(a.cu + si) : 0;
+        }
       }
-      sh[u] = shift;
-      ss[u] = 0.f;
+      if constexpr (CHECK) sh[u] = shift;
+      float2 ss2 = f2(0.f);
 #pragma unroll
       for (int c = 0; c < CPL; c += 2) {
         float2 cv = fmul2(make_float2(wt[0][c], wt[0][c + 1]), make_float2(xv[c], xv[c + 1]));
@@ -410,23 +473,49 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
           hw[1][c + e] = hw[0][c + e];
           hw[0][c + e] = xv[c + e];
         }
-        s[u][c] = cv.x * sigm<FAST>(cv.x);
-        s[u][c + 1] = cv.y * sigm<FAST>(cv.y);
-        ss[u] += s[u][c] * s[u][c] + s[u][c + 1] * s[u][c + 1];
+        const float2 s2 = swish2<FAST>(cv);
+        s[u][c] = s2.x;
+        s[u][c + 1] = s2.y;
+        if constexpr (NORM) ss2 = ffma2(s2, s2, ss2);
       }
+      ss[u] = ss2.x + ss2.y;
     }
-    if (role < 2) {  // q, k: x / (|x| + eps), the batch's norms in one reduction
+    if constexpr (NORM) {  // q, k: x / (|x| + eps), the batch's norms in one reduction
       const float tot = warp_colsum<kPre>(ss, lane);  // lane l: token l % kPre
+      const float inv_l = 1.f / (sqrtf(tot) + kL2Eps);  // each lane's token, once
 #pragma unroll
       for (int u = 0; u < kPre; ++u) {
-        const float inv = 1.f / (sqrtf(__shfl_sync(0xffffffffu, tot, u)) + kL2Eps);
+        const float2 inv = f2(__shfl_sync(0xffffffffu, inv_l, u));
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) s[u][c] *= inv;
+        for (int c = 0; c < CPL; c += 2) {
+          const float2 r = fmul2(make_float2(s[u][c], s[u][c + 1]), inv);
+          s[u][c] = r.x;
+          s[u][c + 1] = r.y;
+        }
       }
     }
+    if constexpr (CHECK) {
 #pragma unroll
-    for (int u = 0; u < kPre; ++u)
-      if (tb + u < t1) stv<CPL>(y + static_cast<size_t>(tb + u + sh[u]) * HD, s[u]);
+      for (int u = 0; u < kPre; ++u)
+        if (tb + u < t1) stv<CPL>(y + static_cast<size_t>(tb + u + sh[u]) * HD, s[u]);
+      yp = y + static_cast<size_t>(tb + kPre + shift) * HD;
+    } else {
+#pragma unroll
+      for (int u = 0; u < kPre; ++u) {
+        stv<CPL>(yp, s[u]);
+        yp += HD;
+      }
+    }
+  };
+  for (int bi = 0; bi < nbat; ++bi) {
+    tc::cp_async_wait<kStages - 2>();
+    __syncwarp();
+    if (bi + kStages - 1 < nbat) fill(bi + kStages - 1);
+    tc::cp_async_commit();
+    const unsigned char* st = ring + (bi % kStages) * STG;
+    const int tb = t0 + bi * kPre;
+    if (tb + kPre <= t1 && (!VARLEN || tb + kPre <= nb)) batch(st, tb, std::false_type{});
+    else batch(st, tb, std::true_type{});
   }
   tc::cp_async_wait<0>();
   __syncwarp();
@@ -441,12 +530,44 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
   }
 }
 
-template <bool FAST>
-__device__ __forceinline__ float gate_fwd(float u, float ea, float g_min, int kind) {
-  return kind == KDA_GATE_SIGMOID_MIN ? g_min * sigm<FAST>(ea * u) : -ea * softp<FAST>(u);
+// The decay gate of two channels, u = z + b: g_min sigmoid(e^A u)
+// (KDA_GATE_SIGMOID_MIN) or -e^A softplus(u) (KDA_GATE_SOFTPLUS).  FAST (bf16
+// results): sigmoid through one tanh.approx and softplus(u) = max(u, 0) +
+// log(1 + e^-|u|) through ex2 / lg2, errors below bf16's resolution.
+// c0, c1: (e^A / 2, g_min / 2) or (-e^A, -e^A ln 2) for FAST; (e^A, g_min) or (-e^A, -) else.
+template <bool FAST, int KIND>
+__device__ __forceinline__ float2 gate2(float2 u, float2 c0, float2 c1) {
+  if constexpr (KIND == KDA_GATE_SIGMOID_MIN) {
+    if constexpr (FAST) {
+      const float2 h = fmul2(u, c0);
+      return ffma2(make_float2(tanh_approx(h.x), tanh_approx(h.y)), c1, c1);
+    } else {
+      return make_float2(c1.x * sigmoidf_(c0.x * u.x), c1.x * sigmoidf_(c0.x * u.y));
+    }
+  } else {
+    if constexpr (FAST) {
+      constexpr float kLog2e = 1.4426950408889634f;
+      const float2 l = make_float2(log2f(1.f + exp2f(-fabsf(u.x) * kLog2e)), log2f(1.f + exp2f(-fabsf(u.y) * kLog2e)));
+      return ffma2(l, c1, fmul2(make_float2(fmaxf(u.x, 0.f), fmaxf(u.y, 0.f)), c0));
+    } else {
+      return make_float2(c0.x * softplusf_(u.x), c0.x * softplusf_(u.y));
+    }
+  }
 }
 
-template <int CPL, bool VARLEN, typename Tin, typename Tout>
+template <bool FAST, int KIND>
+__device__ __forceinline__ void gate_consts(float ea, float g_min, float2& c0, float2& c1) {
+  constexpr float kLn2 = 0.6931471805599453f;
+  if constexpr (KIND == KDA_GATE_SIGMOID_MIN) {
+    c0 = f2(FAST ? 0.5f * ea : ea);
+    c1 = f2(FAST ? 0.5f * g_min : g_min);
+  } else {
+    c0 = f2(-ea);
+    c1 = f2(-ea * kLn2);
+  }
+}
+
+template <int CPL, bool VARLEN, int KIND, typename Tin, typename Tout>
 __device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane, unsigned char* ring) {
   constexpr bool FAST = std::is_same<Tout, bf16>::value;
   constexpr int D = CPL * 32, RB = D * static_cast<int>(sizeof(Tin)), STG = kPre * RB;
@@ -454,17 +575,26 @@ __device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
   const int ch = h * D + lane * CPL;
   const size_t row0 = static_cast<size_t>(b) * a.T;
   const Tin* zh = static_cast<const Tin*>(a.x[3]) + row0 * HD + h * D;
-  Tout* g = static_cast<Tout*>(a.y[3]) + row0 * HD + ch;
+  Tout* const g = static_cast<Tout*>(a.y[3]) + row0 * HD + ch;
   float bias[CPL];
 #pragma unroll
   for (int c = 0; c < CPL; ++c) bias[c] = a.b_gate ? a.b_gate[ch + c] : 0.f;
-  const float ea = __expf(a.A[h]);
+  float2 c0, c1;
+  gate_consts<FAST, KIND>(__expf(a.A[h]), a.g_min, c0, c1);
   const int nbat = (t1 - t0 + kPre - 1) / kPre;
+  const long long stride = static_cast<long long>(HD) * sizeof(Tin);
+  const unsigned char* src = reinterpret_cast<const unsigned char*>(zh + static_cast<size_t>(t0) * HD) +
+                             lane_src_off<RB>(lane, stride);
+  const uint32_t dst = tc::smem_u32(ring) + lane_dst_off<RB>(lane);
   auto fill = [&](int bi) {
     const int tb = t0 + bi * kPre;
-    ring_fill<RB, kPre>(ring + (bi % kStages) * STG, lane, zh, [&](int r) -> const void* {
-      return tb + r < t1 ? zh + static_cast<size_t>(tb + r) * HD : nullptr;
-    });
+    if (tb + kPre <= t1) {
+      ring_fill_rows<RB, kPre>(dst + (bi % kStages) * STG, src + static_cast<long long>(bi) * kPre * stride, stride);
+    } else {
+      ring_fill<RB, kPre>(ring + (bi % kStages) * STG, lane, zh, [&](int r) -> const void* {
+        return tb + r < t1 ? zh + static_cast<size_t>(tb + r) * HD : nullptr;
+      });
+    }
   };
 #pragma unroll
   for (int bi = 0; bi < kStages - 1; ++bi) {
@@ -499,16 +629,32 @@ __device__ void pro_fwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
     tc::cp_async_commit();
     const unsigned char* st = ring + (bi % kStages) * STG;
     const int tb = t0 + bi * kPre;
+    const int rb = VARLEN ? rwm(tb) : tb;  // output row of the batch's first token
+    const bool plain = tb + kPre <= t1 && (!VARLEN || tb + kPre <= rwm.edge || rwm.s == a.n_seqs - 1);
+    float o[kPre][CPL];
 #pragma unroll
     for (int u = 0; u < kPre; ++u) {
-      if (tb + u < t1) {
-        float o[CPL];
-        ld_row<CPL, Tin>(st + u * RB, lane, o);
+      float zv[CPL];
+      ld_row<CPL, Tin>(st + u * RB, lane, zv);
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) o[c] = gate_fwd<FAST>(o[c] + bias[c], ea, a.g_min, a.gate_kind);
-        const int r = VARLEN ? rwm(tb + u) : tb + u;
-        stv<CPL>(g + static_cast<size_t>(r) * HD, o);
+      for (int c = 0; c < CPL; c += 2) {
+        const float2 r = gate2<FAST, KIND>(fadd2(make_float2(zv[c], zv[c + 1]), make_float2(bias[c], bias[c + 1])),
+                                           c0, c1);
+        o[u][c] = r.x;
+        o[u][c + 1] = r.y;
       }
+    }
+    if (plain) {
+      Tout* p = g + static_cast<size_t>(rb) * HD;
+#pragma unroll
+      for (int u = 0; u < kPre; ++u) {
+        stv<CPL>(p, o[u]);
+        p += HD;
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < kPre; ++u)
+        if (tb + u < t1) stv<CPL>(g + static_cast<size_t>(VARLEN ? rwm(tb + u) : tb + u) * HD, o[u]);
     }
   }
   tc::cp_async_wait<0>();
@@ -528,8 +674,11 @@ __global__ void __launch_bounds__(kWarps * 32) prologue_fwd_kernel(const ProArgs
   const int h = blockIdx.y, role = (a.roles >> (4 * blockIdx.z)) & 15;
   const int b = s / a.spb;
   const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
-  if (role < 3) pro_fwd_conv<CPL, VARLEN, Tin, Tout>(a, role, b, t0, t1, h, lane, ring);
-  else pro_fwd_gate<CPL, VARLEN, Tin, Tout>(a, b, t0, t1, h, lane, ring);
+  if (role < 2) pro_fwd_conv<CPL, VARLEN, true, Tin, Tout>(a, role, b, t0, t1, h, lane, ring);
+  else if (role == 2) pro_fwd_conv<CPL, VARLEN, false, Tin, Tout>(a, role, b, t0, t1, h, lane, ring);
+  else if (a.gate_kind == KDA_GATE_SIGMOID_MIN)
+    pro_fwd_gate<CPL, VARLEN, KDA_GATE_SIGMOID_MIN, Tin, Tout>(a, b, t0, t1, h, lane, ring);
+  else pro_fwd_gate<CPL, VARLEN, KDA_GATE_SOFTPLUS, Tin, Tout>(a, b, t0, t1, h, lane, ring);
 }
 
 // --------------------------------------------------------------- backward ----
@@ -540,8 +689,10 @@ __global__ void __launch_bounds__(kWarps * 32) prologue_fwd_kernel(const ProArgs
 // dcw the conv cotangents of the three tokens above the batch.  A batch's
 // cotangent rows and the input rows the window slides onto stream through the
 // warp's ring.  The L2-norm cotangent needs two sums per token; a batch's
-// 2 kBw sums are one column-sum reduction.
-template <int CPL, bool VARLEN, typename Tin, typename Tout>
+// 2 kBw sums are one column-sum reduction.  Batches inside the strip and
+// inside one packed sequence, taps included, take the plain path (no
+// per-token tests); the strip's ends and sequence edges test every token.
+template <int CPL, bool VARLEN, bool NORM, typename Tin, typename Tout>
 __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, int h, int lane,
                              float (&dw)[4][4], unsigned char* ring) {
   constexpr bool FAST = std::is_same<Tin, bf16>::value;  // the cotangents leave as Tin
@@ -566,23 +717,44 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
   const int nbat = (hi - lo) / kBw + 1;
   // stage bi: the input rows base - NX - u (the window's next rows), then the
   // cotangent rows base - u, u < kBw, base = hi - bi kBw
+  const long long sx = static_cast<long long>(HD) * sizeof(Tin), sy = static_cast<long long>(HD) * sizeof(Tout);
+  const unsigned char* xsrc = reinterpret_cast<const unsigned char*>(xh) + lane_src_off<RBX>(lane, -sx);
+  const unsigned char* ysrc = reinterpret_cast<const unsigned char*>(dyh) + lane_src_off<RBY>(lane, -sy);
+  const uint32_t dstx = tc::smem_u32(ring) + lane_dst_off<RBX>(lane);
+  const uint32_t dsty = tc::smem_u32(ring) + kBw * RBX + lane_dst_off<RBY>(lane);
+  const int ylo = max(lo, 0);
   RowWalk<false> rwf;  // rows of the cotangent tokens the fills walk down
   if (VARLEN) rwf.init(a, max(hi, 0));
   auto fill = [&](int bi) {
     const int base = hi - bi * kBw;
-    unsigned char* st = ring + (bi % kBwStages) * STG;
-    ring_fill<RBX, kBw>(st, lane, xh, [&](int r) -> const void* {
-      const int t = base - NX - r;
-      return t >= 0 ? xh + static_cast<size_t>(t) * HD : nullptr;
-    });
-    int rw[kBw];  // cotangent row of token base - u
+    const uint32_t so = (bi % kBwStages) * STG;
+    unsigned char* st = ring + so;
+    if (base - NX - kBw + 1 >= 0) {
+      ring_fill_rows<RBX, kBw>(dstx + so, xsrc + (base - NX) * sx, -sx);
+    } else {
+      ring_fill<RBX, kBw>(st, lane, xh, [&](int r) -> const void* {
+        const int t = base - NX - r;
+        return t >= 0 ? xh + static_cast<size_t>(t) * HD : nullptr;
+      });
+    }
+    int ry = base;  // cotangent row of token base
+    bool yplain = base - kBw + 1 >= ylo;
+    if (VARLEN && base >= 0) {
+      ry = rwf(base);
+      yplain = yplain && base - kBw + 1 >= rwf.edge;
+    }
+    if (yplain) {
+      ring_fill_rows<RBY, kBw>(dsty + so, ysrc + ry * sy, -sy);
+    } else {
+      int rw[kBw];  // cotangent row of token base - u
 #pragma unroll
-    for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && base - u >= 0 ? rwf(base - u) : base - u;
-    ring_fill<RBY, kBw>(st + kBw * RBX, lane, dyh, [&](int r) -> const void* {
-      const int t = base - r;
-      const int row = r == 0 ? rw[0] : r == 1 ? rw[1] : r == 2 ? rw[2] : rw[3];
-      return t >= 0 && t >= lo ? dyh + static_cast<size_t>(row) * HD : nullptr;
-    });
+      for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && base - u >= 0 ? rwf(base - u) : base - u;
+      ring_fill<RBY, kBw>(st + kBw * RBX, lane, dyh, [&](int r) -> const void* {
+        const int t = base - r;
+        const int row = r == 0 ? rw[0] : r == 1 ? rw[1] : r == 2 ? rw[2] : rw[3];
+        return t >= 0 && t >= lo ? dyh + static_cast<size_t>(row) * HD : nullptr;
+      });
+    }
   };
 #pragma unroll
   for (int bi = 0; bi < kBwStages - 1; ++bi) {
@@ -604,37 +776,25 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
 #pragma unroll
     for (int c = 0; c < CPL; ++c) dcw[j][c] = 0.f;
   const int sw = a.H * (2 * a.dk + a.dv);
-  for (int bi = 0; bi < nbat; ++bi) {
-    tc::cp_async_wait<kBwStages - 2>();
-    __syncwarp();
-    if (bi + kBwStages - 1 < nbat) fill(bi + kBwStages - 1);
-    tc::cp_async_commit();
-    const unsigned char* st = ring + (bi % kBwStages) * STG;
-    const int base = hi - bi * kBw;
-    int lbu[kBw], ubu[kBw];
+  // One batch; CHECK: tokens may lie outside [t0, t1) or below 0, and taps may
+  // cross a packed sequence's edge (lbu / ubu per token).
+  auto batch = [&](const unsigned char* st, int base, const int (&lbu)[kBw], const int (&ubu)[kBw], auto check) {
+    constexpr bool CHECK = decltype(check)::value;
+    constexpr bool MASK = CHECK && VARLEN;
+    // dc[u] = swish'(c) dv and, for the norm, bq[u] = swish'(c) s: the conv
+    // cotangent of token u is then dc c1 + bq c2 with two scalars per token.
+    float dc[kBw][CPL], sums[2 * kBw];
+    [[maybe_unused]] float bq[NORM ? kBw : 1][CPL];
 #pragma unroll
     for (int u = 0; u < kBw; ++u) {
       const int tau = base - u;
-      if constexpr (VARLEN) {
-        while (tau < lb && si > 0) {  // below lb lies the previous sequence
-          ub = lb;
-          --si;
-          lb = __ldg(a.cu + si);
-        }
-      }
-      lbu[u] = lb;
-      ubu[u] = ub;
-    }
-    float s[kBw][CPL], sg[kBw][CPL], dv[kBw][CPL], sums[2 * kBw];
-#pragma unroll
-    for (int u = 0; u < kBw; ++u) {
-      const int tau = base - u;
-      ld_row<CPL, Tout>(st + kBw * RBX + u * RBY, lane, dv[u]);
-      float ss = 0.f, sd = 0.f;
+      float dvr[CPL];
+      ld_row<CPL, Tout>(st + kBw * RBX + u * RBY, lane, dvr);
+      float2 ss2 = f2(0.f), sd2 = f2(0.f);
 #pragma unroll
       for (int c = 0; c < CPL; c += 2) {
         float2 cv2;
-        if constexpr (VARLEN) {
+        if constexpr (MASK) {
           cv2 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -646,49 +806,59 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
           for (int i = 1; i < 4; ++i)
             cv2 = ffma2(make_float2(wt[i][c], wt[i][c + 1]), make_float2(X[u + i][c], X[u + i][c + 1]), cv2);
         }
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float cv = e ? cv2.y : cv2.x;
-          const float sig = sigm<FAST>(cv);
-          s[u][c + e] = cv * sig;
-          sg[u][c + e] = sig * (1.f + cv * (1.f - sig));
-          ss += s[u][c + e] * s[u][c + e];
-          sd += s[u][c + e] * dv[u][c + e];
+        float2 s2, ds2;
+        swish_grad2<FAST>(cv2, s2, ds2);
+        const float2 d2 = make_float2(dvr[c], dvr[c + 1]);
+        const float2 a2 = fmul2(ds2, d2);
+        dc[u][c] = a2.x;
+        dc[u][c + 1] = a2.y;
+        if constexpr (NORM) {
+          const float2 b2 = fmul2(ds2, s2);
+          bq[u][c] = b2.x;
+          bq[u][c + 1] = b2.y;
+          ss2 = ffma2(s2, s2, ss2);
+          sd2 = ffma2(s2, d2, sd2);
         }
       }
-      sums[u] = ss;
-      sums[kBw + u] = sd;
+      sums[u] = ss2.x + ss2.y;
+      sums[kBw + u] = sd2.x + sd2.y;
     }
-    float dc[kBw][CPL];
-    if (role < 2) {  // cotangent of x / (|x| + eps); zero at x = 0
+    if constexpr (NORM) {
+      // cotangent of s / (n + eps), n = |s|, p = s . dv: (dv - s p / (n (n + eps))) / (n + eps),
+      // zero at n = 0.  Lane u (< kBw) holds n^2 and, after one exchange, p of token u.
       const float tot = warp_colsum<2 * kBw>(sums, lane);  // lane l: sum l % (2 kBw)
+      const float p = __shfl_xor_sync(0xffffffffu, tot, kBw);
+      const float n = sqrtf(tot);
+      const float inv = 1.f / (n + kL2Eps);
+      const float c1 = n > 0.f ? inv : 0.f;
+      const float c2 = n > 0.f ? -p / n * inv * inv : 0.f;
 #pragma unroll
       for (int u = 0; u < kBw; ++u) {
-        const float n = sqrtf(__shfl_sync(0xffffffffu, tot, u));
-        const float p = __shfl_sync(0xffffffffu, tot, kBw + u);
-        const float den = n + kL2Eps;
-        const float pr = n > 0.f ? p / n : 0.f;
+        const float2 k1 = f2(__shfl_sync(0xffffffffu, c1, u)), k2 = f2(__shfl_sync(0xffffffffu, c2, u));
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) dc[u][c] = n > 0.f ? (dv[u][c] - s[u][c] * pr / den) / den * sg[u][c] : 0.f;
+        for (int c = 0; c < CPL; c += 2) {
+          const float2 r = ffma2(make_float2(bq[u][c], bq[u][c + 1]), k2,
+                                 fmul2(make_float2(dc[u][c], dc[u][c + 1]), k1));
+          dc[u][c] = r.x;
+          dc[u][c + 1] = r.y;
+        }
       }
-    } else {
-#pragma unroll
-      for (int u = 0; u < kBw; ++u)
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) dc[u][c] = dv[u][c] * sg[u][c];
     }
+    if (CHECK && base < kBw - 1) {  // the batch reaches below token 0 (the conv state's rows)
 #pragma unroll
-    for (int u = 0; u < kBw; ++u) {
-      if (base - u < 0) {
+      for (int u = 0; u < kBw; ++u) {
+        if (base - u < 0) {
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) dc[u][c] = 0.f;
+          for (int c = 0; c < CPL; ++c) dc[u][c] = 0.f;
+        }
       }
     }
     // dx[tau] = sum_i w[i] dc[tau + i] (same sequence); dw[i] += dc[tau] x[tau - i]
+    Tin* dxp = CHECK ? dx : dx + static_cast<size_t>(base) * HD;  // plain: row of token base
 #pragma unroll
     for (int u = 0; u < kBw; ++u) {
       const int tau = base - u;
-      if (tau >= lo && tau < t1) {
+      if (!CHECK || (tau >= lo && tau < t1)) {
         float o[CPL];
 #pragma unroll
         for (int c = 0; c < CPL; c += 2) {
@@ -697,16 +867,21 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
           for (int i = 1; i < 4; ++i) {
             const float2 d = i <= u ? make_float2(dc[u - i][c], dc[u - i][c + 1])
                                     : make_float2(dcw[i - u - 1][c], dcw[i - u - 1][c + 1]);
-            if (!VARLEN || tau + i < ubu[u]) acc = ffma2(make_float2(wt[i][c], wt[i][c + 1]), d, acc);
+            if (!MASK || tau + i < ubu[u]) acc = ffma2(make_float2(wt[i][c], wt[i][c + 1]), d, acc);
           }
           o[c] = acc.x;
           o[c + 1] = acc.y;
         }
-        if (tau >= t0) {
-          stv<CPL>(dx + static_cast<size_t>(tau) * HD, o);
+        if (!CHECK || tau >= t0) {
+          if constexpr (CHECK) {
+            stv<CPL>(dx + static_cast<size_t>(tau) * HD, o);
+          } else {
+            stv<CPL>(dxp, o);
+            dxp -= HD;
+          }
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            if (!VARLEN || tau - i >= lbu[u]) {
+            if (!MASK || tau - i >= lbu[u]) {
 #pragma unroll
               for (int c = 0; c < CPL; c += 2) {
                 const float2 w2 = ffma2(make_float2(dc[u][c], dc[u][c + 1]), make_float2(X[u + i][c], X[u + i][c + 1]),
@@ -733,15 +908,78 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
 #pragma unroll
     for (int u = 0; u < kBw; ++u) {
       const int t = base - NX - u;  // row of X[NX - kBw + u] after the slide
-      if (t >= 0) ld_row<CPL, Tin>(st + u * RBX, lane, X[NX - kBw + u]);
+      if (!CHECK || t >= 0) ld_row<CPL, Tin>(st + u * RBX, lane, X[NX - kBw + u]);
       else load_x<CPL>(a, xb, row0, HD, ch, b, role, t, X[NX - kBw + u]);
     }
+  };
+  for (int bi = 0; bi < nbat; ++bi) {
+    tc::cp_async_wait<kBwStages - 2>();
+    __syncwarp();
+    if (bi + kBwStages - 1 < nbat) fill(bi + kBwStages - 1);
+    tc::cp_async_commit();
+    const unsigned char* st = ring + (bi % kBwStages) * STG;
+    const int base = hi - bi * kBw;
+    int lbu[kBw], ubu[kBw];
+#pragma unroll
+    for (int u = 0; u < kBw; ++u) {
+      const int tau = base - u;
+      if constexpr (VARLEN) {
+        while (tau < lb && si > 0) {  // below lb lies the previous sequence
+          ub = lb;
+          --si;
+          lb = __ldg(a.cu + si);
+        }
+      }
+      lbu[u] = lb;
+      ubu[u] = ub;
+    }
+    // plain: every token in [t0, t1), the window's next rows at or above 0, and
+    // (packed) every tap of the batch inside the lowest token's sequence
+    const bool plain = base < t1 && base - kBw + 1 >= t0 && base - NX - kBw + 1 >= 0 &&
+                       (!VARLEN || (base + 3 < ub && base - kBw + 1 - 3 >= lb));
+    if (plain) batch(st, base, lbu, ubu, std::false_type{});
+    else batch(st, base, lbu, ubu, std::true_type{});
   }
   tc::cp_async_wait<0>();
   __syncwarp();
 }
 
-template <int CPL, bool VARLEN, typename Tin, typename Tout>
+// Cotangents of gate2 for two channels: dz (written) and the terms of dA
+// (accumulated in dA2), dg the gate's cotangent.  SIGMOID_MIN: dz = dg g_min
+// sig (1 - sig) e^A, dA += dz u; SOFTPLUS: dz = -dg e^A sigmoid(u), dA -= dg e^A softplus(u).
+template <bool FAST, int KIND>
+__device__ __forceinline__ float2 gate_grad2(float2 u, float2 dg, float ea, float g_min, float2& dA2) {
+  if constexpr (KIND == KDA_GATE_SIGMOID_MIN) {
+    float2 sg;
+    if constexpr (FAST) {
+      const float2 h = fmul2(u, f2(0.5f * ea));
+      sg = ffma2(make_float2(tanh_approx(h.x), tanh_approx(h.y)), f2(0.5f), f2(0.5f));
+    } else {
+      sg = make_float2(sigmoidf_(ea * u.x), sigmoidf_(ea * u.y));
+    }
+    // dg g_min e^A sg (1 - sg)
+    const float2 t = fmul2(fmul2(dg, f2(g_min * ea)), fmul2(sg, ffma2(sg, f2(-1.f), f2(1.f))));
+    dA2 = ffma2(t, u, dA2);
+    return t;
+  } else {
+    const float2 gn = fmul2(dg, f2(-ea));
+    float2 sg, sp;
+    if constexpr (FAST) {
+      constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+      const float2 h = fmul2(u, f2(0.5f));
+      sg = ffma2(make_float2(tanh_approx(h.x), tanh_approx(h.y)), f2(0.5f), f2(0.5f));
+      const float2 l = make_float2(log2f(1.f + exp2f(-fabsf(u.x) * kLog2e)), log2f(1.f + exp2f(-fabsf(u.y) * kLog2e)));
+      sp = ffma2(l, f2(kLn2), make_float2(fmaxf(u.x, 0.f), fmaxf(u.y, 0.f)));
+    } else {
+      sg = make_float2(sigmoidf_(u.x), sigmoidf_(u.y));
+      sp = make_float2(softplusf_(u.x), softplusf_(u.y));
+    }
+    dA2 = ffma2(gn, sp, dA2);
+    return fmul2(gn, sg);
+  }
+}
+
+template <int CPL, bool VARLEN, int KIND, typename Tin, typename Tout>
 __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int lane, float (&db)[4],
                              float& dA, unsigned char* ring) {
   constexpr bool FAST = std::is_same<Tin, bf16>::value;
@@ -759,6 +997,11 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
   for (int c = 0; c < CPL; ++c) bias[c] = a.b_gate ? a.b_gate[ch + c] : 0.f;
   const float ea = __expf(a.A[h]);
   const int nbat = (t1 - t0 + kBw - 1) / kBw;
+  const long long sx = static_cast<long long>(HD) * sizeof(Tin), sy = static_cast<long long>(HD) * sizeof(Tout);
+  const unsigned char* xsrc = reinterpret_cast<const unsigned char*>(zh) + lane_src_off<RBX>(lane, sx);
+  const unsigned char* ysrc = reinterpret_cast<const unsigned char*>(dgh) + lane_src_off<RBY>(lane, sy);
+  const uint32_t dstx = tc::smem_u32(ring) + lane_dst_off<RBX>(lane);
+  const uint32_t dsty = tc::smem_u32(ring) + kBw * RBX + lane_dst_off<RBY>(lane);
   RowWalk<true> rwf, rwb;  // rows of the cotangent tokens the fills walk up, of this lane's beta tokens
   if (VARLEN) {
     rwf.init(a, t0);
@@ -766,17 +1009,28 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
   }
   auto fill = [&](int bi) {
     const int tb = t0 + bi * kBw;
-    unsigned char* st = ring + (bi % kBwStages) * STG;
-    ring_fill<RBX, kBw>(st, lane, zh, [&](int r) -> const void* {
-      return tb + r < t1 ? zh + static_cast<size_t>(tb + r) * HD : nullptr;
-    });
-    int rw[kBw];  // cotangent row of token tb + u
+    const uint32_t so = (bi % kBwStages) * STG;
+    unsigned char* st = ring + so;
+    const bool full = tb + kBw <= t1;
+    if (full) {
+      ring_fill_rows<RBX, kBw>(dstx + so, xsrc + tb * sx, sx);
+    } else {
+      ring_fill<RBX, kBw>(st, lane, zh, [&](int r) -> const void* {
+        return tb + r < t1 ? zh + static_cast<size_t>(tb + r) * HD : nullptr;
+      });
+    }
+    const int ry = VARLEN ? rwf(tb) : tb;  // cotangent row of token tb
+    if (full && (!VARLEN || tb + kBw <= rwf.edge || rwf.s == a.n_seqs - 1)) {
+      ring_fill_rows<RBY, kBw>(dsty + so, ysrc + ry * sy, sy);
+    } else {
+      int rw[kBw];  // cotangent row of token tb + u
 #pragma unroll
-    for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && tb + u < t1 ? rwf(tb + u) : tb + u;
-    ring_fill<RBY, kBw>(st + kBw * RBX, lane, dgh, [&](int r) -> const void* {
-      const int row = r == 0 ? rw[0] : r == 1 ? rw[1] : r == 2 ? rw[2] : rw[3];
-      return tb + r < t1 ? dgh + static_cast<size_t>(row) * HD : nullptr;
-    });
+      for (int u = 0; u < kBw; ++u) rw[u] = VARLEN && tb + u < t1 ? rwf(tb + u) : tb + u;
+      ring_fill<RBY, kBw>(st + kBw * RBX, lane, dgh, [&](int r) -> const void* {
+        const int row = r == 0 ? rw[0] : r == 1 ? rw[1] : r == 2 ? rw[2] : rw[3];
+        return tb + r < t1 ? dgh + static_cast<size_t>(row) * HD : nullptr;
+      });
+    }
   };
 #pragma unroll
   for (int bi = 0; bi < kBwStages - 1; ++bi) {
@@ -792,6 +1046,7 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
     const int r = VARLEN ? rwb(t) : t;
     stf(dbl + i, ldf(dbt + (row0 + r) * a.H + h) * s * (1.f - s));
   }
+  float2 dA2 = f2(0.f);
   for (int bi = 0; bi < nbat; ++bi) {
     tc::cp_async_wait<kBwStages - 2>();
     __syncwarp();
@@ -799,30 +1054,30 @@ __device__ void pro_bwd_gate(const ProArgs& a, int b, int t0, int t1, int h, int
     tc::cp_async_commit();
     const unsigned char* st = ring + (bi % kBwStages) * STG;
     const int tb = t0 + bi * kBw;
+    const bool full = tb + kBw <= t1;
+    Tin* p = dz + static_cast<size_t>(tb) * HD;
 #pragma unroll
     for (int u = 0; u < kBw; ++u) {
-      if (tb + u < t1) {
+      if (full || tb + u < t1) {
         float o[CPL], zv[CPL], gv[CPL];
         ld_row<CPL, Tin>(st + u * RBX, lane, zv);
         ld_row<CPL, Tout>(st + kBw * RBX + u * RBY, lane, gv);
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          const float uu = zv[c] + bias[c];
-          if (a.gate_kind == KDA_GATE_SIGMOID_MIN) {
-            const float sg = sigm<FAST>(ea * uu);
-            const float t = gv[c] * a.g_min * sg * (1.f - sg) * ea;
-            o[c] = t;
-            dA += t * uu;
-          } else {
-            o[c] = -gv[c] * ea * sigm<FAST>(uu);
-            dA -= gv[c] * ea * softp<FAST>(uu);
-          }
-          db[c] += o[c];
+        for (int c = 0; c < CPL; c += 2) {
+          const float2 uu = fadd2(make_float2(zv[c], zv[c + 1]), make_float2(bias[c], bias[c + 1]));
+          const float2 r = gate_grad2<FAST, KIND>(uu, make_float2(gv[c], gv[c + 1]), ea, a.g_min, dA2);
+          o[c] = r.x;
+          o[c + 1] = r.y;
+          const float2 d2 = fadd2(make_float2(db[c], db[c + 1]), r);
+          db[c] = d2.x;
+          db[c + 1] = d2.y;
         }
-        stv<CPL>(dz + static_cast<size_t>(tb + u) * HD, o);
+        stv<CPL>(p, o);
       }
+      p += HD;
     }
   }
+  dA += dA2.x + dA2.y;
   tc::cp_async_wait<0>();
   __syncwarp();
 }
@@ -846,8 +1101,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32) prologue_bwd_kernel(const ProA
   if (s < a.n_strips) {
     const int b = s / a.spb;
     const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
-    if (role < 3) pro_bwd_conv<CPL, VARLEN, Tin, Tout>(a, role, b, t0, t1, h, lane, acc, ring);
-    else pro_bwd_gate<CPL, VARLEN, Tin, Tout>(a, b, t0, t1, h, lane, acc[0], dA, ring);
+    if (role < 2) pro_bwd_conv<CPL, VARLEN, true, Tin, Tout>(a, role, b, t0, t1, h, lane, acc, ring);
+    else if (role == 2) pro_bwd_conv<CPL, VARLEN, false, Tin, Tout>(a, role, b, t0, t1, h, lane, acc, ring);
+    else if (a.gate_kind == KDA_GATE_SIGMOID_MIN)
+      pro_bwd_gate<CPL, VARLEN, KDA_GATE_SIGMOID_MIN, Tin, Tout>(a, b, t0, t1, h, lane, acc[0], dA, ring);
+    else pro_bwd_gate<CPL, VARLEN, KDA_GATE_SOFTPLUS, Tin, Tout>(a, b, t0, t1, h, lane, acc[0], dA, ring);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i)
