@@ -454,8 +454,10 @@ __device__ void pro_fwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
           for (int j = 0; j < 3; ++j)
 #pragma unroll
             for (int c = 0; c < CPL; ++c) hw[j][c] = 0.f;
-          ++si;
-          nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+          do {  // past the empty sequences that start at the same token
+            ++si;
+            nb = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
+          } while (tb + u == nb);
           shift = a.out_rows ? __ldg(a.out_rows + si) - __ldg(a.cu + si) : 0;
         }
       }

@@ -78,29 +78,35 @@ def test_prologue_fwd_matches_oracle(B, T, H, dk, dv, K, dt, kind, state):
         assert scale_rel_err(_np(st_out), ref["state_out"]) <= 1e-6  # copies of the inputs
 
 
-def test_prologue_varlen_restarts_each_sequence():
+@pytest.mark.parametrize("cu,dt", [
+    ([0, 5, 6, 70, 200, 300], torch.float32),
+    # empty sequences inside the pack, two starting at the same token, and a
+    # boundary inside an 8-token batch of a 256-token strip
+    ([0, 5, 5, 70, 70, 70, 203, 300], torch.float32),
+    ([0, 0, 1, 9, 9, 261, 300, 300], torch.bfloat16),
+])
+def test_prologue_varlen_restarts_each_sequence(cu, dt):
     H, dk, dv, K, T = 2, 128, 128, 4, 300
-    x, w, _ = _case(2, 1, T, H, dk, dv, K, torch.float32)
-    cu = [0, 5, 6, 70, 200, 300]
-    q, k, v, g, beta = _run_fwd(x, w, None, H, torch.float32, "sigmoid_min", cu=cu)
+    x, w, _ = _case(2, 1, T, H, dk, dv, K, dt)
+    q, k, v, g, beta = _run_fwd(x, w, None, H, dt, "sigmoid_min", cu=cu)
     ref = M.prologue_fwd(x["qp"], x["kp"], x["vp"], x["z"], x["beta_logit"], w["conv_q"], w["conv_k"], w["conv_v"],
                          w["b_gate"], w["A"], H, dk, dv, cu_seqlens=cu)
     for name, got in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
-        assert scale_rel_err(_np(got), ref[name]) <= 1e-4, name
+        assert scale_rel_err(_np(got), ref[name]) <= (1e-4 if dt == torch.float32 else 1e-2), name
 
 
-@pytest.mark.parametrize("B,T,H,dk,dv,K,dt,kind,state,varlen", [
-    (2, 200, 2, 128, 128, 4, torch.float32, "sigmoid_min", True, False),
-    (1, 150, 2, 64, 128, 3, torch.float32, "softplus", False, False),
-    (1, 260, 2, 128, 128, 4, torch.float32, "sigmoid_min", False, True),
-    (2, 130, 2, 128, 128, 4, torch.bfloat16, "sigmoid_min", False, False),
-    (1, 3, 1, 64, 64, 4, torch.float32, "softplus", True, False),
+@pytest.mark.parametrize("B,T,H,dk,dv,K,dt,kind,state,cu", [
+    (2, 200, 2, 128, 128, 4, torch.float32, "sigmoid_min", True, None),
+    (1, 150, 2, 64, 128, 3, torch.float32, "softplus", False, None),
+    (1, 260, 2, 128, 128, 4, torch.float32, "sigmoid_min", False, [0, 40, 41, 190, 260]),
+    (1, 300, 2, 128, 128, 4, torch.bfloat16, "softplus", False, [0, 5, 5, 70, 70, 70, 203, 300]),
+    (2, 130, 2, 128, 128, 4, torch.bfloat16, "sigmoid_min", False, None),
+    (1, 3, 1, 64, 64, 4, torch.float32, "softplus", True, None),
 ])
-def test_prologue_bwd_matches_oracle(B, T, H, dk, dv, K, dt, kind, state, varlen):
+def test_prologue_bwd_matches_oracle(B, T, H, dk, dv, K, dt, kind, state, cu):
     from axiom_b200 import mixer
 
     x, w, st = _case(3, B, T, H, dk, dv, K, dt, state)
-    cu = [0, 40, 41, 190, 260] if varlen else None
     rng = np.random.default_rng(9)
     r = (lambda a: bf16_round(a).astype(np.float64)) if dt == torch.bfloat16 else (lambda a: a.astype(np.float32).astype(np.float64))
     cot = dict(dq=r(rng.standard_normal((B, T, H, dk))), dk=r(rng.standard_normal((B, T, H, dk))),
