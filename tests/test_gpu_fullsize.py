@@ -122,3 +122,43 @@ def test_cfg2_full_size_prefill_units_match_oracle():
         o_ref, s_ref = K.chunk_fwd(*xs, S0[b:b + 1, h:h + 1].double().cpu().numpy(), chunk=64)
         assert K.scale_rel_err(_np(o[b:b + 1, :, h:h + 1]), o_ref) <= TOL, (b, h)
         assert K.scale_rel_err(_np(s_t[b:b + 1, h:h + 1]), s_ref) <= TOL, (b, h)
+
+
+def test_cfg3_full_size_with_the_mixer_gate_at_zero_bias():
+    """cfg3's shapes with BASELINE's mixer decay at b = 0: g = -exp(A_log)
+    softplus(x), A_log ~ U(log 1, log 16) per head, x ~ N(0, 1) per (token,
+    channel), up to ~50 per token, so every chunk is far past the single-anchor
+    exponent budget and takes the exact score path.  The reference's
+    tile-anchored scores clamp here, so sampled units are checked against the
+    oracle's direct decay ratio (``tile=None``), forward and backward; the whole
+    call against two half calls with the state carried."""
+    from axiom_b200 import kda_bwd, kda_fwd
+
+    B, T, H = 4, 8192, 32
+    q, k, v, _, beta, _ = _inputs(B, T, H, seed=9)
+    gen = torch.Generator("cuda").manual_seed(10)
+    a_log = torch.empty(H, device="cuda").uniform_(0.0, float(np.log(16.0)), generator=gen)
+    x = torch.randn(B, T, H, 128, device="cuda", generator=gen)
+    g = (-a_log.exp()[None, None, :, None] * torch.nn.functional.softplus(x)).to(torch.bfloat16)
+    do = torch.randn(B, T, H, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    o, s_t, ckpt = kda_fwd(q, k, v, g, beta, None, chunk=64, o_dtype=torch.float32, need_ckpt=True)
+    grads = kda_bwd(q, k, v, g, beta, ckpt, do, None, chunk=64, need_ds0=False)
+    torch.cuda.synchronize()
+    del ckpt
+    for b, h in ((0, 5), (3, 30)):
+        xs = [_unit(t, b, h) for t in (q, k, v, g)] + [beta[b:b + 1, :, h:h + 1].double().cpu().numpy()]
+        o_ref, s_ref = K.chunk_fwd(*xs, None, chunk=64, tile=None)
+        assert K.scale_rel_err(_np(o[b:b + 1, :, h:h + 1]), o_ref) <= TOL, (b, h)
+        assert K.scale_rel_err(_np(s_t[b:b + 1, h:h + 1]), s_ref) <= TOL, (b, h)
+        ref = K.chunk_bwd(*xs, None, _unit(do, b, h), None, chunk=64, tile=None)
+        for name, gr, rf in zip(("dq", "dk", "dv", "dg", "dbeta"), grads[:5], ref[:5]):
+            assert K.scale_rel_err(_np(gr[b:b + 1, :, h:h + 1]), rf) <= TOL, (name, b, h)
+    del grads
+    m = T // 2
+    halves = [[t[:, :m].contiguous() for t in (q, k, v, g, beta)], [t[:, m:].contiguous() for t in (q, k, v, g, beta)]]
+    o1, s_mid, _ = kda_fwd(*halves[0], None, chunk=64, o_dtype=torch.float32)
+    o2, s_end, _ = kda_fwd(*halves[1], s_mid, chunk=64, o_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert K.scale_rel_err(_np(o1), _np(o[:, :m])) <= TOL_SPLIT
+    assert K.scale_rel_err(_np(o2), _np(o[:, m:])) <= TOL_SPLIT
+    assert K.scale_rel_err(_np(s_end), _np(s_t)) <= TOL_SPLIT
