@@ -66,6 +66,7 @@ KINDS = {"sigmoid_min": M.GATE_SIGMOID_MIN, "softplus": M.GATE_SOFTPLUS}
     (2, 64, 2, 128, 64, 2, torch.float32, "sigmoid_min", True),
     (1, 2, 2, 64, 64, 4, torch.float32, "softplus", True),     # T < K - 1: the state shifts through
     (1, 77, 1, 128, 128, 1, torch.bfloat16, "softplus", False),
+    (1, 150, 2, 64, 64, 4, torch.bfloat16, "softplus", True),    # two channels per lane, bf16
 ])
 def test_prologue_fwd_matches_oracle(B, T, H, dk, dv, K, dt, kind, state):
     x, w, st = _case(1, B, T, H, dk, dv, K, dt, state)
@@ -102,6 +103,8 @@ def test_prologue_varlen_restarts_each_sequence(cu, dt):
     (1, 300, 2, 128, 128, 4, torch.bfloat16, "softplus", False, [0, 5, 5, 70, 70, 70, 203, 300]),
     (2, 130, 2, 128, 128, 4, torch.bfloat16, "sigmoid_min", False, None),
     (1, 3, 1, 64, 64, 4, torch.float32, "softplus", True, None),
+    (1, 140, 2, 64, 64, 4, torch.bfloat16, "sigmoid_min", True, None),
+    (1, 270, 2, 64, 64, 3, torch.bfloat16, "softplus", False, [0, 100, 100, 133, 270]),
 ])
 def test_prologue_bwd_matches_oracle(B, T, H, dk, dv, K, dt, kind, state, cu):
     from axiom_b200 import mixer
