@@ -123,3 +123,56 @@ def test_layer_at_config5_width_matches_oracle(gate_bias):
         got = getattr(p, name).grad
         assert got is not None, name
         assert scale_rel_err(got.double().cpu().numpy(), g[name]) <= tol, name
+
+
+def test_boundary_decay_sgd_steps_stay_finite_and_match():
+    """The reference's boundary-alpha nan gate (``net/tests/test_kda_cc_fused_persist.py:1405-1456``):
+    the K3 gate g = g_min sigmoid(e^A z) at its model bound -- A = 0, W_a = 0 and
+    gate bias 6 give |g| = 5 sigmoid(6) = 4.99 per token on every channel, where an
+    exponent taken over a whole chunk before masking leaves fp32's range ~18
+    tokens in.  The tensor-core path (bf16, dk = dv = 128), ten SGD steps of the
+    layer on the linear loss sum(out * w): every loss and gradient finite, and
+    the first step's output and gradients equal the float64 oracle layer (5e-2;
+    1e-1 for A, whose gradient here is 6 g_min sigmoid'(6) times the sum of the
+    core's dg over all tokens and channels: a sum that cancels to a few 1e-3
+    while the bf16 rounding of each dg term does not)."""
+    from axiom_b200 import layer
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    d_model, H, dk, T, lr, steps = 96, 2, 128, 256, 1e-4, 10
+    fields = ("W_q", "W_k", "W_v", "W_g", "W_beta", "W_a_down", "W_a_up", "b_gate", "A", "conv_q", "conv_k",
+              "conv_v", "W_o")
+    p = layer.init_params(d_model, H, dk, dk, rank=16, K=4, gate_kind="sigmoid_min", dtype=torch.bfloat16, seed=7)
+    with torch.no_grad():
+        p.W_a_down.zero_()
+        p.W_a_up.zero_()
+        p.A.zero_()
+        p.b_gate.fill_(6.0)
+    gen = torch.Generator(device="cpu").manual_seed(8)
+    x = torch.randn(T, d_model, generator=gen).to("cuda", torch.bfloat16)
+    w = torch.randn(T, d_model, generator=gen).to("cuda", torch.bfloat16)
+    for step in range(steps):
+        xr = x.clone().requires_grad_(True)
+        out = layer.kda_layer(p, xr, H=H, gate_kind="sigmoid_min")
+        loss = (out.float() * w.float()).sum()
+        loss.backward()
+        assert torch.isfinite(loss), step
+        assert torch.isfinite(xr.grad).all(), step
+        for f in fields:
+            assert torch.isfinite(getattr(p, f).grad).all(), (step, f)
+        if step == 0:
+            P = {f: getattr(p, f).detach().double().cpu().numpy() for f in fields}
+            ref, cache = M.layer_fwd(P, x.double().cpu().numpy(), H, None, kind=M.GATE_SIGMOID_MIN)
+            g = M.layer_bwd(P, cache, w.double().cpu().numpy())
+            assert scale_rel_err(out.detach().double().cpu().numpy(), ref) <= 5e-2
+            assert scale_rel_err(xr.grad.double().cpu().numpy(), g["x"]) <= 5e-2
+            for f in fields:
+                if f in ("W_a_down", "W_a_up"):  # zero with zero factors on both sides
+                    continue
+                tol = 1e-1 if f == "A" else 5e-2
+                assert scale_rel_err(getattr(p, f).grad.double().cpu().numpy(), g[f]) <= tol, f
+        with torch.no_grad():
+            for f in fields:
+                t = getattr(p, f)
+                t -= lr * t.grad.to(t.dtype)
+                t.grad = None
