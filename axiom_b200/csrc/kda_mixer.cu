@@ -270,6 +270,7 @@ struct ProArgs {
   int spb;      // strips per batch row
   int n_strips;
   int roles;    // tensor of each blockIdx.z, 4 bits each
+  int head_x;   // forward grid (heads, strip groups): the heads of one token range run together
 };
 
 // Element r (0..3) of a 4-pointer parameter array by selects: indexing the
@@ -670,10 +671,10 @@ template <int CPL, bool VARLEN, typename Tin, typename Tout>
 __global__ void __launch_bounds__(kWarps * 32) prologue_fwd_kernel(const ProArgs a) {
   extern __shared__ __align__(16) unsigned char pro_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int s = blockIdx.x * kWarps + warp;
+  const int s = (a.head_x ? blockIdx.y : blockIdx.x) * kWarps + warp;
   if (s >= a.n_strips) return;
   unsigned char* ring = pro_smem + warp * fwd_ring_bytes<CPL, Tin>();
-  const int h = blockIdx.y, role = (a.roles >> (4 * blockIdx.z)) & 15;
+  const int h = a.head_x ? blockIdx.x : blockIdx.y, role = (a.roles >> (4 * blockIdx.z)) & 15;
   const int b = s / a.spb;
   const int t0 = (s % a.spb) * kStrip, t1 = min(t0 + kStrip, a.T);
   if (role < 2) pro_fwd_conv<CPL, VARLEN, true, Tin, Tout>(a, role, b, t0, t1, h, lane, ring);
@@ -1453,7 +1454,12 @@ template <int CPL, bool VARLEN, typename Tin, typename Tout>
 int launch_prologue_v(ProArgs& a, int roles, int n_roles, bool bwd, cudaStream_t st) {
   a.roles = roles;
   const int w = bwd ? kBwdWarps : kWarps;
-  const dim3 grid((a.n_strips + w - 1) / w, a.H, n_roles);
+  const int groups = (a.n_strips + w - 1) / w;
+  // forward: heads along x, so the blocks in flight read every head of the same
+  // token rows (whole DRAM rows; measured 4 % faster); the backward, bound by its
+  // arithmetic, keeps (strip groups, heads)
+  a.head_x = !bwd && groups <= 65535;
+  const dim3 grid(a.head_x ? a.H : groups, a.head_x ? groups : a.H, n_roles);
   static bool done_f[64] = {false}, done_b[64] = {false};
   if (bwd) {
     constexpr int smem = kBwdWarps * bwd_ring_bytes<CPL, Tin, Tout>();
