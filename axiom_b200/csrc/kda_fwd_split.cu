@@ -58,6 +58,9 @@ constexpr int R_TRI = R_BAR + 128;       // [L ; U'] bf16 CM[128][64] (0/1, buil
 constexpr int R_GN = R_TRI + 16384;      // exp(-G_C) fp32[128] (G_C itself while staged)
 constexpr int PREP_SMEM = R_GN + 512;
 
+// Unit u = (b H + h) n_chunks + c: the kernels below also use u itself as the
+// chunk-head's slot in the checkpoint (factor blocks, states), so this order
+// and that addressing change together.
 __device__ __forceinline__ void unit_coords(long long u, int n_chunks, int H, int& b, int& h, int& c) {
   const long long bh = u / n_chunks;
   c = static_cast<int>(u - bh * n_chunks);
