@@ -140,7 +140,7 @@ def kda_layer(p: KDALayerParams, x, *, H, cu_seqlens=None, gate_kind="softplus",
                                               gate_kind=gate_kind, cu_seqlens=cu, out_rows=rows)
         o, s_t = chunk_kda_varlen(q, k, v, g, beta, offs, S0, chunk=chunk)
         y = mixer.gated_rmsnorm(o, gl[None], cu_seqlens=cu, out_rows=rows)
-    out = y[0] @ p.W_o
+    out = y.squeeze(0) @ p.W_o  # a view both ways (indexing's backward would zero-fill y's shape)
     return (out, s_t) if return_state else out
 
 
