@@ -688,10 +688,10 @@ __global__ void __launch_bounds__(kWarps * 32) prologue_fwd_kernel(const ProArgs
 
 // q, k, v of one strip, swept from its end (hi: the last token whose conv
 // cotangent the strip's inputs need) down to its start, kBw tokens a batch:
-// X[j] holds x[base - j] (j < kBw + 3: every tap of every token of the batch),
-// dcw the conv cotangents of the three tokens above the batch.  A batch's
-// cotangent rows and the input rows the window slides onto stream through the
-// warp's ring.  The L2-norm cotangent needs two sums per token; a batch's
+// the window x[base - j], j < kBw + 3 (every tap of every token of the batch),
+// and the conv cotangents of the three tokens above the batch live in
+// registers.  A batch's cotangent rows and the input rows the window moves
+// onto stream through the warp's shared-memory ring.  The L2-norm cotangent needs two sums per token; a batch's
 // 2 kBw sums are one column-sum reduction.  Batches inside the strip and
 // inside one packed sequence, taps included, take the plain path (no
 // per-token tests); the strip's ends and sequence edges test every token.
@@ -770,23 +770,37 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     lb = __ldg(a.cu + si);
     ub = si + 1 < a.n_seqs ? __ldg(a.cu + si + 1) : INT_MAX;
   }
-  float X[NX][CPL];
+  // The input rows in a ring of 8: a batch of phase P (its index's parity)
+  // sees x[base - j] in R[(4 P + j) % 8], j < NX, and loads the rows the next
+  // batch adds into the slots its own first kBw rows leave (and the spare), so
+  // the window moves by renaming instead of copies.  Likewise the two batches'
+  // conv cotangents alternate between DA and DB, each batch reading the other's
+  // as the cotangents of the three tokens above it.
+  // (Packed sequences keep one phase and copy the rows instead: their masks
+  // leave no registers for the second set.)
+  constexpr bool RING = !VARLEN;
+  static_assert(NX + 1 == 8 && kBw == 4, "an 8-row ring, 4 rows a batch");
+  float R[8][CPL], DA[kBw][CPL], DB[kBw][CPL];
 #pragma unroll
-  for (int j = 0; j < NX; ++j) load_x<CPL>(a, xb, row0, HD, ch, b, role, hi - j, X[j]);
-  float dcw[3][CPL];
+  for (int j = 0; j < NX; ++j) load_x<CPL>(a, xb, row0, HD, ch, b, role, hi - j, R[j]);
 #pragma unroll
-  for (int j = 0; j < 3; ++j)
+  for (int c = 0; c < CPL; ++c) R[NX][c] = 0.f;
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) dcw[j][c] = 0.f;
+  for (int j = 0; j < kBw; ++j)
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) DA[j][c] = DB[j][c] = 0.f;
   const int sw = a.H * (2 * a.dk + a.dv);
   // One batch; CHECK: tokens may lie outside [t0, t1) or below 0, and taps may
   // cross a packed sequence's edge (lbu / ubu per token).
-  auto batch = [&](const unsigned char* st, int base, const int (&lbu)[kBw], const int (&ubu)[kBw], auto check) {
+  auto batch = [&](const unsigned char* st, int base, const int (&lbu)[kBw], const int (&ubu)[kBw], auto check,
+                   auto phase, float (&dc)[kBw][CPL], const float (&dcp)[kBw][CPL]) {
     constexpr bool CHECK = decltype(check)::value;
     constexpr bool MASK = CHECK && VARLEN;
+    constexpr int P4 = 4 * decltype(phase)::value;
+#define X(j) R[(P4 + (j)) & 7]
     // dc[u] = swish'(c) dv and, for the norm, bq[u] = swish'(c) s: the conv
     // cotangent of token u is then dc c1 + bq c2 with two scalars per token.
-    float dc[kBw][CPL], sums[2 * kBw];
+    float sums[2 * kBw];
     [[maybe_unused]] float bq[NORM ? kBw : 1][CPL];
 #pragma unroll
     for (int u = 0; u < kBw; ++u) {
@@ -802,12 +816,12 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             if (tau - i >= lbu[u])
-              cv2 = ffma2(make_float2(wt[i][c], wt[i][c + 1]), make_float2(X[u + i][c], X[u + i][c + 1]), cv2);
+              cv2 = ffma2(make_float2(wt[i][c], wt[i][c + 1]), make_float2(X(u + i)[c], X(u + i)[c + 1]), cv2);
         } else {
-          cv2 = fmul2(make_float2(wt[0][c], wt[0][c + 1]), make_float2(X[u][c], X[u][c + 1]));
+          cv2 = fmul2(make_float2(wt[0][c], wt[0][c + 1]), make_float2(X(u)[c], X(u)[c + 1]));
 #pragma unroll
           for (int i = 1; i < 4; ++i)
-            cv2 = ffma2(make_float2(wt[i][c], wt[i][c + 1]), make_float2(X[u + i][c], X[u + i][c + 1]), cv2);
+            cv2 = ffma2(make_float2(wt[i][c], wt[i][c + 1]), make_float2(X(u + i)[c], X(u + i)[c + 1]), cv2);
         }
         float2 s2, ds2;
         swish_grad2<FAST>(cv2, s2, ds2);
@@ -869,7 +883,7 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
 #pragma unroll
           for (int i = 1; i < 4; ++i) {
             const float2 d = i <= u ? make_float2(dc[u - i][c], dc[u - i][c + 1])
-                                    : make_float2(dcw[i - u - 1][c], dcw[i - u - 1][c + 1]);
+                                    : make_float2(dcp[kBw - i + u][c], dcp[kBw - i + u][c + 1]);
             if (!MASK || tau + i < ubu[u]) acc = ffma2(make_float2(wt[i][c], wt[i][c + 1]), d, acc);
           }
           o[c] = acc.x;
@@ -887,7 +901,7 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
             if (!MASK || tau - i >= lbu[u]) {
 #pragma unroll
               for (int c = 0; c < CPL; c += 2) {
-                const float2 w2 = ffma2(make_float2(dc[u][c], dc[u][c + 1]), make_float2(X[u + i][c], X[u + i][c + 1]),
+                const float2 w2 = ffma2(make_float2(dc[u][c], dc[u][c + 1]), make_float2(X(u + i)[c], X(u + i)[c + 1]),
                                         make_float2(dw[i][c], dw[i][c + 1]));
                 dw[i][c] = w2.x;
                 dw[i][c + 1] = w2.y;
@@ -899,21 +913,22 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
         }
       }
     }
-    // slide down by kBw tokens
+    // the next batch's window: its rows NX - kBw .. NX - 1 come in over this
+    // batch's first kBw (ring), or after the rows that stay move down (copies)
+    if constexpr (!RING) {
 #pragma unroll
-    for (int j = 0; j < 3; ++j)
+      for (int j = 0; j < NX - kBw; ++j)
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) dcw[j][c] = dc[kBw - 1 - j][c];
-#pragma unroll
-    for (int j = 0; j < NX - kBw; ++j)
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) X[j][c] = X[j + kBw][c];
+        for (int c = 0; c < CPL; ++c) R[j][c] = R[j + kBw][c];
+    }
 #pragma unroll
     for (int u = 0; u < kBw; ++u) {
-      const int t = base - NX - u;  // row of X[NX - kBw + u] after the slide
-      if (!CHECK || t >= 0) ld_row<CPL, Tin>(st + u * RBX, lane, X[NX - kBw + u]);
-      else load_x<CPL>(a, xb, row0, HD, ch, b, role, t, X[NX - kBw + u]);
+      const int t = base - NX - u;
+      float (&row)[CPL] = RING ? X(NX + u) : R[NX - kBw + u];
+      if (!CHECK || t >= 0) ld_row<CPL, Tin>(st + u * RBX, lane, row);
+      else load_x<CPL>(a, xb, row0, HD, ch, b, role, t, row);
     }
+#undef X
   };
   for (int bi = 0; bi < nbat; ++bi) {
     tc::cp_async_wait<kBwStages - 2>();
@@ -940,8 +955,21 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     // (packed) every tap of the batch inside the lowest token's sequence
     const bool plain = base < t1 && base - kBw + 1 >= t0 && base - NX - kBw + 1 >= 0 &&
                        (!VARLEN || (base + 3 < ub && base - kBw + 1 - 3 >= lb));
-    if (plain) batch(st, base, lbu, ubu, std::false_type{});
-    else batch(st, base, lbu, ubu, std::true_type{});
+    using P0 = std::integral_constant<int, 0>;
+    using P1 = std::integral_constant<int, 1>;
+    if (RING && (bi & 1)) {
+      if (plain) batch(st, base, lbu, ubu, std::false_type{}, P1{}, DB, DA);
+      else batch(st, base, lbu, ubu, std::true_type{}, P1{}, DB, DA);
+    } else {
+      if (plain) batch(st, base, lbu, ubu, std::false_type{}, P0{}, DA, DB);
+      else batch(st, base, lbu, ubu, std::true_type{}, P0{}, DA, DB);
+      if constexpr (!RING) {
+#pragma unroll
+        for (int j = 0; j < kBw; ++j)
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) DB[j][c] = DA[j][c];
+      }
+    }
   }
   tc::cp_async_wait<0>();
   __syncwarp();
