@@ -2,7 +2,8 @@
 core, output gate and output projection, differentiable end to end.
 
 Mirrors the reference's layer function ``apply_kda(params, cfg, x,
-chunk_size)`` (AXIOM ``net/kda.py:929-946``; ``_project`` :157-191,
+chunk_size)`` (AXIOM ``net/kda.py:929-946``; :func:`apply_kda` takes its
+arguments as they are, :func:`kda_layer` is the layer underneath; ``_project`` :157-191,
 ``_postprocess`` :194-203, ``_output_gate`` :206-214), with two additions the
 mixer configuration needs: packed variable-length batches (``cu_seqlens``) and
 the decay gate ``g = -exp(A_log) * softplus(z + b)`` beside the reference's
@@ -142,6 +143,56 @@ def kda_layer(p: KDALayerParams, x, *, H, cu_seqlens=None, gate_kind="softplus",
         y = mixer.gated_rmsnorm(o, gl[None], cu_seqlens=cu, out_rows=rows)
     out = y.squeeze(0) @ p.W_o  # a view both ways (indexing's backward would zero-fill y's shape)
     return (out, s_t) if return_state else out
+
+
+def apply_kda(params, cfg, x, chunk_size=None):
+    """The reference's layer entry point ``apply_kda(params, cfg, x, chunk_size)``
+    (``net/kda.py:929-946``) on this library.
+
+    ``params``: the reference's ``KDAParams`` fields as torch tensors (an object
+    with those attributes, or a dict): ``W_q, W_k, W_v, W_o, W_g, W_beta,
+    W_a_down, W_a_up, b_alpha, A, conv_q, conv_k, conv_v`` (the window fields are
+    not read).  ``cfg``: its ``ModelConfig`` fields ``num_heads, kda_impl,
+    kda_wyut_chunk, kda_g_min, swa_window, attn_dense_reference``.  ``x``:
+    ``(T, hidden)`` as the reference takes it, or ``(B, T, hidden)``, which runs as
+    one call over B packed sequences (where the reference maps the layer over
+    the batch with ``vmap``, ``net/model.py:341-347``).
+
+    The dispatch fails closed like the reference's: ``cfg.kda_impl`` must be
+    ``chunked_cc`` (the form this library implements; ``chunked`` and ``wyut``
+    are other algorithms, ``:929-946``), ``AXIOM_KDA_CC_IMPL`` must be ``b200``
+    (``jax``, ``mosaic`` and ``persistent`` are the reference's JAX / Pallas
+    bodies, not present here; an unknown value raises ``ValueError``), and the
+    window branch must be off (``_with_window`` :261-269: ``attn_dense_reference``
+    or ``swa_window == 0``, the reference's default).  The layer is then the
+    reference's ``_apply_chunked_cc_persistent`` (:790-853): projections, short
+    conv, Swish, L2 norm, sigmoid beta, the decay gate ``g = g_min sigmoid(exp(A)
+    z)`` with ``z = x W_a_down W_a_up + b_alpha``, the chunked core, the
+    head-wise RMSNorm times ``sigmoid(x W_g)`` and ``W_o``; differentiable."""
+    from .kda import kda_cc_impl
+
+    if cfg.kda_impl != "chunked_cc":
+        raise NotImplementedError(
+            f"kda_impl={cfg.kda_impl!r}: this library implements the chunked_cc form only")
+    impl = kda_cc_impl()
+    if impl != "b200":
+        raise NotImplementedError(
+            f"AXIOM_KDA_CC_IMPL={impl!r} selects a JAX / Pallas body of the reference; here only 'b200' runs")
+    if not cfg.attn_dense_reference and cfg.swa_window > 0:
+        raise NotImplementedError("the sliding-window branch (swa_window > 0) is not part of this library")
+    get = (lambda n: params[n]) if isinstance(params, dict) else (lambda n: getattr(params, n))
+    p = KDALayerParams(W_q=get("W_q"), W_k=get("W_k"), W_v=get("W_v"), W_g=get("W_g"), W_beta=get("W_beta"),
+                       W_a_down=get("W_a_down"), W_a_up=get("W_a_up"), b_gate=get("b_alpha"), A=get("A"),
+                       conv_q=get("conv_q"), conv_k=get("conv_k"), conv_v=get("conv_v"), W_o=get("W_o"))
+    chunk = int(chunk_size or cfg.kda_wyut_chunk)
+    kw = dict(H=cfg.num_heads, gate_kind="sigmoid_min", g_min=float(cfg.kda_g_min), chunk=chunk)
+    if x.dim() == 2:
+        return kda_layer(p, x, **kw)
+    if x.dim() != 3:
+        raise ValueError(f"x: expected (T, hidden) or (B, T, hidden), got {tuple(x.shape)}")
+    B, T, hid = x.shape
+    cu = [i * T for i in range(B + 1)]
+    return kda_layer(p, x.reshape(B * T, hid), cu_seqlens=cu, **kw).reshape(B, T, -1)
 
 
 @dataclass

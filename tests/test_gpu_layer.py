@@ -176,3 +176,55 @@ def test_boundary_decay_sgd_steps_stay_finite_and_match():
                 t = getattr(p, f)
                 t -= lr * t.grad.to(t.dtype)
                 t.grad = None
+
+
+@pytest.mark.parametrize("batched", [False, True])
+def test_apply_kda_with_the_reference_arguments(batched, monkeypatch):
+    """``apply_kda(params, cfg, x)`` with the reference's ``KDAParams`` field names
+    (``b_alpha`` the gate bias) and ``ModelConfig`` fields, its K3 gate
+    ``g = g_min sigmoid(exp(A) z)``: output and gradients against the float64
+    oracle layer; ``(B, T, hidden)`` runs as one packed call, each row against
+    the oracle alone.  bf16, dk = dv = 128 (tensor-core path), bound 5e-2; 1e-1
+    for A, whose gradient sums dg g_min sigmoid' exp(A) u over every token and
+    channel with u = z + b centred on zero: in the oracle |dA| is 0.2-0.7 % of
+    the sum of its terms' magnitudes here, so a 0.06 % correlated error of the
+    core's bf16 dg moves it by several percent."""
+    from types import SimpleNamespace
+
+    from axiom_b200 import layer
+
+    monkeypatch.setenv("AXIOM_KDA_CC_IMPL", "b200")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    H, dk, hid, rank, K = 2, 128, 256, 16, 4
+    cfg = SimpleNamespace(num_heads=H, kda_dk=dk, kda_dv=dk, kda_g_min=-5.0, kda_impl="chunked_cc",
+                          kda_wyut_chunk=64, swa_window=128, attn_dense_reference=True)
+    p = layer.init_params(hid, H, dk, dk, rank=rank, K=K, gate_kind="sigmoid_min", dtype=torch.bfloat16, seed=9)
+    with torch.no_grad():
+        g0 = torch.Generator(device="cpu").manual_seed(15)
+        p.b_gate.copy_(torch.randn(p.b_gate.shape, generator=g0) * 0.3)
+        p.A.copy_(torch.randn(p.A.shape, generator=g0) * 0.3)
+    fields_ = ("W_q", "W_k", "W_v", "W_g", "W_beta", "W_a_down", "W_a_up", "A", "conv_q", "conv_k", "conv_v", "W_o")
+    params = {f: getattr(p, f) for f in fields_}
+    params["b_alpha"] = p.b_gate
+    B, T = (2, 150) if batched else (1, 150)
+    gen = torch.Generator(device="cpu").manual_seed(16)
+    x = torch.randn(B, T, hid, generator=gen).to("cuda", torch.bfloat16)
+    dout = torch.randn(B, T, hid, generator=gen).to("cuda", torch.bfloat16)
+    xin = (x if batched else x[0]).clone().requires_grad_(True)
+    out = layer.apply_kda(params, cfg, xin)
+    assert out.shape == xin.shape
+    out.backward(dout if batched else dout[0])
+    P = {f: getattr(p, f).detach().double().cpu().numpy() for f in fields_ + ("b_gate",)}
+    grads = {f: 0.0 for f in P}
+    for b in range(B):
+        ref, cache = M.layer_fwd(P, x[b].double().cpu().numpy(), H, None, kind=M.GATE_SIGMOID_MIN)
+        g = M.layer_bwd(P, cache, dout[b].double().cpu().numpy())
+        got = out[b] if batched else out
+        gx = xin.grad[b] if batched else xin.grad
+        assert scale_rel_err(got.detach().double().cpu().numpy(), ref) <= 5e-2, b
+        assert scale_rel_err(gx.double().cpu().numpy(), g["x"]) <= 5e-2, b
+        for f in P:
+            grads[f] = grads[f] + g[f]
+    for f in P:
+        tol = 1e-1 if f == "A" else 5e-2
+        assert scale_rel_err(getattr(p, f).grad.double().cpu().numpy(), grads[f]) <= tol, f
