@@ -18,7 +18,9 @@ tested in, so nothing imports this module by default.  With them installed::
 
 The reference calls its scan per batch element under ``vmap``
 (``net/model.py:341-347``); these calls take the batch dimension directly, so
-the caller drops the ``vmap`` around the core interval.
+the caller drops the ``vmap`` around the core interval and makes one launch for
+the batch.  Under a ``vmap`` that stays, each call declares
+``vmap_method="sequential"``: one call per mapped element.
 """
 
 from __future__ import annotations
@@ -71,7 +73,7 @@ def _fwd_call(q, k, v, g, beta, S0, chunk):
         jax.ShapeDtypeStruct((B, T, H, dv), q.dtype),
         jax.ShapeDtypeStruct((B, H, dk, dv), jnp.float32),
         jax.ShapeDtypeStruct((nbytes,), jnp.uint8),
-    ))(q, k, v, g, beta, S0.astype(jnp.float32), chunk=chunk)
+    ), vmap_method="sequential")(q, k, v, g, beta, S0.astype(jnp.float32), chunk=chunk)
 
 
 @partial(jax.custom_vjp, nondiff_argnums=(6,))
@@ -94,7 +96,7 @@ def _cc_bwd(chunk, res, cot):
         jax.ShapeDtypeStruct(q.shape, q.dtype), jax.ShapeDtypeStruct(k.shape, k.dtype),
         jax.ShapeDtypeStruct(v.shape, v.dtype), jax.ShapeDtypeStruct(g.shape, g.dtype),
         jax.ShapeDtypeStruct(beta.shape, beta.dtype), jax.ShapeDtypeStruct(S0.shape, jnp.float32),
-    ))(q, k, v, g, beta, ckpt, do.astype(q.dtype), dsT.astype(jnp.float32), chunk=chunk)
+    ), vmap_method="sequential")(q, k, v, g, beta, ckpt, do.astype(q.dtype), dsT.astype(jnp.float32), chunk=chunk)
     # cotangents in the primal dtypes (kda_cc_fused_persist.py:1716-1719)
     return dq, dk_, dv_, dg, dbeta, ds0.astype(S0.dtype)
 
@@ -108,4 +110,4 @@ def decode_step_b200(S, q, k, v, g, beta):
     o_shape = q.shape[:-1] + (S.shape[-1],)
     return jax.ffi.ffi_call("kda_decode", (
         jax.ShapeDtypeStruct(o_shape, q.dtype), jax.ShapeDtypeStruct(S.shape, jnp.float32),
-    ), input_output_aliases={0: 1})(S, q, k, v, g, beta)
+    ), input_output_aliases={0: 1}, vmap_method="sequential")(S, q, k, v, g, beta)
