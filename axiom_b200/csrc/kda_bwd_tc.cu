@@ -1372,7 +1372,7 @@ template <int DVS>
 int launch_seq_sliced(const void* dout, const unsigned char* factors, const float* dsT, float* ds0, bf16* dsw,
                       int B, int T, int H, const int* cs, int n_seqs, int* err, const CUtensorMap& tm_do,
                       int use_tma, cudaStream_t st) {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   auto kern = bwd_seq_sliced_kernel<DVS>;
   int rc = ensure_smem(kern, SeqSliceMap<DVS>::SMEM, done);
   if (rc != KDA_OK) return rc;
@@ -1389,15 +1389,15 @@ int tc_scan_slices(long long heads, int n_sm);  // kda_fwd_split.cu
 namespace {
 
 int sm_count() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];  // 0 until looked up (threads may race to fill it: same value)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int n = 0;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (!n) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cached[dev] = n;
+    cached[dev].store(n, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return n;
 }
 
 template <typename Tc>
@@ -1405,7 +1405,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* g, const
                const void* s_ckpt, const void* dout, const float* dsT, void* dq, void* dk_,
                void* dv_, void* dg, void* dbeta, float* ds0, void* work, int B, int T, int H,
                const int* cs, int n_seqs, cudaStream_t st) {
-  static bool done_seq[64] = {false}, done_par[64] = {false};
+  static std::atomic<bool> done_seq[64], done_par[64];
   int rc = ensure_smem(bwd_seq_kernel, SEQ_SMEM, done_seq);
   if (rc != KDA_OK) return rc;
   rc = ensure_smem(bwd_par_kernel<Tc>, PAR_SMEM, done_par);

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "kda_b200.h"
 
 namespace kda {
@@ -27,13 +29,16 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Opt a kernel into more than 48 KB of dynamic shared memory, once per device.
 template <typename Kern>
-inline int ensure_smem(Kern kern, int bytes, bool* done_per_device, int max_devices = 64) {
+// The flags are atomics: host threads may launch concurrently (the calls are
+// reentrant); setting the attribute twice is harmless, so a plain test-and-set
+// suffices.
+inline int ensure_smem(Kern kern, int bytes, std::atomic<bool>* done_per_device, int max_devices = 64) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= max_devices) return KDA_ERR_DEVICE;
-  if (!done_per_device[dev]) {
+  if (!done_per_device[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
       return KDA_ERR_LAUNCH;
-    done_per_device[dev] = true;
+    done_per_device[dev].store(true, std::memory_order_release);
   }
   return KDA_OK;
 }

@@ -862,7 +862,7 @@ fwd_out_kernel(unsigned char* __restrict__ factors, const Tc* __restrict__ s_ckp
 template <typename Tc, int DVS>
 int launch_scan(const unsigned char* factors, const float* s0, float* s_out, void* s_ckpt, int B, int T, int H,
                 const int* cs, int n_seqs, int* err, cudaStream_t st) {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   auto kern = fwd_scan_kernel<Tc, DVS>;
   int rc = ensure_smem(kern, ScanMap<DVS>::SMEM, done);
   if (rc != KDA_OK) return rc;
@@ -877,7 +877,7 @@ template <typename To, typename Tc>
 int launch_split(const void* q, const void* k, const void* v, const void* g, const void* beta, const float* s0,
                  void* o, float* s_out, void* s_ckpt, int B, int T, int H, const int* cs, int n_seqs,
                  int slices, cudaStream_t st) {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   auto prep = fwd_prep_kernel<Tc>;
   int rc = ensure_smem(prep, PREP_SMEM, done);
   if (rc != KDA_OK) return rc;
@@ -909,7 +909,7 @@ int launch_split(const void* q, const void* k, const void* v, const void* g, con
     default: return KDA_ERR_SHAPE;
   }
   if (rc != KDA_OK) return rc;
-  static bool done_out[64] = {false};
+  static std::atomic<bool> done_out[64];
   auto out = fwd_out_kernel<To, Tc>;
   rc = ensure_smem(out, OUT_SMEM, done_out);
   if (rc != KDA_OK) return rc;

@@ -591,7 +591,7 @@ template <typename To, typename Tc>
 int launch_t(const void* q, const void* k, const void* v, const void* g, const void* beta,
              const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
              const int* cs, int n_seqs, cudaStream_t st) {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   auto kern = fwd_tc_kernel<To, Tc>;
   int rc = ensure_smem(kern, SMEM_BYTES, done);
   if (rc != KDA_OK) return rc;

@@ -1488,7 +1488,7 @@ int launch_prologue_v(ProArgs& a, int roles, int n_roles, bool bwd, cudaStream_t
   // arithmetic, keeps (strip groups, heads)
   a.head_x = !bwd && groups <= 65535;
   const dim3 grid(a.head_x ? a.H : groups, a.head_x ? groups : a.H, n_roles);
-  static bool done_f[64] = {false}, done_b[64] = {false};
+  static std::atomic<bool> done_f[64], done_b[64];
   if (bwd) {
     constexpr int smem = kBwdWarps * bwd_ring_bytes<CPL, Tin, Tout>();
     const int rc = ensure_smem(prologue_bwd_kernel<CPL, VARLEN, Tin, Tout>, smem, done_b);
@@ -1562,7 +1562,7 @@ int grms_types(const void* o, const void* gate, const void* dy, void* y, void* d
 
 template <int DK, int DV, typename Tin, typename To>
 int dec_launch(const DecArgs& a, int N, cudaStream_t st) {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   constexpr int smem = DK * DV * 4;
   const int rc = ensure_smem(decode_fused_kernel<DK, DV, Tin, To>, smem, done);
   if (rc != KDA_OK) return rc;

@@ -471,7 +471,7 @@ template <typename Tin, typename To, typename Tc>
 int fwd_launch_t(const void* q, const void* k, const void* v, const void* g, const void* beta,
                  const float* s0, void* o, float* s_out, void* s_ckpt, int B, int T, int H,
                  int dk, int dv, int C, const int* cs, int n_seqs, cudaStream_t st) {
-  static bool done[64] = {false};
+  static std::atomic<bool> done[64];
   const int bytes = static_cast<int>(sizeof(float)) *
                     (4 * C * (dk + 1) + C * kFwdSlice + 2 * C * (C + 1) + dk * kFwdSlice + C + dk);
   auto kern = fwd_simt_kernel<Tin, To, Tc>;
