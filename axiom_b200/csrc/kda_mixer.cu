@@ -776,9 +776,7 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
   // the window moves by renaming instead of copies.  Likewise the two batches'
   // conv cotangents alternate between DA and DB, each batch reading the other's
   // as the cotangents of the three tokens above it.
-  // (Packed sequences keep one phase and copy the rows instead: their masks
-  // leave no registers for the second set.)
-  constexpr bool RING = !VARLEN;
+  constexpr bool RING = true;
   static_assert(NX + 1 == 8 && kBw == 4, "an 8-row ring, 4 rows a batch");
   float R[8][CPL], DA[kBw][CPL], DB[kBw][CPL];
 #pragma unroll
@@ -791,8 +789,9 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     for (int c = 0; c < CPL; ++c) DA[j][c] = DB[j][c] = 0.f;
   const int sw = a.H * (2 * a.dk + a.dv);
   // One batch; CHECK: tokens may lie outside [t0, t1) or below 0, and taps may
-  // cross a packed sequence's edge (lbu / ubu per token).
-  auto batch = [&](const unsigned char* st, int base, const int (&lbu)[kBw], const int (&ubu)[kBw], auto check,
+  // cross a packed sequence's edge: bit 4 u + i of cm (dm) says whether token u's
+  // tap i below (above) it lies in its sequence.
+  auto batch = [&](const unsigned char* st, int base, unsigned cm, unsigned dm, auto check,
                    auto phase, float (&dc)[kBw][CPL], const float (&dcp)[kBw][CPL]) {
     constexpr bool CHECK = decltype(check)::value;
     constexpr bool MASK = CHECK && VARLEN;
@@ -804,7 +803,6 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     [[maybe_unused]] float bq[NORM ? kBw : 1][CPL];
 #pragma unroll
     for (int u = 0; u < kBw; ++u) {
-      const int tau = base - u;
       float dvr[CPL];
       ld_row<CPL, Tout>(st + kBw * RBX + u * RBY, lane, dvr);
       float2 ss2 = f2(0.f), sd2 = f2(0.f);
@@ -815,7 +813,7 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
           cv2 = make_float2(0.f, 0.f);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            if (tau - i >= lbu[u])
+            if ((cm >> (4 * u + i)) & 1u)
               cv2 = ffma2(make_float2(wt[i][c], wt[i][c + 1]), make_float2(X(u + i)[c], X(u + i)[c + 1]), cv2);
         } else {
           cv2 = fmul2(make_float2(wt[0][c], wt[0][c + 1]), make_float2(X(u)[c], X(u)[c + 1]));
@@ -884,7 +882,7 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
           for (int i = 1; i < 4; ++i) {
             const float2 d = i <= u ? make_float2(dc[u - i][c], dc[u - i][c + 1])
                                     : make_float2(dcp[kBw - i + u][c], dcp[kBw - i + u][c + 1]);
-            if (!MASK || tau + i < ubu[u]) acc = ffma2(make_float2(wt[i][c], wt[i][c + 1]), d, acc);
+            if (!MASK || ((dm >> (4 * u + i)) & 1u)) acc = ffma2(make_float2(wt[i][c], wt[i][c + 1]), d, acc);
           }
           o[c] = acc.x;
           o[c + 1] = acc.y;
@@ -898,7 +896,7 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
           }
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            if (!MASK || tau - i >= lbu[u]) {
+            if (!MASK || ((cm >> (4 * u + i)) & 1u)) {
 #pragma unroll
               for (int c = 0; c < CPL; c += 2) {
                 const float2 w2 = ffma2(make_float2(dc[u][c], dc[u][c + 1]), make_float2(X(u + i)[c], X(u + i)[c + 1]),
@@ -937,32 +935,36 @@ __device__ void pro_bwd_conv(const ProArgs& a, int role, int b, int t0, int t1, 
     tc::cp_async_commit();
     const unsigned char* st = ring + (bi % kBwStages) * STG;
     const int base = hi - bi * kBw;
-    int lbu[kBw], ubu[kBw];
+    // plain: every token in [t0, t1), the window's next rows at or above 0, and
+    // (packed) every tap of the batch inside the sequence [lb, ub) the walk is
+    // in (that of the token above the batch), so the walk stays where it is
+    const bool plain = base < t1 && base - kBw + 1 >= t0 && base - NX - kBw + 1 >= 0 &&
+                       (!VARLEN || (base + 3 < ub && base - kBw + 1 - 3 >= lb));
+    unsigned cm = 0u, dm = 0u;
+    if (VARLEN && !plain) {  // walk down to each token's sequence; its taps inside it
 #pragma unroll
-    for (int u = 0; u < kBw; ++u) {
-      const int tau = base - u;
-      if constexpr (VARLEN) {
+      for (int u = 0; u < kBw; ++u) {
+        const int tau = base - u;
         while (tau < lb && si > 0) {  // below lb lies the previous sequence
           ub = lb;
           --si;
           lb = __ldg(a.cu + si);
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          cm |= static_cast<unsigned>(tau - i >= lb) << (4 * u + i);
+          dm |= static_cast<unsigned>(tau + i < ub) << (4 * u + i);
+        }
       }
-      lbu[u] = lb;
-      ubu[u] = ub;
     }
-    // plain: every token in [t0, t1), the window's next rows at or above 0, and
-    // (packed) every tap of the batch inside the lowest token's sequence
-    const bool plain = base < t1 && base - kBw + 1 >= t0 && base - NX - kBw + 1 >= 0 &&
-                       (!VARLEN || (base + 3 < ub && base - kBw + 1 - 3 >= lb));
     using P0 = std::integral_constant<int, 0>;
     using P1 = std::integral_constant<int, 1>;
     if (RING && (bi & 1)) {
-      if (plain) batch(st, base, lbu, ubu, std::false_type{}, P1{}, DB, DA);
-      else batch(st, base, lbu, ubu, std::true_type{}, P1{}, DB, DA);
+      if (plain) batch(st, base, cm, dm, std::false_type{}, P1{}, DB, DA);
+      else batch(st, base, cm, dm, std::true_type{}, P1{}, DB, DA);
     } else {
-      if (plain) batch(st, base, lbu, ubu, std::false_type{}, P0{}, DA, DB);
-      else batch(st, base, lbu, ubu, std::true_type{}, P0{}, DA, DB);
+      if (plain) batch(st, base, cm, dm, std::false_type{}, P0{}, DA, DB);
+      else batch(st, base, cm, dm, std::true_type{}, P0{}, DA, DB);
       if constexpr (!RING) {
 #pragma unroll
         for (int j = 0; j < kBw; ++j)
