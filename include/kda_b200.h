@@ -26,7 +26,9 @@
  *     only enqueues work on `stream` (NULL = legacy default stream).  Scratch
  *     memory comes from the caller (`workspace`), except for kda_bwd_noalloc,
  *     which uses a fixed array built into the library (see its comment); all
- *     other entry points are stateless.
+ *     other entry points are stateless and may be called from several host
+ *     threads at once, each on its own stream (the only state the library
+ *     keeps is a per-device cache of launch attributes, held in atomics).
  *   - Return value: KDA_OK (0) or a negative KDA_ERR_* code; invalid shapes,
  *     dtypes, alignment or null pointers are rejected before any launch
  *     (fail-closed, the reference's typed-error contract net/kda.py:759-763).
