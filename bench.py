@@ -545,6 +545,28 @@ def run_mixer_sharded(torch, dist, world, rank, dev, steps=5, warmup=3):
     (ms,) = _max_over_ranks(torch, dist, world, dev, [e0.elapsed_time(e1) / steps])
     tok_rank = len(rows)
     (tok_max,) = _max_over_ranks(torch, dist, world, dev, [float(tok_rank)])
+
+    # the same per-rank work without any collective (the rank's partial output and
+    # gradients): what the mesh costs in compute alone, max over ranks
+    def step_local():
+        for t in pl.tensors() + [x]:
+            t.grad = None
+        layer.kda_layer(pl, x, H=Hl, cu_seqlens=cu_loc, gate_kind="softplus").backward(dout)
+
+    ms_local = ms  # one rank: the step has no collective
+    if world > 1:
+        for _ in range(warmup):
+            step_local()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0.record()
+        for _ in range(steps):
+            step_local()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        (ms_local,) = _max_over_ranks(torch, dist, world, dev, [e0.elapsed_time(e1) / steps])
+    coll_ms = max(0.0, ms - ms_local)  # two timed legs: run-to-run noise can exceed a small difference
     del pl, x, dout
     torch.cuda.empty_cache()
     return {"workload": "cfg5 KDA mixer layer fwd+bwd, 16 packed seqs, T=65536, d_model=2048, H=16, "
@@ -553,6 +575,10 @@ def run_mixer_sharded(torch, dist, world, rank, dev, steps=5, warmup=3):
             "ms_per_step": ms, "tokens_per_s": 65536 / (ms / 1e3), "max_tokens_per_sequence_group": tok_max,
             "heads_per_rank": Hl, "collectives": "NCCL all-reduce: W_o partial outputs and input cotangent "
                                                  "(head groups > 1), weight gradients (sequence groups > 1)",
+            "ms_per_step_compute_only": ms_local, "collective_ms_per_step": coll_ms,
+            "limiter": (f"per-rank compute {ms_local:.3f} ms (the busiest rank: {int(tok_max)} tokens x {Hl} heads; "
+                        f"a rank's KDA core is bound by its longest sequence's chain of chunks), "
+                        f"collectives {coll_ms:.3f} ms"),
             "steps": steps, "timing": "CUDA events, max over ranks"}
 
 
